@@ -1,0 +1,551 @@
+"""Benchmark of the structured matrix-multiply hot path: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--op diag|gemm|upper|sandwich|toeplitz] [--mode 3xtf32|tf32|bf16]
+
+Default workload (what the metric is quoted on at N = 8192, one GPU):
+diagonal x dense, C = diag(d) B with d (8192) ~ U[0.5,1.5] and B (8192 x 8192)
+~ U[-1,1] (seeded, cpp1_b200.workloads), GB/s over the bytes the operation
+must move: 4N + 8N^2 per call.  The other ops are the remaining configured
+workloads (GEMM 8192^3, U B at 8192, A S B at 4096, T B at 16384), reported
+as useful TFLOP/s (structural zeros excluded).
+
+Multi-GPU (torchrun, one process per GPU, NCCL):
+  diag      weak scaling: every rank scales its own 8192 x 8192 row slab;
+            no collective on the data path (the rows are independent).
+  others    strong scaling: the output is split into row slabs (equal-work
+            boundaries for the triangular operand); the shared right operand
+            B is broadcast from rank 0 each step inside the timed region.
+
+Timing: W untimed warm-up steps, then K steps between a barrier +
+synchronize on both sides, CUDA events on the launching stream, max over
+ranks.  Inputs are larger than L2 (126 MB) for every workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "useful TFLOP/s (GB/s for diag) at N=8192, 1/2/4/8 B200, % of roofline vs CPU"
+
+WORKLOADS = {
+    "diag": dict(N=8192, unit="GB/s", bound="hbm", desc="C = diag(d) B, d 8192, B 8192x8192 fp32"),
+    "gemm": dict(N=8192, unit="TFLOP/s", bound="tensor", desc="C = A B, 8192^3 fp32"),
+    "upper": dict(N=8192, unit="TFLOP/s", bound="tensor", desc="C = U B, U 8192 upper (packed), B 8192x8192"),
+    "sandwich": dict(N=4096, unit="TFLOP/s", bound="tensor", desc="C = A S B, 4096, S packed symmetric"),
+    "toeplitz": dict(N=16384, unit="TFLOP/s", bound="tensor", desc="C = T B, T from a 32767 generator, B 16384^2"),
+}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--op", choices=sorted(WORKLOADS), default="diag")
+    ap.add_argument("--mode", choices=["3xtf32", "tf32", "bf16"], default="3xtf32")
+    ap.add_argument("--n", type=int, default=None, help="override the problem order")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    a = ap.parse_args()
+    if a.steps is None:
+        a.steps = {"diag": 400, "gemm": 20, "upper": 30, "sandwich": 30, "toeplitz": 3}[a.op]
+    if a.warmup is None:
+        a.warmup = {"diag": 20, "gemm": 3, "upper": 3, "sandwich": 3, "toeplitz": 3}[a.op]
+    return a
+
+
+# ---------------------------------------------------------------- peaks
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(op: str):
+    """DRAM bytes per launch of the op's dominant kernel from the committed
+    ncu summary (profiles/ncu_traffic.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            t = json.load(f)
+        return t.get(op, {}).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML in a thread while
+    the timed region runs (reading only; no setting is changed)."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        self.index = index
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
+        names = [k for k, v in self.REASONS.items() if self.reasons & v]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- distributed
+def dist_init(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif args.impl == "ours":
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_reference_call(op: str, n: int, sample_n: int):
+    """One call of the reference's own CPU kernel (oracle/_ref) on a seeded
+    problem of order sample_n; returns (kernel ms, units moved/computed, kind)."""
+    import oracle as O
+    from cpp1_b200 import workloads as W
+    if not O.ref_available():
+        raise RuntimeError("oracle/_ref not built")
+    if op == "diag":
+        w = W.make_diag(sample_n, sample_n, seed=0)
+        _, ms = O.ref_diag_rows(w["d"], w["B"])
+        return ms, 4 * sample_n + 8 * sample_n * sample_n
+    if op == "gemm":
+        w = W.make_gemm(sample_n, sample_n, sample_n, seed=0)
+        _, ms = O.ref_gemm(w["A"], w["B"])
+        return ms, 2 * sample_n ** 3
+    if op == "upper":
+        w = W.make_upper(sample_n, seed=0)
+        _, ms = O.ref_upper_left(w["U"], w["B"])
+        return ms, sample_n * sample_n * (sample_n + 1)
+    if op == "sandwich":
+        w = W.make_sandwich(sample_n, seed=0)
+        _, ms = O.ref_sandwich(w["A"], w["S"], w["B"])
+        return ms, 4 * sample_n ** 3
+    if op == "toeplitz":
+        w = W.make_toeplitz(sample_n, seed=0)
+        _, ms = O.ref_toeplitz_left(w["g"], w["B"])
+        return ms, 2 * sample_n ** 3
+    raise ValueError(op)
+
+
+CPU_SAMPLE_N = {"diag": 8192, "gemm": 2048, "upper": 2048, "sandwich": 1024, "toeplitz": 2048}
+
+
+def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
+    cores = os.cpu_count() or 1
+    sn = min(n, CPU_SAMPLE_N[op])
+    rates = []
+    t0 = time.time()
+    while time.time() - t0 < budget_s or len(rates) < 2:
+        ms, units = cpu_reference_call(op, n, sn)
+        rates.append(units / (ms * 1e-3))
+        if len(rates) >= 50:
+            break
+    rate = statistics.median(rates)
+    scale = 1e9 if op == "diag" else 1e12
+    return {"value": rate / scale, "unit": WORKLOADS[op]["unit"], "cores": cores, "kind": "reference",
+            "sample": f"{op} at order {sn} ({len(rates)} calls, median; the reference's AVX2+OpenMP kernel, "
+                      f"its own chrono window, OMP threads = {cores})"}
+
+
+# ---------------------------------------------------------------- our arm
+def equal_work_bounds(n: int, world: int, triangular: bool, align: int = 128):
+    """Row-slab boundaries.  For U (row i costs n - i), boundary g sits at
+    n (1 - sqrt(1 - g/G)), rounded to the tile height."""
+    b = [0]
+    for g in range(1, world):
+        x = n * (1 - math.sqrt(1 - g / world)) if triangular else n * g / world
+        b.append(min(n, max(b[-1], int(round(x / align)) * align)))
+    b.append(n)
+    return b
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+    from cpp1_b200 import _lib, ops
+    from cpp1_b200 import workloads as W
+
+    L = _lib.load()
+    op = args.op
+    n = args.n or WORKLOADS[op]["N"]
+    stream = torch.cuda.current_stream()
+    peaks = measured_peaks()
+    mode = args.mode
+
+    # ---- inputs (host, seeded) -> device
+    if op == "diag":
+        w = W.make_diag(n, n, seed=rank)
+        h_in = [w["d"], w["B"]]
+    elif op == "gemm":
+        w = W.make_gemm(n, n, n, seed=0)
+        h_in = [w["A"], w["B"]]
+    elif op == "upper":
+        w = W.make_upper(n, seed=0)
+        h_in = [w["U"], w["B"]]
+    elif op == "sandwich":
+        w = W.make_sandwich(n, seed=0)
+        h_in = [w["A"], w["S"], w["B"]]
+    else:
+        w = W.make_toeplitz(n, seed=0)
+        h_in = [w["g"], w["B"]]
+    d_in = [torch.from_numpy(x).cuda() for x in h_in]
+
+    bounds = equal_work_bounds(n, world, triangular=(op == "upper")) if op != "diag" else None
+    r0, r1 = (bounds[rank], bounds[rank + 1]) if bounds else (0, n)
+    nrows = r1 - r0
+    out = torch.empty((nrows if op != "diag" else n, n), dtype=torch.float32, device="cuda")
+    m = _lib.MODES[mode]
+
+    def ws_for(nbytes):
+        buf = ops.workspace(nbytes, out.device)
+        return (buf.data_ptr(), buf.numel()) if buf is not None else (None, 0)
+
+    sp = stream.cuda_stream or None
+    if op == "diag":
+        d, B = d_in
+
+        def step():
+            _lib.check(L.smm_diag_rows(d.data_ptr(), B.data_ptr(), out.data_ptr(), n, n, sp), "diag")
+        units_per_rank_call = 4 * n + 8 * n * n
+    elif op == "gemm":
+        A, B = d_in
+        ws, wsb = ws_for(L.smm_gemm_workspace_size(nrows, n, n, m))
+
+        def step():
+            if world > 1:
+                dist.broadcast(B, src=0)
+            Ap = A.data_ptr() + r0 * n * 4
+            _lib.check(L.smm_gemm(Ap, B.data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+        units_per_rank_call = 2 * nrows * n * n
+    elif op == "upper":
+        U, B = d_in
+        ws, wsb = ws_for(L.smm_upper_left_workspace_size(n, n, _lib.FMT_PACKED, m))
+
+        def step():
+            if world > 1:
+                dist.broadcast(B, src=0)
+            _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, B.data_ptr(), out.data_ptr(), n, n, r0,
+                                             nrows, m, ws, wsb, sp), "upper")
+        units_per_rank_call = sum(n - i for i in range(r0, r1)) * n  # N^2(N+1) summed over ranks
+    elif op == "sandwich":
+        A, S, B = d_in
+        X = torch.empty((n, n), dtype=torch.float32, device="cuda")
+        ws, wsb = ws_for(L.smm_gemm_workspace_size(nrows, n, n, m))
+        wsx, wsxb = None, 0
+
+        def step():
+            if world > 1:
+                dist.broadcast(S, src=0)
+                dist.broadcast(B, src=0)
+            # X = S B on every rank is redundant work at G > 1; the slab
+            # variant of the sandwich computes only this rank's rows of A S B.
+            _lib.check(L.smm_symm_left(S.data_ptr(), B.data_ptr(), X.data_ptr(), n, n, m, ws, wsb, sp), "symm")
+            Ap = A.data_ptr() + r0 * n * 4
+            _lib.check(L.smm_gemm(Ap, X.data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+        units_per_rank_call = (4 * n ** 3) // world
+    else:
+        g, B = d_in
+        ws, wsb = ws_for(L.smm_toeplitz_left_workspace_size(n, n, m))
+
+        def step():
+            if world > 1:
+                dist.broadcast(B, src=0)
+            _lib.check(L.smm_toeplitz_left_rows(g.data_ptr(), B.data_ptr(), out.data_ptr(), n, n, r0, nrows, m, ws,
+                                                wsb, sp), "toeplitz")
+        units_per_rank_call = 2 * nrows * n * n
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.device_status()
+
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = L.smm_launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = ev0.elapsed_time(ev1)
+    launches = L.smm_launch_count() - launches0
+    ops.device_status()
+    ms = max_over_ranks(ms_local, world)
+    ms_per_step = ms / args.steps
+
+    total_units = units_per_rank_call * world if op == "diag" else (
+        n * n * (n + 1) if op == "upper" else (4 * n ** 3 if op == "sandwich" else 2 * n ** 3))
+    scale = 1e9 if op == "diag" else 1e12
+    value = total_units / (ms_per_step * 1e-3) / scale
+
+    # ---- roofline of the dominant kernel, timed on its own on this rank
+    roof = roofline(op, n, nrows, mode, step, stream, peaks, units_per_rank_call, world)
+
+    res = {
+        "metric": METRIC, "value": round(value, 3), "unit": WORKLOADS[op]["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak" if op == "diag" else "strong", "vs_baseline": None,
+        "dtype": "f32" if op == "diag" else {"3xtf32": "f32 (3xTF32 tensor cores)", "tf32": "tf32",
+                                            "bf16": "bf16 (fp32 accumulate)"}[mode],
+        "data": "synthetic (seeded numpy PCG64, cpp1_b200.workloads)",
+        "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "mode": mode if op != "diag" else "f32",
+                   "parallelism": f"row-slabs x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (126 MB): no flush needed"},
+        "roofline": roof,
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    return res, d_in, h_in
+
+
+def roofline(op, n, nrows, mode, step, stream, peaks, units_rank, world):
+    import torch
+    reps = 50 if op == "diag" else 3
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        return {"bound": WORKLOADS[op]["bound"], "note": "reported at n_gpus = 1"}
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(reps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launch_ms = ev0.elapsed_time(ev1) / reps / (2 if op == "sandwich" else 1)
+    if op == "diag":
+        bytes_launch = 4 * n + 8 * n * n
+        achieved = bytes_launch / (launch_ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        traffic = profile_traffic(op)
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": round(launch_ms, 4),
+                "peak_source": f"{peaks['source']} HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"}
+    passes = {"3xtf32": 3, "tf32": 1, "bf16": 1}[mode]
+    useful = units_rank / (2 if op == "sandwich" else 1)
+    mma_flops = passes * useful
+    achieved = mma_flops / (launch_ms * 1e-3) / 1e12
+    if mode == "bf16":
+        peak, src = peaks["bf16_tflops"], f"{peaks['source']} cuBLAS bf16 burst"
+    else:
+        peak, src = peaks["bf16_tflops"] / 2, f"TF32 = half the {peaks['source']} cuBLAS bf16 burst"
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4), "traffic": profile_traffic(op),
+            "algorithmic_flops_per_launch": mma_flops, "launch_ms": round(launch_ms, 4),
+            "peak_source": src + f"; {passes} MMA pass(es) per useful FLOP"}
+
+
+def e2e_ours(args, h_in, n):
+    """The same metric through the C ABI with HOST buffers: copy-in, compute
+    and copy-out of each step inside the timed region."""
+    import torch
+    from cpp1_b200 import _lib, ops
+    L = _lib.load()
+    op = args.op
+    if op == "diag":
+        d = torch.from_numpy(h_in[0]).pin_memory()
+        B = torch.from_numpy(h_in[1]).pin_memory()
+        C = torch.empty_like(B).pin_memory()
+        need = L.smm_diag_rows_host_workspace_size(n, n)
+        ws = ops.workspace(need, torch.device("cuda", torch.cuda.current_device()))
+
+        def step():
+            _lib.check(L.smm_diag_rows_host(d.data_ptr(), B.data_ptr(), C.data_ptr(), n, n, ws.data_ptr(),
+                                            ws.numel()), "smm_diag_rows_host")
+        h2d = 4 * n + 4 * n * n
+        d2h = 4 * n * n
+        units = 4 * n + 8 * n * n
+        steps = max(5, min(args.steps // 20, 30))
+    else:
+        hp = [torch.from_numpy(x).pin_memory() for x in h_in]
+        Cn = n
+        C = torch.empty((Cn, Cn), dtype=torch.float32).pin_memory()
+        fn = {"gemm": lambda a, b: ops.gemm(a, b, mode=args.mode),
+              "upper": lambda u, b: ops.upper_left(u, b, mode=args.mode),
+              "toeplitz": lambda g, b: ops.toeplitz_left(g, b, mode=args.mode),
+              "sandwich": lambda a, s, b: ops.symm_sandwich(a, s, b, mode=args.mode)}[op]
+
+        def step():
+            dev = [x.cuda(non_blocking=True) for x in hp]
+            C.copy_(fn(*dev), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        h2d = sum(x.nbytes for x in h_in)
+        d2h = C.numel() * 4
+        units = {"gemm": 2 * n ** 3, "upper": n * n * (n + 1), "sandwich": 4 * n ** 3, "toeplitz": 2 * n ** 3}[op]
+        steps = 2 if op == "toeplitz" else 5
+    step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / steps
+    scale = 1e9 if op == "diag" else 1e12
+    return {"value": round(units / dt / scale, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(dt * 1e3, 3),
+            "api": "C ABI with pinned host buffers" + (" (smm_diag_rows_host)" if op == "diag" else " via cpp1_b200.ops")}
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    """The reference's own CPU implementation of the path (oracle/_ref: its
+    AVX2+OpenMP kernels compiled from its sources) on this host's cores, same
+    config, metric and unit.  Rank 0 only."""
+    op = args.op
+    n = args.n or WORKLOADS[op]["N"]
+    import oracle as O
+    if not O.ref_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref (the reference CPU kernels) was not built"}
+    sn = min(n, CPU_SAMPLE_N[op])
+    for _ in range(max(0, min(args.warmup, 2))):
+        cpu_reference_call(op, n, sn)
+    times, units = [], 0
+    for _ in range(args.steps if op == "diag" else min(args.steps, 3)):
+        ms, units = cpu_reference_call(op, n, sn)
+        times.append(ms)
+    ms = statistics.median(times)
+    scale = 1e9 if op == "diag" else 1e12
+    value = units / (ms * 1e-3) / scale
+    cores = os.cpu_count() or 1
+    sample = f"{op} at order {sn}" + ("" if sn == n else f" (bounded sample of the order-{n} workload)")
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": WORKLOADS[op]["unit"], "n_gpus": world,
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak" if op == "diag" else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded numpy PCG64, cpp1_b200.workloads)",
+        "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "sample_N": sn},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 3), "unit": WORKLOADS[op]["unit"], "cores": cores, "kind": "reference",
+                         "sample": sample + "; the reference's AVX2+OpenMP kernel, its own chrono window"},
+        "e2e": {"value": round(value, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args, rank, world)), flush=True)
+        return 0
+
+    rank, world, local = dist_init(args)
+    res, d_in, h_in = run_ours(args, rank, world, local)
+    n = args.n or WORKLOADS[args.op]["N"]
+    if not args.no_e2e:
+        # Every rank runs the same host-buffer path; rank 0 reports its own
+        # (per-GPU) rate times the rank count for the whole job at weak
+        # scaling, or the single-GPU rate otherwise.
+        del d_in
+        e2e = e2e_ours(args, h_in, n)
+        if world > 1 and args.op == "diag":
+            e2e["value"] = round(max_over_ranks(-e2e["value"], world) * -1 * world, 3)
+        res["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            res["cpu_baseline"] = cpu_baseline(args.op, n)
+        except Exception as e:  # the baseline is reported, not required
+            res["cpu_baseline"] = {"value": None, "unavailable": str(e)}
+    if world > 1:
+        import torch.distributed as dist
+        barrier(world)
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,354 @@
+// The tcgen05 contraction engine shared by every tensor-core operation of the
+// library: C(M x N) = Aop(M x K) * B(K x N), fp32 row-major C, accumulator in
+// tensor memory.
+//
+// Tile: 128 x BN output per CTA (BN = 64, 128 or 256), K-blocks of 16 fp32
+// (64 bytes) per pipeline stage, STAGES stages in shared memory.
+//
+// Operand staging per stage:
+//   A (K-major, 128 rows x 64 B, 64-byte swizzle):
+//     AKind::Dense       TMA tile load of a row-major A
+//     AKind::UpperPacked built by the transform warps from packed-upper
+//                        storage (zeros below the diagonal; k-blocks left of
+//                        the row tile's diagonal are never visited)
+//     AKind::Toeplitz    built from the 2N-1 generator: row r of the tile is
+//                        a contiguous generator window
+//     AKind::SymmPacked  built from packed-upper storage, mirrored below the
+//                        diagonal
+//   B (MN-major, BN columns x 16 k-rows): TMA tile loads of a row-major B,
+//     32 columns (128 B) per box, 128-byte swizzle with 32-byte atoms (the
+//     only swizzle kind::tf32 accepts for an MN-major operand; with the plain
+//     128-byte swizzle the MMA produces nothing).
+//
+// 3xTF32 (SPLIT3): the transform warps write lo = x - tf32(x) planes of both
+// operands next to the raw tiles, and the MMA issuer runs three MMAs per
+// k-step: hi*hi + hi*lo + lo*hi.  The raw fp32 tile serves as the hi operand
+// (kind::tf32 reads the upper 19 bits of each element).
+//
+// Warp roles (192 threads):
+//   warp 0     TMA producer (one lane)
+//   warp 1     TMEM allocator + MMA issuer (one lane)
+//   warps 2-5  transform (lo planes, structured A tiles), then epilogue
+//              (TMEM -> registers -> global C)
+//
+// Every wait is bounded (WaitCtx): on expiry the kernel records
+// kDevErrTimeout in the status word, the other roles stop waiting, in-flight
+// copies/MMAs are drained (bounded), TMEM is freed and the CTA exits.
+#pragma once
+#include "smm_device.cuh"
+
+namespace smm {
+
+enum class AKind : int { Dense = 0, UpperPacked = 1, Toeplitz = 2, SymmPacked = 3, UpperDense = 4 };
+
+struct UmmaParams {
+  int M, N, K;             // C is M x N; reduction length K
+  float* C;                // row-major, leading dimension ldc
+  int ldc;
+  const float* a_src;      // packed U / generator / packed S (structured A kinds)
+  int a_dim;               // order of the structured matrix
+  int a_row0;              // row of the structured matrix that output row 0 maps to
+  int row_tiles;           // ceil(M / 128)
+  int col_tiles;           // ceil(N / BN)
+  uint32_t* status;        // device status word (sticky error bits)
+  unsigned long long wait_limit_ns;
+  uint32_t* trace;         // optional diagnostic record of CTA (0,0); null in normal use
+};
+
+// Slots of the diagnostic record (UmmaParams::trace, 64 words).
+enum : int {
+  kTrTmem = 0, kTrNumKb = 1, kTrA = 2 /*8 words*/, kTrB = 10 /*8 words*/, kTrAccOk = 18,
+  kTrAcc = 19 /*16 words*/, kTrMmas = 35, kTrDescA = 36 /*2 words*/, kTrDescB = 38 /*2*/, kTrIdesc = 40,
+  kTrEpiDone = 41, kTrWords = 64
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 16;                   // fp32 elements per k-block (64 bytes)
+constexpr int kThreads = 192;
+constexpr int kATileBytes = kBM * kBK * 4;  // 8 KiB
+
+template <int BN>
+struct TileGeom {
+  static constexpr int kBTileBytes = BN * kBK * 4;  // BN/32 boxes of 16 rows x 128 B
+  static constexpr int kBChunkBytes = 16 * 128;     // one 32-column box
+};
+
+template <int BN, bool SPLIT3>
+__host__ __device__ constexpr int stage_bytes() {
+  return (SPLIT3 ? 2 : 1) * (kATileBytes + TileGeom<BN>::kBTileBytes);
+}
+
+template <int BN, bool SPLIT3, int STAGES>
+__host__ __device__ constexpr int umma_smem_bytes() {
+  return 1024 /*alignment slack*/ + STAGES * stage_bytes<BN, SPLIT3>() + 256 /*barriers etc*/;
+}
+
+__device__ __forceinline__ long long packed_idx(long long i, long long j, long long n) {
+  return i * n - i * (i - 1) / 2 + (j - i);
+}
+
+// Value of the structured left operand at (row gr, column k); zero outside
+// the n x n matrix.
+template <AKind AK>
+__device__ __forceinline__ float a_value(const float* __restrict__ src, int n, int gr, int k) {
+  if (gr >= n || k >= n) return 0.0f;
+  if constexpr (AK == AKind::UpperPacked) {
+    return k >= gr ? __ldg(src + packed_idx(gr, k, n)) : 0.0f;
+  } else if constexpr (AK == AKind::Toeplitz) {
+    return __ldg(src + (n - 1 + k - gr));
+  } else {  // SymmPacked
+    return k >= gr ? __ldg(src + packed_idx(gr, k, n)) : __ldg(src + packed_idx(k, gr, n));
+  }
+}
+
+template <AKind AK, bool SPLIT3, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const UmmaParams p) {
+  constexpr int kBTile = TileGeom<BN>::kBTileBytes;
+  constexpr int kStage = stage_bytes<BN, SPLIT3>();
+  constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
+  constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + kBTile;
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  constexpr uint32_t kIdesc = make_idesc(kFmtTF32, kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStage);
+  uint64_t* ready = full + STAGES;
+  uint64_t* empty = ready + STAGES;
+  uint64_t* accum_full = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  auto a_hi = [&](int s) { return smem + s * kStage; };
+  auto b_hi = [&](int s) { return smem + s * kStage + kATileBytes; };
+  auto a_lo = [&](int s) { return smem + s * kStage + kATileBytes + kBTile; };
+  auto b_lo = [&](int s) { return smem + s * kStage + 2 * kATileBytes + kBTile; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Tile coordinates.  blockIdx.y walks row tiles first-to-last, so for the
+  // triangular operand (whose row tile i has K range [128 i, N)) the longest
+  // tiles are dispatched first.
+  const int n_tile = blockIdx.x;
+  const int m_tile = blockIdx.y;
+  const int m0 = m_tile * kBM;
+  const int n0 = n_tile * BN;
+  // Rows of a triangular operand are zero left of the diagonal: row tile
+  // [g0, g0+128) of U needs k >= g0 only.
+  int kb_begin = 0;
+  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + m0) / kBK;
+  const int kb_end = (p.K + kBK - 1) / kBK;
+  const int num_kb = kb_end - kb_begin;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    if constexpr (kATma) tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const bool tr = p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0;
+  if (tr && threadIdx.x == 0) {
+    p.trace[kTrTmem] = tmem_base;
+    p.trace[kTrNumKb] = static_cast<uint32_t>(num_kb);
+  }
+
+  const WaitCtx wprod{abort_flag, p.status, p.wait_limit_ns, kWaitProducer};
+  const WaitCtx wmma{abort_flag, p.status, p.wait_limit_ns, kWaitMma};
+  const WaitCtx wxf{abort_flag, p.status, p.wait_limit_ns, kWaitTransform};
+  const WaitCtx wepi{abort_flag, p.status, p.wait_limit_ns, kWaitEpilogue};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < num_kb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
+        mbar_arrive_expect_tx(&full[s], kTxBytes);
+        const int k0 = (kb_begin + i) * kBK;
+        if constexpr (kATma) tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+          tma_load_2d(b_hi(s) + c * TileGeom<BN>::kBChunkBytes, &tmB, &full[s], n0 + 32 * c, k0);
+        ++issued;
+      }
+      if (*abort_flag) {
+        // Drain: wait (bounded, ignoring the abort flag) for the last copy
+        // issued into each stage, so no bulk copy lands in shared memory
+        // after the CTA has exited.
+        volatile int no_abort = 0;
+        const WaitCtx drain{&no_abort, p.status, p.wait_limit_ns, kWaitDrain};
+        for (int i = (issued > STAGES ? issued - STAGES : 0); i < issued; ++i)
+          mbar_wait(&full[i % STAGES], (i / STAGES) & 1, drain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      for (int i = 0; i < num_kb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!mbar_wait(&ready[s], ph, wmma)) break;
+        tc_fence_after_sync();
+        const uint32_t sa = smem_u32(a_hi(s));
+        const uint32_t sb = smem_u32(b_hi(s));
+#pragma unroll
+        for (int kk = 0; kk < kBK / 8; ++kk) {
+          // A: K-major, 64-byte rows, 8-row groups 512 B apart; a k-step of
+          // 8 tf32 is 32 bytes along the row.
+          const uint64_t da = make_smem_desc(sa + kk * 32, 16, 512, kLayoutSw64);
+          // B: MN-major, 32-column boxes 2048 B apart (LBO), k-rows 128 B
+          // apart in 4-row swizzle atoms 512 B apart (SBO); a k-step of 8
+          // rows is 1024 B.
+          const uint64_t db = make_smem_desc(sb + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma_tf32(tmem_base, da, db, kIdesc, acc);
+          if constexpr (SPLIT3) {
+            const uint32_t sal = smem_u32(a_lo(s));
+            const uint32_t sbl = smem_u32(b_lo(s));
+            const uint64_t dal = make_smem_desc(sal + kk * 32, 16, 512, kLayoutSw64);
+            const uint64_t dbl =
+                make_smem_desc(sbl + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
+            umma_tf32(tmem_base, da, dbl, kIdesc, 1u);
+            umma_tf32(tmem_base, dal, db, kIdesc, 1u);
+          }
+        }
+        umma_commit(&empty[s]);
+        if (tr && i == 0) {
+          const uint64_t da = make_smem_desc(sa, 16, 512, kLayoutSw64);
+          const uint64_t db = make_smem_desc(sb, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
+          p.trace[kTrDescA] = static_cast<uint32_t>(da);
+          p.trace[kTrDescA + 1] = static_cast<uint32_t>(da >> 32);
+          p.trace[kTrDescB] = static_cast<uint32_t>(db);
+          p.trace[kTrDescB + 1] = static_cast<uint32_t>(db >> 32);
+          p.trace[kTrIdesc] = kIdesc;
+        }
+        if (tr) p.trace[kTrMmas] = static_cast<uint32_t>(i + 1);
+      }
+      // Signals the epilogue; on abort it still fires once every MMA issued
+      // so far has finished.  The issuer waits for it too (bounded, ignoring
+      // the abort flag) so tensor memory is quiescent before it is freed.
+      umma_commit(accum_full);
+      volatile int no_abort = 0;
+      const WaitCtx drain{&no_abort, p.status, p.wait_limit_ns, kWaitDrain};
+      mbar_wait(accum_full, 0, drain);
+    }
+  } else {
+    // ------------------------------------------------------------ transform
+    const int t = threadIdx.x - 64;  // 0..127
+    const int tw = t >> 5;           // transform warp 0..3
+    bool ok = true;
+    for (int i = 0; i < num_kb && ok; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1;
+      // Warp-uniform outcome: the tcgen05.ld below is .sync.aligned, so the
+      // lanes of a warp must never take different paths.
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) {
+        ok = false;
+        break;
+      }
+      const int k0 = (kb_begin + i) * kBK;
+      if constexpr (!kATma) {
+        // Build the structured A tile: 16 lanes per row (one k each), two
+        // rows per warp instruction, 32 rows per warp.
+        const int kl = lane & 15;
+        uint8_t* ah = a_hi(s);
+        uint8_t* al = a_lo(s);
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+          const int r = tw * 32 + it * 2 + (lane >> 4);
+          const float v = a_value<AK>(p.a_src, p.a_dim, p.a_row0 + m0 + r, k0 + kl);
+          const uint32_t off = swz_offset(r, kl >> 2, 64) + (kl & 3) * 4;
+          const float hi = tf32_hi(v);
+          *reinterpret_cast<float*>(ah + off) = hi;
+          if constexpr (SPLIT3) *reinterpret_cast<float*>(al + off) = v - hi;
+        }
+      } else if constexpr (SPLIT3) {
+        const float4* src = reinterpret_cast<const float4*>(a_hi(s));
+        float4* dst = reinterpret_cast<float4*>(a_lo(s));
+#pragma unroll
+        for (int j = t; j < kATileBytes / 16; j += 128) {
+          const float4 x = src[j];
+          dst[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+        }
+      }
+      if constexpr (SPLIT3) {
+        const float4* src = reinterpret_cast<const float4*>(b_hi(s));
+        float4* dst = reinterpret_cast<float4*>(b_lo(s));
+#pragma unroll
+        for (int j = t; j < kBTile / 16; j += 128) {
+          const float4 x = src[j];
+          dst[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+        }
+      }
+      if (tr && i == 0 && t == 0) {
+        for (int j = 0; j < 8; ++j) {
+          p.trace[kTrA + j] = reinterpret_cast<const uint32_t*>(a_hi(s))[j];
+          p.trace[kTrB + j] = reinterpret_cast<const uint32_t*>(b_hi(s))[j];
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&ready[s]);
+    }
+
+    // ------------------------------------------------------------ epilogue
+    const bool acc_ok = __all_sync(0xffffffffu, ok && mbar_wait(accum_full, 0, wepi) && !*abort_flag);
+    if (tr && t == 0) p.trace[kTrAccOk] = acc_ok ? 1u : 0u;
+    if (acc_ok) {
+      tc_fence_after_sync();
+      const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to this warp
+      const int row = m0 + q * 32 + lane;
+      const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+      float* crow = p.C + static_cast<long long>(row) * p.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c, r);
+        tmem_wait_ld();
+        if (tr && q == 0 && lane == 0 && c == 0)
+          for (int j = 0; j < 16; ++j) p.trace[kTrAcc + j] = r[j];
+        const int col = n0 + c;
+        if (row < p.M) {
+          if (vec && col + 16 <= p.N) {
+            float4* dst = reinterpret_cast<float4*>(crow + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          } else {
+#pragma unroll
+            for (int v = 0; v < 16; ++v)
+              if (col + v < p.N) crow[col + v] = __uint_as_float(r[v]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace smm

@@ -1,0 +1,185 @@
+"""Tensor-level API over libsmm: each function takes torch CUDA tensors
+(row-major fp32, contiguous), calls one C ABI entry point on the current
+stream, and returns the output tensor.
+
+Storage conventions follow the reference DSL (src/dsl/layout_functions.py):
+packed upper / symmetric operands are the row-major upper triangle
+(``torch.triu_indices`` order), diagonals are length-N vectors and Toeplitz
+matrices are their 2N-1 generator with ``T[i][j] = g[(N-1) + (j-i)]``.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_ws_cache = {}
+
+
+def _stream_ptr(stream: Optional[torch.cuda.Stream]) -> Optional[int]:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream or None
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _check_f32(name: str, t: torch.Tensor, numel: Optional[int] = None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32, got {t.dtype}")
+    if not t.is_contiguous():
+        t = t.contiguous()
+    if numel is not None and t.numel() != numel:
+        raise ValueError(f"{name} has {t.numel()} elements, expected {numel}")
+    return t
+
+
+def _mode(mode: str) -> int:
+    try:
+        return _lib.MODES[mode]
+    except KeyError:
+        raise ValueError(f"unknown mode {mode!r}; expected one of {sorted(_lib.MODES)}") from None
+
+
+def workspace(nbytes: int, device: torch.device) -> Optional[torch.Tensor]:
+    """A cached device buffer of at least nbytes (grown on demand)."""
+    if nbytes <= 0:
+        return None
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
+
+
+def _ws_args(nbytes: int, device: torch.device):
+    buf = workspace(nbytes, device)
+    return (buf.data_ptr(), buf.numel()) if buf is not None else (None, 0)
+
+
+def _out(out: Optional[torch.Tensor], shape, like: torch.Tensor) -> torch.Tensor:
+    if out is None:
+        return torch.empty(shape, dtype=torch.float32, device=like.device)
+    out = _check_f32("out", out)
+    if tuple(out.shape) != tuple(shape) and out.numel() != int(torch.tensor(shape).prod()):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {tuple(shape)}")
+    return out
+
+
+def diag_rows(d: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """C = diag(d) @ B (row scale), bit-exact single fp32 multiply."""
+    B = _check_f32("B", B)
+    M, N = B.shape
+    d = _check_f32("d", d, M)
+    C = _out(out, (M, N), B)
+    _lib.check(_lib.load().smm_diag_rows(_ptr(d), _ptr(B), _ptr(C), M, N, _stream_ptr(stream)), "smm_diag_rows")
+    return C
+
+
+def diag_cols(A: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """C = A @ diag(b) (column scale)."""
+    A = _check_f32("A", A)
+    M, N = A.shape
+    b = _check_f32("b", b, N)
+    C = _out(out, (M, N), A)
+    _lib.check(_lib.load().smm_diag_cols(_ptr(A), _ptr(b), _ptr(C), M, N, _stream_ptr(stream)), "smm_diag_cols")
+    return C
+
+
+def gemm(A: torch.Tensor, B: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+         stream=None) -> torch.Tensor:
+    """C = A @ B."""
+    A = _check_f32("A", A)
+    B = _check_f32("B", B)
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_gemm_workspace_size(M, N, K, m), A.device)
+    C = _out(out, (M, N), A)
+    _lib.check(L.smm_gemm(_ptr(A), _ptr(B), _ptr(C), M, N, K, m, ws, wsb, _stream_ptr(stream)), "smm_gemm")
+    return C
+
+
+def upper_left(U: torch.Tensor, B: torch.Tensor, packed: bool = True, mode: str = "3xtf32",
+               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """C = U @ B with U upper triangular, packed (N(N+1)/2) or dense N x N
+    with exact zeros below the diagonal."""
+    B = _check_f32("B", B)
+    N, ncols = B.shape
+    U = _check_f32("U", U, N * (N + 1) // 2 if packed else N * N)
+    fmt = _lib.FMT_PACKED if packed else _lib.FMT_DENSE
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_upper_left_workspace_size(N, ncols, fmt, m), B.device)
+    C = _out(out, (N, ncols), B)
+    _lib.check(L.smm_upper_left(_ptr(U), fmt, _ptr(B), _ptr(C), N, ncols, m, ws, wsb, _stream_ptr(stream)),
+               "smm_upper_left")
+    return C
+
+
+def toeplitz_left(g: torch.Tensor, B: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+                  stream=None) -> torch.Tensor:
+    """C = T @ B, T the Toeplitz matrix of generator g (2N-1)."""
+    B = _check_f32("B", B)
+    N, ncols = B.shape
+    g = _check_f32("g", g, 2 * N - 1)
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_toeplitz_left_workspace_size(N, ncols, m), B.device)
+    C = _out(out, (N, ncols), B)
+    _lib.check(L.smm_toeplitz_left(_ptr(g), _ptr(B), _ptr(C), N, ncols, m, ws, wsb, _stream_ptr(stream)),
+               "smm_toeplitz_left")
+    return C
+
+
+def symm_left(S: torch.Tensor, B: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+              stream=None) -> torch.Tensor:
+    """C = S @ B, S symmetric given packed upper."""
+    B = _check_f32("B", B)
+    N, ncols = B.shape
+    S = _check_f32("S", S, N * (N + 1) // 2)
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_symm_left_workspace_size(N, ncols, m), B.device)
+    C = _out(out, (N, ncols), B)
+    _lib.check(L.smm_symm_left(_ptr(S), _ptr(B), _ptr(C), N, ncols, m, ws, wsb, _stream_ptr(stream)),
+               "smm_symm_left")
+    return C
+
+
+def symm_sandwich(A: torch.Tensor, S: torch.Tensor, B: torch.Tensor, mode: str = "3xtf32",
+                  out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """C = A @ S @ B, S symmetric given packed upper, all N x N."""
+    A = _check_f32("A", A)
+    N = A.shape[0]
+    if tuple(A.shape) != (N, N):
+        raise ValueError("A must be square")
+    B = _check_f32("B", B, N * N)
+    S = _check_f32("S", S, N * (N + 1) // 2)
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_symm_sandwich_workspace_size(N, m), A.device)
+    C = _out(out, (N, N), A)
+    _lib.check(L.smm_symm_sandwich(_ptr(A), _ptr(S), _ptr(B), _ptr(C), N, m, ws, wsb, _stream_ptr(stream)),
+               "smm_symm_sandwich")
+    return C
+
+
+def device_status(stream=None) -> None:
+    """Raise SmmError(SMM_ERR_DEVICE_TIMEOUT) if a kernel gave up a bounded wait."""
+    _lib.check(_lib.load().smm_device_status(_stream_ptr(stream)), "smm_device_status")
+
+
+def launch_count() -> int:
+    return int(_lib.load().smm_launch_count())

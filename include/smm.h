@@ -1,0 +1,161 @@
+/* smm.h — C ABI of libsmm, the B200 (sm_100a) structured matrix-multiply library.
+ *
+ * Plain pointers and sizes only.  Every matrix is row-major fp32 in device
+ * memory owned by the caller; the library never allocates user outputs.
+ * Every entry point returns an smm_status and never exits the process; the
+ * thread-local text of the last failure is available from smm_last_error().
+ * Calls are asynchronous on the given stream (NULL = the legacy default
+ * stream) unless stated otherwise.
+ *
+ * Storage conventions, as defined by the reference DSL
+ * (src/dsl/layout_functions.py) and its CUDA runner (src/dsl/runner_cuda.py):
+ *   packed upper / symmetric  row-major upper triangle incl. diagonal,
+ *                             idx(i,j) = i*N - i*(i-1)/2 + (j-i) for i <= j,
+ *                             N*(N+1)/2 floats (layout_functions.py:8-23,
+ *                             50-68; runner_cuda.py:96-97)
+ *   diagonal                  N floats (layout_functions.py:38-43;
+ *                             runner_cuda.py:98-99)
+ *   Toeplitz                  2N-1 generator, T[i][j] = g[(N-1) + (j-i)]
+ *                             (layout_functions.py:45-48; Cuda
+ *                             kernels/toeplitz.cu:91, 255-262)
+ *
+ * Arithmetic modes of the tensor-core contractions:
+ *   SMM_MODE_3XTF32  fp32 semantics: each operand x = hi + lo with
+ *                    hi = tf32(x), lo = x - hi; C = hi*hi + hi*lo + lo*hi,
+ *                    fp32 accumulation in tensor memory (3 MMA passes)
+ *   SMM_MODE_TF32    one TF32 pass (fast, ~1e-3 relative)
+ *   SMM_MODE_BF16    operands rounded to bf16 (inside the call), fp32
+ *                    accumulation
+ */
+#ifndef SMM_H
+#define SMM_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SMM_OK = 0,
+  SMM_ERR_INVALID = 1,        /* bad pointer, shape, mode or format */
+  SMM_ERR_CUDA = 2,           /* a CUDA runtime/driver call failed */
+  SMM_ERR_NCCL = 3,           /* reserved for the multi-GPU layer */
+  SMM_ERR_DEVICE_TIMEOUT = 4, /* a kernel's bounded wait expired; the kernel exited cleanly */
+  SMM_ERR_WORKSPACE = 5,      /* caller workspace missing or too small */
+  SMM_ERR_UNSUPPORTED = 6     /* device is not sm_100 or feature not built */
+} smm_status;
+
+typedef enum { SMM_MODE_3XTF32 = 0, SMM_MODE_TF32 = 1, SMM_MODE_BF16 = 2 } smm_mode;
+typedef enum { SMM_FMT_PACKED = 0, SMM_FMT_DENSE = 1 } smm_format;
+
+/* ---- library ---------------------------------------------------------- */
+
+/* Thread-local message describing the last non-OK status ("" if none). */
+const char* smm_last_error(void);
+/* Library version as 10000*major + 100*minor + patch. */
+int smm_version(void);
+/* Number of kernel launches this library has issued in this process. */
+unsigned long long smm_launch_count(void);
+/* Synchronises `stream`, then reads and clears this device's sticky kernel
+ * status word: SMM_ERR_DEVICE_TIMEOUT if any kernel since the last call gave
+ * up a bounded wait (it then wrote no output and exited cleanly), else SMM_OK. */
+int smm_device_status(void* stream);
+
+/* ---- diagonal scaling (HBM-bound, no tensor cores, bit-exact) ---------- */
+
+/* C[i][j] = d[i] * B[i][j], B and C M x N (ldb = ldc = N).  One fp32 multiply
+ * per element, no contraction.  Replaces kernel_diag_x_gen + its wrapper
+ * (src/dsl/codegen_cuda.py:1253-1332), the DSL's DiagonalMatrix @
+ * GeneralMatrix. */
+int smm_diag_rows(const float* d, const float* B, float* C, int M, int N, void* stream);
+
+/* C[i][j] = A[i][j] * b[j] (column scale).  Replaces kernel_gen_x_diag
+ * (src/dsl/codegen_cuda.py:808-964) and gemm_diag (Cuda kernels/diagonal.cu:44-148). */
+int smm_diag_cols(const float* A, const float* b, float* C, int M, int N, void* stream);
+
+/* Row scale with HOST (ideally pinned) buffers: copies d and B in, scales and
+ * copies C out in row chunks on two internal streams so the transfers in
+ * both directions overlap each other and the kernel.  Synchronous.  dev_ws
+ * must hold smm_diag_rows_host_workspace_size(M, N) bytes of device memory. */
+size_t smm_diag_rows_host_workspace_size(int M, int N);
+int smm_diag_rows_host(const float* d_host, const float* B_host, float* C_host, int M, int N, void* dev_ws,
+                       size_t ws_bytes);
+
+/* ---- tensor-core contractions (tcgen05 + TMEM, TMA-fed) ---------------- */
+
+/* Workspace (device bytes) an entry point needs for the given shape/mode;
+ * 0 means none.  Passing a larger workspace is always allowed. */
+size_t smm_gemm_workspace_size(int M, int N, int K, int mode);
+size_t smm_upper_left_workspace_size(int N, int ncols, int u_fmt, int mode);
+size_t smm_toeplitz_left_workspace_size(int N, int ncols, int mode);
+size_t smm_symm_sandwich_workspace_size(int N, int mode);
+size_t smm_symm_left_workspace_size(int N, int ncols, int mode);
+
+/* C(MxN) = A(MxK) B(KxN).  Replaces kernel_gen_x_gen + wrapper
+ * (src/dsl/codegen_cuda.py:62-278) and KernelOptimized::run
+ * (Cuda kernels/gemmoptimized.cu:249-272). */
+int smm_gemm(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* ws, size_t ws_bytes,
+             void* stream);
+
+/* C(N x ncols) = U(NxN upper) B(N x ncols).  u_fmt SMM_FMT_PACKED: U packed
+ * upper (N(N+1)/2 floats); SMM_FMT_DENSE: U a dense N x N array whose strict
+ * lower part is exactly zero (never read).  All-zero tiles of U are skipped;
+ * only diagonal tiles are masked.  Left-side counterpart of kernel_gen_x_upper
+ * (src/dsl/codegen_cuda.py:280-544) and Cuda kernels/upper.cu:177-313, which
+ * compute A*U. */
+int smm_upper_left(const float* U, int u_fmt, const float* B, float* C, int N, int ncols, int mode, void* ws,
+                   size_t ws_bytes, void* stream);
+
+/* C(N x ncols) = T B, T the N x N Toeplitz matrix of generator g[2N-1].  The
+ * generator is expanded on chip; HBM traffic is B and C only.  Left-side
+ * counterpart of gemm_toeplitz_double_buffer (Cuda kernels/toeplitz.cu:158-253),
+ * which computes A*T; the DSL has no CUDA lowering for ToeplitzMatrix
+ * (src/dsl/codegen_cuda.py:1681-1682). */
+int smm_toeplitz_left(const float* g, const float* B, float* C, int N, int ncols, int mode, void* ws,
+                      size_t ws_bytes, void* stream);
+
+/* C(N x ncols) = S B, S symmetric given packed upper, mirrored on chip.
+ * Replaces kernel_symm_x_gen (src/dsl/codegen_cuda.py:973-1245). */
+int smm_symm_left(const float* S_packed, const float* B, float* C, int N, int ncols, int mode, void* ws,
+                  size_t ws_bytes, void* stream);
+
+/* Row slabs of the three structured products, for partitioning a product
+ * by output rows (one slab per GPU): C (nrows x ncols) = X[row0 : row0+nrows, :] B,
+ * X being the N x N upper-triangular / Toeplitz / symmetric operand.  The
+ * full-matrix entry points above are the slab [0, N).  For the triangular
+ * operand a slab's K range starts at row0 (zero tiles are never visited). */
+int smm_upper_left_rows(const float* U, int u_fmt, const float* B, float* C, int N, int ncols, int row0, int nrows,
+                        int mode, void* ws, size_t ws_bytes, void* stream);
+int smm_toeplitz_left_rows(const float* g, const float* B, float* C, int N, int ncols, int row0, int nrows,
+                           int mode, void* ws, size_t ws_bytes, void* stream);
+int smm_symm_left_rows(const float* S_packed, const float* B, float* C, int N, int ncols, int row0, int nrows,
+                       int mode, void* ws, size_t ws_bytes, void* stream);
+
+/* C = A S B (all N x N, S packed upper symmetric), computed as A (S B) with
+ * the intermediate in the workspace.  Replaces the two launches
+ * src/dsl/runner_cuda.py:147-197 run_graph makes for A@S@B
+ * (kernel_gen_x_symm, src/dsl/codegen_cuda.py:546-806, then kernel_gen_x_gen). */
+int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, float* C, int N, int mode, void* ws,
+                      size_t ws_bytes, void* stream);
+
+/* ---- failure-detection probe ------------------------------------------- */
+
+/* Launches one CTA that waits on a shared-memory barrier nothing ever
+ * arrives on, with the given wait limit (ns), exactly like the pipeline
+ * waits in the contraction kernels.  Returns SMM_ERR_DEVICE_TIMEOUT when the
+ * limit expired and the kernel exited cleanly (the expected outcome); used
+ * to test the timeout path without faulting or hanging the GPU. */
+int smm_debug_timeout_probe(unsigned long long wait_limit_ns, void* stream);
+
+/* Diagnostic: the next tensor-core contraction launched from the calling
+ * thread records the state of its first CTA into `trace` (64 device words:
+ * tensor-memory base, k-block count, first staged operand words, matrix and
+ * instruction descriptors, first accumulator words).  NULL disables. */
+int smm_debug_trace_next(unsigned* trace);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMM_H */

@@ -1,0 +1,72 @@
+"""The C-ABI library loads and exports exactly what include/smm.h declares,
+and rejects invalid arguments on the host (no kernel is launched).  CPU only."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from cpp1_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "smm.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(smm_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_binding_table():
+    assert declared_functions() == sorted(name for name, _, _ in _lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    L = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [f for f in declared_functions() if not hasattr(L, f)]
+    assert not missing, missing
+
+
+def test_version_and_error_text():
+    L = _lib.load()
+    assert L.smm_version() >= 100
+    assert isinstance(_lib.last_error(), str)
+
+
+@pytest.mark.parametrize("call", [
+    lambda L: L.smm_gemm(None, None, None, -1, 4, 4, 0, None, 0, None),
+    lambda L: L.smm_gemm(None, None, None, 4, 4, 4, 7, None, 0, None),
+    lambda L: L.smm_gemm(None, None, None, 4, 4, 4, 0, None, 0, None),
+    lambda L: L.smm_diag_rows(None, None, None, -3, 2, None),
+    lambda L: L.smm_diag_rows(None, None, None, 3, 2, None),
+    lambda L: L.smm_upper_left(None, 5, None, None, 4, 4, 0, None, 0, None),
+    lambda L: L.smm_upper_left_rows(None, 0, None, None, 8, 4, 6, 4, 0, None, 0, None),
+    lambda L: L.smm_toeplitz_left(None, None, None, -1, 4, 0, None, 0, None),
+    lambda L: L.smm_symm_sandwich(None, None, None, None, 4, 9, None, 0, None),
+])
+def test_invalid_arguments_rejected_on_host(call):
+    L = _lib.load()
+    assert call(L) == _lib.SMM_ERR_INVALID
+    assert _lib.last_error()
+
+
+def test_empty_shapes_are_noops():
+    L = _lib.load()
+    assert L.smm_gemm(None, None, None, 0, 5, 5, 0, None, 0, None) == _lib.SMM_OK
+    assert L.smm_diag_rows(None, None, None, 0, 0, None) == _lib.SMM_OK
+    assert L.smm_toeplitz_left(None, None, None, 0, 0, 0, None, 0, None) == _lib.SMM_OK
+
+
+def test_workspace_queries_are_host_only():
+    L = _lib.load()
+    assert L.smm_gemm_workspace_size(0, 4, 4, 0) == 0
+    assert L.smm_gemm_workspace_size(128, 128, 128, 0) >= 0
+    assert L.smm_symm_sandwich_workspace_size(4096, 0) >= 4096 * 4096 * 4
+    assert L.smm_diag_rows_host_workspace_size(8192, 8192) >= 8192 * 4
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "absent.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _lib.load()

@@ -1,0 +1,182 @@
+"""GPU parity of every operation against the oracle (the reference's own CPU
+kernels' outputs in tests/golden, and the fp64 recomputation of oracle.c).
+
+Tolerances (normwise relative error against fp64):
+  3xtf32  <= 1e-5   (fp32 semantics)
+  tf32    <= 5e-3   (one TF32 pass)
+  bf16    <= 1e-2
+The diagonal scale is bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from cpp1_b200 import ops
+from cpp1_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"3xtf32": 1e-5, "tf32": 5e-3, "bf16": 1e-2}
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+# ---------------------------------------------------------------- diagonal
+def test_diag_rows_golden_bitexact(cuda, golden):
+    C = host(ops.diag_rows(dev(golden["diag_d"]), dev(golden["diag_B"])))
+    assert np.array_equal(C, golden["diag_C"])
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (3, 5), (7, 129), (64, 4100), (129, 257), (8192, 8192)])
+def test_diag_rows_bitexact(cuda, shape):
+    M, N = shape
+    w = W.make_diag(M, N, seed=M * 31 + N)
+    C = host(ops.diag_rows(dev(w["d"]), dev(w["B"])))
+    assert np.array_equal(C, O.diag_rows_f32(w["d"], w["B"]))
+
+
+@pytest.mark.parametrize("shape", [(5, 3), (128, 256), (77, 1030)])
+def test_diag_cols_bitexact(cuda, shape):
+    M, N = shape
+    rng = np.random.default_rng(7)
+    A = rng.uniform(-1, 1, (M, N)).astype(np.float32)
+    b = rng.uniform(0.5, 1.5, N).astype(np.float32)
+    C = host(ops.diag_cols(dev(A), dev(b)))
+    assert np.array_equal(C, O.diag_cols_f32(A, b))
+
+
+def test_diag_rows_unaligned_views(cuda):
+    # Offset views (not 16-byte aligned) take the scalar path.
+    w = W.make_diag(33, 67, seed=3)
+    Bbig = dev(np.concatenate([np.zeros(1, np.float32), w["B"].ravel()]))
+    B = Bbig[1:].view(33, 67)
+    out = torch.empty(33 * 67 + 1, device="cuda")[1:].view(33, 67)
+    C = host(ops.diag_rows(dev(w["d"]), B, out=out))
+    assert np.array_equal(C, O.diag_rows_f32(w["d"], w["B"]))
+
+
+# ---------------------------------------------------------------- contractions
+def _relerr_full(C, R):
+    return O.relerr(C, R)
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+def test_gemm_golden(cuda, golden, mode):
+    A, B = golden["gemm_A"], golden["gemm_B"]
+    C = host(ops.gemm(dev(A), dev(B), mode=mode))
+    R = O.gemm_rows_f64(A, B, np.arange(A.shape[0]))
+    assert _relerr_full(C, R) <= TOL[mode]
+    # The reference's own kernel meets the same bound on the same inputs.
+    assert O.relerr(golden["gemm_C"], R) <= 1e-5
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+@pytest.mark.parametrize("mnk", [(128, 256, 64), (256, 512, 1024), (1, 1, 1), (7, 5, 3), (129, 257, 127),
+                                 (300, 200, 100), (1024, 1024, 1024)])
+def test_gemm_shapes(cuda, mode, mnk):
+    M, N, K = mnk
+    w = W.make_gemm(M, N, K, seed=M + 7 * N + 13 * K)
+    C = host(ops.gemm(dev(w["A"]), dev(w["B"]), mode=mode))
+    R = O.gemm_rows_f64(w["A"], w["B"], np.arange(M))
+    assert _relerr_full(C, R) <= TOL[mode], (mnk, _relerr_full(C, R))
+
+
+def test_tf32_operand_reading_truncates(cuda):
+    """kind::tf32 must ignore the 13 low mantissa bits of an fp32 operand
+    (truncation): the 3xTF32 split relies on hi = raw bits & 0xffffe000.
+    x = 1 + 3*2^-12 truncates to 1 and rounds to 1 + 2^-10."""
+    x = np.float32(1.0 + 3.0 * 2.0 ** -12)
+    A = np.full((128, 8), x, np.float32)
+    B = np.zeros((8, 64), np.float32)
+    B[0, :] = 1.0
+    C = host(ops.gemm(dev(A), dev(B), mode="tf32"))
+    assert np.all(C == 1.0), np.unique(C)
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+def test_upper_packed_golden(cuda, golden, mode):
+    Up, B = golden["upper_U"], golden["upper_B"]
+    C = host(ops.upper_left(dev(Up), dev(B), packed=True, mode=mode))
+    R = O.upper_left_rows_f64(Up, B, np.arange(B.shape[0]))
+    assert _relerr_full(C, R) <= TOL[mode]
+    assert O.relerr(golden["upper_C"], R) <= 1e-5
+
+
+@pytest.mark.parametrize("packed", [True, False])
+@pytest.mark.parametrize("n_cols", [(1, 1), (5, 9), (128, 64), (129, 200), (300, 260), (1024, 1024)])
+def test_upper_shapes(cuda, packed, n_cols):
+    N, ncols = n_cols
+    w = W.make_upper(N, ncols, seed=N + ncols)
+    U = w["U"] if packed else W.unpack_upper(w["U"], N)
+    C = host(ops.upper_left(dev(U), dev(w["B"]), packed=packed))
+    R = O.upper_left_rows_f64(w["U"], w["B"], np.arange(N))
+    assert _relerr_full(C, R) <= 1e-5, (n_cols, _relerr_full(C, R))
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+def test_toeplitz_golden(cuda, golden, mode):
+    g, B = golden["toeplitz_g"], golden["toeplitz_B"]
+    C = host(ops.toeplitz_left(dev(g), dev(B), mode=mode))
+    R = O.toeplitz_left_rows_f64(g, B, np.arange(B.shape[0]))
+    assert _relerr_full(C, R) <= TOL[mode]
+    assert O.relerr(golden["toeplitz_C"], R) <= 1e-5
+
+
+@pytest.mark.parametrize("n_cols", [(1, 1), (3, 8), (128, 64), (130, 70), (512, 1024)])
+def test_toeplitz_shapes(cuda, n_cols):
+    N, ncols = n_cols
+    w = W.make_toeplitz(N, ncols, seed=N * 3 + ncols)
+    C = host(ops.toeplitz_left(dev(w["g"]), dev(w["B"])))
+    R = O.toeplitz_left_rows_f64(w["g"], w["B"], np.arange(N))
+    assert _relerr_full(C, R) <= 1e-5, (n_cols, _relerr_full(C, R))
+
+
+@pytest.mark.parametrize("n_cols", [(1, 1), (6, 10), (128, 128), (257, 130)])
+def test_symm_left_shapes(cuda, n_cols):
+    N, ncols = n_cols
+    s = W.make_sandwich(N, seed=N)
+    B = W.make_gemm(N, ncols, 1, seed=ncols)["A"]  # any N x ncols matrix
+    C = host(ops.symm_left(dev(s["S"]), dev(B)))
+    S = W.unpack_symmetric(s["S"], N).astype(np.float64)
+    R = S @ B.astype(np.float64)
+    assert _relerr_full(C, R) <= 1e-5
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+def test_sandwich_golden(cuda, golden, mode):
+    A, S, B = golden["sandwich_A"], golden["sandwich_S"], golden["sandwich_B"]
+    C = host(ops.symm_sandwich(dev(A), dev(S), dev(B), mode=mode))
+    R = O.sandwich_rows_f64(A, S, B, np.arange(A.shape[0]))
+    assert _relerr_full(C, R) <= TOL[mode]
+    assert O.relerr(golden["sandwich_C"], R) <= 1e-5
+
+
+@pytest.mark.parametrize("N", [1, 7, 130, 512])
+def test_sandwich_shapes(cuda, N):
+    s = W.make_sandwich(N, seed=N + 1)
+    C = host(ops.symm_sandwich(dev(s["A"]), dev(s["S"]), dev(s["B"])))
+    R = O.sandwich_rows_f64(s["A"], s["S"], s["B"], np.arange(N))
+    assert _relerr_full(C, R) <= 1e-5
+
+
+# ---------------------------------------------------------------- failure detection
+def test_timeout_probe_returns_status_and_context_survives(cuda):
+    from cpp1_b200 import _lib
+    L = _lib.load()
+    rc = L.smm_debug_timeout_probe(50_000_000, None)  # 50 ms
+    assert rc == _lib.SMM_ERR_DEVICE_TIMEOUT, _lib.last_error()
+    # The status word was consumed; the context still works.
+    ops.device_status()
+    w = W.make_gemm(128, 128, 32, seed=1)
+    C = host(ops.gemm(dev(w["A"]), dev(w["B"])))
+    R = O.gemm_rows_f64(w["A"], w["B"], np.arange(128))
+    assert O.relerr(C, R) <= 1e-5
+    ops.device_status()

@@ -1,0 +1,110 @@
+"""The oracle pinned against the reference: the C restatement (oracle.c)
+reproduces, bit for bit, the outputs of the reference's own CPU kernels
+stored in tests/golden/golden_outputs.npz (made by tests/golden/make_golden.py
+from oracle/_ref), and the storage conventions match the reference DSL's
+layout functions (golden_layouts.npz).  CPU only."""
+import numpy as np
+import pytest
+
+import oracle as O
+from cpp1_b200 import workloads as W
+from cpp1_b200.dsl import layout_functions as LF
+from cpp1_b200.dsl.var import Var, evaluate
+
+
+def test_gemm_restatement_bitexact(golden):
+    assert np.array_equal(O.gemm_f32(golden["gemm_A"], golden["gemm_B"]), golden["gemm_C"])
+
+
+def test_diag_restatement_bitexact(golden):
+    assert np.array_equal(O.diag_rows_f32(golden["diag_d"], golden["diag_B"]), golden["diag_C"])
+
+
+def test_upper_restatement_bitexact(golden):
+    assert np.array_equal(O.upper_left_f32(golden["upper_U"], golden["upper_B"]), golden["upper_C"])
+
+
+def test_sandwich_restatement_bitexact(golden):
+    C = O.sandwich_f32(golden["sandwich_A"], golden["sandwich_S"], golden["sandwich_B"])
+    assert np.array_equal(C, golden["sandwich_C"])
+
+
+def test_toeplitz_restatement_bitexact(golden):
+    assert np.array_equal(O.toeplitz_left_f32(golden["toeplitz_g"], golden["toeplitz_B"]), golden["toeplitz_C"])
+
+
+@pytest.mark.parametrize("op", ["gemm", "upper", "sandwich", "toeplitz"])
+def test_reference_outputs_meet_fp32_bound(golden, op):
+    """The reference's own results are within the 1e-5 normwise bound of the
+    fp64 recomputation (the bound the library's 3xTF32 mode is held to)."""
+    if op == "gemm":
+        R = O.gemm_rows_f64(golden["gemm_A"], golden["gemm_B"], np.arange(golden["gemm_A"].shape[0]))
+    elif op == "upper":
+        R = O.upper_left_rows_f64(golden["upper_U"], golden["upper_B"], np.arange(golden["upper_B"].shape[0]))
+    elif op == "sandwich":
+        R = O.sandwich_rows_f64(golden["sandwich_A"], golden["sandwich_S"], golden["sandwich_B"],
+                                np.arange(golden["sandwich_A"].shape[0]))
+    else:
+        R = O.toeplitz_left_rows_f64(golden["toeplitz_g"], golden["toeplitz_B"],
+                                     np.arange(golden["toeplitz_B"].shape[0]))
+    assert O.relerr(golden[f"{op}_C"], R) <= 1e-5
+
+
+def test_fp64_rows_match_dense_numpy():
+    w = W.make_upper(37, 11, seed=5)
+    R = O.upper_left_rows_f64(w["U"], w["B"], np.arange(37))
+    U = W.unpack_upper(w["U"], 37).astype(np.float64)
+    assert np.allclose(R, U @ w["B"].astype(np.float64), rtol=0, atol=1e-12)
+    t = W.make_toeplitz(29, 6, seed=2)
+    R = O.toeplitz_left_rows_f64(t["g"], t["B"], np.arange(29))
+    assert np.allclose(R, W.toeplitz_dense(t["g"], 29).astype(np.float64) @ t["B"], rtol=0, atol=1e-12)
+
+
+def test_relerr_detects_planted_error(golden):
+    """A single perturbed element in an oracle output is caught by the
+    tolerance the GPU tests use (the mistake is planted on the CPU)."""
+    A, B = golden["gemm_A"], golden["gemm_B"]
+    R = O.gemm_rows_f64(A, B, np.arange(A.shape[0]))
+    C = O.gemm_f32(A, B).copy()
+    C[5, 7] += 0.05
+    assert O.relerr(C, R) > 1e-5
+
+
+# ---------------------------------------------------------------- layouts
+def _index_of(expr):
+    """Storage index an element expression selects, or -1 for a structural zero."""
+    from cpp1_b200.dsl.var import ArithmeticExpression, Conditional
+    if isinstance(expr, Conditional):
+        return _index_of(expr.true_value if evaluate(expr.condition, {}) else expr.false_value)
+    if isinstance(expr, int):
+        return -1 if expr == 0 else expr
+    assert isinstance(expr, ArithmeticExpression) and expr.op == "subscript", expr
+    return evaluate(expr.right, {})
+
+
+def _layout_map(fn, n):
+    return np.array([[_index_of(fn(i, j, Var("X_data"), n)) for j in range(n)] for i in range(n)], np.int64)
+
+
+@pytest.mark.parametrize("name", ["general", "upper_triangular", "lower_triangular", "diagonal", "toeplitz",
+                                  "symmetric"])
+def test_layouts_match_reference_dsl(golden_layouts, name):
+    n = int(golden_layouts["layout_n"])
+    mine = _layout_map(getattr(LF, f"{name}_layout"), n)
+    assert np.array_equal(mine, golden_layouts[f"layout_{name}"])
+
+
+def test_workload_packing_matches_reference_layouts(golden_layouts):
+    n = int(golden_layouts["layout_n"])
+    M = np.arange(n * n, dtype=np.float32).reshape(n, n)
+    p = W.pack_upper(M)
+    ref = golden_layouts["layout_upper_triangular"]
+    for i in range(n):
+        for j in range(n):
+            if ref[i, j] >= 0:
+                assert p[ref[i, j]] == M[i, j]
+    g = np.arange(2 * n - 1, dtype=np.float32)
+    T = W.toeplitz_dense(g, n)
+    assert np.array_equal(T, g[golden_layouts["layout_toeplitz"]])
+    S = W.unpack_symmetric(p, n)
+    assert np.array_equal(S, p[golden_layouts["layout_symmetric"]])
