@@ -69,6 +69,10 @@ SIGNATURES = [
     ("smm_upper_left_rows", _i, [_vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_toeplitz_left_rows", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_symm_left_rows", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_gen_x_struct_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_gen_x_upper", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_gen_x_symm", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_symm_x_symm", _i, [_vp, _vp, _vp, _i, _i, _vp]),
     ("smm_debug_timeout_probe", _i, [_ull, _vp]),
     ("smm_debug_trace_next", _i, [_vp]),
 ]

@@ -122,9 +122,9 @@ int pad_copy(const float* src, int rows, int cols, float* dst, int ld_dst, cudaS
 }
 
 // ---------------------------------------------------------------- launches
-template <AKind AK, bool SPLIT3, int BN, int STAGES>
+template <AKind AK, BKind BK, bool SPLIT3, int BN, int STAGES>
 int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& p, cudaStream_t st) {
-  auto kern = umma_gemm_kernel<AK, SPLIT3, BN, STAGES>;
+  auto kern = umma_gemm_kernel<AK, BK, SPLIT3, BN, STAGES>;
   constexpr int smem = umma_smem_bytes<BN, SPLIT3, STAGES>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
   static bool attr_set[64] = {};
@@ -143,23 +143,23 @@ int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& 
 }
 
 // Stage counts fill ~192 KiB of shared memory.
-template <AKind AK, int BN>
+template <AKind AK, BKind BK, int BN>
 int launch_mode(bool split3, const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& p, cudaStream_t st) {
   if (split3) {
     constexpr int S = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-    return launch_umma<AK, true, BN, S>(ta, tb, p, st);
+    return launch_umma<AK, BK, true, BN, S>(ta, tb, p, st);
   }
-  constexpr int S = (BN == 256) ? 8 : 8;
-  return launch_umma<AK, false, BN, S>(ta, tb, p, st);
+  constexpr int S = 8;
+  return launch_umma<AK, BK, false, BN, S>(ta, tb, p, st);
 }
 
-template <AKind AK>
+template <AKind AK, BKind BK>
 int launch_bn(int bn, bool split3, const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& p,
               cudaStream_t st) {
   switch (bn) {
-    case 256: return launch_mode<AK, 256>(split3, ta, tb, p, st);
-    case 128: return launch_mode<AK, 128>(split3, ta, tb, p, st);
-    default: return launch_mode<AK, 64>(split3, ta, tb, p, st);
+    case 256: return launch_mode<AK, BK, 256>(split3, ta, tb, p, st);
+    case 128: return launch_mode<AK, BK, 128>(split3, ta, tb, p, st);
+    default: return launch_mode<AK, BK, 64>(split3, ta, tb, p, st);
   }
 }
 
@@ -184,17 +184,29 @@ bool valid_mode(int mode) { return mode == SMM_MODE_3XTF32 || mode == SMM_MODE_T
 
 // Core contraction: C(M x N, ldc) = Aop(M x K) * B(K x N, ldb).
 // Preconditions: B (and A when dense) 16-byte aligned with ld % 4 == 0.
-int run_contraction(AKind ak, int mode, const float* A, int lda, const float* a_src, int a_dim, int a_row0,
-                    const float* B, int ldb, float* C, int ldc, int M, int N, int K, cudaStream_t st) {
+// Operand description for run_contraction: a dense TMA-loaded matrix (ptr,
+// ld) or a structured one (src, dim, row0).
+struct Operand {
+  const float* ptr = nullptr;
+  int ld = 0;
+  const float* src = nullptr;
+  int dim = 0;
+  int row0 = 0;
+};
+
+int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
+                    int N, int K, cudaStream_t st) {
   if (mode == SMM_MODE_BF16) return set_error(SMM_ERR_UNSUPPORTED, "bf16 mode not built for this operation");
   const bool split3 = (mode == SMM_MODE_3XTF32);
   const int bn = pick_bn(M, N);
-  CUtensorMap tb, ta;
-  if (int rc = make_tmap(&tb, B, K, N, ldb, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) return rc;
-  if (ak == AKind::Dense || ak == AKind::UpperDense) {
-    if (int rc = make_tmap(&ta, A, M, K, lda, 16, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
-  } else {
-    ta = tb;  // unused by the kernel
+  CUtensorMap tb{}, ta{};
+  const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
+  const bool b_tma = (bk == BKind::Dense);
+  if (b_tma) {
+    if (int rc = make_tmap(&tb, b.ptr, K, N, b.ld, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) return rc;
+  }
+  if (a_tma) {
+    if (int rc = make_tmap(&ta, a.ptr, M, K, a.ld, 16, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
   }
   UmmaParams p{};
   p.M = M;
@@ -202,9 +214,11 @@ int run_contraction(AKind ak, int mode, const float* A, int lda, const float* a_
   p.K = K;
   p.C = C;
   p.ldc = ldc;
-  p.a_src = a_src;
-  p.a_dim = a_dim;
-  p.a_row0 = a_row0;
+  p.a_src = a.src;
+  p.a_dim = a.dim;
+  p.a_row0 = a.row0;
+  p.b_src = b.src;
+  p.b_dim = b.dim;
   p.row_tiles = (M + kBM - 1) / kBM;
   p.col_tiles = (N + bn - 1) / bn;
   p.status = device_status_word();
@@ -213,14 +227,36 @@ int run_contraction(AKind ak, int mode, const float* A, int lda, const float* a_
   if (!p.status) return set_error(SMM_ERR_CUDA, "device status word unavailable");
   if (p.row_tiles > 65535) return set_error(SMM_ERR_INVALID, "M = %d too large (max %d)", M, 65535 * kBM);
   g_trace = nullptr;
-  switch (ak) {
-    case AKind::Dense: return launch_bn<AKind::Dense>(bn, split3, ta, tb, p, st);
-    case AKind::UpperDense: return launch_bn<AKind::UpperDense>(bn, split3, ta, tb, p, st);
-    case AKind::UpperPacked: return launch_bn<AKind::UpperPacked>(bn, split3, ta, tb, p, st);
-    case AKind::Toeplitz: return launch_bn<AKind::Toeplitz>(bn, split3, ta, tb, p, st);
-    case AKind::SymmPacked: return launch_bn<AKind::SymmPacked>(bn, split3, ta, tb, p, st);
+  if (bk == BKind::Dense) {
+    switch (ak) {
+      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, split3, ta, tb, p, st);
+      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, split3, ta, tb, p, st);
+      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, split3, ta, tb, p, st);
+      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, split3, ta, tb, p, st);
+      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, split3, ta, tb, p, st);
+    }
   }
-  return set_error(SMM_ERR_INVALID, "unknown operand kind");
+  if (ak == AKind::Dense && bk == BKind::UpperPacked)
+    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, split3, ta, tb, p, st);
+  if (ak == AKind::Dense && bk == BKind::SymmPacked)
+    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, split3, ta, tb, p, st);
+  if (ak == AKind::SymmPacked && bk == BKind::SymmPacked)
+    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, split3, ta, tb, p, st);
+  return set_error(SMM_ERR_INVALID, "unsupported operand kinds");
+}
+
+Operand dense_op(const float* ptr, int ld) {
+  Operand o;
+  o.ptr = ptr;
+  o.ld = ld;
+  return o;
+}
+Operand structured_op(const float* src, int dim, int row0 = 0) {
+  Operand o;
+  o.src = src;
+  o.dim = dim;
+  o.row0 = row0;
+  return o;
 }
 
 // A right operand (rows x cols row-major) usable by TMA: either the caller's
@@ -310,7 +346,8 @@ extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, 
   Staged a, b;
   if (int rc = stage_operand(A, M, K, cur, &a, st)) return rc;
   if (int rc = stage_operand(B, K, N, cur, &b, st)) return rc;
-  return run_contraction(AKind::Dense, mode, a.ptr, a.ld, nullptr, 0, 0, b.ptr, b.ld, C, N, M, N, K, st);
+  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.ld), dense_op(b.ptr, b.ld), C, N, M, N, K,
+                         st);
 }
 
 extern "C" size_t smm_upper_left_workspace_size(int N, int ncols, int u_fmt, int mode) {
@@ -348,11 +385,14 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
     Staged u;
     if (int rc = stage_operand(U, N, N, cur, &u, st)) return rc;
     const float* urows = u.ptr + static_cast<size_t>(row0) * u.ld;
-    return run_contraction(AKind::UpperDense, mode, urows, u.ld, nullptr, N, row0, b.ptr, b.ld, C, ncols, nrows,
-                           ncols, N, st);
+    Operand ua = dense_op(urows, u.ld);
+    ua.dim = N;
+    ua.row0 = row0;
+    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.ld), C, ncols, nrows, ncols,
+                           N, st);
   }
-  return run_contraction(AKind::UpperPacked, mode, nullptr, 0, U, N, row0, b.ptr, b.ld, C, ncols, nrows, ncols, N,
-                         st);
+  return run_contraction(AKind::UpperPacked, BKind::Dense, mode, structured_op(U, N, row0), dense_op(b.ptr, b.ld), C,
+                         ncols, nrows, ncols, N, st);
 }
 
 extern "C" int smm_upper_left(const float* U, int u_fmt, const float* B, float* C, int N, int ncols, int mode,
@@ -377,7 +417,8 @@ extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, 
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
   if (int rc = stage_operand(B, N, ncols, cur, &b, st)) return rc;
-  return run_contraction(AKind::Toeplitz, mode, nullptr, 0, g, N, row0, b.ptr, b.ld, C, ncols, nrows, ncols, N, st);
+  return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), dense_op(b.ptr, b.ld), C,
+                         ncols, nrows, ncols, N, st);
 }
 
 extern "C" int smm_toeplitz_left(const float* g, const float* B, float* C, int N, int ncols, int mode, void* ws,
@@ -400,8 +441,8 @@ extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int 
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
   if (int rc = stage_operand(B, N, ncols, cur, &b, st)) return rc;
-  return run_contraction(AKind::SymmPacked, mode, nullptr, 0, S, N, row0, b.ptr, b.ld, C, ncols, nrows, ncols, N,
-                         st);
+  return run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N, row0), dense_op(b.ptr, b.ld), C,
+                         ncols, nrows, ncols, N, st);
 }
 
 extern "C" int smm_symm_left(const float* S, const float* B, float* C, int N, int ncols, int mode, void* ws,
@@ -435,9 +476,51 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   if (int rc = stage_operand(B, N, N, cur, &b, st)) return rc;
   if (ldx != N) SMM_CUDA_TRY(cudaMemsetAsync(X, 0, xbytes, st), "zero intermediate padding");
   // X = S B (S packed, mirrored on chip), then C = A X.
-  if (int rc = run_contraction(AKind::SymmPacked, mode, nullptr, 0, S, N, 0, b.ptr, b.ld, X, ldx, N, N, N, st))
+  if (int rc = run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N), dense_op(b.ptr, b.ld), X,
+                               ldx, N, N, N, st))
     return rc;
-  return run_contraction(AKind::Dense, mode, a.ptr, a.ld, nullptr, 0, 0, X, ldx, C, N, N, N, N, st);
+  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.ld), dense_op(X, ldx), C, N, N, N, N, st);
+}
+
+// ---------------------------------------------------------------- structured right operand
+extern "C" size_t smm_gen_x_struct_workspace_size(int M, int N, int mode) {
+  (void)mode;
+  if (M <= 0 || N <= 0) return 0;
+  return round256(static_cast<size_t>(M) * round4(N) * sizeof(float));
+}
+
+namespace {
+int gen_x_struct(const char* who, BKind bk, const float* A, const float* X, float* C, int M, int N, int mode, void* ws,
+                 size_t ws_bytes, cudaStream_t st) {
+  if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "%s: negative shape", who);
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
+  if (M == 0 || N == 0) return SMM_OK;
+  if (!A || !X || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
+  if (int rc = check_ws(who, ws, ws_bytes, pad_bytes(A, M, N))) return rc;
+  uint8_t* cur = static_cast<uint8_t*>(ws);
+  Staged a;
+  if (int rc = stage_operand(A, M, N, cur, &a, st)) return rc;
+  return run_contraction(AKind::Dense, bk, mode, dense_op(a.ptr, a.ld), structured_op(X, N), C, N, M, N, N, st);
+}
+}  // namespace
+
+extern "C" int smm_gen_x_upper(const float* A, const float* U, float* C, int M, int N, int mode, void* ws,
+                               size_t ws_bytes, void* stream) {
+  return gen_x_struct("smm_gen_x_upper", BKind::UpperPacked, A, U, C, M, N, mode, ws, ws_bytes, as_stream(stream));
+}
+
+extern "C" int smm_gen_x_symm(const float* A, const float* S, float* C, int M, int N, int mode, void* ws,
+                              size_t ws_bytes, void* stream) {
+  return gen_x_struct("smm_gen_x_symm", BKind::SymmPacked, A, S, C, M, N, mode, ws, ws_bytes, as_stream(stream));
+}
+
+extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N, int mode, void* stream) {
+  if (N < 0) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: negative shape");
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: unknown mode %d", mode);
+  if (N == 0) return SMM_OK;
+  if (!S1 || !S2 || !C) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: null pointer");
+  return run_contraction(AKind::SymmPacked, BKind::SymmPacked, mode, structured_op(S1, N), structured_op(S2, N), C,
+                         N, N, N, N, as_stream(stream));
 }
 
 // ---------------------------------------------------------------- timeout probe

@@ -40,6 +40,9 @@
 namespace smm {
 
 enum class AKind : int { Dense = 0, UpperPacked = 1, Toeplitz = 2, SymmPacked = 3, UpperDense = 4 };
+// Right operand: a dense row-major matrix loaded by TMA, or a packed
+// upper-triangular / symmetric matrix built on chip by the transform warps.
+enum class BKind : int { Dense = 0, UpperPacked = 1, SymmPacked = 2 };
 
 struct UmmaParams {
   int M, N, K;             // C is M x N; reduction length K
@@ -48,6 +51,8 @@ struct UmmaParams {
   const float* a_src;      // packed U / generator / packed S (structured A kinds)
   int a_dim;               // order of the structured matrix
   int a_row0;              // row of the structured matrix that output row 0 maps to
+  const float* b_src;      // packed U / packed S (structured B kinds)
+  int b_dim;               // order of the structured right operand
   int row_tiles;           // ceil(M / 128)
   int col_tiles;           // ceil(N / BN)
   uint32_t* status;        // device status word (sticky error bits)
@@ -101,14 +106,79 @@ __device__ __forceinline__ float a_value(const float* __restrict__ src, int n, i
   }
 }
 
-template <AKind AK, bool SPLIT3, int BN, int STAGES>
+// The 16 values one transform thread contributes to a structured A stage
+// tile (rows m0.., columns k0..k0+15), gathered into registers so all 16
+// loads are in flight together (the tile is rebuilt every stage, so load
+// latency, not bandwidth, bounds this producer).
+//   lanes along k (16 lanes per row, two rows per warp instruction): rows
+//     tw*32 + 2*it + lane/16, column lane%16 — coalesced along a packed row
+//     or a generator window;
+//   lanes along rows (symmetric tiles wholly below the diagonal, whose
+//     elements are the mirror S[k][row]): row tw*32 + lane, column it —
+//     coalesced along packed row k.
+template <AKind AK>
+__device__ __forceinline__ bool a_rows_mapping(int g_first, int k0) {
+  return AK == AKind::SymmPacked && k0 + kBK <= g_first;
+}
+
+template <AKind AK>
+__device__ __forceinline__ void a_gather(float (&v)[16], const UmmaParams& p, int g_first, int k0, int tw,
+                                         int lane) {
+  if (a_rows_mapping<AK>(g_first, k0)) {
+    const int gr = g_first + tw * 32 + lane;
+#pragma unroll
+    for (int it = 0; it < 16; ++it) v[it] = a_value<AK>(p.a_src, p.a_dim, gr, k0 + it);
+  } else {
+    const int k = k0 + (lane & 15);
+#pragma unroll
+    for (int it = 0; it < 16; ++it) v[it] = a_value<AK>(p.a_src, p.a_dim, g_first + tw * 32 + it * 2 + (lane >> 4), k);
+  }
+}
+
+template <AKind AK, bool SPLIT3>
+__device__ __forceinline__ void a_store(const float (&v)[16], uint8_t* ah, uint8_t* al, int g_first, int k0, int tw,
+                                        int lane) {
+  const bool rows = a_rows_mapping<AK>(g_first, k0);
+#pragma unroll
+  for (int it = 0; it < 16; ++it) {
+    const int r = rows ? tw * 32 + lane : tw * 32 + it * 2 + (lane >> 4);
+    const int kl = rows ? it : (lane & 15);
+    const uint32_t off = swz_offset(r, kl >> 2, 64) + (kl & 3) * 4;
+    const float hi = tf32_hi(v[it]);
+    *reinterpret_cast<float*>(ah + off) = hi;
+    if constexpr (SPLIT3) *reinterpret_cast<float*>(al + off) = v[it] - hi;
+  }
+}
+
+// Value of the structured right operand at (row k, column n); zero outside
+// the n x n matrix.
+template <BKind BK>
+__device__ __forceinline__ float b_value(const float* __restrict__ src, int nd, int k, int n) {
+  if (k >= nd || n >= nd) return 0.0f;
+  if constexpr (BK == BKind::UpperPacked) {
+    return n >= k ? __ldg(src + packed_idx(k, n, nd)) : 0.0f;
+  } else {  // SymmPacked
+    return n >= k ? __ldg(src + packed_idx(k, n, nd)) : __ldg(src + packed_idx(n, k, nd));
+  }
+}
+
+// Byte offset of element (k-row kr, column n) in a B stage tile: 32-column
+// boxes of 16 rows x 128 B, 128-byte swizzle with 32-byte atoms
+// (32-byte granule index ^= row & 3).
+__device__ __forceinline__ uint32_t b_tile_offset(uint32_t kr, uint32_t n) {
+  const uint32_t j = n & 31u;
+  return (n >> 5) * 2048u + kr * 128u + ((((j >> 3) ^ (kr & 3u))) << 5) + (j & 7u) * 4u;
+}
+
+template <AKind AK, BKind BK, bool SPLIT3, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const UmmaParams p) {
   constexpr int kBTile = TileGeom<BN>::kBTileBytes;
   constexpr int kStage = stage_bytes<BN, SPLIT3>();
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
-  constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + kBTile;
+  constexpr bool kBTma = (BK == BKind::Dense);
+  constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0);
   constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
   constexpr uint32_t kIdesc = make_idesc(kFmtTF32, kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
 
@@ -140,7 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // [g0, g0+128) of U needs k >= g0 only.
   int kb_begin = 0;
   if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + m0) / kBK;
-  const int kb_end = (p.K + kBK - 1) / kBK;
+  int kb_end = (p.K + kBK - 1) / kBK;
+  // An upper-triangular right operand is zero below its diagonal: column
+  // tile [n0, n0+BN) needs k < n0 + BN only.
+  if constexpr (BK == BKind::UpperPacked) kb_end = min(kb_end, (n0 + BN - 1) / kBK + 1);
   const int num_kb = kb_end - kb_begin;
 
   if (threadIdx.x == 0) {
@@ -155,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     if constexpr (kATma) tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    if constexpr (kBTma) tma_prefetch_desc(&tmB);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before_sync();
@@ -184,9 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[s], kTxBytes);
         const int k0 = (kb_begin + i) * kBK;
         if constexpr (kATma) tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
+        if constexpr (kBTma) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-          tma_load_2d(b_hi(s) + c * TileGeom<BN>::kBChunkBytes, &tmB, &full[s], n0 + 32 * c, k0);
+          for (int c = 0; c < BN / 32; ++c)
+            tma_load_2d(b_hi(s) + c * TileGeom<BN>::kBChunkBytes, &tmB, &full[s], n0 + 32 * c, k0);
+        }
         ++issued;
       }
       if (*abort_flag) {
@@ -255,9 +330,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x - 64;  // 0..127
     const int tw = t >> 5;           // transform warp 0..3
     bool ok = true;
+    const int g_first = p.a_row0 + m0;  // structured-A row of tile row 0
+    float a_cur[16], a_nxt[16];
+    if constexpr (!kATma) {
+      if (num_kb > 0) a_gather<AK>(a_cur, p, g_first, kb_begin * kBK, tw, lane);
+    }
     for (int i = 0; i < num_kb && ok; ++i) {
       const int s = i % STAGES;
       const uint32_t ph = (i / STAGES) & 1;
+      // Issue the next stage's global loads before waiting on this one: they
+      // need no shared memory, so their latency overlaps the wait and the
+      // stores below.
+      if constexpr (!kATma) {
+        if (i + 1 < num_kb) a_gather<AK>(a_nxt, p, g_first, (kb_begin + i + 1) * kBK, tw, lane);
+      }
       // Warp-uniform outcome: the tcgen05.ld below is .sync.aligned, so the
       // lanes of a warp must never take different paths.
       if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) {
@@ -266,20 +352,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int k0 = (kb_begin + i) * kBK;
       if constexpr (!kATma) {
-        // Build the structured A tile: 16 lanes per row (one k each), two
-        // rows per warp instruction, 32 rows per warp.
-        const int kl = lane & 15;
-        uint8_t* ah = a_hi(s);
-        uint8_t* al = a_lo(s);
-#pragma unroll 4
-        for (int it = 0; it < 16; ++it) {
-          const int r = tw * 32 + it * 2 + (lane >> 4);
-          const float v = a_value<AK>(p.a_src, p.a_dim, p.a_row0 + m0 + r, k0 + kl);
-          const uint32_t off = swz_offset(r, kl >> 2, 64) + (kl & 3) * 4;
-          const float hi = tf32_hi(v);
-          *reinterpret_cast<float*>(ah + off) = hi;
-          if constexpr (SPLIT3) *reinterpret_cast<float*>(al + off) = v - hi;
-        }
+        a_store<AK, SPLIT3>(a_cur, a_hi(s), a_lo(s), g_first, k0, tw, lane);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a_cur[j] = a_nxt[j];
       } else if constexpr (SPLIT3) {
         const float4* src = reinterpret_cast<const float4*>(a_hi(s));
         float4* dst = reinterpret_cast<float4*>(a_lo(s));
@@ -289,7 +364,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           dst[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
         }
       }
-      if constexpr (SPLIT3) {
+      if constexpr (!kBTma) {
+        // Build the structured B tile: warp tw fills k-rows tw, tw+4, ...;
+        // each lane one column of a 32-column box (coalesced along packed rows).
+        uint8_t* bh = b_hi(s);
+        uint8_t* bl = b_lo(s);
+        // Symmetric tiles wholly below the diagonal (every column n < k) read
+        // the mirror S[n][k]: 16 lanes along k per column keep those loads
+        // coalesced along packed row n.
+        const bool mirror = (BK == BKind::SymmPacked) && (n0 + BN <= k0);
+        constexpr int kPer = (kBK * BN) / 128;  // elements per thread per stage
+        constexpr int kBatch = kPer < 16 ? kPer : 16;
+#pragma unroll 1
+        for (int b0 = 0; b0 < kPer; b0 += kBatch) {
+          float v[kBatch];
+#pragma unroll
+          for (int e = 0; e < kBatch; ++e) {
+            const int q = b0 + e;  // 0 .. kPer-1
+            int kr, n;
+            if (mirror) {
+              kr = lane & 15;
+              n = (q * 4 + tw) * 2 + (lane >> 4);
+            } else {
+              kr = tw + 4 * (q / (BN / 32));
+              n = (q % (BN / 32)) * 32 + lane;
+            }
+            v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
+          }
+#pragma unroll
+          for (int e = 0; e < kBatch; ++e) {
+            const int q = b0 + e;
+            int kr, n;
+            if (mirror) {
+              kr = lane & 15;
+              n = (q * 4 + tw) * 2 + (lane >> 4);
+            } else {
+              kr = tw + 4 * (q / (BN / 32));
+              n = (q % (BN / 32)) * 32 + lane;
+            }
+            const uint32_t off = b_tile_offset(kr, n);
+            const float hi = tf32_hi(v[e]);
+            *reinterpret_cast<float*>(bh + off) = hi;
+            if constexpr (SPLIT3) *reinterpret_cast<float*>(bl + off) = v[e] - hi;
+          }
+        }
+      } else if constexpr (SPLIT3) {
         const float4* src = reinterpret_cast<const float4*>(b_hi(s));
         float4* dst = reinterpret_cast<float4*>(b_lo(s));
 #pragma unroll

@@ -176,6 +176,46 @@ def symm_sandwich(A: torch.Tensor, S: torch.Tensor, B: torch.Tensor, mode: str =
     return C
 
 
+def _gen_x_struct(entry: str, A: torch.Tensor, X: torch.Tensor, mode: str, out, stream) -> torch.Tensor:
+    A = _check_f32("A", A)
+    M, N = A.shape
+    X = _check_f32("packed operand", X, N * (N + 1) // 2)
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_gen_x_struct_workspace_size(M, N, m), A.device)
+    C = _out(out, (M, N), A)
+    _lib.check(getattr(L, entry)(_ptr(A), _ptr(X), _ptr(C), M, N, m, ws, wsb, _stream_ptr(stream)), entry)
+    return C
+
+
+def gen_x_upper(A: torch.Tensor, U: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+                stream=None) -> torch.Tensor:
+    """C = A @ U, U upper triangular given packed (right side)."""
+    return _gen_x_struct("smm_gen_x_upper", A, U, mode, out, stream)
+
+
+def gen_x_symm(A: torch.Tensor, S: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+               stream=None) -> torch.Tensor:
+    """C = A @ S, S symmetric given packed upper (right side)."""
+    return _gen_x_struct("smm_gen_x_symm", A, S, mode, out, stream)
+
+
+def symm_x_symm(S1: torch.Tensor, S2: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+                stream=None) -> torch.Tensor:
+    """C = S1 @ S2, both symmetric given packed upper."""
+    S1 = _check_f32("S1", S1)
+    p = S1.numel()
+    N = int((-1 + (1 + 8 * p) ** 0.5) // 2)
+    if N * (N + 1) // 2 != p:
+        raise ValueError(f"S1 has {p} elements, not a packed triangle")
+    S2 = _check_f32("S2", S2, p)
+    C = _out(out, (N, N), S1)
+    L = _lib.load()
+    _lib.check(L.smm_symm_x_symm(_ptr(S1), _ptr(S2), _ptr(C), N, _mode(mode), _stream_ptr(stream)),
+               "smm_symm_x_symm")
+    return C
+
+
 def device_status(stream=None) -> None:
     """Raise SmmError(SMM_ERR_DEVICE_TIMEOUT) if a kernel gave up a bounded wait."""
     _lib.check(_lib.load().smm_device_status(_stream_ptr(stream)), "smm_device_status")

@@ -139,6 +139,29 @@ int smm_symm_left_rows(const float* S_packed, const float* B, float* C, int N, i
 int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, float* C, int N, int mode, void* ws,
                       size_t ws_bytes, void* stream);
 
+/* ---- structured right operand (the reference's own orientation) ------- */
+
+/* Workspace for smm_gen_x_upper / smm_gen_x_symm (a padded copy of A when its
+ * rows are not 16-byte multiples). */
+size_t smm_gen_x_struct_workspace_size(int M, int N, int mode);
+
+/* C(M x N) = A(M x N) U(N x N, packed upper).  Replaces kernel_gen_x_upper +
+ * copy_B_to_Reg_Upper (src/dsl/codegen_cuda.py:280-544) and Cuda
+ * kernels/upper.cu:73-313.  K-blocks below a column tile's diagonal are
+ * never visited. */
+int smm_gen_x_upper(const float* A, const float* U_packed, float* C, int M, int N, int mode, void* ws,
+                    size_t ws_bytes, void* stream);
+
+/* C(M x N) = A(M x N) S(N x N, packed upper symmetric), S mirrored on chip.
+ * Replaces kernel_gen_x_symm + copy_B_to_Reg_Symm (src/dsl/codegen_cuda.py:546-806)
+ * and Cuda kernels/symmetric.cu:76-271. */
+int smm_gen_x_symm(const float* A, const float* S_packed, float* C, int M, int N, int mode, void* ws,
+                   size_t ws_bytes, void* stream);
+
+/* C(N x N) = S1 S2, both packed upper symmetric.  Replaces kernel_symm_x_symm
+ * (src/dsl/codegen_cuda.py:1340-1613).  No workspace. */
+int smm_symm_x_symm(const float* S1_packed, const float* S2_packed, float* C, int N, int mode, void* stream);
+
 /* ---- failure-detection probe ------------------------------------------- */
 
 /* Launches one CTA that waits on a shared-memory barrier nothing ever

@@ -143,8 +143,9 @@ def test_toeplitz_shapes(cuda, n_cols):
 def test_symm_left_shapes(cuda, n_cols):
     N, ncols = n_cols
     s = W.make_sandwich(N, seed=N)
-    B = W.make_gemm(N, ncols, 1, seed=ncols)["A"]  # any N x ncols matrix
+    B = W.make_gemm(N, 1, ncols, seed=ncols)["A"]  # N x ncols
     C = host(ops.symm_left(dev(s["S"]), dev(B)))
+    assert B.shape == (N, ncols)
     S = W.unpack_symmetric(s["S"], N).astype(np.float64)
     R = S @ B.astype(np.float64)
     assert _relerr_full(C, R) <= 1e-5
