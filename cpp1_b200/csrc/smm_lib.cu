@@ -145,9 +145,13 @@ int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& 
 // Stage counts fill ~192 KiB of shared memory.
 template <AKind AK, BKind BK, int BN>
 int launch_mode(bool split3, const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& p, cudaStream_t st) {
-  if (split3) {
-    constexpr int S = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-    return launch_umma<AK, BK, true, BN, S>(ta, tb, p, st);
+  if constexpr (BN <= 128) {
+    if (split3) {
+      constexpr int S = (BN == 128) ? 6 : 8;
+      return launch_umma<AK, BK, true, BN, S>(ta, tb, p, st);
+    }
+  } else {
+    if (split3) return set_error(SMM_ERR_INVALID, "3xTF32 tiles are at most 128 columns wide");
   }
   constexpr int S = 8;
   return launch_umma<AK, BK, false, BN, S>(ta, tb, p, st);
@@ -198,7 +202,9 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
                     int N, int K, cudaStream_t st) {
   if (mode == SMM_MODE_BF16) return set_error(SMM_ERR_UNSUPPORTED, "bf16 mode not built for this operation");
   const bool split3 = (mode == SMM_MODE_3XTF32);
-  const int bn = pick_bn(M, N);
+  // 3xTF32 keeps two chunk accumulators and a running sum in tensor memory
+  // (3 x BN of its 512 columns), so its tiles are at most 128 wide.
+  const int bn = split3 ? std::min(pick_bn(M, N), 128) : pick_bn(M, N);
   CUtensorMap tb{}, ta{};
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);

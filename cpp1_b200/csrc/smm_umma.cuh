@@ -83,6 +83,21 @@ __host__ __device__ constexpr int stage_bytes() {
   return (SPLIT3 ? 2 : 1) * (kATileBytes + TileGeom<BN>::kBTileBytes);
 }
 
+// 3xTF32 accumulates in chunks of kChunk k-blocks: the tensor core's fp32
+// accumulation truncates on every update, so with same-sign data its error
+// grows with the number of updates into one accumulator.  Each chunk goes
+// to one of two ping-pong accumulators (overwritten at chunk start) and the
+// transform warps fold finished chunks into a third TMEM region with
+// round-to-nearest fp32 adds, bounding the truncation bias to
+// 3 * kChunk * 2 updates whatever K is.
+constexpr int kChunk = 8;
+
+template <int BN, bool SPLIT3>
+__host__ __device__ constexpr uint32_t tmem_cols() {
+  // SPLIT3: acc0 [0,BN), acc1 [BN,2BN), running sum [2BN,3BN)
+  return SPLIT3 ? (3 * BN <= 256 ? 256u : 512u) : (BN < 32 ? 32u : static_cast<uint32_t>(BN));
+}
+
 template <int BN, bool SPLIT3, int STAGES>
 __host__ __device__ constexpr int umma_smem_bytes() {
   return 1024 /*alignment slack*/ + STAGES * stage_bytes<BN, SPLIT3>() + 256 /*barriers etc*/;
@@ -179,7 +194,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
   constexpr bool kBTma = (BK == BKind::Dense);
   constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0);
-  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  constexpr uint32_t kTmemCols = tmem_cols<BN, SPLIT3>();
+  static_assert(!SPLIT3 || 3 * BN <= 512, "3xTF32 needs three BN-column regions of tensor memory");
+  // A chunk's accumulator is folded when the transform warps reach stage
+  // (c+1)*kChunk + kFoldLag: by then the MMAs of chunk c have completed
+  // (the producer only refills a stage after its MMAs finish), and the fold
+  // still precedes the first stage of chunk c+2, which reuses the buffer.
+  constexpr int kFoldLag = STAGES - 1;
+  static_assert(!SPLIT3 || kFoldLag <= kChunk, "fold lag must not exceed the chunk length");
   constexpr uint32_t kIdesc = make_idesc(kFmtTF32, kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
 
   extern __shared__ uint8_t smem_raw[];
@@ -188,7 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* ready = full + STAGES;
   uint64_t* empty = ready + STAGES;
   uint64_t* accum_full = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_full + 1);
+  uint64_t* acc_full = accum_full + 1;  // [2]: chunk finished in ping-pong buffer b
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   auto a_hi = [&](int s) { return smem + s * kStage; };
@@ -223,6 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum_full, 1);
+    mbar_init(&acc_full[0], 1);
+    mbar_init(&acc_full[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -284,6 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after_sync();
         const uint32_t sa = smem_u32(a_hi(s));
         const uint32_t sb = smem_u32(b_hi(s));
+        // 3xTF32: chunk c = i / kChunk accumulates into buffer c & 1 and
+        // starts from zero; otherwise one accumulator for the whole K.
+        const bool chunk_start = SPLIT3 ? (i % kChunk == 0) : (i == 0);
+        const uint32_t d_tmem = SPLIT3 ? tmem_base + static_cast<uint32_t>(((i / kChunk) & 1) * BN) : tmem_base;
 #pragma unroll
         for (int kk = 0; kk < kBK / 8; ++kk) {
           // A: K-major, 64-byte rows, 8-row groups 512 B apart; a k-step of
@@ -293,19 +322,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           // apart in 4-row swizzle atoms 512 B apart (SBO); a k-step of 8
           // rows is 1024 B.
           const uint64_t db = make_smem_desc(sb + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_tf32(tmem_base, da, db, kIdesc, acc);
+          const uint32_t acc = (!chunk_start || kk > 0) ? 1u : 0u;
+          umma_tf32(d_tmem, da, db, kIdesc, acc);
           if constexpr (SPLIT3) {
             const uint32_t sal = smem_u32(a_lo(s));
             const uint32_t sbl = smem_u32(b_lo(s));
             const uint64_t dal = make_smem_desc(sal + kk * 32, 16, 512, kLayoutSw64);
             const uint64_t dbl =
                 make_smem_desc(sbl + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
-            umma_tf32(tmem_base, da, dbl, kIdesc, 1u);
-            umma_tf32(tmem_base, dal, db, kIdesc, 1u);
+            umma_tf32(d_tmem, da, dbl, kIdesc, 1u);
+            umma_tf32(d_tmem, dal, db, kIdesc, 1u);
           }
         }
         umma_commit(&empty[s]);
+        if constexpr (SPLIT3) {
+          if (i % kChunk == kChunk - 1 || i == num_kb - 1) umma_commit(&acc_full[(i / kChunk) & 1]);
+        }
         if (tr && i == 0) {
           const uint64_t da = make_smem_desc(sa, 16, 512, kLayoutSw64);
           const uint64_t db = make_smem_desc(sb, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
@@ -330,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x - 64;  // 0..127
     const int tw = t >> 5;           // transform warp 0..3
     bool ok = true;
+    int folded = 0;                     // chunks already summed into the running sum
     const int g_first = p.a_row0 + m0;  // structured-A row of tile row 0
     float a_cur[16], a_nxt[16];
     if constexpr (!kATma) {
@@ -343,6 +376,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       // stores below.
       if constexpr (!kATma) {
         if (i + 1 < num_kb) a_gather<AK>(a_nxt, p, g_first, (kb_begin + i + 1) * kBK, tw, lane);
+      }
+      if constexpr (SPLIT3) {
+        if (i >= kChunk + kFoldLag && (i - kFoldLag) % kChunk == 0) {
+          const int f = (i - kFoldLag) / kChunk - 1;  // chunk to fold
+          if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[f & 1], (f >> 1) & 1, wxf))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
+          const uint32_t src = tmem_base + lanes + static_cast<uint32_t>((f & 1) * BN);
+          const uint32_t sum = tmem_base + lanes + static_cast<uint32_t>(2 * BN);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t r[16], q[16];
+            tmem_ld_32x32b_x16(src + c, r);
+            if (f > 0) tmem_ld_32x32b_x16(sum + c, q);
+            tmem_wait_ld();
+            if (f > 0) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
+            }
+            tmem_st_32x32b_x16(sum + c, r);
+          }
+          tmem_wait_st();
+          tc_fence_before_sync();
+          folded = f + 1;
+        }
       }
       // Warp-uniform outcome: the tcgen05.ld below is .sync.aligned, so the
       // lanes of a warp must never take different paths.
@@ -436,11 +497,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m0 + q * 32 + lane;
       const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
       float* crow = p.C + static_cast<long long>(row) * p.ldc;
+      const int nch = (num_kb + kChunk - 1) / kChunk;
+      const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         uint32_t r[16];
-        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c, r);
-        tmem_wait_ld();
+        if constexpr (SPLIT3) {
+          // result = running sum (chunks [0, folded)) + the unfolded chunks
+          // (at most two, in distinct ping-pong buffers).
+          float acc[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+          if (folded > 0) {
+            tmem_ld_32x32b_x16(tmem_base + lanes + 2 * BN + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(r[j]);
+          }
+#pragma unroll 1
+          for (int f = folded; f < nch; ++f) {
+            tmem_ld_32x32b_x16(tmem_base + lanes + static_cast<uint32_t>((f & 1) * BN) + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] += __uint_as_float(r[j]);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(acc[j]);
+        } else {
+          tmem_ld_32x32b_x16(tmem_base + lanes + c, r);
+          tmem_wait_ld();
+        }
         if (tr && q == 0 && lane == 0 && c == 0)
           for (int j = 0; j < 16; ++j) p.trace[kTrAcc + j] = r[j];
         const int col = n0 + c;

@@ -58,6 +58,10 @@ def lib() -> ctypes.CDLL:
         L.orc_toeplitz_left_rows_f64.argtypes = [_F32P, _F32P, _I32P, _c_int, _F64P, _c_int, _c_int]
         L.orc_sandwich_rows_f64.argtypes = [_F32P, _F32P, _F32P, _I32P, _c_int, _F64P, _c_int]
         L.orc_symm_right_rows_f64.argtypes = [_F32P, _F32P, _I32P, _c_int, _F64P, _c_int, _c_int]
+        L.orc_gemm_rows_f32.argtypes = [_F32P, _F32P, _I32P, _c_int, _F32P, _c_int, _c_int]
+        L.orc_upper_left_rows_f32.argtypes = [_F32P, _F32P, _I32P, _c_int, _F32P, _c_int, _c_int]
+        L.orc_toeplitz_left_rows_f32.argtypes = [_F32P, _F32P, _I32P, _c_int, _F32P, _c_int, _c_int]
+        L.orc_sandwich_rows_f32.argtypes = [_F32P, _F32P, _F32P, _I32P, _c_int, _F32P, _c_int]
         L.orc_relerr.argtypes = [_F32P, _F64P, ctypes.c_size_t]
         L.orc_relerr.restype = ctypes.c_double
         _lib = L
@@ -169,6 +173,34 @@ def symm_right_rows_f64(A, Sp, rows) -> np.ndarray:
     A, Sp, r = _f32(A), _f32(Sp), _rows(rows)
     out = np.empty((len(r), A.shape[1]), np.float64)
     lib().orc_symm_right_rows_f64(A, Sp, r, len(r), out, A.shape[0], A.shape[1])
+    return out
+
+
+def gemm_rows_f32(A, B, rows) -> np.ndarray:
+    A, B, r = _f32(A), _f32(B), _rows(rows)
+    out = np.empty((len(r), B.shape[1]), np.float32)
+    lib().orc_gemm_rows_f32(A, B, r, len(r), out, B.shape[1], A.shape[1])
+    return out
+
+
+def upper_left_rows_f32(Up, B, rows) -> np.ndarray:
+    Up, B, r = _f32(Up), _f32(B), _rows(rows)
+    out = np.empty((len(r), B.shape[1]), np.float32)
+    lib().orc_upper_left_rows_f32(Up, B, r, len(r), out, B.shape[0], B.shape[1])
+    return out
+
+
+def toeplitz_left_rows_f32(g, B, rows) -> np.ndarray:
+    g, B, r = _f32(g), _f32(B), _rows(rows)
+    out = np.empty((len(r), B.shape[1]), np.float32)
+    lib().orc_toeplitz_left_rows_f32(g, B, r, len(r), out, B.shape[0], B.shape[1])
+    return out
+
+
+def sandwich_rows_f32(A, Sp, B, rows) -> np.ndarray:
+    A, Sp, B, r = _f32(A), _f32(Sp), _f32(B), _rows(rows)
+    out = np.empty((len(r), A.shape[0]), np.float32)
+    lib().orc_sandwich_rows_f32(A, Sp, B, r, len(r), out, A.shape[0])
     return out
 
 

@@ -249,3 +249,72 @@ double orc_relerr(const float* X, const double* R, size_t n) {
   }
   return den > 0.0 ? sqrt(num / den) : sqrt(num);
 }
+
+/* ---------------- fp32 restatements on selected rows ----------------
+ * Same FMA order as the full restatements above (and so as the reference
+ * kernels), for checking the reference's own result at sizes where a full
+ * CPU product is too slow. */
+
+void orc_gemm_rows_f32(const float* A, const float* B, const int* rows, int nrows, float* out, int N, int K) {
+#pragma omp parallel for schedule(dynamic, 1)
+  for (long t = 0; t < nrows; ++t) {
+    float* c = out + (size_t)t * N;
+    for (long j = 0; j < N; ++j) c[j] = 0.0f;
+    for (long k = 0; k < K; ++k) {
+      const float a = A[(size_t)rows[t] * K + k];
+      const float* b = B + (size_t)k * N;
+      for (long j = 0; j < N; ++j) c[j] = fmaf(a, b[j], c[j]);
+    }
+  }
+}
+
+void orc_upper_left_rows_f32(const float* Up, const float* B, const int* rows, int nrows, float* out, int N,
+                             int ncols) {
+#pragma omp parallel for schedule(dynamic, 1)
+  for (long t = 0; t < nrows; ++t) {
+    const long c = rows[t];
+    float* o = out + (size_t)t * ncols;
+    for (long r = 0; r < ncols; ++r) o[r] = 0.0f;
+    for (long k = N - 1; k >= c; --k) {
+      const float u = Up[pidx(c, k, N)];
+      const float* b = B + (size_t)k * ncols;
+      for (long r = 0; r < ncols; ++r) o[r] = fmaf(b[r], u, o[r]);
+    }
+  }
+}
+
+void orc_toeplitz_left_rows_f32(const float* g, const float* B, const int* rows, int nrows, float* out, int N,
+                                int ncols) {
+#pragma omp parallel for schedule(dynamic, 1)
+  for (long t = 0; t < nrows; ++t) {
+    const long c = rows[t];
+    float* o = out + (size_t)t * ncols;
+    for (long r = 0; r < ncols; ++r) o[r] = 0.0f;
+    for (long k = 0; k < N; ++k) {
+      const float v = g[N - 1 + k - c];
+      const float* b = B + (size_t)k * ncols;
+      for (long r = 0; r < ncols; ++r) o[r] = fmaf(b[r], v, o[r]);
+    }
+  }
+}
+
+void orc_sandwich_rows_f32(const float* A, const float* Sp, const float* B, const int* rows, int nrows, float* out,
+                           int N) {
+#pragma omp parallel for schedule(dynamic, 1)
+  for (long t = 0; t < nrows; ++t) {
+    const long i = rows[t];
+    float* w = (float*)calloc((size_t)N, sizeof(float));
+    for (long k = 0; k < N; ++k) {
+      const float a = A[(size_t)i * N + k];
+      for (long j = 0; j < N; ++j) w[j] = fmaf(a, sym_at(Sp, k, j, N), w[j]);
+    }
+    float* c = out + (size_t)t * N;
+    for (long j = 0; j < N; ++j) c[j] = 0.0f;
+    for (long k = 0; k < N; ++k) {
+      const float a = w[k];
+      const float* b = B + (size_t)k * N;
+      for (long j = 0; j < N; ++j) c[j] = fmaf(a, b[j], c[j]);
+    }
+    free(w);
+  }
+}
