@@ -73,6 +73,7 @@ SIGNATURES = [
     ("smm_gen_x_upper", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_gen_x_symm", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_symm_x_symm", _i, [_vp, _vp, _vp, _i, _i, _vp]),
+    ("smm_symm_sandwich_noalloc", _i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     ("smm_debug_timeout_probe", _i, [_ull, _vp]),
     ("smm_debug_trace_next", _i, [_vp]),
 ]

@@ -569,3 +569,54 @@ extern "C" int smm_debug_trace_next(unsigned* trace) {
   g_trace = trace;
   return SMM_OK;
 }
+
+// ---------------------------------------------------------------- allocation-free sandwich
+// Scratch of smm_symm_sandwich_noalloc: the S*B intermediate, plus padded
+// copies of A and B when their rows are not 16-byte multiples.  A fixed
+// 16 MiB that every GPU which loads this library holds until process exit.
+// Host code must not use this name as an address (it is a host-side stand-in
+// for the symbol); the device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[size_t(16) << 20];
+
+namespace smm {
+namespace {
+constexpr size_t kNoallocScratchBytes = sizeof(g_noalloc_scratch);
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  static void* addr[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev & 63]) {
+    void* p = nullptr;
+    SMM_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(static sandwich scratch)");
+    addr[dev & 63] = p;
+  }
+  *out = addr[dev & 63];
+  return SMM_OK;
+}
+}  // namespace
+}  // namespace smm
+
+extern "C" int smm_symm_sandwich_noalloc(const float* A, const float* S, const float* B, float* C, int N, int mode,
+                                         void* stream) {
+  if (N < 0) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: negative shape");
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: unknown mode %d", mode);
+  if (N == 0) return SMM_OK;
+  if (!A || !S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: null pointer");
+  // Same scratch layout smm_symm_sandwich uses: X = S B with a 16-byte row
+  // stride, then any padded operand copies.
+  const size_t need = round256(static_cast<size_t>(N) * round4(N) * sizeof(float)) + pad_bytes(A, N, N) +
+                      pad_bytes(B, N, N);
+  if (need > kNoallocScratchBytes)
+    return set_error(SMM_ERR_WORKSPACE,
+                     "smm_symm_sandwich_noalloc: N = %d needs %zu bytes of scratch but the static scratch holds %zu "
+                     "(N <= 2048 when N %% 4 == 0 and A, B are 16-byte aligned)",
+                     N, need, kNoallocScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  return smm_symm_sandwich(A, S, B, C, N, mode, scratch, kNoallocScratchBytes, stream);
+}

@@ -139,6 +139,23 @@ int smm_symm_left_rows(const float* S_packed, const float* B, float* C, int N, i
 int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, float* C, int N, int mode, void* ws,
                       size_t ws_bytes, void* stream);
 
+/* Allocation-free variant of smm_symm_sandwich (no counterpart in the
+ * reference).  For callers that cannot allocate device memory: code inside a
+ * host framework that owns all device memory through its own pool, or a
+ * latency-critical path where cudaMalloc's implicit device synchronisation is
+ * not acceptable.  The S*B intermediate (and padded copies of A and B when
+ * N % 4 != 0 or they are not 16-byte aligned) lives in a fixed 16 MiB static
+ * device array inside libsmm, which every GPU that loads the library holds
+ * until process exit; N <= 2048 with aligned operands (about 1180 when padded
+ * copies are needed), larger N returns SMM_ERR_WORKSPACE.  Calls no
+ * cudaMalloc/cudaFree.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) and must come before any stream
+ * capture.  Every call shares the one array and it keeps the last call's
+ * contents: calls that overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller. */
+int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float* B, float* C, int N, int mode,
+                              void* stream);
+
 /* ---- structured right operand (the reference's own orientation) ------- */
 
 /* Workspace for smm_gen_x_upper / smm_gen_x_symm (a padded copy of A when its
