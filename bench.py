@@ -242,17 +242,6 @@ def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
 
 
 # ---------------------------------------------------------------- our arm
-def equal_work_bounds(n: int, world: int, triangular: bool, align: int = 128):
-    """Row-slab boundaries.  For U (row i costs n - i), boundary g sits at
-    n (1 - sqrt(1 - g/G)), rounded to the tile height."""
-    b = [0]
-    for g in range(1, world):
-        x = n * (1 - math.sqrt(1 - g / world)) if triangular else n * g / world
-        b.append(min(n, max(b[-1], int(round(x / align)) * align)))
-    b.append(n)
-    return b
-
-
 def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
@@ -284,7 +273,8 @@ def run_ours(args, rank, world, local):
         h_in = [w["g"], w["B"]]
     d_in = [torch.from_numpy(x).cuda() for x in h_in]
 
-    bounds = equal_work_bounds(n, world, triangular=(op == "upper")) if op != "diag" else None
+    from cpp1_b200.multigpu import row_slabs, slab_useful_flops
+    bounds = row_slabs(n, world, triangular=(op == "upper")) if op != "diag" else None
     r0, r1 = (bounds[rank], bounds[rank + 1]) if bounds else (0, n)
     nrows = r1 - r0
     out = torch.empty((nrows if op != "diag" else n, n), dtype=torch.float32, device="cuda")
@@ -320,7 +310,7 @@ def run_ours(args, rank, world, local):
                 dist.broadcast(B, src=0)
             _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, B.data_ptr(), out.data_ptr(), n, n, r0,
                                              nrows, m, ws, wsb, sp), "upper")
-        units_per_rank_call = sum(n - i for i in range(r0, r1)) * n  # N^2(N+1) summed over ranks
+        units_per_rank_call = slab_useful_flops("upper", n, r0, r1)
     elif op == "sandwich":
         A, S, B = d_in
         X = torch.empty((n, n), dtype=torch.float32, device="cuda")

@@ -99,31 +99,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 int round4(int x) { return (x + 3) & ~3; }
 
-// ---------------------------------------------------------------- pad copy
-// dst (rows x ld_dst) = src (rows x cols, ld_src) with zero columns appended.
-__global__ void pad_cols_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
-                                float* __restrict__ dst, int ld_dst) {
-  const long long total = static_cast<long long>(rows) * ld_dst;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / ld_dst;
-    const int c = static_cast<int>(i - r * ld_dst);
-    dst[i] = c < cols ? src[r * ld_src + c] : 0.0f;
-  }
-}
-
-int pad_copy(const float* src, int rows, int cols, float* dst, int ld_dst, cudaStream_t st) {
-  const long long total = static_cast<long long>(rows) * ld_dst;
-  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-  pad_cols_kernel<<<std::max(grid, 1), 256, 0, st>>>(src, rows, cols, cols, dst, ld_dst);
-  count_launch();
-  SMM_CUDA_TRY(cudaGetLastError(), "pad copy launch");
-  return SMM_OK;
-}
-
 // ---------------------------------------------------------------- launches
+struct Maps {
+  CUtensorMap a{}, b{}, al{}, bl{};
+};
+
 template <AKind AK, BKind BK, bool SPLIT3, int BN, int STAGES>
-int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& p, cudaStream_t st) {
+int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
   auto kern = umma_gemm_kernel<AK, BK, SPLIT3, BN, STAGES>;
   constexpr int smem = umma_smem_bytes<BN, SPLIT3, STAGES>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
@@ -135,35 +117,32 @@ int launch_umma(const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& 
                  "cudaFuncSetAttribute(max dynamic smem)");
     attr_set[dev & 63] = true;
   }
-  dim3 grid(p.col_tiles, p.row_tiles);
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  const long long blocks = static_cast<long long>(p.row_tiles) * p.col_tiles;
+  if (blocks > 0x7FFFFFFFLL) return set_error(SMM_ERR_INVALID, "product too large for one launch");
+  kern<<<static_cast<unsigned>(blocks), kThreads, smem, st>>>(m.a, m.b, m.al, m.bl, p);
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "tcgen05 contraction launch");
   return SMM_OK;
 }
 
 // Stage counts fill ~192 KiB of shared memory.
+// Stage counts fill ~192 KiB of shared memory.
 template <AKind AK, BKind BK, int BN>
-int launch_mode(bool split3, const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& p, cudaStream_t st) {
-  if constexpr (BN <= 128) {
-    if (split3) {
-      constexpr int S = (BN == 128) ? 6 : 8;
-      return launch_umma<AK, BK, true, BN, S>(ta, tb, p, st);
-    }
-  } else {
-    if (split3) return set_error(SMM_ERR_INVALID, "3xTF32 tiles are at most 128 columns wide");
+int launch_mode(bool split3, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+  if (split3) {
+    constexpr int S = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
+    return launch_umma<AK, BK, true, BN, S>(m, p, st);
   }
   constexpr int S = 8;
-  return launch_umma<AK, BK, false, BN, S>(ta, tb, p, st);
+  return launch_umma<AK, BK, false, BN, S>(m, p, st);
 }
 
 template <AKind AK, BKind BK>
-int launch_bn(int bn, bool split3, const CUtensorMap& ta, const CUtensorMap& tb, const UmmaParams& p,
-              cudaStream_t st) {
+int launch_bn(int bn, bool split3, const Maps& m, const UmmaParams& p, cudaStream_t st) {
   switch (bn) {
-    case 256: return launch_mode<AK, BK, 256>(split3, ta, tb, p, st);
-    case 128: return launch_mode<AK, BK, 128>(split3, ta, tb, p, st);
-    default: return launch_mode<AK, BK, 64>(split3, ta, tb, p, st);
+    case 256: return launch_mode<AK, BK, 256>(split3, m, p, st);
+    case 128: return launch_mode<AK, BK, 128>(split3, m, p, st);
+    default: return launch_mode<AK, BK, 64>(split3, m, p, st);
   }
 }
 
@@ -192,6 +171,7 @@ bool valid_mode(int mode) { return mode == SMM_MODE_3XTF32 || mode == SMM_MODE_T
 // ld) or a structured one (src, dim, row0).
 struct Operand {
   const float* ptr = nullptr;
+  const float* lo = nullptr;  // lo plane of ptr (3xTF32), same ld
   int ld = 0;
   const float* src = nullptr;
   int dim = 0;
@@ -199,20 +179,26 @@ struct Operand {
 };
 
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
-                    int N, int K, cudaStream_t st) {
+                    int N, int K, cudaStream_t st, float* C_lo = nullptr) {
   if (mode == SMM_MODE_BF16) return set_error(SMM_ERR_UNSUPPORTED, "bf16 mode not built for this operation");
   const bool split3 = (mode == SMM_MODE_3XTF32);
-  // 3xTF32 keeps two chunk accumulators and a running sum in tensor memory
-  // (3 x BN of its 512 columns), so its tiles are at most 128 wide.
-  const int bn = split3 ? std::min(pick_bn(M, N), 128) : pick_bn(M, N);
-  CUtensorMap tb{}, ta{};
+  const int bn = pick_bn(M, N);
+  Maps m;
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);
   if (b_tma) {
-    if (int rc = make_tmap(&tb, b.ptr, K, N, b.ld, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) return rc;
+    if (int rc = make_tmap(&m.b, b.ptr, K, N, b.ld, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) return rc;
+    if (split3) {
+      if (!b.lo) return set_error(SMM_ERR_INVALID, "internal: missing lo plane of B");
+      if (int rc = make_tmap(&m.bl, b.lo, K, N, b.ld, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) return rc;
+    }
   }
   if (a_tma) {
-    if (int rc = make_tmap(&ta, a.ptr, M, K, a.ld, 16, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
+    if (int rc = make_tmap(&m.a, a.ptr, M, K, a.ld, 16, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
+    if (split3) {
+      if (!a.lo) return set_error(SMM_ERR_INVALID, "internal: missing lo plane of A");
+      if (int rc = make_tmap(&m.al, a.lo, M, K, a.ld, 16, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
+    }
   }
   UmmaParams p{};
   p.M = M;
@@ -220,6 +206,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.K = K;
   p.C = C;
   p.ldc = ldc;
+  p.C_lo = C_lo;
   p.a_src = a.src;
   p.a_dim = a.dim;
   p.a_row0 = a.row0;
@@ -227,33 +214,34 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.b_dim = b.dim;
   p.row_tiles = (M + kBM - 1) / kBM;
   p.col_tiles = (N + bn - 1) / bn;
+  p.raster_group = 8;
   p.status = device_status_word();
   p.wait_limit_ns = wait_limit_ns();
   p.trace = g_trace;
   if (!p.status) return set_error(SMM_ERR_CUDA, "device status word unavailable");
-  if (p.row_tiles > 65535) return set_error(SMM_ERR_INVALID, "M = %d too large (max %d)", M, 65535 * kBM);
   g_trace = nullptr;
   if (bk == BKind::Dense) {
     switch (ak) {
-      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, split3, ta, tb, p, st);
-      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, split3, ta, tb, p, st);
-      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, split3, ta, tb, p, st);
-      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, split3, ta, tb, p, st);
-      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, split3, ta, tb, p, st);
+      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, split3, m, p, st);
+      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, split3, m, p, st);
+      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, split3, m, p, st);
+      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, split3, m, p, st);
+      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, split3, m, p, st);
     }
   }
   if (ak == AKind::Dense && bk == BKind::UpperPacked)
-    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, split3, ta, tb, p, st);
+    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, split3, m, p, st);
   if (ak == AKind::Dense && bk == BKind::SymmPacked)
-    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, split3, ta, tb, p, st);
+    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, split3, m, p, st);
   if (ak == AKind::SymmPacked && bk == BKind::SymmPacked)
-    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, split3, ta, tb, p, st);
+    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, split3, m, p, st);
   return set_error(SMM_ERR_INVALID, "unsupported operand kinds");
 }
 
-Operand dense_op(const float* ptr, int ld) {
+Operand dense_op(const float* ptr, const float* lo, int ld) {
   Operand o;
   o.ptr = ptr;
+  o.lo = lo;
   o.ld = ld;
   return o;
 }
@@ -265,28 +253,80 @@ Operand structured_op(const float* src, int dim, int row0 = 0) {
   return o;
 }
 
-// A right operand (rows x cols row-major) usable by TMA: either the caller's
-// array or a padded copy in the workspace.
+// ---------------------------------------------------------------- operand staging
+// hi (optional) = src with zero columns appended up to ld_dst; lo (optional)
+// = the same minus its tf32 truncation, i.e. the 3xTF32 low plane.
+__global__ void split_planes_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
+                                    float* __restrict__ hi, float* __restrict__ lo, int ld_dst) {
+  const long long total = static_cast<long long>(rows) * ld_dst;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / ld_dst;
+    const int c = static_cast<int>(i - r * ld_dst);
+    const float x = c < cols ? src[r * ld_src + c] : 0.0f;
+    if (hi) hi[i] = x;
+    if (lo) lo[i] = x - tf32_hi(x);
+  }
+}
+
+// lo plane of a contiguous, 16-byte-aligned matrix (the common case), 128-bit.
+__global__ void lo_plane_vec4_kernel(const float4* __restrict__ src, float4* __restrict__ lo, long long n4) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 x = __ldcs(src + i);
+    __stcs(lo + i, make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w)));
+  }
+}
+
+// A TMA-fed operand (rows x cols row-major): the caller's array or a padded
+// copy, plus its lo plane in 3xTF32 mode, both in the workspace.
 struct Staged {
   const float* ptr;
+  const float* lo;
   int ld;
 };
 
 bool needs_pad(const float* p, int cols) { return (cols % 4 != 0) || !aligned16(p); }
-size_t pad_bytes(const float* p, int rows, int cols) {
-  return needs_pad(p, cols) ? round256(static_cast<size_t>(rows) * round4(cols) * sizeof(float)) : 0;
+size_t plane_bytes(int rows, int cols) { return round256(static_cast<size_t>(rows) * round4(cols) * sizeof(float)); }
+size_t staged_bytes(const float* p, int rows, int cols, bool split3) {
+  return (needs_pad(p, cols) ? plane_bytes(rows, cols) : 0) + (split3 ? plane_bytes(rows, cols) : 0);
+}
+// Workspace bound when the pointer is not known yet (assumes a padded copy).
+size_t staged_bytes_bound(int rows, int cols, bool split3) {
+  return (split3 ? 2 : 1) * plane_bytes(rows, cols);
 }
 
-int stage_operand(const float* src, int rows, int cols, uint8_t*& ws_cur, Staged* out, cudaStream_t st) {
-  if (!needs_pad(src, cols)) {
-    *out = {src, cols};
+int stage_operand(const float* src, int rows, int cols, bool split3, uint8_t*& ws_cur, Staged* out,
+                  cudaStream_t st) {
+  const bool pad = needs_pad(src, cols);
+  if (!pad && !split3) {
+    *out = {src, nullptr, cols};
     return SMM_OK;
   }
-  float* dst = reinterpret_cast<float*>(ws_cur);
-  const int ld = round4(cols);
-  if (int rc = pad_copy(src, rows, cols, dst, ld, st)) return rc;
-  ws_cur += round256(static_cast<size_t>(rows) * ld * sizeof(float));
-  *out = {dst, ld};
+  const int ld = pad ? round4(cols) : cols;
+  float* hi = nullptr;
+  if (pad) {
+    hi = reinterpret_cast<float*>(ws_cur);
+    ws_cur += plane_bytes(rows, cols);
+  }
+  float* lo = nullptr;
+  if (split3) {
+    lo = reinterpret_cast<float*>(ws_cur);
+    ws_cur += plane_bytes(rows, cols);
+  }
+  const long long total = static_cast<long long>(rows) * ld;
+  if (!pad) {
+    const long long n4 = total / 4;
+    const int grid = static_cast<int>(std::min<long long>((n4 + 255) / 256, 148LL * 8));
+    lo_plane_vec4_kernel<<<std::max(grid, 1), 256, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                                            reinterpret_cast<float4*>(lo), n4);
+  } else {
+    const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    split_planes_kernel<<<std::max(grid, 1), 256, 0, st>>>(src, rows, cols, cols, hi, lo, ld);
+  }
+  count_launch();
+  SMM_CUDA_TRY(cudaGetLastError(), "operand staging launch");
+  *out = {pad ? hi : src, lo, ld};
   return SMM_OK;
 }
 
@@ -328,14 +368,9 @@ extern "C" int smm_device_status(void* stream) {
 }
 
 extern "C" size_t smm_gemm_workspace_size(int M, int N, int K, int mode) {
-  (void)mode;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  // Conservative: assumes both operands need a padded copy unless the shape
-  // alone guarantees they do not (pointer alignment is not known here).
-  size_t b = 0;
-  b += round256(static_cast<size_t>(M) * round4(K) * sizeof(float));
-  b += round256(static_cast<size_t>(K) * round4(N) * sizeof(float));
-  return b;
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  return staged_bytes_bound(M, K, s3) + staged_bytes_bound(K, N, s3);
 }
 
 extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* ws,
@@ -346,21 +381,22 @@ extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, 
   if (!C || (K > 0 && (!A || !B))) return set_error(SMM_ERR_INVALID, "smm_gemm: null pointer");
   cudaStream_t st = as_stream(stream);
   if (K == 0) return zero_output(C, M, N, st);
-  const size_t need = pad_bytes(A, M, K) + pad_bytes(B, K, N);
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  const size_t need = staged_bytes(A, M, K, s3) + staged_bytes(B, K, N, s3);
   if (int rc = check_ws("smm_gemm", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged a, b;
-  if (int rc = stage_operand(A, M, K, cur, &a, st)) return rc;
-  if (int rc = stage_operand(B, K, N, cur, &b, st)) return rc;
-  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.ld), dense_op(b.ptr, b.ld), C, N, M, N, K,
-                         st);
+  if (int rc = stage_operand(A, M, K, s3, cur, &a, st)) return rc;
+  if (int rc = stage_operand(B, K, N, s3, cur, &b, st)) return rc;
+  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld), dense_op(b.ptr, b.lo, b.ld),
+                         C, N, M, N, K, st);
 }
 
 extern "C" size_t smm_upper_left_workspace_size(int N, int ncols, int u_fmt, int mode) {
-  (void)mode;
   if (N <= 0 || ncols <= 0) return 0;
-  size_t b = round256(static_cast<size_t>(N) * round4(ncols) * sizeof(float));
-  if (u_fmt == SMM_FMT_DENSE) b += round256(static_cast<size_t>(N) * round4(N) * sizeof(float));
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  size_t b = staged_bytes_bound(N, ncols, s3);
+  if (u_fmt == SMM_FMT_DENSE) b += staged_bytes_bound(N, N, s3);
   return b;
 }
 
@@ -381,24 +417,25 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!U || !B || !C) return set_error(SMM_ERR_INVALID, "smm_upper_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  size_t need = pad_bytes(B, N, ncols);
-  if (u_fmt == SMM_FMT_DENSE) need += pad_bytes(U, N, N);
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  size_t need = staged_bytes(B, N, ncols, s3);
+  if (u_fmt == SMM_FMT_DENSE) need += staged_bytes(U, N, N, s3);
   if (int rc = check_ws("smm_upper_left", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
-  if (int rc = stage_operand(B, N, ncols, cur, &b, st)) return rc;
+  if (int rc = stage_operand(B, N, ncols, s3, cur, &b, st)) return rc;
   if (u_fmt == SMM_FMT_DENSE) {
     Staged u;
-    if (int rc = stage_operand(U, N, N, cur, &u, st)) return rc;
-    const float* urows = u.ptr + static_cast<size_t>(row0) * u.ld;
-    Operand ua = dense_op(urows, u.ld);
+    if (int rc = stage_operand(U, N, N, s3, cur, &u, st)) return rc;
+    const size_t off = static_cast<size_t>(row0) * u.ld;
+    Operand ua = dense_op(u.ptr + off, u.lo ? u.lo + off : nullptr, u.ld);
     ua.dim = N;
     ua.row0 = row0;
-    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.ld), C, ncols, nrows, ncols,
-                           N, st);
+    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.lo, b.ld), C, ncols, nrows,
+                           ncols, N, st);
   }
-  return run_contraction(AKind::UpperPacked, BKind::Dense, mode, structured_op(U, N, row0), dense_op(b.ptr, b.ld), C,
-                         ncols, nrows, ncols, N, st);
+  return run_contraction(AKind::UpperPacked, BKind::Dense, mode, structured_op(U, N, row0), dense_op(b.ptr, b.lo, b.ld),
+                         C, ncols, nrows, ncols, N, st);
 }
 
 extern "C" int smm_upper_left(const float* U, int u_fmt, const float* B, float* C, int N, int ncols, int mode,
@@ -407,9 +444,8 @@ extern "C" int smm_upper_left(const float* U, int u_fmt, const float* B, float* 
 }
 
 extern "C" size_t smm_toeplitz_left_workspace_size(int N, int ncols, int mode) {
-  (void)mode;
   if (N <= 0 || ncols <= 0) return 0;
-  return round256(static_cast<size_t>(N) * round4(ncols) * sizeof(float));
+  return staged_bytes_bound(N, ncols, mode == SMM_MODE_3XTF32);
 }
 
 extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, int N, int ncols, int row0,
@@ -419,11 +455,12 @@ extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, 
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!g || !B || !C) return set_error(SMM_ERR_INVALID, "smm_toeplitz_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  if (int rc = check_ws("smm_toeplitz_left", ws, ws_bytes, pad_bytes(B, N, ncols))) return rc;
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  if (int rc = check_ws("smm_toeplitz_left", ws, ws_bytes, staged_bytes(B, N, ncols, s3))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
-  if (int rc = stage_operand(B, N, ncols, cur, &b, st)) return rc;
-  return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), dense_op(b.ptr, b.ld), C,
+  if (int rc = stage_operand(B, N, ncols, s3, cur, &b, st)) return rc;
+  return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), dense_op(b.ptr, b.lo, b.ld), C,
                          ncols, nrows, ncols, N, st);
 }
 
@@ -443,12 +480,13 @@ extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int 
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, pad_bytes(B, N, ncols))) return rc;
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, staged_bytes(B, N, ncols, s3))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
-  if (int rc = stage_operand(B, N, ncols, cur, &b, st)) return rc;
-  return run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N, row0), dense_op(b.ptr, b.ld), C,
-                         ncols, nrows, ncols, N, st);
+  if (int rc = stage_operand(B, N, ncols, s3, cur, &b, st)) return rc;
+  return run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N, row0), dense_op(b.ptr, b.lo, b.ld),
+                         C, ncols, nrows, ncols, N, st);
 }
 
 extern "C" int smm_symm_left(const float* S, const float* B, float* C, int N, int ncols, int mode, void* ws,
@@ -456,11 +494,18 @@ extern "C" int smm_symm_left(const float* S, const float* B, float* C, int N, in
   return smm_symm_left_rows(S, B, C, N, ncols, 0, N, mode, ws, ws_bytes, stream);
 }
 
+namespace {
+// Workspace of the sandwich: X = S B (16-byte row stride) and, in 3xTF32, its
+// lo plane (written by the first product's epilogue), then the staged A and B.
+size_t sandwich_need(const float* A, const float* B, int N, bool s3) {
+  return (s3 ? 2 : 1) * plane_bytes(N, N) + staged_bytes(A, N, N, s3) + staged_bytes(B, N, N, s3);
+}
+}  // namespace
+
 extern "C" size_t smm_symm_sandwich_workspace_size(int N, int mode) {
-  (void)mode;
   if (N <= 0) return 0;
-  const size_t mat = round256(static_cast<size_t>(N) * round4(N) * sizeof(float));
-  return 3 * mat;  // X = S B (padded stride), plus padded copies of A and B when needed
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  return (s3 ? 2 : 1) * plane_bytes(N, N) + 2 * staged_bytes_bound(N, N, s3);
 }
 
 extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B, float* C, int N, int mode,
@@ -470,29 +515,33 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   if (N == 0) return SMM_OK;
   if (!A || !S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich: null pointer");
   cudaStream_t st = as_stream(stream);
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  if (int rc = check_ws("smm_symm_sandwich", ws, ws_bytes, sandwich_need(A, B, N, s3))) return rc;
   const int ldx = round4(N);
-  const size_t xbytes = round256(static_cast<size_t>(N) * ldx * sizeof(float));
-  const size_t need = xbytes + pad_bytes(A, N, N) + pad_bytes(B, N, N);
-  if (int rc = check_ws("smm_symm_sandwich", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   float* X = reinterpret_cast<float*>(cur);
-  cur += xbytes;
+  cur += plane_bytes(N, N);
+  float* X_lo = nullptr;
+  if (s3) {
+    X_lo = reinterpret_cast<float*>(cur);
+    cur += plane_bytes(N, N);
+  }
   Staged a, b;
-  if (int rc = stage_operand(A, N, N, cur, &a, st)) return rc;
-  if (int rc = stage_operand(B, N, N, cur, &b, st)) return rc;
-  if (ldx != N) SMM_CUDA_TRY(cudaMemsetAsync(X, 0, xbytes, st), "zero intermediate padding");
-  // X = S B (S packed, mirrored on chip), then C = A X.
-  if (int rc = run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N), dense_op(b.ptr, b.ld), X,
-                               ldx, N, N, N, st))
+  if (int rc = stage_operand(A, N, N, s3, cur, &a, st)) return rc;
+  if (int rc = stage_operand(B, N, N, s3, cur, &b, st)) return rc;
+  // X = S B (S packed, mirrored on chip; the epilogue also writes X's lo
+  // plane), then C = A X.
+  if (int rc = run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N), dense_op(b.ptr, b.lo, b.ld),
+                               X, ldx, N, N, N, st, X_lo))
     return rc;
-  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.ld), dense_op(X, ldx), C, N, N, N, N, st);
+  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld), dense_op(X, X_lo, ldx), C, N,
+                         N, N, N, st);
 }
 
 // ---------------------------------------------------------------- structured right operand
 extern "C" size_t smm_gen_x_struct_workspace_size(int M, int N, int mode) {
-  (void)mode;
   if (M <= 0 || N <= 0) return 0;
-  return round256(static_cast<size_t>(M) * round4(N) * sizeof(float));
+  return staged_bytes_bound(M, N, mode == SMM_MODE_3XTF32);
 }
 
 namespace {
@@ -502,11 +551,12 @@ int gen_x_struct(const char* who, BKind bk, const float* A, const float* X, floa
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
   if (M == 0 || N == 0) return SMM_OK;
   if (!A || !X || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
-  if (int rc = check_ws(who, ws, ws_bytes, pad_bytes(A, M, N))) return rc;
+  const bool s3 = (mode == SMM_MODE_3XTF32);
+  if (int rc = check_ws(who, ws, ws_bytes, staged_bytes(A, M, N, s3))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged a;
-  if (int rc = stage_operand(A, M, N, cur, &a, st)) return rc;
-  return run_contraction(AKind::Dense, bk, mode, dense_op(a.ptr, a.ld), structured_op(X, N), C, N, M, N, N, st);
+  if (int rc = stage_operand(A, M, N, s3, cur, &a, st)) return rc;
+  return run_contraction(AKind::Dense, bk, mode, dense_op(a.ptr, a.lo, a.ld), structured_op(X, N), C, N, M, N, N, st);
 }
 }  // namespace
 
@@ -571,9 +621,10 @@ extern "C" int smm_debug_trace_next(unsigned* trace) {
 }
 
 // ---------------------------------------------------------------- allocation-free sandwich
-// Scratch of smm_symm_sandwich_noalloc: the S*B intermediate, plus padded
-// copies of A and B when their rows are not 16-byte multiples.  A fixed
-// 16 MiB that every GPU which loads this library holds until process exit.
+// Scratch of smm_symm_sandwich_noalloc: the S*B intermediate, its lo plane and
+// those of A and B (3xTF32), plus padded copies of A and B when their rows
+// are not 16-byte multiples.  A fixed 16 MiB that every GPU which loads this
+// library holds until process exit.
 // Host code must not use this name as an address (it is a host-side stand-in
 // for the symbol); the device address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[size_t(16) << 20];
@@ -607,14 +658,12 @@ extern "C" int smm_symm_sandwich_noalloc(const float* A, const float* S, const f
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: unknown mode %d", mode);
   if (N == 0) return SMM_OK;
   if (!A || !S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: null pointer");
-  // Same scratch layout smm_symm_sandwich uses: X = S B with a 16-byte row
-  // stride, then any padded operand copies.
-  const size_t need = round256(static_cast<size_t>(N) * round4(N) * sizeof(float)) + pad_bytes(A, N, N) +
-                      pad_bytes(B, N, N);
+  // Same scratch layout smm_symm_sandwich uses.
+  const size_t need = sandwich_need(A, B, N, mode == SMM_MODE_3XTF32);
   if (need > kNoallocScratchBytes)
     return set_error(SMM_ERR_WORKSPACE,
                      "smm_symm_sandwich_noalloc: N = %d needs %zu bytes of scratch but the static scratch holds %zu "
-                     "(N <= 2048 when N %% 4 == 0 and A, B are 16-byte aligned)",
+                     "(3xTF32: N <= 1024, TF32: N <= 2048, with N %% 4 == 0 and 16-byte-aligned A, B)",
                      N, need, kNoallocScratchBytes);
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;

@@ -1,38 +1,47 @@
 // The tcgen05 contraction engine shared by every tensor-core operation of the
 // library: C(M x N) = Aop(M x K) * B(K x N), fp32 row-major C, accumulator in
-// tensor memory.
+// tensor memory (TMEM).
 //
 // Tile: 128 x BN output per CTA (BN = 64, 128 or 256), K-blocks of 16 fp32
 // (64 bytes) per pipeline stage, STAGES stages in shared memory.
 //
-// Operand staging per stage:
+// Operand staging per stage (hi = the fp32 value; kind::tf32 reads its upper
+// 19 bits, i.e. truncates; lo = x - tf32(x), exact in fp32):
 //   A (K-major, 128 rows x 64 B, 64-byte swizzle):
-//     AKind::Dense       TMA tile load of a row-major A
-//     AKind::UpperPacked built by the transform warps from packed-upper
-//                        storage (zeros below the diagonal; k-blocks left of
-//                        the row tile's diagonal are never visited)
-//     AKind::Toeplitz    built from the 2N-1 generator: row r of the tile is
-//                        a contiguous generator window
-//     AKind::SymmPacked  built from packed-upper storage, mirrored below the
-//                        diagonal
-//   B (MN-major, BN columns x 16 k-rows): TMA tile loads of a row-major B,
-//     32 columns (128 B) per box, 128-byte swizzle with 32-byte atoms (the
-//     only swizzle kind::tf32 accepts for an MN-major operand; with the plain
-//     128-byte swizzle the MMA produces nothing).
+//     AKind::Dense / UpperDense   TMA tile loads of a row-major A (and, in
+//                                 3xTF32, of its precomputed lo plane)
+//     AKind::UpperPacked          built on chip from packed-upper storage;
+//                                 k-blocks left of the row tile's diagonal are
+//                                 never visited
+//     AKind::Toeplitz             built on chip from the 2N-1 generator (row r
+//                                 of the tile is a contiguous window)
+//     AKind::SymmPacked           built on chip from packed-upper storage,
+//                                 mirrored below the diagonal
+//   B (MN-major, BN columns x 16 k-rows, 32-column boxes, 128-byte swizzle
+//     with 32-byte atoms — the only swizzle kind::tf32 accepts for an MN-major
+//     operand; with the plain 128-byte swizzle the MMA produces nothing):
+//     BKind::Dense                TMA tile loads of a row-major B (+ lo plane)
+//     BKind::UpperPacked/SymmPacked  built on chip (the DSL's Gen@Upper,
+//                                 Gen@Symm, Symm@Symm)
 //
-// 3xTF32 (SPLIT3): the transform warps write lo = x - tf32(x) planes of both
-// operands next to the raw tiles, and the MMA issuer runs three MMAs per
-// k-step: hi*hi + hi*lo + lo*hi.  The raw fp32 tile serves as the hi operand
-// (kind::tf32 reads the upper 19 bits of each element).
+// 3xTF32 (SPLIT3): three MMAs per k-step, hi*hi + hi*lo + lo*hi.  The tensor
+// core's fp32 accumulation truncates on every update, so with same-sign data
+// its error grows with the number of updates into one accumulator.  The MMA
+// therefore accumulates chunks of kChunk k-blocks, each starting from zero;
+// at every chunk boundary the epilogue warps copy the accumulator to
+// registers (the MMA waits only for that copy), then add it into a running
+// sum kept in a second TMEM region with round-to-nearest fp32 adds while the
+// next chunk runs.  Error stays ~1e-6 normwise whatever K is.
 //
-// Warp roles (192 threads):
-//   warp 0     TMA producer (one lane)
-//   warp 1     TMEM allocator + MMA issuer (one lane)
-//   warps 2-5  transform (lo planes, structured A tiles), then epilogue
-//              (TMEM -> registers -> global C)
+// Warp roles (320 threads):
+//   warp 0      TMA producer (one lane)
+//   warp 1      TMEM allocator + MMA issuer (one lane)
+//   warps 2-9   transform (structured operand tiles), chunk folds, epilogue
+//               (TMEM -> registers -> global C); warp w owns TMEM lanes
+//               32*(w%4).. and column half (w-2)/4 of the tile
 //
-// Every wait is bounded (WaitCtx): on expiry the kernel records
-// kDevErrTimeout in the status word, the other roles stop waiting, in-flight
+// Every wait is bounded (WaitCtx): on expiry the kernel records which role
+// gave up in the status word, the other roles stop waiting, in-flight
 // copies/MMAs are drained (bounded), TMEM is freed and the CTA exits.
 #pragma once
 #include "smm_device.cuh"
@@ -48,6 +57,8 @@ struct UmmaParams {
   int M, N, K;             // C is M x N; reduction length K
   float* C;                // row-major, leading dimension ldc
   int ldc;
+  float* C_lo;             // optional: also store lo(C) = C - tf32(C) here (same ldc), so
+                           // a following 3xTF32 product can read C as a split operand
   const float* a_src;      // packed U / generator / packed S (structured A kinds)
   int a_dim;               // order of the structured matrix
   int a_row0;              // row of the structured matrix that output row 0 maps to
@@ -55,22 +66,23 @@ struct UmmaParams {
   int b_dim;               // order of the structured right operand
   int row_tiles;           // ceil(M / 128)
   int col_tiles;           // ceil(N / BN)
+  int raster_group;        // row tiles per rasterisation group (L2 reuse)
   uint32_t* status;        // device status word (sticky error bits)
   unsigned long long wait_limit_ns;
-  uint32_t* trace;         // optional diagnostic record of CTA (0,0); null in normal use
+  uint32_t* trace;         // optional diagnostic record of CTA 0; null in normal use
 };
 
 // Slots of the diagnostic record (UmmaParams::trace, 64 words).
-enum : int {
-  kTrTmem = 0, kTrNumKb = 1, kTrA = 2 /*8 words*/, kTrB = 10 /*8 words*/, kTrAccOk = 18,
-  kTrAcc = 19 /*16 words*/, kTrMmas = 35, kTrDescA = 36 /*2 words*/, kTrDescB = 38 /*2*/, kTrIdesc = 40,
-  kTrEpiDone = 41, kTrWords = 64
-};
+enum : int { kTrTmem = 0, kTrNumKb = 1, kTrAccOk = 2, kTrMmas = 3, kTrAcc = 4 /*16 words*/, kTrWords = 64 };
 
 constexpr int kBM = 128;
-constexpr int kBK = 16;                   // fp32 elements per k-block (64 bytes)
-constexpr int kThreads = 192;
+constexpr int kBK = 16;                     // fp32 elements per k-block (64 bytes)
+constexpr int kThreads = 320;
+constexpr int kXformThreads = 256;          // warps 2-9
 constexpr int kATileBytes = kBM * kBK * 4;  // 8 KiB
+// 3xTF32 chunk length in k-blocks: 3 * 12 * 2 = 72 truncating updates per
+// chunk accumulator (measured bias ~5e-8 of |C| per update on same-sign data).
+constexpr int kChunk = 12;
 
 template <int BN>
 struct TileGeom {
@@ -83,19 +95,10 @@ __host__ __device__ constexpr int stage_bytes() {
   return (SPLIT3 ? 2 : 1) * (kATileBytes + TileGeom<BN>::kBTileBytes);
 }
 
-// 3xTF32 accumulates in chunks of kChunk k-blocks: the tensor core's fp32
-// accumulation truncates on every update, so with same-sign data its error
-// grows with the number of updates into one accumulator.  Each chunk goes
-// to one of two ping-pong accumulators (overwritten at chunk start) and the
-// transform warps fold finished chunks into a third TMEM region with
-// round-to-nearest fp32 adds, bounding the truncation bias to
-// 3 * kChunk * 2 updates whatever K is.
-constexpr int kChunk = 8;
-
 template <int BN, bool SPLIT3>
 __host__ __device__ constexpr uint32_t tmem_cols() {
-  // SPLIT3: acc0 [0,BN), acc1 [BN,2BN), running sum [2BN,3BN)
-  return SPLIT3 ? (3 * BN <= 256 ? 256u : 512u) : (BN < 32 ? 32u : static_cast<uint32_t>(BN));
+  // SPLIT3: chunk accumulator [0,BN) and running sum [BN,2BN)
+  return SPLIT3 ? (2 * BN <= 128 ? 128u : (2 * BN <= 256 ? 256u : 512u)) : (BN < 32 ? 32u : static_cast<uint32_t>(BN));
 }
 
 template <int BN, bool SPLIT3, int STAGES>
@@ -121,52 +124,7 @@ __device__ __forceinline__ float a_value(const float* __restrict__ src, int n, i
   }
 }
 
-// The 16 values one transform thread contributes to a structured A stage
-// tile (rows m0.., columns k0..k0+15), gathered into registers so all 16
-// loads are in flight together (the tile is rebuilt every stage, so load
-// latency, not bandwidth, bounds this producer).
-//   lanes along k (16 lanes per row, two rows per warp instruction): rows
-//     tw*32 + 2*it + lane/16, column lane%16 — coalesced along a packed row
-//     or a generator window;
-//   lanes along rows (symmetric tiles wholly below the diagonal, whose
-//     elements are the mirror S[k][row]): row tw*32 + lane, column it —
-//     coalesced along packed row k.
-template <AKind AK>
-__device__ __forceinline__ bool a_rows_mapping(int g_first, int k0) {
-  return AK == AKind::SymmPacked && k0 + kBK <= g_first;
-}
-
-template <AKind AK>
-__device__ __forceinline__ void a_gather(float (&v)[16], const UmmaParams& p, int g_first, int k0, int tw,
-                                         int lane) {
-  if (a_rows_mapping<AK>(g_first, k0)) {
-    const int gr = g_first + tw * 32 + lane;
-#pragma unroll
-    for (int it = 0; it < 16; ++it) v[it] = a_value<AK>(p.a_src, p.a_dim, gr, k0 + it);
-  } else {
-    const int k = k0 + (lane & 15);
-#pragma unroll
-    for (int it = 0; it < 16; ++it) v[it] = a_value<AK>(p.a_src, p.a_dim, g_first + tw * 32 + it * 2 + (lane >> 4), k);
-  }
-}
-
-template <AKind AK, bool SPLIT3>
-__device__ __forceinline__ void a_store(const float (&v)[16], uint8_t* ah, uint8_t* al, int g_first, int k0, int tw,
-                                        int lane) {
-  const bool rows = a_rows_mapping<AK>(g_first, k0);
-#pragma unroll
-  for (int it = 0; it < 16; ++it) {
-    const int r = rows ? tw * 32 + lane : tw * 32 + it * 2 + (lane >> 4);
-    const int kl = rows ? it : (lane & 15);
-    const uint32_t off = swz_offset(r, kl >> 2, 64) + (kl & 3) * 4;
-    const float hi = tf32_hi(v[it]);
-    *reinterpret_cast<float*>(ah + off) = hi;
-    if constexpr (SPLIT3) *reinterpret_cast<float*>(al + off) = v[it] - hi;
-  }
-}
-
-// Value of the structured right operand at (row k, column n); zero outside
-// the n x n matrix.
+// Value of the structured right operand at (row k, column n); zero outside.
 template <BKind BK>
 __device__ __forceinline__ float b_value(const float* __restrict__ src, int nd, int k, int n) {
   if (k >= nd || n >= nd) return 0.0f;
@@ -178,40 +136,131 @@ __device__ __forceinline__ float b_value(const float* __restrict__ src, int nd, 
 }
 
 // Byte offset of element (k-row kr, column n) in a B stage tile: 32-column
-// boxes of 16 rows x 128 B, 128-byte swizzle with 32-byte atoms
-// (32-byte granule index ^= row & 3).
+// boxes of 16 rows x 128 B, 128-byte swizzle with 32-byte atoms (32-byte
+// granule index ^= row & 3).
 __device__ __forceinline__ uint32_t b_tile_offset(uint32_t kr, uint32_t n) {
   const uint32_t j = n & 31u;
   return (n >> 5) * 2048u + kr * 128u + ((((j >> 3) ^ (kr & 3u))) << 5) + (j & 7u) * 4u;
 }
 
+// ---------------------------------------------------------------- structured A
+// The 8 values one transform thread contributes to a structured A stage tile
+// (rows m0.., columns k0..k0+15), gathered into registers so all loads are in
+// flight together (latency, not bandwidth, bounds this producer).
+//   lanes along k (16 lanes per row, two rows per warp instruction): rows
+//     xw*16 + 2*it + lane/16, column lane%16 — coalesced along a packed row
+//     or a generator window;
+//   lanes along rows (symmetric tiles wholly below the diagonal, whose
+//     elements are the mirror S[k][row]): row (xw%4)*32 + lane, column
+//     (xw/4)*8 + it — coalesced along packed row k.
+template <AKind AK>
+__device__ __forceinline__ bool a_rows_mapping(int g_first, int k0) {
+  return AK == AKind::SymmPacked && k0 + kBK <= g_first;
+}
+
+__device__ __forceinline__ void a_coord(bool rows, int xw, int lane, int it, int& r, int& kl) {
+  if (rows) {
+    r = (xw & 3) * 32 + lane;
+    kl = (xw >> 2) * 8 + it;
+  } else {
+    r = xw * 16 + it * 2 + (lane >> 4);
+    kl = lane & 15;
+  }
+}
+
+template <AKind AK>
+__device__ __forceinline__ void a_gather(float (&v)[8], const UmmaParams& p, int g_first, int k0, int xw, int lane) {
+  const bool rows = a_rows_mapping<AK>(g_first, k0);
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    int r, kl;
+    a_coord(rows, xw, lane, it, r, kl);
+    v[it] = a_value<AK>(p.a_src, p.a_dim, g_first + r, k0 + kl);
+  }
+}
+
+template <AKind AK, bool SPLIT3>
+__device__ __forceinline__ void a_store(const float (&v)[8], uint8_t* ah, uint8_t* al, int g_first, int k0, int xw,
+                                        int lane) {
+  const bool rows = a_rows_mapping<AK>(g_first, k0);
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    int r, kl;
+    a_coord(rows, xw, lane, it, r, kl);
+    const uint32_t off = swz_offset(r, kl >> 2, 64) + (kl & 3) * 4;
+    const float hi = tf32_hi(v[it]);
+    *reinterpret_cast<float*>(ah + off) = hi;
+    if constexpr (SPLIT3) *reinterpret_cast<float*>(al + off) = v[it] - hi;
+  }
+}
+
+// ---------------------------------------------------------------- structured B
+// Element e (0 .. BN/16-1) of transform thread t in a B stage tile.  Lanes
+// run along n (coalesced along packed row k); for symmetric tiles wholly
+// below the diagonal (every n < k, elements are the mirror S[n][k]) 16 lanes
+// run along k instead (coalesced along packed row n).
+template <int BN>
+__device__ __forceinline__ void b_coord(bool mirror, int t, int e, int& kr, int& n) {
+  if (mirror) {
+    const int xw = t >> 5, lane = t & 31;
+    kr = lane & 15;
+    n = (e * 8 + xw) * 2 + (lane >> 4);
+  } else {
+    const int lin = e * kXformThreads + t;
+    kr = lin / BN;
+    n = lin % BN;
+  }
+}
+
+template <BKind BK, int BN, bool SPLIT3>
+__device__ __forceinline__ void b_build(const UmmaParams& p, uint8_t* bh, uint8_t* bl, int k0, int n0, int t) {
+  const bool mirror = (BK == BKind::SymmPacked) && (n0 + BN <= k0);
+  constexpr int kPer = (kBK * BN) / kXformThreads;  // 4, 8 or 16
+  float v[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    int kr, n;
+    b_coord<BN>(mirror, t, e, kr, n);
+    v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
+  }
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    int kr, n;
+    b_coord<BN>(mirror, t, e, kr, n);
+    const uint32_t off = b_tile_offset(kr, n);
+    const float hi = tf32_hi(v[e]);
+    *reinterpret_cast<float*>(bh + off) = hi;
+    if constexpr (SPLIT3) *reinterpret_cast<float*>(bl + off) = v[e] - hi;
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+// tmA/tmB map the operands (hi), tmAl/tmBl their lo planes (3xTF32 only).
 template <AKind AK, BKind BK, bool SPLIT3, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
                      const UmmaParams p) {
   constexpr int kBTile = TileGeom<BN>::kBTileBytes;
   constexpr int kStage = stage_bytes<BN, SPLIT3>();
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
   constexpr bool kBTma = (BK == BKind::Dense);
-  constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0);
+  constexpr bool kXform = !kATma || !kBTma;  // a tile is built on chip every stage
+  constexpr int kPlanes = SPLIT3 ? 2 : 1;
+  constexpr uint32_t kTxBytes = (kATma ? kPlanes * kATileBytes : 0) + (kBTma ? kPlanes * kBTile : 0);
   constexpr uint32_t kTmemCols = tmem_cols<BN, SPLIT3>();
-  static_assert(!SPLIT3 || 3 * BN <= 512, "3xTF32 needs three BN-column regions of tensor memory");
-  // A chunk's accumulator is folded when the transform warps reach stage
-  // (c+1)*kChunk + kFoldLag: by then the MMAs of chunk c have completed
-  // (the producer only refills a stage after its MMAs finish), and the fold
-  // still precedes the first stage of chunk c+2, which reuses the buffer.
-  constexpr int kFoldLag = STAGES - 1;
-  static_assert(!SPLIT3 || kFoldLag <= kChunk, "fold lag must not exceed the chunk length");
   constexpr uint32_t kIdesc = make_idesc(kFmtTF32, kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
+  constexpr int kHalf = BN / 2;  // columns per epilogue warp
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * kStage);
   uint64_t* ready = full + STAGES;
   uint64_t* empty = ready + STAGES;
-  uint64_t* accum_full = empty + STAGES;
-  uint64_t* acc_full = accum_full + 1;  // [2]: chunk finished in ping-pong buffer b
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 2);
+  uint64_t* accum_full = empty + STAGES;  // every MMA done
+  uint64_t* acc_full = accum_full + 1;    // chunk c done (phase c)
+  uint64_t* acc_empty = acc_full + 1;     // chunk c copied out of the accumulator (phase c)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   auto a_hi = [&](int s) { return smem + s * kStage; };
@@ -222,15 +271,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Tile coordinates.  blockIdx.y walks row tiles first-to-last, so for the
-  // triangular operand (whose row tile i has K range [128 i, N)) the longest
-  // tiles are dispatched first.
-  const int n_tile = blockIdx.x;
-  const int m_tile = blockIdx.y;
+  // Grouped rasterisation: consecutive CTAs cover raster_group row tiles x
+  // all column tiles, so a wave shares A and B slices through L2.  Groups go
+  // top to bottom, so for the triangular operand (row tile i has K range
+  // [128 i, N)) the longest tiles are dispatched first.
+  int m_tile, n_tile;
+  {
+    const int b = blockIdx.x;
+    const int per_group = p.raster_group * p.col_tiles;
+    const int g = b / per_group;
+    const int first = g * p.raster_group;
+    const int rows_here = min(p.raster_group, p.row_tiles - first);
+    const int in = b - g * per_group;
+    m_tile = first + in % rows_here;
+    n_tile = in / rows_here;
+  }
   const int m0 = m_tile * kBM;
   const int n0 = n_tile * BN;
-  // Rows of a triangular operand are zero left of the diagonal: row tile
-  // [g0, g0+128) of U needs k >= g0 only.
+  // Rows of a triangular left operand are zero left of the diagonal: row
+  // tile [g0, g0+128) of U needs k >= g0 only.
   int kb_begin = 0;
   if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + m0) / kBK;
   int kb_end = (p.K + kBK - 1) / kBK;
@@ -238,29 +297,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   // tile [n0, n0+BN) needs k < n0 + BN only.
   if constexpr (BK == BKind::UpperPacked) kb_end = min(kb_end, (n0 + BN - 1) / kBK + 1);
   const int num_kb = kb_end - kb_begin;
+  const int nch = SPLIT3 ? (num_kb + kChunk - 1) / kChunk : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 128);
+      mbar_init(&ready[s], kXformThreads);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum_full, 1);
-    mbar_init(&acc_full[0], 1);
-    mbar_init(&acc_full[1], 1);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kXformThreads);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    if constexpr (kATma) tma_prefetch_desc(&tmA);
-    if constexpr (kBTma) tma_prefetch_desc(&tmB);
+    if constexpr (kATma) {
+      tma_prefetch_desc(&tmA);
+      if constexpr (SPLIT3) tma_prefetch_desc(&tmAl);
+    }
+    if constexpr (kBTma) {
+      tma_prefetch_desc(&tmB);
+      if constexpr (SPLIT3) tma_prefetch_desc(&tmBl);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
-  const bool tr = p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0;
+  const bool tr = p.trace != nullptr && blockIdx.x == 0;
   if (tr && threadIdx.x == 0) {
     p.trace[kTrTmem] = tmem_base;
     p.trace[kTrNumKb] = static_cast<uint32_t>(num_kb);
@@ -281,11 +347,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
         mbar_arrive_expect_tx(&full[s], kTxBytes);
         const int k0 = (kb_begin + i) * kBK;
-        if constexpr (kATma) tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
+        if constexpr (kATma) {
+          tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
+          if constexpr (SPLIT3) tma_load_2d(a_lo(s), &tmAl, &full[s], k0, m0);
+        }
         if constexpr (kBTma) {
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
+          for (int c = 0; c < BN / 32; ++c) {
             tma_load_2d(b_hi(s) + c * TileGeom<BN>::kBChunkBytes, &tmB, &full[s], n0 + 32 * c, k0);
+            if constexpr (SPLIT3)
+              tma_load_2d(b_lo(s) + c * TileGeom<BN>::kBChunkBytes, &tmBl, &full[s], n0 + 32 * c, k0);
+          }
         }
         ++issued;
       }
@@ -305,14 +377,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < num_kb; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
-        if (!mbar_wait(&ready[s], ph, wmma)) break;
+        if (!mbar_wait(kXform ? &ready[s] : &full[s], ph, wmma)) break;
+        // 3xTF32: chunk c starts from zero once chunk c-1 has been copied out.
+        const bool chunk_start = SPLIT3 ? (i % kChunk == 0) : (i == 0);
+        if (SPLIT3 && chunk_start && i > 0) {
+          if (!mbar_wait(acc_empty, ((i / kChunk) - 1) & 1, wmma)) break;
+        }
         tc_fence_after_sync();
         const uint32_t sa = smem_u32(a_hi(s));
         const uint32_t sb = smem_u32(b_hi(s));
-        // 3xTF32: chunk c = i / kChunk accumulates into buffer c & 1 and
-        // starts from zero; otherwise one accumulator for the whole K.
-        const bool chunk_start = SPLIT3 ? (i % kChunk == 0) : (i == 0);
-        const uint32_t d_tmem = SPLIT3 ? tmem_base + static_cast<uint32_t>(((i / kChunk) & 1) * BN) : tmem_base;
 #pragma unroll
         for (int kk = 0; kk < kBK / 8; ++kk) {
           // A: K-major, 64-byte rows, 8-row groups 512 B apart; a k-step of
@@ -323,29 +396,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           // rows is 1024 B.
           const uint64_t db = make_smem_desc(sb + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
           const uint32_t acc = (!chunk_start || kk > 0) ? 1u : 0u;
-          umma_tf32(d_tmem, da, db, kIdesc, acc);
+          umma_tf32(tmem_base, da, db, kIdesc, acc);
           if constexpr (SPLIT3) {
             const uint32_t sal = smem_u32(a_lo(s));
             const uint32_t sbl = smem_u32(b_lo(s));
             const uint64_t dal = make_smem_desc(sal + kk * 32, 16, 512, kLayoutSw64);
             const uint64_t dbl =
                 make_smem_desc(sbl + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
-            umma_tf32(d_tmem, da, dbl, kIdesc, 1u);
-            umma_tf32(d_tmem, dal, db, kIdesc, 1u);
+            umma_tf32(tmem_base, da, dbl, kIdesc, 1u);
+            umma_tf32(tmem_base, dal, db, kIdesc, 1u);
           }
         }
         umma_commit(&empty[s]);
         if constexpr (SPLIT3) {
-          if (i % kChunk == kChunk - 1 || i == num_kb - 1) umma_commit(&acc_full[(i / kChunk) & 1]);
-        }
-        if (tr && i == 0) {
-          const uint64_t da = make_smem_desc(sa, 16, 512, kLayoutSw64);
-          const uint64_t db = make_smem_desc(sb, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
-          p.trace[kTrDescA] = static_cast<uint32_t>(da);
-          p.trace[kTrDescA + 1] = static_cast<uint32_t>(da >> 32);
-          p.trace[kTrDescB] = static_cast<uint32_t>(db);
-          p.trace[kTrDescB + 1] = static_cast<uint32_t>(db >> 32);
-          p.trace[kTrIdesc] = kIdesc;
+          if (i % kChunk == kChunk - 1 || i == num_kb - 1) umma_commit(acc_full);
         }
         if (tr) p.trace[kTrMmas] = static_cast<uint32_t>(i + 1);
       }
@@ -358,178 +422,118 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(accum_full, 0, drain);
     }
   } else {
-    // ------------------------------------------------------------ transform
-    const int t = threadIdx.x - 64;  // 0..127
-    const int tw = t >> 5;           // transform warp 0..3
+    // ------------------------------------------------------------ transform + epilogue
+    const int t = threadIdx.x - 64;  // 0..255
+    const int xw = t >> 5;           // transform warp 0..7
+    const int q = warp & 3;          // TMEM lanes 32q..32q+31 belong to this warp
+    const int h = xw >> 2;           // column half of the tile this warp reads back
+    const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t acc_col = tmem_base + lanes + static_cast<uint32_t>(h * kHalf);
+    const uint32_t sum_col = acc_col + static_cast<uint32_t>(BN);
     bool ok = true;
-    int folded = 0;                     // chunks already summed into the running sum
-    const int g_first = p.a_row0 + m0;  // structured-A row of tile row 0
-    float a_cur[16], a_nxt[16];
-    if constexpr (!kATma) {
-      if (num_kb > 0) a_gather<AK>(a_cur, p, g_first, kb_begin * kBK, tw, lane);
-    }
-    for (int i = 0; i < num_kb && ok; ++i) {
-      const int s = i % STAGES;
-      const uint32_t ph = (i / STAGES) & 1;
-      // Issue the next stage's global loads before waiting on this one: they
-      // need no shared memory, so their latency overlaps the wait and the
-      // stores below.
-      if constexpr (!kATma) {
-        if (i + 1 < num_kb) a_gather<AK>(a_nxt, p, g_first, (kb_begin + i + 1) * kBK, tw, lane);
+    int folded = 0;  // chunks already added into the running sum
+
+    // Copy chunk f's accumulator (this warp's 32 lanes x kHalf columns) to
+    // registers, release it to the MMA, then add it into the running sum.
+    auto fold = [&](int f) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(acc_full, f & 1, wxf))) return false;
+      tc_fence_after_sync();
+      uint32_t a[kHalf];
+#pragma unroll
+      for (int c = 0; c < kHalf; c += 16) tmem_ld_32x32b_x16(acc_col + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
+      tmem_wait_ld();
+      tc_fence_before_sync();
+      mbar_arrive(acc_empty);
+      if (f > 0) {
+#pragma unroll
+        for (int c = 0; c < kHalf; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(sum_col + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) a[c + j] = __float_as_uint(__uint_as_float(a[c + j]) + __uint_as_float(r[j]));
+        }
       }
-      if constexpr (SPLIT3) {
-        if (i >= kChunk + kFoldLag && (i - kFoldLag) % kChunk == 0) {
-          const int f = (i - kFoldLag) / kChunk - 1;  // chunk to fold
-          if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[f & 1], (f >> 1) & 1, wxf))) {
+#pragma unroll
+      for (int c = 0; c < kHalf; c += 16) tmem_st_32x32b_x16(sum_col + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
+      tmem_wait_st();
+      return true;
+    };
+
+    if constexpr (kXform) {
+      const int g_first = p.a_row0 + m0;  // structured-A row of tile row 0
+      float a_cur[8], a_nxt[8];
+      if constexpr (!kATma) {
+        if (num_kb > 0) a_gather<AK>(a_cur, p, g_first, kb_begin * kBK, xw, lane);
+      }
+      for (int i = 0; i < num_kb && ok; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        // Fold chunk `folded` once the stages after it are in flight: the
+        // MMA of chunk folded+1 cannot start before it, and stage i needs
+        // the MMA of stage i - STAGES, the first one of chunk folded+1.
+        if (SPLIT3 && folded < nch - 1 && i == (folded + 1) * kChunk + STAGES) {
+          if (!fold(folded)) {
             ok = false;
             break;
           }
-          tc_fence_after_sync();
-          const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
-          const uint32_t src = tmem_base + lanes + static_cast<uint32_t>((f & 1) * BN);
-          const uint32_t sum = tmem_base + lanes + static_cast<uint32_t>(2 * BN);
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 16) {
-            uint32_t r[16], q[16];
-            tmem_ld_32x32b_x16(src + c, r);
-            if (f > 0) tmem_ld_32x32b_x16(sum + c, q);
-            tmem_wait_ld();
-            if (f > 0) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(q[j]));
-            }
-            tmem_st_32x32b_x16(sum + c, r);
-          }
-          tmem_wait_st();
-          tc_fence_before_sync();
-          folded = f + 1;
+          ++folded;
         }
-      }
-      // Warp-uniform outcome: the tcgen05.ld below is .sync.aligned, so the
-      // lanes of a warp must never take different paths.
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) {
-        ok = false;
-        break;
-      }
-      const int k0 = (kb_begin + i) * kBK;
-      if constexpr (!kATma) {
-        a_store<AK, SPLIT3>(a_cur, a_hi(s), a_lo(s), g_first, k0, tw, lane);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) a_cur[j] = a_nxt[j];
-      } else if constexpr (SPLIT3) {
-        const float4* src = reinterpret_cast<const float4*>(a_hi(s));
-        float4* dst = reinterpret_cast<float4*>(a_lo(s));
-#pragma unroll
-        for (int j = t; j < kATileBytes / 16; j += 128) {
-          const float4 x = src[j];
-          dst[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+        // Issue the next stage's global loads before waiting on this one.
+        if constexpr (!kATma) {
+          if (i + 1 < num_kb) a_gather<AK>(a_nxt, p, g_first, (kb_begin + i + 1) * kBK, xw, lane);
         }
-      }
-      if constexpr (!kBTma) {
-        // Build the structured B tile: warp tw fills k-rows tw, tw+4, ...;
-        // each lane one column of a 32-column box (coalesced along packed rows).
-        uint8_t* bh = b_hi(s);
-        uint8_t* bl = b_lo(s);
-        // Symmetric tiles wholly below the diagonal (every column n < k) read
-        // the mirror S[n][k]: 16 lanes along k per column keep those loads
-        // coalesced along packed row n.
-        const bool mirror = (BK == BKind::SymmPacked) && (n0 + BN <= k0);
-        constexpr int kPer = (kBK * BN) / 128;  // elements per thread per stage
-        constexpr int kBatch = kPer < 16 ? kPer : 16;
-#pragma unroll 1
-        for (int b0 = 0; b0 < kPer; b0 += kBatch) {
-          float v[kBatch];
-#pragma unroll
-          for (int e = 0; e < kBatch; ++e) {
-            const int q = b0 + e;  // 0 .. kPer-1
-            int kr, n;
-            if (mirror) {
-              kr = lane & 15;
-              n = (q * 4 + tw) * 2 + (lane >> 4);
-            } else {
-              kr = tw + 4 * (q / (BN / 32));
-              n = (q % (BN / 32)) * 32 + lane;
-            }
-            v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
-          }
-#pragma unroll
-          for (int e = 0; e < kBatch; ++e) {
-            const int q = b0 + e;
-            int kr, n;
-            if (mirror) {
-              kr = lane & 15;
-              n = (q * 4 + tw) * 2 + (lane >> 4);
-            } else {
-              kr = tw + 4 * (q / (BN / 32));
-              n = (q % (BN / 32)) * 32 + lane;
-            }
-            const uint32_t off = b_tile_offset(kr, n);
-            const float hi = tf32_hi(v[e]);
-            *reinterpret_cast<float*>(bh + off) = hi;
-            if constexpr (SPLIT3) *reinterpret_cast<float*>(bl + off) = v[e] - hi;
-          }
+        // Warp-uniform outcome: tcgen05.ld/st are .sync.aligned.
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) {
+          ok = false;
+          break;
         }
-      } else if constexpr (SPLIT3) {
-        const float4* src = reinterpret_cast<const float4*>(b_hi(s));
-        float4* dst = reinterpret_cast<float4*>(b_lo(s));
+        const int k0 = (kb_begin + i) * kBK;
+        if constexpr (!kATma) {
+          a_store<AK, SPLIT3>(a_cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
 #pragma unroll
-        for (int j = t; j < kBTile / 16; j += 128) {
-          const float4 x = src[j];
-          dst[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+          for (int j = 0; j < 8; ++j) a_cur[j] = a_nxt[j];
         }
+        if constexpr (!kBTma) b_build<BK, BN, SPLIT3>(p, b_hi(s), b_lo(s), k0, n0, t);
+        fence_proxy_async_smem();
+        mbar_arrive(&ready[s]);
       }
-      if (tr && i == 0 && t == 0) {
-        for (int j = 0; j < 8; ++j) {
-          p.trace[kTrA + j] = reinterpret_cast<const uint32_t*>(a_hi(s))[j];
-          p.trace[kTrB + j] = reinterpret_cast<const uint32_t*>(b_hi(s))[j];
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&ready[s]);
+    }
+    if constexpr (SPLIT3) {
+      for (; ok && folded < nch - 1; ++folded)
+        if (!fold(folded)) ok = false;
     }
 
     // ------------------------------------------------------------ epilogue
-    const bool acc_ok = __all_sync(0xffffffffu, ok && mbar_wait(accum_full, 0, wepi) && !*abort_flag);
+    // Result = running sum (chunks [0, nch-1)) + the last chunk's accumulator.
+    bool last_ok = ok;
+    if constexpr (SPLIT3)
+      last_ok = last_ok && mbar_wait(acc_full, (nch - 1) & 1, wepi);
+    else
+      last_ok = last_ok && mbar_wait(accum_full, 0, wepi);
+    const bool acc_ok = __all_sync(0xffffffffu, last_ok && !*abort_flag);
     if (tr && t == 0) p.trace[kTrAccOk] = acc_ok ? 1u : 0u;
     if (acc_ok) {
       tc_fence_after_sync();
-      const int q = warp & 3;  // TMEM lanes 32q..32q+31 belong to this warp
       const int row = m0 + q * 32 + lane;
       const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
       float* crow = p.C + static_cast<long long>(row) * p.ldc;
-      const int nch = (num_kb + kChunk - 1) / kChunk;
-      const uint32_t lanes = static_cast<uint32_t>(q * 32) << 16;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = 0; c < kHalf; c += 16) {
         uint32_t r[16];
-        if constexpr (SPLIT3) {
-          // result = running sum (chunks [0, folded)) + the unfolded chunks
-          // (at most two, in distinct ping-pong buffers).
-          float acc[16];
+        tmem_ld_32x32b_x16(acc_col + c, r);
+        if (SPLIT3 && nch > 1) {
+          uint32_t s16[16];
+          tmem_ld_32x32b_x16(sum_col + c, s16);
+          tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
-          if (folded > 0) {
-            tmem_ld_32x32b_x16(tmem_base + lanes + 2 * BN + c, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(r[j]);
-          }
-#pragma unroll 1
-          for (int f = folded; f < nch; ++f) {
-            tmem_ld_32x32b_x16(tmem_base + lanes + static_cast<uint32_t>((f & 1) * BN) + c, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] += __uint_as_float(r[j]);
-          }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(acc[j]);
+          for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(s16[j]) + __uint_as_float(r[j]));
         } else {
-          tmem_ld_32x32b_x16(tmem_base + lanes + c, r);
           tmem_wait_ld();
         }
-        if (tr && q == 0 && lane == 0 && c == 0)
+        if (tr && q == 0 && lane == 0 && h == 0 && c == 0)
           for (int j = 0; j < 16; ++j) p.trace[kTrAcc + j] = r[j];
-        const int col = n0 + c;
+        const int col = n0 + h * kHalf + c;
         if (row < p.M) {
           if (vec && col + 16 <= p.N) {
             float4* dst = reinterpret_cast<float4*>(crow + col);
@@ -541,6 +545,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int v = 0; v < 16; ++v)
               if (col + v < p.N) crow[col + v] = __uint_as_float(r[v]);
+          }
+          if (p.C_lo != nullptr) {
+            float* lrow = p.C_lo + static_cast<long long>(row) * p.ldc;
+#pragma unroll
+            for (int v = 0; v < 16; ++v) {
+              const float x = __uint_as_float(r[v]);
+              if (col + v < p.N) lrow[col + v] = x - tf32_hi(x);
+            }
           }
         }
       }

@@ -1,0 +1,130 @@
+"""Row-slab partition of a structured product across the GPUs of one node.
+
+One process per GPU (torchrun), torch.distributed over NCCL for the
+plumbing.  For C = X B with X one of the library's left operands (dense A,
+packed U, Toeplitz generator, packed S):
+
+* every rank owns output rows [r0, r1) and computes them with the slab entry
+  point of libsmm (``smm_*_rows``; a row offset of A for the dense GEMM);
+* the right operand B is shared: rank 0 holds it and broadcasts it (one
+  NCCL broadcast per product); X itself is small (generator, packed
+  triangle) or row-sliced, so it is replicated or sliced locally;
+* for the triangular operand row i costs N - i, so slab boundaries are
+  equal-work: boundary g of G sits at N (1 - sqrt(1 - g/G)), rounded to the
+  128-row tile height;
+* the diagonal scale shards with no collective at all (rows independent).
+
+No kernel reads another GPU's memory; remote data reaches local HBM through
+NCCL before any kernel touches it.
+
+The collective steps take a ``compute`` callable so the host logic runs the
+same way under the gloo backend on CPU (tests) and NCCL on GPUs.
+"""
+from __future__ import annotations
+
+import math
+from typing import Callable, List, Optional, Sequence, Tuple
+
+TILE_ROWS = 128
+
+
+def _tile_work(n: int, triangular: bool, align: int) -> List[int]:
+    tiles = (n + align - 1) // align
+    if not triangular:
+        return [min(align, n - t * align) for t in range(tiles)]
+    # rows [a, b) of U cost sum (n - i)
+    return [sum_range_cost(n, t * align, min(n, (t + 1) * align)) for t in range(tiles)]
+
+
+def sum_range_cost(n: int, a: int, b: int) -> int:
+    return (b - a) * n - (b * (b - 1) - a * (a - 1)) // 2
+
+
+def row_slabs(n: int, world: int, triangular: bool = False, align: int = TILE_ROWS) -> List[int]:
+    """Slab boundaries b[0]=0 <= ... <= b[world]=n on tile (align-row)
+    granularity, minimising the largest slab's work: uniform rows for dense
+    operands, rows of cost (n - i) for the upper-triangular one (the
+    continuous optimum is N (1 - sqrt(1 - g/G)); the tile-granular optimum is
+    found by binary search on the largest slab).  Slabs may be empty when n
+    has fewer tiles than ranks."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    if n <= 0:
+        return [0] * (world + 1)
+    w = _tile_work(n, triangular, align)
+
+    def groups_needed(cap: int) -> int:
+        count, acc = 1, 0
+        for x in w:
+            if acc + x > cap:
+                count, acc = count + 1, x
+            else:
+                acc += x
+        return count
+
+    lo, hi = max(w), sum(w)
+    while lo < hi:
+        mid = (lo + hi) // 2
+        if groups_needed(mid) <= world:
+            hi = mid
+        else:
+            lo = mid + 1
+    cuts, acc = [0], 0
+    for t, x in enumerate(w):
+        if acc + x > lo:
+            cuts.append(t * align)
+            acc = x
+        else:
+            acc += x
+    cuts.append(n)
+    while len(cuts) < world + 1:  # fewer non-empty slabs than ranks
+        cuts.insert(len(cuts) - 1, n)
+    return cuts
+
+
+def slab_of(n: int, rank: int, world: int, triangular: bool = False) -> Tuple[int, int]:
+    b = row_slabs(n, world, triangular)
+    return b[rank], b[rank + 1]
+
+
+def slab_useful_flops(op: str, n: int, r0: int, r1: int, ncols: Optional[int] = None) -> int:
+    """Useful FLOPs of output rows [r0, r1) (structural zeros excluded)."""
+    ncols = n if ncols is None else ncols
+    rows = r1 - r0
+    if op in ("gemm", "toeplitz", "symm"):
+        return 2 * rows * n * ncols
+    if op == "upper":
+        # row i of U has n - i nonzeros: 2 * ncols * sum_{i=r0}^{r1-1} (n - i)
+        s = rows * n - (r1 * (r1 - 1) - r0 * (r0 - 1)) // 2
+        return 2 * ncols * s
+    raise ValueError(op)
+
+
+def distributed_product(compute: Callable[[int, int], object], B, rank: int, world: int, n: int,
+                        triangular: bool = False, broadcast: Callable = None, gather: Callable = None):
+    """Run one row-slab product on this rank.
+
+    compute(r0, r1) -> C slab (rows [r0, r1) of the product), called after B
+    holds rank 0's data.  ``broadcast(tensor, src)`` and ``gather(slab)``
+    default to torch.distributed; ``gather`` returning None skips assembly."""
+    import torch.distributed as dist
+    bcast = broadcast or (lambda t, src: dist.broadcast(t, src=src))
+    if world > 1:
+        bcast(B, 0)
+    r0, r1 = slab_of(n, rank, world, triangular)
+    C = compute(r0, r1)
+    if gather is not None:
+        return gather(C)
+    return C
+
+
+def gather_rows(slab, world: int, shapes: Sequence[int], ncols: int):
+    """all_gather of uneven row slabs (pads to the largest slab, then trims)."""
+    import torch
+    import torch.distributed as dist
+    rmax = max(shapes)
+    pad = torch.zeros((rmax, ncols), dtype=slab.dtype, device=slab.device)
+    pad[: slab.shape[0]] = slab
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad)
+    return torch.cat([p[:r] for p, r in zip(parts, shapes)], dim=0)

@@ -1,0 +1,90 @@
+"""Host logic of the multi-GPU row-slab partition, on CPU: slab boundaries,
+equal-work splits for the triangular operand, and the broadcast + slab
+compute + gather sequence run by two gloo ranks (the slab products computed
+by the oracle, since there is no GPU here)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from cpp1_b200 import multigpu as MG
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_slabs_cover_rows(world):
+    for n in (1, 100, 1024, 8192, 16384):
+        for tri in (False, True):
+            b = MG.row_slabs(n, world, tri)
+            assert b[0] == 0 and b[-1] == n and len(b) == world + 1
+            assert all(b[i] <= b[i + 1] for i in range(world))
+            assert all(x % 128 == 0 or x == n for x in b[1:-1])
+
+
+def test_triangular_slabs_balance_work():
+    n, world = 8192, 8
+    b = MG.row_slabs(n, world, triangular=True)
+    work = [MG.slab_useful_flops("upper", n, b[i], b[i + 1]) for i in range(world)]
+    total = MG.slab_useful_flops("upper", n, 0, n)
+    assert sum(work) == total == n * n * (n + 1)
+    # the slowest rank sets the time: within 10% of an equal share (the first
+    # 128-row tile alone is a quarter of a share, so tile granularity costs ~9%)
+    assert max(work) <= 1.10 * total / world
+    uniform = MG.row_slabs(n, world, triangular=False)
+    uw = [MG.slab_useful_flops("upper", n, uniform[i], uniform[i + 1]) for i in range(world)]
+    assert max(uw) > 1.7 * total / world  # uniform rows would be 1.9x slower
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, results):
+    import oracle as O
+    from cpp1_b200 import workloads as W
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = 384
+        w = W.make_upper(n, 96, seed=3)
+        U = w["U"]
+        # only rank 0 starts with B; the others hold garbage until the broadcast
+        B = torch.from_numpy(w["B"]) if rank == 0 else torch.full((n, 96), float("nan"))
+
+        def compute(r0, r1):
+            Bn = B.numpy()
+            full = O.upper_left_f32(U, Bn)  # stands in for the GPU slab kernel
+            return torch.from_numpy(np.ascontiguousarray(full[r0:r1]))
+
+        bounds = MG.row_slabs(n, world, triangular=True)
+        shapes = [bounds[i + 1] - bounds[i] for i in range(world)]
+        C = MG.distributed_product(compute, B, rank, world, n, triangular=True,
+                                   gather=lambda s: MG.gather_rows(s, world, shapes, 96))
+        if rank == 0:
+            results["ok"] = bool(np.array_equal(C.numpy(), O.upper_left_f32(U, w["B"])))
+            results["bounds"] = bounds
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_broadcast_slab_gather_gloo():
+    world = 2
+    port = _free_port()
+    with mp.Manager() as m:
+        results = m.dict()
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert results["ok"], results
