@@ -77,19 +77,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D fp32 tensor map over a row-major matrix (rows x cols, leading dimension
-// ld elements), box of box_cols x box_rows elements.
-int make_tmap(CUtensorMap* m, const float* base, int rows, int cols, int ld, int box_cols, int box_rows,
-              CUtensorMapSwizzle swz) {
+// 2-D tensor map over a row-major matrix (rows x cols, leading dimension ld
+// elements of fp32 or bf16), box of box_cols x box_rows elements.
+int make_tmap(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_cols, int box_rows,
+              CUtensorMapSwizzle swz, bool bf16 = false) {
   auto fn = encode_fn();
   if (!fn) return set_error(SMM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const size_t esz = bf16 ? 2 : 4;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * sizeof(float)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esz};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(SMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %d x %d (ld %d)", int(r), rows, cols, ld);
   return SMM_OK;
@@ -98,16 +99,17 @@ int make_tmap(CUtensorMap* m, const float* base, int rows, int cols, int ld, int
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 int round4(int x) { return (x + 3) & ~3; }
+int round8(int x) { return (x + 7) & ~7; }
 
 // ---------------------------------------------------------------- launches
 struct Maps {
   CUtensorMap a{}, b{}, al{}, bl{};
 };
 
-template <AKind AK, BKind BK, bool SPLIT3, int BN, int STAGES>
+template <AKind AK, BKind BK, Mode MD, int BN, int STAGES>
 int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
-  auto kern = umma_gemm_kernel<AK, BK, SPLIT3, BN, STAGES>;
-  constexpr int smem = umma_smem_bytes<BN, SPLIT3, STAGES>();
+  auto kern = umma_gemm_kernel<AK, BK, MD, BN, STAGES>;
+  constexpr int smem = umma_smem_bytes<BN, MD == Mode::TF32x3, STAGES>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
   static bool attr_set[64] = {};
   int dev = 0;
@@ -128,21 +130,21 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
 // Stage counts fill ~192 KiB of shared memory.
 // Stage counts fill ~192 KiB of shared memory.
 template <AKind AK, BKind BK, int BN>
-int launch_mode(bool split3, const Maps& m, const UmmaParams& p, cudaStream_t st) {
-  if (split3) {
+int launch_mode(int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+  if (mode == SMM_MODE_3XTF32) {
     constexpr int S = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-    return launch_umma<AK, BK, true, BN, S>(m, p, st);
+    return launch_umma<AK, BK, Mode::TF32x3, BN, S>(m, p, st);
   }
-  constexpr int S = 8;
-  return launch_umma<AK, BK, false, BN, S>(m, p, st);
+  if (mode == SMM_MODE_BF16) return launch_umma<AK, BK, Mode::BF16, BN, 8>(m, p, st);
+  return launch_umma<AK, BK, Mode::TF32, BN, 8>(m, p, st);
 }
 
 template <AKind AK, BKind BK>
-int launch_bn(int bn, bool split3, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+int launch_bn(int bn, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
   switch (bn) {
-    case 256: return launch_mode<AK, BK, 256>(split3, m, p, st);
-    case 128: return launch_mode<AK, BK, 128>(split3, m, p, st);
-    default: return launch_mode<AK, BK, 64>(split3, m, p, st);
+    case 256: return launch_mode<AK, BK, 256>(mode, m, p, st);
+    case 128: return launch_mode<AK, BK, 128>(mode, m, p, st);
+    default: return launch_mode<AK, BK, 64>(mode, m, p, st);
   }
 }
 
@@ -171,7 +173,8 @@ bool valid_mode(int mode) { return mode == SMM_MODE_3XTF32 || mode == SMM_MODE_T
 // ld) or a structured one (src, dim, row0).
 struct Operand {
   const float* ptr = nullptr;
-  const float* lo = nullptr;  // lo plane of ptr (3xTF32), same ld
+  const float* lo = nullptr;            // lo plane of ptr (3xTF32), same ld
+  const __nv_bfloat16* bf16 = nullptr;  // bf16 copy (bf16 mode), leading dimension ld
   int ld = 0;
   const float* src = nullptr;
   int dim = 0;
@@ -179,26 +182,30 @@ struct Operand {
 };
 
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
-                    int N, int K, cudaStream_t st, float* C_lo = nullptr) {
-  if (mode == SMM_MODE_BF16) return set_error(SMM_ERR_UNSUPPORTED, "bf16 mode not built for this operation");
+                    int N, int K, cudaStream_t st, float* C_lo = nullptr, __nv_bfloat16* C_bf16 = nullptr,
+                    int ldc_bf16 = 0) {
   const bool split3 = (mode == SMM_MODE_3XTF32);
+  const bool bf16 = (mode == SMM_MODE_BF16);
   const int bn = pick_bn(M, N);
   Maps m;
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);
+  // fp32: A boxes 16 x 128 (64-byte swizzle), B boxes 32 x 16 (128-byte
+  // swizzle, 32-byte atoms); bf16: A boxes 32 x 128, B boxes 64 x 32 (128-byte).
+  const int a_box = bf16 ? 32 : 16;
+  const int b_box_c = bf16 ? 64 : 32, b_box_r = bf16 ? 32 : 16;
+  const CUtensorMapSwizzle b_swz = bf16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   if (b_tma) {
-    if (int rc = make_tmap(&m.b, b.ptr, K, N, b.ld, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) return rc;
-    if (split3) {
-      if (!b.lo) return set_error(SMM_ERR_INVALID, "internal: missing lo plane of B");
-      if (int rc = make_tmap(&m.bl, b.lo, K, N, b.ld, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) return rc;
-    }
+    const void* bp = bf16 ? static_cast<const void*>(b.bf16) : static_cast<const void*>(b.ptr);
+    if (!bp) return set_error(SMM_ERR_INVALID, "internal: missing B operand plane");
+    if (int rc = make_tmap(&m.b, bp, K, N, b.ld, b_box_c, b_box_r, b_swz, bf16)) return rc;
+
   }
   if (a_tma) {
-    if (int rc = make_tmap(&m.a, a.ptr, M, K, a.ld, 16, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
-    if (split3) {
-      if (!a.lo) return set_error(SMM_ERR_INVALID, "internal: missing lo plane of A");
-      if (int rc = make_tmap(&m.al, a.lo, M, K, a.ld, 16, 128, CU_TENSOR_MAP_SWIZZLE_64B)) return rc;
-    }
+    const void* ap = bf16 ? static_cast<const void*>(a.bf16) : static_cast<const void*>(a.ptr);
+    if (!ap) return set_error(SMM_ERR_INVALID, "internal: missing A operand plane");
+    if (int rc = make_tmap(&m.a, ap, M, K, a.ld, a_box, 128, CU_TENSOR_MAP_SWIZZLE_64B, bf16)) return rc;
+
   }
   UmmaParams p{};
   p.M = M;
@@ -207,6 +214,8 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.C = C;
   p.ldc = ldc;
   p.C_lo = C_lo;
+  p.C_bf16 = C_bf16;
+  p.ldc_bf16 = ldc_bf16;
   p.a_src = a.src;
   p.a_dim = a.dim;
   p.a_row0 = a.row0;
@@ -222,27 +231,28 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   g_trace = nullptr;
   if (bk == BKind::Dense) {
     switch (ak) {
-      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, split3, m, p, st);
-      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, split3, m, p, st);
-      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, split3, m, p, st);
-      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, split3, m, p, st);
-      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, split3, m, p, st);
+      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, mode, m, p, st);
+      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, mode, m, p, st);
+      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, mode, m, p, st);
+      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, mode, m, p, st);
+      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, mode, m, p, st);
     }
   }
   if (ak == AKind::Dense && bk == BKind::UpperPacked)
-    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, split3, m, p, st);
+    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, mode, m, p, st);
   if (ak == AKind::Dense && bk == BKind::SymmPacked)
-    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, split3, m, p, st);
+    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, mode, m, p, st);
   if (ak == AKind::SymmPacked && bk == BKind::SymmPacked)
-    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, split3, m, p, st);
+    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, mode, m, p, st);
   return set_error(SMM_ERR_INVALID, "unsupported operand kinds");
 }
 
-Operand dense_op(const float* ptr, const float* lo, int ld) {
+Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf = nullptr) {
   Operand o;
   o.ptr = ptr;
   o.lo = lo;
   o.ld = ld;
+  o.bf16 = bf;
   return o;
 }
 Operand structured_op(const float* src, int dim, int row0 = 0) {
@@ -278,26 +288,56 @@ __global__ void lo_plane_vec4_kernel(const float4* __restrict__ src, float4* __r
   }
 }
 
+// bf16 copy of an fp32 matrix (round to nearest even), rows padded with zeros
+// to ld_dst elements (a 16-byte multiple).
+__global__ void to_bf16_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
+                               __nv_bfloat16* __restrict__ dst, int ld_dst) {
+  const long long total = static_cast<long long>(rows) * ld_dst;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / ld_dst;
+    const int c = static_cast<int>(i - r * ld_dst);
+    dst[i] = __float2bfloat16_rn(c < cols ? src[r * ld_src + c] : 0.0f);
+  }
+}
+
 // A TMA-fed operand (rows x cols row-major): the caller's array or a padded
-// copy, plus its lo plane in 3xTF32 mode, both in the workspace.
+// copy, plus its lo plane in 3xTF32 mode, or its bf16 copy in bf16 mode, all
+// in the workspace.
 struct Staged {
   const float* ptr;
   const float* lo;
   int ld;
+  const __nv_bfloat16* bf16 = nullptr;
 };
 
 bool needs_pad(const float* p, int cols) { return (cols % 4 != 0) || !aligned16(p); }
 size_t plane_bytes(int rows, int cols) { return round256(static_cast<size_t>(rows) * round4(cols) * sizeof(float)); }
-size_t staged_bytes(const float* p, int rows, int cols, bool split3) {
-  return (needs_pad(p, cols) ? plane_bytes(rows, cols) : 0) + (split3 ? plane_bytes(rows, cols) : 0);
+size_t bf16_plane_bytes(int rows, int cols) { return round256(static_cast<size_t>(rows) * round8(cols) * 2); }
+size_t staged_bytes(const float* p, int rows, int cols, int mode) {
+  if (mode == SMM_MODE_BF16) return bf16_plane_bytes(rows, cols);
+  return needs_pad(p, cols) ? plane_bytes(rows, cols) : 0;
 }
 // Workspace bound when the pointer is not known yet (assumes a padded copy).
-size_t staged_bytes_bound(int rows, int cols, bool split3) {
-  return (split3 ? 2 : 1) * plane_bytes(rows, cols);
+size_t staged_bytes_bound(int rows, int cols, int mode) {
+  if (mode == SMM_MODE_BF16) return bf16_plane_bytes(rows, cols);
+  return plane_bytes(rows, cols);
 }
 
-int stage_operand(const float* src, int rows, int cols, bool split3, uint8_t*& ws_cur, Staged* out,
-                  cudaStream_t st) {
+int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st) {
+  if (mode == SMM_MODE_BF16) {
+    const int ld = round8(cols);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
+    ws_cur += bf16_plane_bytes(rows, cols);
+    const long long total = static_cast<long long>(rows) * ld;
+    const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+    to_bf16_kernel<<<std::max(grid, 1), 256, 0, st>>>(src, rows, cols, cols, dst, ld);
+    count_launch();
+    SMM_CUDA_TRY(cudaGetLastError(), "bf16 staging launch");
+    *out = {nullptr, nullptr, ld, dst};
+    return SMM_OK;
+  }
+  const bool split3 = false;  // lo tiles are derived on chip
   const bool pad = needs_pad(src, cols);
   if (!pad && !split3) {
     *out = {src, nullptr, cols};
@@ -370,7 +410,7 @@ extern "C" int smm_device_status(void* stream) {
 extern "C" size_t smm_gemm_workspace_size(int M, int N, int K, int mode) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  return staged_bytes_bound(M, K, s3) + staged_bytes_bound(K, N, s3);
+  return staged_bytes_bound(M, K, mode) + staged_bytes_bound(K, N, mode);
 }
 
 extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* ws,
@@ -382,21 +422,21 @@ extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, 
   cudaStream_t st = as_stream(stream);
   if (K == 0) return zero_output(C, M, N, st);
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  const size_t need = staged_bytes(A, M, K, s3) + staged_bytes(B, K, N, s3);
+  const size_t need = staged_bytes(A, M, K, mode) + staged_bytes(B, K, N, mode);
   if (int rc = check_ws("smm_gemm", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged a, b;
-  if (int rc = stage_operand(A, M, K, s3, cur, &a, st)) return rc;
-  if (int rc = stage_operand(B, K, N, s3, cur, &b, st)) return rc;
-  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld), dense_op(b.ptr, b.lo, b.ld),
+  if (int rc = stage_operand(A, M, K, mode, cur, &a, st)) return rc;
+  if (int rc = stage_operand(B, K, N, mode, cur, &b, st)) return rc;
+  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16), dense_op(b.ptr, b.lo, b.ld, b.bf16),
                          C, N, M, N, K, st);
 }
 
 extern "C" size_t smm_upper_left_workspace_size(int N, int ncols, int u_fmt, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  size_t b = staged_bytes_bound(N, ncols, s3);
-  if (u_fmt == SMM_FMT_DENSE) b += staged_bytes_bound(N, N, s3);
+  size_t b = staged_bytes_bound(N, ncols, mode);
+  if (u_fmt == SMM_FMT_DENSE) b += staged_bytes_bound(N, N, mode);
   return b;
 }
 
@@ -418,23 +458,24 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
   if (!U || !B || !C) return set_error(SMM_ERR_INVALID, "smm_upper_left: null pointer");
   cudaStream_t st = as_stream(stream);
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  size_t need = staged_bytes(B, N, ncols, s3);
-  if (u_fmt == SMM_FMT_DENSE) need += staged_bytes(U, N, N, s3);
+  size_t need = staged_bytes(B, N, ncols, mode);
+  if (u_fmt == SMM_FMT_DENSE) need += staged_bytes(U, N, N, mode);
   if (int rc = check_ws("smm_upper_left", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
-  if (int rc = stage_operand(B, N, ncols, s3, cur, &b, st)) return rc;
+  if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
   if (u_fmt == SMM_FMT_DENSE) {
     Staged u;
-    if (int rc = stage_operand(U, N, N, s3, cur, &u, st)) return rc;
+    if (int rc = stage_operand(U, N, N, mode, cur, &u, st)) return rc;
     const size_t off = static_cast<size_t>(row0) * u.ld;
-    Operand ua = dense_op(u.ptr + off, u.lo ? u.lo + off : nullptr, u.ld);
+    Operand ua = dense_op(u.ptr ? u.ptr + off : nullptr, u.lo ? u.lo + off : nullptr, u.ld,
+                          u.bf16 ? u.bf16 + off : nullptr);
     ua.dim = N;
     ua.row0 = row0;
-    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.lo, b.ld), C, ncols, nrows,
+    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, nrows,
                            ncols, N, st);
   }
-  return run_contraction(AKind::UpperPacked, BKind::Dense, mode, structured_op(U, N, row0), dense_op(b.ptr, b.lo, b.ld),
+  return run_contraction(AKind::UpperPacked, BKind::Dense, mode, structured_op(U, N, row0), dense_op(b.ptr, b.lo, b.ld, b.bf16),
                          C, ncols, nrows, ncols, N, st);
 }
 
@@ -445,7 +486,7 @@ extern "C" int smm_upper_left(const float* U, int u_fmt, const float* B, float* 
 
 extern "C" size_t smm_toeplitz_left_workspace_size(int N, int ncols, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
-  return staged_bytes_bound(N, ncols, mode == SMM_MODE_3XTF32);
+  return staged_bytes_bound(N, ncols, mode);
 }
 
 extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, int N, int ncols, int row0,
@@ -456,11 +497,11 @@ extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, 
   if (!g || !B || !C) return set_error(SMM_ERR_INVALID, "smm_toeplitz_left: null pointer");
   cudaStream_t st = as_stream(stream);
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  if (int rc = check_ws("smm_toeplitz_left", ws, ws_bytes, staged_bytes(B, N, ncols, s3))) return rc;
+  if (int rc = check_ws("smm_toeplitz_left", ws, ws_bytes, staged_bytes(B, N, ncols, mode))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
-  if (int rc = stage_operand(B, N, ncols, s3, cur, &b, st)) return rc;
-  return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), dense_op(b.ptr, b.lo, b.ld), C,
+  if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
+  return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), dense_op(b.ptr, b.lo, b.ld, b.bf16), C,
                          ncols, nrows, ncols, N, st);
 }
 
@@ -481,11 +522,11 @@ extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int 
   if (!S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_left: null pointer");
   cudaStream_t st = as_stream(stream);
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, staged_bytes(B, N, ncols, s3))) return rc;
+  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, staged_bytes(B, N, ncols, mode))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
-  if (int rc = stage_operand(B, N, ncols, s3, cur, &b, st)) return rc;
-  return run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N, row0), dense_op(b.ptr, b.lo, b.ld),
+  if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
+  return run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N, row0), dense_op(b.ptr, b.lo, b.ld, b.bf16),
                          C, ncols, nrows, ncols, N, st);
 }
 
@@ -496,16 +537,20 @@ extern "C" int smm_symm_left(const float* S, const float* B, float* C, int N, in
 
 namespace {
 // Workspace of the sandwich: X = S B (16-byte row stride) and, in 3xTF32, its
-// lo plane (written by the first product's epilogue), then the staged A and B.
-size_t sandwich_need(const float* A, const float* B, int N, bool s3) {
-  return (s3 ? 2 : 1) * plane_bytes(N, N) + staged_bytes(A, N, N, s3) + staged_bytes(B, N, N, s3);
+// lo plane, or in bf16 mode its bf16 copy (both written by the first
+// product's epilogue), then the staged A and B.
+size_t sandwich_x_bytes(int N, int mode) {
+  if (mode == SMM_MODE_BF16) return plane_bytes(N, N) + bf16_plane_bytes(N, N);
+  return plane_bytes(N, N);
+}
+size_t sandwich_need(const float* A, const float* B, int N, int mode) {
+  return sandwich_x_bytes(N, mode) + staged_bytes(A, N, N, mode) + staged_bytes(B, N, N, mode);
 }
 }  // namespace
 
 extern "C" size_t smm_symm_sandwich_workspace_size(int N, int mode) {
   if (N <= 0) return 0;
-  const bool s3 = (mode == SMM_MODE_3XTF32);
-  return (s3 ? 2 : 1) * plane_bytes(N, N) + 2 * staged_bytes_bound(N, N, s3);
+  return sandwich_x_bytes(N, mode) + 2 * staged_bytes_bound(N, N, mode);
 }
 
 extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B, float* C, int N, int mode,
@@ -516,32 +561,38 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   if (!A || !S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich: null pointer");
   cudaStream_t st = as_stream(stream);
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  if (int rc = check_ws("smm_symm_sandwich", ws, ws_bytes, sandwich_need(A, B, N, s3))) return rc;
+  const bool bf = (mode == SMM_MODE_BF16);
+  if (int rc = check_ws("smm_symm_sandwich", ws, ws_bytes, sandwich_need(A, B, N, mode))) return rc;
   const int ldx = round4(N);
+  const int ldx_bf = round8(N);
   uint8_t* cur = static_cast<uint8_t*>(ws);
   float* X = reinterpret_cast<float*>(cur);
   cur += plane_bytes(N, N);
   float* X_lo = nullptr;
-  if (s3) {
-    X_lo = reinterpret_cast<float*>(cur);
-    cur += plane_bytes(N, N);
+  __nv_bfloat16* X_bf = nullptr;
+  (void)s3;
+  if (bf) {
+    X_bf = reinterpret_cast<__nv_bfloat16*>(cur);
+    cur += bf16_plane_bytes(N, N);
+    // the bf16 row padding must read as zeros (never multiplied, but keep it defined)
+    if (ldx_bf != N) SMM_CUDA_TRY(cudaMemsetAsync(X_bf, 0, bf16_plane_bytes(N, N), st), "zero bf16 intermediate");
   }
   Staged a, b;
-  if (int rc = stage_operand(A, N, N, s3, cur, &a, st)) return rc;
-  if (int rc = stage_operand(B, N, N, s3, cur, &b, st)) return rc;
+  if (int rc = stage_operand(A, N, N, mode, cur, &a, st)) return rc;
+  if (int rc = stage_operand(B, N, N, mode, cur, &b, st)) return rc;
   // X = S B (S packed, mirrored on chip; the epilogue also writes X's lo
-  // plane), then C = A X.
-  if (int rc = run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N), dense_op(b.ptr, b.lo, b.ld),
-                               X, ldx, N, N, N, st, X_lo))
+  // plane or bf16 copy), then C = A X.
+  if (int rc = run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N),
+                               dense_op(b.ptr, b.lo, b.ld, b.bf16), X, ldx, N, N, N, st, X_lo, X_bf, ldx_bf))
     return rc;
-  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld), dense_op(X, X_lo, ldx), C, N,
-                         N, N, N, st);
+  return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16),
+                         dense_op(X, X_lo, bf ? ldx_bf : ldx, X_bf), C, N, N, N, N, st);
 }
 
 // ---------------------------------------------------------------- structured right operand
 extern "C" size_t smm_gen_x_struct_workspace_size(int M, int N, int mode) {
   if (M <= 0 || N <= 0) return 0;
-  return staged_bytes_bound(M, N, mode == SMM_MODE_3XTF32);
+  return staged_bytes_bound(M, N, mode);
 }
 
 namespace {
@@ -552,11 +603,11 @@ int gen_x_struct(const char* who, BKind bk, const float* A, const float* X, floa
   if (M == 0 || N == 0) return SMM_OK;
   if (!A || !X || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
   const bool s3 = (mode == SMM_MODE_3XTF32);
-  if (int rc = check_ws(who, ws, ws_bytes, staged_bytes(A, M, N, s3))) return rc;
+  if (int rc = check_ws(who, ws, ws_bytes, staged_bytes(A, M, N, mode))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged a;
-  if (int rc = stage_operand(A, M, N, s3, cur, &a, st)) return rc;
-  return run_contraction(AKind::Dense, bk, mode, dense_op(a.ptr, a.lo, a.ld), structured_op(X, N), C, N, M, N, N, st);
+  if (int rc = stage_operand(A, M, N, mode, cur, &a, st)) return rc;
+  return run_contraction(AKind::Dense, bk, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16), structured_op(X, N), C, N, M, N, N, st);
 }
 }  // namespace
 
@@ -621,10 +672,10 @@ extern "C" int smm_debug_trace_next(unsigned* trace) {
 }
 
 // ---------------------------------------------------------------- allocation-free sandwich
-// Scratch of smm_symm_sandwich_noalloc: the S*B intermediate, its lo plane and
-// those of A and B (3xTF32), plus padded copies of A and B when their rows
-// are not 16-byte multiples.  A fixed 16 MiB that every GPU which loads this
-// library holds until process exit.
+// Scratch of smm_symm_sandwich_noalloc: the S*B intermediate, plus padded
+// copies of A and B when their rows are not 16-byte multiples, or the bf16
+// copies in bf16 mode.  A fixed 16 MiB that every GPU which loads this library
+// holds until process exit.
 // Host code must not use this name as an address (it is a host-side stand-in
 // for the symbol); the device address comes from cudaGetSymbolAddress.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[size_t(16) << 20];
@@ -659,11 +710,11 @@ extern "C" int smm_symm_sandwich_noalloc(const float* A, const float* S, const f
   if (N == 0) return SMM_OK;
   if (!A || !S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: null pointer");
   // Same scratch layout smm_symm_sandwich uses.
-  const size_t need = sandwich_need(A, B, N, mode == SMM_MODE_3XTF32);
+  const size_t need = sandwich_need(A, B, N, mode);
   if (need > kNoallocScratchBytes)
     return set_error(SMM_ERR_WORKSPACE,
                      "smm_symm_sandwich_noalloc: N = %d needs %zu bytes of scratch but the static scratch holds %zu "
-                     "(3xTF32: N <= 1024, TF32: N <= 2048, with N %% 4 == 0 and 16-byte-aligned A, B)",
+                     "(fp32 modes: N <= 2048 with N %% 4 == 0 and 16-byte-aligned A, B; bf16: N <= 1290)",
                      N, need, kNoallocScratchBytes);
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;

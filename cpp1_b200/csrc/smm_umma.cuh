@@ -6,10 +6,11 @@
 // (64 bytes) per pipeline stage, STAGES stages in shared memory.
 //
 // Operand staging per stage (hi = the fp32 value; kind::tf32 reads its upper
-// 19 bits, i.e. truncates; lo = x - tf32(x), exact in fp32):
+// 19 bits, i.e. truncates; lo = x - tf32(x), exact in fp32, computed in shared
+// memory by the transform warps from the TMA-loaded tile, so only the raw
+// operands cross L2):
 //   A (K-major, 128 rows x 64 B, 64-byte swizzle):
-//     AKind::Dense / UpperDense   TMA tile loads of a row-major A (and, in
-//                                 3xTF32, of its precomputed lo plane)
+//     AKind::Dense / UpperDense   TMA tile loads of a row-major A
 //     AKind::UpperPacked          built on chip from packed-upper storage;
 //                                 k-blocks left of the row tile's diagonal are
 //                                 never visited
@@ -20,7 +21,7 @@
 //   B (MN-major, BN columns x 16 k-rows, 32-column boxes, 128-byte swizzle
 //     with 32-byte atoms — the only swizzle kind::tf32 accepts for an MN-major
 //     operand; with the plain 128-byte swizzle the MMA produces nothing):
-//     BKind::Dense                TMA tile loads of a row-major B (+ lo plane)
+//     BKind::Dense                TMA tile loads of a row-major B
 //     BKind::UpperPacked/SymmPacked  built on chip (the DSL's Gen@Upper,
 //                                 Gen@Symm, Symm@Symm)
 //
@@ -36,7 +37,7 @@
 // Warp roles (320 threads):
 //   warp 0      TMA producer (one lane)
 //   warp 1      TMEM allocator + MMA issuer (one lane)
-//   warps 2-9   transform (structured operand tiles), chunk folds, epilogue
+//   warps 2-9   transform (lo tiles, structured operand tiles), chunk folds, epilogue
 //               (TMEM -> registers -> global C); warp w owns TMEM lanes
 //               32*(w%4).. and column half (w-2)/4 of the tile
 //
@@ -44,6 +45,8 @@
 // gave up in the status word, the other roles stop waiting, in-flight
 // copies/MMAs are drained (bounded), TMEM is freed and the CTA exits.
 #pragma once
+#include <cuda_bf16.h>
+
 #include "smm_device.cuh"
 
 namespace smm {
@@ -53,12 +56,38 @@ enum class AKind : int { Dense = 0, UpperPacked = 1, Toeplitz = 2, SymmPacked = 
 // upper-triangular / symmetric matrix built on chip by the transform warps.
 enum class BKind : int { Dense = 0, UpperPacked = 1, SymmPacked = 2 };
 
+// Arithmetic of the contraction (values match smm_mode).
+enum class Mode : int { TF32x3 = 0, TF32 = 1, BF16 = 2 };
+
+// Per-mode geometry.  A stage holds 64 bytes of K per A row in every mode
+// (16 fp32 or 32 bf16) and a BN x 64-byte B tile:
+//   fp32: B boxes of 32 columns x 16 k-rows (2 KiB), 128-byte swizzle with
+//         32-byte atoms (descriptor layout 1), a k-step of 8 rows = 1 KiB;
+//   bf16: B boxes of 64 columns x 32 k-rows (4 KiB), plain 128-byte swizzle
+//         (layout 2), a k-step of 16 rows = 2 KiB.
+template <Mode MD>
+struct ModeTraits {
+  static constexpr bool kSplit3 = (MD == Mode::TF32x3);
+  static constexpr bool kBf16 = (MD == Mode::BF16);
+  static constexpr int kElem = kBf16 ? 2 : 4;
+  static constexpr int kStageK = 64 / kElem;        // K elements per stage
+  static constexpr int kBoxCols = 128 / kElem;      // B box width (elements)
+  static constexpr int kBoxRows = kStageK;          // B box height (k-rows)
+  static constexpr int kBoxBytes = kBoxRows * 128;  // 2 or 4 KiB
+  static constexpr uint32_t kBLayout = kBf16 ? kLayoutSw128 : kLayoutSw128Base32;
+  static constexpr uint32_t kBSbo = kBf16 ? 1024 : 512;     // swizzle-atom row-group stride
+  static constexpr uint32_t kBStepBytes = kBf16 ? 2048 : 1024;  // B bytes per MMA k-step
+  static constexpr uint32_t kFmt = kBf16 ? kFmtBF16 : kFmtTF32;
+};
+
 struct UmmaParams {
   int M, N, K;             // C is M x N; reduction length K
   float* C;                // row-major, leading dimension ldc
   int ldc;
   float* C_lo;             // optional: also store lo(C) = C - tf32(C) here (same ldc), so
                            // a following 3xTF32 product can read C as a split operand
+  __nv_bfloat16* C_bf16;   // optional: also store bf16(C) here (leading dimension ldc_bf16),
+  int ldc_bf16;            // so a following bf16 product can read C as an operand
   const float* a_src;      // packed U / generator / packed S (structured A kinds)
   int a_dim;               // order of the structured matrix
   int a_row0;              // row of the structured matrix that output row 0 maps to
@@ -153,44 +182,58 @@ __device__ __forceinline__ uint32_t b_tile_offset(uint32_t kr, uint32_t n) {
 //   lanes along rows (symmetric tiles wholly below the diagonal, whose
 //     elements are the mirror S[k][row]): row (xw%4)*32 + lane, column
 //     (xw/4)*8 + it — coalesced along packed row k.
-template <AKind AK>
+template <AKind AK, int KS>
 __device__ __forceinline__ bool a_rows_mapping(int g_first, int k0) {
-  return AK == AKind::SymmPacked && k0 + kBK <= g_first;
+  return AK == AKind::SymmPacked && k0 + KS <= g_first;
 }
 
+// KS = K elements per stage (16 fp32 or 32 bf16): 128*KS/256 = KS/2
+// elements per thread; KS/16 k-columns per lane group in the k mapping.
+template <int KS>
 __device__ __forceinline__ void a_coord(bool rows, int xw, int lane, int it, int& r, int& kl) {
   if (rows) {
     r = (xw & 3) * 32 + lane;
-    kl = (xw >> 2) * 8 + it;
-  } else {
+    kl = (xw >> 2) * (KS / 2) + it;
+  } else if (KS == 16) {
     r = xw * 16 + it * 2 + (lane >> 4);
     kl = lane & 15;
+  } else {  // 32: one row per warp instruction
+    r = xw * 16 + it;
+    kl = lane;
   }
 }
 
-template <AKind AK>
-__device__ __forceinline__ void a_gather(float (&v)[8], const UmmaParams& p, int g_first, int k0, int xw, int lane) {
-  const bool rows = a_rows_mapping<AK>(g_first, k0);
+template <AKind AK, int KS>
+__device__ __forceinline__ void a_gather(float (&v)[KS / 2], const UmmaParams& p, int g_first, int k0, int xw,
+                                         int lane) {
+  const bool rows = a_rows_mapping<AK, KS>(g_first, k0);
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
+  for (int it = 0; it < KS / 2; ++it) {
     int r, kl;
-    a_coord(rows, xw, lane, it, r, kl);
+    a_coord<KS>(rows, xw, lane, it, r, kl);
     v[it] = a_value<AK>(p.a_src, p.a_dim, g_first + r, k0 + kl);
   }
 }
 
-template <AKind AK, bool SPLIT3>
-__device__ __forceinline__ void a_store(const float (&v)[8], uint8_t* ah, uint8_t* al, int g_first, int k0, int xw,
-                                        int lane) {
-  const bool rows = a_rows_mapping<AK>(g_first, k0);
+template <AKind AK, Mode MD>
+__device__ __forceinline__ void a_store(const float (&v)[ModeTraits<MD>::kStageK / 2], uint8_t* ah, uint8_t* al,
+                                        int g_first, int k0, int xw, int lane) {
+  using T = ModeTraits<MD>;
+  constexpr int KS = T::kStageK;
+  const bool rows = a_rows_mapping<AK, KS>(g_first, k0);
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
+  for (int it = 0; it < KS / 2; ++it) {
     int r, kl;
-    a_coord(rows, xw, lane, it, r, kl);
-    const uint32_t off = swz_offset(r, kl >> 2, 64) + (kl & 3) * 4;
-    const float hi = tf32_hi(v[it]);
-    *reinterpret_cast<float*>(ah + off) = hi;
-    if constexpr (SPLIT3) *reinterpret_cast<float*>(al + off) = v[it] - hi;
+    a_coord<KS>(rows, xw, lane, it, r, kl);
+    if constexpr (T::kBf16) {
+      const uint32_t off = swz_offset(r, kl >> 3, 64) + (kl & 7) * 2;
+      *reinterpret_cast<__nv_bfloat16*>(ah + off) = __float2bfloat16_rn(v[it]);
+    } else {
+      const uint32_t off = swz_offset(r, kl >> 2, 64) + (kl & 3) * 4;
+      const float hi = tf32_hi(v[it]);
+      *reinterpret_cast<float*>(ah + off) = hi;
+      if constexpr (T::kSplit3) *reinterpret_cast<float*>(al + off) = v[it] - hi;
+    }
   }
 }
 
@@ -199,12 +242,18 @@ __device__ __forceinline__ void a_store(const float (&v)[8], uint8_t* ah, uint8_
 // run along n (coalesced along packed row k); for symmetric tiles wholly
 // below the diagonal (every n < k, elements are the mirror S[n][k]) 16 lanes
 // run along k instead (coalesced along packed row n).
-template <int BN>
+// KS = k-rows per stage (16 fp32, 32 bf16).
+template <int BN, int KS>
 __device__ __forceinline__ void b_coord(bool mirror, int t, int e, int& kr, int& n) {
+  const int xw = t >> 5, lane = t & 31;
   if (mirror) {
-    const int xw = t >> 5, lane = t & 31;
-    kr = lane & 15;
-    n = (e * 8 + xw) * 2 + (lane >> 4);
+    if (KS == 16) {
+      kr = lane & 15;
+      n = (e * 8 + xw) * 2 + (lane >> 4);
+    } else {
+      kr = lane;
+      n = e * 8 + xw;
+    }
   } else {
     const int lin = e * kXformThreads + t;
     kr = lin / BN;
@@ -212,44 +261,66 @@ __device__ __forceinline__ void b_coord(bool mirror, int t, int e, int& kr, int&
   }
 }
 
-template <BKind BK, int BN, bool SPLIT3>
+// Byte offset of (k-row kr, column n) in a bf16 B stage tile: 64-column boxes
+// of 32 rows x 128 B, plain 128-byte swizzle (16-byte chunk index ^= row & 7).
+__device__ __forceinline__ uint32_t b_tile_offset_bf16(uint32_t kr, uint32_t n) {
+  const uint32_t j = n & 63u;
+  return (n >> 6) * 4096u + kr * 128u + (((j >> 3) ^ (kr & 7u)) << 4) + (j & 7u) * 2u;
+}
+
+template <BKind BK, int BN, Mode MD>
 __device__ __forceinline__ void b_build(const UmmaParams& p, uint8_t* bh, uint8_t* bl, int k0, int n0, int t) {
+  using T = ModeTraits<MD>;
+  constexpr int KS = T::kStageK;
   const bool mirror = (BK == BKind::SymmPacked) && (n0 + BN <= k0);
-  constexpr int kPer = (kBK * BN) / kXformThreads;  // 4, 8 or 16
-  float v[kPer];
+  constexpr int kPer = (KS * BN) / kXformThreads;
+  constexpr int kBatch = kPer < 16 ? kPer : 16;
+#pragma unroll 1
+  for (int b0 = 0; b0 < kPer; b0 += kBatch) {
+    float v[kBatch];
 #pragma unroll
-  for (int e = 0; e < kPer; ++e) {
-    int kr, n;
-    b_coord<BN>(mirror, t, e, kr, n);
-    v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
-  }
+    for (int e = 0; e < kBatch; ++e) {
+      int kr, n;
+      b_coord<BN, KS>(mirror, t, b0 + e, kr, n);
+      v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
+    }
 #pragma unroll
-  for (int e = 0; e < kPer; ++e) {
-    int kr, n;
-    b_coord<BN>(mirror, t, e, kr, n);
-    const uint32_t off = b_tile_offset(kr, n);
-    const float hi = tf32_hi(v[e]);
-    *reinterpret_cast<float*>(bh + off) = hi;
-    if constexpr (SPLIT3) *reinterpret_cast<float*>(bl + off) = v[e] - hi;
+    for (int e = 0; e < kBatch; ++e) {
+      int kr, n;
+      b_coord<BN, KS>(mirror, t, b0 + e, kr, n);
+      if constexpr (T::kBf16) {
+        *reinterpret_cast<__nv_bfloat16*>(bh + b_tile_offset_bf16(kr, n)) = __float2bfloat16_rn(v[e]);
+      } else {
+        const uint32_t off = b_tile_offset(kr, n);
+        const float hi = tf32_hi(v[e]);
+        *reinterpret_cast<float*>(bh + off) = hi;
+        if constexpr (T::kSplit3) *reinterpret_cast<float*>(bl + off) = v[e] - hi;
+      }
+    }
   }
 }
 
 // ---------------------------------------------------------------- kernel
-// tmA/tmB map the operands (hi), tmAl/tmBl their lo planes (3xTF32 only).
-template <AKind AK, BKind BK, bool SPLIT3, int BN, int STAGES>
+// tmA/tmB map the operands (hi, or bf16 copies), tmAl/tmBl their lo planes
+// (3xTF32 only).
+template <AKind AK, BKind BK, Mode MD, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
                      const UmmaParams p) {
+  using MT = ModeTraits<MD>;
+  constexpr bool SPLIT3 = MT::kSplit3;
+  constexpr int KS = MT::kStageK;
   constexpr int kBTile = TileGeom<BN>::kBTileBytes;
   constexpr int kStage = stage_bytes<BN, SPLIT3>();
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
   constexpr bool kBTma = (BK == BKind::Dense);
-  constexpr bool kXform = !kATma || !kBTma;  // a tile is built on chip every stage
-  constexpr int kPlanes = SPLIT3 ? 2 : 1;
-  constexpr uint32_t kTxBytes = (kATma ? kPlanes * kATileBytes : 0) + (kBTma ? kPlanes * kBTile : 0);
+  // The transform warps touch every stage when a tile is built on chip or
+  // when lo tiles are derived from the TMA-loaded ones (3xTF32).
+  constexpr bool kXform = !kATma || !kBTma || SPLIT3;
+  constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0);
   constexpr uint32_t kTmemCols = tmem_cols<BN, SPLIT3>();
-  constexpr uint32_t kIdesc = make_idesc(kFmtTF32, kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
+  constexpr uint32_t kIdesc = make_idesc(MT::kFmt, kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
   constexpr int kHalf = BN / 2;  // columns per epilogue warp
 
   extern __shared__ uint8_t smem_raw[];
@@ -291,35 +362,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Rows of a triangular left operand are zero left of the diagonal: row
   // tile [g0, g0+128) of U needs k >= g0 only.
   int kb_begin = 0;
-  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + m0) / kBK;
-  int kb_end = (p.K + kBK - 1) / kBK;
+  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + m0) / KS;
+  int kb_end = (p.K + KS - 1) / KS;
   // An upper-triangular right operand is zero below its diagonal: column
   // tile [n0, n0+BN) needs k < n0 + BN only.
-  if constexpr (BK == BKind::UpperPacked) kb_end = min(kb_end, (n0 + BN - 1) / kBK + 1);
+  if constexpr (BK == BKind::UpperPacked) kb_end = min(kb_end, (n0 + BN - 1) / KS + 1);
   const int num_kb = kb_end - kb_begin;
   const int nch = SPLIT3 ? (num_kb + kChunk - 1) / kChunk : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], kXformThreads);
+      mbar_init(&ready[s], kXformThreads / 32);  // one arrival per transform warp
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum_full, 1);
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kXformThreads);
+    mbar_init(acc_empty, kXformThreads / 32);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    if constexpr (kATma) {
-      tma_prefetch_desc(&tmA);
-      if constexpr (SPLIT3) tma_prefetch_desc(&tmAl);
-    }
-    if constexpr (kBTma) {
-      tma_prefetch_desc(&tmB);
-      if constexpr (SPLIT3) tma_prefetch_desc(&tmBl);
-    }
+    if constexpr (kATma) tma_prefetch_desc(&tmA);
+    if constexpr (kBTma) tma_prefetch_desc(&tmB);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before_sync();
@@ -346,18 +411,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
         mbar_arrive_expect_tx(&full[s], kTxBytes);
-        const int k0 = (kb_begin + i) * kBK;
-        if constexpr (kATma) {
-          tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
-          if constexpr (SPLIT3) tma_load_2d(a_lo(s), &tmAl, &full[s], k0, m0);
-        }
+        const int k0 = (kb_begin + i) * KS;
+        if constexpr (kATma) tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
         if constexpr (kBTma) {
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-            tma_load_2d(b_hi(s) + c * TileGeom<BN>::kBChunkBytes, &tmB, &full[s], n0 + 32 * c, k0);
-            if constexpr (SPLIT3)
-              tma_load_2d(b_lo(s) + c * TileGeom<BN>::kBChunkBytes, &tmBl, &full[s], n0 + 32 * c, k0);
-          }
+          for (int c = 0; c < BN / MT::kBoxCols; ++c)
+            tma_load_2d(b_hi(s) + c * MT::kBoxBytes, &tmB, &full[s], n0 + MT::kBoxCols * c, k0);
         }
         ++issued;
       }
@@ -387,22 +446,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sa = smem_u32(a_hi(s));
         const uint32_t sb = smem_u32(b_hi(s));
 #pragma unroll
-        for (int kk = 0; kk < kBK / 8; ++kk) {
-          // A: K-major, 64-byte rows, 8-row groups 512 B apart; a k-step of
-          // 8 tf32 is 32 bytes along the row.
+        for (int kk = 0; kk < 2; ++kk) {
+          // A: K-major, 64-byte rows, 8-row groups 512 B apart; a k-step (8
+          // tf32 or 16 bf16) is 32 bytes along the row.
           const uint64_t da = make_smem_desc(sa + kk * 32, 16, 512, kLayoutSw64);
-          // B: MN-major, 32-column boxes 2048 B apart (LBO), k-rows 128 B
-          // apart in 4-row swizzle atoms 512 B apart (SBO); a k-step of 8
-          // rows is 1024 B.
-          const uint64_t db = make_smem_desc(sb + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
+          // B: MN-major boxes kBoxBytes apart (LBO), k-rows 128 B apart in
+          // swizzle atoms kBSbo apart (SBO); a k-step is kBStepBytes.
+          const uint64_t db = make_smem_desc(sb + kk * MT::kBStepBytes, MT::kBoxBytes, MT::kBSbo, MT::kBLayout);
           const uint32_t acc = (!chunk_start || kk > 0) ? 1u : 0u;
-          umma_tf32(tmem_base, da, db, kIdesc, acc);
+          if constexpr (MT::kBf16) {
+            umma_f16(tmem_base, da, db, kIdesc, acc);
+          } else {
+            umma_tf32(tmem_base, da, db, kIdesc, acc);
+          }
           if constexpr (SPLIT3) {
             const uint32_t sal = smem_u32(a_lo(s));
             const uint32_t sbl = smem_u32(b_lo(s));
             const uint64_t dal = make_smem_desc(sal + kk * 32, 16, 512, kLayoutSw64);
-            const uint64_t dbl =
-                make_smem_desc(sbl + kk * 1024, TileGeom<BN>::kBChunkBytes, 512, kLayoutSw128Base32);
+            const uint64_t dbl = make_smem_desc(sbl + kk * MT::kBStepBytes, MT::kBoxBytes, MT::kBSbo, MT::kBLayout);
             umma_tf32(tmem_base, da, dbl, kIdesc, 1u);
             umma_tf32(tmem_base, dal, db, kIdesc, 1u);
           }
@@ -443,7 +504,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < kHalf; c += 16) tmem_ld_32x32b_x16(acc_col + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
       tmem_wait_ld();
       tc_fence_before_sync();
-      mbar_arrive(acc_empty);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
       if (f > 0) {
 #pragma unroll
         for (int c = 0; c < kHalf; c += 16) {
@@ -462,9 +524,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if constexpr (kXform) {
       const int g_first = p.a_row0 + m0;  // structured-A row of tile row 0
-      float a_cur[8], a_nxt[8];
+      float a_cur[KS / 2], a_nxt[KS / 2];
       if constexpr (!kATma) {
-        if (num_kb > 0) a_gather<AK>(a_cur, p, g_first, kb_begin * kBK, xw, lane);
+        if (num_kb > 0) a_gather<AK, KS>(a_cur, p, g_first, kb_begin * KS, xw, lane);
       }
       for (int i = 0; i < num_kb && ok; ++i) {
         const int s = i % STAGES;
@@ -481,22 +543,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // Issue the next stage's global loads before waiting on this one.
         if constexpr (!kATma) {
-          if (i + 1 < num_kb) a_gather<AK>(a_nxt, p, g_first, (kb_begin + i + 1) * kBK, xw, lane);
+          if (i + 1 < num_kb) a_gather<AK, KS>(a_nxt, p, g_first, (kb_begin + i + 1) * KS, xw, lane);
         }
         // Warp-uniform outcome: tcgen05.ld/st are .sync.aligned.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) {
           ok = false;
           break;
         }
-        const int k0 = (kb_begin + i) * kBK;
+        const int k0 = (kb_begin + i) * KS;
         if constexpr (!kATma) {
-          a_store<AK, SPLIT3>(a_cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
+          a_store<AK, MD>(a_cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) a_cur[j] = a_nxt[j];
+          for (int j = 0; j < KS / 2; ++j) a_cur[j] = a_nxt[j];
         }
-        if constexpr (!kBTma) b_build<BK, BN, SPLIT3>(p, b_hi(s), b_lo(s), k0, n0, t);
+        if constexpr (!kBTma) b_build<BK, BN, MD>(p, b_hi(s), b_lo(s), k0, n0, t);
+        if constexpr (SPLIT3) {
+          // lo = x - tf32(x) of the TMA-loaded tiles, elementwise at the same
+          // (swizzled) offsets.
+          auto lo_of = [](const uint8_t* src, uint8_t* dst, int bytes, int tid) {
+            const float4* in = reinterpret_cast<const float4*>(src);
+            float4* out = reinterpret_cast<float4*>(dst);
+#pragma unroll 4
+            for (int j = tid; j < bytes / 16; j += kXformThreads) {
+              const float4 x = in[j];
+              out[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+            }
+          };
+          if constexpr (kATma) lo_of(a_hi(s), a_lo(s), kATileBytes, t);
+          if constexpr (kBTma) lo_of(b_hi(s), b_lo(s), kBTile, t);
+        }
         fence_proxy_async_smem();
-        mbar_arrive(&ready[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[s]);
       }
     }
     if constexpr (SPLIT3) {
@@ -545,6 +623,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int v = 0; v < 16; ++v)
               if (col + v < p.N) crow[col + v] = __uint_as_float(r[v]);
+          }
+          if (p.C_bf16 != nullptr) {
+            __nv_bfloat16* brow = p.C_bf16 + static_cast<long long>(row) * p.ldc_bf16;
+#pragma unroll
+            for (int v = 0; v < 16; ++v)
+              if (col + v < p.N) brow[col + v] = __float2bfloat16_rn(__uint_as_float(r[v]));
           }
           if (p.C_lo != nullptr) {
             float* lrow = p.C_lo + static_cast<long long>(row) * p.ldc;

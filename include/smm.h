@@ -146,10 +146,10 @@ int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, flo
  * not acceptable.  The S*B intermediate (and padded copies of A and B when
  * N % 4 != 0 or they are not 16-byte aligned) lives in a fixed 16 MiB static
  * device array inside libsmm, which every GPU that loads the library holds
- * until process exit.  In 3xTF32 mode it holds the intermediate and the lo
- * planes of A, B and the intermediate: N <= 1024 with N % 4 == 0 and
- * 16-byte-aligned A, B (about 830 when padded copies are needed); in TF32 mode
- * N <= 2048.  Larger N returns SMM_ERR_WORKSPACE.  Calls no
+ * until process exit: N <= 2048 in the fp32 modes with N % 4 == 0 and
+ * 16-byte-aligned A, B (about 1180 when padded copies are needed), N <= 1290
+ * in bf16 mode (the bf16 copies share it).  Larger N returns
+ * SMM_ERR_WORKSPACE.  Calls no
  * cudaMalloc/cudaFree.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress) and must come before any stream
  * capture.  Every call shares the one array and it keeps the last call's

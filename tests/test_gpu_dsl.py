@@ -25,14 +25,15 @@ def relerr64(C, R):
     return O.relerr(np.ascontiguousarray(C, np.float32), np.asarray(R, np.float64))
 
 
+@pytest.mark.parametrize("mode,tol", [("3xtf32", 1e-5), ("bf16", 1e-2)])
 @pytest.mark.parametrize("mn", [(1, 1), (7, 9), (128, 128), (200, 130), (512, 384)])
-def test_gen_x_upper(cuda, mn):
+def test_gen_x_upper(cuda, mn, mode, tol):
     M, N = mn
     A = W.make_gemm(M, 1, N, seed=M)["A"]  # M x N
     Up = W.make_upper(N, 1, seed=N)["U"]
-    C = ops.gen_x_upper(dev(A), dev(Up)).cpu().numpy()
+    C = ops.gen_x_upper(dev(A), dev(Up), mode=mode).cpu().numpy()
     R = A.astype(np.float64) @ W.unpack_upper(Up, N).astype(np.float64)
-    assert relerr64(C, R) <= 1e-5
+    assert relerr64(C, R) <= tol
 
 
 @pytest.mark.parametrize("mn", [(1, 1), (5, 6), (128, 256), (300, 257)])
@@ -45,13 +46,14 @@ def test_gen_x_symm(cuda, mn):
     assert relerr64(C, R) <= 1e-5
 
 
+@pytest.mark.parametrize("mode,tol", [("3xtf32", 1e-5), ("bf16", 1e-2)])
 @pytest.mark.parametrize("N", [1, 3, 128, 257])
-def test_symm_x_symm(cuda, N):
+def test_symm_x_symm(cuda, N, mode, tol):
     S1 = W.make_sandwich(N, seed=N)["S"]
     S2 = W.make_sandwich(N, seed=N + 9)["S"]
-    C = ops.symm_x_symm(dev(S1), dev(S2)).cpu().numpy()
+    C = ops.symm_x_symm(dev(S1), dev(S2), mode=mode).cpu().numpy()
     R = W.unpack_symmetric(S1, N).astype(np.float64) @ W.unpack_symmetric(S2, N).astype(np.float64)
-    assert relerr64(C, R) <= 1e-5
+    assert relerr64(C, R) <= tol
 
 
 # ---------------------------------------------------------------- DSL drop-in

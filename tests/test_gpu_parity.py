@@ -68,7 +68,7 @@ def _relerr_full(C, R):
     return O.relerr(C, R)
 
 
-@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
 def test_gemm_golden(cuda, golden, mode):
     A, B = golden["gemm_A"], golden["gemm_B"]
     C = host(ops.gemm(dev(A), dev(B), mode=mode))
@@ -78,7 +78,7 @@ def test_gemm_golden(cuda, golden, mode):
     assert O.relerr(golden["gemm_C"], R) <= 1e-5
 
 
-@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
 @pytest.mark.parametrize("mnk", [(128, 256, 64), (256, 512, 1024), (1, 1, 1), (7, 5, 3), (129, 257, 127),
                                  (300, 200, 100), (1024, 1024, 1024)])
 def test_gemm_shapes(cuda, mode, mnk):
@@ -101,7 +101,7 @@ def test_tf32_operand_reading_truncates(cuda):
     assert np.all(C == 1.0), np.unique(C)
 
 
-@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
 def test_upper_packed_golden(cuda, golden, mode):
     Up, B = golden["upper_U"], golden["upper_B"]
     C = host(ops.upper_left(dev(Up), dev(B), packed=True, mode=mode))
@@ -110,18 +110,19 @@ def test_upper_packed_golden(cuda, golden, mode):
     assert O.relerr(golden["upper_C"], R) <= 1e-5
 
 
+@pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
 @pytest.mark.parametrize("packed", [True, False])
 @pytest.mark.parametrize("n_cols", [(1, 1), (5, 9), (128, 64), (129, 200), (300, 260), (1024, 1024)])
-def test_upper_shapes(cuda, packed, n_cols):
+def test_upper_shapes(cuda, packed, n_cols, mode):
     N, ncols = n_cols
     w = W.make_upper(N, ncols, seed=N + ncols)
     U = w["U"] if packed else W.unpack_upper(w["U"], N)
-    C = host(ops.upper_left(dev(U), dev(w["B"]), packed=packed))
+    C = host(ops.upper_left(dev(U), dev(w["B"]), packed=packed, mode=mode))
     R = O.upper_left_rows_f64(w["U"], w["B"], np.arange(N))
-    assert _relerr_full(C, R) <= 1e-5, (n_cols, _relerr_full(C, R))
+    assert _relerr_full(C, R) <= TOL[mode], (n_cols, _relerr_full(C, R))
 
 
-@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
 def test_toeplitz_golden(cuda, golden, mode):
     g, B = golden["toeplitz_g"], golden["toeplitz_B"]
     C = host(ops.toeplitz_left(dev(g), dev(B), mode=mode))
@@ -130,13 +131,14 @@ def test_toeplitz_golden(cuda, golden, mode):
     assert O.relerr(golden["toeplitz_C"], R) <= 1e-5
 
 
+@pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
 @pytest.mark.parametrize("n_cols", [(1, 1), (3, 8), (128, 64), (130, 70), (512, 1024)])
-def test_toeplitz_shapes(cuda, n_cols):
+def test_toeplitz_shapes(cuda, n_cols, mode):
     N, ncols = n_cols
     w = W.make_toeplitz(N, ncols, seed=N * 3 + ncols)
-    C = host(ops.toeplitz_left(dev(w["g"]), dev(w["B"])))
+    C = host(ops.toeplitz_left(dev(w["g"]), dev(w["B"]), mode=mode))
     R = O.toeplitz_left_rows_f64(w["g"], w["B"], np.arange(N))
-    assert _relerr_full(C, R) <= 1e-5, (n_cols, _relerr_full(C, R))
+    assert _relerr_full(C, R) <= TOL[mode], (n_cols, _relerr_full(C, R))
 
 
 @pytest.mark.parametrize("n_cols", [(1, 1), (6, 10), (128, 128), (257, 130)])
@@ -151,7 +153,7 @@ def test_symm_left_shapes(cuda, n_cols):
     assert _relerr_full(C, R) <= 1e-5
 
 
-@pytest.mark.parametrize("mode", ["3xtf32", "tf32"])
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
 def test_sandwich_golden(cuda, golden, mode):
     A, S, B = golden["sandwich_A"], golden["sandwich_S"], golden["sandwich_B"]
     C = host(ops.symm_sandwich(dev(A), dev(S), dev(B), mode=mode))
@@ -160,12 +162,13 @@ def test_sandwich_golden(cuda, golden, mode):
     assert O.relerr(golden["sandwich_C"], R) <= 1e-5
 
 
+@pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
 @pytest.mark.parametrize("N", [1, 7, 130, 512])
-def test_sandwich_shapes(cuda, N):
+def test_sandwich_shapes(cuda, N, mode):
     s = W.make_sandwich(N, seed=N + 1)
-    C = host(ops.symm_sandwich(dev(s["A"]), dev(s["S"]), dev(s["B"])))
+    C = host(ops.symm_sandwich(dev(s["A"]), dev(s["S"]), dev(s["B"]), mode=mode))
     R = O.sandwich_rows_f64(s["A"], s["S"], s["B"], np.arange(N))
-    assert _relerr_full(C, R) <= 1e-5
+    assert _relerr_full(C, R) <= TOL[mode]
 
 
 # ---------------------------------------------------------------- failure detection
