@@ -225,7 +225,7 @@ CPU_SAMPLE_N = {"diag": 8192, "gemm": 2048, "upper": 2048, "sandwich": 1024, "to
 
 
 def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
-    cores = os.cpu_count() or 1
+    cores = int(os.environ.get("OMP_NUM_THREADS", host_threads()))
     sn = min(n, CPU_SAMPLE_N[op])
     rates = []
     t0 = time.time()
@@ -473,12 +473,30 @@ def e2e_ours(args, h_in, n):
 
 
 # ---------------------------------------------------------------- reference arm
+def host_threads() -> int:
+    """Host cores this process may use (its CPU affinity)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def use_all_host_threads() -> int:
+    """torchrun sets OMP_NUM_THREADS=1 per rank; the CPU kernels of the
+    reference arm and the CPU baseline run alone on the host and get every
+    core.  Must run before the OpenMP runtime is loaded."""
+    n = host_threads()
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    return n
+
+
 def run_reference(args, rank, world):
     """The reference's own CPU implementation of the path (oracle/_ref: its
     AVX2+OpenMP kernels compiled from its sources) on this host's cores, same
     config, metric and unit.  Rank 0 only."""
     op = args.op
     n = args.n or WORKLOADS[op]["N"]
+    use_all_host_threads()
     import oracle as O
     if not O.ref_available():
         return {"impl": "reference", "unavailable": "oracle/_ref (the reference CPU kernels) was not built"}
@@ -492,7 +510,7 @@ def run_reference(args, rank, world):
     ms = statistics.median(times)
     scale = 1e9 if op == "diag" else 1e12
     value = units / (ms * 1e-3) / scale
-    cores = os.cpu_count() or 1
+    cores = int(os.environ.get("OMP_NUM_THREADS", host_threads()))
     sample = f"{op} at order {sn}" + ("" if sn == n else f" (bounded sample of the order-{n} workload)")
     return {
         "metric": METRIC, "value": round(value, 3), "unit": WORKLOADS[op]["unit"], "n_gpus": world,
@@ -518,6 +536,8 @@ def main():
         print(json.dumps(run_reference(args, rank, world)), flush=True)
         return 0
 
+    if int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        use_all_host_threads()  # the CPU baseline leg runs at N = 1 only
     rank, world, local = dist_init(args)
     res, d_in, h_in = run_ours(args, rank, world, local)
     n = args.n or WORKLOADS[args.op]["N"]

@@ -446,11 +446,21 @@ int check_slab(const char* who, int N, int ncols, int row0, int nrows) {
     return set_error(SMM_ERR_INVALID, "%s: bad shape N=%d ncols=%d rows [%d, %d)", who, N, ncols, row0, row0 + nrows);
   return SMM_OK;
 }
+
+// Packed triangles are addressed with 32-bit offsets on chip.
+constexpr int kMaxPackedOrder = 92681;  // N(N+1)/2 < 2^32
+int check_packed(const char* who, int N) {
+  if (N > kMaxPackedOrder)
+    return set_error(SMM_ERR_INVALID, "%s: packed order N = %d exceeds %d", who, N, kMaxPackedOrder);
+  return SMM_OK;
+}
 }  // namespace
 
 extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, float* C, int N, int ncols, int row0,
                                    int nrows, int mode, void* ws, size_t ws_bytes, void* stream) {
   if (int rc = check_slab("smm_upper_left", N, ncols, row0, nrows)) return rc;
+  if (u_fmt == SMM_FMT_PACKED)
+    if (int rc = check_packed("smm_upper_left", N)) return rc;
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_upper_left: unknown mode %d", mode);
   if (u_fmt != SMM_FMT_PACKED && u_fmt != SMM_FMT_DENSE)
     return set_error(SMM_ERR_INVALID, "smm_upper_left: unknown U format %d", u_fmt);
@@ -517,6 +527,7 @@ extern "C" size_t smm_symm_left_workspace_size(int N, int ncols, int mode) {
 extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int N, int ncols, int row0, int nrows,
                                   int mode, void* ws, size_t ws_bytes, void* stream) {
   if (int rc = check_slab("smm_symm_left", N, ncols, row0, nrows)) return rc;
+  if (int rc = check_packed("smm_symm_left", N)) return rc;
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_left: unknown mode %d", mode);
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_left: null pointer");
@@ -559,6 +570,7 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich: unknown mode %d", mode);
   if (N == 0) return SMM_OK;
   if (!A || !S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich: null pointer");
+  if (int rc = check_packed("smm_symm_sandwich", N)) return rc;
   cudaStream_t st = as_stream(stream);
   const bool s3 = (mode == SMM_MODE_3XTF32);
   const bool bf = (mode == SMM_MODE_BF16);
@@ -602,6 +614,7 @@ int gen_x_struct(const char* who, BKind bk, const float* A, const float* X, floa
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
   if (M == 0 || N == 0) return SMM_OK;
   if (!A || !X || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
+  if (int rc = check_packed(who, N)) return rc;
   const bool s3 = (mode == SMM_MODE_3XTF32);
   if (int rc = check_ws(who, ws, ws_bytes, staged_bytes(A, M, N, mode))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
@@ -626,6 +639,7 @@ extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: unknown mode %d", mode);
   if (N == 0) return SMM_OK;
   if (!S1 || !S2 || !C) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: null pointer");
+  if (int rc = check_packed("smm_symm_x_symm", N)) return rc;
   return run_contraction(AKind::SymmPacked, BKind::SymmPacked, mode, structured_op(S1, N), structured_op(S2, N), C,
                          N, N, N, N, as_stream(stream));
 }

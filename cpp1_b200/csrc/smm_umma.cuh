@@ -203,15 +203,66 @@ __device__ __forceinline__ void a_coord(bool rows, int xw, int lane, int it, int
   }
 }
 
+// Offset of element (gr, 0) in the operand's storage for the rows a thread
+// gathers in the k mapping (fixed for the whole K loop): packed upper
+// row start minus gr, or n - 1 - gr for a Toeplitz generator, so the element
+// (gr, k) is src[base + k].  Packed storage of order n < 92682 has fewer than
+// 2^32 elements (the host rejects larger), so offsets are 32-bit; an
+// out-of-range row's base may wrap but is never dereferenced.
+__device__ __forceinline__ uint32_t packed_row_base(long long i, long long n) {
+  return static_cast<uint32_t>(i * n - i * (i - 1) / 2 - i);
+}
+
 template <AKind AK, int KS>
-__device__ __forceinline__ void a_gather(float (&v)[KS / 2], const UmmaParams& p, int g_first, int k0, int xw,
-                                         int lane) {
-  const bool rows = a_rows_mapping<AK, KS>(g_first, k0);
+__device__ __forceinline__ void a_row_bases(uint32_t (&rb)[KS / 2], const UmmaParams& p, int g_first, int xw,
+                                            int lane) {
 #pragma unroll
   for (int it = 0; it < KS / 2; ++it) {
     int r, kl;
-    a_coord<KS>(rows, xw, lane, it, r, kl);
-    v[it] = a_value<AK>(p.a_src, p.a_dim, g_first + r, k0 + kl);
+    a_coord<KS>(false, xw, lane, it, r, kl);
+    const long long gr = g_first + r;
+    rb[it] = (AK == AKind::Toeplitz) ? static_cast<uint32_t>(p.a_dim - 1 - gr) : packed_row_base(gr, p.a_dim);
+  }
+}
+
+template <AKind AK, int KS>
+__device__ __forceinline__ void a_gather(float (&v)[KS / 2], const UmmaParams& p, const uint32_t (&rb)[KS / 2],
+                                         int g_first, int k0, int xw, int lane) {
+  const int n = p.a_dim;
+  const float* __restrict__ src = p.a_src;
+  if (a_rows_mapping<AK, KS>(g_first, k0)) {
+    // symmetric tile wholly below the diagonal: element (gr, k) = S[k][gr],
+    // at row start of packed row k (+ gr), k consecutive per thread
+    int r, kl;
+    a_coord<KS>(true, xw, lane, 0, r, kl);
+    const int gr = g_first + r;
+    uint32_t base = packed_row_base(k0 + kl, n);
+#pragma unroll
+    for (int it = 0; it < KS / 2; ++it) {
+      const int k = k0 + kl + it;
+      v[it] = (gr < n && k < n) ? __ldg(src + (base + static_cast<uint32_t>(gr))) : 0.0f;
+      base += static_cast<uint32_t>(n - k - 1);  // row start of packed row k+1
+    }
+    return;
+  }
+  int r0, kl;
+  a_coord<KS>(false, xw, lane, 0, r0, kl);
+  const int k = k0 + kl;
+  uint32_t mbase = 0;  // symmetric, below-diagonal elements: packed row k
+  if constexpr (AK == AKind::SymmPacked) mbase = packed_row_base(k, n);
+#pragma unroll
+  for (int it = 0; it < KS / 2; ++it) {
+    int r;
+    a_coord<KS>(false, xw, lane, it, r, kl);
+    const int gr = g_first + r;
+    const bool in = gr < n && k < n;
+    if constexpr (AK == AKind::UpperPacked) {
+      v[it] = (in && k >= gr) ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
+    } else if constexpr (AK == AKind::Toeplitz) {
+      v[it] = in ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
+    } else {
+      v[it] = in ? __ldg(src + (k >= gr ? rb[it] + static_cast<uint32_t>(k) : mbase + static_cast<uint32_t>(gr))) : 0.0f;
+    }
   }
 }
 
@@ -525,8 +576,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kXform) {
       const int g_first = p.a_row0 + m0;  // structured-A row of tile row 0
       float a_cur[KS / 2], a_nxt[KS / 2];
+      uint32_t a_rb[KS / 2];
       if constexpr (!kATma) {
-        if (num_kb > 0) a_gather<AK, KS>(a_cur, p, g_first, kb_begin * KS, xw, lane);
+        a_row_bases<AK, KS>(a_rb, p, g_first, xw, lane);
+        if (num_kb > 0) a_gather<AK, KS>(a_cur, p, a_rb, g_first, kb_begin * KS, xw, lane);
       }
       for (int i = 0; i < num_kb && ok; ++i) {
         const int s = i % STAGES;
@@ -543,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // Issue the next stage's global loads before waiting on this one.
         if constexpr (!kATma) {
-          if (i + 1 < num_kb) a_gather<AK, KS>(a_nxt, p, g_first, (kb_begin + i + 1) * KS, xw, lane);
+          if (i + 1 < num_kb) a_gather<AK, KS>(a_nxt, p, a_rb, g_first, (kb_begin + i + 1) * KS, xw, lane);
         }
         // Warp-uniform outcome: tcgen05.ld/st are .sync.aligned.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) {
