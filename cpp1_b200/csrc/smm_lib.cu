@@ -106,10 +106,10 @@ struct Maps {
   CUtensorMap a{}, b{}, al{}, bl{};
 };
 
-template <AKind AK, BKind BK, Mode MD, int BN, int STAGES>
+template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR>
 int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
-  auto kern = umma_gemm_kernel<AK, BK, MD, BN, STAGES>;
-  constexpr int smem = umma_smem_bytes<BN, MD == Mode::TF32x3, STAGES>();
+  auto kern = umma_gemm_kernel<AK, BK, MD, BN, STAGES, PAIR>;
+  constexpr int smem = umma_smem_bytes<PAIR ? BN / 2 : BN, MD == Mode::TF32x3, STAGES>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
   static bool attr_set[64] = {};
   int dev = 0;
@@ -119,43 +119,81 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
                  "cudaFuncSetAttribute(max dynamic smem)");
     attr_set[dev & 63] = true;
   }
-  const long long blocks = static_cast<long long>(p.row_tiles) * p.col_tiles;
+  const long long blocks = static_cast<long long>(p.row_tiles) * p.col_tiles * (PAIR ? 2 : 1);
   if (blocks > 0x7FFFFFFFLL) return set_error(SMM_ERR_INVALID, "product too large for one launch");
-  kern<<<static_cast<unsigned>(blocks), kThreads, smem, st>>>(m.a, m.b, m.al, m.bl, p);
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.al, m.bl, p), "tcgen05 pair contraction launch");
+  } else {
+    kern<<<static_cast<unsigned>(blocks), kThreads, smem, st>>>(m.a, m.b, m.al, m.bl, p);
+  }
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "tcgen05 contraction launch");
   return SMM_OK;
 }
 
-// Stage counts fill ~192 KiB of shared memory.
-// Stage counts fill ~192 KiB of shared memory.
-template <AKind AK, BKind BK, int BN>
+// Stage counts fill ~192 KiB of shared memory (a pair CTA stages half the B
+// columns, so its stages are smaller and more of them fit).
+template <AKind AK, BKind BK, int BN, bool PAIR>
 int launch_mode(int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+  constexpr int kCols = PAIR ? BN / 2 : BN;  // B columns per CTA
   if (mode == SMM_MODE_3XTF32) {
-    constexpr int S = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-    return launch_umma<AK, BK, Mode::TF32x3, BN, S>(m, p, st);
+    constexpr int S = (kCols == 256) ? 4 : (kCols == 128 ? 6 : 8);
+    return launch_umma<AK, BK, Mode::TF32x3, BN, S, PAIR>(m, p, st);
   }
-  if (mode == SMM_MODE_BF16) return launch_umma<AK, BK, Mode::BF16, BN, 8>(m, p, st);
-  return launch_umma<AK, BK, Mode::TF32, BN, 8>(m, p, st);
+  if (mode == SMM_MODE_BF16) return launch_umma<AK, BK, Mode::BF16, BN, 8, PAIR>(m, p, st);
+  return launch_umma<AK, BK, Mode::TF32, BN, 8, PAIR>(m, p, st);
 }
 
 template <AKind AK, BKind BK>
-int launch_bn(int bn, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+int launch_bn(int bn, bool pair, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+  if (pair) {
+    if (bn == 256) return launch_mode<AK, BK, 256, true>(mode, m, p, st);
+    return launch_mode<AK, BK, 128, true>(mode, m, p, st);
+  }
   switch (bn) {
-    case 256: return launch_mode<AK, BK, 256>(mode, m, p, st);
-    case 128: return launch_mode<AK, BK, 128>(mode, m, p, st);
-    default: return launch_mode<AK, BK, 64>(mode, m, p, st);
+    case 256: return launch_mode<AK, BK, 256, false>(mode, m, p, st);
+    case 128: return launch_mode<AK, BK, 128, false>(mode, m, p, st);
+    default: return launch_mode<AK, BK, 64, false>(mode, m, p, st);
   }
 }
 
-// Output tile width: the widest tile that still yields about a wave of CTAs.
-int pick_bn(int M, int N) {
-  const long long rt = (M + kBM - 1) / kBM;
+// CTA pairs (256-row tiles, tcgen05 cta_group::2) whenever there are at least
+// two row tiles and the pair tiles fill about a wave of the 74 SM pairs.
+// SMM_PAIR=0 forces single-CTA tiles, SMM_PAIR=1 pairs for every M > 128.
+bool use_pairs(int M, int N) {
+  const char* e = std::getenv("SMM_PAIR");
+  if (e && e[0] == '0') return false;
+  if (M <= kBM) return false;
+  if (e && e[0] == '1') return true;
+  const long long rp = (M + 2 * kBM - 1) / (2 * kBM);
+  return rp * ((N + 127) / 128) >= 60;
+}
+
+// Output tile width: the widest tile that still yields about a wave of CTAs
+// (of CTA pairs when pair is set).
+int pick_bn(int M, int N, bool pair) {
   const char* e = std::getenv("SMM_TILE_N");
   if (e) {
     int v = std::atoi(e);
-    if (v == 64 || v == 128 || v == 256) return v;
+    if (v == 256 || v == 128 || (v == 64 && !pair)) return v;
   }
+  if (pair) {
+    const long long rp = (M + 2 * kBM - 1) / (2 * kBM);
+    return (N > 128 && rp * ((N + 255) / 256) >= 60) ? 256 : 128;
+  }
+  const long long rt = (M + kBM - 1) / kBM;
   if (N > 128 && rt * ((N + 255) / 256) >= 120) return 256;
   if (N > 64 && rt * ((N + 127) / 128) >= 100) return 128;
   return 64;
@@ -186,7 +224,8 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
                     int ldc_bf16 = 0) {
   const bool split3 = (mode == SMM_MODE_3XTF32);
   const bool bf16 = (mode == SMM_MODE_BF16);
-  const int bn = pick_bn(M, N);
+  const bool pair = use_pairs(M, N);
+  const int bn = pick_bn(M, N, pair);
   Maps m;
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);
@@ -221,7 +260,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.a_row0 = a.row0;
   p.b_src = b.src;
   p.b_dim = b.dim;
-  p.row_tiles = (M + kBM - 1) / kBM;
+  p.row_tiles = pair ? (M + 2 * kBM - 1) / (2 * kBM) : (M + kBM - 1) / kBM;
   p.col_tiles = (N + bn - 1) / bn;
   p.raster_group = 8;
   p.status = device_status_word();
@@ -231,19 +270,19 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   g_trace = nullptr;
   if (bk == BKind::Dense) {
     switch (ak) {
-      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, mode, m, p, st);
-      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, mode, m, p, st);
-      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, mode, m, p, st);
-      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, mode, m, p, st);
-      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, mode, m, p, st);
+      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, pair, mode, m, p, st);
+      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, pair, mode, m, p, st);
+      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, pair, mode, m, p, st);
+      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, pair, mode, m, p, st);
+      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, pair, mode, m, p, st);
     }
   }
   if (ak == AKind::Dense && bk == BKind::UpperPacked)
-    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, mode, m, p, st);
+    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, pair, mode, m, p, st);
   if (ak == AKind::Dense && bk == BKind::SymmPacked)
-    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, mode, m, p, st);
+    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, pair, mode, m, p, st);
   if (ak == AKind::SymmPacked && bk == BKind::SymmPacked)
-    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, mode, m, p, st);
+    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, pair, mode, m, p, st);
   return set_error(SMM_ERR_INVALID, "unsupported operand kinds");
 }
 

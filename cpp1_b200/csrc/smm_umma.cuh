@@ -354,7 +354,19 @@ __device__ __forceinline__ void b_build(const UmmaParams& p, uint8_t* bh, uint8_
 // ---------------------------------------------------------------- kernel
 // tmA/tmB map the operands (hi, or bf16 copies), tmAl/tmBl their lo planes
 // (3xTF32 only).
-template <AKind AK, BKind BK, Mode MD, int BN, int STAGES>
+//
+// PAIR: the CTA pair form.  Clusters of two CTAs compute a 256 x BN tile with
+// tcgen05.mma.cta_group::2 issued by the even CTA (the leader): each CTA
+// stages its own 128 A rows and BN/2 B columns (so per SM the MMA reads 1.5x
+// fewer shared-memory bytes per flop than the one-CTA 128 x BN tile, and the
+// stage is smaller, so more stages fit), and holds its 128 rows of the
+// accumulator in its own tensor memory.  Each CTA's TMA completes on its own
+// `full` barrier; its transform warps then arrive on the leader's `ready`
+// barrier, the leader's MMA commits to the `empty`,
+// `acc_full` and `accum_full` barriers of both CTAs (one commit per CTA), and
+// the fold warps of both CTAs arrive on the leader's `acc_empty`.  No load is
+// multicast.
+template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
@@ -362,17 +374,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   using MT = ModeTraits<MD>;
   constexpr bool SPLIT3 = MT::kSplit3;
   constexpr int KS = MT::kStageK;
-  constexpr int kBTile = TileGeom<BN>::kBTileBytes;
-  constexpr int kStage = stage_bytes<BN, SPLIT3>();
+  constexpr int kBCols = PAIR ? BN / 2 : BN;  // B columns staged by this CTA
+  constexpr int kBTile = TileGeom<kBCols>::kBTileBytes;
+  constexpr int kStage = stage_bytes<kBCols, SPLIT3>();
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
   constexpr bool kBTma = (BK == BKind::Dense);
   // The transform warps touch every stage when a tile is built on chip or
-  // when lo tiles are derived from the TMA-loaded ones (3xTF32).
-  constexpr bool kXform = !kATma || !kBTma || SPLIT3;
+  // when lo tiles are derived from the TMA-loaded ones (3xTF32); in a pair
+  // they also relay TMA completion to the leader.
+  constexpr bool kXform = !kATma || !kBTma || SPLIT3 || PAIR;
   constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0);
   constexpr uint32_t kTmemCols = tmem_cols<BN, SPLIT3>();
-  constexpr uint32_t kIdesc = make_idesc(MT::kFmt, kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
+  constexpr uint32_t kIdesc = make_idesc(MT::kFmt, PAIR ? 2 * kBM : kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
   constexpr int kHalf = BN / 2;  // columns per epilogue warp
+  constexpr uint32_t kArrivals = (PAIR ? 2 : 1) * (kXformThreads / 32);  // warps arriving on ready / acc_empty
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -392,14 +407,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = (rank == 0);
+  // shared::cluster address of a barrier of this CTA in CTA `r` of the pair
+  auto in_cta = [&](uint64_t* bar, uint32_t r) { return mapa_shared(smem_u32(bar), r); };
 
-  // Grouped rasterisation: consecutive CTAs cover raster_group row tiles x
+  // Grouped rasterisation: consecutive tiles cover raster_group row tiles x
   // all column tiles, so a wave shares A and B slices through L2.  Groups go
   // top to bottom, so for the triangular operand (row tile i has K range
-  // [128 i, N)) the longest tiles are dispatched first.
+  // [tile height * i, N)) the longest tiles are dispatched first.  In a pair,
+  // a row tile is 256 rows and both CTAs take the same tile.
   int m_tile, n_tile;
   {
-    const int b = blockIdx.x;
+    const int b = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
     const int per_group = p.raster_group * p.col_tiles;
     const int g = b / per_group;
     const int first = g * p.raster_group;
@@ -408,12 +428,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     m_tile = first + in % rows_here;
     n_tile = in / rows_here;
   }
-  const int m0 = m_tile * kBM;
-  const int n0 = n_tile * BN;
-  // Rows of a triangular left operand are zero left of the diagonal: row
-  // tile [g0, g0+128) of U needs k >= g0 only.
+  const int tile_m0 = m_tile * (PAIR ? 2 * kBM : kBM);
+  const int m0 = tile_m0 + static_cast<int>(rank) * kBM;   // this CTA's A rows / C rows
+  const int n0 = n_tile * BN;                              // the tile's columns
+  const int nb0 = n0 + static_cast<int>(rank) * kBCols;    // this CTA's B columns
+  // Rows of a triangular left operand are zero left of the diagonal: a row
+  // tile starting at row g0 needs k >= g0 only.
   int kb_begin = 0;
-  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + m0) / KS;
+  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + tile_m0) / KS;
   int kb_end = (p.K + KS - 1) / KS;
   // An upper-triangular right operand is zero below its diagonal: column
   // tile [n0, n0+BN) needs k < n0 + BN only.
@@ -424,12 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], kXformThreads / 32);  // one arrival per transform warp
+      mbar_init(&ready[s], kArrivals);  // one arrival per transform warp (of both CTAs)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum_full, 1);
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kXformThreads / 32);
+    mbar_init(acc_empty, kArrivals);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -437,9 +459,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kATma) tma_prefetch_desc(&tmA);
     if constexpr (kBTma) tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+    else
+      tmem_alloc(tmem_slot, kTmemCols);
+  }
   tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync_all();  // both CTAs' barriers initialised before any remote arrival
+  else
+    __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   const bool tr = p.trace != nullptr && blockIdx.x == 0;
@@ -452,6 +482,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const WaitCtx wmma{abort_flag, p.status, p.wait_limit_ns, kWaitMma};
   const WaitCtx wxf{abort_flag, p.status, p.wait_limit_ns, kWaitTransform};
   const WaitCtx wepi{abort_flag, p.status, p.wait_limit_ns, kWaitEpilogue};
+
+  // MMA completion signals: to this CTA's barrier, or (pair) to the barrier
+  // at the same offset in both CTAs.
+  auto commit_all = [&](uint64_t* bar) {
+    if constexpr (PAIR) {
+      umma_commit_pair(in_cta(bar, 0));
+      umma_commit_pair(in_cta(bar, 1));
+    } else {
+      umma_commit(bar);
+    }
+  };
+  // Transform / fold warps report to the MMA issuer (the leader's barrier).
+  auto arrive_issuer = [&](uint64_t* bar) {
+    if constexpr (PAIR)
+      mbar_arrive_cluster(in_cta(bar, 0));
+    else
+      mbar_arrive(bar);
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -466,8 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (kATma) tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
         if constexpr (kBTma) {
 #pragma unroll
-          for (int c = 0; c < BN / MT::kBoxCols; ++c)
-            tma_load_2d(b_hi(s) + c * MT::kBoxBytes, &tmB, &full[s], n0 + MT::kBoxCols * c, k0);
+          for (int c = 0; c < kBCols / MT::kBoxCols; ++c)
+            tma_load_2d(b_hi(s) + c * MT::kBoxBytes, &tmB, &full[s], nb0 + MT::kBoxCols * c, k0);
         }
         ++issued;
       }
@@ -483,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       for (int i = 0; i < num_kb; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
@@ -505,30 +553,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           // swizzle atoms kBSbo apart (SBO); a k-step is kBStepBytes.
           const uint64_t db = make_smem_desc(sb + kk * MT::kBStepBytes, MT::kBoxBytes, MT::kBSbo, MT::kBLayout);
           const uint32_t acc = (!chunk_start || kk > 0) ? 1u : 0u;
-          if constexpr (MT::kBf16) {
-            umma_f16(tmem_base, da, db, kIdesc, acc);
-          } else {
-            umma_tf32(tmem_base, da, db, kIdesc, acc);
-          }
+          auto mma = [&](uint64_t x, uint64_t y, uint32_t accumulate) {
+            if constexpr (PAIR) {
+              if constexpr (MT::kBf16)
+                umma_f16_pair(tmem_base, x, y, kIdesc, accumulate);
+              else
+                umma_tf32_pair(tmem_base, x, y, kIdesc, accumulate);
+            } else {
+              if constexpr (MT::kBf16)
+                umma_f16(tmem_base, x, y, kIdesc, accumulate);
+              else
+                umma_tf32(tmem_base, x, y, kIdesc, accumulate);
+            }
+          };
+          mma(da, db, acc);
           if constexpr (SPLIT3) {
             const uint32_t sal = smem_u32(a_lo(s));
             const uint32_t sbl = smem_u32(b_lo(s));
             const uint64_t dal = make_smem_desc(sal + kk * 32, 16, 512, kLayoutSw64);
             const uint64_t dbl = make_smem_desc(sbl + kk * MT::kBStepBytes, MT::kBoxBytes, MT::kBSbo, MT::kBLayout);
-            umma_tf32(tmem_base, da, dbl, kIdesc, 1u);
-            umma_tf32(tmem_base, dal, db, kIdesc, 1u);
+            mma(da, dbl, 1u);
+            mma(dal, db, 1u);
           }
         }
-        umma_commit(&empty[s]);
+        commit_all(&empty[s]);
         if constexpr (SPLIT3) {
-          if (i % kChunk == kChunk - 1 || i == num_kb - 1) umma_commit(acc_full);
+          if (i % kChunk == kChunk - 1 || i == num_kb - 1) commit_all(acc_full);
         }
         if (tr) p.trace[kTrMmas] = static_cast<uint32_t>(i + 1);
       }
       // Signals the epilogue; on abort it still fires once every MMA issued
       // so far has finished.  The issuer waits for it too (bounded, ignoring
       // the abort flag) so tensor memory is quiescent before it is freed.
-      umma_commit(accum_full);
+      commit_all(accum_full);
       volatile int no_abort = 0;
       const WaitCtx drain{&no_abort, p.status, p.wait_limit_ns, kWaitDrain};
       mbar_wait(accum_full, 0, drain);
@@ -545,71 +602,72 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int folded = 0;  // chunks already added into the running sum
 
-    // Copy chunk f's accumulator (this warp's 32 lanes x kHalf columns) to
-    // registers, release it to the MMA, then add it into the running sum.
+    // Add chunk f's accumulator (this warp's 32 lanes x kHalf columns) into
+    // the running sum, a quarter tile (kHalf/2 columns) at a time so the
+    // registers it needs stay small, then release the accumulator to the MMA.
     auto fold = [&](int f) -> bool {
       if (!__all_sync(0xffffffffu, mbar_wait(acc_full, f & 1, wxf))) return false;
       tc_fence_after_sync();
-      uint32_t a[kHalf];
+      constexpr int kQ = kHalf / 2;
+#pragma unroll 1
+      for (int hq = 0; hq < 2; ++hq) {
+        uint32_t a[kQ];
 #pragma unroll
-      for (int c = 0; c < kHalf; c += 16) tmem_ld_32x32b_x16(acc_col + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
-      tmem_wait_ld();
+        for (int c = 0; c < kQ; c += 16)
+          tmem_ld_32x32b_x16(acc_col + hq * kQ + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
+        tmem_wait_ld();
+        if (f > 0) {
+#pragma unroll
+          for (int c = 0; c < kQ; c += 16) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(sum_col + hq * kQ + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) a[c + j] = __float_as_uint(__uint_as_float(a[c + j]) + __uint_as_float(r[j]));
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < kQ; c += 16)
+          tmem_st_32x32b_x16(sum_col + hq * kQ + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
+      }
+      tmem_wait_st();
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
-      if (f > 0) {
-#pragma unroll
-        for (int c = 0; c < kHalf; c += 16) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(sum_col + c, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) a[c + j] = __float_as_uint(__uint_as_float(a[c + j]) + __uint_as_float(r[j]));
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < kHalf; c += 16) tmem_st_32x32b_x16(sum_col + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
-      tmem_wait_st();
+      if (lane == 0) arrive_issuer(acc_empty);
       return true;
     };
 
     if constexpr (kXform) {
-      const int g_first = p.a_row0 + m0;  // structured-A row of tile row 0
-      float a_cur[KS / 2], a_nxt[KS / 2];
+      const int g_first = p.a_row0 + m0;  // structured-A row of this CTA's tile row 0
+      // Gathered A values rotate through three register buffers, named at
+      // compile time (no register moves): stage i is stored from buffer i % 3
+      // while the loads of stage i + 2 are in flight into buffer (i + 2) % 3,
+      // so a gather has two stage times to return from L2.
+      float a_b0[KS / 2], a_b1[KS / 2], a_b2[KS / 2];
       uint32_t a_rb[KS / 2];
       if constexpr (!kATma) {
         a_row_bases<AK, KS>(a_rb, p, g_first, xw, lane);
-        if (num_kb > 0) a_gather<AK, KS>(a_cur, p, a_rb, g_first, kb_begin * KS, xw, lane);
+        if (num_kb > 0) a_gather<AK, KS>(a_b0, p, a_rb, g_first, kb_begin * KS, xw, lane);
+        if (num_kb > 1) a_gather<AK, KS>(a_b1, p, a_rb, g_first, (kb_begin + 1) * KS, xw, lane);
       }
-      for (int i = 0; i < num_kb && ok; ++i) {
+      auto stage = [&](int i, const float (&cur)[KS / 2], float (&ahead)[KS / 2]) -> bool {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
         // Fold chunk `folded` once the stages after it are in flight: the
         // MMA of chunk folded+1 cannot start before it, and stage i needs
         // the MMA of stage i - STAGES, the first one of chunk folded+1.
         if (SPLIT3 && folded < nch - 1 && i == (folded + 1) * kChunk + STAGES) {
-          if (!fold(folded)) {
-            ok = false;
-            break;
-          }
+          if (!fold(folded)) return false;
           ++folded;
         }
-        // Issue the next stage's global loads before waiting on this one.
         if constexpr (!kATma) {
-          if (i + 1 < num_kb) a_gather<AK, KS>(a_nxt, p, a_rb, g_first, (kb_begin + i + 1) * KS, xw, lane);
+          if (i + 2 < num_kb) a_gather<AK, KS>(ahead, p, a_rb, g_first, (kb_begin + i + 2) * KS, xw, lane);
         }
         // Warp-uniform outcome: tcgen05.ld/st are .sync.aligned.
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) {
-          ok = false;
-          break;
-        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) return false;
         const int k0 = (kb_begin + i) * KS;
-        if constexpr (!kATma) {
-          a_store<AK, MD>(a_cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
-#pragma unroll
-          for (int j = 0; j < KS / 2; ++j) a_cur[j] = a_nxt[j];
-        }
-        if constexpr (!kBTma) b_build<BK, BN, MD>(p, b_hi(s), b_lo(s), k0, n0, t);
+        if constexpr (!kATma) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
+        if constexpr (!kBTma) b_build<BK, kBCols, MD>(p, b_hi(s), b_lo(s), k0, nb0, t);
         if constexpr (SPLIT3) {
           // lo = x - tf32(x) of the TMA-loaded tiles, elementwise at the same
           // (swizzled) offsets.
@@ -627,7 +685,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[s]);
+        if (lane == 0) arrive_issuer(&ready[s]);
+        return true;
+      };
+      for (int i = 0; i < num_kb && ok; i += 3) {
+        ok = stage(i, a_b0, a_b2);
+        if (ok && i + 1 < num_kb) ok = stage(i + 1, a_b1, a_b0);
+        if (ok && i + 2 < num_kb) ok = stage(i + 2, a_b2, a_b1);
       }
     }
     if constexpr (SPLIT3) {
@@ -697,11 +761,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   tc_fence_before_sync();
-  __syncthreads();
+  if constexpr (PAIR) {
+    // Neither CTA leaves while the leader's MMAs may still read the other's
+    // shared memory or the other may still arrive on the leader's barriers.
+    cluster_sync_all();
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after_sync();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    else
+      tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
