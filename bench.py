@@ -1,14 +1,15 @@
 """Benchmark of the structured matrix-multiply hot path: one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--op diag|gemm|upper|sandwich|toeplitz] [--mode 3xtf32|tf32|bf16]
+                    [--op diag|gemm|upper|sandwich|toeplitz|add] [--mode 3xtf32|tf32|bf16]
 
 Default workload (what the metric is quoted on at N = 8192, one GPU):
 diagonal x dense, C = diag(d) B with d (8192) ~ U[0.5,1.5] and B (8192 x 8192)
 ~ U[-1,1] (seeded, cpp1_b200.workloads), GB/s over the bytes the operation
 must move: 4N + 8N^2 per call.  The other ops are the remaining configured
 workloads (GEMM 8192^3, U B at 8192, A S B at 4096, T B at 16384), reported
-as useful TFLOP/s (structural zeros excluded).
+as useful TFLOP/s (structural zeros excluded); `add` (general + packed
+symmetric at 8192, the DSL's `+`) is reported in GB/s like the diagonal scale.
 
 Multi-GPU (torchrun, one process per GPU, NCCL):
   diag      weak scaling: every rank scales its own 8192 x 8192 row slab;
@@ -46,7 +47,17 @@ WORKLOADS = {
     "upper": dict(N=8192, unit="TFLOP/s", bound="tensor", desc="C = U B, U 8192 upper (packed), B 8192x8192"),
     "sandwich": dict(N=4096, unit="TFLOP/s", bound="tensor", desc="C = A S B, 4096, S packed symmetric"),
     "toeplitz": dict(N=16384, unit="TFLOP/s", bound="tensor", desc="C = T B, T from a 32767 generator, B 16384^2"),
+    "add": dict(N=8192, unit="GB/s", bound="hbm",
+                desc="C = A + S, A 8192x8192, S packed symmetric (the DSL's General + Symmetric)"),
 }
+HBM_OPS = ("diag", "add")
+
+
+def hbm_bytes(op: str, n: int) -> int:
+    """Bytes an HBM-bound call must move (read the inputs, write C)."""
+    if op == "diag":
+        return 4 * n + 8 * n * n
+    return 8 * n * n + 2 * n * (n + 1)  # A and C dense, S packed
 
 
 def parse_args():
@@ -62,9 +73,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = {"diag": 400, "gemm": 20, "upper": 30, "sandwich": 30, "toeplitz": 3}[a.op]
+        a.steps = {"diag": 400, "gemm": 20, "upper": 30, "sandwich": 30, "toeplitz": 3, "add": 300}[a.op]
     if a.warmup is None:
-        a.warmup = {"diag": 20, "gemm": 3, "upper": 3, "sandwich": 3, "toeplitz": 3}[a.op]
+        a.warmup = {"diag": 20, "gemm": 3, "upper": 3, "sandwich": 3, "toeplitz": 3, "add": 20}[a.op]
     return a
 
 
@@ -189,9 +200,20 @@ _REF_INPUTS = {}
 
 def cpu_reference_call(op: str, n: int, sample_n: int):
     """One call of the reference's own CPU kernel (oracle/_ref) on a seeded
-    problem of order sample_n; returns (kernel ms, units moved/computed)."""
+    problem of order sample_n; returns (kernel ms, units moved/computed).
+    The reference's `+` has no CPU kernel of its own on this path (its CUDA
+    backend generates it), so `add` times the oracle's C restatement."""
     import oracle as O
     from cpp1_b200 import workloads as W
+    if op == "add":
+        key = (op, sample_n)
+        if key not in _REF_INPUTS:
+            _REF_INPUTS.clear()
+            _REF_INPUTS[key] = W.make_add(sample_n, seed=0)
+        w = _REF_INPUTS[key]
+        t0 = time.perf_counter()
+        O.add_struct_f32(w["A"], w["S"], "symm")
+        return (time.perf_counter() - t0) * 1e3, hbm_bytes(op, sample_n)
     if not O.ref_available():
         raise RuntimeError("oracle/_ref not built")
     key = (op, sample_n)
@@ -221,7 +243,8 @@ def cpu_reference_call(op: str, n: int, sample_n: int):
     raise ValueError(op)
 
 
-CPU_SAMPLE_N = {"diag": 8192, "gemm": 2048, "upper": 2048, "sandwich": 1024, "toeplitz": 2048}
+CPU_SAMPLE_N = {"diag": 8192, "gemm": 2048, "upper": 2048, "sandwich": 1024, "toeplitz": 2048, "add": 4096}
+CPU_KIND = {"add": "port"}  # every other op runs the reference's own kernel
 
 
 def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
@@ -235,7 +258,12 @@ def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
         if len(rates) >= 50:
             break
     rate = statistics.median(rates)
-    scale = 1e9 if op == "diag" else 1e12
+    scale = 1e9 if op in HBM_OPS else 1e12
+    kind = CPU_KIND.get(op, "reference")
+    if kind == "port":
+        return {"value": rate / scale, "unit": WORKLOADS[op]["unit"], "cores": 1, "kind": "port",
+                "sample": f"{op} at order {sn} ({len(rates)} calls, median; the oracle's scalar C restatement, "
+                          "one thread)"}
     return {"value": rate / scale, "unit": WORKLOADS[op]["unit"], "cores": cores, "kind": "reference",
             "sample": f"{op} at order {sn} ({len(rates)} calls, median; the reference's AVX2+OpenMP kernel, "
                       f"its own chrono window, OMP threads = {cores})"}
@@ -268,16 +296,19 @@ def run_ours(args, rank, world, local):
     elif op == "sandwich":
         w = W.make_sandwich(n, seed=0)
         h_in = [w["A"], w["S"], w["B"]]
-    else:
+    elif op == "toeplitz":
         w = W.make_toeplitz(n, seed=0)
         h_in = [w["g"], w["B"]]
+    else:
+        w = W.make_add(n, seed=rank)
+        h_in = [w["A"], w["S"]]
     d_in = [torch.from_numpy(x).cuda() for x in h_in]
 
     from cpp1_b200.multigpu import row_slabs, slab_useful_flops
-    bounds = row_slabs(n, world, triangular=(op == "upper")) if op != "diag" else None
+    bounds = row_slabs(n, world, triangular=(op == "upper")) if op not in HBM_OPS else None
     r0, r1 = (bounds[rank], bounds[rank + 1]) if bounds else (0, n)
     nrows = r1 - r0
-    out = torch.empty((nrows if op != "diag" else n, n), dtype=torch.float32, device="cuda")
+    out = torch.empty((nrows, n), dtype=torch.float32, device="cuda")
     m = _lib.MODES[mode]
 
     def ws_for(nbytes):
@@ -290,7 +321,14 @@ def run_ours(args, rank, world, local):
 
         def step():
             _lib.check(L.smm_diag_rows(d.data_ptr(), B.data_ptr(), out.data_ptr(), n, n, sp), "diag")
-        units_per_rank_call = 4 * n + 8 * n * n
+        units_per_rank_call = hbm_bytes(op, n)
+    elif op == "add":
+        A, S = d_in
+
+        def step():
+            _lib.check(L.smm_add_struct(A.data_ptr(), S.data_ptr(), _lib.STRUCTS["symm"], out.data_ptr(), n, sp),
+                       "add")
+        units_per_rank_call = hbm_bytes(op, n)
     elif op == "gemm":
         A, B = d_in
         ws, wsb = ws_for(L.smm_gemm_workspace_size(nrows, n, n, m))
@@ -360,9 +398,9 @@ def run_ours(args, rank, world, local):
     ms = max_over_ranks(ms_local, world)
     ms_per_step = ms / args.steps
 
-    total_units = units_per_rank_call * world if op == "diag" else (
+    total_units = units_per_rank_call * world if op in HBM_OPS else (
         n * n * (n + 1) if op == "upper" else (4 * n ** 3 if op == "sandwich" else 2 * n ** 3))
-    scale = 1e9 if op == "diag" else 1e12
+    scale = 1e9 if op in HBM_OPS else 1e12
     value = total_units / (ms_per_step * 1e-3) / scale
 
     # ---- roofline of the dominant kernel, timed on its own on this rank
@@ -371,11 +409,11 @@ def run_ours(args, rank, world, local):
     res = {
         "metric": METRIC, "value": round(value, 3), "unit": WORKLOADS[op]["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak" if op == "diag" else "strong", "vs_baseline": None,
-        "dtype": "f32" if op == "diag" else {"3xtf32": "f32 (3xTF32 tensor cores)", "tf32": "tf32",
-                                            "bf16": "bf16 (fp32 accumulate)"}[mode],
+        "higher_is_better": True, "scaling": "weak" if op in HBM_OPS else "strong", "vs_baseline": None,
+        "dtype": "f32" if op in HBM_OPS else {"3xtf32": "f32 (3xTF32 tensor cores)", "tf32": "tf32",
+                                             "bf16": "bf16 (fp32 accumulate)"}[mode],
         "data": "synthetic (seeded numpy PCG64, cpp1_b200.workloads)",
-        "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "mode": mode if op != "diag" else "f32",
+        "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "mode": mode if op not in HBM_OPS else "f32",
                    "parallelism": f"row-slabs x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (126 MB): no flush needed"},
         "roofline": roof,
@@ -387,7 +425,7 @@ def run_ours(args, rank, world, local):
 
 def roofline(op, n, nrows, mode, step, stream, peaks, units_rank, world):
     import torch
-    reps = 50 if op == "diag" else 3
+    reps = 50 if op in HBM_OPS else 3
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         return {"bound": WORKLOADS[op]["bound"], "note": "reported at n_gpus = 1"}
@@ -398,8 +436,8 @@ def roofline(op, n, nrows, mode, step, stream, peaks, units_rank, world):
     ev1.record(stream)
     torch.cuda.synchronize()
     launch_ms = ev0.elapsed_time(ev1) / reps / (2 if op == "sandwich" else 1)
-    if op == "diag":
-        bytes_launch = 4 * n + 8 * n * n
+    if op in HBM_OPS:
+        bytes_launch = hbm_bytes(op, n)
         achieved = bytes_launch / (launch_ms * 1e-3) / 1e9
         peak = peaks["hbm_gbs"]
         traffic = profile_traffic(op)
@@ -442,6 +480,18 @@ def e2e_ours(args, h_in, n):
         d2h = 4 * n * n
         units = 4 * n + 8 * n * n
         steps = max(5, min(args.steps // 20, 30))
+    elif op == "add":
+        hp = [torch.from_numpy(x).pin_memory() for x in h_in]
+        C = torch.empty((n, n), dtype=torch.float32).pin_memory()
+
+        def step():
+            A, S = [x.cuda(non_blocking=True) for x in hp]
+            C.copy_(ops.add_struct(A, S, "symm"), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        h2d = sum(x.nbytes for x in h_in)
+        d2h = C.numel() * 4
+        units = hbm_bytes(op, n)
+        steps = 10
     else:
         hp = [torch.from_numpy(x).pin_memory() for x in h_in]
         Cn = n
@@ -466,7 +516,7 @@ def e2e_ours(args, h_in, n):
         step()
     torch.cuda.synchronize()
     dt = (time.perf_counter() - t0) / steps
-    scale = 1e9 if op == "diag" else 1e12
+    scale = 1e9 if op in HBM_OPS else 1e12
     return {"value": round(units / dt / scale, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(dt * 1e3, 3),
             "api": "C ABI with pinned host buffers" + (" (smm_diag_rows_host)" if op == "diag" else " via cpp1_b200.ops")}
@@ -498,7 +548,8 @@ def run_reference(args, rank, world):
     n = args.n or WORKLOADS[op]["N"]
     use_all_host_threads()
     import oracle as O
-    if not O.ref_available():
+    kind = CPU_KIND.get(op, "reference")
+    if kind == "reference" and not O.ref_available():
         return {"impl": "reference", "unavailable": "oracle/_ref (the reference CPU kernels) was not built"}
     sn = min(n, CPU_SAMPLE_N[op])
     for _ in range(max(0, min(args.warmup, 2))):
@@ -508,19 +559,21 @@ def run_reference(args, rank, world):
         ms, units = cpu_reference_call(op, n, sn)
         times.append(ms)
     ms = statistics.median(times)
-    scale = 1e9 if op == "diag" else 1e12
+    scale = 1e9 if op in HBM_OPS else 1e12
     value = units / (ms * 1e-3) / scale
-    cores = int(os.environ.get("OMP_NUM_THREADS", host_threads()))
+    cores = 1 if kind == "port" else int(os.environ.get("OMP_NUM_THREADS", host_threads()))
+    how = ("the oracle's scalar C restatement (the reference's `+` is generated CUDA only), one thread"
+           if kind == "port" else "the reference's AVX2+OpenMP kernel, its own chrono window")
     sample = f"{op} at order {sn}" + ("" if sn == n else f" (bounded sample of the order-{n} workload)")
     return {
         "metric": METRIC, "value": round(value, 3), "unit": WORKLOADS[op]["unit"], "n_gpus": world,
         "steps": len(times), "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "weak" if op == "diag" else "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak" if op in HBM_OPS else "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded numpy PCG64, cpp1_b200.workloads)",
         "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "sample_N": sn},
         "impl": "reference",
-        "cpu_baseline": {"value": round(value, 3), "unit": WORKLOADS[op]["unit"], "cores": cores, "kind": "reference",
-                         "sample": sample + "; the reference's AVX2+OpenMP kernel, its own chrono window"},
+        "cpu_baseline": {"value": round(value, 3), "unit": WORKLOADS[op]["unit"], "cores": cores, "kind": kind,
+                         "sample": sample + "; " + how},
         "e2e": {"value": round(value, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -547,7 +600,7 @@ def main():
         # scaling, or the single-GPU rate otherwise.
         del d_in
         e2e = e2e_ours(args, h_in, n)
-        if world > 1 and args.op == "diag":
+        if world > 1 and args.op in HBM_OPS:
             e2e["value"] = round(max_over_ranks(-e2e["value"], world) * -1 * world, 3)
         res["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

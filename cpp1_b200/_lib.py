@@ -33,6 +33,7 @@ STATUS_NAMES = {
 MODES = {"3xtf32": 0, "tf32": 1, "bf16": 2}
 FMT_PACKED = 0
 FMT_DENSE = 1
+STRUCTS = {"upper": 0, "lower": 1, "symm": 2, "diag": 3, "toeplitz": 4}
 
 
 class SmmError(RuntimeError):
@@ -45,6 +46,7 @@ _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _sz = ctypes.c_size_t
 _ull = ctypes.c_ulonglong
+_ll = ctypes.c_longlong
 
 # (name, restype, argtypes) for every entry point of include/smm.h.
 SIGNATURES = [
@@ -74,6 +76,11 @@ SIGNATURES = [
     ("smm_gen_x_symm", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_symm_x_symm", _i, [_vp, _vp, _vp, _i, _i, _vp]),
     ("smm_symm_sandwich_noalloc", _i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
+    ("smm_add", _i, [_vp, _vp, _vp, _ll, _vp]),
+    ("smm_add_struct", _i, [_vp, _vp, _i, _vp, _i, _vp]),
+    ("smm_unpack", _i, [_vp, _i, _vp, _i, _vp]),
+    ("smm_pack", _i, [_vp, _i, _vp, _i, _vp]),
+    ("smm_toeplitz_compact", _i, [_vp, _vp, _i, _i, _vp]),
     ("smm_debug_timeout_probe", _i, [_ull, _vp]),
     ("smm_debug_trace_next", _i, [_vp]),
 ]

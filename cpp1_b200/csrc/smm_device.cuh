@@ -107,6 +107,21 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// ---------------------------------------------------------------- cp.async
+// 4-byte asynchronous copy global -> shared; src_bytes = 0 writes a zero
+// without reading global memory (the source address is then unused).
+__device__ __forceinline__ void cp_async_4(uint32_t smem_dst, const float* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+// The arrival is not pre-counted (.noinc): the barrier's expected count
+// includes it.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---------------------------------------------------------------- tcgen05
 // Tensor-memory allocation by one full warp; the TMEM base address is written
 // to *dst (shared memory).

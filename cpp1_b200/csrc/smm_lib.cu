@@ -124,7 +124,7 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
   if constexpr (PAIR) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(umma_threads(AK, MD), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -136,7 +136,7 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
     cfg.numAttrs = 1;
     SMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.al, m.bl, p), "tcgen05 pair contraction launch");
   } else {
-    kern<<<static_cast<unsigned>(blocks), kThreads, smem, st>>>(m.a, m.b, m.al, m.bl, p);
+    kern<<<static_cast<unsigned>(blocks), umma_threads(AK, MD), smem, st>>>(m.a, m.b, m.al, m.bl, p);
   }
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "tcgen05 contraction launch");

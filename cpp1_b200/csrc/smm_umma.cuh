@@ -34,12 +34,16 @@
 // sum kept in a second TMEM region with round-to-nearest fp32 adds while the
 // next chunk runs.  Error stays ~1e-6 normwise whatever K is.
 //
-// Warp roles (320 threads):
+// Warp roles (384 threads):
 //   warp 0      TMA producer (one lane)
 //   warp 1      TMEM allocator + MMA issuer (one lane)
 //   warps 2-9   transform (lo tiles, structured operand tiles), chunk folds, epilogue
 //               (TMEM -> registers -> global C); warp w owns TMEM lanes
 //               32*(w%4).. and column half (w-2)/4 of the tile
+//   warps 10-11 structured-A fill (fp32 modes): 4-byte cp.async copies from
+//               packed / generator storage straight into the swizzled A tile,
+//               zero-filled outside the structure, completing on the stage's
+//               `full` barrier (so the transform warps only derive lo tiles)
 //
 // Every wait is bounded (WaitCtx): on expiry the kernel records which role
 // gave up in the status word, the other roles stop waiting, in-flight
@@ -80,6 +84,15 @@ struct ModeTraits {
   static constexpr uint32_t kFmt = kBf16 ? kFmtBF16 : kFmtTF32;
 };
 
+// Structured A in fp32 modes is filled by cp.async warps (raw fp32, like a
+// TMA tile); in bf16 mode the transform warps gather and convert it.
+__host__ __device__ constexpr bool a_async_filled(AKind ak, Mode md) {
+  return ak != AKind::Dense && ak != AKind::UpperDense && md != Mode::BF16;
+}
+// Threads per CTA: producer, MMA and 8 transform warps, plus the 2 fill warps
+// when the kernel has them.
+__host__ __device__ constexpr int umma_threads(AKind ak, Mode md) { return a_async_filled(ak, md) ? 384 : 320; }
+
 struct UmmaParams {
   int M, N, K;             // C is M x N; reduction length K
   float* C;                // row-major, leading dimension ldc
@@ -106,8 +119,8 @@ enum : int { kTrTmem = 0, kTrNumKb = 1, kTrAccOk = 2, kTrMmas = 3, kTrAcc = 4 /*
 
 constexpr int kBM = 128;
 constexpr int kBK = 16;                     // fp32 elements per k-block (64 bytes)
-constexpr int kThreads = 320;
 constexpr int kXformThreads = 256;          // warps 2-9
+constexpr int kAFillThreads = 64;           // warps 10-11 (structured A, fp32 modes)
 constexpr int kATileBytes = kBM * kBK * 4;  // 8 KiB
 // 3xTF32 chunk length in k-blocks: 3 * 12 * 2 = 72 truncating updates per
 // chunk accumulator (measured bias ~5e-8 of |C| per update on same-sign data).
@@ -288,6 +301,72 @@ __device__ __forceinline__ void a_store(const float (&v)[ModeTraits<MD>::kStageK
   }
 }
 
+// Fill this CTA's A stage tile (128 rows x 16 fp32, rows g_first.., columns
+// k0..k0+15, 64-byte swizzle) from structured storage with 4-byte cp.async
+// copies; fill thread `ft` of kAFillThreads issues 32.  Lanes run along k
+// (16 lanes per row, two rows per warp instruction: coalesced along a packed
+// row or a generator window), except for symmetric tiles wholly below the
+// diagonal, whose elements are mirrors S[k][row]: there 32 lanes run along
+// rows (coalesced along packed row k).  Elements outside the matrix or
+// below an upper-triangular diagonal are written as zeros without a read.
+template <AKind AK>
+__device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, int g_first, int k0, int ft) {
+  constexpr int KS = 16;
+  const int n = p.a_dim;
+  const float* __restrict__ src = p.a_src;
+  const uint32_t dst0 = smem_u32(ah);
+  const int fw = ft >> 5, lane = ft & 31;
+  if (a_rows_mapping<AK, KS>(g_first, k0)) {
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int kl = fw * 8 + kk;
+      const int k = k0 + kl;
+      const uint32_t kb = packed_row_base(k, n);  // S[k][gr] = src[kb + gr]
+#pragma unroll
+      for (int rg = 0; rg < 4; ++rg) {
+        const int r = rg * 32 + lane;
+        const int gr = g_first + r;
+        const bool in = gr < n && k < n;
+        cp_async_4(dst0 + swz_offset(r, kl >> 2, 64) + (kl & 3) * 4, in ? src + (kb + static_cast<uint32_t>(gr)) : src,
+                   in ? 4u : 0u);
+      }
+    }
+    return;
+  }
+  const int kl = lane & 15;
+  const int k = k0 + kl;
+  uint32_t mbase = 0;  // symmetric, below-diagonal elements: packed row k
+  if constexpr (AK == AKind::SymmPacked) mbase = packed_row_base(k, n);
+  int r = fw * 64 + (lane >> 4);
+  int gr = g_first + r;
+  // offset of element (gr, 0): packed row start minus gr, or n - 1 - gr
+  uint32_t rb = (AK == AKind::Toeplitz) ? static_cast<uint32_t>(n - 1 - gr) : packed_row_base(gr, n);
+#pragma unroll 8
+  for (int it = 0; it < 32; ++it) {
+    const bool in = gr < n && k < n;
+    bool valid;
+    uint32_t so;
+    if constexpr (AK == AKind::UpperPacked) {
+      valid = in && k >= gr;
+      so = rb + static_cast<uint32_t>(k);
+    } else if constexpr (AK == AKind::Toeplitz) {
+      valid = in;
+      so = rb + static_cast<uint32_t>(k);
+    } else {
+      valid = in;
+      so = k >= gr ? rb + static_cast<uint32_t>(k) : mbase + static_cast<uint32_t>(gr);
+    }
+    cp_async_4(dst0 + swz_offset(r, kl >> 2, 64) + (kl & 3) * 4, valid ? src + so : src, valid ? 4u : 0u);
+    // next row of this lane: two rows down
+    if constexpr (AK == AKind::Toeplitz)
+      rb -= 2u;
+    else
+      rb += static_cast<uint32_t>(2 * n - 2 * gr - 3);  // packed row base(gr + 2) - base(gr)
+    r += 2;
+    gr += 2;
+  }
+}
+
 // ---------------------------------------------------------------- structured B
 // Element e (0 .. BN/16-1) of transform thread t in a B stage tile.  Lanes
 // run along n (coalesced along packed row k); for symmetric tiles wholly
@@ -367,7 +446,7 @@ __device__ __forceinline__ void b_build(const UmmaParams& p, uint8_t* bh, uint8_
 // the fold warps of both CTAs arrive on the leader's `acc_empty`.  No load is
 // multicast.
 template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR = false>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
                      const UmmaParams p) {
@@ -379,15 +458,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kStage = stage_bytes<kBCols, SPLIT3>();
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
   constexpr bool kBTma = (BK == BKind::Dense);
+  constexpr bool kACp = a_async_filled(AK, MD);
   // The transform warps touch every stage when a tile is built on chip or
-  // when lo tiles are derived from the TMA-loaded ones (3xTF32); in a pair
-  // they also relay TMA completion to the leader.
+  // when lo tiles are derived from the loaded ones (3xTF32); in a pair they
+  // also relay stage completion to the leader.
   constexpr bool kXform = !kATma || !kBTma || SPLIT3 || PAIR;
   constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0);
   constexpr uint32_t kTmemCols = tmem_cols<BN, SPLIT3>();
   constexpr uint32_t kIdesc = make_idesc(MT::kFmt, PAIR ? 2 * kBM : kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
   constexpr int kHalf = BN / 2;  // columns per epilogue warp
   constexpr uint32_t kArrivals = (PAIR ? 2 : 1) * (kXformThreads / 32);  // warps arriving on ready / acc_empty
+  constexpr int kFoldLag = STAGES / 2;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -445,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 1 + (kACp ? kAFillThreads : 0));  // TMA producer (+ fill threads)
       mbar_init(&ready[s], kArrivals);  // one arrival per transform warp (of both CTAs)
       mbar_init(&empty[s], 1);
     }
@@ -590,6 +671,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const WaitCtx drain{&no_abort, p.status, p.wait_limit_ns, kWaitDrain};
       mbar_wait(accum_full, 0, drain);
     }
+  } else if (warp >= 2 + kXformThreads / 32) {
+    // ------------------------------------------------------------ structured-A fill
+    if constexpr (kACp) {
+      const int ft = threadIdx.x - (64 + kXformThreads);  // 0..kAFillThreads-1
+      const int g_first = p.a_row0 + m0;
+      for (int i = 0; i < num_kb; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
+        a_async_fill<AK>(p, a_hi(s), g_first, (kb_begin + i) * KS, ft);
+        cp_async_mbar_arrive_noinc(&full[s]);
+      }
+      // no copy may land after the CTA has exited (bounded: all in flight)
+      cp_async_wait_all();
+    }
   } else {
     // ------------------------------------------------------------ transform + epilogue
     const int t = threadIdx.x - 64;  // 0..255
@@ -645,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // so a gather has two stage times to return from L2.
       float a_b0[KS / 2], a_b1[KS / 2], a_b2[KS / 2];
       uint32_t a_rb[KS / 2];
-      if constexpr (!kATma) {
+      if constexpr (!kATma && !kACp) {
         a_row_bases<AK, KS>(a_rb, p, g_first, xw, lane);
         if (num_kb > 0) a_gather<AK, KS>(a_b0, p, a_rb, g_first, kb_begin * KS, xw, lane);
         if (num_kb > 1) a_gather<AK, KS>(a_b1, p, a_rb, g_first, (kb_begin + 1) * KS, xw, lane);
@@ -653,20 +749,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto stage = [&](int i, const float (&cur)[KS / 2], float (&ahead)[KS / 2]) -> bool {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
-        // Fold chunk `folded` once the stages after it are in flight: the
-        // MMA of chunk folded+1 cannot start before it, and stage i needs
-        // the MMA of stage i - STAGES, the first one of chunk folded+1.
-        if (SPLIT3 && folded < nch - 1 && i == (folded + 1) * kChunk + STAGES) {
+        // Fold chunk `folded` once the first kFoldLag stages of the next
+        // chunk are ready, so the MMA resumes on them as soon as the
+        // accumulator is released.  Any lag in [0, STAGES] is deadlock-free
+        // (the fold needs only the MMAs of chunk `folded`, whose stages are
+        // all ready by now); a lag of STAGES would make the fold wait for a
+        // TMA round trip started by the chunk's very last MMA.
+        if (SPLIT3 && folded < nch - 1 && i == (folded + 1) * kChunk + kFoldLag) {
           if (!fold(folded)) return false;
           ++folded;
         }
-        if constexpr (!kATma) {
+        if constexpr (!kATma && !kACp) {
           if (i + 2 < num_kb) a_gather<AK, KS>(ahead, p, a_rb, g_first, (kb_begin + i + 2) * KS, xw, lane);
         }
         // Warp-uniform outcome: tcgen05.ld/st are .sync.aligned.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) return false;
         const int k0 = (kb_begin + i) * KS;
-        if constexpr (!kATma) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
+        if constexpr (!kATma && !kACp) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
         if constexpr (!kBTma) b_build<BK, kBCols, MD>(p, b_hi(s), b_lo(s), k0, nb0, t);
         if constexpr (SPLIT3) {
           // lo = x - tf32(x) of the TMA-loaded tiles, elementwise at the same
@@ -680,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               out[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
             }
           };
-          if constexpr (kATma) lo_of(a_hi(s), a_lo(s), kATileBytes, t);
+          if constexpr (kATma || kACp) lo_of(a_hi(s), a_lo(s), kATileBytes, t);
           if constexpr (kBTma) lo_of(b_hi(s), b_lo(s), kBTile, t);
         }
         fence_proxy_async_smem();

@@ -25,7 +25,9 @@ Conventions kept from the reference:
   (M*N for a diagonal scale), as the reference wrappers report.
 
 A graph of the form A @ S @ B (S symmetric) is executed by the sandwich
-entry point in one call instead of two.
+entry point in one call instead of two.  `+` of two operands lowers to
+smm_add (same class, over the storage) or smm_add_struct (general plus a
+structured operand, expanded on the fly).
 """
 from __future__ import annotations
 
@@ -138,9 +140,11 @@ def run(outs, inputs, backend="cuda", out_matrix_obj=None, bm=None, bn=None, bk=
         raise ValueError(f"runner_cuda only supports backend='cuda', got {backend!r}")
     node = outs[0]
     target = out_matrix_obj if out_matrix_obj is not None else node
+    if isinstance(node, Operation) and node.operator == "add":
+        return _run_add(node, target, inputs)
     if not isinstance(node, Operation) or node.operator != "matmul":
         op_name = getattr(node, "operator", type(node).__name__)
-        raise NotImplementedError(f"CUDA backend supports matmul expressions, got {op_name!r}")
+        raise NotImplementedError(f"CUDA backend supports matmul and add expressions, got {op_name!r}")
     lhs, rhs = node.operands
     M, K = get_shape(lhs.shape, inputs)
     K2, N = get_shape(rhs.shape, inputs)
@@ -158,6 +162,54 @@ def run(outs, inputs, backend="cuda", out_matrix_obj=None, bm=None, bn=None, bk=
         raise NotImplementedError(f"output class {type(target).__name__} of a matmul must be general (M x N)")
     _, ms = _timed(lambda: call(a, b, M, N, K, mode, out.view(M, N)))
     gflops = flops(M, N, K) * 1e-9 / (ms * 1e-3) if ms > 0 else 0.0
+    return {target.name: out}, ms, gflops
+
+
+_STRUCT_FMT = {"upper": "upper", "lower": "lower", "symm": "symm", "diag": "diag", "toeplitz": "toeplitz"}
+
+
+def _run_add(node, target, inputs):
+    """The DSL's `+` (src/dsl/codegen_cuda.py:1643-1827).  Operands of the
+    same class are added over their storage (kernel_add_1d_vec4's role); a
+    general operand plus a structured one gives a general result with the
+    structured operand expanded on the fly (kernel_add_gen_symm's role, here
+    for every structured class and either operand order).  gflops counts one
+    operation per stored output element, as the reference wrappers do."""
+    lhs, rhs = node.operands
+    shape = get_shape(lhs.shape, inputs)
+    if get_shape(rhs.shape, inputs) != shape:
+        raise ValueError(f"Shapes must match for add operation: {lhs.shape} vs {rhs.shape}")
+    for m in (lhs, rhs):
+        if m.name not in inputs:
+            raise KeyError(f"input {m.name!r} missing")
+    a = _device_tensor(inputs[lhs.name])
+    b = _device_tensor(inputs[rhs.name])
+    lk, rk = _kind(lhs), _kind(rhs)
+    out_shape = get_shape(target.shape, inputs)
+    out_size = _storage_size(target, out_shape)
+    out = torch.zeros(out_size, dtype=torch.float32, device=a.device)
+    if lk == rk:
+        size = _storage_size(lhs, shape)
+        if out_size != size:
+            raise NotImplementedError(f"add of two {lk} operands into a {type(target).__name__} output")
+        if a.numel() < size or b.numel() < size:
+            raise ValueError(f"add operands hold {a.numel()} and {b.numel()} elements, need {size}")
+        _, ms = _timed(lambda: ops.add(a[:size], b[:size], out=out))
+        work = size
+    elif (lk == "gen") != (rk == "gen") and (lk in _STRUCT_FMT or rk in _STRUCT_FMT):
+        n = shape[0]
+        if shape[1] != n:
+            raise ValueError("a structured operand must be square")
+        if out_size != n * n:
+            raise NotImplementedError(f"general + {lk if lk != 'gen' else rk} gives a general output")
+        gen, st, st_obj = (a, b, rhs) if lk == "gen" else (b, a, lhs)
+        fmt = _STRUCT_FMT[_kind(st_obj)]
+        st_size = _storage_size(st_obj, shape)
+        _, ms = _timed(lambda: ops.add_struct(gen[:n * n].view(n, n), st[:st_size], fmt, out=out.view(n, n)))
+        work = n * n
+    else:
+        raise NotImplementedError(f"Addition for {lk} + {rk} is not implemented in the CUDA backend")
+    gflops = work * 1e-9 / (ms * 1e-3) if ms > 0 else 0.0
     return {target.name: out}, ms, gflops
 
 

@@ -216,6 +216,77 @@ def symm_x_symm(S1: torch.Tensor, S2: torch.Tensor, mode: str = "3xtf32", out: O
     return C
 
 
+# ---------------------------------------------------------------- elementwise / converters
+def _struct(fmt: str) -> int:
+    try:
+        return _lib.STRUCTS[fmt]
+    except KeyError:
+        raise ValueError(f"unknown structure {fmt!r}; expected one of {sorted(_lib.STRUCTS)}") from None
+
+
+def struct_numel(fmt: str, N: int) -> int:
+    """Storage size of an order-N structured matrix."""
+    _struct(fmt)
+    return {"upper": N * (N + 1) // 2, "lower": N * (N + 1) // 2, "symm": N * (N + 1) // 2, "diag": N,
+            "toeplitz": max(2 * N - 1, 0)}[fmt]
+
+
+def add(A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """C = A + B elementwise over the storage of two operands of the same
+    structure (flat, any shape with equal element counts)."""
+    A = _check_f32("A", A)
+    B = _check_f32("B", B, A.numel())
+    C = _out(out, tuple(A.shape), A)
+    _lib.check(_lib.load().smm_add(_ptr(A), _ptr(B), _ptr(C), A.numel(), _stream_ptr(stream)), "smm_add")
+    return C
+
+
+def add_struct(A: torch.Tensor, S: torch.Tensor, fmt: str, out: Optional[torch.Tensor] = None,
+               stream=None) -> torch.Tensor:
+    """C = A + S with A dense N x N and S structured (fmt: upper, lower, symm,
+    diag, toeplitz) in its packed storage."""
+    A = _check_f32("A", A)
+    N = int(round(A.numel() ** 0.5))
+    if N * N != A.numel():
+        raise ValueError(f"A has {A.numel()} elements, not a square matrix")
+    S = _check_f32("S", S, struct_numel(fmt, N))
+    C = _out(out, (N, N), A)
+    _lib.check(_lib.load().smm_add_struct(_ptr(A), _ptr(S), _struct(fmt), _ptr(C), N, _stream_ptr(stream)),
+               "smm_add_struct")
+    return C
+
+
+def unpack(S: torch.Tensor, fmt: str, N: int, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Dense N x N matrix of the structured storage S."""
+    S = _check_f32("S", S, struct_numel(fmt, N))
+    D = _out(out, (N, N), S)
+    _lib.check(_lib.load().smm_unpack(_ptr(S), _struct(fmt), _ptr(D), N, _stream_ptr(stream)), "smm_unpack")
+    return D
+
+
+def pack(D: torch.Tensor, fmt: str, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Packed upper (fmt upper or symm) or lower triangle of the dense square D."""
+    D = _check_f32("D", D)
+    N = int(round(D.numel() ** 0.5))
+    if N * N != D.numel():
+        raise ValueError(f"D has {D.numel()} elements, not a square matrix")
+    P = _out(out, (N * (N + 1) // 2,), D)
+    _lib.check(_lib.load().smm_pack(_ptr(D), _struct(fmt), _ptr(P), N, _stream_ptr(stream)), "smm_pack")
+    return P
+
+
+def toeplitz_compact(T: torch.Tensor, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Generator (rows + cols - 1) of the Toeplitz matrix T (2-D)."""
+    if T.dim() != 2:
+        raise ValueError("T must be 2-D")
+    T = _check_f32("T", T)
+    rows, cols = T.shape
+    g = _out(out, (max(rows + cols - 1, 0),), T)
+    _lib.check(_lib.load().smm_toeplitz_compact(_ptr(T), _ptr(g), rows, cols, _stream_ptr(stream)),
+               "smm_toeplitz_compact")
+    return g
+
+
 def device_status(stream=None) -> None:
     """Raise SmmError(SMM_ERR_DEVICE_TIMEOUT) if a kernel gave up a bounded wait."""
     _lib.check(_lib.load().smm_device_status(_stream_ptr(stream)), "smm_device_status")

@@ -101,3 +101,12 @@ def make_toeplitz(N: int, ncols: int = None, seed: int = 0) -> Dict[str, np.ndar
     g = _uniform(rng, (2 * N - 1,), -1.0, 1.0)
     B = _uniform(rng, (N, ncols), -1.0, 1.0)
     return {"g": g, "B": B}
+
+
+def make_add(N: int, seed: int = 0) -> Dict[str, np.ndarray]:
+    """General + symmetric (the DSL's GeneralMatrix + SymmetricMatrix): A
+    (N x N) then the packed upper triangle of S, both ~ U[-1, 1]."""
+    rng = np.random.default_rng(seed)
+    A = _uniform(rng, (N, N), -1.0, 1.0)
+    S = _uniform(rng, (packed_size(N),), -1.0, 1.0)
+    return {"A": A, "S": S}

@@ -48,6 +48,18 @@ typedef enum {
 
 typedef enum { SMM_MODE_3XTF32 = 0, SMM_MODE_TF32 = 1, SMM_MODE_BF16 = 2 } smm_mode;
 typedef enum { SMM_FMT_PACKED = 0, SMM_FMT_DENSE = 1 } smm_format;
+/* Structured storage formats of the elementwise and converter entry points:
+ * packed upper, packed lower (row-major lower triangle incl. diagonal,
+ * idx(i,j) = i*(i+1)/2 + j for j <= i, layout_functions.py:25-36), packed
+ * symmetric (upper storage, mirrored), diagonal (N floats), Toeplitz (2N-1
+ * generator). */
+typedef enum {
+  SMM_STRUCT_UPPER = 0,
+  SMM_STRUCT_LOWER = 1,
+  SMM_STRUCT_SYMM = 2,
+  SMM_STRUCT_DIAG = 3,
+  SMM_STRUCT_TOEPLITZ = 4
+} smm_struct;
 
 /* ---- library ---------------------------------------------------------- */
 
@@ -180,6 +192,39 @@ int smm_gen_x_symm(const float* A, const float* S_packed, float* C, int M, int N
 /* C(N x N) = S1 S2, both packed upper symmetric.  Replaces kernel_symm_x_symm
  * (src/dsl/codegen_cuda.py:1340-1613).  No workspace. */
 int smm_symm_x_symm(const float* S1_packed, const float* S2_packed, float* C, int N, int mode, void* stream);
+
+/* ---- elementwise sums and storage converters (HBM-bound, bit-exact) ---- */
+
+/* C[k] = A[k] + B[k] for k < count: the DSL's `+` of two operands in the same
+ * storage (general + general over M*N floats, symmetric/upper/lower + the
+ * same class over N(N+1)/2, diagonal + diagonal over N).  One IEEE fp32 add
+ * per element.  Replaces kernel_add_1d_vec4 + wrapper
+ * (src/dsl/codegen_cuda.py:1718-1812). */
+int smm_add(const float* A, const float* B, float* C, long long count, void* stream);
+
+/* C = A + S, A and C dense N x N, S in structured storage s_fmt (an
+ * smm_struct) expanded on the fly: C[i][j] = A[i][j] + S(i,j).  For
+ * SMM_STRUCT_SYMM this replaces kernel_add_gen_symm + wrapper
+ * (src/dsl/codegen_cuda.py:1650-1716), the DSL's GeneralMatrix +
+ * SymmetricMatrix. */
+int smm_add_struct(const float* A, const float* S, int s_fmt, float* C, int N, void* stream);
+
+/* D (dense N x N) = the structured matrix S (s_fmt): zeros outside the
+ * triangle / diagonal, the mirror for SMM_STRUCT_SYMM, T[i][j] =
+ * g[N-1+j-i] for SMM_STRUCT_TOEPLITZ (layout_functions.py:8-75). */
+int smm_unpack(const float* S, int s_fmt, float* D, int N, void* stream);
+
+/* P (packed, N(N+1)/2 floats) = the upper (SMM_STRUCT_UPPER or _SYMM) or
+ * lower (SMM_STRUCT_LOWER) triangle of the dense N x N matrix D, in the DSL's
+ * packed order (layout_functions.py:8-36; the torch.triu_indices order of
+ * main2.py:44-45 and runner_cuda.py:96-97).  N <= 65535. */
+int smm_pack(const float* D, int s_fmt, float* P, int N, void* stream);
+
+/* g (rows + cols - 1 floats) = the generator of the rows x cols Toeplitz
+ * matrix T: g[rows-1-i] = T[i][0], g[rows-1+j] = T[0][j].  Replaces
+ * build_toeplitz_compact (Cuda kernels/toeplitz.cu:254-261,
+ * toeplitz_matmul2.cpp:34-41). */
+int smm_toeplitz_compact(const float* T, float* g, int rows, int cols, void* stream);
 
 /* ---- failure-detection probe ------------------------------------------- */
 

@@ -62,6 +62,11 @@ def lib() -> ctypes.CDLL:
         L.orc_upper_left_rows_f32.argtypes = [_F32P, _F32P, _I32P, _c_int, _F32P, _c_int, _c_int]
         L.orc_toeplitz_left_rows_f32.argtypes = [_F32P, _F32P, _I32P, _c_int, _F32P, _c_int, _c_int]
         L.orc_sandwich_rows_f32.argtypes = [_F32P, _F32P, _F32P, _I32P, _c_int, _F32P, _c_int]
+        L.orc_add_f32.argtypes = [_F32P, _F32P, _F32P, ctypes.c_long]
+        L.orc_add_struct_f32.argtypes = [_F32P, _F32P, _c_int, _F32P, _c_int]
+        L.orc_unpack_f32.argtypes = [_F32P, _c_int, _F32P, _c_int]
+        L.orc_pack_f32.argtypes = [_F32P, _c_int, _F32P, _c_int]
+        L.orc_toeplitz_compact_f32.argtypes = [_F32P, _F32P, _c_int, _c_int]
         L.orc_relerr.argtypes = [_F32P, _F64P, ctypes.c_size_t]
         L.orc_relerr.restype = ctypes.c_double
         _lib = L
@@ -134,6 +139,53 @@ def toeplitz_left_f32(g, B) -> np.ndarray:
     C = np.empty((N, ncols), np.float32)
     lib().orc_toeplitz_left_f32(g, B, C, N, ncols)
     return C
+
+
+# ---------------------------------------------------------------- elementwise / converters
+STRUCTS = {"upper": 0, "lower": 1, "symm": 2, "diag": 3, "toeplitz": 4}
+
+
+def struct_numel(fmt: str, N: int) -> int:
+    return {"upper": N * (N + 1) // 2, "lower": N * (N + 1) // 2, "symm": N * (N + 1) // 2, "diag": N,
+            "toeplitz": max(2 * N - 1, 0)}[fmt]
+
+
+def add_f32(A, B) -> np.ndarray:
+    A, B = _f32(A), _f32(B)
+    C = np.empty_like(A)
+    lib().orc_add_f32(A.reshape(-1), B.reshape(-1), C.reshape(-1), A.size)
+    return C
+
+
+def add_struct_f32(A, S, fmt: str) -> np.ndarray:
+    A, S = _f32(A), _f32(S)
+    N = A.shape[0]
+    C = np.empty((N, N), np.float32)
+    lib().orc_add_struct_f32(A, S, STRUCTS[fmt], C, N)
+    return C
+
+
+def unpack_f32(S, fmt: str, N: int) -> np.ndarray:
+    S = _f32(S)
+    D = np.empty((N, N), np.float32)
+    lib().orc_unpack_f32(S, STRUCTS[fmt], D, N)
+    return D
+
+
+def pack_f32(D, fmt: str) -> np.ndarray:
+    D = _f32(D)
+    N = D.shape[0]
+    P = np.empty(N * (N + 1) // 2, np.float32)
+    lib().orc_pack_f32(D, STRUCTS[fmt], P, N)
+    return P
+
+
+def toeplitz_compact_f32(T) -> np.ndarray:
+    T = _f32(T)
+    rows, cols = T.shape
+    g = np.empty(rows + cols - 1, np.float32)
+    lib().orc_toeplitz_compact_f32(T, g, rows, cols)
+    return g
 
 
 # ---------------------------------------------------------------- fp64 sampled rows
@@ -246,6 +298,8 @@ def _ref_lib(name: str) -> ctypes.CDLL:
             L.ref_toeplitz_left.restype = d
             L.ref_toeplitz_right.argtypes = [_F32P, _F32P, _F32P, _c_int, _c_int, _c_int]
             L.ref_toeplitz_right.restype = d
+            L.ref_toeplitz_compact.argtypes = [_F32P, _F32P, _c_int, _c_int]
+            L.ref_toeplitz_compact.restype = None
         _ref[name] = L
     return _ref[name]
 
@@ -309,6 +363,15 @@ def ref_toeplitz_left(g, B) -> Tuple[np.ndarray, float]:
     N, ncols = B.shape
     C = np.empty((N, ncols), np.float32)
     return C, _check_ms(_ref_lib("toeplitz").ref_toeplitz_left(g, B, C, N, ncols), "toeplitz")
+
+
+def ref_toeplitz_compact(T) -> np.ndarray:
+    """The reference's build_toeplitz_compact (toeplitz_matmul2.cpp:34-41)."""
+    T = _f32(T)
+    rows, cols = T.shape
+    g = np.zeros(rows + cols - 1, np.float32)
+    _ref_lib("toeplitz").ref_toeplitz_compact(T, g, rows, cols)
+    return g
 
 
 def ref_toeplitz_right(X, g, N: Optional[int] = None) -> Tuple[np.ndarray, float]:

@@ -156,6 +156,60 @@ void orc_toeplitz_left_f32(const float* g, const float* B, float* C, int N, int 
   }
 }
 
+/* ---------------- elementwise sums and storage converters ---------------- */
+/* Structure codes: 0 packed upper, 1 packed lower, 2 packed symmetric,
+ * 3 diagonal, 4 Toeplitz generator (src/dsl/layout_functions.py:8-75). */
+static inline size_t lidx(long i, long j) { return (size_t)(i * (i + 1) / 2 + j); }
+
+static float struct_at(const float* S, int fmt, long n, long i, long j) {
+  switch (fmt) {
+    case 0: return i <= j ? S[pidx(i, j, n)] : 0.0f;                     /* upper_triangular_layout :8-23 */
+    case 1: return j <= i ? S[lidx(i, j)] : 0.0f;                        /* lower_triangular_layout :25-36 */
+    case 2: return i <= j ? S[pidx(i, j, n)] : S[pidx(j, i, n)];         /* symmetric_layout :50-68 */
+    case 3: return i == j ? S[i] : 0.0f;                                 /* diagonal_layout :38-43 */
+    default: return S[n - 1 + j - i];                                    /* toeplitz_layout :45-48 */
+  }
+}
+
+/* C[k] = A[k] + B[k]: kernel_add_1d_vec4 (src/dsl/codegen_cuda.py:1745-1773),
+ * one fp32 add per element in either of its branches. */
+void orc_add_f32(const float* A, const float* B, float* C, long count) {
+  for (long k = 0; k < count; ++k) C[k] = A[k] + B[k];
+}
+
+/* C = A + S expanded.  For the symmetric case this is kernel_add_gen_symm
+ * (src/dsl/codegen_cuda.py:1665-1681): r = min(i,j), c = max(i,j),
+ * C[i][j] = A[i][j] + S[r*n - r(r-1)/2 + (c-r)]. */
+void orc_add_struct_f32(const float* A, const float* S, int fmt, float* C, int N) {
+  const long n = N;
+  for (long i = 0; i < n; ++i)
+    for (long j = 0; j < n; ++j) C[i * n + j] = A[i * n + j] + struct_at(S, fmt, n, i, j);
+}
+
+/* D = the dense matrix of structured storage S. */
+void orc_unpack_f32(const float* S, int fmt, float* D, int N) {
+  const long n = N;
+  for (long i = 0; i < n; ++i)
+    for (long j = 0; j < n; ++j) D[i * n + j] = struct_at(S, fmt, n, i, j);
+}
+
+/* P = packed triangle of the dense D: upper (fmt 0 or 2) or lower (fmt 1). */
+void orc_pack_f32(const float* D, int fmt, float* P, int N) {
+  const long n = N;
+  for (long i = 0; i < n; ++i)
+    for (long j = 0; j < n; ++j) {
+      if (fmt == 1 && j <= i) P[lidx(i, j)] = D[i * n + j];
+      if (fmt != 1 && i <= j) P[pidx(i, j, n)] = D[i * n + j];
+    }
+}
+
+/* g = generator of the rows x cols Toeplitz matrix T, as build_toeplitz_compact
+ * (toeplitz_matmul2.cpp:34-41): g[rows-1-i] = T[i][0], g[rows-1+j] = T[0][j]. */
+void orc_toeplitz_compact_f32(const float* T, float* g, int rows, int cols) {
+  for (long i = 0; i < rows; ++i) g[rows - 1 - i] = T[i * cols];
+  for (long j = 1; j < cols; ++j) g[rows - 1 + j] = T[j];
+}
+
 /* ---------------- fp64 ground truth on selected rows ---------------- */
 
 /* out[r][:] = sum_k x_r[k] * B[k][:] in double, x_r given in double. */

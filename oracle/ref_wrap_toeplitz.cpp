@@ -35,6 +35,11 @@ double run_right(float* X, float* gen, float* Y, int M, int N, int K) {
 
 extern "C" {
 
+// The driver's own generator builder: g (K+N-1) of the K x N Toeplitz T.
+void ref_toeplitz_compact(const float* T, float* g, int K, int N) {
+  build_toeplitz_compact(const_cast<float*>(T), g, K, N);
+}
+
 // Right-side product as the driver runs it: Y(MxN) = X(MxK) * T(KxN).
 double ref_toeplitz_right(const float* X, const float* gen, float* Y, int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || M % kBM || N % kBN || K % kBK) return -1.0;

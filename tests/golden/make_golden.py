@@ -15,6 +15,7 @@ Two kinds of fixture:
    upper_       upper_triag_matmul.cpp:41-137 (via (UB)^T=(B^TJ)(JU^TJ)J)  N=64, 128 cols
    sandwich_    symmetric_matmul.cpp:84-211, then gemm_benchmark.cpp   N=64
    toeplitz_    toeplitz_matmul2.cpp:44-144 (via (TB)^T = B^T T^T)    N=128, 64 cols
+   tcompact_    toeplitz_matmul2.cpp:34-41 build_toeplitz_compact      T 37 x 53
    ===========  =====================================================  ==============
 
 2. ``golden_layouts.npz`` — the reference DSL's storage conventions, obtained
@@ -113,6 +114,11 @@ def outputs() -> dict:
                sandwich_C=O.ref_sandwich(s["A"], s["S"], s["B"])[0])
     t = W.make_toeplitz(128, 64, seed=15)
     out.update(toeplitz_g=t["g"], toeplitz_B=t["B"], toeplitz_C=O.ref_toeplitz_left(t["g"], t["B"])[0])
+    # generator of a rectangular Toeplitz matrix, by the driver's own
+    # build_toeplitz_compact (toeplitz_matmul2.cpp:34-41)
+    rng = np.random.default_rng(16)
+    tc = np.ascontiguousarray(rng.uniform(-1, 1, (37, 53)).astype(np.float32))
+    out.update(tcompact_T=tc, tcompact_g=O.ref_toeplitz_compact(tc))
     return out
 
 

@@ -43,6 +43,14 @@ def test_version_and_error_text():
     lambda L: L.smm_upper_left_rows(None, 0, None, None, 8, 4, 6, 4, 0, None, 0, None),
     lambda L: L.smm_toeplitz_left(None, None, None, -1, 4, 0, None, 0, None),
     lambda L: L.smm_symm_sandwich(None, None, None, None, 4, 9, None, 0, None),
+    lambda L: L.smm_add(None, None, None, -1, None),
+    lambda L: L.smm_add(None, None, None, 8, None),
+    lambda L: L.smm_add_struct(None, None, 9, None, 4, None),
+    lambda L: L.smm_add_struct(None, None, 2, None, 4, None),
+    lambda L: L.smm_unpack(None, 5, None, 4, None),
+    lambda L: L.smm_pack(None, 3, None, 4, None),   # diagonal: no packed triangle
+    lambda L: L.smm_pack(None, 4, None, 4, None),   # toeplitz: no packed triangle
+    lambda L: L.smm_toeplitz_compact(None, None, -1, 3, None),
 ])
 def test_invalid_arguments_rejected_on_host(call):
     L = _lib.load()
@@ -55,6 +63,11 @@ def test_empty_shapes_are_noops():
     assert L.smm_gemm(None, None, None, 0, 5, 5, 0, None, 0, None) == _lib.SMM_OK
     assert L.smm_diag_rows(None, None, None, 0, 0, None) == _lib.SMM_OK
     assert L.smm_toeplitz_left(None, None, None, 0, 0, 0, None, 0, None) == _lib.SMM_OK
+    assert L.smm_add(None, None, None, 0, None) == _lib.SMM_OK
+    assert L.smm_add_struct(None, None, 2, None, 0, None) == _lib.SMM_OK
+    assert L.smm_pack(None, 1, None, 0, None) == _lib.SMM_OK
+    assert L.smm_unpack(None, 4, None, 0, None) == _lib.SMM_OK
+    assert L.smm_toeplitz_compact(None, None, 0, 5, None) == _lib.SMM_OK
 
 
 def test_workspace_queries_are_host_only():

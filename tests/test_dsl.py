@@ -158,3 +158,41 @@ def test_run_graph_chains_in_post_order(recorder):
     assert ms == 2.0
     # the operands were restored after the placeholder substitution
     assert expr.operands[0] is inner
+
+
+@pytest.mark.parametrize("lhs,rhs,entry,out_cls,size", [
+    (GeneralMatrix, GeneralMatrix, "add", GeneralMatrix, 16),
+    (SymmetricMatrix, SymmetricMatrix, "add", SymmetricMatrix, 10),
+    (UpperTriangularMatrix, UpperTriangularMatrix, "add", UpperTriangularMatrix, 10),
+    (DiagonalMatrix, DiagonalMatrix, "add", DiagonalMatrix, 4),
+    (GeneralMatrix, SymmetricMatrix, "add_struct", GeneralMatrix, 16),
+    (SymmetricMatrix, GeneralMatrix, "add_struct", GeneralMatrix, 16),
+    (GeneralMatrix, UpperTriangularMatrix, "add_struct", GeneralMatrix, 16),
+    (LowerTriangularMatrix, GeneralMatrix, "add_struct", GeneralMatrix, 16),
+    (GeneralMatrix, DiagonalMatrix, "add_struct", GeneralMatrix, 16),
+    (ToeplitzMatrix, GeneralMatrix, "add_struct", GeneralMatrix, 16),
+])
+def test_add_lowering(recorder, lhs, rhs, entry, out_cls, size):
+    n = Var("n")
+    nv = 4
+    sizes = {GeneralMatrix: nv * nv, DiagonalMatrix: nv, UpperTriangularMatrix: nv * (nv + 1) // 2,
+             LowerTriangularMatrix: nv * (nv + 1) // 2, SymmetricMatrix: nv * (nv + 1) // 2,
+             ToeplitzMatrix: 2 * nv - 1}
+    L, R = lhs((n, n), "A"), rhs((n, n), "B")
+    inputs = {"n": nv, "A": np.ones(sizes[lhs], np.float32), "B": np.ones(sizes[rhs], np.float32)}
+    out, ms, gflops = RC.run([L + R], inputs, "cuda", out_cls((n, n), "C"))
+    assert list(out) == ["C"] and out["C"].numel() == size
+    assert [c[0] for c in recorder.calls] == [entry]
+    if entry == "add_struct":
+        fmt = recorder.calls[0][1][2]
+        assert fmt == {UpperTriangularMatrix: "upper", LowerTriangularMatrix: "lower", SymmetricMatrix: "symm",
+                       DiagonalMatrix: "diag", ToeplitzMatrix: "toeplitz"}[rhs if lhs is GeneralMatrix else lhs]
+    assert gflops == pytest.approx(size * 1e-9 / 1e-3)
+
+
+def test_add_of_unrelated_structures_raises(recorder):
+    n = Var("n")
+    with pytest.raises(NotImplementedError):
+        RC.run([SymmetricMatrix((n, n), "A") + UpperTriangularMatrix((n, n), "B")],
+               {"n": 2, "A": np.ones(3, np.float32), "B": np.ones(3, np.float32)}, "cuda",
+               GeneralMatrix((n, n), "C"))

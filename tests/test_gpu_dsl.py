@@ -139,3 +139,23 @@ def test_dsl_run_graph_sandwich_and_chain(cuda):
     res, ms, _ = run_graph([chain], {"n": 256, "G1": dev(w[0]), "G2": dev(w[1]), "G3": dev(w[2])}, "cuda")
     exp = w[0].astype(np.float64) @ w[1] @ w[2]
     assert relerr64(res[chain.name].view(256, 256).cpu().numpy(), exp) <= 1e-5
+
+
+def test_dsl_add_gen_symm_and_same_class(cuda):
+    """The DSL's `+` (codegen_cuda.py:1643-1827): general + symmetric expands
+    the packed operand; same-class operands add over their storage.  Exact
+    against the oracle."""
+    n = Var("n")
+    rng = np.random.default_rng(9)
+    nv = 300
+    A = rng.uniform(-1, 1, (nv, nv)).astype(np.float32)
+    Sp = rng.uniform(-1, 1, nv * (nv + 1) // 2).astype(np.float32)
+    res, ms, gflops = run([GeneralMatrix((n, n), "A") + SymmetricMatrix((n, n), "S")],
+                          {"n": nv, "A": dev(A), "S": dev(Sp)}, "cuda", GeneralMatrix((n, n), "C"))
+    assert np.array_equal(res["C"].view(nv, nv).cpu().numpy(), O.add_struct_f32(A, Sp, "symm"))
+    assert ms > 0 and gflops > 0
+    Sq = rng.uniform(-1, 1, Sp.size).astype(np.float32)
+    res, _, _ = run([SymmetricMatrix((n, n), "P") + SymmetricMatrix((n, n), "Q")],
+                    {"n": nv, "P": dev(Sp), "Q": dev(Sq)}, "cuda", SymmetricMatrix((n, n), "R"))
+    assert res["R"].numel() == Sp.size
+    assert np.array_equal(res["R"].cpu().numpy(), O.add_f32(Sp, Sq))

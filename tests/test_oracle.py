@@ -108,3 +108,46 @@ def test_workload_packing_matches_reference_layouts(golden_layouts):
     assert np.array_equal(T, g[golden_layouts["layout_toeplitz"]])
     S = W.unpack_symmetric(p, n)
     assert np.array_equal(S, p[golden_layouts["layout_symmetric"]])
+
+
+# ---------------------------------------------------------------- elementwise / converters
+_LAYOUT_OF = {"upper": "layout_upper_triangular", "lower": "layout_lower_triangular", "symm": "layout_symmetric",
+              "diag": "layout_diagonal", "toeplitz": "layout_toeplitz"}
+
+
+def _expand_by_map(storage, idx):
+    """Dense matrix of `storage` under a reference layout map (-1 = zero)."""
+    return np.where(idx >= 0, storage[np.maximum(idx, 0)], np.float32(0))
+
+
+@pytest.mark.parametrize("fmt", sorted(_LAYOUT_OF))
+def test_unpack_restatement_matches_reference_layouts(golden_layouts, fmt):
+    n = int(golden_layouts["layout_n"])
+    storage = np.arange(1, O.struct_numel(fmt, n) + 1, dtype=np.float32)
+    assert np.array_equal(O.unpack_f32(storage, fmt, n), _expand_by_map(storage, golden_layouts[_LAYOUT_OF[fmt]]))
+
+
+@pytest.mark.parametrize("fmt", ["upper", "lower", "symm"])
+def test_pack_restatement_inverts_unpack(golden_layouts, fmt):
+    n = int(golden_layouts["layout_n"])
+    storage = np.arange(1, O.struct_numel(fmt, n) + 1, dtype=np.float32)
+    assert np.array_equal(O.pack_f32(O.unpack_f32(storage, fmt, n), fmt), storage)
+
+
+@pytest.mark.parametrize("fmt", sorted(_LAYOUT_OF))
+def test_add_struct_restatement_is_one_add_per_element(golden_layouts, fmt):
+    n = 9
+    rng = np.random.default_rng(5)
+    A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    S = rng.uniform(-1, 1, O.struct_numel(fmt, n)).astype(np.float32)
+    assert np.array_equal(O.add_struct_f32(A, S, fmt), A + O.unpack_f32(S, fmt, n))
+
+
+def test_add_restatement():
+    rng = np.random.default_rng(6)
+    A, B = rng.standard_normal(1001).astype(np.float32), rng.standard_normal(1001).astype(np.float32)
+    assert np.array_equal(O.add_f32(A, B), A + B)
+
+
+def test_toeplitz_compact_restatement_matches_reference_builder(golden):
+    assert np.array_equal(O.toeplitz_compact_f32(golden["tcompact_T"]), golden["tcompact_g"])
