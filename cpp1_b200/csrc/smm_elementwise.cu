@@ -12,10 +12,9 @@
 // rows (128-bit streaming loads/stores of the dense operands when rows are
 // 16-byte aligned).  The structured operand is read where it lies: packed rows
 // and generator windows are contiguous along j, so lanes along j coalesce.
-// The one exception is the mirrored half of a symmetric matrix: element
-// (i, j), i > j, lives in packed row j, so a tile wholly below the diagonal is
-// read transposed (lanes along i, contiguous in packed row j) into shared
-// memory and then consumed row-wise.
+// The symmetric operand is the exception: element (i, j), i > j, lives in
+// packed row j, so each CTA takes a pair of mirror tiles, reads their packed
+// block once into shared memory and writes both (symm_pair_kernel).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -44,8 +43,6 @@ __device__ __forceinline__ float struct_at(const float* __restrict__ s, int n, i
     return i <= j ? __ldg(s + pk_upper(i, j, n)) : 0.0f;
   } else if constexpr (SF == SMM_STRUCT_LOWER) {
     return j <= i ? __ldg(s + pk_lower(i, j)) : 0.0f;
-  } else if constexpr (SF == SMM_STRUCT_SYMM) {
-    return i <= j ? __ldg(s + pk_upper(i, j, n)) : __ldg(s + pk_upper(j, i, n));
   } else if constexpr (SF == SMM_STRUCT_DIAG) {
     return i == j ? __ldg(s + i) : 0.0f;
   } else {  // SMM_STRUCT_TOEPLITZ
@@ -54,12 +51,12 @@ __device__ __forceinline__ float struct_at(const float* __restrict__ s, int n, i
 }
 
 // C = A + S (HAS_A) or C = S, all n x n, A and C row-major with leading
-// dimension n, S in structured storage of format SF.
+// dimension n, S in structured storage of format SF (upper, lower, diagonal,
+// Toeplitz: read row-wise, contiguous along j).
 template <int SF, bool HAS_A>
 __global__ void __launch_bounds__(kEwThreads) dense_struct_kernel(const float* __restrict__ A,
                                                                   const float* __restrict__ S,
                                                                   float* __restrict__ C, int n, int vec) {
-  __shared__ float tr[kTileR][kTileC + 1];  // transposed staging (symmetric, below the diagonal)
   const int row0 = blockIdx.y * kTileR;
   const int col0 = blockIdx.x * kTileC;
   const int t = threadIdx.x;
@@ -69,18 +66,6 @@ __global__ void __launch_bounds__(kEwThreads) dense_struct_kernel(const float* _
   const bool above = row0 + kTileR - 1 <= col0;       // every i <= every j
   const bool zero_tile = (SF == SMM_STRUCT_UPPER && below) || (SF == SMM_STRUCT_LOWER && above) ||
                          (SF == SMM_STRUCT_DIAG && (below || above));
-  const bool staged = (SF == SMM_STRUCT_SYMM) && below;
-  if (staged) {
-    // element (i, j) = S[j][i], packed row j: lanes along i
-    const int li = t & 31;
-#pragma unroll 4
-    for (int k = 0; k < kTileC / 8; ++k) {
-      const int lj = (t >> 5) + 8 * k;
-      const int i = row0 + li, j = col0 + lj;
-      tr[li][lj] = (i < n && j < n) ? __ldg(S + pk_upper(j, i, n)) : 0.0f;
-    }
-    __syncthreads();
-  }
 #pragma unroll
   for (int it = 0; it < kTileR / 8; ++it) {
     const int r = rr + 8 * it;
@@ -93,13 +78,7 @@ __global__ void __launch_bounds__(kEwThreads) dense_struct_kernel(const float* _
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int j = j0 + e;
-      if (j >= n || zero_tile) {
-        s[e] = 0.0f;
-      } else if (staged) {
-        s[e] = tr[r][4 * cq + e];
-      } else {
-        s[e] = struct_at<SF>(S, n, i, j);
-      }
+      s[e] = (j >= n || zero_tile) ? 0.0f : struct_at<SF>(S, n, i, j);
     }
     if (vec && j0 + 4 <= n) {
       float4 c = make_float4(s[0], s[1], s[2], s[3]);
@@ -113,6 +92,106 @@ __global__ void __launch_bounds__(kEwThreads) dense_struct_kernel(const float* _
       for (int e = 0; e < 4; ++e) {
         const int j = j0 + e;
         if (j < n) C[base + j] = HAS_A ? __fadd_rn(A[base + j], s[e]) : s[e];
+      }
+    }
+  }
+}
+
+// Symmetric operand: one CTA per pair of mirror tiles (I, J), I <= J, of
+// kSymT x kSymT.  The packed block P[rows of I][cols of J] (contiguous along
+// each packed row) is read once into shared memory, then C[I][J] = A + P and,
+// for I != J, C[J][I] = A + P^T are written.  Every packed element crosses
+// HBM once (an element-per-output expansion reads the upper triangle twice).
+constexpr int kSymT = 64;
+constexpr bool kSymPrefetch = false;  // load the dense operand before the barrier
+
+__device__ __forceinline__ void tri_tile(int b, int& I, int& J, int nt) {
+  // b enumerates (I, J), I <= J < nt, row by row: row I holds nt - I tiles.
+  int lo = 0, hi = nt - 1;
+  while (lo < hi) {  // largest I with first(I) <= b, first(I) = I*nt - I(I-1)/2
+    const int mid = (lo + hi + 1) >> 1;
+    const long long first = static_cast<long long>(mid) * nt - static_cast<long long>(mid) * (mid - 1) / 2;
+    if (first <= b) lo = mid; else hi = mid - 1;
+  }
+  I = lo;
+  J = I + static_cast<int>(b - (static_cast<long long>(I) * nt - static_cast<long long>(I) * (I - 1) / 2));
+}
+
+template <bool HAS_A>
+__global__ void __launch_bounds__(kEwThreads) symm_pair_kernel(const float* __restrict__ A,
+                                                               const float* __restrict__ P, float* __restrict__ C,
+                                                               int n, int vec) {
+  constexpr int T = kSymT;
+  constexpr int kQ = T / 4;               // float4 quads per tile row
+  constexpr int kRowsPass = kEwThreads / kQ;  // tile rows written per pass
+  static_assert(kRowsPass <= T && T % kRowsPass == 0, "tile / thread geometry");
+  __shared__ float tile[T][T + 1];
+  const int nt = (n + T - 1) / T;
+  int I, J;
+  tri_tile(blockIdx.x, I, J, nt);
+  const int i0 = I * T, j0 = J * T;
+  const int t = threadIdx.x;
+  const bool pair = I != J;
+  const int c4 = 4 * (t % kQ);
+  const int rbase = t / kQ;
+  // Dense operand of this thread's output quads, loaded before the barrier
+  // so the loads overlap the packed-block loads.
+  float4 a[2][T / kRowsPass];
+#pragma unroll
+  for (int tt = 0; tt < 2; ++tt) {
+#pragma unroll
+    for (int k = 0; k < T / kRowsPass; ++k) {
+      a[tt][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (HAS_A && kSymPrefetch) {
+        const int i = (tt ? j0 : i0) + rbase + kRowsPass * k, j = (tt ? i0 : j0) + c4;
+        if (vec && (tt == 0 || pair) && i < n && j + 4 <= n)
+          a[tt][k] = __ldcs(reinterpret_cast<const float4*>(A + static_cast<long long>(i) * n + j));
+      }
+    }
+  }
+  {
+    // packed block rows i (of tile I), columns j (of tile J), i <= j; lanes
+    // along j (contiguous in packed row i)
+    const int lc = t % T;
+#pragma unroll
+    for (int k = 0; k < T * T / kEwThreads; ++k) {
+      const int lr = t / T + (kEwThreads / T) * k;
+      const int i = i0 + lr, j = j0 + lc;
+      tile[lr][lc] = (i < n && j < n && i <= j) ? __ldg(P + pk_upper(i, j, n)) : 0.0f;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int tt = 0; tt < 2; ++tt) {
+    if (tt == 1 && !pair) break;
+    const int r0g = tt ? j0 : i0, c0g = tt ? i0 : j0;
+#pragma unroll
+    for (int k = 0; k < T / kRowsPass; ++k) {
+      const int lr = rbase + kRowsPass * k;
+      const int i = r0g + lr;
+      if (i >= n) continue;
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int lcol = c4 + e;
+        if (tt == 0)  // diagonal tiles take the mirror below the diagonal
+          v[e] = (!pair && lr > lcol) ? tile[lcol][lr] : tile[lr][lcol];
+        else          // C[J rows][I cols] = P^T
+          v[e] = tile[lcol][lr];
+      }
+      const long long base = static_cast<long long>(i) * n;
+      const int j = c0g + c4;
+      if (vec && j + 4 <= n) {
+        float4 c = make_float4(v[0], v[1], v[2], v[3]);
+        if constexpr (HAS_A) {
+          const float4 x = kSymPrefetch ? a[tt][k] : __ldcs(reinterpret_cast<const float4*>(A + base + j));
+          c = make_float4(__fadd_rn(x.x, c.x), __fadd_rn(x.y, c.y), __fadd_rn(x.z, c.z), __fadd_rn(x.w, c.w));
+        }
+        __stcs(reinterpret_cast<float4*>(C + base + j), c);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (j + e < n) C[base + j + e] = HAS_A ? __fadd_rn(A[base + j + e], v[e]) : v[e];
       }
     }
   }
@@ -136,20 +215,55 @@ __global__ void __launch_bounds__(kEwThreads) add_scalar_kernel(const float* __r
     C[k] = __fadd_rn(A[k], B[k]);
 }
 
-// Packed upper / lower storage from a dense n x n matrix: block (x, i) copies
-// chunk x (1024 elements) of packed row i.
+// Packed upper / lower storage from a dense n x n matrix, over the packed
+// index: each thread writes 4 consecutive packed elements (one aligned
+// 128-bit store when the packed array is 16-byte aligned), reading them from
+// the dense row(s) they come from, so reads walk dense rows contiguously and
+// writes stream through the packed array.
+template <int SF>
+__device__ __forceinline__ long long packed_row_start(long long i, long long n) {
+  return SF == SMM_STRUCT_LOWER ? i * (i + 1) / 2 : i * n - i * (i - 1) / 2;
+}
+
 template <int SF>
 __global__ void __launch_bounds__(kEwThreads) pack_kernel(const float* __restrict__ D, float* __restrict__ P,
-                                                          int n) {
-  const int i = blockIdx.y;
-  const int len = (SF == SMM_STRUCT_LOWER) ? i + 1 : n - i;  // packed row length
-  const int first = (SF == SMM_STRUCT_LOWER) ? 0 : i;          // first dense column
-  const long long out0 = (SF == SMM_STRUCT_LOWER) ? pk_lower(i, 0) : pk_upper(i, i, n);
-  const float* src = D + static_cast<long long>(i) * n + first;
+                                                          int n, int vec) {
+  const long long nn = n;
+  const long long total = nn * (nn + 1) / 2;
+  const long long stride = 4LL * gridDim.x * blockDim.x;
+  for (long long p0 = 4LL * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x); p0 < total;
+       p0 += stride) {
+    // row i holding packed element p0: the largest i with start(i) <= p0
+    long long i;
+    if constexpr (SF == SMM_STRUCT_LOWER) {
+      i = static_cast<long long>((sqrt(8.0 * static_cast<double>(p0) + 1.0) - 1.0) * 0.5);
+    } else {
+      const double b = 2.0 * static_cast<double>(nn) + 1.0;
+      i = static_cast<long long>((b - sqrt(b * b - 8.0 * static_cast<double>(p0))) * 0.5);
+    }
+    i = i < 0 ? 0 : (i > nn - 1 ? nn - 1 : i);
+    while (i > 0 && packed_row_start<SF>(i, nn) > p0) --i;
+    while (i + 1 < nn && packed_row_start<SF>(i + 1, nn) <= p0) ++i;
+    // column of p0 in row i, then step along the packed order
+    long long j = (SF == SMM_STRUCT_LOWER ? 0 : i) + (p0 - packed_row_start<SF>(i, nn));
+    float v[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int k = blockIdx.x * (4 * kEwThreads) + e * kEwThreads + threadIdx.x;
-    if (k < len) P[out0 + k] = __ldcs(src + k);
+    for (int e = 0; e < 4; ++e) {
+      v[e] = (p0 + e < total) ? __ldcs(D + i * nn + j) : 0.0f;
+      ++j;
+      const long long row_end = SF == SMM_STRUCT_LOWER ? i + 1 : nn;  // one past the row's last column
+      if (j >= row_end) {
+        ++i;
+        j = SF == SMM_STRUCT_LOWER ? 0 : i;
+      }
+    }
+    if (vec && p0 + 4 <= total) {
+      __stcs(reinterpret_cast<float4*>(P + p0), make_float4(v[0], v[1], v[2], v[3]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (p0 + e < total) P[p0 + e] = v[e];
+    }
   }
 }
 
@@ -186,10 +300,18 @@ int launch_dense_struct(const float* A, const float* S, int fmt, float* C, int n
   const dim3 grid((n + kTileC - 1) / kTileC, (n + kTileR - 1) / kTileR);
   if (grid.y > 65535u) return set_error(SMM_ERR_INVALID, "order %d too large for the tile grid", n);
   const int vec = (n % 4 == 0) && aligned16(C) && (!HAS_A || aligned16(A)) ? 1 : 0;
+  if (fmt == SMM_STRUCT_SYMM) {
+    const long long nt = (n + kSymT - 1) / kSymT;
+    const long long pairs = nt * (nt + 1) / 2;
+    if (pairs > 0x7FFFFFFFLL) return set_error(SMM_ERR_INVALID, "order %d too large for the tile grid", n);
+    symm_pair_kernel<HAS_A><<<static_cast<unsigned>(pairs), kEwThreads, 0, st>>>(A, S, C, n, vec);
+    count_launch();
+    SMM_CUDA_TRY(cudaGetLastError(), "symmetric elementwise launch");
+    return SMM_OK;
+  }
   switch (fmt) {
     case SMM_STRUCT_UPPER: dense_struct_kernel<SMM_STRUCT_UPPER, HAS_A><<<grid, kEwThreads, 0, st>>>(A, S, C, n, vec); break;
     case SMM_STRUCT_LOWER: dense_struct_kernel<SMM_STRUCT_LOWER, HAS_A><<<grid, kEwThreads, 0, st>>>(A, S, C, n, vec); break;
-    case SMM_STRUCT_SYMM: dense_struct_kernel<SMM_STRUCT_SYMM, HAS_A><<<grid, kEwThreads, 0, st>>>(A, S, C, n, vec); break;
     case SMM_STRUCT_DIAG: dense_struct_kernel<SMM_STRUCT_DIAG, HAS_A><<<grid, kEwThreads, 0, st>>>(A, S, C, n, vec); break;
     default: dense_struct_kernel<SMM_STRUCT_TOEPLITZ, HAS_A><<<grid, kEwThreads, 0, st>>>(A, S, C, n, vec); break;
   }
@@ -260,13 +382,14 @@ extern "C" int smm_pack(const float* D, int s_fmt, float* P, int N, void* stream
                      valid_struct(s_fmt) ? struct_name(s_fmt) : "unknown");
   if (N == 0) return SMM_OK;
   if (!D || !P) return set_error(SMM_ERR_INVALID, "smm_pack: null pointer");
-  if (N > 65535) return set_error(SMM_ERR_INVALID, "smm_pack: order %d above 65535", N);
   cudaStream_t st = as_stream(stream);
-  const dim3 grid((N + 4 * kEwThreads - 1) / (4 * kEwThreads), N);
+  const long long total = static_cast<long long>(N) * (N + 1) / 2;
+  const int grid = grid_for((total + 3) / 4);
+  const int vec = aligned16(P) ? 1 : 0;
   if (s_fmt == SMM_STRUCT_LOWER)
-    pack_kernel<SMM_STRUCT_LOWER><<<grid, kEwThreads, 0, st>>>(D, P, N);
+    pack_kernel<SMM_STRUCT_LOWER><<<grid, kEwThreads, 0, st>>>(D, P, N, vec);
   else
-    pack_kernel<SMM_STRUCT_UPPER><<<grid, kEwThreads, 0, st>>>(D, P, N);
+    pack_kernel<SMM_STRUCT_UPPER><<<grid, kEwThreads, 0, st>>>(D, P, N, vec);
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "smm_pack launch");
   clear_error();

@@ -217,7 +217,7 @@ int smm_unpack(const float* S, int s_fmt, float* D, int N, void* stream);
 /* P (packed, N(N+1)/2 floats) = the upper (SMM_STRUCT_UPPER or _SYMM) or
  * lower (SMM_STRUCT_LOWER) triangle of the dense N x N matrix D, in the DSL's
  * packed order (layout_functions.py:8-36; the torch.triu_indices order of
- * main2.py:44-45 and runner_cuda.py:96-97).  N <= 65535. */
+ * main2.py:44-45 and runner_cuda.py:96-97). */
 int smm_pack(const float* D, int s_fmt, float* P, int N, void* stream);
 
 /* g (rows + cols - 1 floats) = the generator of the rows x cols Toeplitz
