@@ -12,7 +12,7 @@
 #include <mutex>
 
 #include "smm_host.h"
-#include "smm_umma.cuh"
+#include "smm_launch.cuh"
 
 // Sticky kernel status word, one per device context.
 __device__ uint32_t g_smm_status;
@@ -102,73 +102,6 @@ int round4(int x) { return (x + 3) & ~3; }
 int round8(int x) { return (x + 7) & ~7; }
 
 // ---------------------------------------------------------------- launches
-struct Maps {
-  CUtensorMap a{}, b{}, al{}, bl{};
-};
-
-template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR>
-int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
-  auto kern = umma_gemm_kernel<AK, BK, MD, BN, STAGES, PAIR>;
-  constexpr int smem = umma_smem_bytes<PAIR ? BN / 2 : BN, MD == Mode::TF32x3, STAGES>();
-  static_assert(smem <= 227 * 1024, "shared memory budget");
-  static bool attr_set[64] = {};
-  int dev = 0;
-  SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-  if (!attr_set[dev & 63]) {
-    SMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                 "cudaFuncSetAttribute(max dynamic smem)");
-    attr_set[dev & 63] = true;
-  }
-  const long long blocks = static_cast<long long>(p.row_tiles) * p.col_tiles * (PAIR ? 2 : 1);
-  if (blocks > 0x7FFFFFFFLL) return set_error(SMM_ERR_INVALID, "product too large for one launch");
-  if constexpr (PAIR) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
-    cfg.blockDim = dim3(umma_threads(AK, MD), 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    SMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.al, m.bl, p), "tcgen05 pair contraction launch");
-  } else {
-    kern<<<static_cast<unsigned>(blocks), umma_threads(AK, MD), smem, st>>>(m.a, m.b, m.al, m.bl, p);
-  }
-  count_launch();
-  SMM_CUDA_TRY(cudaGetLastError(), "tcgen05 contraction launch");
-  return SMM_OK;
-}
-
-// Stage counts fill ~192 KiB of shared memory (a pair CTA stages half the B
-// columns, so its stages are smaller and more of them fit).
-template <AKind AK, BKind BK, int BN, bool PAIR>
-int launch_mode(int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
-  constexpr int kCols = PAIR ? BN / 2 : BN;  // B columns per CTA
-  if (mode == SMM_MODE_3XTF32) {
-    constexpr int S = (kCols == 256) ? 4 : (kCols == 128 ? 6 : 8);
-    return launch_umma<AK, BK, Mode::TF32x3, BN, S, PAIR>(m, p, st);
-  }
-  if (mode == SMM_MODE_BF16) return launch_umma<AK, BK, Mode::BF16, BN, 8, PAIR>(m, p, st);
-  return launch_umma<AK, BK, Mode::TF32, BN, 8, PAIR>(m, p, st);
-}
-
-template <AKind AK, BKind BK>
-int launch_bn(int bn, bool pair, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
-  if (pair) {
-    if (bn == 256) return launch_mode<AK, BK, 256, true>(mode, m, p, st);
-    return launch_mode<AK, BK, 128, true>(mode, m, p, st);
-  }
-  switch (bn) {
-    case 256: return launch_mode<AK, BK, 256, false>(mode, m, p, st);
-    case 128: return launch_mode<AK, BK, 128, false>(mode, m, p, st);
-    default: return launch_mode<AK, BK, 64, false>(mode, m, p, st);
-  }
-}
-
 // CTA pairs (256-row tiles, tcgen05 cta_group::2) whenever there are at least
 // two row tiles and the pair tiles fill about a wave of the 74 SM pairs.
 // SMM_PAIR=0 forces single-CTA tiles, SMM_PAIR=1 pairs for every M > 128.
@@ -268,22 +201,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.trace = g_trace;
   if (!p.status) return set_error(SMM_ERR_CUDA, "device status word unavailable");
   g_trace = nullptr;
-  if (bk == BKind::Dense) {
-    switch (ak) {
-      case AKind::Dense: return launch_bn<AKind::Dense, BKind::Dense>(bn, pair, mode, m, p, st);
-      case AKind::UpperDense: return launch_bn<AKind::UpperDense, BKind::Dense>(bn, pair, mode, m, p, st);
-      case AKind::UpperPacked: return launch_bn<AKind::UpperPacked, BKind::Dense>(bn, pair, mode, m, p, st);
-      case AKind::Toeplitz: return launch_bn<AKind::Toeplitz, BKind::Dense>(bn, pair, mode, m, p, st);
-      case AKind::SymmPacked: return launch_bn<AKind::SymmPacked, BKind::Dense>(bn, pair, mode, m, p, st);
-    }
-  }
-  if (ak == AKind::Dense && bk == BKind::UpperPacked)
-    return launch_bn<AKind::Dense, BKind::UpperPacked>(bn, pair, mode, m, p, st);
-  if (ak == AKind::Dense && bk == BKind::SymmPacked)
-    return launch_bn<AKind::Dense, BKind::SymmPacked>(bn, pair, mode, m, p, st);
-  if (ak == AKind::SymmPacked && bk == BKind::SymmPacked)
-    return launch_bn<AKind::SymmPacked, BKind::SymmPacked>(bn, pair, mode, m, p, st);
-  return set_error(SMM_ERR_INVALID, "unsupported operand kinds");
+  return launch_kinds(ak, bk, bn, pair, mode, m, p, st);
 }
 
 Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf = nullptr) {
@@ -673,6 +591,11 @@ extern "C" int smm_gen_x_symm(const float* A, const float* S, float* C, int M, i
   return gen_x_struct("smm_gen_x_symm", BKind::SymmPacked, A, S, C, M, N, mode, ws, ws_bytes, as_stream(stream));
 }
 
+extern "C" int smm_gen_x_lower(const float* A, const float* Lp, float* C, int M, int N, int mode, void* ws,
+                               size_t ws_bytes, void* stream) {
+  return gen_x_struct("smm_gen_x_lower", BKind::LowerPacked, A, Lp, C, M, N, mode, ws, ws_bytes, as_stream(stream));
+}
+
 extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N, int mode, void* stream) {
   if (N < 0) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: negative shape");
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: unknown mode %d", mode);
@@ -680,6 +603,38 @@ extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N
   if (!S1 || !S2 || !C) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: null pointer");
   if (int rc = check_packed("smm_symm_x_symm", N)) return rc;
   return run_contraction(AKind::SymmPacked, BKind::SymmPacked, mode, structured_op(S1, N), structured_op(S2, N), C,
+                         N, N, N, N, as_stream(stream));
+}
+
+// ---------------------------------------------------------------- lower-triangular operands
+extern "C" size_t smm_lower_left_workspace_size(int N, int ncols, int mode) {
+  if (N <= 0 || ncols <= 0) return 0;
+  return staged_bytes_bound(N, ncols, mode);
+}
+
+extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, int ncols, int mode, void* ws,
+                              size_t ws_bytes, void* stream) {
+  if (N < 0 || ncols < 0) return set_error(SMM_ERR_INVALID, "smm_lower_left: negative shape");
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_lower_left: unknown mode %d", mode);
+  if (N == 0 || ncols == 0) return SMM_OK;
+  if (!Lp || !B || !C) return set_error(SMM_ERR_INVALID, "smm_lower_left: null pointer");
+  if (int rc = check_packed("smm_lower_left", N)) return rc;
+  cudaStream_t st = as_stream(stream);
+  if (int rc = check_ws("smm_lower_left", ws, ws_bytes, staged_bytes(B, N, ncols, mode))) return rc;
+  uint8_t* cur = static_cast<uint8_t*>(ws);
+  Staged b;
+  if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
+  return run_contraction(AKind::LowerPacked, BKind::Dense, mode, structured_op(Lp, N), dense_op(b.ptr, b.lo, b.ld, b.bf16),
+                         C, ncols, N, ncols, N, st);
+}
+
+extern "C" int smm_lower_x_lower(const float* L1, const float* L2, float* C, int N, int mode, void* stream) {
+  if (N < 0) return set_error(SMM_ERR_INVALID, "smm_lower_x_lower: negative shape");
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_lower_x_lower: unknown mode %d", mode);
+  if (N == 0) return SMM_OK;
+  if (!L1 || !L2 || !C) return set_error(SMM_ERR_INVALID, "smm_lower_x_lower: null pointer");
+  if (int rc = check_packed("smm_lower_x_lower", N)) return rc;
+  return run_contraction(AKind::LowerPacked, BKind::LowerPacked, mode, structured_op(L1, N), structured_op(L2, N), C,
                          N, N, N, N, as_stream(stream));
 }
 

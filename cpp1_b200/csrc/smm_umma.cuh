@@ -18,12 +18,17 @@
 //                                 of the tile is a contiguous window)
 //     AKind::SymmPacked           built on chip from packed-upper storage,
 //                                 mirrored below the diagonal
+//     AKind::LowerPacked          built on chip from packed-lower storage
+//                                 (idx(i,j) = i(i+1)/2 + j); k-blocks right of
+//                                 the row tile's last diagonal element are
+//                                 never visited
 //   B (MN-major, BN columns x 16 k-rows, 32-column boxes, 128-byte swizzle
 //     with 32-byte atoms — the only swizzle kind::tf32 accepts for an MN-major
 //     operand; with the plain 128-byte swizzle the MMA produces nothing):
 //     BKind::Dense                TMA tile loads of a row-major B
-//     BKind::UpperPacked/SymmPacked  built on chip (the DSL's Gen@Upper,
-//                                 Gen@Symm, Symm@Symm)
+//     BKind::UpperPacked/SymmPacked/LowerPacked  built on chip (the DSL's
+//                                 Gen@Upper, Gen@Symm, Symm@Symm, Gen@Lower,
+//                                 Lower@Lower)
 //
 // 3xTF32 (SPLIT3): three MMAs per k-step, hi*hi + hi*lo + lo*hi.  The tensor
 // core's fp32 accumulation truncates on every update, so with same-sign data
@@ -55,10 +60,10 @@
 
 namespace smm {
 
-enum class AKind : int { Dense = 0, UpperPacked = 1, Toeplitz = 2, SymmPacked = 3, UpperDense = 4 };
+enum class AKind : int { Dense = 0, UpperPacked = 1, Toeplitz = 2, SymmPacked = 3, UpperDense = 4, LowerPacked = 5 };
 // Right operand: a dense row-major matrix loaded by TMA, or a packed
 // upper-triangular / symmetric matrix built on chip by the transform warps.
-enum class BKind : int { Dense = 0, UpperPacked = 1, SymmPacked = 2 };
+enum class BKind : int { Dense = 0, UpperPacked = 1, SymmPacked = 2, LowerPacked = 3 };
 
 // Arithmetic of the contraction (values match smm_mode).
 enum class Mode : int { TF32x3 = 0, TF32 = 1, BF16 = 2 };
@@ -161,6 +166,8 @@ __device__ __forceinline__ float a_value(const float* __restrict__ src, int n, i
     return k >= gr ? __ldg(src + packed_idx(gr, k, n)) : 0.0f;
   } else if constexpr (AK == AKind::Toeplitz) {
     return __ldg(src + (n - 1 + k - gr));
+  } else if constexpr (AK == AKind::LowerPacked) {
+    return k <= gr ? __ldg(src + (static_cast<long long>(gr) * (gr + 1) / 2 + k)) : 0.0f;
   } else {  // SymmPacked
     return k >= gr ? __ldg(src + packed_idx(gr, k, n)) : __ldg(src + packed_idx(k, gr, n));
   }
@@ -172,6 +179,8 @@ __device__ __forceinline__ float b_value(const float* __restrict__ src, int nd, 
   if (k >= nd || n >= nd) return 0.0f;
   if constexpr (BK == BKind::UpperPacked) {
     return n >= k ? __ldg(src + packed_idx(k, n, nd)) : 0.0f;
+  } else if constexpr (BK == BKind::LowerPacked) {
+    return n <= k ? __ldg(src + (static_cast<long long>(k) * (k + 1) / 2 + n)) : 0.0f;
   } else {  // SymmPacked
     return n >= k ? __ldg(src + packed_idx(k, n, nd)) : __ldg(src + packed_idx(n, k, nd));
   }
@@ -225,6 +234,8 @@ __device__ __forceinline__ void a_coord(bool rows, int xw, int lane, int it, int
 __device__ __forceinline__ uint32_t packed_row_base(long long i, long long n) {
   return static_cast<uint32_t>(i * n - i * (i - 1) / 2 - i);
 }
+// Same for packed-lower storage: element (i, k), k <= i, at i(i+1)/2 + k.
+__device__ __forceinline__ uint32_t lower_row_base(long long i) { return static_cast<uint32_t>(i * (i + 1) / 2); }
 
 template <AKind AK, int KS>
 __device__ __forceinline__ void a_row_bases(uint32_t (&rb)[KS / 2], const UmmaParams& p, int g_first, int xw,
@@ -234,7 +245,9 @@ __device__ __forceinline__ void a_row_bases(uint32_t (&rb)[KS / 2], const UmmaPa
     int r, kl;
     a_coord<KS>(false, xw, lane, it, r, kl);
     const long long gr = g_first + r;
-    rb[it] = (AK == AKind::Toeplitz) ? static_cast<uint32_t>(p.a_dim - 1 - gr) : packed_row_base(gr, p.a_dim);
+    rb[it] = (AK == AKind::Toeplitz)      ? static_cast<uint32_t>(p.a_dim - 1 - gr)
+             : (AK == AKind::LowerPacked) ? lower_row_base(gr)
+                                          : packed_row_base(gr, p.a_dim);
   }
 }
 
@@ -271,6 +284,8 @@ __device__ __forceinline__ void a_gather(float (&v)[KS / 2], const UmmaParams& p
     const bool in = gr < n && k < n;
     if constexpr (AK == AKind::UpperPacked) {
       v[it] = (in && k >= gr) ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
+    } else if constexpr (AK == AKind::LowerPacked) {
+      v[it] = (in && k <= gr) ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
     } else if constexpr (AK == AKind::Toeplitz) {
       v[it] = in ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
     } else {
@@ -339,8 +354,10 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
   if constexpr (AK == AKind::SymmPacked) mbase = packed_row_base(k, n);
   int r = fw * 64 + (lane >> 4);
   int gr = g_first + r;
-  // offset of element (gr, 0): packed row start minus gr, or n - 1 - gr
-  uint32_t rb = (AK == AKind::Toeplitz) ? static_cast<uint32_t>(n - 1 - gr) : packed_row_base(gr, n);
+  // offset of element (gr, 0): packed row start minus gr, lower row start, or n - 1 - gr
+  uint32_t rb = (AK == AKind::Toeplitz)      ? static_cast<uint32_t>(n - 1 - gr)
+                : (AK == AKind::LowerPacked) ? lower_row_base(gr)
+                                             : packed_row_base(gr, n);
 #pragma unroll 8
   for (int it = 0; it < 32; ++it) {
     const bool in = gr < n && k < n;
@@ -348,6 +365,9 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
     uint32_t so;
     if constexpr (AK == AKind::UpperPacked) {
       valid = in && k >= gr;
+      so = rb + static_cast<uint32_t>(k);
+    } else if constexpr (AK == AKind::LowerPacked) {
+      valid = in && k <= gr;
       so = rb + static_cast<uint32_t>(k);
     } else if constexpr (AK == AKind::Toeplitz) {
       valid = in;
@@ -360,6 +380,8 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
     // next row of this lane: two rows down
     if constexpr (AK == AKind::Toeplitz)
       rb -= 2u;
+    else if constexpr (AK == AKind::LowerPacked)
+      rb += static_cast<uint32_t>(2 * gr + 3);  // lower row base(gr + 2) - base(gr)
     else
       rb += static_cast<uint32_t>(2 * n - 2 * gr - 3);  // packed row base(gr + 2) - base(gr)
     r += 2;
@@ -518,10 +540,17 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   int kb_begin = 0;
   if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + tile_m0) / KS;
   int kb_end = (p.K + KS - 1) / KS;
+  // A lower-triangular left operand is zero right of its diagonal: rows up
+  // to g1 need k <= g1 only.
+  if constexpr (AK == AKind::LowerPacked)
+    kb_end = min(kb_end, (p.a_row0 + tile_m0 + (PAIR ? 2 * kBM : kBM) - 1) / KS + 1);
   // An upper-triangular right operand is zero below its diagonal: column
-  // tile [n0, n0+BN) needs k < n0 + BN only.
+  // tile [n0, n0+BN) needs k < n0 + BN only; a lower-triangular one is zero
+  // above it: the tile needs k >= n0 only.
   if constexpr (BK == BKind::UpperPacked) kb_end = min(kb_end, (n0 + BN - 1) / KS + 1);
-  const int num_kb = kb_end - kb_begin;
+  if constexpr (BK == BKind::LowerPacked) kb_begin = max(kb_begin, n0 / KS);
+  // Empty for a tile of L1 L2 wholly above the diagonal: it is written as zeros.
+  const int num_kb = max(kb_end - kb_begin, 0);
   const int nch = SPLIT3 ? (num_kb + kChunk - 1) / kChunk : 1;
 
   if (threadIdx.x == 0) {
@@ -801,10 +830,13 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     // ------------------------------------------------------------ epilogue
     // Result = running sum (chunks [0, nch-1)) + the last chunk's accumulator.
     bool last_ok = ok;
-    if constexpr (SPLIT3)
-      last_ok = last_ok && mbar_wait(acc_full, (nch - 1) & 1, wepi);
-    else
-      last_ok = last_ok && mbar_wait(accum_full, 0, wepi);
+    const bool no_k = num_kb == 0;  // nothing accumulated: the tile is zero
+    if (!no_k) {
+      if constexpr (SPLIT3)
+        last_ok = last_ok && mbar_wait(acc_full, (nch - 1) & 1, wepi);
+      else
+        last_ok = last_ok && mbar_wait(accum_full, 0, wepi);
+    }
     const bool acc_ok = __all_sync(0xffffffffu, last_ok && !*abort_flag);
     if (tr && t == 0) p.trace[kTrAccOk] = acc_ok ? 1u : 0u;
     if (acc_ok) {
@@ -815,6 +847,10 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
 #pragma unroll 1
       for (int c = 0; c < kHalf; c += 16) {
         uint32_t r[16];
+        if (no_k) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) r[j] = 0u;
+        } else {
         tmem_ld_32x32b_x16(acc_col + c, r);
         if (SPLIT3 && nch > 1) {
           uint32_t s16[16];
@@ -824,6 +860,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
           for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(s16[j]) + __uint_as_float(r[j]));
         } else {
           tmem_wait_ld();
+        }
         }
         if (tr && q == 0 && lane == 0 && h == 0 && c == 0)
           for (int j = 0; j < 16; ++j) p.trace[kTrAcc + j] = r[j];

@@ -119,6 +119,18 @@ def _lower(lk: str, rk: str):
     if (lk, rk) == ("symm", "symm"):
         return (lambda s1, s2, M, N, K, mode, out: ops.symm_x_symm(s1, s2, mode=mode, out=out),
                 lambda M, N, K: 2.0 * M * N * K)
+    # Lower-triangular operands: the reference implements Gen @ Lower and
+    # Lower @ Lower in its CPU AVX backend only (codegen_multiply_avx.py:546,
+    # 644); Lower @ Gen is the left-side counterpart of Upper @ Gen.
+    if (lk, rk) == ("gen", "lower"):
+        return (lambda a, l, M, N, K, mode, out: ops.gen_x_lower(a.view(M, K), l, mode=mode, out=out),
+                lambda M, N, K: 2.0 * M * N * K)
+    if (lk, rk) == ("lower", "gen"):
+        return (lambda l, b, M, N, K, mode, out: ops.lower_left(l, b.view(K, N), mode=mode, out=out),
+                lambda M, N, K: 2.0 * M * N * K)
+    if (lk, rk) == ("lower", "lower"):
+        return (lambda l1, l2, M, N, K, mode, out: ops.lower_x_lower(l1, l2, mode=mode, out=out),
+                lambda M, N, K: 2.0 * M * N * K)
     raise NotImplementedError(f"Matmul for {lk} @ {rk} not implemented in the CUDA backend")
 
 

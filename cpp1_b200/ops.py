@@ -200,6 +200,47 @@ def gen_x_symm(A: torch.Tensor, S: torch.Tensor, mode: str = "3xtf32", out: Opti
     return _gen_x_struct("smm_gen_x_symm", A, S, mode, out, stream)
 
 
+def gen_x_lower(A: torch.Tensor, Lp: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+                stream=None) -> torch.Tensor:
+    """C = A @ L with L lower triangular given packed lower (i(i+1)/2 + j)."""
+    return _gen_x_struct("smm_gen_x_lower", A, Lp, mode, out, stream)
+
+
+def _packed_order(name: str, t: torch.Tensor) -> int:
+    p = t.numel()
+    N = int((-1 + (1 + 8 * p) ** 0.5) // 2)
+    if N * (N + 1) // 2 != p:
+        raise ValueError(f"{name} has {p} elements, not a packed triangle")
+    return N
+
+
+def lower_left(Lp: torch.Tensor, B: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+               stream=None) -> torch.Tensor:
+    """C = L @ B with L lower triangular given packed lower."""
+    B = _check_f32("B", B)
+    N, ncols = B.shape
+    Lp = _check_f32("L", Lp, N * (N + 1) // 2)
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_lower_left_workspace_size(N, ncols, m), B.device)
+    C = _out(out, (N, ncols), B)
+    _lib.check(L.smm_lower_left(_ptr(Lp), _ptr(B), _ptr(C), N, ncols, m, ws, wsb, _stream_ptr(stream)),
+               "smm_lower_left")
+    return C
+
+
+def lower_x_lower(L1: torch.Tensor, L2: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
+                  stream=None) -> torch.Tensor:
+    """C = L1 @ L2, both lower triangular given packed lower."""
+    L1 = _check_f32("L1", L1)
+    N = _packed_order("L1", L1)
+    L2 = _check_f32("L2", L2, L1.numel())
+    C = _out(out, (N, N), L1)
+    _lib.check(_lib.load().smm_lower_x_lower(_ptr(L1), _ptr(L2), _ptr(C), N, _mode(mode), _stream_ptr(stream)),
+               "smm_lower_x_lower")
+    return C
+
+
 def symm_x_symm(S1: torch.Tensor, S2: torch.Tensor, mode: str = "3xtf32", out: Optional[torch.Tensor] = None,
                 stream=None) -> torch.Tensor:
     """C = S1 @ S2, both symmetric given packed upper."""

@@ -189,9 +189,34 @@ int smm_gen_x_upper(const float* A, const float* U_packed, float* C, int M, int 
 int smm_gen_x_symm(const float* A, const float* S_packed, float* C, int M, int N, int mode, void* ws,
                    size_t ws_bytes, void* stream);
 
+/* C(M x N) = A(M x N) L(N x N, packed lower, idx(i,j) = i(i+1)/2 + j).
+ * Replaces the DSL's GeneralMatrix @ LowerTriangularMatrix, which the
+ * reference implements only in its CPU AVX backend
+ * (src/dsl/codegen_multiply_avx.py:546-642).  K-blocks above a column tile's
+ * diagonal are never visited.  Workspace: smm_gen_x_struct_workspace_size. */
+int smm_gen_x_lower(const float* A, const float* L_packed, float* C, int M, int N, int mode, void* ws,
+                    size_t ws_bytes, void* stream);
+
 /* C(N x N) = S1 S2, both packed upper symmetric.  Replaces kernel_symm_x_symm
  * (src/dsl/codegen_cuda.py:1340-1613).  No workspace. */
 int smm_symm_x_symm(const float* S1_packed, const float* S2_packed, float* C, int N, int mode, void* stream);
+
+/* ---- lower-triangular operands (packed lower, idx(i,j) = i(i+1)/2 + j) ---- */
+
+size_t smm_lower_left_workspace_size(int N, int ncols, int mode);
+
+/* C(N x ncols) = L B, L packed lower.  The left-side counterpart of
+ * smm_upper_left (the DSL's LowerTriangularMatrix @ GeneralMatrix; the
+ * reference's lower-triangular layout is src/dsl/layout_functions.py:25-36).
+ * K-blocks right of a row tile's diagonal are never visited. */
+int smm_lower_left(const float* L_packed, const float* B, float* C, int N, int ncols, int mode, void* ws,
+                   size_t ws_bytes, void* stream);
+
+/* C(N x N) = L1 L2, both packed lower.  Replaces the DSL's
+ * LowerTriangularMatrix @ LowerTriangularMatrix of the reference's CPU AVX
+ * backend (src/dsl/codegen_multiply_avx.py:644-923).  Output tiles wholly
+ * above the diagonal are written as zeros without a K loop.  No workspace. */
+int smm_lower_x_lower(const float* L1_packed, const float* L2_packed, float* C, int N, int mode, void* stream);
 
 /* ---- elementwise sums and storage converters (HBM-bound, bit-exact) ---- */
 

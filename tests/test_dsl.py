@@ -106,13 +106,17 @@ def recorder(monkeypatch):
     (GeneralMatrix, SymmetricMatrix, "gen_x_symm"),
     (GeneralMatrix, UpperTriangularMatrix, "gen_x_upper"),
     (SymmetricMatrix, SymmetricMatrix, "symm_x_symm"),
+    (GeneralMatrix, LowerTriangularMatrix, "gen_x_lower"),
+    (LowerTriangularMatrix, GeneralMatrix, "lower_left"),
+    (LowerTriangularMatrix, LowerTriangularMatrix, "lower_x_lower"),
 ])
 def test_lowering_table(recorder, lhs, rhs, entry):
     n = Var("n")
     nv = 4
     L, R = lhs((n, n), "A"), rhs((n, n), "B")
     sizes = {GeneralMatrix: nv * nv, DiagonalMatrix: nv, UpperTriangularMatrix: nv * (nv + 1) // 2,
-             SymmetricMatrix: nv * (nv + 1) // 2, ToeplitzMatrix: 2 * nv - 1}
+             SymmetricMatrix: nv * (nv + 1) // 2, ToeplitzMatrix: 2 * nv - 1,
+             LowerTriangularMatrix: nv * (nv + 1) // 2}
     inputs = {"n": nv, "A": np.ones(sizes[lhs], np.float32), "B": np.ones(sizes[rhs], np.float32)}
     out, ms, gflops = RC.run([L @ R], inputs, "cuda", GeneralMatrix((n, n), "C"))
     assert list(out) == ["C"] and out["C"].numel() == nv * nv
@@ -125,8 +129,8 @@ def test_lowering_table(recorder, lhs, rhs, entry):
 def test_unsupported_pair_raises(recorder):
     n = Var("n")
     with pytest.raises(NotImplementedError):
-        RC.run([LowerTriangularMatrix((n, n), "A") @ GeneralMatrix((n, n), "B")],
-               {"n": 2, "A": np.ones(3, np.float32), "B": np.ones(4, np.float32)})
+        RC.run([ToeplitzMatrix((n, n), "A") @ ToeplitzMatrix((n, n), "B")],
+               {"n": 2, "A": np.ones(3, np.float32), "B": np.ones(3, np.float32)})
 
 
 def test_non_cuda_backend_rejected(recorder):
