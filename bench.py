@@ -15,8 +15,12 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
   diag      weak scaling: every rank scales its own 8192 x 8192 row slab;
             no collective on the data path (the rows are independent).
   others    strong scaling: the output is split into row slabs (equal-work
-            boundaries for the triangular operand); the shared right operand
-            B is broadcast from rank 0 each step inside the timed region.
+            boundaries for the triangular operand); the shared operand B (S
+            and B for A S B) is broadcast from rank 0 each step inside the
+            timed region, double-buffered so that the broadcast for the next
+            step overlaps this step's compute; the line also carries the
+            compute-only time.  A S B computes row slabs of X = S B, all-gathers
+            X, then row slabs of A X.
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launching stream, max over
@@ -270,6 +274,39 @@ def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
 
 
 # ---------------------------------------------------------------- our arm
+class SharedOperandPipeline:
+    """Double-buffered NCCL broadcast of the operands every rank needs (held
+    by rank 0): step i computes with buffer i % 2 while the broadcast for step
+    i+1 fills the other buffer on a side stream.  Every rank issues the same
+    collectives in the same order."""
+
+    def __init__(self, shared, stream):
+        import torch
+        self.torch = torch
+        self.bufs = [list(shared), [t.clone() for t in shared]]
+        self.stream = stream
+        self.comm = torch.cuda.Stream()
+        self.done = [torch.cuda.Event(), torch.cuda.Event()]
+        self.works = [None, None]
+        self.i = 0
+        self._issue(0)
+
+    def _issue(self, idx):
+        import torch.distributed as dist
+        with self.torch.cuda.stream(self.comm):
+            self.comm.wait_event(self.done[idx])  # buffer idx no longer read by compute
+            self.works[idx] = [dist.broadcast(t, src=0, async_op=True) for t in self.bufs[idx]]
+
+    def step(self, compute):
+        idx = self.i % 2
+        for w in self.works[idx]:
+            w.wait()  # the compute stream waits for this buffer's broadcast
+        compute(self.bufs[idx])
+        self.done[idx].record(self.stream)
+        self._issue(1 - idx)
+        self.i += 1
+
+
 def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
@@ -305,7 +342,13 @@ def run_ours(args, rank, world, local):
     d_in = [torch.from_numpy(x).cuda() for x in h_in]
 
     from cpp1_b200.multigpu import row_slabs, slab_useful_flops
-    bounds = row_slabs(n, world, triangular=(op == "upper")) if op not in HBM_OPS else None
+    if op in HBM_OPS:
+        bounds = None
+    elif op == "sandwich":
+        from cpp1_b200.multigpu import uniform_shares
+        bounds = uniform_shares(n, world)
+    else:
+        bounds = row_slabs(n, world, triangular=(op == "upper"))
     r0, r1 = (bounds[rank], bounds[rank + 1]) if bounds else (0, n)
     nrows = r1 - r0
     out = torch.empty((nrows, n), dtype=torch.float32, device="cuda")
@@ -329,53 +372,72 @@ def run_ours(args, rank, world, local):
             _lib.check(L.smm_add_struct(A.data_ptr(), S.data_ptr(), _lib.STRUCTS["symm"], out.data_ptr(), n, sp),
                        "add")
         units_per_rank_call = hbm_bytes(op, n)
-    elif op == "gemm":
-        A, B = d_in
-        ws, wsb = ws_for(L.smm_gemm_workspace_size(nrows, n, n, m))
-
-        def step():
-            if world > 1:
-                dist.broadcast(B, src=0)
-            Ap = A.data_ptr() + r0 * n * 4
-            _lib.check(L.smm_gemm(Ap, B.data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
-        units_per_rank_call = 2 * nrows * n * n
-    elif op == "upper":
-        U, B = d_in
-        ws, wsb = ws_for(L.smm_upper_left_workspace_size(n, n, _lib.FMT_PACKED, m))
-
-        def step():
-            if world > 1:
-                dist.broadcast(B, src=0)
-            _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, B.data_ptr(), out.data_ptr(), n, n, r0,
-                                             nrows, m, ws, wsb, sp), "upper")
-        units_per_rank_call = slab_useful_flops("upper", n, r0, r1)
-    elif op == "sandwich":
-        A, S, B = d_in
-        X = torch.empty((n, n), dtype=torch.float32, device="cuda")
-        ws, wsb = ws_for(L.smm_gemm_workspace_size(nrows, n, n, m))
-        wsx, wsxb = None, 0
-
-        def step():
-            if world > 1:
-                dist.broadcast(S, src=0)
-                dist.broadcast(B, src=0)
-            # X = S B on every rank is redundant work at G > 1; the slab
-            # variant of the sandwich computes only this rank's rows of A S B.
-            _lib.check(L.smm_symm_left(S.data_ptr(), B.data_ptr(), X.data_ptr(), n, n, m, ws, wsb, sp), "symm")
-            Ap = A.data_ptr() + r0 * n * 4
-            _lib.check(L.smm_gemm(Ap, X.data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
-        units_per_rank_call = (4 * n ** 3) // world
     else:
-        g, B = d_in
-        ws, wsb = ws_for(L.smm_toeplitz_left_workspace_size(n, n, m))
+        # Contractions: compute(shared) runs this rank's row slab with the
+        # shared operands (B; S and B for the sandwich).  At G > 1 they are
+        # broadcast from rank 0 every step, double-buffered: the broadcast for
+        # step i+1 runs on a side stream while step i computes.
+        if op == "gemm":
+            A, B = d_in
+            shared0 = [B]
+            ws, wsb = ws_for(L.smm_gemm_workspace_size(nrows, n, n, m))
 
-        def step():
-            if world > 1:
-                dist.broadcast(B, src=0)
-            _lib.check(L.smm_toeplitz_left_rows(g.data_ptr(), B.data_ptr(), out.data_ptr(), n, n, r0, nrows, m, ws,
-                                                wsb, sp), "toeplitz")
-        units_per_rank_call = 2 * nrows * n * n
+            def compute(sh):
+                Ap = A.data_ptr() + r0 * n * 4
+                _lib.check(L.smm_gemm(Ap, sh[0].data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+            units_per_rank_call = 2 * nrows * n * n
+        elif op == "upper":
+            U, B = d_in
+            shared0 = [B]
+            ws, wsb = ws_for(L.smm_upper_left_workspace_size(n, n, _lib.FMT_PACKED, m))
 
+            def compute(sh):
+                _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, sh[0].data_ptr(), out.data_ptr(), n,
+                                                 n, r0, nrows, m, ws, wsb, sp), "upper")
+            units_per_rank_call = slab_useful_flops("upper", n, r0, r1)
+        elif op == "sandwich":
+            A, S, B = d_in
+            shared0 = [S, B]
+            from cpp1_b200.multigpu import uniform_shares, allgather_rows
+            xb = uniform_shares(n, world)
+            x0, x1 = xb[rank], xb[rank + 1]
+            per = xb[1] - xb[0]
+            X = torch.empty((max(per * world, n), n), dtype=torch.float32, device="cuda")
+            X_share = torch.empty((per, n), dtype=torch.float32, device="cuda")
+            ws, wsb = ws_for(max(L.smm_gemm_workspace_size(nrows, n, n, m), L.smm_symm_left_workspace_size(n, n, m)))
+
+            def compute(sh):
+                # X rows [x0, x1) = S[x0:x1] B on this rank, X all-gathered,
+                # then this rank's rows of C = A X: no work is repeated.
+                if world > 1:
+                    if x1 > x0:
+                        _lib.check(L.smm_symm_left_rows(sh[0].data_ptr(), sh[1].data_ptr(), X_share.data_ptr(), n, n,
+                                                        x0, x1 - x0, m, ws, wsb, sp), "symm")
+                    allgather_rows(X_share, world, n, out=X)
+                else:
+                    _lib.check(L.smm_symm_left(sh[0].data_ptr(), sh[1].data_ptr(), X.data_ptr(), n, n, m, ws, wsb,
+                                               sp), "symm")
+                if nrows > 0:
+                    Ap = A.data_ptr() + r0 * n * 4
+                    _lib.check(L.smm_gemm(Ap, X.data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+            units_per_rank_call = (4 * n ** 3) // world
+        else:
+            g, B = d_in
+            shared0 = [B]
+            ws, wsb = ws_for(L.smm_toeplitz_left_workspace_size(n, n, m))
+
+            def compute(sh):
+                _lib.check(L.smm_toeplitz_left_rows(g.data_ptr(), sh[0].data_ptr(), out.data_ptr(), n, n, r0, nrows,
+                                                    m, ws, wsb, sp), "toeplitz")
+            units_per_rank_call = 2 * nrows * n * n
+        if world > 1:
+            pipe = SharedOperandPipeline(shared0, stream)
+
+            def step():
+                pipe.step(compute)
+        else:
+            def step():
+                compute(shared0)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -398,6 +460,26 @@ def run_ours(args, rank, world, local):
     ms = max_over_ranks(ms_local, world)
     ms_per_step = ms / args.steps
 
+    # ---- G > 1: the same steps without the operand broadcasts (the
+    # sandwich keeps its X all-gather, part of the algorithm), so the line
+    # shows compute-only and broadcast-inclusive times side by side.
+    multi = None
+    if world > 1 and op not in HBM_OPS:
+        barrier(world)
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(args.steps):
+            compute(shared0)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms_c = max_over_ranks(c0.elapsed_time(c1), world) / args.steps
+        multi = {"compute_only_ms_per_step": round(ms_c, 4), "broadcast_inclusive_ms_per_step": round(ms_per_step, 4),
+                 "broadcast_bytes_per_step": int(sum(t.numel() * 4 for t in shared0)),
+                 "overlap": "broadcast of step i+1 on a side stream during step i (double-buffered operands)",
+                 "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)]}
+
     total_units = units_per_rank_call * world if op in HBM_OPS else (
         n * n * (n + 1) if op == "upper" else (4 * n ** 3 if op == "sandwich" else 2 * n ** 3))
     scale = 1e9 if op in HBM_OPS else 1e12
@@ -418,6 +500,7 @@ def run_ours(args, rank, world, local):
                    "l2": "inputs larger than L2 (126 MB): no flush needed"},
         "roofline": roof,
         "gpu_launches": int(launches),
+        **({"multi_gpu": multi} if multi else {}),
         "clocks": clk.summary(),
     }
     return res, d_in, h_in
@@ -522,6 +605,126 @@ def e2e_ours(args, h_in, n):
             "api": "C ABI with pinned host buffers" + (" (smm_diag_rows_host)" if op == "diag" else " via cpp1_b200.ops")}
 
 
+def e2e_dist(args, h_in, n, rank, world):
+    """Host-buffer end to end at G > 1 for the contractions.  Every rank copies
+    only its share of the host inputs over its own PCIe link: its row slab of
+    the left operand (the whole 128 KiB generator for T B) and 1/G of the rows
+    of B (for the sandwich also 1/G of packed S).  The shared operands are
+    assembled by NVLink all-gathers, each rank computes its slab and copies
+    its rows of C back to the host.  Wall time per step, max over ranks."""
+    import torch
+    from cpp1_b200 import _lib, ops
+    from cpp1_b200.multigpu import allgather_rows, row_slabs, uniform_shares
+    L = _lib.load()
+    op = args.op
+    m = _lib.MODES[args.mode]
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream or None
+    dev = torch.device("cuda", torch.cuda.current_device())
+    bounds = uniform_shares(n, world) if op == "sandwich" else row_slabs(n, world, triangular=(op == "upper"))
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    nrows = r1 - r0
+    sb = uniform_shares(n, world)
+    s0, s1 = sb[rank], sb[rank + 1]
+    per = sb[1] - sb[0]
+
+    def pin(x):
+        return torch.from_numpy(np.ascontiguousarray(x)).pin_memory()
+
+    Bh = h_in[-1]  # B is the last input of every contraction
+    hB = pin(Bh[s0:s1])
+    B_share = torch.zeros((per, n), dtype=torch.float32, device=dev)
+    B_full = torch.empty((per * world, n), dtype=torch.float32, device=dev)
+    C = torch.empty((max(nrows, 1), n), dtype=torch.float32, device=dev)
+    hC = torch.empty((nrows, n), dtype=torch.float32).pin_memory()
+    need = max(L.smm_gemm_workspace_size(max(nrows, 1), n, n, m), L.smm_symm_left_workspace_size(n, n, m),
+               L.smm_upper_left_workspace_size(n, n, _lib.FMT_PACKED, m), L.smm_toeplitz_left_workspace_size(n, n, m))
+    wbuf = ops.workspace(need, dev)
+    ws, wsb = (wbuf.data_ptr(), wbuf.numel()) if wbuf is not None else (None, 0)
+    h2d = Bh.nbytes
+    if op in ("gemm", "sandwich"):
+        hA = pin(h_in[0][r0:r1])
+        A = torch.empty((max(nrows, 1), n), dtype=torch.float32, device=dev)
+        h2d += h_in[0].nbytes
+    if op == "gemm":
+        def load():
+            A[:nrows].copy_(hA, non_blocking=True)
+
+        def comp(Bf):
+            _lib.check(L.smm_gemm(A.data_ptr(), Bf.data_ptr(), C.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+    elif op == "upper":
+        Up = h_in[0]
+        lo, hi = r0 * n - r0 * (r0 - 1) // 2, r1 * n - r1 * (r1 - 1) // 2  # packed rows [r0, r1)
+        hU = pin(Up[lo:hi])
+        U = torch.empty(Up.size, dtype=torch.float32, device=dev)
+        h2d += Up.nbytes
+
+        def load():
+            U[lo:hi].copy_(hU, non_blocking=True)
+
+        def comp(Bf):
+            _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, Bf.data_ptr(), C.data_ptr(), n, n, r0,
+                                             nrows, m, ws, wsb, sp), "upper")
+    elif op == "toeplitz":
+        hg = pin(h_in[0])
+        g = torch.empty(h_in[0].size, dtype=torch.float32, device=dev)
+        h2d += world * h_in[0].nbytes
+
+        def load():
+            g.copy_(hg, non_blocking=True)
+
+        def comp(Bf):
+            _lib.check(L.smm_toeplitz_left_rows(g.data_ptr(), Bf.data_ptr(), C.data_ptr(), n, n, r0, nrows, m, ws,
+                                                wsb, sp), "toeplitz")
+    else:
+        Sh = h_in[1]
+        pb = uniform_shares(Sh.size, world)
+        sper = pb[1] - pb[0]
+        hS = pin(Sh[pb[rank]:pb[rank + 1]])
+        S_share = torch.zeros((sper, 1), dtype=torch.float32, device=dev)
+        S_full = torch.empty((sper * world, 1), dtype=torch.float32, device=dev)
+        X_share = torch.empty((per, n), dtype=torch.float32, device=dev)
+        X_full = torch.empty((per * world, n), dtype=torch.float32, device=dev)
+        h2d += Sh.nbytes
+
+        def load():
+            A[:nrows].copy_(hA, non_blocking=True)
+            S_share[:pb[rank + 1] - pb[rank]].copy_(hS.view(-1, 1), non_blocking=True)
+
+        def comp(Bf):
+            Sf = allgather_rows(S_share, world, Sh.size, out=S_full)
+            if s1 > s0:
+                _lib.check(L.smm_symm_left_rows(Sf.data_ptr(), Bf.data_ptr(), X_share.data_ptr(), n, n, s0, s1 - s0,
+                                                m, ws, wsb, sp), "symm")
+            Xf = allgather_rows(X_share, world, n, out=X_full)
+            if nrows > 0:
+                _lib.check(L.smm_gemm(A.data_ptr(), Xf.data_ptr(), C.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+
+    def step():
+        load()
+        B_share[:s1 - s0].copy_(hB, non_blocking=True)
+        Bf = allgather_rows(B_share, world, n, out=B_full)
+        comp(Bf)
+        if nrows > 0:
+            hC.copy_(C[:nrows], non_blocking=True)
+        stream.synchronize()
+
+    steps = 2 if op == "toeplitz" else 5
+    step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize()
+    dt = max_over_ranks(time.perf_counter() - t0, world) / steps
+    units = {"gemm": 2 * n ** 3, "upper": n * n * (n + 1), "sandwich": 4 * n ** 3, "toeplitz": 2 * n ** 3}[op]
+    return {"value": round(units / dt / 1e12, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(n * n * 4), "steps": steps, "ms_per_step": round(dt * 1e3, 3),
+            "api": "C ABI with pinned host buffers; per-rank input shares over each GPU's PCIe link, "
+                   "NVLink all-gather of the shared operands (whole-job bytes)"}
+
+
 # ---------------------------------------------------------------- reference arm
 def host_threads() -> int:
     """Host cores this process may use (its CPU affinity)."""
@@ -595,11 +798,15 @@ def main():
     res, d_in, h_in = run_ours(args, rank, world, local)
     n = args.n or WORKLOADS[args.op]["N"]
     if not args.no_e2e:
-        # Every rank runs the same host-buffer path; rank 0 reports its own
-        # (per-GPU) rate times the rank count for the whole job at weak
-        # scaling, or the single-GPU rate otherwise.
+        # HBM-bound ops (weak scaling): every rank runs the single-GPU
+        # host-buffer path on its own problem and the whole job is the
+        # slowest rank's rate times the rank count.  Contractions at G > 1:
+        # one distributed product over per-rank input shares (e2e_dist).
         del d_in
-        e2e = e2e_ours(args, h_in, n)
+        if world > 1 and args.op not in HBM_OPS:
+            e2e = e2e_dist(args, h_in, n, rank, world)
+        else:
+            e2e = e2e_ours(args, h_in, n)
         if world > 1 and args.op in HBM_OPS:
             e2e["value"] = round(max_over_ranks(-e2e["value"], world) * -1 * world, 3)
         res["e2e"] = e2e

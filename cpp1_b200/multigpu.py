@@ -128,3 +128,56 @@ def gather_rows(slab, world: int, shapes: Sequence[int], ncols: int):
     parts = [torch.empty_like(pad) for _ in range(world)]
     dist.all_gather(parts, pad)
     return torch.cat([p[:r] for p, r in zip(parts, shapes)], dim=0)
+
+
+# ---------------------------------------------------------------- shares and row all-gather
+def uniform_shares(n: int, world: int) -> List[int]:
+    """Boundaries of `world` equal row shares of n rows (the last ones may be
+    short or empty): share g is rows [b[g], b[g+1]), each at most ceil(n/world)."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    per = -(-n // world) if n > 0 else 0
+    return [min(n, g * per) for g in range(world)] + [n]
+
+
+def allgather_rows(share, world: int, n: int, out=None):
+    """Assemble an n-row matrix from every rank's row share (uniform_shares
+    boundaries) over torch.distributed: each rank contributes its share padded
+    to ceil(n/world) rows; the result is the first n rows.  `out`, if given,
+    must hold world * ceil(n/world) rows (it is filled in place and its first
+    n rows are returned).  NCCL gathers straight into `out`; other backends
+    (gloo, in the CPU tests) gather a list and copy."""
+    import torch
+    import torch.distributed as dist
+    per = -(-n // world) if n > 0 else 0
+    cols = share.shape[1] if share.dim() == 2 else 1
+    if share.shape[0] < per:
+        pad = torch.zeros((per, cols), dtype=share.dtype, device=share.device)
+        pad[: share.shape[0]] = share.view(-1, cols)
+        share = pad
+    if out is None:
+        out = torch.empty((world * per, cols), dtype=share.dtype, device=share.device)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(out, share.contiguous())
+    else:
+        parts = list(out.view(world, per, cols).unbind(0))
+        gathered = [torch.empty_like(share) for _ in range(world)]
+        dist.all_gather(gathered, share.contiguous())
+        for p, g in zip(parts, gathered):
+            p.copy_(g)
+    return out[:n]
+
+
+def distributed_sandwich(x_rows: Callable[[int, int], object], c_rows: Callable[[object, int, int], object],
+                         rank: int, world: int, n: int, x_out=None):
+    """C = A S B by row slabs without redundant work: this rank computes rows
+    [r0, r1) of X = S B (x_rows(r0, r1)), the X row shares are all-gathered
+    (every rank then holds all of X), and this rank computes its rows of
+    C = A X (c_rows(X, r0, r1)).  Shares are uniform_shares(n, world); the
+    caller has already made S and B available on every rank.  Returns this
+    rank's C rows."""
+    b = uniform_shares(n, world)
+    r0, r1 = b[rank], b[rank + 1]
+    X = x_rows(r0, r1)
+    X_full = allgather_rows(X, world, n, out=x_out) if world > 1 else X
+    return c_rows(X_full, r0, r1)

@@ -88,3 +88,56 @@ def test_two_rank_broadcast_slab_gather_gloo():
             p.join(120)
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         assert results["ok"], results
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_uniform_shares_cover_rows(world):
+    for n in (0, 1, 5, 4096, 4099):
+        b = MG.uniform_shares(n, world)
+        assert b[0] == 0 and b[-1] == n and len(b) == world + 1
+        assert all(b[i] <= b[i + 1] for i in range(world))
+        assert max(b[i + 1] - b[i] for i in range(world)) <= -(-n // world) if n else True
+
+
+def _sandwich_worker(rank, world, port, results):
+    import oracle as O
+    from cpp1_b200 import workloads as W
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = 97  # not a multiple of the rank count: the last share is short
+        w = W.make_sandwich(n, seed=4)
+        S = W.unpack_symmetric(w["S"], n).astype(np.float64)
+        A, B = w["A"].astype(np.float64), w["B"].astype(np.float64)
+
+        def x_rows(r0, r1):  # stands in for the GPU slab kernel X[r0:r1] = S[r0:r1] B
+            return torch.from_numpy((S[r0:r1] @ B).astype(np.float32))
+
+        def c_rows(X, r0, r1):
+            return torch.from_numpy((A[r0:r1] @ X.numpy().astype(np.float64)).astype(np.float32))
+
+        C = MG.distributed_sandwich(x_rows, c_rows, rank, world, n)
+        b = MG.uniform_shares(n, world)
+        Cs = MG.allgather_rows(C, world, n)
+        if rank == 0:
+            ref = (A @ (S @ B).astype(np.float32).astype(np.float64)).astype(np.float32)
+            results["ok"] = bool(np.allclose(Cs.numpy(), ref, rtol=1e-5, atol=1e-4))
+            results["rows"] = b
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_sandwich_slabs_gloo():
+    world = 2
+    port = _free_port()
+    with mp.Manager() as m:
+        results = m.dict()
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=_sandwich_worker, args=(r, world, port, results)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        assert results["ok"], results
