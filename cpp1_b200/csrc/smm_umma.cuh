@@ -728,32 +728,29 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     int folded = 0;  // chunks already added into the running sum
 
     // Add chunk f's accumulator (this warp's 32 lanes x kHalf columns) into
-    // the running sum, a quarter tile (kHalf/2 columns) at a time so the
-    // registers it needs stay small, then release the accumulator to the MMA.
+    // the running sum, 32 columns at a time (both loads in flight before one
+    // wait, so registers stay few and the MMA waits for 4 round trips, not
+    // one per 16 columns), then release the accumulator to the MMA.
     auto fold = [&](int f) -> bool {
       if (!__all_sync(0xffffffffu, mbar_wait(acc_full, f & 1, wxf))) return false;
       tc_fence_after_sync();
-      constexpr int kQ = kHalf / 2;
+      constexpr int kQ = 32;
 #pragma unroll 1
-      for (int hq = 0; hq < 2; ++hq) {
-        uint32_t a[kQ];
-#pragma unroll
-        for (int c = 0; c < kQ; c += 16)
-          tmem_ld_32x32b_x16(acc_col + hq * kQ + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
+      for (int c0 = 0; c0 < kHalf; c0 += kQ) {
+        uint32_t a[kQ], r[kQ];
+        tmem_ld_32x32b_x16(acc_col + c0, *reinterpret_cast<uint32_t(*)[16]>(a));
+        tmem_ld_32x32b_x16(acc_col + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(a + 16));
+        if (f > 0) {
+          tmem_ld_32x32b_x16(sum_col + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld_32x32b_x16(sum_col + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+        }
         tmem_wait_ld();
         if (f > 0) {
 #pragma unroll
-          for (int c = 0; c < kQ; c += 16) {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(sum_col + hq * kQ + c, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) a[c + j] = __float_as_uint(__uint_as_float(a[c + j]) + __uint_as_float(r[j]));
-          }
+          for (int j = 0; j < kQ; ++j) a[j] = __float_as_uint(__uint_as_float(a[j]) + __uint_as_float(r[j]));
         }
-#pragma unroll
-        for (int c = 0; c < kQ; c += 16)
-          tmem_st_32x32b_x16(sum_col + hq * kQ + c, *reinterpret_cast<uint32_t(*)[16]>(a + c));
+        tmem_st_32x32b_x16(sum_col + c0, *reinterpret_cast<uint32_t(*)[16]>(a));
+        tmem_st_32x32b_x16(sum_col + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(a + 16));
       }
       tmem_wait_st();
       tc_fence_before_sync();
