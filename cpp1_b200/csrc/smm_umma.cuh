@@ -641,57 +641,72 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // The issuing thread is the pipeline's serial step: per stage it only
+    // adds small offsets to precomputed descriptor words, tries the stage's
+    // barrier once (the slow bounded wait only when it is not ready yet) and
+    // commits to precomputed barrier addresses; no 64-bit arithmetic and no
+    // divisions in the loop.
     if (lane == 0 && leader) {
+      const uint64_t dA0 = make_smem_desc(smem_u32(a_hi(0)), 16, 512, kLayoutSw64);
+      const uint64_t dB0 = make_smem_desc(smem_u32(b_hi(0)), MT::kBoxBytes, MT::kBSbo, MT::kBLayout);
+      const uint32_t a_lo0 = static_cast<uint32_t>(dA0), a_hi32 = static_cast<uint32_t>(dA0 >> 32);
+      const uint32_t b_lo0 = static_cast<uint32_t>(dB0), b_hi32 = static_cast<uint32_t>(dB0 >> 32);
+      // Start-address field steps (16-byte units): a k-step along an A row
+      // (32 B), along B (kBStepBytes), hi -> lo tile, one stage.
+      constexpr uint32_t kAKStep = 32 >> 4, kBKStep = MT::kBStepBytes >> 4;
+      constexpr uint32_t kLoOff = (kATileBytes + kBTile) >> 4;
+      constexpr uint32_t kStageOff = kStage >> 4;
+      const uint32_t wait0 = smem_u32(kXform ? &ready[0] : &full[0]);
+      uint32_t empty_c[PAIR ? 2 : 1], accf_c[PAIR ? 2 : 1];
+#pragma unroll
+      for (int r = 0; r < (PAIR ? 2 : 1); ++r) {
+        empty_c[r] = PAIR ? in_cta(&empty[0], r) : smem_u32(&empty[0]);
+        accf_c[r] = PAIR ? in_cta(acc_full, r) : smem_u32(acc_full);
+      }
+      int s = 0, kc = 0, chunk = 0, issued = 0;
+      uint32_t ph = 0, soff = 0;
       for (int i = 0; i < num_kb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1;
-        if (!mbar_wait(kXform ? &ready[s] : &full[s], ph, wmma)) break;
+        if (!mbar_try_wait(wait0 + 8u * s, ph) && !mbar_wait(kXform ? &ready[s] : &full[s], ph, wmma)) break;
         // 3xTF32: chunk c starts from zero once chunk c-1 has been copied out.
-        const bool chunk_start = SPLIT3 ? (i % kChunk == 0) : (i == 0);
+        const bool chunk_start = SPLIT3 ? (kc == 0) : (i == 0);
         if (SPLIT3 && chunk_start && i > 0) {
-          if (!mbar_wait(acc_empty, ((i / kChunk) - 1) & 1, wmma)) break;
+          if (!mbar_wait(acc_empty, (chunk - 1) & 1, wmma)) break;
         }
         tc_fence_after_sync();
-        const uint32_t sa = smem_u32(a_hi(s));
-        const uint32_t sb = smem_u32(b_hi(s));
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
-          // A: K-major, 64-byte rows, 8-row groups 512 B apart; a k-step (8
-          // tf32 or 16 bf16) is 32 bytes along the row.
-          const uint64_t da = make_smem_desc(sa + kk * 32, 16, 512, kLayoutSw64);
-          // B: MN-major boxes kBoxBytes apart (LBO), k-rows 128 B apart in
-          // swizzle atoms kBSbo apart (SBO); a k-step is kBStepBytes.
-          const uint64_t db = make_smem_desc(sb + kk * MT::kBStepBytes, MT::kBoxBytes, MT::kBSbo, MT::kBLayout);
-          const uint32_t acc = (!chunk_start || kk > 0) ? 1u : 0u;
-          auto mma = [&](uint64_t x, uint64_t y, uint32_t accumulate) {
-            if constexpr (PAIR) {
-              if constexpr (MT::kBf16)
-                umma_f16_pair(tmem_base, x, y, kIdesc, accumulate);
-              else
-                umma_tf32_pair(tmem_base, x, y, kIdesc, accumulate);
-            } else {
-              if constexpr (MT::kBf16)
-                umma_f16(tmem_base, x, y, kIdesc, accumulate);
-              else
-                umma_tf32(tmem_base, x, y, kIdesc, accumulate);
-            }
-          };
-          mma(da, db, acc);
+          // A: K-major, 64-byte rows, 8-row groups 512 B apart; B: MN-major
+          // boxes kBoxBytes apart (LBO), atoms kBSbo apart (SBO).
+          const uint32_t al = a_lo0 + soff + kk * kAKStep;
+          const uint32_t bl = b_lo0 + soff + kk * kBKStep;
+          umma_lohi<PAIR, MT::kBf16>(tmem_base, al, a_hi32, bl, b_hi32, kIdesc, (!chunk_start || kk > 0) ? 1u : 0u);
           if constexpr (SPLIT3) {
-            const uint32_t sal = smem_u32(a_lo(s));
-            const uint32_t sbl = smem_u32(b_lo(s));
-            const uint64_t dal = make_smem_desc(sal + kk * 32, 16, 512, kLayoutSw64);
-            const uint64_t dbl = make_smem_desc(sbl + kk * MT::kBStepBytes, MT::kBoxBytes, MT::kBSbo, MT::kBLayout);
-            mma(da, dbl, 1u);
-            mma(dal, db, 1u);
+            umma_lohi<PAIR, false>(tmem_base, al, a_hi32, bl + kLoOff, b_hi32, kIdesc, 1u);
+            umma_lohi<PAIR, false>(tmem_base, al + kLoOff, a_hi32, bl, b_hi32, kIdesc, 1u);
           }
         }
-        commit_all(&empty[s]);
+#pragma unroll
+        for (int r = 0; r < (PAIR ? 2 : 1); ++r) umma_commit_addr<PAIR>(empty_c[r] + 8u * s);
         if constexpr (SPLIT3) {
-          if (i % kChunk == kChunk - 1 || i == num_kb - 1) commit_all(acc_full);
+          if (kc == kChunk - 1 || i == num_kb - 1) {
+#pragma unroll
+            for (int r = 0; r < (PAIR ? 2 : 1); ++r) umma_commit_addr<PAIR>(accf_c[r]);
+          }
+          if (++kc == kChunk) {
+            kc = 0;
+            ++chunk;
+          }
         }
-        if (tr) p.trace[kTrMmas] = static_cast<uint32_t>(i + 1);
+        ++issued;
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+          soff = 0;
+        } else {
+          soff += kStageOff;
+        }
       }
+      if (tr) p.trace[kTrMmas] = static_cast<uint32_t>(issued);
       // Signals the epilogue; on abort it still fires once every MMA issued
       // so far has finished.  The issuer waits for it too (bounded, ignoring
       // the abort flag) so tensor memory is quiescent before it is freed.
