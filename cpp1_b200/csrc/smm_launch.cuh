@@ -17,7 +17,7 @@ struct Maps {
 template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR>
 int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
   auto kern = umma_gemm_kernel<AK, BK, MD, BN, STAGES, PAIR>;
-  constexpr int smem = umma_smem_bytes<PAIR ? BN / 2 : BN, MD == Mode::TF32x3, STAGES>();
+  constexpr int smem = umma_smem_bytes<AK, MD, PAIR ? BN / 2 : BN, STAGES>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
   static bool attr_set[64] = {};
   int dev = 0;
@@ -51,17 +51,15 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
   return SMM_OK;
 }
 
-// Stage counts fill ~192 KiB of shared memory (a pair CTA stages half the B
-// columns, so its stages are smaller and more of them fit).
+// Stage counts fill ~192 KiB of shared memory (umma_stages).
 template <AKind AK, BKind BK, int BN, bool PAIR>
 int launch_mode(int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
   constexpr int kCols = PAIR ? BN / 2 : BN;  // B columns per CTA
-  if (mode == SMM_MODE_3XTF32) {
-    constexpr int S = (kCols == 256) ? 4 : (kCols == 128 ? 6 : 8);
-    return launch_umma<AK, BK, Mode::TF32x3, BN, S, PAIR>(m, p, st);
-  }
-  if (mode == SMM_MODE_BF16) return launch_umma<AK, BK, Mode::BF16, BN, 8, PAIR>(m, p, st);
-  return launch_umma<AK, BK, Mode::TF32, BN, 8, PAIR>(m, p, st);
+  if (mode == SMM_MODE_3XTF32)
+    return launch_umma<AK, BK, Mode::TF32x3, BN, umma_stages<AK, Mode::TF32x3, kCols>(), PAIR>(m, p, st);
+  if (mode == SMM_MODE_BF16)
+    return launch_umma<AK, BK, Mode::BF16, BN, umma_stages<AK, Mode::BF16, kCols>(), PAIR>(m, p, st);
+  return launch_umma<AK, BK, Mode::TF32, BN, umma_stages<AK, Mode::TF32, kCols>(), PAIR>(m, p, st);
 }
 
 template <AKind AK, BKind BK>

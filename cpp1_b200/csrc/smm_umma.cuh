@@ -148,9 +148,30 @@ __host__ __device__ constexpr uint32_t tmem_cols() {
   return SPLIT3 ? (2 * BN <= 128 ? 128u : (2 * BN <= 256 ? 256u : 512u)) : (BN < 32 ? 32u : static_cast<uint32_t>(BN));
 }
 
-template <int BN, bool SPLIT3, int STAGES>
+// k-blocks (64 bytes of K each) per pipeline stage.  Two wherever the
+// two-block stage still fits three times into 192 KiB: every barrier round
+// trip, wait and commit of the serial MMA-issuing thread then covers 4 MMAs
+// per pass instead of 2 (each of those instructions costs that thread ~60
+// cycles, about half of a 2-MMA stage's tensor time in one-pass modes).
+// bf16 structured A, gathered through registers one k-block at a time,
+// keeps one.
+template <AKind AK, Mode MD, int BCOLS>
+__host__ __device__ constexpr int umma_subs() {
+  return (AK != AKind::Dense && AK != AKind::UpperDense && MD == Mode::BF16)
+             ? 1
+             : (3 * 2 * stage_bytes<BCOLS, MD == Mode::TF32x3>() <= 192 * 1024 ? 2 : 1);
+}
+// Pipeline stages: as many as fit into 192 KiB, at most 8.
+template <AKind AK, Mode MD, int BCOLS>
+__host__ __device__ constexpr int umma_stages() {
+  return (192 * 1024 / (umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3>())) > 8
+             ? 8
+             : 192 * 1024 / (umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3>());
+}
+template <AKind AK, Mode MD, int BCOLS, int STAGES>
 __host__ __device__ constexpr int umma_smem_bytes() {
-  return 1024 /*alignment slack*/ + STAGES * stage_bytes<BN, SPLIT3>() + 256 /*barriers etc*/;
+  return 1024 /*alignment slack*/ + STAGES * umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3>() +
+         256 /*barriers etc*/;
 }
 
 __device__ __forceinline__ long long packed_idx(long long i, long long j, long long n) {
@@ -477,7 +498,12 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   constexpr int KS = MT::kStageK;
   constexpr int kBCols = PAIR ? BN / 2 : BN;  // B columns staged by this CTA
   constexpr int kBTile = TileGeom<kBCols>::kBTileBytes;
-  constexpr int kStage = stage_bytes<kBCols, SPLIT3>();
+  // A stage holds kSubs k-blocks of KS: [A hi x kSubs | B hi x kSubs | A lo x
+  // kSubs | B lo x kSubs], each block in the one-block layouts below.
+  constexpr int kSubs = umma_subs<AK, MD, kBCols>();
+  constexpr int kStage = kSubs * stage_bytes<kBCols, SPLIT3>();
+  constexpr int kChunkS = kChunk / kSubs;  // chunk length in stages
+  static_assert(kChunk % kSubs == 0, "chunk of whole stages");
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
   constexpr bool kBTma = (BK == BKind::Dense);
   constexpr bool kACp = a_async_filled(AK, MD);
@@ -485,7 +511,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // when lo tiles are derived from the loaded ones (3xTF32); in a pair they
   // also relay stage completion to the leader.
   constexpr bool kXform = !kATma || !kBTma || SPLIT3 || PAIR;
-  constexpr uint32_t kTxBytes = (kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0);
+  constexpr uint32_t kTxBytes = kSubs * ((kATma ? kATileBytes : 0) + (kBTma ? kBTile : 0));
   constexpr uint32_t kTmemCols = tmem_cols<BN, SPLIT3>();
   constexpr uint32_t kIdesc = make_idesc(MT::kFmt, PAIR ? 2 * kBM : kBM, BN, /*a_mn=*/0, /*b_mn=*/1);
   constexpr int kHalf = BN / 2;  // columns per epilogue warp
@@ -504,9 +530,9 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   auto a_hi = [&](int s) { return smem + s * kStage; };
-  auto b_hi = [&](int s) { return smem + s * kStage + kATileBytes; };
-  auto a_lo = [&](int s) { return smem + s * kStage + kATileBytes + kBTile; };
-  auto b_lo = [&](int s) { return smem + s * kStage + 2 * kATileBytes + kBTile; };
+  auto b_hi = [&](int s) { return smem + s * kStage + kSubs * kATileBytes; };
+  auto a_lo = [&](int s) { return smem + s * kStage + kSubs * (kATileBytes + kBTile); };
+  auto b_lo = [&](int s) { return smem + s * kStage + kSubs * (2 * kATileBytes + kBTile); };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -549,9 +575,11 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // above it: the tile needs k >= n0 only.
   if constexpr (BK == BKind::UpperPacked) kb_end = min(kb_end, (n0 + BN - 1) / KS + 1);
   if constexpr (BK == BKind::LowerPacked) kb_begin = max(kb_begin, n0 / KS);
-  // Empty for a tile of L1 L2 wholly above the diagonal: it is written as zeros.
-  const int num_kb = max(kb_end - kb_begin, 0);
-  const int nch = SPLIT3 ? (num_kb + kChunk - 1) / kChunk : 1;
+  // Empty for a tile of L1 L2 wholly above the diagonal: it is written as
+  // zeros.  num_kb counts stages of kSubs k-blocks; a last stage reaching
+  // past kb_end multiplies zeros (past K, past a triangle's diagonal).
+  const int num_kb = (max(kb_end - kb_begin, 0) + kSubs - 1) / kSubs;
+  const int nch = SPLIT3 ? (num_kb + kChunkS - 1) / kChunkS : 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -620,12 +648,15 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         const uint32_t ph = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
         mbar_arrive_expect_tx(&full[s], kTxBytes);
-        const int k0 = (kb_begin + i) * KS;
-        if constexpr (kATma) tma_load_2d(a_hi(s), &tmA, &full[s], k0, m0);
-        if constexpr (kBTma) {
 #pragma unroll
-          for (int c = 0; c < kBCols / MT::kBoxCols; ++c)
-            tma_load_2d(b_hi(s) + c * MT::kBoxBytes, &tmB, &full[s], nb0 + MT::kBoxCols * c, k0);
+        for (int j = 0; j < kSubs; ++j) {
+          const int k0 = (kb_begin + i * kSubs + j) * KS;
+          if constexpr (kATma) tma_load_2d(a_hi(s) + j * kATileBytes, &tmA, &full[s], k0, m0);
+          if constexpr (kBTma) {
+#pragma unroll
+            for (int c = 0; c < kBCols / MT::kBoxCols; ++c)
+              tma_load_2d(b_hi(s) + j * kBTile + c * MT::kBoxBytes, &tmB, &full[s], nb0 + MT::kBoxCols * c, k0);
+          }
         }
         ++issued;
       }
@@ -654,7 +685,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
       // Start-address field steps (16-byte units): a k-step along an A row
       // (32 B), along B (kBStepBytes), hi -> lo tile, one stage.
       constexpr uint32_t kAKStep = 32 >> 4, kBKStep = MT::kBStepBytes >> 4;
-      constexpr uint32_t kLoOff = (kATileBytes + kBTile) >> 4;
+      constexpr uint32_t kLoOff = (kSubs * (kATileBytes + kBTile)) >> 4;
       constexpr uint32_t kStageOff = kStage >> 4;
       const uint32_t wait0 = smem_u32(kXform ? &ready[0] : &full[0]);
       uint32_t empty_c[PAIR ? 2 : 1], accf_c[PAIR ? 2 : 1];
@@ -674,12 +705,14 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         }
         tc_fence_after_sync();
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          // A: K-major, 64-byte rows, 8-row groups 512 B apart; B: MN-major
-          // boxes kBoxBytes apart (LBO), atoms kBSbo apart (SBO).
-          const uint32_t al = a_lo0 + soff + kk * kAKStep;
-          const uint32_t bl = b_lo0 + soff + kk * kBKStep;
-          umma_lohi<PAIR, MT::kBf16>(tmem_base, al, a_hi32, bl, b_hi32, kIdesc, (!chunk_start || kk > 0) ? 1u : 0u);
+        for (int q = 0; q < 2 * kSubs; ++q) {
+          // k-step q: block q/2, step q%2.  A: K-major, 64-byte rows, 8-row
+          // groups 512 B apart; B: MN-major boxes kBoxBytes apart (LBO),
+          // atoms kBSbo apart (SBO).
+          const int j = q >> 1, kk = q & 1;
+          const uint32_t al = a_lo0 + soff + j * (kATileBytes >> 4) + kk * kAKStep;
+          const uint32_t bl = b_lo0 + soff + j * (kBTile >> 4) + kk * kBKStep;
+          umma_lohi<PAIR, MT::kBf16>(tmem_base, al, a_hi32, bl, b_hi32, kIdesc, (!chunk_start || q > 0) ? 1u : 0u);
           if constexpr (SPLIT3) {
             umma_lohi<PAIR, false>(tmem_base, al, a_hi32, bl + kLoOff, b_hi32, kIdesc, 1u);
             umma_lohi<PAIR, false>(tmem_base, al + kLoOff, a_hi32, bl, b_hi32, kIdesc, 1u);
@@ -688,11 +721,11 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
 #pragma unroll
         for (int r = 0; r < (PAIR ? 2 : 1); ++r) umma_commit_addr<PAIR>(empty_c[r] + 8u * s);
         if constexpr (SPLIT3) {
-          if (kc == kChunk - 1 || i == num_kb - 1) {
+          if (kc == kChunkS - 1 || i == num_kb - 1) {
 #pragma unroll
             for (int r = 0; r < (PAIR ? 2 : 1); ++r) umma_commit_addr<PAIR>(accf_c[r]);
           }
-          if (++kc == kChunk) {
+          if (++kc == kChunkS) {
             kc = 0;
             ++chunk;
           }
@@ -724,7 +757,9 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
-        a_async_fill<AK>(p, a_hi(s), g_first, (kb_begin + i) * KS, ft);
+#pragma unroll
+        for (int j = 0; j < kSubs; ++j)
+          a_async_fill<AK>(p, a_hi(s) + j * kATileBytes, g_first, (kb_begin + i * kSubs + j) * KS, ft);
         cp_async_mbar_arrive_noinc(&full[s]);
       }
       // no copy may land after the CTA has exited (bounded: all in flight)
@@ -796,7 +831,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         // (the fold needs only the MMAs of chunk `folded`, whose stages are
         // all ready by now); a lag of STAGES would make the fold wait for a
         // TMA round trip started by the chunk's very last MMA.
-        if (SPLIT3 && folded < nch - 1 && i == (folded + 1) * kChunk + kFoldLag) {
+        if (SPLIT3 && folded < nch - 1 && i == (folded + 1) * kChunkS + kFoldLag) {
           if (!fold(folded)) return false;
           ++folded;
         }
@@ -805,9 +840,14 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         }
         // Warp-uniform outcome: tcgen05.ld/st are .sync.aligned.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) return false;
-        const int k0 = (kb_begin + i) * KS;
+        const int k0 = (kb_begin + i * kSubs) * KS;
+        // (register-gathered A only with one k-block per stage)
         if constexpr (!kATma && !kACp) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
-        if constexpr (!kBTma) b_build<BK, kBCols, MD>(p, b_hi(s), b_lo(s), k0, nb0, t);
+        if constexpr (!kBTma) {
+#pragma unroll 1
+          for (int j = 0; j < kSubs; ++j)
+            b_build<BK, kBCols, MD>(p, b_hi(s) + j * kBTile, b_lo(s) + j * kBTile, k0 + j * KS, nb0, t);
+        }
         if constexpr (SPLIT3) {
           // lo = x - tf32(x) of the TMA-loaded tiles, elementwise at the same
           // (swizzled) offsets.
@@ -820,8 +860,8 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
               out[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
             }
           };
-          if constexpr (kATma || kACp) lo_of(a_hi(s), a_lo(s), kATileBytes, t);
-          if constexpr (kBTma) lo_of(b_hi(s), b_lo(s), kBTile, t);
+          if constexpr (kATma || kACp) lo_of(a_hi(s), a_lo(s), kSubs * kATileBytes, t);
+          if constexpr (kBTma) lo_of(b_hi(s), b_lo(s), kSubs * kBTile, t);
         }
         fence_proxy_async_smem();
         __syncwarp();
