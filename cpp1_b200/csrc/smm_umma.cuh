@@ -149,17 +149,21 @@ __host__ __device__ constexpr uint32_t tmem_cols() {
 }
 
 // k-blocks (64 bytes of K each) per pipeline stage.  Two wherever the
-// two-block stage still fits three times into 192 KiB: every barrier round
-// trip, wait and commit of the serial MMA-issuing thread then covers 4 MMAs
-// per pass instead of 2 (each of those instructions costs that thread ~60
-// cycles, about half of a 2-MMA stage's tensor time in one-pass modes).
-// bf16 structured A, gathered through registers one k-block at a time,
-// keeps one.
+// two-block stage still fits three times into 192 KiB (four for the one-pass
+// modes on TMA-fed operands): every barrier round trip, wait and commit of
+// the serial MMA-issuing thread then covers 4 (8) MMAs per pass instead of 2.
+// Each of those instructions costs that thread ~60 cycles, about half of a
+// 2-MMA stage's tensor time in one-pass modes.  3xTF32 with three blocks (two
+// stages) measured slower.  bf16 structured A, gathered through registers one
+// k-block at a time, keeps one.
 template <AKind AK, Mode MD, int BCOLS>
 __host__ __device__ constexpr int umma_subs() {
   return (AK != AKind::Dense && AK != AKind::UpperDense && MD == Mode::BF16)
              ? 1
-             : (3 * 2 * stage_bytes<BCOLS, MD == Mode::TF32x3>() <= 192 * 1024 ? 2 : 1);
+             : ((AK == AKind::Dense || AK == AKind::UpperDense) && MD != Mode::TF32x3 &&
+                3 * 4 * stage_bytes<BCOLS, false>() <= 192 * 1024)
+                   ? 4  // one-pass modes on TMA-fed operands: 8 MMAs per stage
+                   : (3 * 2 * stage_bytes<BCOLS, MD == Mode::TF32x3>() <= 192 * 1024 ? 2 : 1);
 }
 // Pipeline stages: as many as fit into 192 KiB, at most 8.
 template <AKind AK, Mode MD, int BCOLS>
