@@ -77,7 +77,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     a = ap.parse_args()
     if a.steps is None:
-        a.steps = {"diag": 400, "gemm": 20, "upper": 30, "sandwich": 30, "toeplitz": 3, "add": 300}[a.op]
+        a.steps = {"diag": 400, "gemm": 20, "upper": 30, "sandwich": 30, "toeplitz": 6, "add": 300}[a.op]
     if a.warmup is None:
         a.warmup = {"diag": 20, "gemm": 3, "upper": 3, "sandwich": 3, "toeplitz": 3, "add": 20}[a.op]
     return a
@@ -121,6 +121,7 @@ class ClockSampler:
         self.index = index
         self.period = period_s
         self.samples = []
+        self.power = []
         self.reasons = 0
         self.max_mhz = None
         self._stop = threading.Event()
@@ -142,6 +143,7 @@ class ClockSampler:
             try:
                 self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
                 self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.power.append(nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0)
             except Exception:
                 pass
             time.sleep(self.period)
@@ -161,8 +163,12 @@ class ClockSampler:
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
         names = [k for k, v in self.REASONS.items() if self.reasons & v]
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
-                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+        if self.power:
+            out["power_w_median"] = round(statistics.median(self.power), 1)
+            out["power_w_max"] = round(max(self.power), 1)
+        return out
 
 
 # ---------------------------------------------------------------- distributed
