@@ -85,6 +85,20 @@ SIGNATURES = [
     ("smm_unpack", _i, [_vp, _i, _vp, _i, _vp]),
     ("smm_pack", _i, [_vp, _i, _vp, _i, _vp]),
     ("smm_toeplitz_compact", _i, [_vp, _vp, _i, _i, _vp]),
+    ("smm_compat_gen_x_gen", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_diag_x_gen", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_gen_x_diag", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_upper_x_gen", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_toeplitz_x_gen", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_symm_x_gen", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_gen_x_symm", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_gen_x_upper", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_symm_x_symm", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_gen_x_lower", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_lower_x_gen", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_lower_x_lower", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_add_gen_symm", _i, [_vp, _vp, _vp, _vp, _i, _vp]),
+    ("smm_compat_symm_sandwich", _i, [_vp, _vp, _vp, _vp, _vp, _i, _vp]),
     ("smm_debug_timeout_probe", _i, [_ull, _vp]),
     ("smm_debug_trace_next", _i, [_vp]),
 ]

@@ -251,6 +251,36 @@ int smm_pack(const float* D, int s_fmt, float* P, int N, void* stream);
  * toeplitz_matmul2.cpp:34-41). */
 int smm_toeplitz_compact(const float* T, float* g, int rows, int cols, void* stream);
 
+/* ---- reference-compatible wrappers (synchronous, timed) ---------------- */
+
+/* One per operation the DSL's CUDA runner generates, with the generated
+ * wrapper's calling convention <Out>_computation(lhs_data, rhs_data,
+ * out_data, gflops_out, n, time_ms_out) (src/dsl/codegen_cuda.py:44-45,
+ * 250-275): device pointers in the DSL's storage formats, a square order n,
+ * synchronous on the legacy default stream, the kernels timed with CUDA
+ * events into *time_ms_out, and *gflops_out counted as the generated wrappers
+ * do (2 n^3 for a product; n^2 for a diagonal scale or a sum).  fp32
+ * (3xTF32) mode.  Any workspace is allocated stream-ordered outside the timed
+ * window.  Returns a status (the generated wrappers ignore errors; a ctypes
+ * caller that sets no restype may do the same).  Each replaces the generated
+ * wrapper of the kernel named: */
+int smm_compat_gen_x_gen(const float* A, const float* B, float* C, float* gflops_out, int n, float* time_ms_out);      /* kernel_gen_x_gen :62-278 */
+int smm_compat_diag_x_gen(const float* d, const float* B, float* C, float* gflops_out, int n, float* time_ms_out);     /* kernel_diag_x_gen :1253-1332 */
+int smm_compat_gen_x_diag(const float* A, const float* d, float* C, float* gflops_out, int n, float* time_ms_out);     /* kernel_gen_x_diag :808-964 */
+int smm_compat_upper_x_gen(const float* U, const float* B, float* C, float* gflops_out, int n, float* time_ms_out);    /* no CUDA kernel in the reference (:1681) */
+int smm_compat_toeplitz_x_gen(const float* g, const float* B, float* C, float* gflops_out, int n, float* time_ms_out); /* no CUDA kernel in the reference (:1681) */
+int smm_compat_symm_x_gen(const float* S, const float* B, float* C, float* gflops_out, int n, float* time_ms_out);     /* kernel_symm_x_gen :973-1245 */
+int smm_compat_gen_x_symm(const float* A, const float* S, float* C, float* gflops_out, int n, float* time_ms_out);     /* kernel_gen_x_symm :546-806 */
+int smm_compat_gen_x_upper(const float* A, const float* U, float* C, float* gflops_out, int n, float* time_ms_out);    /* kernel_gen_x_upper :280-544 */
+int smm_compat_symm_x_symm(const float* S1, const float* S2, float* C, float* gflops_out, int n, float* time_ms_out);  /* kernel_symm_x_symm :1340-1613 */
+int smm_compat_gen_x_lower(const float* A, const float* L, float* C, float* gflops_out, int n, float* time_ms_out);    /* CPU AVX backend only */
+int smm_compat_lower_x_gen(const float* L, const float* B, float* C, float* gflops_out, int n, float* time_ms_out);    /* none in the reference */
+int smm_compat_lower_x_lower(const float* L1, const float* L2, float* C, float* gflops_out, int n, float* time_ms_out);/* CPU AVX backend only */
+int smm_compat_add_gen_symm(const float* A, const float* S, float* C, float* gflops_out, int n, float* time_ms_out);   /* kernel_add_gen_symm :1650-1716 */
+/* A S B in one call: run_graph's two generated launches (src/dsl/runner_cuda.py:147-197). */
+int smm_compat_symm_sandwich(const float* A, const float* S, const float* B, float* C, float* gflops_out, int n,
+                             float* time_ms_out);
+
 /* ---- failure-detection probe ------------------------------------------- */
 
 /* Launches one CTA that waits on a shared-memory barrier nothing ever
