@@ -221,27 +221,16 @@ Operand structured_op(const float* src, int dim, int row0 = 0) {
 }
 
 // ---------------------------------------------------------------- operand staging
-// hi (optional) = src with zero columns appended up to ld_dst; lo (optional)
-// = the same minus its tf32 truncation, i.e. the 3xTF32 low plane.
-__global__ void split_planes_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
-                                    float* __restrict__ hi, float* __restrict__ lo, int ld_dst) {
+// dst = src with zero columns appended up to ld_dst (a 16-byte multiple), so
+// that TMA can address its rows.
+__global__ void pad_rows_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
+                                float* __restrict__ dst, int ld_dst) {
   const long long total = static_cast<long long>(rows) * ld_dst;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long r = i / ld_dst;
     const int c = static_cast<int>(i - r * ld_dst);
-    const float x = c < cols ? src[r * ld_src + c] : 0.0f;
-    if (hi) hi[i] = x;
-    if (lo) lo[i] = x - tf32_hi(x);
-  }
-}
-
-// lo plane of a contiguous, 16-byte-aligned matrix (the common case), 128-bit.
-__global__ void lo_plane_vec4_kernel(const float4* __restrict__ src, float4* __restrict__ lo, long long n4) {
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const float4 x = __ldcs(src + i);
-    __stcs(lo + i, make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w)));
+    dst[i] = c < cols ? src[r * ld_src + c] : 0.0f;
   }
 }
 
@@ -259,8 +248,8 @@ __global__ void to_bf16_kernel(const float* __restrict__ src, int rows, int cols
 }
 
 // A TMA-fed operand (rows x cols row-major): the caller's array or a padded
-// copy, plus its lo plane in 3xTF32 mode, or its bf16 copy in bf16 mode, all
-// in the workspace.
+// copy in the workspace (fp32 modes), or its bf16 copy in the workspace (bf16
+// mode).  `lo` stays null: 3xTF32 lo tiles are derived on chip.
 struct Staged {
   const float* ptr;
   const float* lo;
@@ -294,36 +283,21 @@ int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_c
     *out = {nullptr, nullptr, ld, dst};
     return SMM_OK;
   }
-  const bool split3 = false;  // lo tiles are derived on chip
-  const bool pad = needs_pad(src, cols);
-  if (!pad && !split3) {
+  // fp32 modes: the caller's array when TMA can address it (the 3xTF32 lo
+  // tiles are derived on chip), else a copy with 16-byte-multiple rows.
+  if (!needs_pad(src, cols)) {
     *out = {src, nullptr, cols};
     return SMM_OK;
   }
-  const int ld = pad ? round4(cols) : cols;
-  float* hi = nullptr;
-  if (pad) {
-    hi = reinterpret_cast<float*>(ws_cur);
-    ws_cur += plane_bytes(rows, cols);
-  }
-  float* lo = nullptr;
-  if (split3) {
-    lo = reinterpret_cast<float*>(ws_cur);
-    ws_cur += plane_bytes(rows, cols);
-  }
+  const int ld = round4(cols);
+  float* dst = reinterpret_cast<float*>(ws_cur);
+  ws_cur += plane_bytes(rows, cols);
   const long long total = static_cast<long long>(rows) * ld;
-  if (!pad) {
-    const long long n4 = total / 4;
-    const int grid = static_cast<int>(std::min<long long>((n4 + 255) / 256, 148LL * 8));
-    lo_plane_vec4_kernel<<<std::max(grid, 1), 256, 0, st>>>(reinterpret_cast<const float4*>(src),
-                                                            reinterpret_cast<float4*>(lo), n4);
-  } else {
-    const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-    split_planes_kernel<<<std::max(grid, 1), 256, 0, st>>>(src, rows, cols, cols, hi, lo, ld);
-  }
+  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
+  pad_rows_kernel<<<std::max(grid, 1), 256, 0, st>>>(src, rows, cols, cols, dst, ld);
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "operand staging launch");
-  *out = {pad ? hi : src, lo, ld};
+  *out = {dst, nullptr, ld};
   return SMM_OK;
 }
 
