@@ -155,7 +155,6 @@ struct Operand {
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
                     int N, int K, cudaStream_t st, float* C_lo = nullptr, __nv_bfloat16* C_bf16 = nullptr,
                     int ldc_bf16 = 0) {
-  const bool split3 = (mode == SMM_MODE_3XTF32);
   const bool bf16 = (mode == SMM_MODE_BF16);
   const bool pair = use_pairs(M, N);
   const int bn = pick_bn(M, N, pair);
@@ -171,13 +170,11 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
     const void* bp = bf16 ? static_cast<const void*>(b.bf16) : static_cast<const void*>(b.ptr);
     if (!bp) return set_error(SMM_ERR_INVALID, "internal: missing B operand plane");
     if (int rc = make_tmap(&m.b, bp, K, N, b.ld, b_box_c, b_box_r, b_swz, bf16)) return rc;
-
   }
   if (a_tma) {
     const void* ap = bf16 ? static_cast<const void*>(a.bf16) : static_cast<const void*>(a.ptr);
     if (!ap) return set_error(SMM_ERR_INVALID, "internal: missing A operand plane");
     if (int rc = make_tmap(&m.a, ap, M, K, a.ld, a_box, 128, CU_TENSOR_MAP_SWIZZLE_64B, bf16)) return rc;
-
   }
   UmmaParams p{};
   p.M = M;
@@ -340,7 +337,6 @@ extern "C" int smm_device_status(void* stream) {
 
 extern "C" size_t smm_gemm_workspace_size(int M, int N, int K, int mode) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   return staged_bytes_bound(M, K, mode) + staged_bytes_bound(K, N, mode);
 }
 
@@ -352,7 +348,6 @@ extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, 
   if (!C || (K > 0 && (!A || !B))) return set_error(SMM_ERR_INVALID, "smm_gemm: null pointer");
   cudaStream_t st = as_stream(stream);
   if (K == 0) return zero_output(C, M, N, st);
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   const size_t need = staged_bytes(A, M, K, mode) + staged_bytes(B, K, N, mode);
   if (int rc = check_ws("smm_gemm", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
@@ -365,7 +360,6 @@ extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, 
 
 extern "C" size_t smm_upper_left_workspace_size(int N, int ncols, int u_fmt, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   size_t b = staged_bytes_bound(N, ncols, mode);
   if (u_fmt == SMM_FMT_DENSE) b += staged_bytes_bound(N, N, mode);
   return b;
@@ -398,7 +392,6 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!U || !B || !C) return set_error(SMM_ERR_INVALID, "smm_upper_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   size_t need = staged_bytes(B, N, ncols, mode);
   if (u_fmt == SMM_FMT_DENSE) need += staged_bytes(U, N, N, mode);
   if (int rc = check_ws("smm_upper_left", ws, ws_bytes, need)) return rc;
@@ -437,7 +430,6 @@ extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, 
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!g || !B || !C) return set_error(SMM_ERR_INVALID, "smm_toeplitz_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   if (int rc = check_ws("smm_toeplitz_left", ws, ws_bytes, staged_bytes(B, N, ncols, mode))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
@@ -463,7 +455,6 @@ extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int 
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   if (int rc = check_ws("smm_symm_left", ws, ws_bytes, staged_bytes(B, N, ncols, mode))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
@@ -503,7 +494,6 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   if (!A || !S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich: null pointer");
   if (int rc = check_packed("smm_symm_sandwich", N)) return rc;
   cudaStream_t st = as_stream(stream);
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   const bool bf = (mode == SMM_MODE_BF16);
   if (int rc = check_ws("smm_symm_sandwich", ws, ws_bytes, sandwich_need(A, B, N, mode))) return rc;
   const int ldx = round4(N);
@@ -513,7 +503,6 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   cur += plane_bytes(N, N);
   float* X_lo = nullptr;
   __nv_bfloat16* X_bf = nullptr;
-  (void)s3;
   if (bf) {
     X_bf = reinterpret_cast<__nv_bfloat16*>(cur);
     cur += bf16_plane_bytes(N, N);
@@ -546,7 +535,6 @@ int gen_x_struct(const char* who, BKind bk, const float* A, const float* X, floa
   if (M == 0 || N == 0) return SMM_OK;
   if (!A || !X || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
   if (int rc = check_packed(who, N)) return rc;
-  const bool s3 = (mode == SMM_MODE_3XTF32);
   if (int rc = check_ws(who, ws, ws_bytes, staged_bytes(A, M, N, mode))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged a;
