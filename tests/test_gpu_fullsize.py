@@ -83,3 +83,33 @@ def test_gemm_same_sign_data_2048(cuda, lo, hi):
     C = ops.gemm(dev(A), dev(B)).cpu().numpy()
     r = sample_rows(n, seed=4)
     assert O.relerr(C[r], O.gemm_rows_f64(A, B, r)) <= TOL
+
+
+def test_lower_left_8192(cuda):
+    """L B with L packed lower (the left-side counterpart of U B) at 8192."""
+    n = 8192
+    rng = np.random.default_rng(7)
+    Lp = rng.uniform(-1, 1, n * (n + 1) // 2).astype(np.float32)
+    B = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    C = ops.lower_left(dev(Lp), dev(B)).cpu().numpy()
+    r = sample_rows(n, seed=6)
+    B64 = B.astype(np.float64)
+    R = np.stack([Lp[i * (i + 1) // 2: i * (i + 1) // 2 + i + 1].astype(np.float64) @ B64[: i + 1] for i in r])
+    assert O.relerr(C[r], R) <= TOL
+
+
+@pytest.mark.parametrize("op", ["gemm", "upper"])
+def test_bf16_mode_8192(cuda, op):
+    """bf16 mode at the bench size: operands rounded to bf16 inside the call,
+    fp32 accumulation; normwise bound 1e-2 against fp64."""
+    n = 8192
+    r = sample_rows(n, seed=8)
+    if op == "gemm":
+        w = W.make_gemm(n, n, n, seed=0)
+        C = ops.gemm(dev(w["A"]), dev(w["B"]), mode="bf16").cpu().numpy()
+        R = O.gemm_rows_f64(w["A"], w["B"], r)
+    else:
+        w = W.make_upper(n, seed=0)
+        C = ops.upper_left(dev(w["U"]), dev(w["B"]), mode="bf16").cpu().numpy()
+        R = O.upper_left_rows_f64(w["U"], w["B"], r)
+    assert O.relerr(C[r], R) <= 1e-2
