@@ -114,6 +114,10 @@ __device__ __forceinline__ void cp_async_4(uint32_t smem_dst, const float* src, 
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_dst), "l"(src), "r"(src_bytes)
                : "memory");
 }
+// 16-byte asynchronous copy global -> shared, both 16-byte aligned, through L1.
+__device__ __forceinline__ void cp_async_16(uint32_t smem_dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_dst), "l"(src) : "memory");
+}
 // Arrive on `bar` once every cp.async this thread issued so far has landed.
 // The arrival is not pre-counted (.noinc): the barrier's expected count
 // includes it.

@@ -150,6 +150,7 @@ struct Operand {
   const float* src = nullptr;
   int dim = 0;
   int row0 = 0;
+  bool lower = false;  // dense A with exact zeros above the diagonal (K range clipped)
 };
 
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
@@ -188,6 +189,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.a_src = a.src;
   p.a_dim = a.dim;
   p.a_row0 = a.row0;
+  p.a_lower = a.lower ? 1 : 0;
   p.b_src = b.src;
   p.b_dim = b.dim;
   p.row_tiles = pair ? (M + 2 * kBM - 1) / (2 * kBM) : (M + kBM - 1) / kBM;
@@ -298,6 +300,78 @@ int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_c
   return SMM_OK;
 }
 
+// bf16 dense copy of rows [row0, row0 + rows) of a packed structured matrix of
+// order n: upper (zeros below the diagonal), lower (zeros above) or symmetric
+// (mirrored), each row padded with zeros to ld (a multiple of 8).  64 x 64
+// tiles, 256 threads, lanes along columns (two per lane: coalesced packed-row
+// reads, 128-byte row writes).  A symmetric tile wholly below the diagonal
+// holds mirrors S[j][i]: it reads its block along packed rows j (coalesced)
+// and transposes it through shared memory.
+template <int SF>
+__global__ void __launch_bounds__(256) expand_bf16_kernel(const float* __restrict__ P, int n, int row0, int rows,
+                                                          __nv_bfloat16* __restrict__ dst, int ld) {
+  __shared__ float tile[64][65];
+  const int r0 = blockIdx.y * 64;  // slab row of the tile
+  const int c0 = blockIdx.x * 64;  // column of the tile
+  const int t = threadIdx.x;
+  const bool mirror = SF == SMM_STRUCT_SYMM && c0 + 63 < row0 + r0;
+  if (mirror) {
+    const int il = t & 63;
+    const int i = row0 + r0 + il;
+    for (int jl = t >> 6; jl < 64; jl += 4) {
+      const int j = c0 + jl;  // j < i for every element of the tile
+      tile[jl][il] = (r0 + il < rows && j < n) ? __ldg(P + packed_idx(j, i, n)) : 0.0f;
+    }
+    __syncthreads();
+  }
+  const int cp = 2 * (t & 31);
+  const int j = c0 + cp;
+  if (j >= ld) return;  // ld and j even: both columns of the pair are inside or outside
+  for (int rl = t >> 5; rl < 64; rl += 8) {
+    const int r = r0 + rl;
+    if (r >= rows) break;
+    const int i = row0 + r;
+    float v[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int jj = j + e;
+      if (mirror) {
+        v[e] = tile[cp + e][rl];
+      } else if (jj >= n) {
+        v[e] = 0.0f;
+      } else if constexpr (SF == SMM_STRUCT_UPPER) {
+        v[e] = jj >= i ? __ldg(P + packed_idx(i, jj, n)) : 0.0f;
+      } else if constexpr (SF == SMM_STRUCT_LOWER) {
+        v[e] = jj <= i ? __ldg(P + (static_cast<long long>(i) * (i + 1) / 2 + jj)) : 0.0f;
+      } else {
+        v[e] = __ldg(P + (jj >= i ? packed_idx(i, jj, n) : packed_idx(jj, i, n)));
+      }
+    }
+    *reinterpret_cast<__nv_bfloat162*>(dst + static_cast<long long>(r) * ld + j) = __floats2bfloat162_rn(v[0], v[1]);
+  }
+}
+
+// bf16 mode, packed operand (upper, lower or symmetric) on the left: rows
+// [row0, row0 + rows) expanded into a dense bf16 copy in the workspace, which
+// the tensor cores then read by TMA like any dense operand (a packed row has
+// no fixed alignment, so on-chip gathers of it cannot use wide copies).
+int expand_operand(const float* P, int sf, int n, int row0, int rows, uint8_t*& ws_cur, Staged* out,
+                   cudaStream_t st) {
+  const int ld = round8(n);
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
+  ws_cur += bf16_plane_bytes(rows, n);
+  const dim3 grid((ld + 63) / 64, (rows + 63) / 64);
+  switch (sf) {
+    case SMM_STRUCT_UPPER: expand_bf16_kernel<SMM_STRUCT_UPPER><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
+    case SMM_STRUCT_LOWER: expand_bf16_kernel<SMM_STRUCT_LOWER><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
+    default: expand_bf16_kernel<SMM_STRUCT_SYMM><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
+  }
+  count_launch();
+  SMM_CUDA_TRY(cudaGetLastError(), "packed operand expansion launch");
+  *out = {nullptr, nullptr, ld, dst};
+  return SMM_OK;
+}
+
 int check_ws(const char* who, void* ws, size_t have, size_t need) {
   if (need == 0) return SMM_OK;
   if (!ws || have < need)
@@ -361,7 +435,7 @@ extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, 
 extern "C" size_t smm_upper_left_workspace_size(int N, int ncols, int u_fmt, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
   size_t b = staged_bytes_bound(N, ncols, mode);
-  if (u_fmt == SMM_FMT_DENSE) b += staged_bytes_bound(N, N, mode);
+  if (u_fmt == SMM_FMT_DENSE || mode == SMM_MODE_BF16) b += staged_bytes_bound(N, N, mode);
   return b;
 }
 
@@ -392,8 +466,10 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!U || !B || !C) return set_error(SMM_ERR_INVALID, "smm_upper_left: null pointer");
   cudaStream_t st = as_stream(stream);
+  const bool expand = u_fmt == SMM_FMT_PACKED && mode == SMM_MODE_BF16;
   size_t need = staged_bytes(B, N, ncols, mode);
   if (u_fmt == SMM_FMT_DENSE) need += staged_bytes(U, N, N, mode);
+  if (expand) need += bf16_plane_bytes(nrows, N);
   if (int rc = check_ws("smm_upper_left", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
@@ -404,6 +480,15 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
     const size_t off = static_cast<size_t>(row0) * u.ld;
     Operand ua = dense_op(u.ptr ? u.ptr + off : nullptr, u.lo ? u.lo + off : nullptr, u.ld,
                           u.bf16 ? u.bf16 + off : nullptr);
+    ua.dim = N;
+    ua.row0 = row0;
+    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, nrows,
+                           ncols, N, st);
+  }
+  if (expand) {
+    Staged u;
+    if (int rc = expand_operand(U, SMM_STRUCT_UPPER, N, row0, nrows, cur, &u, st)) return rc;
+    Operand ua = dense_op(nullptr, nullptr, u.ld, u.bf16);
     ua.dim = N;
     ua.row0 = row0;
     return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, nrows,
@@ -444,7 +529,8 @@ extern "C" int smm_toeplitz_left(const float* g, const float* B, float* C, int N
 }
 
 extern "C" size_t smm_symm_left_workspace_size(int N, int ncols, int mode) {
-  return smm_toeplitz_left_workspace_size(N, ncols, mode);
+  if (N <= 0 || ncols <= 0) return 0;
+  return staged_bytes_bound(N, ncols, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, N) : 0);
 }
 
 extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int N, int ncols, int row0, int nrows,
@@ -455,10 +541,18 @@ extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int 
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, staged_bytes(B, N, ncols, mode))) return rc;
+  const bool expand = mode == SMM_MODE_BF16;
+  const size_t need = staged_bytes(B, N, ncols, mode) + (expand ? bf16_plane_bytes(nrows, N) : 0);
+  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
   if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
+  if (expand) {
+    Staged s;
+    if (int rc = expand_operand(S, SMM_STRUCT_SYMM, N, row0, nrows, cur, &s, st)) return rc;
+    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(nullptr, nullptr, s.ld, s.bf16),
+                           dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, nrows, ncols, N, st);
+  }
   return run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N, row0), dense_op(b.ptr, b.lo, b.ld, b.bf16),
                          C, ncols, nrows, ncols, N, st);
 }
@@ -469,11 +563,11 @@ extern "C" int smm_symm_left(const float* S, const float* B, float* C, int N, in
 }
 
 namespace {
-// Workspace of the sandwich: X = S B (16-byte row stride) and, in 3xTF32, its
-// lo plane, or in bf16 mode its bf16 copy (both written by the first
-// product's epilogue), then the staged A and B.
+// Workspace of the sandwich: X = S B (16-byte row stride) and, in bf16 mode,
+// its bf16 copy (written by the first product's epilogue) and the dense bf16
+// expansion of S, then the staged A and B.
 size_t sandwich_x_bytes(int N, int mode) {
-  if (mode == SMM_MODE_BF16) return plane_bytes(N, N) + bf16_plane_bytes(N, N);
+  if (mode == SMM_MODE_BF16) return plane_bytes(N, N) + 2 * bf16_plane_bytes(N, N);
   return plane_bytes(N, N);
 }
 size_t sandwich_need(const float* A, const float* B, int N, int mode) {
@@ -509,12 +603,16 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
     // the bf16 row padding must read as zeros (never multiplied, but keep it defined)
     if (ldx_bf != N) SMM_CUDA_TRY(cudaMemsetAsync(X_bf, 0, bf16_plane_bytes(N, N), st), "zero bf16 intermediate");
   }
+  Staged s_bf{};
+  if (bf)
+    if (int rc = expand_operand(S, SMM_STRUCT_SYMM, N, 0, N, cur, &s_bf, st)) return rc;
   Staged a, b;
   if (int rc = stage_operand(A, N, N, mode, cur, &a, st)) return rc;
   if (int rc = stage_operand(B, N, N, mode, cur, &b, st)) return rc;
-  // X = S B (S packed, mirrored on chip; the epilogue also writes X's lo
-  // plane or bf16 copy), then C = A X.
-  if (int rc = run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N),
+  // X = S B (fp32 modes: S packed, mirrored on chip; bf16: its dense bf16
+  // expansion; the epilogue also writes X's bf16 copy), then C = A X.
+  const Operand s_op = bf ? dense_op(nullptr, nullptr, s_bf.ld, s_bf.bf16) : structured_op(S, N);
+  if (int rc = run_contraction(bf ? AKind::Dense : AKind::SymmPacked, BKind::Dense, mode, s_op,
                                dense_op(b.ptr, b.lo, b.ld, b.bf16), X, ldx, N, N, N, st, X_lo, X_bf, ldx_bf))
     return rc;
   return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16),
@@ -571,7 +669,7 @@ extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N
 // ---------------------------------------------------------------- lower-triangular operands
 extern "C" size_t smm_lower_left_workspace_size(int N, int ncols, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
-  return staged_bytes_bound(N, ncols, mode);
+  return staged_bytes_bound(N, ncols, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, N) : 0);
 }
 
 extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, int ncols, int mode, void* ws,
@@ -582,10 +680,20 @@ extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, 
   if (!Lp || !B || !C) return set_error(SMM_ERR_INVALID, "smm_lower_left: null pointer");
   if (int rc = check_packed("smm_lower_left", N)) return rc;
   cudaStream_t st = as_stream(stream);
-  if (int rc = check_ws("smm_lower_left", ws, ws_bytes, staged_bytes(B, N, ncols, mode))) return rc;
+  const bool expand = mode == SMM_MODE_BF16;
+  const size_t need = staged_bytes(B, N, ncols, mode) + (expand ? bf16_plane_bytes(N, N) : 0);
+  if (int rc = check_ws("smm_lower_left", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
   if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
+  if (expand) {
+    Staged l;
+    if (int rc = expand_operand(Lp, SMM_STRUCT_LOWER, N, 0, N, cur, &l, st)) return rc;
+    Operand la = dense_op(nullptr, nullptr, l.ld, l.bf16);
+    la.lower = true;
+    return run_contraction(AKind::Dense, BKind::Dense, mode, la, dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, N,
+                           ncols, N, st);
+  }
   return run_contraction(AKind::LowerPacked, BKind::Dense, mode, structured_op(Lp, N), dense_op(b.ptr, b.lo, b.ld, b.bf16),
                          C, ncols, N, ncols, N, st);
 }
@@ -684,7 +792,7 @@ extern "C" int smm_symm_sandwich_noalloc(const float* A, const float* S, const f
   if (need > kNoallocScratchBytes)
     return set_error(SMM_ERR_WORKSPACE,
                      "smm_symm_sandwich_noalloc: N = %d needs %zu bytes of scratch but the static scratch holds %zu "
-                     "(fp32 modes: N <= 2048 with N %% 4 == 0 and 16-byte-aligned A, B; bf16: N <= 1290)",
+                     "(fp32 modes: N <= 2048 with N %% 4 == 0 and 16-byte-aligned A, B; bf16: N <= 1180)",
                      N, need, kNoallocScratchBytes);
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;

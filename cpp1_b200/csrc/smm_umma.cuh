@@ -90,10 +90,19 @@ struct ModeTraits {
 };
 
 // Structured A in fp32 modes is filled by cp.async warps (raw fp32, like a
-// TMA tile); in bf16 mode the transform warps gather and convert it.
+// TMA tile).  In bf16 mode a Toeplitz block is staged the same way (the one
+// generator window its 128 rows slide over, fp32) and converted by the
+// transform warps; the other structured kinds are gathered and converted by
+// the transform warps.
 __host__ __device__ constexpr bool a_async_filled(AKind ak, Mode md) {
-  return ak != AKind::Dense && ak != AKind::UpperDense && md != Mode::BF16;
+  return ak != AKind::Dense && ak != AKind::UpperDense && (md != Mode::BF16 || ak == AKind::Toeplitz);
 }
+__host__ __device__ constexpr bool a_staged(AKind ak, Mode md) { return ak == AKind::Toeplitz && md == Mode::BF16; }
+// bf16 Toeplitz staging: generator elements [lo, lo + 159) of a k-block
+// (lo = n - 1 - (last row) + k0) from the 16-byte boundary at or below lo:
+// 41 chunks of 16 bytes, in a 1 KiB slot (stages stay 1 KiB aligned).
+constexpr int kStgGenChunks = 41;
+constexpr int kStgBytes = 1024;
 // Threads per CTA: producer, MMA and 8 transform warps, plus the 2 fill warps
 // when the kernel has them.
 __host__ __device__ constexpr int umma_threads(AKind ak, Mode md) { return a_async_filled(ak, md) ? 384 : 320; }
@@ -109,6 +118,7 @@ struct UmmaParams {
   const float* a_src;      // packed U / generator / packed S (structured A kinds)
   int a_dim;               // order of the structured matrix
   int a_row0;              // row of the structured matrix that output row 0 maps to
+  int a_lower;             // dense A is lower triangular: rows up to g need k <= g only
   const float* b_src;      // packed U / packed S (structured B kinds)
   int b_dim;               // order of the structured right operand
   int row_tiles;           // ceil(M / 128)
@@ -137,9 +147,9 @@ struct TileGeom {
   static constexpr int kBChunkBytes = 16 * 128;     // one 32-column box
 };
 
-template <int BN, bool SPLIT3>
+template <int BN, bool SPLIT3, bool STAGING = false>
 __host__ __device__ constexpr int stage_bytes() {
-  return (SPLIT3 ? 2 : 1) * (kATileBytes + TileGeom<BN>::kBTileBytes);
+  return (SPLIT3 ? 2 : 1) * (kATileBytes + TileGeom<BN>::kBTileBytes) + (STAGING ? kStgBytes : 0);
 }
 
 template <int BN, bool SPLIT3>
@@ -165,17 +175,19 @@ __host__ __device__ constexpr int umma_subs() {
                    ? 4  // one-pass modes on TMA-fed operands: 8 MMAs per stage
                    : (3 * 2 * stage_bytes<BCOLS, MD == Mode::TF32x3>() <= 192 * 1024 ? 2 : 1);
 }
+// Bytes of one pipeline stage.
+template <AKind AK, Mode MD, int BCOLS>
+__host__ __device__ constexpr int umma_stage_bytes() {
+  return umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3, a_staged(AK, MD)>();
+}
 // Pipeline stages: as many as fit into 192 KiB, at most 8.
 template <AKind AK, Mode MD, int BCOLS>
 __host__ __device__ constexpr int umma_stages() {
-  return (192 * 1024 / (umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3>())) > 8
-             ? 8
-             : 192 * 1024 / (umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3>());
+  return (192 * 1024 / umma_stage_bytes<AK, MD, BCOLS>()) > 8 ? 8 : 192 * 1024 / umma_stage_bytes<AK, MD, BCOLS>();
 }
 template <AKind AK, Mode MD, int BCOLS, int STAGES>
 __host__ __device__ constexpr int umma_smem_bytes() {
-  return 1024 /*alignment slack*/ + STAGES * umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3>() +
-         256 /*barriers etc*/;
+  return 1024 /*alignment slack*/ + STAGES * umma_stage_bytes<AK, MD, BCOLS>() + 256 /*barriers etc*/;
 }
 
 __device__ __forceinline__ long long packed_idx(long long i, long long j, long long n) {
@@ -414,6 +426,65 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
   }
 }
 
+// ---------------------------------------------------------------- Toeplitz A, bf16
+// Generator index of element (g_first + 127, k0), the lowest one a k-block of
+// the tile reads (negative when the window starts before the generator).
+__device__ __forceinline__ long long toeplitz_lo(long long n, int g_first, int k0) {
+  return n - 1 - (g_first + kBM - 1) + k0;
+}
+
+// Stage the generator window of one bf16 k-block (32 k from k0) of this
+// CTA's Toeplitz rows g_first..: 41 aligned 16-byte chunks, one per fill
+// thread.  A chunk wholly outside the generator [g, g + 2n - 1) is skipped
+// (the conversion never reads it); one that overlaps either end is copied
+// element by element, so no byte outside the generator is read.
+__device__ __forceinline__ void a_stage_fill_toeplitz_bf16(const UmmaParams& p, uint8_t* stg, int g_first, int k0,
+                                                           int ft) {
+  if (ft >= kStgGenChunks) return;
+  const long long n = p.a_dim;
+  const uintptr_t b = reinterpret_cast<uintptr_t>(p.a_src);
+  const uintptr_t e = b + 4 * static_cast<uintptr_t>(2 * n - 1);
+  const uintptr_t a16 = ((b + 4 * toeplitz_lo(n, g_first, k0)) & ~uintptr_t(15)) + 16 * static_cast<uintptr_t>(ft);
+  const uint32_t dst = smem_u32(stg) + 16 * ft;
+  if (a16 + 16 <= b || a16 >= e) return;
+  if (a16 >= b && a16 + 16 <= e) {
+    cp_async_16(dst, reinterpret_cast<const void*>(a16));
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uintptr_t x = a16 + 4 * j;
+    if (x >= b && x < e) cp_async_4(dst + 4 * j, reinterpret_cast<const float*>(x), 4u);
+  }
+}
+
+// bf16 A tile (128 rows x 32 k, 64-byte swizzle) from the staged window:
+// element (row r, k0 + kk) is window element (127 - r) + kk.  Each transform
+// thread converts 4 groups of 4 consecutive k of one row (rows t/8 + 32 it,
+// columns 4 (t % 8)..), zero outside the matrix.
+__device__ __forceinline__ void a_stage_convert_toeplitz_bf16(const UmmaParams& p, const uint8_t* stg, uint8_t* ah,
+                                                              int g_first, int k0, int t) {
+  const long long n = p.a_dim;
+  const float* sf = reinterpret_cast<const float*>(stg);
+  const int off =
+      static_cast<int>(((reinterpret_cast<uintptr_t>(p.a_src) + 4 * toeplitz_lo(n, g_first, k0)) & 15) >> 2);
+  const int q = t & 7, kk0 = 4 * q;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 32 + (t >> 3);
+    const bool row_in = g_first + r < n;
+    const float* w = sf + off + (kBM - 1 - r) + kk0;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = (row_in && k0 + kk0 + j < n) ? w[j] : 0.0f;
+    __nv_bfloat162 lo2 = __floats2bfloat162_rn(v[0], v[1]), hi2 = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&lo2);
+    pk.y = *reinterpret_cast<uint32_t*>(&hi2);
+    *reinterpret_cast<uint2*>(ah + swz_offset(r, kk0 >> 3, 64) + (kk0 & 7) * 2) = pk;
+  }
+}
+
 // ---------------------------------------------------------------- structured B
 // Element e (0 .. BN/16-1) of transform thread t in a B stage tile.  Lanes
 // run along n (coalesced along packed row k); for symmetric tiles wholly
@@ -505,7 +576,9 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // A stage holds kSubs k-blocks of KS: [A hi x kSubs | B hi x kSubs | A lo x
   // kSubs | B lo x kSubs], each block in the one-block layouts below.
   constexpr int kSubs = umma_subs<AK, MD, kBCols>();
-  constexpr int kStage = kSubs * stage_bytes<kBCols, SPLIT3>();
+  constexpr bool kStaging = a_staged(AK, MD);  // bf16 Toeplitz: fp32 generator window after the tiles
+  static_assert(!kStaging || kSubs == 1, "staged A converts one k-block per stage");
+  constexpr int kStage = umma_stage_bytes<AK, MD, kBCols>();
   constexpr int kChunkS = kChunk / kSubs;  // chunk length in stages
   static_assert(kChunk % kSubs == 0, "chunk of whole stages");
   constexpr bool kATma = (AK == AKind::Dense || AK == AKind::UpperDense);
@@ -537,6 +610,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   auto b_hi = [&](int s) { return smem + s * kStage + kSubs * kATileBytes; };
   auto a_lo = [&](int s) { return smem + s * kStage + kSubs * (kATileBytes + kBTile); };
   auto b_lo = [&](int s) { return smem + s * kStage + kSubs * (2 * kATileBytes + kBTile); };
+  auto stg = [&](int s) { return smem + s * kStage + kSubs * (kATileBytes + kBTile); };  // bf16 only
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -572,7 +646,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   int kb_end = (p.K + KS - 1) / KS;
   // A lower-triangular left operand is zero right of its diagonal: rows up
   // to g1 need k <= g1 only.
-  if constexpr (AK == AKind::LowerPacked)
+  if (AK == AKind::LowerPacked || (AK == AKind::Dense && p.a_lower))
     kb_end = min(kb_end, (p.a_row0 + tile_m0 + (PAIR ? 2 * kBM : kBM) - 1) / KS + 1);
   // An upper-triangular right operand is zero below its diagonal: column
   // tile [n0, n0+BN) needs k < n0 + BN only; a lower-triangular one is zero
@@ -761,9 +835,13 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
+        if constexpr (kStaging) {
+          a_stage_fill_toeplitz_bf16(p, stg(s), g_first, (kb_begin + i) * KS, ft);
+        } else {
 #pragma unroll
-        for (int j = 0; j < kSubs; ++j)
-          a_async_fill<AK>(p, a_hi(s) + j * kATileBytes, g_first, (kb_begin + i * kSubs + j) * KS, ft);
+          for (int j = 0; j < kSubs; ++j)
+            a_async_fill<AK>(p, a_hi(s) + j * kATileBytes, g_first, (kb_begin + i * kSubs + j) * KS, ft);
+        }
         cp_async_mbar_arrive_noinc(&full[s]);
       }
       // no copy may land after the CTA has exited (bounded: all in flight)
@@ -847,6 +925,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         const int k0 = (kb_begin + i * kSubs) * KS;
         // (register-gathered A only with one k-block per stage)
         if constexpr (!kATma && !kACp) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
+        if constexpr (kStaging) a_stage_convert_toeplitz_bf16(p, stg(s), a_hi(s), g_first, k0, t);
         if constexpr (!kBTma) {
 #pragma unroll 1
           for (int j = 0; j < kSubs; ++j)
@@ -864,7 +943,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
               out[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
             }
           };
-          if constexpr (kATma || kACp) lo_of(a_hi(s), a_lo(s), kSubs * kATileBytes, t);
+          lo_of(a_hi(s), a_lo(s), kSubs * kATileBytes, t);
           if constexpr (kBTma) lo_of(b_hi(s), b_lo(s), kSubs * kBTile, t);
         }
         fence_proxy_async_smem();

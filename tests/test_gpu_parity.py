@@ -141,16 +141,58 @@ def test_toeplitz_shapes(cuda, n_cols, mode):
     assert _relerr_full(C, R) <= TOL[mode], (n_cols, _relerr_full(C, R))
 
 
-@pytest.mark.parametrize("n_cols", [(1, 1), (6, 10), (128, 128), (257, 130)])
-def test_symm_left_shapes(cuda, n_cols):
+@pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
+@pytest.mark.parametrize("n_cols", [(1, 1), (6, 10), (128, 128), (257, 130), (700, 300)])
+def test_symm_left_shapes(cuda, n_cols, mode):
     N, ncols = n_cols
     s = W.make_sandwich(N, seed=N)
     B = W.make_gemm(N, 1, ncols, seed=ncols)["A"]  # N x ncols
-    C = host(ops.symm_left(dev(s["S"]), dev(B)))
+    C = host(ops.symm_left(dev(s["S"]), dev(B), mode=mode))
     assert B.shape == (N, ncols)
     S = W.unpack_symmetric(s["S"], N).astype(np.float64)
     R = S @ B.astype(np.float64)
-    assert _relerr_full(C, R) <= 1e-5
+    assert _relerr_full(C, R) <= TOL[mode]
+
+
+# ---------------------------------------------------------------- row slabs
+def _slab_call(entry, L, first, B, C, N, ncols, r0, nrows, m, ws, wsb):
+    from cpp1_b200 import _lib
+    args = [first.data_ptr()] + ([_lib.FMT_PACKED] if entry == "smm_upper_left_rows" else [])
+    rc = getattr(L, entry)(*args, B.data_ptr(), C.data_ptr(), N, ncols, r0, nrows, m, ws, wsb, None)
+    assert rc == _lib.SMM_OK, _lib.last_error()
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
+@pytest.mark.parametrize("kind", ["upper", "symm", "toeplitz"])
+def test_row_slab_entries(cuda, kind, mode):
+    """The multi-GPU row-slab entries (rows [r0, r0 + nrows) of the product)
+    against fp64, slabs starting off the 128- and 256-row tile grid."""
+    from cpp1_b200 import _lib
+    N, ncols = 1000, 384
+    L = _lib.load()
+    m = ops._mode(mode)
+    if kind == "upper":
+        w = W.make_upper(N, ncols, seed=5)
+        first, Bn, entry = w["U"], w["B"], "smm_upper_left_rows"
+        R = O.upper_left_rows_f64(w["U"], w["B"], np.arange(N))
+        need = L.smm_upper_left_workspace_size(N, ncols, _lib.FMT_PACKED, m)
+    elif kind == "symm":
+        s = W.make_sandwich(N, seed=6)
+        Bn = W.make_gemm(N, 1, ncols, seed=7)["A"]
+        first, entry = s["S"], "smm_symm_left_rows"
+        R = W.unpack_symmetric(s["S"], N).astype(np.float64) @ Bn.astype(np.float64)
+        need = L.smm_symm_left_workspace_size(N, ncols, m)
+    else:
+        w = W.make_toeplitz(N, ncols, seed=8)
+        first, Bn, entry = w["g"], w["B"], "smm_toeplitz_left_rows"
+        R = O.toeplitz_left_rows_f64(w["g"], w["B"], np.arange(N))
+        need = L.smm_toeplitz_left_workspace_size(N, ncols, m)
+    ws = ops.workspace(need, torch.device("cuda"))
+    first_d, B = dev(first), dev(Bn)
+    for r0, nrows in ((0, 300), (300, 333), (633, 367), (999, 1)):
+        C = torch.full((nrows, ncols), float("nan"), device="cuda")
+        _slab_call(entry, L, first_d, B, C, N, ncols, r0, nrows, m, ws.data_ptr(), ws.numel())
+        assert _relerr_full(host(C), R[r0:r0 + nrows]) <= TOL[mode], (r0, nrows)
 
 
 @pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
