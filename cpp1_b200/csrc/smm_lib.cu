@@ -300,16 +300,22 @@ int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_c
   return SMM_OK;
 }
 
-// bf16 dense copy of rows [row0, row0 + rows) of a packed structured matrix of
-// order n: upper (zeros below the diagonal), lower (zeros above) or symmetric
-// (mirrored), each row padded with zeros to ld (a multiple of 8).  64 x 64
-// tiles, 256 threads, lanes along columns (two per lane: coalesced packed-row
-// reads, 128-byte row writes).  A symmetric tile wholly below the diagonal
-// holds mirrors S[j][i]: it reads its block along packed rows j (coalesced)
-// and transposes it through shared memory.
-template <int SF>
-__global__ void __launch_bounds__(256) expand_bf16_kernel(const float* __restrict__ P, int n, int row0, int rows,
-                                                          __nv_bfloat16* __restrict__ dst, int ld) {
+// Dense copy (fp32, or bf16 rounded to nearest even) of rows [row0, row0 +
+// rows) of a packed structured matrix of order n: upper (zeros below the
+// diagonal), lower (zeros above) or symmetric (mirrored), each row padded with
+// zeros to ld (even).  64 x 64 tiles, 256 threads, lanes along columns (two
+// per lane: coalesced packed-row reads and row writes).  A symmetric tile
+// wholly below the diagonal holds mirrors S[j][i]: it reads its block along
+// packed rows j (coalesced) and transposes it through shared memory.
+__device__ __forceinline__ void store_pair(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+__device__ __forceinline__ void store_pair(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+template <int SF, typename T>
+__global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P, int n, int row0, int rows,
+                                                     T* __restrict__ dst, int ld) {
   __shared__ float tile[64][65];
   const int r0 = blockIdx.y * 64;  // slab row of the tile
   const int c0 = blockIdx.x * 64;  // column of the tile
@@ -347,29 +353,57 @@ __global__ void __launch_bounds__(256) expand_bf16_kernel(const float* __restric
         v[e] = __ldg(P + (jj >= i ? packed_idx(i, jj, n) : packed_idx(jj, i, n)));
       }
     }
-    *reinterpret_cast<__nv_bfloat162*>(dst + static_cast<long long>(r) * ld + j) = __floats2bfloat162_rn(v[0], v[1]);
+    store_pair(dst + static_cast<long long>(r) * ld + j, v[0], v[1]);
   }
 }
 
-// bf16 mode, packed operand (upper, lower or symmetric) on the left: rows
-// [row0, row0 + rows) expanded into a dense bf16 copy in the workspace, which
-// the tensor cores then read by TMA like any dense operand (a packed row has
-// no fixed alignment, so on-chip gathers of it cannot use wide copies).
-int expand_operand(const float* P, int sf, int n, int row0, int rows, uint8_t*& ws_cur, Staged* out,
-                   cudaStream_t st) {
-  const int ld = round8(n);
-  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
-  ws_cur += bf16_plane_bytes(rows, n);
+template <typename T>
+void launch_expand(const float* P, int sf, int n, int row0, int rows, T* dst, int ld, cudaStream_t st) {
   const dim3 grid((ld + 63) / 64, (rows + 63) / 64);
   switch (sf) {
-    case SMM_STRUCT_UPPER: expand_bf16_kernel<SMM_STRUCT_UPPER><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
-    case SMM_STRUCT_LOWER: expand_bf16_kernel<SMM_STRUCT_LOWER><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
-    default: expand_bf16_kernel<SMM_STRUCT_SYMM><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
+    case SMM_STRUCT_UPPER: expand_kernel<SMM_STRUCT_UPPER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
+    case SMM_STRUCT_LOWER: expand_kernel<SMM_STRUCT_LOWER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
+    default: expand_kernel<SMM_STRUCT_SYMM, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
   }
+}
+
+// A packed operand (upper, lower or symmetric) on the left: rows [row0, row0 +
+// rows) expanded into a dense copy in the workspace (fp32 in the fp32 modes,
+// bf16 in bf16 mode), which the tensor cores then read by TMA like any dense
+// operand.  A packed row has no fixed alignment, so an on-chip fill of it
+// issues one 4-byte copy per element; the expansion is one HBM pass that
+// costs ~3% of the product at N = 4096..8192 (measured with it: U B 3xTF32
+// 218 -> 258 TFLOP/s, TF32 258 -> 569; S B 3xTF32 158 -> 200).
+size_t expanded_bytes(int rows, int n, int mode) {
+  return mode == SMM_MODE_BF16 ? bf16_plane_bytes(rows, n) : plane_bytes(rows, n);
+}
+int expand_operand(const float* P, int sf, int n, int row0, int rows, int mode, uint8_t*& ws_cur, Staged* out,
+                   cudaStream_t st) {
+  if (mode == SMM_MODE_BF16) {
+    const int ld = round8(n);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
+    launch_expand(P, sf, n, row0, rows, dst, ld, st);
+    *out = {nullptr, nullptr, ld, dst};
+  } else {
+    const int ld = round4(n);
+    float* dst = reinterpret_cast<float*>(ws_cur);
+    launch_expand(P, sf, n, row0, rows, dst, ld, st);
+    *out = {dst, nullptr, ld};
+  }
+  ws_cur += expanded_bytes(rows, n, mode);
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "packed operand expansion launch");
-  *out = {nullptr, nullptr, ld, dst};
   return SMM_OK;
+}
+
+// Expand a packed left operand when the workspace has room for the copy (the
+// *_workspace_size functions include it); a smaller workspace (down to what
+// the on-chip path needs) builds the operand on chip instead.  SMM_EXPAND=0
+// forces the on-chip path.
+bool expand_packed(void* ws, size_t ws_bytes, size_t need_expanded) {
+  const char* e = std::getenv("SMM_EXPAND");
+  if (e && e[0] == '0') return false;
+  return ws != nullptr && ws_bytes >= need_expanded;
 }
 
 int check_ws(const char* who, void* ws, size_t have, size_t need) {
@@ -434,9 +468,8 @@ extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, 
 
 extern "C" size_t smm_upper_left_workspace_size(int N, int ncols, int u_fmt, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
-  size_t b = staged_bytes_bound(N, ncols, mode);
-  if (u_fmt == SMM_FMT_DENSE || mode == SMM_MODE_BF16) b += staged_bytes_bound(N, N, mode);
-  return b;
+  // + a staged copy of a dense U, or the expansion of a packed one
+  return staged_bytes_bound(N, ncols, mode) + staged_bytes_bound(N, N, mode);
 }
 
 namespace {
@@ -466,10 +499,11 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!U || !B || !C) return set_error(SMM_ERR_INVALID, "smm_upper_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  const bool expand = u_fmt == SMM_FMT_PACKED && mode == SMM_MODE_BF16;
   size_t need = staged_bytes(B, N, ncols, mode);
   if (u_fmt == SMM_FMT_DENSE) need += staged_bytes(U, N, N, mode);
-  if (expand) need += bf16_plane_bytes(nrows, N);
+  const bool expand =
+      u_fmt == SMM_FMT_PACKED && expand_packed(ws, ws_bytes, need + expanded_bytes(nrows, N, mode));
+  if (expand) need += expanded_bytes(nrows, N, mode);
   if (int rc = check_ws("smm_upper_left", ws, ws_bytes, need)) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
@@ -487,8 +521,8 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
   }
   if (expand) {
     Staged u;
-    if (int rc = expand_operand(U, SMM_STRUCT_UPPER, N, row0, nrows, cur, &u, st)) return rc;
-    Operand ua = dense_op(nullptr, nullptr, u.ld, u.bf16);
+    if (int rc = expand_operand(U, SMM_STRUCT_UPPER, N, row0, nrows, mode, cur, &u, st)) return rc;
+    Operand ua = dense_op(u.ptr, nullptr, u.ld, u.bf16);
     ua.dim = N;
     ua.row0 = row0;
     return run_contraction(AKind::UpperDense, BKind::Dense, mode, ua, dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, nrows,
@@ -530,7 +564,7 @@ extern "C" int smm_toeplitz_left(const float* g, const float* B, float* C, int N
 
 extern "C" size_t smm_symm_left_workspace_size(int N, int ncols, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
-  return staged_bytes_bound(N, ncols, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, N) : 0);
+  return staged_bytes_bound(N, ncols, mode) + expanded_bytes(N, N, mode);
 }
 
 extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int N, int ncols, int row0, int nrows,
@@ -541,16 +575,17 @@ extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int 
   if (nrows == 0 || ncols == 0) return SMM_OK;
   if (!S || !B || !C) return set_error(SMM_ERR_INVALID, "smm_symm_left: null pointer");
   cudaStream_t st = as_stream(stream);
-  const bool expand = mode == SMM_MODE_BF16;
-  const size_t need = staged_bytes(B, N, ncols, mode) + (expand ? bf16_plane_bytes(nrows, N) : 0);
-  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, need)) return rc;
+  const size_t need_b = staged_bytes(B, N, ncols, mode);
+  const bool expand = expand_packed(ws, ws_bytes, need_b + expanded_bytes(nrows, N, mode));
+  if (int rc = check_ws("smm_symm_left", ws, ws_bytes, need_b + (expand ? expanded_bytes(nrows, N, mode) : 0)))
+    return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
   if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
   if (expand) {
     Staged s;
-    if (int rc = expand_operand(S, SMM_STRUCT_SYMM, N, row0, nrows, cur, &s, st)) return rc;
-    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(nullptr, nullptr, s.ld, s.bf16),
+    if (int rc = expand_operand(S, SMM_STRUCT_SYMM, N, row0, nrows, mode, cur, &s, st)) return rc;
+    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(s.ptr, nullptr, s.ld, s.bf16),
                            dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, nrows, ncols, N, st);
   }
   return run_contraction(AKind::SymmPacked, BKind::Dense, mode, structured_op(S, N, row0), dense_op(b.ptr, b.lo, b.ld, b.bf16),
@@ -564,12 +599,13 @@ extern "C" int smm_symm_left(const float* S, const float* B, float* C, int N, in
 
 namespace {
 // Workspace of the sandwich: X = S B (16-byte row stride) and, in bf16 mode,
-// its bf16 copy (written by the first product's epilogue) and the dense bf16
-// expansion of S, then the staged A and B.
+// its bf16 copy (written by the first product's epilogue), the dense
+// expansion of S when there is room for it, then the staged A and B.
 size_t sandwich_x_bytes(int N, int mode) {
-  if (mode == SMM_MODE_BF16) return plane_bytes(N, N) + 2 * bf16_plane_bytes(N, N);
+  if (mode == SMM_MODE_BF16) return plane_bytes(N, N) + bf16_plane_bytes(N, N);
   return plane_bytes(N, N);
 }
+// Without the expansion of S.
 size_t sandwich_need(const float* A, const float* B, int N, int mode) {
   return sandwich_x_bytes(N, mode) + staged_bytes(A, N, N, mode) + staged_bytes(B, N, N, mode);
 }
@@ -577,7 +613,7 @@ size_t sandwich_need(const float* A, const float* B, int N, int mode) {
 
 extern "C" size_t smm_symm_sandwich_workspace_size(int N, int mode) {
   if (N <= 0) return 0;
-  return sandwich_x_bytes(N, mode) + 2 * staged_bytes_bound(N, N, mode);
+  return sandwich_x_bytes(N, mode) + expanded_bytes(N, N, mode) + 2 * staged_bytes_bound(N, N, mode);
 }
 
 extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B, float* C, int N, int mode,
@@ -589,7 +625,10 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   if (int rc = check_packed("smm_symm_sandwich", N)) return rc;
   cudaStream_t st = as_stream(stream);
   const bool bf = (mode == SMM_MODE_BF16);
-  if (int rc = check_ws("smm_symm_sandwich", ws, ws_bytes, sandwich_need(A, B, N, mode))) return rc;
+  const size_t need = sandwich_need(A, B, N, mode);
+  const bool expand = expand_packed(ws, ws_bytes, need + expanded_bytes(N, N, mode));
+  if (int rc = check_ws("smm_symm_sandwich", ws, ws_bytes, need + (expand ? expanded_bytes(N, N, mode) : 0)))
+    return rc;
   const int ldx = round4(N);
   const int ldx_bf = round8(N);
   uint8_t* cur = static_cast<uint8_t*>(ws);
@@ -603,16 +642,16 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
     // the bf16 row padding must read as zeros (never multiplied, but keep it defined)
     if (ldx_bf != N) SMM_CUDA_TRY(cudaMemsetAsync(X_bf, 0, bf16_plane_bytes(N, N), st), "zero bf16 intermediate");
   }
-  Staged s_bf{};
-  if (bf)
-    if (int rc = expand_operand(S, SMM_STRUCT_SYMM, N, 0, N, cur, &s_bf, st)) return rc;
+  Staged s_ex{};
+  if (expand)
+    if (int rc = expand_operand(S, SMM_STRUCT_SYMM, N, 0, N, mode, cur, &s_ex, st)) return rc;
   Staged a, b;
   if (int rc = stage_operand(A, N, N, mode, cur, &a, st)) return rc;
   if (int rc = stage_operand(B, N, N, mode, cur, &b, st)) return rc;
-  // X = S B (fp32 modes: S packed, mirrored on chip; bf16: its dense bf16
-  // expansion; the epilogue also writes X's bf16 copy), then C = A X.
-  const Operand s_op = bf ? dense_op(nullptr, nullptr, s_bf.ld, s_bf.bf16) : structured_op(S, N);
-  if (int rc = run_contraction(bf ? AKind::Dense : AKind::SymmPacked, BKind::Dense, mode, s_op,
+  // X = S B (S expanded, or packed and mirrored on chip; the epilogue also
+  // writes X's bf16 copy in bf16 mode), then C = A X.
+  const Operand s_op = expand ? dense_op(s_ex.ptr, nullptr, s_ex.ld, s_ex.bf16) : structured_op(S, N);
+  if (int rc = run_contraction(expand ? AKind::Dense : AKind::SymmPacked, BKind::Dense, mode, s_op,
                                dense_op(b.ptr, b.lo, b.ld, b.bf16), X, ldx, N, N, N, st, X_lo, X_bf, ldx_bf))
     return rc;
   return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16),
@@ -669,7 +708,7 @@ extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N
 // ---------------------------------------------------------------- lower-triangular operands
 extern "C" size_t smm_lower_left_workspace_size(int N, int ncols, int mode) {
   if (N <= 0 || ncols <= 0) return 0;
-  return staged_bytes_bound(N, ncols, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, N) : 0);
+  return staged_bytes_bound(N, ncols, mode) + expanded_bytes(N, N, mode);
 }
 
 extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, int ncols, int mode, void* ws,
@@ -680,16 +719,17 @@ extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, 
   if (!Lp || !B || !C) return set_error(SMM_ERR_INVALID, "smm_lower_left: null pointer");
   if (int rc = check_packed("smm_lower_left", N)) return rc;
   cudaStream_t st = as_stream(stream);
-  const bool expand = mode == SMM_MODE_BF16;
-  const size_t need = staged_bytes(B, N, ncols, mode) + (expand ? bf16_plane_bytes(N, N) : 0);
-  if (int rc = check_ws("smm_lower_left", ws, ws_bytes, need)) return rc;
+  const size_t need_b = staged_bytes(B, N, ncols, mode);
+  const bool expand = expand_packed(ws, ws_bytes, need_b + expanded_bytes(N, N, mode));
+  if (int rc = check_ws("smm_lower_left", ws, ws_bytes, need_b + (expand ? expanded_bytes(N, N, mode) : 0)))
+    return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged b;
   if (int rc = stage_operand(B, N, ncols, mode, cur, &b, st)) return rc;
   if (expand) {
     Staged l;
-    if (int rc = expand_operand(Lp, SMM_STRUCT_LOWER, N, 0, N, cur, &l, st)) return rc;
-    Operand la = dense_op(nullptr, nullptr, l.ld, l.bf16);
+    if (int rc = expand_operand(Lp, SMM_STRUCT_LOWER, N, 0, N, mode, cur, &l, st)) return rc;
+    Operand la = dense_op(l.ptr, nullptr, l.ld, l.bf16);
     la.lower = true;
     return run_contraction(AKind::Dense, BKind::Dense, mode, la, dense_op(b.ptr, b.lo, b.ld, b.bf16), C, ncols, N,
                            ncols, N, st);
@@ -792,7 +832,7 @@ extern "C" int smm_symm_sandwich_noalloc(const float* A, const float* S, const f
   if (need > kNoallocScratchBytes)
     return set_error(SMM_ERR_WORKSPACE,
                      "smm_symm_sandwich_noalloc: N = %d needs %zu bytes of scratch but the static scratch holds %zu "
-                     "(fp32 modes: N <= 2048 with N %% 4 == 0 and 16-byte-aligned A, B; bf16: N <= 1180)",
+                     "(fp32 modes: N <= 2048 with N %% 4 == 0 and 16-byte-aligned A, B; bf16: N <= 1290)",
                      N, need, kNoallocScratchBytes);
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;

@@ -25,9 +25,16 @@
  *                    fp32 accumulation in tensor memory (3 MMA passes)
  *   SMM_MODE_TF32    one TF32 pass (fast, ~1e-3 relative)
  *   SMM_MODE_BF16    operands rounded to bf16 (inside the call), fp32
- *                    accumulation; a packed upper / symmetric / lower left
- *                    operand of an entry with a workspace is expanded into a
- *                    dense bf16 copy there (the workspace size includes it)
+ *                    accumulation
+ *
+ * A packed upper / symmetric / lower LEFT operand of an entry point with a
+ * workspace is expanded into a dense copy there (fp32, or bf16 in bf16 mode)
+ * and read by TMA; the *_workspace_size functions include that copy.  Given
+ * less workspace (at least the rest of the requirement) the entry point builds
+ * the operand on chip from its packed rows instead (slower), so callers that
+ * sized the workspace without the copy keep working.  Both give results
+ * within the mode's tolerance; SMM_EXPAND=0 in the environment forces the
+ * on-chip path.
  */
 #ifndef SMM_H
 #define SMM_H
@@ -161,8 +168,9 @@ int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, flo
  * N % 4 != 0 or they are not 16-byte aligned) lives in a fixed 16 MiB static
  * device array inside libsmm, which every GPU that loads the library holds
  * until process exit: N <= 2048 in the fp32 modes with N % 4 == 0 and
- * 16-byte-aligned A, B (about 1180 when padded copies are needed), N <= 1180
- * in bf16 mode (the bf16 copies and the expansion of S share it).  Larger N returns
+ * 16-byte-aligned A, B (about 1180 when padded copies are needed), N <= 1290
+ * in bf16 mode (the bf16 copies share it).  S is expanded into a dense copy
+ * only when the scratch has room left for it, else mirrored on chip.  Larger N returns
  * SMM_ERR_WORKSPACE.  Calls no
  * cudaMalloc/cudaFree.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress) and must come before any stream

@@ -39,7 +39,9 @@ def tiles(request, monkeypatch):
 
 @pytest.mark.parametrize("mode,tol", MODES)
 @pytest.mark.parametrize("n,ncols", [(1, 1), (7, 9), (128, 128), (300, 200), (1000, 512)])
-def test_lower_left(cuda, tiles, mode, tol, n, ncols):
+@pytest.mark.parametrize("expand", ["1", "0"])
+def test_lower_left(cuda, tiles, mode, tol, n, ncols, expand, monkeypatch):
+    monkeypatch.setenv("SMM_EXPAND", expand)
     Lp = lower_packed(n, n)
     B = np.random.default_rng(n + 1).uniform(-1, 1, (n, ncols)).astype(np.float32)
     C = ops.lower_left(dev(Lp), dev(B), mode=mode).cpu().numpy()

@@ -20,6 +20,14 @@ pytestmark = pytest.mark.gpu
 TOL = {"3xtf32": 1e-5, "tf32": 5e-3, "bf16": 1e-2}
 
 
+@pytest.fixture(params=["1", "0"], ids=["expanded", "on_chip"])
+def expand(request, monkeypatch):
+    """Packed left operands expanded into a dense copy (the default with a
+    full workspace) or built on chip from their packed rows."""
+    monkeypatch.setenv("SMM_EXPAND", request.param)
+    return request.param
+
+
 def dev(x):
     return torch.from_numpy(np.ascontiguousarray(x)).cuda()
 
@@ -113,7 +121,7 @@ def test_upper_packed_golden(cuda, golden, mode):
 @pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
 @pytest.mark.parametrize("packed", [True, False])
 @pytest.mark.parametrize("n_cols", [(1, 1), (5, 9), (128, 64), (129, 200), (300, 260), (1024, 1024)])
-def test_upper_shapes(cuda, packed, n_cols, mode):
+def test_upper_shapes(cuda, expand, packed, n_cols, mode):
     N, ncols = n_cols
     w = W.make_upper(N, ncols, seed=N + ncols)
     U = w["U"] if packed else W.unpack_upper(w["U"], N)
@@ -143,7 +151,7 @@ def test_toeplitz_shapes(cuda, n_cols, mode):
 
 @pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
 @pytest.mark.parametrize("n_cols", [(1, 1), (6, 10), (128, 128), (257, 130), (700, 300)])
-def test_symm_left_shapes(cuda, n_cols, mode):
+def test_symm_left_shapes(cuda, expand, n_cols, mode):
     N, ncols = n_cols
     s = W.make_sandwich(N, seed=N)
     B = W.make_gemm(N, 1, ncols, seed=ncols)["A"]  # N x ncols
@@ -164,7 +172,7 @@ def _slab_call(entry, L, first, B, C, N, ncols, r0, nrows, m, ws, wsb):
 
 @pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
 @pytest.mark.parametrize("kind", ["upper", "symm", "toeplitz"])
-def test_row_slab_entries(cuda, kind, mode):
+def test_row_slab_entries(cuda, expand, kind, mode):
     """The multi-GPU row-slab entries (rows [r0, r0 + nrows) of the product)
     against fp64, slabs starting off the 128- and 256-row tile grid."""
     from cpp1_b200 import _lib
@@ -206,11 +214,33 @@ def test_sandwich_golden(cuda, golden, mode):
 
 @pytest.mark.parametrize("mode", ["3xtf32", "bf16"])
 @pytest.mark.parametrize("N", [1, 7, 130, 512])
-def test_sandwich_shapes(cuda, N, mode):
+def test_sandwich_shapes(cuda, expand, N, mode):
     s = W.make_sandwich(N, seed=N + 1)
     C = host(ops.symm_sandwich(dev(s["A"]), dev(s["S"]), dev(s["B"]), mode=mode))
     R = O.sandwich_rows_f64(s["A"], s["S"], s["B"], np.arange(N))
     assert _relerr_full(C, R) <= TOL[mode]
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
+def test_packed_left_without_room_for_expansion(cuda, mode):
+    """A workspace with no room for the dense copy of the packed operand (none
+    at all when B needs no staging) still computes the product, on chip."""
+    from cpp1_b200 import _lib
+    L = _lib.load()
+    m = ops._mode(mode)
+    N, ncols = 520, 256
+    w = W.make_upper(N, ncols, seed=11)
+    U, B = dev(w["U"]), dev(w["B"])
+    full = L.smm_upper_left_workspace_size(N, ncols, _lib.FMT_PACKED, m)
+    small = full - (N * ((N + 7) // 8 * 8) * 2 if mode == "bf16" else N * ((N + 3) // 4 * 4) * 4)
+    small = small // 256 * 256
+    ws = ops.workspace(max(small, 1), torch.device("cuda"))
+    C = torch.full((N, ncols), float("nan"), device="cuda")
+    rc = L.smm_upper_left(U.data_ptr(), _lib.FMT_PACKED, B.data_ptr(), C.data_ptr(), N, ncols, m,
+                          ws.data_ptr() if small > 0 else None, small, None)
+    assert rc == _lib.SMM_OK, _lib.last_error()
+    R = O.upper_left_rows_f64(w["U"], w["B"], np.arange(N))
+    assert _relerr_full(host(C), R) <= TOL[mode]
 
 
 # ---------------------------------------------------------------- failure detection
