@@ -551,6 +551,8 @@ def roofline(op, n, nrows, mode, step, stream, peaks, units_rank, world):
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4), "traffic": profile_traffic(op),
             "algorithmic_flops_per_launch": mma_flops, "launch_ms": round(launch_ms, 4),
+            "launch_covers": "one whole product call: operand staging / packed-operand expansion kernels "
+                             "plus the contraction kernel (the sandwich: half of its two-product call)",
             "peak_source": src + f"; {passes} MMA pass(es) per useful FLOP"}
 
 
