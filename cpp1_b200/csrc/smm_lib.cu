@@ -151,6 +151,7 @@ struct Operand {
   int dim = 0;
   int row0 = 0;
   bool lower = false;  // dense A with exact zeros above the diagonal (K range clipped)
+  int tri = 0;         // dense B: 1 upper / 2 lower triangular (K range clipped per column tile)
 };
 
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
@@ -190,6 +191,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.a_dim = a.dim;
   p.a_row0 = a.row0;
   p.a_lower = a.lower ? 1 : 0;
+  p.b_tri = b.tri;
   p.b_src = b.src;
   p.b_dim = b.dim;
   p.row_tiles = pair ? (M + 2 * kBM - 1) / (2 * kBM) : (M + kBM - 1) / kBM;
@@ -661,7 +663,7 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
 // ---------------------------------------------------------------- structured right operand
 extern "C" size_t smm_gen_x_struct_workspace_size(int M, int N, int mode) {
   if (M <= 0 || N <= 0) return 0;
-  return staged_bytes_bound(M, N, mode);
+  return staged_bytes_bound(M, N, mode) + expanded_bytes(N, N, mode);
 }
 
 namespace {
@@ -672,10 +674,23 @@ int gen_x_struct(const char* who, BKind bk, const float* A, const float* X, floa
   if (M == 0 || N == 0) return SMM_OK;
   if (!A || !X || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
   if (int rc = check_packed(who, N)) return rc;
-  if (int rc = check_ws(who, ws, ws_bytes, staged_bytes(A, M, N, mode))) return rc;
+  // The packed right operand is expanded into a dense copy (read by TMA, its
+  // K range clipped per column tile when triangular) when the workspace has
+  // room for it, else built on chip by the transform warps.
+  const size_t need_a = staged_bytes(A, M, N, mode);
+  const bool expand = expand_packed(ws, ws_bytes, need_a + expanded_bytes(N, N, mode));
+  if (int rc = check_ws(who, ws, ws_bytes, need_a + (expand ? expanded_bytes(N, N, mode) : 0))) return rc;
   uint8_t* cur = static_cast<uint8_t*>(ws);
   Staged a;
   if (int rc = stage_operand(A, M, N, mode, cur, &a, st)) return rc;
+  if (expand) {
+    const int sf = bk == BKind::UpperPacked ? SMM_STRUCT_UPPER : (bk == BKind::LowerPacked ? SMM_STRUCT_LOWER : SMM_STRUCT_SYMM);
+    Staged x;
+    if (int rc = expand_operand(X, sf, N, 0, N, mode, cur, &x, st)) return rc;
+    Operand xb = dense_op(x.ptr, nullptr, x.ld, x.bf16);
+    xb.tri = sf == SMM_STRUCT_UPPER ? 1 : (sf == SMM_STRUCT_LOWER ? 2 : 0);
+    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16), xb, C, N, M, N, N, st);
+  }
   return run_contraction(AKind::Dense, bk, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16), structured_op(X, N), C, N, M, N, N, st);
 }
 }  // namespace

@@ -119,6 +119,7 @@ struct UmmaParams {
   int a_dim;               // order of the structured matrix
   int a_row0;              // row of the structured matrix that output row 0 maps to
   int a_lower;             // dense A is lower triangular: rows up to g need k <= g only
+  int b_tri;               // dense B is upper (1) / lower (2) triangular: K range clipped per column tile
   const float* b_src;      // packed U / packed S (structured B kinds)
   int b_dim;               // order of the structured right operand
   int row_tiles;           // ceil(M / 128)
@@ -651,8 +652,8 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // An upper-triangular right operand is zero below its diagonal: column
   // tile [n0, n0+BN) needs k < n0 + BN only; a lower-triangular one is zero
   // above it: the tile needs k >= n0 only.
-  if constexpr (BK == BKind::UpperPacked) kb_end = min(kb_end, (n0 + BN - 1) / KS + 1);
-  if constexpr (BK == BKind::LowerPacked) kb_begin = max(kb_begin, n0 / KS);
+  if (BK == BKind::UpperPacked || (BK == BKind::Dense && p.b_tri == 1)) kb_end = min(kb_end, (n0 + BN - 1) / KS + 1);
+  if (BK == BKind::LowerPacked || (BK == BKind::Dense && p.b_tri == 2)) kb_begin = max(kb_begin, n0 / KS);
   // Empty for a tile of L1 L2 wholly above the diagonal: it is written as
   // zeros.  num_kb counts stages of kSubs k-blocks; a last stage reaching
   // past kb_end multiplies zeros (past K, past a triangle's diagonal).

@@ -27,7 +27,7 @@
  *   SMM_MODE_BF16    operands rounded to bf16 (inside the call), fp32
  *                    accumulation
  *
- * A packed upper / symmetric / lower LEFT operand of an entry point with a
+ * A packed upper / symmetric / lower operand of an entry point with a
  * workspace is expanded into a dense copy there (fp32, or bf16 in bf16 mode)
  * and read by TMA; the *_workspace_size functions include that copy.  Given
  * less workspace (at least the rest of the requirement) the entry point builds
@@ -182,8 +182,10 @@ int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float
 
 /* ---- structured right operand (the reference's own orientation) ------- */
 
-/* Workspace for smm_gen_x_upper / smm_gen_x_symm (a padded copy of A when its
- * rows are not 16-byte multiples). */
+/* Workspace for smm_gen_x_upper / smm_gen_x_symm / smm_gen_x_lower: a padded
+ * (or bf16) copy of A, plus the dense expansion of the packed right operand
+ * (see the note on packed operands above; without room for it the operand is
+ * built on chip by the transform warps). */
 size_t smm_gen_x_struct_workspace_size(int M, int N, int mode);
 
 /* C(M x N) = A(M x N) U(N x N, packed upper).  Replaces kernel_gen_x_upper +
@@ -193,7 +195,7 @@ size_t smm_gen_x_struct_workspace_size(int M, int N, int mode);
 int smm_gen_x_upper(const float* A, const float* U_packed, float* C, int M, int N, int mode, void* ws,
                     size_t ws_bytes, void* stream);
 
-/* C(M x N) = A(M x N) S(N x N, packed upper symmetric), S mirrored on chip.
+/* C(M x N) = A(M x N) S(N x N, packed upper symmetric).
  * Replaces kernel_gen_x_symm + copy_B_to_Reg_Symm (src/dsl/codegen_cuda.py:546-806)
  * and Cuda kernels/symmetric.cu:76-271. */
 int smm_gen_x_symm(const float* A, const float* S_packed, float* C, int M, int N, int mode, void* ws,

@@ -25,9 +25,17 @@ def relerr64(C, R):
     return O.relerr(np.ascontiguousarray(C, np.float32), np.asarray(R, np.float64))
 
 
+@pytest.fixture(params=["1", "0"], ids=["expanded", "on_chip"])
+def expand(request, monkeypatch):
+    """Packed right operands expanded into a dense copy read by TMA (the
+    default with a full workspace) or built on chip by the transform warps."""
+    monkeypatch.setenv("SMM_EXPAND", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("mode,tol", [("3xtf32", 1e-5), ("bf16", 1e-2)])
-@pytest.mark.parametrize("mn", [(1, 1), (7, 9), (128, 128), (200, 130), (512, 384)])
-def test_gen_x_upper(cuda, mn, mode, tol):
+@pytest.mark.parametrize("mn", [(1, 1), (7, 9), (128, 128), (200, 130), (512, 384), (300, 1000)])
+def test_gen_x_upper(cuda, expand, mn, mode, tol):
     M, N = mn
     A = W.make_gemm(M, 1, N, seed=M)["A"]  # M x N
     Up = W.make_upper(N, 1, seed=N)["U"]
@@ -36,14 +44,15 @@ def test_gen_x_upper(cuda, mn, mode, tol):
     assert relerr64(C, R) <= tol
 
 
-@pytest.mark.parametrize("mn", [(1, 1), (5, 6), (128, 256), (300, 257)])
-def test_gen_x_symm(cuda, mn):
+@pytest.mark.parametrize("mode,tol", [("3xtf32", 1e-5), ("bf16", 1e-2)])
+@pytest.mark.parametrize("mn", [(1, 1), (5, 6), (128, 256), (300, 257), (700, 600)])
+def test_gen_x_symm(cuda, expand, mn, mode, tol):
     M, N = mn
     A = W.make_gemm(M, 1, N, seed=M + 1)["A"]  # M x N
     Sp = W.make_sandwich(N, seed=N)["S"]
-    C = ops.gen_x_symm(dev(A), dev(Sp)).cpu().numpy()
+    C = ops.gen_x_symm(dev(A), dev(Sp), mode=mode).cpu().numpy()
     R = A.astype(np.float64) @ W.unpack_symmetric(Sp, N).astype(np.float64)
-    assert relerr64(C, R) <= 1e-5
+    assert relerr64(C, R) <= tol
 
 
 @pytest.mark.parametrize("mode,tol", [("3xtf32", 1e-5), ("bf16", 1e-2)])

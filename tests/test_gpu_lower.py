@@ -51,7 +51,9 @@ def test_lower_left(cuda, tiles, mode, tol, n, ncols, expand, monkeypatch):
 
 @pytest.mark.parametrize("mode,tol", MODES)
 @pytest.mark.parametrize("m,n", [(1, 1), (9, 7), (128, 128), (200, 300), (512, 1000)])
-def test_gen_x_lower(cuda, tiles, mode, tol, m, n):
+@pytest.mark.parametrize("expand", ["1", "0"])
+def test_gen_x_lower(cuda, tiles, mode, tol, m, n, expand, monkeypatch):
+    monkeypatch.setenv("SMM_EXPAND", expand)
     A = np.random.default_rng(m).uniform(-1, 1, (m, n)).astype(np.float32)
     Lp = lower_packed(n, n + 3)
     C = ops.gen_x_lower(dev(A), dev(Lp), mode=mode).cpu().numpy()
