@@ -75,11 +75,15 @@ SIGNATURES = [
     ("smm_gen_x_upper", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_gen_x_symm", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_symm_x_symm", _i, [_vp, _vp, _vp, _i, _i, _vp]),
+    ("smm_symm_x_symm_workspace_size", _sz, [_i, _i]),
+    ("smm_symm_x_symm_ws", _i, [_vp, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     ("smm_symm_sandwich_noalloc", _i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     ("smm_gen_x_lower", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_lower_left_workspace_size", _sz, [_i, _i, _i]),
     ("smm_lower_left", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_lower_x_lower", _i, [_vp, _vp, _vp, _i, _i, _vp]),
+    ("smm_lower_x_lower_workspace_size", _sz, [_i, _i]),
+    ("smm_lower_x_lower_ws", _i, [_vp, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     ("smm_add", _i, [_vp, _vp, _vp, _ll, _vp]),
     ("smm_add_struct", _i, [_vp, _vp, _i, _vp, _i, _vp]),
     ("smm_unpack", _i, [_vp, _i, _vp, _i, _vp]),

@@ -118,8 +118,11 @@ extern "C" int smm_compat_gen_x_upper(const float* A, const float* U, float* C, 
 
 extern "C" int smm_compat_symm_x_symm(const float* S1, const float* S2, float* C, float* gflops_out, int n,
                                       float* time_ms_out) {
-  return compat_run("smm_compat_symm_x_symm", gflops_out, time_ms_out, cube(n), 0,
-                    [&](void*, size_t, cudaStream_t st) { return smm_symm_x_symm(S1, S2, C, n, SMM_COMPAT_MODE, st); });
+  return compat_run("smm_compat_symm_x_symm", gflops_out, time_ms_out, cube(n),
+                    n > 0 ? smm_symm_x_symm_workspace_size(n, SMM_COMPAT_MODE) : 0,
+                    [&](void* ws, size_t wb, cudaStream_t st) {
+                      return smm_symm_x_symm_ws(S1, S2, C, n, SMM_COMPAT_MODE, ws, wb, st);
+                    });
 }
 
 extern "C" int smm_compat_gen_x_lower(const float* A, const float* L, float* C, float* gflops_out, int n,
@@ -142,8 +145,11 @@ extern "C" int smm_compat_lower_x_gen(const float* L, const float* B, float* C, 
 
 extern "C" int smm_compat_lower_x_lower(const float* L1, const float* L2, float* C, float* gflops_out, int n,
                                         float* time_ms_out) {
-  return compat_run("smm_compat_lower_x_lower", gflops_out, time_ms_out, cube(n), 0,
-                    [&](void*, size_t, cudaStream_t st) { return smm_lower_x_lower(L1, L2, C, n, SMM_COMPAT_MODE, st); });
+  return compat_run("smm_compat_lower_x_lower", gflops_out, time_ms_out, cube(n),
+                    n > 0 ? smm_lower_x_lower_workspace_size(n, SMM_COMPAT_MODE) : 0,
+                    [&](void* ws, size_t wb, cudaStream_t st) {
+                      return smm_lower_x_lower_ws(L1, L2, C, n, SMM_COMPAT_MODE, ws, wb, st);
+                    });
 }
 
 extern "C" int smm_compat_add_gen_symm(const float* A, const float* S, float* C, float* gflops_out, int n,

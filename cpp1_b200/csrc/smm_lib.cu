@@ -711,13 +711,43 @@ extern "C" int smm_gen_x_lower(const float* A, const float* Lp, float* C, int M,
 }
 
 extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N, int mode, void* stream) {
-  if (N < 0) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: negative shape");
-  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: unknown mode %d", mode);
+  return smm_symm_x_symm_ws(S1, S2, C, N, mode, nullptr, 0, stream);
+}
+
+namespace {
+// Product of two packed operands of order N: both expanded into dense copies
+// in the workspace when it has room for them (TMA-fed; a lower-triangular
+// left copy clips each row tile's K range from above, a lower-triangular
+// right copy each column tile's from below), else both built on chip.
+int packed_x_packed(const char* who, AKind ak, BKind bk, int sf, const float* X1, const float* X2, float* C, int N,
+                    int mode, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (N < 0) return set_error(SMM_ERR_INVALID, "%s: negative shape", who);
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
   if (N == 0) return SMM_OK;
-  if (!S1 || !S2 || !C) return set_error(SMM_ERR_INVALID, "smm_symm_x_symm: null pointer");
-  if (int rc = check_packed("smm_symm_x_symm", N)) return rc;
-  return run_contraction(AKind::SymmPacked, BKind::SymmPacked, mode, structured_op(S1, N), structured_op(S2, N), C,
-                         N, N, N, N, as_stream(stream));
+  if (!X1 || !X2 || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
+  if (int rc = check_packed(who, N)) return rc;
+  if (!expand_packed(ws, ws_bytes, 2 * expanded_bytes(N, N, mode)))
+    return run_contraction(ak, bk, mode, structured_op(X1, N), structured_op(X2, N), C, N, N, N, N, st);
+  if (int rc = check_ws(who, ws, ws_bytes, 2 * expanded_bytes(N, N, mode))) return rc;
+  uint8_t* cur = static_cast<uint8_t*>(ws);
+  Staged a, b;
+  if (int rc = expand_operand(X1, sf, N, 0, N, mode, cur, &a, st)) return rc;
+  if (int rc = expand_operand(X2, sf, N, 0, N, mode, cur, &b, st)) return rc;
+  Operand ao = dense_op(a.ptr, nullptr, a.ld, a.bf16), bo = dense_op(b.ptr, nullptr, b.ld, b.bf16);
+  ao.lower = sf == SMM_STRUCT_LOWER;
+  bo.tri = sf == SMM_STRUCT_LOWER ? 2 : 0;
+  return run_contraction(AKind::Dense, BKind::Dense, mode, ao, bo, C, N, N, N, N, st);
+}
+}  // namespace
+
+extern "C" size_t smm_symm_x_symm_workspace_size(int N, int mode) {
+  return N <= 0 ? 0 : 2 * expanded_bytes(N, N, mode);
+}
+
+extern "C" int smm_symm_x_symm_ws(const float* S1, const float* S2, float* C, int N, int mode, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  return packed_x_packed("smm_symm_x_symm", AKind::SymmPacked, BKind::SymmPacked, SMM_STRUCT_SYMM, S1, S2, C, N,
+                         mode, ws, ws_bytes, as_stream(stream));
 }
 
 // ---------------------------------------------------------------- lower-triangular operands
@@ -754,13 +784,17 @@ extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, 
 }
 
 extern "C" int smm_lower_x_lower(const float* L1, const float* L2, float* C, int N, int mode, void* stream) {
-  if (N < 0) return set_error(SMM_ERR_INVALID, "smm_lower_x_lower: negative shape");
-  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_lower_x_lower: unknown mode %d", mode);
-  if (N == 0) return SMM_OK;
-  if (!L1 || !L2 || !C) return set_error(SMM_ERR_INVALID, "smm_lower_x_lower: null pointer");
-  if (int rc = check_packed("smm_lower_x_lower", N)) return rc;
-  return run_contraction(AKind::LowerPacked, BKind::LowerPacked, mode, structured_op(L1, N), structured_op(L2, N), C,
-                         N, N, N, N, as_stream(stream));
+  return smm_lower_x_lower_ws(L1, L2, C, N, mode, nullptr, 0, stream);
+}
+
+extern "C" size_t smm_lower_x_lower_workspace_size(int N, int mode) {
+  return N <= 0 ? 0 : 2 * expanded_bytes(N, N, mode);
+}
+
+extern "C" int smm_lower_x_lower_ws(const float* L1, const float* L2, float* C, int N, int mode, void* ws,
+                                    size_t ws_bytes, void* stream) {
+  return packed_x_packed("smm_lower_x_lower", AKind::LowerPacked, BKind::LowerPacked, SMM_STRUCT_LOWER, L1, L2, C, N,
+                         mode, ws, ws_bytes, as_stream(stream));
 }
 
 // ---------------------------------------------------------------- timeout probe

@@ -236,7 +236,10 @@ def lower_x_lower(L1: torch.Tensor, L2: torch.Tensor, mode: str = "3xtf32", out:
     N = _packed_order("L1", L1)
     L2 = _check_f32("L2", L2, L1.numel())
     C = _out(out, (N, N), L1)
-    _lib.check(_lib.load().smm_lower_x_lower(_ptr(L1), _ptr(L2), _ptr(C), N, _mode(mode), _stream_ptr(stream)),
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_lower_x_lower_workspace_size(N, m), L1.device)
+    _lib.check(L.smm_lower_x_lower_ws(_ptr(L1), _ptr(L2), _ptr(C), N, m, ws, wsb, _stream_ptr(stream)),
                "smm_lower_x_lower")
     return C
 
@@ -251,8 +254,10 @@ def symm_x_symm(S1: torch.Tensor, S2: torch.Tensor, mode: str = "3xtf32", out: O
         raise ValueError(f"S1 has {p} elements, not a packed triangle")
     S2 = _check_f32("S2", S2, p)
     C = _out(out, (N, N), S1)
+    m = _mode(mode)
     L = _lib.load()
-    _lib.check(L.smm_symm_x_symm(_ptr(S1), _ptr(S2), _ptr(C), N, _mode(mode), _stream_ptr(stream)),
+    ws, wsb = _ws_args(L.smm_symm_x_symm_workspace_size(N, m), S1.device)
+    _lib.check(L.smm_symm_x_symm_ws(_ptr(S1), _ptr(S2), _ptr(C), N, m, ws, wsb, _stream_ptr(stream)),
                "smm_symm_x_symm")
     return C
 

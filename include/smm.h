@@ -210,8 +210,16 @@ int smm_gen_x_lower(const float* A, const float* L_packed, float* C, int M, int 
                     size_t ws_bytes, void* stream);
 
 /* C(N x N) = S1 S2, both packed upper symmetric.  Replaces kernel_symm_x_symm
- * (src/dsl/codegen_cuda.py:1340-1613).  No workspace. */
+ * (src/dsl/codegen_cuda.py:1340-1613).  No workspace: both operands are built
+ * on chip from their packed rows. */
 int smm_symm_x_symm(const float* S1_packed, const float* S2_packed, float* C, int N, int mode, void* stream);
+
+/* The same product with a workspace: given smm_symm_x_symm_workspace_size
+ * bytes, both operands are expanded into dense copies there and read by TMA
+ * (about 2.5x faster at N = 8192); given less, as smm_symm_x_symm. */
+size_t smm_symm_x_symm_workspace_size(int N, int mode);
+int smm_symm_x_symm_ws(const float* S1_packed, const float* S2_packed, float* C, int N, int mode, void* ws,
+                       size_t ws_bytes, void* stream);
 
 /* ---- lower-triangular operands (packed lower, idx(i,j) = i(i+1)/2 + j) ---- */
 
@@ -229,6 +237,13 @@ int smm_lower_left(const float* L_packed, const float* B, float* C, int N, int n
  * backend (src/dsl/codegen_multiply_avx.py:644-923).  Output tiles wholly
  * above the diagonal are written as zeros without a K loop.  No workspace. */
 int smm_lower_x_lower(const float* L1_packed, const float* L2_packed, float* C, int N, int mode, void* stream);
+
+/* The same product with a workspace: given smm_lower_x_lower_workspace_size
+ * bytes, both operands are expanded into dense copies there and read by TMA,
+ * with the same K-range clipping; given less, as smm_lower_x_lower. */
+size_t smm_lower_x_lower_workspace_size(int N, int mode);
+int smm_lower_x_lower_ws(const float* L1_packed, const float* L2_packed, float* C, int N, int mode, void* ws,
+                         size_t ws_bytes, void* stream);
 
 /* ---- elementwise sums and storage converters (HBM-bound, bit-exact) ---- */
 

@@ -56,8 +56,8 @@ def test_gen_x_symm(cuda, expand, mn, mode, tol):
 
 
 @pytest.mark.parametrize("mode,tol", [("3xtf32", 1e-5), ("bf16", 1e-2)])
-@pytest.mark.parametrize("N", [1, 3, 128, 257])
-def test_symm_x_symm(cuda, N, mode, tol):
+@pytest.mark.parametrize("N", [1, 3, 128, 257, 700])
+def test_symm_x_symm(cuda, expand, N, mode, tol):
     S1 = W.make_sandwich(N, seed=N)["S"]
     S2 = W.make_sandwich(N, seed=N + 9)["S"]
     C = ops.symm_x_symm(dev(S1), dev(S2), mode=mode).cpu().numpy()

@@ -63,7 +63,9 @@ def test_gen_x_lower(cuda, tiles, mode, tol, m, n, expand, monkeypatch):
 
 @pytest.mark.parametrize("mode,tol", MODES)
 @pytest.mark.parametrize("n", [1, 7, 128, 300, 1000])
-def test_lower_x_lower(cuda, tiles, mode, tol, n):
+@pytest.mark.parametrize("expand", ["1", "0"])
+def test_lower_x_lower(cuda, tiles, mode, tol, n, expand, monkeypatch):
+    monkeypatch.setenv("SMM_EXPAND", expand)
     L1, L2 = lower_packed(n, 2 * n), lower_packed(n, 2 * n + 1)
     C = ops.lower_x_lower(dev(L1), dev(L2), mode=mode).cpu().numpy()
     D1, D2 = O.unpack_f32(L1, "lower", n), O.unpack_f32(L2, "lower", n)
