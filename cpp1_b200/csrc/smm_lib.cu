@@ -236,15 +236,34 @@ __global__ void pad_rows_kernel(const float* __restrict__ src, int rows, int col
 }
 
 // bf16 copy of an fp32 matrix (round to nearest even), rows padded with zeros
-// to ld_dst elements (a 16-byte multiple).
-__global__ void to_bf16_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
-                               __nv_bfloat16* __restrict__ dst, int ld_dst) {
-  const long long total = static_cast<long long>(rows) * ld_dst;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / ld_dst;
-    const int c = static_cast<int>(i - r * ld_dst);
-    dst[i] = __float2bfloat16_rn(c < cols ? src[r * ld_src + c] : 0.0f);
+// to ld_dst elements (a multiple of 8).  Each thread converts 8 consecutive
+// elements of a row: two 128-bit streaming loads when the source rows are
+// 16-byte aligned (vec), one 128-bit store.  Blocks run along a row (x) and
+// stride over rows (y); no per-element index division.
+__global__ void __launch_bounds__(256) to_bf16_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
+                                                      __nv_bfloat16* __restrict__ dst, int ld_dst, int vec) {
+  const int c = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (c >= ld_dst) return;
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    const float* s = src + static_cast<long long>(r) * ld_src + c;
+    float v[8];
+    if (vec && c + 8 <= cols) {
+      const float4 a = __ldcs(reinterpret_cast<const float4*>(s));
+      const float4 b = __ldcs(reinterpret_cast<const float4*>(s + 4));
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = c + e < cols ? s[e] : 0.0f;
+    }
+    uint4 o;
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[4], v[5]), h3 = __floats2bfloat162_rn(v[6], v[7]);
+    o.x = *reinterpret_cast<uint32_t*>(&h0);
+    o.y = *reinterpret_cast<uint32_t*>(&h1);
+    o.z = *reinterpret_cast<uint32_t*>(&h2);
+    o.w = *reinterpret_cast<uint32_t*>(&h3);
+    *reinterpret_cast<uint4*>(dst + static_cast<long long>(r) * ld_dst + c) = o;
   }
 }
 
@@ -276,9 +295,10 @@ int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_c
     const int ld = round8(cols);
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
     ws_cur += bf16_plane_bytes(rows, cols);
-    const long long total = static_cast<long long>(rows) * ld;
-    const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-    to_bf16_kernel<<<std::max(grid, 1), 256, 0, st>>>(src, rows, cols, cols, dst, ld);
+    const int gx = (ld / 8 + 255) / 256;
+    const int gy = std::max(1, std::min(rows, std::max(1, 148 * 16 / gx)));
+    const int vec = (cols % 4 == 0 && aligned16(src)) ? 1 : 0;
+    to_bf16_kernel<<<dim3(gx, gy), 256, 0, st>>>(src, rows, cols, cols, dst, ld, vec);
     count_launch();
     SMM_CUDA_TRY(cudaGetLastError(), "bf16 staging launch");
     *out = {nullptr, nullptr, ld, dst};
