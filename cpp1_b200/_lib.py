@@ -58,6 +58,16 @@ SIGNATURES = [
     ("smm_diag_cols", _i, [_vp, _vp, _vp, _i, _i, _vp]),
     ("smm_diag_rows_host_workspace_size", _sz, [_i, _i]),
     ("smm_diag_rows_host", _i, [_vp, _vp, _vp, _i, _i, _vp, _sz]),
+    ("smm_gemm_host_workspace_size", _sz, [_i, _i, _i, _i]),
+    ("smm_gemm_host", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz]),
+    ("smm_upper_left_host_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_upper_left_host", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz]),
+    ("smm_symm_left_host_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_symm_left_host", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz]),
+    ("smm_toeplitz_left_host_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_toeplitz_left_host", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz]),
+    ("smm_symm_sandwich_host_workspace_size", _sz, [_i, _i]),
+    ("smm_symm_sandwich_host", _i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _sz]),
     ("smm_gemm_workspace_size", _sz, [_i, _i, _i, _i]),
     ("smm_upper_left_workspace_size", _sz, [_i, _i, _i, _i]),
     ("smm_toeplitz_left_workspace_size", _sz, [_i, _i, _i]),

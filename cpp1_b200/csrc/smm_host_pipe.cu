@@ -1,0 +1,234 @@
+// Host-buffer contractions (smm_*_host): C = L B with every operand in host
+// memory, the left operand(s) copied once and B streamed in column chunks
+// whose copies overlap the products.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "smm_contract.h"
+
+// C = L B with L, B and C in host memory (pinned for overlap; pageable works,
+// synchronously): the drop-in for callers of the reference's CPU kernels,
+// which take host arrays.  The left operand(s) cross PCIe once and are
+// prepared on the device (staged, or a packed operand expanded); B then
+// streams through in column chunks.  Chunk j alternates between two streams:
+// its 2-D copy-in, its product and its 2-D copy-out into C's columns are
+// ordered on that stream, and they overlap the other stream's (PCIe is full
+// duplex: chunk j's copy-out runs beside chunk j+1's copy-in).
+namespace smm {
+namespace {
+
+enum class HostLeft { Gemm, Upper, Symm, Toeplitz, Sandwich };
+
+struct HostStreams {
+  cudaStream_t st[2] = {nullptr, nullptr};
+  cudaEvent_t left_ready = nullptr;
+  bool init = false;
+};
+
+int host_streams(HostStreams** out) {
+  static HostStreams per_dev[64];
+  int dev = 0;
+  SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  HostStreams& h = per_dev[dev & 63];
+  if (!h.init) {
+    for (auto& s : h.st) SMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
+    SMM_CUDA_TRY(cudaEventCreateWithFlags(&h.left_ready, cudaEventDisableTiming), "event create");
+    h.init = true;
+  }
+  *out = &h;
+  return SMM_OK;
+}
+
+// Columns of B per chunk: about an eighth of N in multiples of 256, at least
+// 1024 (narrower products lose too much to partial waves), at most N.
+int host_chunk_cols(int N) { return std::min(N, std::max(1024, (N / 8 + 255) / 256 * 256)); }
+
+// Shapes: C is M x N, L is M x K; the sandwich has M = K = N.
+struct HostShape {
+  HostLeft kind;
+  int M, N, K, mode;
+};
+
+size_t left_raw_bytes(const HostShape& h) {
+  switch (h.kind) {
+    case HostLeft::Gemm: return round256(static_cast<size_t>(h.M) * h.K * 4);
+    case HostLeft::Upper:
+    case HostLeft::Symm: return round256(static_cast<size_t>(h.K) * (h.K + 1) / 2 * 4);
+    case HostLeft::Toeplitz: return round256((2 * static_cast<size_t>(h.K) - 1) * 4);
+    default: return round256(static_cast<size_t>(h.N) * h.N * 4) + round256(static_cast<size_t>(h.N) * (h.N + 1) / 2 * 4);
+  }
+}
+size_t left_prep_bytes(const HostShape& h) {
+  switch (h.kind) {
+    case HostLeft::Gemm: return staged_bytes_bound(h.M, h.K, h.mode);
+    case HostLeft::Upper:
+    case HostLeft::Symm: return expanded_bytes(h.K, h.K, h.mode);
+    case HostLeft::Toeplitz: return 0;
+    default: return staged_bytes_bound(h.N, h.N, h.mode) + expanded_bytes(h.N, h.N, h.mode);
+  }
+}
+// One stream's chunk buffers: raw B chunk, its staged copy, the sandwich's X
+// chunk (+ bf16 copy), the C chunk.
+size_t chunk_bytes(const HostShape& h) {
+  const int w = host_chunk_cols(h.N);
+  size_t b = round256(static_cast<size_t>(h.K) * w * 4) + staged_bytes_bound(h.K, w, h.mode) +
+             round256(static_cast<size_t>(h.M) * w * 4);
+  if (h.kind == HostLeft::Sandwich) b += plane_bytes(h.N, w) + bf16_plane_bytes(h.N, w);
+  return b;
+}
+size_t host_ws_bytes(const HostShape& h) {
+  if (h.M <= 0 || h.N <= 0 || h.K <= 0) return 0;
+  return left_raw_bytes(h) + left_prep_bytes(h) + 2 * chunk_bytes(h);
+}
+
+int host_product(const char* who, const HostShape& h, const float* L1, const float* L2, const float* B, float* C,
+                 void* dev_ws, size_t ws_bytes) {
+  const int M = h.M, N = h.N, K = h.K, mode = h.mode;
+  if (M < 0 || N < 0 || K < 0) return set_error(SMM_ERR_INVALID, "%s: negative shape", who);
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
+  if (M == 0 || N == 0) return SMM_OK;
+  if (!L1 || !B || !C || (h.kind == HostLeft::Sandwich && !L2)) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
+  if (h.kind == HostLeft::Upper || h.kind == HostLeft::Symm || h.kind == HostLeft::Sandwich)
+    if (int rc = check_packed(who, K)) return rc;
+  if (int rc = check_ws(who, dev_ws, ws_bytes, host_ws_bytes(h))) return rc;
+  HostStreams* hs = nullptr;
+  if (int rc = host_streams(&hs)) return rc;
+  cudaStream_t s0 = hs->st[0];
+
+  // ---- left operand(s): copy in once, prepare on stream 0
+  uint8_t* cur = static_cast<uint8_t*>(dev_ws);
+  Operand left, amat;  // amat: the sandwich's A
+  if (h.kind == HostLeft::Gemm || h.kind == HostLeft::Sandwich) {
+    float* a = reinterpret_cast<float*>(cur);
+    const size_t ab = static_cast<size_t>(M) * K * 4;
+    cur += round256(ab);
+    SMM_CUDA_TRY(cudaMemcpyAsync(a, L1, ab, cudaMemcpyHostToDevice, s0), "copy A");
+    Staged st;
+    if (int rc = stage_operand(a, M, K, mode, cur, &st, s0)) return rc;
+    amat = dense_op(st.ptr, st.lo, st.ld, st.bf16);
+    left = amat;
+  }
+  if (h.kind != HostLeft::Gemm) {
+    const float* src = h.kind == HostLeft::Sandwich ? L2 : L1;
+    const size_t len = h.kind == HostLeft::Toeplitz ? 2 * static_cast<size_t>(K) - 1 : static_cast<size_t>(K) * (K + 1) / 2;
+    float* p = reinterpret_cast<float*>(cur);
+    cur += round256(len * 4);
+    SMM_CUDA_TRY(cudaMemcpyAsync(p, src, len * 4, cudaMemcpyHostToDevice, s0), "copy structured operand");
+    if (h.kind == HostLeft::Toeplitz) {
+      left = structured_op(p, K);
+    } else {
+      const int sf = h.kind == HostLeft::Upper ? SMM_STRUCT_UPPER : SMM_STRUCT_SYMM;
+      Staged ex;
+      if (int rc = expand_operand(p, sf, K, 0, K, mode, cur, &ex, s0)) return rc;
+      left = dense_op(ex.ptr, nullptr, ex.ld, ex.bf16);
+      left.dim = K;
+    }
+  }
+  const AKind lk = h.kind == HostLeft::Toeplitz ? AKind::Toeplitz
+                   : h.kind == HostLeft::Upper  ? AKind::UpperDense
+                                                : AKind::Dense;
+  SMM_CUDA_TRY(cudaEventRecord(hs->left_ready, s0), "event record");
+  SMM_CUDA_TRY(cudaStreamWaitEvent(hs->st[1], hs->left_ready, 0), "stream wait");
+
+  // ---- B in column chunks, alternating streams
+  const int w = host_chunk_cols(N);
+  uint8_t* region[2] = {cur, cur + chunk_bytes(h)};
+  int c = 0;
+  for (int c0 = 0; c0 < N; c0 += w, ++c) {
+    const int k = c & 1;
+    const int wc = std::min(w, N - c0);
+    cudaStream_t st = hs->st[k];
+    uint8_t* r = region[k];
+    float* braw = reinterpret_cast<float*>(r);
+    r += round256(static_cast<size_t>(K) * w * 4);
+    uint8_t* stage_cur = r;
+    r += staged_bytes_bound(K, w, mode);
+    float* xch = nullptr;
+    __nv_bfloat16* xbf = nullptr;
+    if (h.kind == HostLeft::Sandwich) {
+      xch = reinterpret_cast<float*>(r);
+      r += plane_bytes(N, w);
+      xbf = reinterpret_cast<__nv_bfloat16*>(r);
+      r += bf16_plane_bytes(N, w);
+    }
+    float* cch = reinterpret_cast<float*>(r);
+    SMM_CUDA_TRY(cudaMemcpy2DAsync(braw, static_cast<size_t>(wc) * 4, B + c0, static_cast<size_t>(N) * 4,
+                                   static_cast<size_t>(wc) * 4, K, cudaMemcpyHostToDevice, st),
+                 "copy B chunk");
+    Staged bs;
+    if (int rc = stage_operand(braw, K, wc, mode, stage_cur, &bs, st)) return rc;
+    const Operand bop = dense_op(bs.ptr, bs.lo, bs.ld, bs.bf16);
+    if (h.kind == HostLeft::Sandwich) {
+      // X_j = S B_j (its bf16 copy too in bf16 mode), then C_j = A X_j
+      const int ldx = round4(wc), ldx_bf = round8(wc);
+      const bool bf = mode == SMM_MODE_BF16;
+      if (bf && ldx_bf != wc)
+        SMM_CUDA_TRY(cudaMemsetAsync(xbf, 0, bf16_plane_bytes(N, wc), st), "zero bf16 intermediate");
+      if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, left, bop, xch, ldx, N, wc, N, st, nullptr,
+                                   bf ? xbf : nullptr, ldx_bf))
+        return rc;
+      if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, amat,
+                                   dense_op(xch, nullptr, bf ? ldx_bf : ldx, bf ? xbf : nullptr), cch, wc, N, wc, N,
+                                   st))
+        return rc;
+    } else {
+      if (int rc = run_contraction(lk, BKind::Dense, mode, left, bop, cch, wc, M, wc, K, st)) return rc;
+    }
+    SMM_CUDA_TRY(cudaMemcpy2DAsync(C + c0, static_cast<size_t>(N) * 4, cch, static_cast<size_t>(wc) * 4,
+                                   static_cast<size_t>(wc) * 4, M, cudaMemcpyDeviceToHost, st),
+                 "copy C chunk");
+  }
+  SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[1]), "stream sync");
+  return smm_device_status(s0);
+}
+
+}  // namespace
+}  // namespace smm
+
+using namespace smm;
+
+extern "C" size_t smm_gemm_host_workspace_size(int M, int N, int K, int mode) {
+  return host_ws_bytes({HostLeft::Gemm, M, N, K, mode});
+}
+extern "C" int smm_gemm_host(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* dev_ws,
+                             size_t ws_bytes) {
+  return host_product("smm_gemm_host", {HostLeft::Gemm, M, N, K, mode}, A, nullptr, B, C, dev_ws, ws_bytes);
+}
+
+extern "C" size_t smm_upper_left_host_workspace_size(int N, int ncols, int mode) {
+  return host_ws_bytes({HostLeft::Upper, N, ncols, N, mode});
+}
+extern "C" int smm_upper_left_host(const float* U_packed, const float* B, float* C, int N, int ncols, int mode,
+                                   void* dev_ws, size_t ws_bytes) {
+  return host_product("smm_upper_left_host", {HostLeft::Upper, N, ncols, N, mode}, U_packed, nullptr, B, C, dev_ws,
+                      ws_bytes);
+}
+
+extern "C" size_t smm_symm_left_host_workspace_size(int N, int ncols, int mode) {
+  return host_ws_bytes({HostLeft::Symm, N, ncols, N, mode});
+}
+extern "C" int smm_symm_left_host(const float* S_packed, const float* B, float* C, int N, int ncols, int mode,
+                                  void* dev_ws, size_t ws_bytes) {
+  return host_product("smm_symm_left_host", {HostLeft::Symm, N, ncols, N, mode}, S_packed, nullptr, B, C, dev_ws,
+                      ws_bytes);
+}
+
+extern "C" size_t smm_toeplitz_left_host_workspace_size(int N, int ncols, int mode) {
+  return host_ws_bytes({HostLeft::Toeplitz, N, ncols, N, mode});
+}
+extern "C" int smm_toeplitz_left_host(const float* g, const float* B, float* C, int N, int ncols, int mode,
+                                      void* dev_ws, size_t ws_bytes) {
+  return host_product("smm_toeplitz_left_host", {HostLeft::Toeplitz, N, ncols, N, mode}, g, nullptr, B, C, dev_ws,
+                      ws_bytes);
+}
+
+extern "C" size_t smm_symm_sandwich_host_workspace_size(int N, int mode) {
+  return host_ws_bytes({HostLeft::Sandwich, N, N, N, mode});
+}
+extern "C" int smm_symm_sandwich_host(const float* A, const float* S_packed, const float* B, float* C, int N,
+                                      int mode, void* dev_ws, size_t ws_bytes) {
+  return host_product("smm_symm_sandwich_host", {HostLeft::Sandwich, N, N, N, mode}, A, S_packed, B, C, dev_ws,
+                      ws_bytes);
+}

@@ -1,6 +1,10 @@
 // libsmm host library: C ABI entry points for the tensor-core contractions
-// (dense GEMM, upper-triangular-left, Toeplitz-left, symmetric-left and the
-// symmetric sandwich), error/status plumbing and TMA descriptor encoding.
+// on device buffers (dense GEMM, triangular / Toeplitz / symmetric operands
+// on either side, the symmetric sandwich), the contraction driver
+// (run_contraction: tile policy, TMA descriptors, launch), error/status
+// plumbing, the timeout probe and the allocation-free sandwich.  Operand
+// staging and expansion live in smm_stage.cu, the host-buffer pipeline in
+// smm_host_pipe.cu.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -11,6 +15,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "smm_contract.h"
 #include "smm_host.h"
 #include "smm_launch.cuh"
 
@@ -96,11 +101,6 @@ int make_tmap(CUtensorMap* m, const void* base, int rows, int cols, int ld, int 
   return SMM_OK;
 }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
-size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
-int round4(int x) { return (x + 3) & ~3; }
-int round8(int x) { return (x + 7) & ~7; }
-
 // ---------------------------------------------------------------- launches
 // CTA pairs (256-row tiles, tcgen05 cta_group::2) whenever there are at least
 // two row tiles and the pair tiles fill about a wave of the 74 SM pairs.
@@ -136,27 +136,20 @@ int pick_bn(int M, int N, bool pair) {
 // smm_debug_trace_next, consumed by one launch).
 thread_local uint32_t* g_trace = nullptr;
 
+}  // namespace
+
 bool valid_mode(int mode) { return mode == SMM_MODE_3XTF32 || mode == SMM_MODE_TF32 || mode == SMM_MODE_BF16; }
+
+int check_packed(const char* who, int N) {
+  if (N > kMaxPackedOrder)
+    return set_error(SMM_ERR_INVALID, "%s: packed order N = %d exceeds %d", who, N, kMaxPackedOrder);
+  return SMM_OK;
+}
 
 // Core contraction: C(M x N, ldc) = Aop(M x K) * B(K x N, ldb).
 // Preconditions: B (and A when dense) 16-byte aligned with ld % 4 == 0.
-// Operand description for run_contraction: a dense TMA-loaded matrix (ptr,
-// ld) or a structured one (src, dim, row0).
-struct Operand {
-  const float* ptr = nullptr;
-  const float* lo = nullptr;            // lo plane of ptr (3xTF32), same ld
-  const __nv_bfloat16* bf16 = nullptr;  // bf16 copy (bf16 mode), leading dimension ld
-  int ld = 0;
-  const float* src = nullptr;
-  int dim = 0;
-  int row0 = 0;
-  bool lower = false;  // dense A with exact zeros above the diagonal (K range clipped)
-  int tri = 0;         // dense B: 1 upper / 2 lower triangular (K range clipped per column tile)
-};
-
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
-                    int N, int K, cudaStream_t st, float* C_lo = nullptr, __nv_bfloat16* C_bf16 = nullptr,
-                    int ldc_bf16 = 0) {
+                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16) {
   const bool bf16 = (mode == SMM_MODE_BF16);
   const bool pair = use_pairs(M, N);
   const int bn = pick_bn(M, N, pair);
@@ -205,7 +198,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   return launch_kinds(ak, bk, bn, pair, mode, m, p, st);
 }
 
-Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf = nullptr) {
+Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf) {
   Operand o;
   o.ptr = ptr;
   o.lo = lo;
@@ -213,7 +206,7 @@ Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16*
   o.bf16 = bf;
   return o;
 }
-Operand structured_op(const float* src, int dim, int row0 = 0) {
+Operand structured_op(const float* src, int dim, int row0) {
   Operand o;
   o.src = src;
   o.dim = dim;
@@ -221,227 +214,6 @@ Operand structured_op(const float* src, int dim, int row0 = 0) {
   return o;
 }
 
-// ---------------------------------------------------------------- operand staging
-// dst = src with zero columns appended up to ld_dst (a 16-byte multiple), so
-// that TMA can address its rows.
-__global__ void pad_rows_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
-                                float* __restrict__ dst, int ld_dst) {
-  const long long total = static_cast<long long>(rows) * ld_dst;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / ld_dst;
-    const int c = static_cast<int>(i - r * ld_dst);
-    dst[i] = c < cols ? src[r * ld_src + c] : 0.0f;
-  }
-}
-
-// bf16 copy of an fp32 matrix (round to nearest even), rows padded with zeros
-// to ld_dst elements (a multiple of 8).  Each thread converts 8 consecutive
-// elements of a row: two 128-bit streaming loads when the source rows are
-// 16-byte aligned (vec), one 128-bit store.  Blocks run along a row (x) and
-// stride over rows (y); no per-element index division.
-__global__ void __launch_bounds__(256) to_bf16_kernel(const float* __restrict__ src, int rows, int cols, int ld_src,
-                                                      __nv_bfloat16* __restrict__ dst, int ld_dst, int vec) {
-  const int c = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
-  if (c >= ld_dst) return;
-  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
-    const float* s = src + static_cast<long long>(r) * ld_src + c;
-    float v[8];
-    if (vec && c + 8 <= cols) {
-      const float4 a = __ldcs(reinterpret_cast<const float4*>(s));
-      const float4 b = __ldcs(reinterpret_cast<const float4*>(s + 4));
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = c + e < cols ? s[e] : 0.0f;
-    }
-    uint4 o;
-    __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
-    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[4], v[5]), h3 = __floats2bfloat162_rn(v[6], v[7]);
-    o.x = *reinterpret_cast<uint32_t*>(&h0);
-    o.y = *reinterpret_cast<uint32_t*>(&h1);
-    o.z = *reinterpret_cast<uint32_t*>(&h2);
-    o.w = *reinterpret_cast<uint32_t*>(&h3);
-    *reinterpret_cast<uint4*>(dst + static_cast<long long>(r) * ld_dst + c) = o;
-  }
-}
-
-// A TMA-fed operand (rows x cols row-major): the caller's array or a padded
-// copy in the workspace (fp32 modes), or its bf16 copy in the workspace (bf16
-// mode).  `lo` stays null: 3xTF32 lo tiles are derived on chip.
-struct Staged {
-  const float* ptr;
-  const float* lo;
-  int ld;
-  const __nv_bfloat16* bf16 = nullptr;
-};
-
-bool needs_pad(const float* p, int cols) { return (cols % 4 != 0) || !aligned16(p); }
-size_t plane_bytes(int rows, int cols) { return round256(static_cast<size_t>(rows) * round4(cols) * sizeof(float)); }
-size_t bf16_plane_bytes(int rows, int cols) { return round256(static_cast<size_t>(rows) * round8(cols) * 2); }
-size_t staged_bytes(const float* p, int rows, int cols, int mode) {
-  if (mode == SMM_MODE_BF16) return bf16_plane_bytes(rows, cols);
-  return needs_pad(p, cols) ? plane_bytes(rows, cols) : 0;
-}
-// Workspace bound when the pointer is not known yet (assumes a padded copy).
-size_t staged_bytes_bound(int rows, int cols, int mode) {
-  if (mode == SMM_MODE_BF16) return bf16_plane_bytes(rows, cols);
-  return plane_bytes(rows, cols);
-}
-
-int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st) {
-  if (mode == SMM_MODE_BF16) {
-    const int ld = round8(cols);
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
-    ws_cur += bf16_plane_bytes(rows, cols);
-    const int gx = (ld / 8 + 255) / 256;
-    const int gy = std::max(1, std::min(rows, std::max(1, 148 * 16 / gx)));
-    const int vec = (cols % 4 == 0 && aligned16(src)) ? 1 : 0;
-    to_bf16_kernel<<<dim3(gx, gy), 256, 0, st>>>(src, rows, cols, cols, dst, ld, vec);
-    count_launch();
-    SMM_CUDA_TRY(cudaGetLastError(), "bf16 staging launch");
-    *out = {nullptr, nullptr, ld, dst};
-    return SMM_OK;
-  }
-  // fp32 modes: the caller's array when TMA can address it (the 3xTF32 lo
-  // tiles are derived on chip), else a copy with 16-byte-multiple rows.
-  if (!needs_pad(src, cols)) {
-    *out = {src, nullptr, cols};
-    return SMM_OK;
-  }
-  const int ld = round4(cols);
-  float* dst = reinterpret_cast<float*>(ws_cur);
-  ws_cur += plane_bytes(rows, cols);
-  const long long total = static_cast<long long>(rows) * ld;
-  const int grid = static_cast<int>(std::min<long long>((total + 255) / 256, 148LL * 16));
-  pad_rows_kernel<<<std::max(grid, 1), 256, 0, st>>>(src, rows, cols, cols, dst, ld);
-  count_launch();
-  SMM_CUDA_TRY(cudaGetLastError(), "operand staging launch");
-  *out = {dst, nullptr, ld};
-  return SMM_OK;
-}
-
-// Dense copy (fp32, or bf16 rounded to nearest even) of rows [row0, row0 +
-// rows) of a packed structured matrix of order n: upper (zeros below the
-// diagonal), lower (zeros above) or symmetric (mirrored), each row padded with
-// zeros to ld (even).  64 x 64 tiles, 256 threads, lanes along columns (two
-// per lane: coalesced packed-row reads and row writes).  A symmetric tile
-// wholly below the diagonal holds mirrors S[j][i]: it reads its block along
-// packed rows j (coalesced) and transposes it through shared memory.
-__device__ __forceinline__ void store_pair(float* p, float a, float b) {
-  *reinterpret_cast<float2*>(p) = make_float2(a, b);
-}
-__device__ __forceinline__ void store_pair(__nv_bfloat16* p, float a, float b) {
-  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
-}
-template <int SF, typename T>
-__global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P, int n, int row0, int rows,
-                                                     T* __restrict__ dst, int ld) {
-  __shared__ float tile[64][65];
-  const int r0 = blockIdx.y * 64;  // slab row of the tile
-  const int c0 = blockIdx.x * 64;  // column of the tile
-  const int t = threadIdx.x;
-  const bool mirror = SF == SMM_STRUCT_SYMM && c0 + 63 < row0 + r0;
-  if (mirror) {
-    const int il = t & 63;
-    const int i = row0 + r0 + il;
-    for (int jl = t >> 6; jl < 64; jl += 4) {
-      const int j = c0 + jl;  // j < i for every element of the tile
-      tile[jl][il] = (r0 + il < rows && j < n) ? __ldg(P + packed_idx(j, i, n)) : 0.0f;
-    }
-    __syncthreads();
-  }
-  const int cp = 2 * (t & 31);
-  const int j = c0 + cp;
-  if (j >= ld) return;  // ld and j even: both columns of the pair are inside or outside
-  for (int rl = t >> 5; rl < 64; rl += 8) {
-    const int r = r0 + rl;
-    if (r >= rows) break;
-    const int i = row0 + r;
-    float v[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int jj = j + e;
-      if (mirror) {
-        v[e] = tile[cp + e][rl];
-      } else if (jj >= n) {
-        v[e] = 0.0f;
-      } else if constexpr (SF == SMM_STRUCT_UPPER) {
-        v[e] = jj >= i ? __ldg(P + packed_idx(i, jj, n)) : 0.0f;
-      } else if constexpr (SF == SMM_STRUCT_LOWER) {
-        v[e] = jj <= i ? __ldg(P + (static_cast<long long>(i) * (i + 1) / 2 + jj)) : 0.0f;
-      } else {
-        v[e] = __ldg(P + (jj >= i ? packed_idx(i, jj, n) : packed_idx(jj, i, n)));
-      }
-    }
-    store_pair(dst + static_cast<long long>(r) * ld + j, v[0], v[1]);
-  }
-}
-
-template <typename T>
-void launch_expand(const float* P, int sf, int n, int row0, int rows, T* dst, int ld, cudaStream_t st) {
-  const dim3 grid((ld + 63) / 64, (rows + 63) / 64);
-  switch (sf) {
-    case SMM_STRUCT_UPPER: expand_kernel<SMM_STRUCT_UPPER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
-    case SMM_STRUCT_LOWER: expand_kernel<SMM_STRUCT_LOWER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
-    default: expand_kernel<SMM_STRUCT_SYMM, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
-  }
-}
-
-// A packed operand (upper, lower or symmetric) on the left: rows [row0, row0 +
-// rows) expanded into a dense copy in the workspace (fp32 in the fp32 modes,
-// bf16 in bf16 mode), which the tensor cores then read by TMA like any dense
-// operand.  A packed row has no fixed alignment, so an on-chip fill of it
-// issues one 4-byte copy per element; the expansion is one HBM pass that
-// costs ~3% of the product at N = 4096..8192 (measured with it: U B 3xTF32
-// 218 -> 258 TFLOP/s, TF32 258 -> 569; S B 3xTF32 158 -> 200).
-size_t expanded_bytes(int rows, int n, int mode) {
-  return mode == SMM_MODE_BF16 ? bf16_plane_bytes(rows, n) : plane_bytes(rows, n);
-}
-int expand_operand(const float* P, int sf, int n, int row0, int rows, int mode, uint8_t*& ws_cur, Staged* out,
-                   cudaStream_t st) {
-  if (mode == SMM_MODE_BF16) {
-    const int ld = round8(n);
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
-    launch_expand(P, sf, n, row0, rows, dst, ld, st);
-    *out = {nullptr, nullptr, ld, dst};
-  } else {
-    const int ld = round4(n);
-    float* dst = reinterpret_cast<float*>(ws_cur);
-    launch_expand(P, sf, n, row0, rows, dst, ld, st);
-    *out = {dst, nullptr, ld};
-  }
-  ws_cur += expanded_bytes(rows, n, mode);
-  count_launch();
-  SMM_CUDA_TRY(cudaGetLastError(), "packed operand expansion launch");
-  return SMM_OK;
-}
-
-// Expand a packed left operand when the workspace has room for the copy (the
-// *_workspace_size functions include it); a smaller workspace (down to what
-// the on-chip path needs) builds the operand on chip instead.  SMM_EXPAND=0
-// forces the on-chip path.
-bool expand_packed(void* ws, size_t ws_bytes, size_t need_expanded) {
-  const char* e = std::getenv("SMM_EXPAND");
-  if (e && e[0] == '0') return false;
-  return ws != nullptr && ws_bytes >= need_expanded;
-}
-
-int check_ws(const char* who, void* ws, size_t have, size_t need) {
-  if (need == 0) return SMM_OK;
-  if (!ws || have < need)
-    return set_error(SMM_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", who, have, need);
-  if (!aligned16(ws)) return set_error(SMM_ERR_WORKSPACE, "%s: workspace must be 16-byte aligned", who);
-  return SMM_OK;
-}
-
-int zero_output(float* C, int rows, int cols, cudaStream_t st) {
-  SMM_CUDA_TRY(cudaMemsetAsync(C, 0, sizeof(float) * static_cast<size_t>(rows) * cols, st), "zero output");
-  return SMM_OK;
-}
-
-}  // namespace
 }  // namespace smm
 
 using namespace smm;
@@ -498,14 +270,6 @@ namespace {
 int check_slab(const char* who, int N, int ncols, int row0, int nrows) {
   if (N < 0 || ncols < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N)
     return set_error(SMM_ERR_INVALID, "%s: bad shape N=%d ncols=%d rows [%d, %d)", who, N, ncols, row0, row0 + nrows);
-  return SMM_OK;
-}
-
-// Packed triangles are addressed with 32-bit offsets on chip.
-constexpr int kMaxPackedOrder = 92681;  // N(N+1)/2 < 2^32
-int check_packed(const char* who, int N) {
-  if (N > kMaxPackedOrder)
-    return set_error(SMM_ERR_INVALID, "%s: packed order N = %d exceeds %d", who, N, kMaxPackedOrder);
   return SMM_OK;
 }
 }  // namespace

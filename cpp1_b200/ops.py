@@ -340,3 +340,69 @@ def device_status(stream=None) -> None:
 
 def launch_count() -> int:
     return int(_lib.load().smm_launch_count())
+
+
+# ---------------------------------------------------------------- host buffers
+def _check_host(name: str, t: torch.Tensor, numel: Optional[int] = None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.is_cuda:
+        raise ValueError(f"{name} must be a host (CPU) tensor")
+    if t.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32, got {t.dtype}")
+    if not t.is_contiguous():
+        t = t.contiguous()
+    if numel is not None and t.numel() != numel:
+        raise ValueError(f"{name} has {t.numel()} elements, expected {numel}")
+    return t
+
+
+def host_product(op: str, *inputs: torch.Tensor, mode: str = "3xtf32",
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """C = the product ``op`` of HOST tensors through the smm_*_host entry
+    points: the left operand(s) cross PCIe once, B streams through in column
+    chunks whose copies overlap the products (pinned tensors overlap; pageable
+    ones work synchronously).  Synchronous; C is a host tensor (pinned unless
+    ``out`` is given).
+
+    op: "gemm" (A, B), "upper" (U_packed, B), "symm" (S_packed, B),
+    "toeplitz" (g, B), "sandwich" (A, S_packed, B)."""
+    m = _mode(mode)
+    L = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if op == "gemm":
+        A, B = _check_host("A", inputs[0]), _check_host("B", inputs[1])
+        (M, K), (K2, N) = A.shape, B.shape
+        if K != K2:
+            raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+        shape, ptrs = (M, N), [A, B]
+        size = L.smm_gemm_host_workspace_size(M, N, K, m)
+        call = lambda C, ws, wsb: L.smm_gemm_host(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, m, ws, wsb)
+    elif op in ("upper", "symm", "toeplitz"):
+        B = _check_host("B", inputs[1])
+        N, ncols = B.shape
+        X = _check_host("left operand", inputs[0], 2 * N - 1 if op == "toeplitz" else N * (N + 1) // 2)
+        shape, ptrs = (N, ncols), [X, B]
+        size = getattr(L, f"smm_{op}_left_host_workspace_size")(N, ncols, m)
+        fn = getattr(L, f"smm_{op}_left_host")
+        call = lambda C, ws, wsb: fn(X.data_ptr(), B.data_ptr(), C.data_ptr(), N, ncols, m, ws, wsb)
+    elif op == "sandwich":
+        A = _check_host("A", inputs[0])
+        N = A.shape[0]
+        if tuple(A.shape) != (N, N):
+            raise ValueError("A must be square")
+        S = _check_host("S", inputs[1], N * (N + 1) // 2)
+        B = _check_host("B", inputs[2], N * N)
+        shape, ptrs = (N, N), [A, S, B]
+        size = L.smm_symm_sandwich_host_workspace_size(N, m)
+        call = lambda C, ws, wsb: L.smm_symm_sandwich_host(A.data_ptr(), S.data_ptr(), B.data_ptr(), C.data_ptr(),
+                                                           N, m, ws, wsb)
+    else:
+        raise ValueError(f"unknown host product {op!r}")
+    if out is None:
+        C = torch.empty(shape, dtype=torch.float32, pin_memory=True)
+    else:
+        C = _check_host("out", out, shape[0] * shape[1])
+    ws, wsb = _ws_args(size, dev)
+    _lib.check(call(C, ws, wsb), f"host product {op}")
+    return C

@@ -180,6 +180,35 @@ int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, flo
 int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float* B, float* C, int N, int mode,
                               void* stream);
 
+/* ---- host-buffer contractions ------------------------------------------ */
+
+/* The contractions above with A, B, C (and U, S, g) in HOST memory: the
+ * drop-in for callers of the reference's CPU kernels, which take host arrays
+ * (Cuda kernels/gemm_benchmark.cpp:40-156 compute_matrix_multi1,
+ * upper_triag_matmul.cpp:41-137, symmetric_matmul.cpp:84-211,
+ * toeplitz_matmul2.cpp:44-144).  Pinned host buffers let the copies overlap:
+ * the left operand(s) cross PCIe once and are prepared on the device (a
+ * packed operand expanded), then B streams through in column chunks on two
+ * internal streams, each chunk's copy-in, product and copy-out overlapping
+ * the neighbouring chunks'.  Synchronous; results equal the device entry
+ * points' within the mode's tolerance.  dev_ws must hold the matching
+ * *_host_workspace_size bytes of device memory (16-byte aligned). */
+size_t smm_gemm_host_workspace_size(int M, int N, int K, int mode);
+int smm_gemm_host(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* dev_ws,
+                  size_t ws_bytes);
+size_t smm_upper_left_host_workspace_size(int N, int ncols, int mode);
+int smm_upper_left_host(const float* U_packed, const float* B, float* C, int N, int ncols, int mode, void* dev_ws,
+                        size_t ws_bytes);
+size_t smm_symm_left_host_workspace_size(int N, int ncols, int mode);
+int smm_symm_left_host(const float* S_packed, const float* B, float* C, int N, int ncols, int mode, void* dev_ws,
+                       size_t ws_bytes);
+size_t smm_toeplitz_left_host_workspace_size(int N, int ncols, int mode);
+int smm_toeplitz_left_host(const float* g, const float* B, float* C, int N, int ncols, int mode, void* dev_ws,
+                           size_t ws_bytes);
+size_t smm_symm_sandwich_host_workspace_size(int N, int mode);
+int smm_symm_sandwich_host(const float* A, const float* S_packed, const float* B, float* C, int N, int mode,
+                           void* dev_ws, size_t ws_bytes);
+
 /* ---- structured right operand (the reference's own orientation) ------- */
 
 /* Workspace for smm_gen_x_upper / smm_gen_x_symm / smm_gen_x_lower: a padded

@@ -51,6 +51,14 @@ def test_version_and_error_text():
     lambda L: L.smm_pack(None, 3, None, 4, None),   # diagonal: no packed triangle
     lambda L: L.smm_pack(None, 4, None, 4, None),   # toeplitz: no packed triangle
     lambda L: L.smm_toeplitz_compact(None, None, -1, 3, None),
+    lambda L: L.smm_symm_x_symm_ws(None, None, None, -2, 0, None, 0, None),
+    lambda L: L.smm_lower_x_lower_ws(None, None, None, 4, 5, None, 0, None),
+    lambda L: L.smm_gemm_host(None, None, None, 4, 4, 4, 0, None, 0),
+    lambda L: L.smm_gemm_host(None, None, None, 4, -4, 4, 0, None, 0),
+    lambda L: L.smm_upper_left_host(None, None, None, 8, 8, 3, None, 0),
+    lambda L: L.smm_symm_left_host(None, None, None, 8, 8, 0, None, 0),
+    lambda L: L.smm_toeplitz_left_host(None, None, None, 8, 8, 0, None, 0),
+    lambda L: L.smm_symm_sandwich_host(None, None, None, None, 8, 0, None, 0),
 ])
 def test_invalid_arguments_rejected_on_host(call):
     L = _lib.load()
@@ -68,6 +76,9 @@ def test_empty_shapes_are_noops():
     assert L.smm_pack(None, 1, None, 0, None) == _lib.SMM_OK
     assert L.smm_unpack(None, 4, None, 0, None) == _lib.SMM_OK
     assert L.smm_toeplitz_compact(None, None, 0, 5, None) == _lib.SMM_OK
+    assert L.smm_gemm_host(None, None, None, 0, 4, 4, 0, None, 0) == _lib.SMM_OK
+    assert L.smm_symm_sandwich_host(None, None, None, None, 0, 2, None, 0) == _lib.SMM_OK
+    assert L.smm_symm_x_symm_ws(None, None, None, 0, 1, None, 0, None) == _lib.SMM_OK
 
 
 def test_workspace_queries_are_host_only():
@@ -76,6 +87,22 @@ def test_workspace_queries_are_host_only():
     assert L.smm_gemm_workspace_size(128, 128, 128, 0) >= 0
     assert L.smm_symm_sandwich_workspace_size(4096, 0) >= 4096 * 4096 * 4
     assert L.smm_diag_rows_host_workspace_size(8192, 8192) >= 8192 * 4
+    # host-buffer products: the left operand(s), their prepared copy and two
+    # chunk buffer sets
+    assert L.smm_gemm_host_workspace_size(8192, 8192, 8192, 0) >= 8192 * 8192 * 4
+    assert L.smm_upper_left_host_workspace_size(8192, 8192, 2) >= 8192 * 8193 // 2 * 4 + 8192 * 8192 * 2
+    assert L.smm_symm_sandwich_host_workspace_size(0, 0) == 0
+    # a packed product with room for both expansions
+    assert L.smm_symm_x_symm_workspace_size(1000, 0) >= 2 * 1000 * 1000 * 4
+    assert L.smm_lower_x_lower_workspace_size(1000, 2) >= 2 * 1000 * 1000 * 2
+
+
+def test_host_products_reject_small_workspace_before_any_device_work():
+    L = _lib.load()
+    need = L.smm_gemm_host_workspace_size(64, 64, 64, 0)
+    buf = ctypes.create_string_buffer(16)
+    rc = L.smm_gemm_host(buf, buf, buf, 64, 64, 64, 0, buf, need - 256)
+    assert rc == _lib.SMM_ERR_WORKSPACE, _lib.last_error()
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
