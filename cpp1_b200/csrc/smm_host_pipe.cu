@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "smm_contract.h"
 
@@ -92,6 +93,10 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
   if (!L1 || !B || !C || (h.kind == HostLeft::Sandwich && !L2)) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
   if (h.kind == HostLeft::Upper || h.kind == HostLeft::Symm || h.kind == HostLeft::Sandwich)
     if (int rc = check_packed(who, K)) return rc;
+  if (K == 0) {  // an empty inner dimension: C = 0
+    std::memset(C, 0, sizeof(float) * static_cast<size_t>(M) * N);
+    return SMM_OK;
+  }
   if (int rc = check_ws(who, dev_ws, ws_bytes, host_ws_bytes(h))) return rc;
   HostStreams* hs = nullptr;
   if (int rc = host_streams(&hs)) return rc;

@@ -404,5 +404,8 @@ def host_product(op: str, *inputs: torch.Tensor, mode: str = "3xtf32",
     else:
         C = _check_host("out", out, shape[0] * shape[1])
     ws, wsb = _ws_args(size, dev)
+    # the entry points run on internal streams: finish work that may still
+    # use the shared workspace
+    torch.cuda.current_stream().synchronize()
     _lib.check(call(C, ws, wsb), f"host product {op}")
     return C

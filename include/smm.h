@@ -136,7 +136,8 @@ int smm_upper_left(const float* U, int u_fmt, const float* B, float* C, int N, i
 int smm_toeplitz_left(const float* g, const float* B, float* C, int N, int ncols, int mode, void* ws,
                       size_t ws_bytes, void* stream);
 
-/* C(N x ncols) = S B, S symmetric given packed upper, mirrored on chip.
+/* C(N x ncols) = S B, S symmetric given packed upper (expanded into a dense
+ * copy in the workspace, or mirrored on chip without room for it).
  * Replaces kernel_symm_x_gen (src/dsl/codegen_cuda.py:973-1245). */
 int smm_symm_left(const float* S_packed, const float* B, float* C, int N, int ncols, int mode, void* ws,
                   size_t ws_bytes, void* stream);
@@ -192,7 +193,9 @@ int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float
  * internal streams, each chunk's copy-in, product and copy-out overlapping
  * the neighbouring chunks'.  Synchronous; results equal the device entry
  * points' within the mode's tolerance.  dev_ws must hold the matching
- * *_host_workspace_size bytes of device memory (16-byte aligned). */
+ * *_host_workspace_size bytes of device memory (16-byte aligned), with no
+ * pending work on it: the calls run on internal streams that are not
+ * ordered after the caller's streams. */
 size_t smm_gemm_host_workspace_size(int M, int N, int K, int mode);
 int smm_gemm_host(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* dev_ws,
                   size_t ws_bytes);

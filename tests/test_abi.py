@@ -97,6 +97,14 @@ def test_workspace_queries_are_host_only():
     assert L.smm_lower_x_lower_workspace_size(1000, 2) >= 2 * 1000 * 1000 * 2
 
 
+def test_host_gemm_with_empty_inner_dimension_writes_zeros():
+    L = _lib.load()
+    C = (ctypes.c_float * 6)(*([7.0] * 6))
+    rc = L.smm_gemm_host(C, C, C, 2, 3, 0, 0, None, 0)
+    assert rc == _lib.SMM_OK, _lib.last_error()
+    assert list(C) == [0.0] * 6
+
+
 def test_host_products_reject_small_workspace_before_any_device_work():
     L = _lib.load()
     need = L.smm_gemm_host_workspace_size(64, 64, 64, 0)
