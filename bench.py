@@ -556,6 +556,12 @@ def roofline(op, n, nrows, mode, step, stream, peaks, units_rank, world):
             "peak_source": src + f"; {passes} MMA pass(es) per useful FLOP"}
 
 
+# The public call each op's e2e goes through.
+E2E_API = {"diag": " (smm_diag_rows_host)", "add": " via cpp1_b200.ops.add_struct",
+           "gemm": " (smm_gemm_host)", "upper": " (smm_upper_left_host)",
+           "toeplitz": " (smm_toeplitz_left_host)", "sandwich": " (smm_symm_sandwich_host)"}
+
+
 def e2e_ours(args, h_in, n):
     """The same metric through the C ABI with HOST buffers: copy-in, compute
     and copy-out of each step inside the timed region."""
@@ -611,8 +617,7 @@ def e2e_ours(args, h_in, n):
     scale = 1e9 if op in HBM_OPS else 1e12
     return {"value": round(units / dt / scale, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": steps, "ms_per_step": round(dt * 1e3, 3),
-            "api": "C ABI with pinned host buffers" + {"diag": " (smm_diag_rows_host)", "add": " via cpp1_b200.ops"}.get(
-                op, f" (smm_{ {'gemm': 'gemm', 'upper': 'upper_left', 'toeplitz': 'toeplitz_left', 'sandwich': 'symm_sandwich'}[op] }_host)")}
+            "api": "C ABI with pinned host buffers" + E2E_API[op]}
 
 
 def e2e_dist(args, h_in, n, rank, world):
