@@ -260,6 +260,18 @@ def cpu_reference_call(op: str, n: int, sample_n: int):
 
 
 CPU_SAMPLE_N = {"diag": 8192, "gemm": 2048, "upper": 2048, "sandwich": 1024, "toeplitz": 2048, "add": 4096}
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (lscpu's), for the baseline record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 CPU_KIND = {"add": "port"}  # every other op runs the reference's own kernel
 
 
@@ -278,9 +290,11 @@ def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
     kind = CPU_KIND.get(op, "reference")
     if kind == "port":
         return {"value": rate / scale, "unit": WORKLOADS[op]["unit"], "cores": 1, "kind": "port",
+                "cpu": cpu_model(), "host_threads": host_threads(),
                 "sample": f"{op} at order {sn} ({len(rates)} calls, median; the oracle's scalar C restatement, "
                           "one thread)"}
     return {"value": rate / scale, "unit": WORKLOADS[op]["unit"], "cores": cores, "kind": "reference",
+            "cpu": cpu_model(), "host_threads": host_threads(),
             "sample": f"{op} at order {sn} ({len(rates)} calls, median; the reference's AVX2+OpenMP kernel, "
                       f"its own chrono window, OMP threads = {cores})"}
 
@@ -791,6 +805,7 @@ def run_reference(args, rank, world):
         "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "sample_N": sn},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 3), "unit": WORKLOADS[op]["unit"], "cores": cores, "kind": kind,
+                         "cpu": cpu_model(), "host_threads": host_threads(),
                          "sample": sample + "; " + how},
         "e2e": {"value": round(value, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
