@@ -367,22 +367,26 @@ def host_product(op: str, *inputs: torch.Tensor, mode: str = "3xtf32",
 
     op: "gemm" (A, B), "upper" (U_packed, B), "symm" (S_packed, B),
     "toeplitz" (g, B), "sandwich" (A, S_packed, B)."""
+    arity = {"gemm": 2, "upper": 2, "symm": 2, "toeplitz": 2, "sandwich": 3}
+    if op not in arity:
+        raise ValueError(f"unknown host product {op!r}; expected one of {sorted(arity)}")
+    if len(inputs) != arity[op]:
+        raise ValueError(f"host product {op!r} takes {arity[op]} inputs, got {len(inputs)}")
     m = _mode(mode)
     L = _lib.load()
-    dev = torch.device("cuda", torch.cuda.current_device())
     if op == "gemm":
         A, B = _check_host("A", inputs[0]), _check_host("B", inputs[1])
         (M, K), (K2, N) = A.shape, B.shape
         if K != K2:
             raise ValueError(f"inner dimensions differ: {K} vs {K2}")
-        shape, ptrs = (M, N), [A, B]
+        shape = (M, N)
         size = L.smm_gemm_host_workspace_size(M, N, K, m)
         call = lambda C, ws, wsb: L.smm_gemm_host(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, m, ws, wsb)
     elif op in ("upper", "symm", "toeplitz"):
         B = _check_host("B", inputs[1])
         N, ncols = B.shape
         X = _check_host("left operand", inputs[0], 2 * N - 1 if op == "toeplitz" else N * (N + 1) // 2)
-        shape, ptrs = (N, ncols), [X, B]
+        shape = (N, ncols)
         size = getattr(L, f"smm_{op}_left_host_workspace_size")(N, ncols, m)
         fn = getattr(L, f"smm_{op}_left_host")
         call = lambda C, ws, wsb: fn(X.data_ptr(), B.data_ptr(), C.data_ptr(), N, ncols, m, ws, wsb)
@@ -393,17 +397,15 @@ def host_product(op: str, *inputs: torch.Tensor, mode: str = "3xtf32",
             raise ValueError("A must be square")
         S = _check_host("S", inputs[1], N * (N + 1) // 2)
         B = _check_host("B", inputs[2], N * N)
-        shape, ptrs = (N, N), [A, S, B]
+        shape = (N, N)
         size = L.smm_symm_sandwich_host_workspace_size(N, m)
         call = lambda C, ws, wsb: L.smm_symm_sandwich_host(A.data_ptr(), S.data_ptr(), B.data_ptr(), C.data_ptr(),
                                                            N, m, ws, wsb)
-    else:
-        raise ValueError(f"unknown host product {op!r}")
     if out is None:
         C = torch.empty(shape, dtype=torch.float32, pin_memory=True)
     else:
         C = _check_host("out", out, shape[0] * shape[1])
-    ws, wsb = _ws_args(size, dev)
+    ws, wsb = _ws_args(size, torch.device("cuda", torch.cuda.current_device()))
     # the entry points run on internal streams: finish work that may still
     # use the shared workspace
     torch.cuda.current_stream().synchronize()
