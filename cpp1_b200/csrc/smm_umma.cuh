@@ -195,22 +195,6 @@ __device__ __forceinline__ long long packed_idx(long long i, long long j, long l
   return i * n - i * (i - 1) / 2 + (j - i);
 }
 
-// Value of the structured left operand at (row gr, column k); zero outside
-// the n x n matrix.
-template <AKind AK>
-__device__ __forceinline__ float a_value(const float* __restrict__ src, int n, int gr, int k) {
-  if (gr >= n || k >= n) return 0.0f;
-  if constexpr (AK == AKind::UpperPacked) {
-    return k >= gr ? __ldg(src + packed_idx(gr, k, n)) : 0.0f;
-  } else if constexpr (AK == AKind::Toeplitz) {
-    return __ldg(src + (n - 1 + k - gr));
-  } else if constexpr (AK == AKind::LowerPacked) {
-    return k <= gr ? __ldg(src + (static_cast<long long>(gr) * (gr + 1) / 2 + k)) : 0.0f;
-  } else {  // SymmPacked
-    return k >= gr ? __ldg(src + packed_idx(gr, k, n)) : __ldg(src + packed_idx(k, gr, n));
-  }
-}
-
 // Value of the structured right operand at (row k, column n); zero outside.
 template <BKind BK>
 __device__ __forceinline__ float b_value(const float* __restrict__ src, int nd, int k, int n) {
