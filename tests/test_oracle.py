@@ -151,3 +151,32 @@ def test_add_restatement():
 
 def test_toeplitz_compact_restatement_matches_reference_builder(golden):
     assert np.array_equal(O.toeplitz_compact_f32(golden["tcompact_T"]), golden["tcompact_g"])
+
+
+# ---------------------------------------------------------------- the reference's own orientation
+@pytest.mark.parametrize("M,N", [(64, 128), (128, 64), (128, 128)])
+def test_right_side_restatements_match_reference_kernels(M, N):
+    """A·U and A·S (the reference drivers' orientation, upper_triag_matmul.cpp
+    and symmetric_matmul.cpp run as built in oracle/_ref) against the C
+    restatements the right-operand GPU tests rely on: bit for bit."""
+    if not O.ref_available():
+        pytest.skip("oracle/_ref not built")
+    rng = np.random.default_rng(M + N)
+    X = rng.uniform(-1, 1, (M, N)).astype(np.float32)
+    P = rng.uniform(-1, 1, N * (N + 1) // 2).astype(np.float32)
+    assert np.array_equal(O.upper_right_f32(X, P), O.ref_upper_right(X, P)[0])
+    assert np.array_equal(O.symm_right_f32(X, P), O.ref_symm_right(X, P)[0])
+    R = X.astype(np.float64) @ W.unpack_symmetric(P, N).astype(np.float64)
+    assert np.abs(O.symm_right_rows_f64(X, P, np.arange(M)) - R).max() <= 1e-12
+    assert O.relerr(O.symm_right_f32(X, P), R) <= 1e-5
+
+
+def test_reference_right_kernels_reject_non_tile_shapes():
+    """The reference's compiled kernels only take tile-multiple sizes; the
+    wrapper turns their refusal into an error rather than a wrong result."""
+    if not O.ref_available():
+        pytest.skip("oracle/_ref not built")
+    X = np.zeros((96, 192), np.float32)
+    P = np.zeros(192 * 193 // 2, np.float32)
+    with pytest.raises(ValueError, match="tile-multiple"):
+        O.ref_upper_right(X, P)
