@@ -52,6 +52,7 @@ using namespace smm;
 
 extern "C" int smm_compat_gen_x_gen(const float* A, const float* B, float* C, float* gflops_out, int n,
                                     float* time_ms_out) {
+  SMM_RANGE("smm_compat_gen_x_gen");
   return compat_run("smm_compat_gen_x_gen", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_gemm_workspace_size(n, n, n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -61,18 +62,21 @@ extern "C" int smm_compat_gen_x_gen(const float* A, const float* B, float* C, fl
 
 extern "C" int smm_compat_diag_x_gen(const float* d, const float* B, float* C, float* gflops_out, int n,
                                      float* time_ms_out) {
+  SMM_RANGE("smm_compat_diag_x_gen");
   return compat_run("smm_compat_diag_x_gen", gflops_out, time_ms_out, square(n), 0,
                     [&](void*, size_t, cudaStream_t st) { return smm_diag_rows(d, B, C, n, n, st); });
 }
 
 extern "C" int smm_compat_gen_x_diag(const float* A, const float* d, float* C, float* gflops_out, int n,
                                      float* time_ms_out) {
+  SMM_RANGE("smm_compat_gen_x_diag");
   return compat_run("smm_compat_gen_x_diag", gflops_out, time_ms_out, square(n), 0,
                     [&](void*, size_t, cudaStream_t st) { return smm_diag_cols(A, d, C, n, n, st); });
 }
 
 extern "C" int smm_compat_upper_x_gen(const float* U, const float* B, float* C, float* gflops_out, int n,
                                       float* time_ms_out) {
+  SMM_RANGE("smm_compat_upper_x_gen");
   return compat_run("smm_compat_upper_x_gen", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_upper_left_workspace_size(n, n, SMM_FMT_PACKED, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -82,6 +86,7 @@ extern "C" int smm_compat_upper_x_gen(const float* U, const float* B, float* C, 
 
 extern "C" int smm_compat_toeplitz_x_gen(const float* g, const float* B, float* C, float* gflops_out, int n,
                                          float* time_ms_out) {
+  SMM_RANGE("smm_compat_toeplitz_x_gen");
   return compat_run("smm_compat_toeplitz_x_gen", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_toeplitz_left_workspace_size(n, n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -91,6 +96,7 @@ extern "C" int smm_compat_toeplitz_x_gen(const float* g, const float* B, float* 
 
 extern "C" int smm_compat_symm_x_gen(const float* S, const float* B, float* C, float* gflops_out, int n,
                                      float* time_ms_out) {
+  SMM_RANGE("smm_compat_symm_x_gen");
   return compat_run("smm_compat_symm_x_gen", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_symm_left_workspace_size(n, n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -100,6 +106,7 @@ extern "C" int smm_compat_symm_x_gen(const float* S, const float* B, float* C, f
 
 extern "C" int smm_compat_gen_x_symm(const float* A, const float* S, float* C, float* gflops_out, int n,
                                      float* time_ms_out) {
+  SMM_RANGE("smm_compat_gen_x_symm");
   return compat_run("smm_compat_gen_x_symm", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_gen_x_struct_workspace_size(n, n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -109,6 +116,7 @@ extern "C" int smm_compat_gen_x_symm(const float* A, const float* S, float* C, f
 
 extern "C" int smm_compat_gen_x_upper(const float* A, const float* U, float* C, float* gflops_out, int n,
                                       float* time_ms_out) {
+  SMM_RANGE("smm_compat_gen_x_upper");
   return compat_run("smm_compat_gen_x_upper", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_gen_x_struct_workspace_size(n, n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -118,6 +126,7 @@ extern "C" int smm_compat_gen_x_upper(const float* A, const float* U, float* C, 
 
 extern "C" int smm_compat_symm_x_symm(const float* S1, const float* S2, float* C, float* gflops_out, int n,
                                       float* time_ms_out) {
+  SMM_RANGE("smm_compat_symm_x_symm");
   return compat_run("smm_compat_symm_x_symm", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_symm_x_symm_workspace_size(n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -127,6 +136,7 @@ extern "C" int smm_compat_symm_x_symm(const float* S1, const float* S2, float* C
 
 extern "C" int smm_compat_gen_x_lower(const float* A, const float* L, float* C, float* gflops_out, int n,
                                       float* time_ms_out) {
+  SMM_RANGE("smm_compat_gen_x_lower");
   return compat_run("smm_compat_gen_x_lower", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_gen_x_struct_workspace_size(n, n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -136,6 +146,7 @@ extern "C" int smm_compat_gen_x_lower(const float* A, const float* L, float* C, 
 
 extern "C" int smm_compat_lower_x_gen(const float* L, const float* B, float* C, float* gflops_out, int n,
                                       float* time_ms_out) {
+  SMM_RANGE("smm_compat_lower_x_gen");
   return compat_run("smm_compat_lower_x_gen", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_lower_left_workspace_size(n, n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -145,6 +156,7 @@ extern "C" int smm_compat_lower_x_gen(const float* L, const float* B, float* C, 
 
 extern "C" int smm_compat_lower_x_lower(const float* L1, const float* L2, float* C, float* gflops_out, int n,
                                         float* time_ms_out) {
+  SMM_RANGE("smm_compat_lower_x_lower");
   return compat_run("smm_compat_lower_x_lower", gflops_out, time_ms_out, cube(n),
                     n > 0 ? smm_lower_x_lower_workspace_size(n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {
@@ -154,12 +166,14 @@ extern "C" int smm_compat_lower_x_lower(const float* L1, const float* L2, float*
 
 extern "C" int smm_compat_add_gen_symm(const float* A, const float* S, float* C, float* gflops_out, int n,
                                        float* time_ms_out) {
+  SMM_RANGE("smm_compat_add_gen_symm");
   return compat_run("smm_compat_add_gen_symm", gflops_out, time_ms_out, square(n), 0,
                     [&](void*, size_t, cudaStream_t st) { return smm_add_struct(A, S, SMM_STRUCT_SYMM, C, n, st); });
 }
 
 extern "C" int smm_compat_symm_sandwich(const float* A, const float* S, const float* B, float* C, float* gflops_out,
                                         int n, float* time_ms_out) {
+  SMM_RANGE("smm_compat_symm_sandwich");
   return compat_run("smm_compat_symm_sandwich", gflops_out, time_ms_out, 2.0 * cube(n),
                     n > 0 ? smm_symm_sandwich_workspace_size(n, SMM_COMPAT_MODE) : 0,
                     [&](void* ws, size_t wb, cudaStream_t st) {

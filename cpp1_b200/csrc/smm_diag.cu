@@ -136,6 +136,7 @@ int launch_rows(const float* d, const float* B, float* C, int M, int N, cudaStre
 using namespace smm;
 
 extern "C" int smm_diag_rows(const float* d, const float* B, float* C, int M, int N, void* stream) {
+  SMM_RANGE("smm_diag_rows");
   if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "smm_diag_rows: negative shape %d x %d", M, N);
   if (M == 0 || N == 0) return SMM_OK;
   if (!d || !B || !C) return set_error(SMM_ERR_INVALID, "smm_diag_rows: null pointer");
@@ -143,6 +144,7 @@ extern "C" int smm_diag_rows(const float* d, const float* B, float* C, int M, in
 }
 
 extern "C" int smm_diag_cols(const float* A, const float* b, float* C, int M, int N, void* stream) {
+  SMM_RANGE("smm_diag_cols");
   if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "smm_diag_cols: negative shape %d x %d", M, N);
   if (M == 0 || N == 0) return SMM_OK;
   if (!A || !b || !C) return set_error(SMM_ERR_INVALID, "smm_diag_cols: null pointer");
@@ -195,6 +197,7 @@ extern "C" size_t smm_diag_rows_host_workspace_size(int M, int N) {
 
 extern "C" int smm_diag_rows_host(const float* d_host, const float* B_host, float* C_host, int M, int N,
                                   void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_diag_rows_host");
   if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "smm_diag_rows_host: negative shape");
   if (M == 0 || N == 0) return SMM_OK;
   if (!d_host || !B_host || !C_host) return set_error(SMM_ERR_INVALID, "smm_diag_rows_host: null pointer");

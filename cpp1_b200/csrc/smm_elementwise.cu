@@ -330,6 +330,7 @@ int grid_for(long long work) {
 using namespace smm;
 
 extern "C" int smm_add(const float* A, const float* B, float* C, long long count, void* stream) {
+  SMM_RANGE("smm_add");
   if (count < 0) return set_error(SMM_ERR_INVALID, "smm_add: negative count");
   if (count == 0) return SMM_OK;
   if (!A || !B || !C) return set_error(SMM_ERR_INVALID, "smm_add: null pointer");
@@ -356,6 +357,7 @@ extern "C" int smm_add(const float* A, const float* B, float* C, long long count
 }
 
 extern "C" int smm_add_struct(const float* A, const float* S, int s_fmt, float* C, int N, void* stream) {
+  SMM_RANGE("smm_add_struct");
   if (N < 0) return set_error(SMM_ERR_INVALID, "smm_add_struct: negative order");
   if (!valid_struct(s_fmt)) return set_error(SMM_ERR_INVALID, "smm_add_struct: unknown structure %d", s_fmt);
   if (N == 0) return SMM_OK;
@@ -366,6 +368,7 @@ extern "C" int smm_add_struct(const float* A, const float* S, int s_fmt, float* 
 }
 
 extern "C" int smm_unpack(const float* S, int s_fmt, float* D, int N, void* stream) {
+  SMM_RANGE("smm_unpack");
   if (N < 0) return set_error(SMM_ERR_INVALID, "smm_unpack: negative order");
   if (!valid_struct(s_fmt)) return set_error(SMM_ERR_INVALID, "smm_unpack: unknown structure %d", s_fmt);
   if (N == 0) return SMM_OK;
@@ -376,6 +379,7 @@ extern "C" int smm_unpack(const float* S, int s_fmt, float* D, int N, void* stre
 }
 
 extern "C" int smm_pack(const float* D, int s_fmt, float* P, int N, void* stream) {
+  SMM_RANGE("smm_pack");
   if (N < 0) return set_error(SMM_ERR_INVALID, "smm_pack: negative order");
   if (s_fmt != SMM_STRUCT_UPPER && s_fmt != SMM_STRUCT_LOWER && s_fmt != SMM_STRUCT_SYMM)
     return set_error(SMM_ERR_INVALID, "smm_pack: structure %d (%s) has no packed triangle", s_fmt,
@@ -397,6 +401,7 @@ extern "C" int smm_pack(const float* D, int s_fmt, float* P, int N, void* stream
 }
 
 extern "C" int smm_toeplitz_compact(const float* T, float* g, int rows, int cols, void* stream) {
+  SMM_RANGE("smm_toeplitz_compact");
   if (rows < 0 || cols < 0) return set_error(SMM_ERR_INVALID, "smm_toeplitz_compact: negative shape");
   if (rows == 0 || cols == 0) return SMM_OK;
   if (!T || !g) return set_error(SMM_ERR_INVALID, "smm_toeplitz_compact: null pointer");

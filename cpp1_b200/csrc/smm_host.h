@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include "../../include/smm.h"
 
@@ -25,6 +26,16 @@ uint32_t* device_status_word();
 unsigned long long wait_limit_ns();
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Names one library call on profiler timelines (an NVTX range, header-only
+// NVTX v3: a no-op unless a profiling tool is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define SMM_RANGE(name) ::smm::NvtxRange smm_nvtx_range_(name)
 
 #define SMM_CUDA_TRY(expr, what)                  \
   do {                                            \

@@ -199,6 +199,7 @@ extern "C" size_t smm_gemm_host_workspace_size(int M, int N, int K, int mode) {
 }
 extern "C" int smm_gemm_host(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* dev_ws,
                              size_t ws_bytes) {
+  SMM_RANGE("smm_gemm_host");
   return host_product("smm_gemm_host", {HostLeft::Gemm, M, N, K, mode}, A, nullptr, B, C, dev_ws, ws_bytes);
 }
 
@@ -207,6 +208,7 @@ extern "C" size_t smm_upper_left_host_workspace_size(int N, int ncols, int mode)
 }
 extern "C" int smm_upper_left_host(const float* U_packed, const float* B, float* C, int N, int ncols, int mode,
                                    void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_upper_left_host");
   return host_product("smm_upper_left_host", {HostLeft::Upper, N, ncols, N, mode}, U_packed, nullptr, B, C, dev_ws,
                       ws_bytes);
 }
@@ -216,6 +218,7 @@ extern "C" size_t smm_symm_left_host_workspace_size(int N, int ncols, int mode) 
 }
 extern "C" int smm_symm_left_host(const float* S_packed, const float* B, float* C, int N, int ncols, int mode,
                                   void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_symm_left_host");
   return host_product("smm_symm_left_host", {HostLeft::Symm, N, ncols, N, mode}, S_packed, nullptr, B, C, dev_ws,
                       ws_bytes);
 }
@@ -225,6 +228,7 @@ extern "C" size_t smm_toeplitz_left_host_workspace_size(int N, int ncols, int mo
 }
 extern "C" int smm_toeplitz_left_host(const float* g, const float* B, float* C, int N, int ncols, int mode,
                                       void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_toeplitz_left_host");
   return host_product("smm_toeplitz_left_host", {HostLeft::Toeplitz, N, ncols, N, mode}, g, nullptr, B, C, dev_ws,
                       ws_bytes);
 }
@@ -234,6 +238,7 @@ extern "C" size_t smm_symm_sandwich_host_workspace_size(int N, int mode) {
 }
 extern "C" int smm_symm_sandwich_host(const float* A, const float* S_packed, const float* B, float* C, int N,
                                       int mode, void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_symm_sandwich_host");
   return host_product("smm_symm_sandwich_host", {HostLeft::Sandwich, N, N, N, mode}, A, S_packed, B, C, dev_ws,
                       ws_bytes);
 }

@@ -244,6 +244,7 @@ extern "C" size_t smm_gemm_workspace_size(int M, int N, int K, int mode) {
 
 extern "C" int smm_gemm(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* ws,
                         size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_gemm");
   if (M < 0 || N < 0 || K < 0) return set_error(SMM_ERR_INVALID, "smm_gemm: negative shape");
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_gemm: unknown mode %d", mode);
   if (M == 0 || N == 0) return SMM_OK;
@@ -276,6 +277,7 @@ int check_slab(const char* who, int N, int ncols, int row0, int nrows) {
 
 extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, float* C, int N, int ncols, int row0,
                                    int nrows, int mode, void* ws, size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_upper_left_rows");
   if (int rc = check_slab("smm_upper_left", N, ncols, row0, nrows)) return rc;
   if (u_fmt == SMM_FMT_PACKED)
     if (int rc = check_packed("smm_upper_left", N)) return rc;
@@ -320,6 +322,7 @@ extern "C" int smm_upper_left_rows(const float* U, int u_fmt, const float* B, fl
 
 extern "C" int smm_upper_left(const float* U, int u_fmt, const float* B, float* C, int N, int ncols, int mode,
                               void* ws, size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_upper_left");
   return smm_upper_left_rows(U, u_fmt, B, C, N, ncols, 0, N, mode, ws, ws_bytes, stream);
 }
 
@@ -330,6 +333,7 @@ extern "C" size_t smm_toeplitz_left_workspace_size(int N, int ncols, int mode) {
 
 extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, int N, int ncols, int row0,
                                       int nrows, int mode, void* ws, size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_toeplitz_left_rows");
   if (int rc = check_slab("smm_toeplitz_left", N, ncols, row0, nrows)) return rc;
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_toeplitz_left: unknown mode %d", mode);
   if (nrows == 0 || ncols == 0) return SMM_OK;
@@ -345,6 +349,7 @@ extern "C" int smm_toeplitz_left_rows(const float* g, const float* B, float* C, 
 
 extern "C" int smm_toeplitz_left(const float* g, const float* B, float* C, int N, int ncols, int mode, void* ws,
                                  size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_toeplitz_left");
   return smm_toeplitz_left_rows(g, B, C, N, ncols, 0, N, mode, ws, ws_bytes, stream);
 }
 
@@ -355,6 +360,7 @@ extern "C" size_t smm_symm_left_workspace_size(int N, int ncols, int mode) {
 
 extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int N, int ncols, int row0, int nrows,
                                   int mode, void* ws, size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_symm_left_rows");
   if (int rc = check_slab("smm_symm_left", N, ncols, row0, nrows)) return rc;
   if (int rc = check_packed("smm_symm_left", N)) return rc;
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_left: unknown mode %d", mode);
@@ -380,6 +386,7 @@ extern "C" int smm_symm_left_rows(const float* S, const float* B, float* C, int 
 
 extern "C" int smm_symm_left(const float* S, const float* B, float* C, int N, int ncols, int mode, void* ws,
                              size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_symm_left");
   return smm_symm_left_rows(S, B, C, N, ncols, 0, N, mode, ws, ws_bytes, stream);
 }
 
@@ -404,6 +411,7 @@ extern "C" size_t smm_symm_sandwich_workspace_size(int N, int mode) {
 
 extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B, float* C, int N, int mode,
                                  void* ws, size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_symm_sandwich");
   if (N < 0) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich: negative shape");
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich: unknown mode %d", mode);
   if (N == 0) return SMM_OK;
@@ -481,20 +489,24 @@ int gen_x_struct(const char* who, BKind bk, const float* A, const float* X, floa
 
 extern "C" int smm_gen_x_upper(const float* A, const float* U, float* C, int M, int N, int mode, void* ws,
                                size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_gen_x_upper");
   return gen_x_struct("smm_gen_x_upper", BKind::UpperPacked, A, U, C, M, N, mode, ws, ws_bytes, as_stream(stream));
 }
 
 extern "C" int smm_gen_x_symm(const float* A, const float* S, float* C, int M, int N, int mode, void* ws,
                               size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_gen_x_symm");
   return gen_x_struct("smm_gen_x_symm", BKind::SymmPacked, A, S, C, M, N, mode, ws, ws_bytes, as_stream(stream));
 }
 
 extern "C" int smm_gen_x_lower(const float* A, const float* Lp, float* C, int M, int N, int mode, void* ws,
                                size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_gen_x_lower");
   return gen_x_struct("smm_gen_x_lower", BKind::LowerPacked, A, Lp, C, M, N, mode, ws, ws_bytes, as_stream(stream));
 }
 
 extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N, int mode, void* stream) {
+  SMM_RANGE("smm_symm_x_symm");
   return smm_symm_x_symm_ws(S1, S2, C, N, mode, nullptr, 0, stream);
 }
 
@@ -530,6 +542,7 @@ extern "C" size_t smm_symm_x_symm_workspace_size(int N, int mode) {
 
 extern "C" int smm_symm_x_symm_ws(const float* S1, const float* S2, float* C, int N, int mode, void* ws,
                                   size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_symm_x_symm_ws");
   return packed_x_packed("smm_symm_x_symm", AKind::SymmPacked, BKind::SymmPacked, SMM_STRUCT_SYMM, S1, S2, C, N,
                          mode, ws, ws_bytes, as_stream(stream));
 }
@@ -542,6 +555,7 @@ extern "C" size_t smm_lower_left_workspace_size(int N, int ncols, int mode) {
 
 extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, int ncols, int mode, void* ws,
                               size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_lower_left");
   if (N < 0 || ncols < 0) return set_error(SMM_ERR_INVALID, "smm_lower_left: negative shape");
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_lower_left: unknown mode %d", mode);
   if (N == 0 || ncols == 0) return SMM_OK;
@@ -568,6 +582,7 @@ extern "C" int smm_lower_left(const float* Lp, const float* B, float* C, int N, 
 }
 
 extern "C" int smm_lower_x_lower(const float* L1, const float* L2, float* C, int N, int mode, void* stream) {
+  SMM_RANGE("smm_lower_x_lower");
   return smm_lower_x_lower_ws(L1, L2, C, N, mode, nullptr, 0, stream);
 }
 
@@ -577,6 +592,7 @@ extern "C" size_t smm_lower_x_lower_workspace_size(int N, int mode) {
 
 extern "C" int smm_lower_x_lower_ws(const float* L1, const float* L2, float* C, int N, int mode, void* ws,
                                     size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_lower_x_lower_ws");
   return packed_x_packed("smm_lower_x_lower", AKind::LowerPacked, BKind::LowerPacked, SMM_STRUCT_LOWER, L1, L2, C, N,
                          mode, ws, ws_bytes, as_stream(stream));
 }
@@ -602,6 +618,7 @@ __global__ void timeout_probe_kernel(uint32_t* status, unsigned long long limit_
 }  // namespace smm
 
 extern "C" int smm_debug_timeout_probe(unsigned long long wait_limit, void* stream) {
+  SMM_RANGE("smm_debug_timeout_probe");
   uint32_t* w = device_status_word();
   if (!w) return set_error(SMM_ERR_CUDA, "device status word unavailable");
   if (wait_limit == 0 || wait_limit > 10ull * 1000000000ull)
@@ -618,6 +635,7 @@ extern "C" int smm_debug_timeout_probe(unsigned long long wait_limit, void* stre
 // count, the first staged A/B words, shared-memory and instruction
 // descriptors, and the first accumulator words read back.
 extern "C" int smm_debug_trace_next(unsigned* trace) {
+  SMM_RANGE("smm_debug_trace_next");
   g_trace = trace;
   return SMM_OK;
 }
