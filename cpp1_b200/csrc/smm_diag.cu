@@ -207,10 +207,16 @@ extern "C" int smm_diag_rows_host(const float* d_host, const float* B_host, floa
   int dev = 0;
   SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
   HostPipe& hp = host_pipe(dev);
-  if (!hp.init) {
-    for (auto& s : hp.st) SMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
-    SMM_CUDA_TRY(cudaEventCreateWithFlags(&hp.d_ready, cudaEventDisableTiming), "event create");
-    hp.init = true;
+  {
+    // first call on this device: create its streams (once, even when several
+    // host threads make their first call together)
+    static std::mutex init_mu;
+    std::lock_guard<std::mutex> lock(init_mu);
+    if (!hp.init) {
+      for (auto& s : hp.st) SMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
+      SMM_CUDA_TRY(cudaEventCreateWithFlags(&hp.d_ready, cudaEventDisableTiming), "event create");
+      hp.init = true;
+    }
   }
   const size_t rows = chunk_rows(M, N);
   const size_t chunk = round256(rows * static_cast<size_t>(N) * sizeof(float));

@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include "smm_contract.h"
 
@@ -33,6 +34,10 @@ int host_streams(HostStreams** out) {
   int dev = 0;
   SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
   HostStreams& h = per_dev[dev & 63];
+  // first call on this device: create its streams (once, even when several
+  // host threads make their first call together)
+  static std::mutex init_mu;
+  std::lock_guard<std::mutex> lock(init_mu);
   if (!h.init) {
     for (auto& s : h.st) SMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
     SMM_CUDA_TRY(cudaEventCreateWithFlags(&h.left_ready, cudaEventDisableTiming), "event create");

@@ -195,7 +195,10 @@ int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float
  * points' within the mode's tolerance.  dev_ws must hold the matching
  * *_host_workspace_size bytes of device memory (16-byte aligned), with no
  * pending work on it: the calls run on internal streams that are not
- * ordered after the caller's streams. */
+ * ordered after the caller's streams.  Host threads may call them
+ * concurrently, each with its own workspace; calls on one device share its
+ * two internal streams (created on the first call) and so run one after
+ * another on the GPU. */
 size_t smm_gemm_host_workspace_size(int M, int N, int K, int mode);
 int smm_gemm_host(const float* A, const float* B, float* C, int M, int N, int K, int mode, void* dev_ws,
                   size_t ws_bytes);
