@@ -3,13 +3,18 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--op diag|gemm|upper|sandwich|toeplitz|add] [--mode 3xtf32|tf32|bf16]
 
-Default workload (what the metric is quoted on at N = 8192, one GPU):
-diagonal x dense, C = diag(d) B with d (8192) ~ U[0.5,1.5] and B (8192 x 8192)
-~ U[-1,1] (seeded, cpp1_b200.workloads), GB/s over the bytes the operation
-must move: 4N + 8N^2 per call.  The other ops are the remaining configured
-workloads (GEMM 8192^3, U B at 8192, A S B at 4096, T B at 16384), reported
-as useful TFLOP/s (structural zeros excluded); `add` (general + packed
+Default workload (what the metric is quoted on at N = 8192, one GPU, in its
+primary unit): upper-triangular x dense, C = U B with U (8192, packed upper,
+entries ~ U[-1,1]) and B (8192 x 8192, ~ U[-1,1]) (seeded,
+cpp1_b200.workloads), 3xTF32 (fp32 semantics), useful TFLOP/s over the
+N^2 (N+1) flops that exclude U's structural zeros.  The other ops are the
+remaining configured workloads (GEMM 8192^3, A S B at 4096, T B at 16384,
+diag(d) B at 8192^2 in GB/s over 4N + 8N^2 bytes); `add` (general + packed
 symmetric at 8192, the DSL's `+`) is reported in GB/s like the diagonal scale.
+
+Before timing, sampled output rows of every rank's slab are checked against
+the oracle's fp64 rows (normwise bound of the mode; the run fails loudly
+beyond it) and the result is reported under "check".
 
 Multi-GPU (torchrun, one process per GPU, NCCL):
   diag      weak scaling: every rank scales its own 8192 x 8192 row slab;
@@ -70,12 +75,14 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=sorted(WORKLOADS), default="diag")
+    ap.add_argument("--op", choices=sorted(WORKLOADS), default="upper")
     ap.add_argument("--mode", choices=["3xtf32", "tf32", "bf16"], default="3xtf32")
     ap.add_argument("--n", "--order", dest="n", type=int, default=None,
                     help="override the problem order (--order under torchrun, whose parser claims --n)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--roofline-s", type=float, default=1.0,
+                    help="seconds of repeated calls over which the roofline kernel is timed")
     a = ap.parse_args()
     if a.steps is None:
         a.steps = {"diag": 400, "gemm": 20, "upper": 30, "sandwich": 30, "toeplitz": 6, "add": 300}[a.op]
@@ -118,7 +125,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
     }
 
-    def __init__(self, index: int, period_s: float = 0.005):
+    def __init__(self, index: int, period_s: float = 0.001):
         self.index = index
         self.period = period_s
         self.samples = []
@@ -464,6 +471,25 @@ def run_ours(args, rank, world, local):
         else:
             def step():
                 compute(shared0)
+    # useful FLOPs of the first contraction kernel of one call (the one the
+    # roofline times alone): the slab product; for the sandwich its S B part
+    if op == "sandwich":
+        kernel_useful = 2 * (n if world == 1 else (x1 - x0)) * n * n
+    elif op not in HBM_OPS:
+        kernel_useful = units_per_rank_call
+    else:
+        kernel_useful = 0
+
+    # correctness of this rank's slab before anything is timed
+    step()
+    torch.cuda.synchronize()
+    ops.device_status()
+    check = check_slab(op, w, r0, r1, out, mode)
+    check["relerr"] = max_over_ranks(check["relerr"], world)
+    if not check["relerr"] <= check["tol"]:
+        raise RuntimeError(f"{op}: sampled rows differ from the oracle: relerr {check['relerr']:.3e} "
+                           f"> {check['tol']:.0e}")
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -512,7 +538,7 @@ def run_ours(args, rank, world, local):
     value = total_units / (ms_per_step * 1e-3) / scale
 
     # ---- roofline of the dominant kernel, timed on its own on this rank
-    roof = roofline(op, n, nrows, mode, step, stream, peaks, units_per_rank_call, world)
+    roof = roofline(op, n, mode, step, stream, peaks, kernel_useful, ms_per_step, world, L, local, args.roofline_s)
 
     res = {
         "metric": METRIC, "value": round(value, 3), "unit": WORKLOADS[op]["unit"], "n_gpus": world,
@@ -525,6 +551,7 @@ def run_ours(args, rank, world, local):
                    "parallelism": f"row-slabs x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (126 MB): no flush needed"},
         "roofline": roof,
+        "check": check,
         "gpu_launches": int(launches),
         **({"multi_gpu": multi} if multi else {}),
         "clocks": clk.summary(),
@@ -532,42 +559,140 @@ def run_ours(args, rank, world, local):
     return res, d_in, h_in
 
 
-def roofline(op, n, nrows, mode, step, stream, peaks, units_rank, world):
+def check_slab(op, w, r0, r1, out, mode):
+    """Normwise relative error of sampled rows of this rank's slab [r0, r1)
+    of C against the oracle's fp64 rows (diag and add: bit-exact against the
+    oracle's fp32 result, reported as 0 or inf)."""
+    import oracle as O
+    rng = np.random.default_rng(r0 + 7)
+    k = min(r1 - r0, 8)
+    if k <= 0:
+        return {"relerr": 0.0, "rows": 0, "tol": 0.0, "against": "no rows on this rank"}
+    rows = np.unique(np.concatenate([[r0, r1 - 1], rng.integers(r0, r1, size=max(k - 2, 0))])).astype(np.int32)
+    got = out[(rows - r0).tolist()].cpu().numpy()
+    if op == "diag":
+        ref = w["d"][rows, None] * w["B"][rows]
+        return {"relerr": 0.0 if np.array_equal(got, ref) else float("inf"), "rows": len(rows), "tol": 0.0,
+                "against": "oracle fp32 (bit-exact)"}
+    if op == "add":
+        S = w["S"]
+        n = w["A"].shape[1]
+        ref = np.empty_like(got)
+        for t, i in enumerate(rows):
+            srow = np.array([S[O_packed(min(i, j), max(i, j), n)] for j in range(n)], np.float32)
+            ref[t] = w["A"][i] + srow
+        return {"relerr": 0.0 if np.array_equal(got, ref) else float("inf"), "rows": len(rows), "tol": 0.0,
+                "against": "oracle fp32 (bit-exact)"}
+    if op == "gemm":
+        R = O.gemm_rows_f64(w["A"], w["B"], rows)
+    elif op == "upper":
+        R = O.upper_left_rows_f64(w["U"], w["B"], rows)
+    elif op == "sandwich":
+        R = O.sandwich_rows_f64(w["A"], w["S"], w["B"], rows)
+    else:
+        R = O.toeplitz_left_rows_f64(w["g"], w["B"], rows)
+    tol = {"3xtf32": 1e-5, "tf32": 5e-3, "bf16": 1e-2}[mode]
+    return {"relerr": float(O.relerr(got, R)), "rows": len(rows), "tol": tol, "against": "oracle fp64 rows"}
+
+
+def O_packed(i, j, n):
+    """Packed-upper index of (i, j), i <= j."""
+    return i * n - i * (i - 1) // 2 + (j - i)
+
+
+def roofline(op, n, mode, step, stream, peaks, kernel_useful, call_ms, world, L, local, seconds=1.0):
+    """Roofline of the dominant kernel, timed on the launching stream with
+    CUDA events.  HBM-bound ops: the kernel is the whole call.  Contractions:
+    the library brackets its first contraction kernel of each call with the
+    caller's events (smm_debug_time_next), so the time excludes operand
+    staging and packed-operand expansion; the whole call's time is reported
+    beside it.  Two runs: a burst of about 50 ms right after the timed region
+    (against the burst peaks: the kernel timed alone) and `seconds` of
+    back-to-back calls (against the sustained peak, under the power cap)."""
     import torch
-    reps = 50 if op in HBM_OPS else 3
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         return {"bound": WORKLOADS[op]["bound"], "note": "reported at n_gpus = 1"}
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for _ in range(reps):
-        step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    launch_ms = ev0.elapsed_time(ev1) / reps / (2 if op == "sandwich" else 1)
+
+    def run(reps):
+        torch.cuda.synchronize()
+        if op in HBM_OPS:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as clk:
+                ev0.record(stream)
+                for _ in range(reps):
+                    step()
+                ev1.record(stream)
+                torch.cuda.synchronize()
+            t = ev0.elapsed_time(ev1) / reps
+            return t, t, clk.summary()
+        pairs = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)  # creates the events; the library records them again around its kernel
+            e1.record(stream)
+            pairs.append((e0, e1))
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            c0.record(stream)
+            for e0, e1 in pairs:
+                _lib_check(L.smm_debug_time_next(e0.cuda_event, e1.cuda_event), "smm_debug_time_next")
+                step()
+            c1.record(stream)
+            torch.cuda.synchronize()
+        return (statistics.fmean(e0.elapsed_time(e1) for e0, e1 in pairs), c0.elapsed_time(c1) / reps,
+                clk.summary())
+
+    burst_reps = int(min(200, max(3, math.ceil(50.0 / max(call_ms, 1e-3)))))
+    sus_reps = int(min(4000, max(3, math.ceil(1000.0 * seconds / max(call_ms, 1e-3)))))
+    launch_ms, whole_ms, clocks = run(burst_reps)
+    s_launch_ms, s_whole_ms, s_clocks = run(sus_reps) if seconds > 0 else (None, None, None)
     if op in HBM_OPS:
         bytes_launch = hbm_bytes(op, n)
         achieved = bytes_launch / (launch_ms * 1e-3) / 1e9
         peak = peaks["hbm_gbs"]
-        traffic = profile_traffic(op)
-        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic,
-                "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": round(launch_ms, 4),
-                "peak_source": f"{peaks['source']} HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"}
+        out = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+               "frac": round(achieved / peak, 4), "traffic": profile_traffic(op),
+               "algorithmic_bytes_per_launch": bytes_launch, "launch_ms": round(launch_ms, 4), "reps": burst_reps,
+               "peak_source": f"{peaks['source']} HBM copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+               "clocks": clocks}
+        if s_launch_ms:
+            a = bytes_launch / (s_launch_ms * 1e-3) / 1e9
+            out["sustained"] = {"seconds": seconds, "reps": sus_reps, "launch_ms": round(s_launch_ms, 4),
+                                "achieved": round(a, 1), "frac": round(a / peak, 4), "clocks": s_clocks}
+        return out
     passes = {"3xtf32": 3, "tf32": 1, "bf16": 1}[mode]
-    useful = units_rank / (2 if op == "sandwich" else 1)
-    mma_flops = passes * useful
+    mma_flops = passes * kernel_useful
     achieved = mma_flops / (launch_ms * 1e-3) / 1e12
     if mode == "bf16":
-        peak, src = peaks["bf16_tflops"], f"{peaks['source']} cuBLAS bf16 burst"
+        peak, peak_s = peaks["bf16_tflops"], peaks["bf16_tflops_sustained"]
+        src = f"{peaks['source']} cuBLAS bf16 burst (sustained: the {peaks['source']} sustained figure)"
     else:
-        peak, src = peaks["bf16_tflops"] / 2, f"TF32 = half the {peaks['source']} cuBLAS bf16 burst"
-    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-            "frac": round(achieved / peak, 4), "traffic": profile_traffic(op),
-            "algorithmic_flops_per_launch": mma_flops, "launch_ms": round(launch_ms, 4),
-            "launch_covers": "one whole product call: operand staging / packed-operand expansion kernels "
-                             "plus the contraction kernel (the sandwich: half of its two-product call)",
-            "peak_source": src + f"; {passes} MMA pass(es) per useful FLOP"}
+        peak, peak_s = peaks["bf16_tflops"] / 2, peaks["bf16_tflops_sustained"] / 2
+        src = (f"TF32 = half the {peaks['source']} cuBLAS bf16 burst (sustained: half the sustained figure); "
+               "datasheet TF32 dense 1100 TFLOP/s")
+    out = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+           "frac": round(achieved / peak, 4), "frac_of_datasheet_tf32": (round(achieved / 1100.0, 4)
+                                                                        if mode != "bf16" else None),
+           "traffic": profile_traffic(op),
+           "algorithmic_flops_per_launch": mma_flops, "launch_ms": round(launch_ms, 4),
+           "call_ms": round(whole_ms, 4), "reps": burst_reps,
+           "launch_covers": "the contraction kernel alone (CUDA events recorded by the library right before and "
+                            "after its launch, on its stream); call_ms is the whole product call"
+                            + (" (the sandwich: its first product, S B)" if op == "sandwich" else ""),
+           "peak_source": src + f"; {passes} MMA pass(es) per useful FLOP",
+           "clocks": clocks}
+    if s_launch_ms:
+        a = mma_flops / (s_launch_ms * 1e-3) / 1e12
+        out["sustained"] = {"seconds": seconds, "reps": sus_reps, "launch_ms": round(s_launch_ms, 4),
+                            "call_ms": round(s_whole_ms, 4), "achieved": round(a, 1), "peak": peak_s,
+                            "frac": round(a / peak_s, 4), "clocks": s_clocks}
+    return out
+
+
+def _lib_check(rc, what):
+    from cpp1_b200 import _lib
+    _lib.check(rc, what)
 
 
 # The public call each op's e2e goes through.

@@ -115,6 +115,8 @@ SIGNATURES = [
     ("smm_compat_symm_sandwich", _i, [_vp, _vp, _vp, _vp, _vp, _i, _vp]),
     ("smm_debug_timeout_probe", _i, [_ull, _vp]),
     ("smm_debug_trace_next", _i, [_vp]),
+    ("smm_debug_time_next", _i, [_vp, _vp]),
+    ("smm_debug_wait_limit_next", _i, [_ull]),
 ]
 
 _lib = None

@@ -56,6 +56,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// The same with an explicit bound on how long the hardware may suspend the
+// thread inside the try (ns): it resumes when the phase completes or when the
+// hint elapses, whichever is first.  Without a hint the suspension bound is
+// system-defined and can exceed a short wait limit.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar_addr, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Shared state every role of a pipelined kernel consults while waiting: an
 // abort flag in shared memory (set by whichever role gives up first, so the
 // others stop waiting too), the wait limit, and the kernel's device status
@@ -70,14 +86,17 @@ struct WaitCtx {
 // Wait until the barrier phase with the given parity has completed.  Bounded:
 // returns false (and raises the abort flag, records kDevErrTimeout) once
 // limit_ns of wall time has passed, or as soon as another role aborted.
+// Each try suspends the thread for at most limit/8 (between 100 ns and
+// 20 us), so the limit, the abort flag and a completing phase are all seen
+// promptly.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& w) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t h = w.limit_ns / 8;
+  const uint32_t hint = static_cast<uint32_t>(h < 100 ? 100 : (h > 20000 ? 20000 : h));
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait_hint(a, parity, hint)) return true;
     if (*w.abort_flag) return false;
     if (globaltimer_ns() - t0 > w.limit_ns) {
       *w.abort_flag = 1;

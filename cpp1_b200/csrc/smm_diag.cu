@@ -174,9 +174,9 @@ struct HostPipe {
   bool init = false;
 };
 
-HostPipe& host_pipe(int dev) {
+HostPipe& host_pipe(int dev) {  // dev in [0, 64)
   static HostPipe pipes[64];
-  return pipes[dev & 63];
+  return pipes[dev];
 }
 
 size_t chunk_rows(int M, int N) {
@@ -206,6 +206,7 @@ extern "C" int smm_diag_rows_host(const float* d_host, const float* B_host, floa
     return set_error(SMM_ERR_WORKSPACE, "smm_diag_rows_host: workspace %zu bytes < %zu required", ws_bytes, need);
   int dev = 0;
   SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return set_error(SMM_ERR_UNSUPPORTED, "smm_diag_rows_host: device index %d >= 64", dev);
   HostPipe& hp = host_pipe(dev);
   {
     // first call on this device: create its streams (once, even when several

@@ -33,7 +33,8 @@ int host_streams(HostStreams** out) {
   static HostStreams per_dev[64];
   int dev = 0;
   SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-  HostStreams& h = per_dev[dev & 63];
+  if (dev < 0 || dev >= 64) return set_error(SMM_ERR_UNSUPPORTED, "host-buffer entry points: device index %d >= 64", dev);
+  HostStreams& h = per_dev[dev];
   // first call on this device: create its streams (once, even when several
   // host threads make their first call together)
   static std::mutex init_mu;

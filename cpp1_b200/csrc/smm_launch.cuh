@@ -22,10 +22,10 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
   static bool attr_set[64] = {};
   int dev = 0;
   SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-  if (!attr_set[dev & 63]) {
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {  // cached for device indices below 64
     SMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                  "cudaFuncSetAttribute(max dynamic smem)");
-    attr_set[dev & 63] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   const long long blocks = static_cast<long long>(p.row_tiles) * p.col_tiles * (PAIR ? 2 : 1);
   if (blocks > 0x7FFFFFFFLL) return set_error(SMM_ERR_INVALID, "product too large for one launch");

@@ -43,29 +43,40 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 void count_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+// Device address of g_smm_status on the current device (cached for device
+// indices below 64; null for others or on failure).
 uint32_t* device_status_word() {
   static uint32_t* addr[64] = {};
   static std::mutex mu;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lk(mu);
-  if (!addr[dev & 63]) {
+  if (!addr[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_smm_status) != cudaSuccess) return nullptr;
-    addr[dev & 63] = static_cast<uint32_t*>(p);
+    addr[dev] = static_cast<uint32_t*>(p);
   }
-  return addr[dev & 63];
+  return addr[dev];
 }
 
+// Limit of every pipeline wait in the contraction kernels: SMM_WAIT_LIMIT_MS
+// (a positive number of milliseconds; unset, 0 or unparsable keeps the
+// 2000 ms default).  smm_debug_wait_limit_next sets a limit in nanoseconds
+// for one launch.
 unsigned long long wait_limit_ns() {
   static unsigned long long v = [] {
     const char* e = std::getenv("SMM_WAIT_LIMIT_MS");
-    unsigned long long ms = e ? std::strtoull(e, nullptr, 10) : 2000ull;
+    unsigned long long ms = e ? std::strtoull(e, nullptr, 10) : 0ull;
     if (ms == 0) ms = 2000ull;
     return ms * 1000000ull;
   }();
   return v;
 }
+
+// Teardown waits (for TMA copies and MMAs a CTA has already issued) get at
+// least a second even when the pipeline limit is far shorter: a CTA must not
+// exit while a bulk copy into its shared memory is still in flight.
+constexpr unsigned long long kMinDrainNs = 1000000000ull;
 
 // ---------------------------------------------------------------- TMA maps
 namespace {
@@ -135,6 +146,12 @@ int pick_bn(int M, int N, bool pair) {
 // Diagnostic record target for the next contraction launch (set by
 // smm_debug_trace_next, consumed by one launch).
 thread_local uint32_t* g_trace = nullptr;
+// Events recorded on the launch stream right before and after the next
+// contraction kernel launched from this thread (smm_debug_time_next), and a
+// pipeline wait limit for that launch (smm_debug_wait_limit_next).
+thread_local cudaEvent_t g_ev_before = nullptr;
+thread_local cudaEvent_t g_ev_after = nullptr;
+thread_local unsigned long long g_wait_next = 0;
 
 }  // namespace
 
@@ -149,8 +166,14 @@ int check_packed(const char* who, int N) {
 // Core contraction: C(M x N, ldc) = Aop(M x K) * B(K x N, ldb).
 // Preconditions: B (and A when dense) 16-byte aligned with ld % 4 == 0.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
-                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16) {
+                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16,
+                    bool accumulate) {
   const bool bf16 = (mode == SMM_MODE_BF16);
+  if (accumulate && (C_lo || C_bf16))
+    return set_error(SMM_ERR_INVALID, "internal: accumulating contraction with extra outputs");
+  const int ks = bf16 ? 32 : 16;  // K elements per k-block
+  if (a.k_off != 0 && (a.k_off % ks != 0 || bk != BKind::Dense || b.tri != 0))
+    return set_error(SMM_ERR_INVALID, "internal: K offset %d with this right operand", a.k_off);
   const bool pair = use_pairs(M, N);
   const int bn = pick_bn(M, N, pair);
   Maps m;
@@ -184,6 +207,8 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.a_dim = a.dim;
   p.a_row0 = a.row0;
   p.a_lower = a.lower ? 1 : 0;
+  p.k_off = a.k_off;
+  p.accumulate = accumulate ? 1 : 0;
   p.b_tri = b.tri;
   p.b_src = b.src;
   p.b_dim = b.dim;
@@ -191,11 +216,18 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.col_tiles = (N + bn - 1) / bn;
   p.raster_group = 8;
   p.status = device_status_word();
-  p.wait_limit_ns = wait_limit_ns();
+  p.wait_limit_ns = g_wait_next ? g_wait_next : wait_limit_ns();
+  p.drain_limit_ns = std::max(p.wait_limit_ns, kMinDrainNs);
   p.trace = g_trace;
-  if (!p.status) return set_error(SMM_ERR_CUDA, "device status word unavailable");
   g_trace = nullptr;
-  return launch_kinds(ak, bk, bn, pair, mode, m, p, st);
+  g_wait_next = 0;
+  cudaEvent_t ev_before = g_ev_before, ev_after = g_ev_after;
+  g_ev_before = g_ev_after = nullptr;
+  if (!p.status) return set_error(SMM_ERR_CUDA, "device status word unavailable");
+  if (ev_before) SMM_CUDA_TRY(cudaEventRecord(ev_before, st), "record event before the contraction");
+  const int rc = launch_kinds(ak, bk, bn, pair, mode, m, p, st);
+  if (rc == SMM_OK && ev_after) SMM_CUDA_TRY(cudaEventRecord(ev_after, st), "record event after the contraction");
+  return rc;
 }
 
 Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf) {
@@ -640,6 +672,26 @@ extern "C" int smm_debug_trace_next(unsigned* trace) {
   return SMM_OK;
 }
 
+// Measurement: the next contraction kernel launched from this thread is
+// bracketed by cudaEventRecord(before) and cudaEventRecord(after) on its
+// stream, so the caller can time that kernel alone (staging and expansion
+// kernels of the same call fall outside the pair).  Either may be NULL.
+extern "C" int smm_debug_time_next(void* event_before, void* event_after) {
+  g_ev_before = static_cast<cudaEvent_t>(event_before);
+  g_ev_after = static_cast<cudaEvent_t>(event_after);
+  return SMM_OK;
+}
+
+// Failure-path test: the next contraction kernel launched from this thread
+// gives every pipeline wait `wait_limit_ns` nanoseconds instead of the
+// default (teardown waits keep at least a second).  0 restores the default.
+extern "C" int smm_debug_wait_limit_next(unsigned long long wait_limit_ns) {
+  if (wait_limit_ns > 10ull * 1000000000ull)
+    return set_error(SMM_ERR_INVALID, "smm_debug_wait_limit_next: limit must be at most 10 s");
+  g_wait_next = wait_limit_ns;
+  return SMM_OK;
+}
+
 // ---------------------------------------------------------------- allocation-free sandwich
 // Scratch of smm_symm_sandwich_noalloc: the S*B intermediate, plus padded
 // copies of A and B when their rows are not 16-byte multiples, or the bf16
@@ -653,20 +705,25 @@ namespace smm {
 namespace {
 constexpr size_t kNoallocScratchBytes = sizeof(g_noalloc_scratch);
 
+constexpr int kMaxCachedDevices = 64;
+
 // Device address of g_noalloc_scratch on the current device, looked up once
 // per device (with that device current) and cached.
 int noalloc_scratch(void** out) {
-  static void* addr[64] = {};
+  static void* addr[kMaxCachedDevices] = {};
   static std::mutex mu;
   int dev = 0;
   SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxCachedDevices)
+    return set_error(SMM_ERR_UNSUPPORTED, "smm_symm_sandwich_noalloc: device index %d (at most %d devices)", dev,
+                     kMaxCachedDevices);
   std::lock_guard<std::mutex> lk(mu);
-  if (!addr[dev & 63]) {
+  if (!addr[dev]) {
     void* p = nullptr;
     SMM_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(static sandwich scratch)");
-    addr[dev & 63] = p;
+    addr[dev] = p;
   }
-  *out = addr[dev & 63];
+  *out = addr[dev];
   return SMM_OK;
 }
 }  // namespace
@@ -674,6 +731,7 @@ int noalloc_scratch(void** out) {
 
 extern "C" int smm_symm_sandwich_noalloc(const float* A, const float* S, const float* B, float* C, int N, int mode,
                                          void* stream) {
+  SMM_RANGE("smm_symm_sandwich_noalloc");
   if (N < 0) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: negative shape");
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_symm_sandwich_noalloc: unknown mode %d", mode);
   if (N == 0) return SMM_OK;
@@ -683,7 +741,8 @@ extern "C" int smm_symm_sandwich_noalloc(const float* A, const float* S, const f
   if (need > kNoallocScratchBytes)
     return set_error(SMM_ERR_WORKSPACE,
                      "smm_symm_sandwich_noalloc: N = %d needs %zu bytes of scratch but the static scratch holds %zu "
-                     "(fp32 modes: N <= 2048 with N %% 4 == 0 and 16-byte-aligned A, B; bf16: N <= 1290)",
+                     "(fp32 modes: N <= 2048 with N %% 4 == 0 and 16-byte-aligned A, B, else N <= 1180; "
+                     "bf16: N <= 1294)",
                      N, need, kNoallocScratchBytes);
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;

@@ -169,10 +169,10 @@ int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, flo
  * N % 4 != 0 or they are not 16-byte aligned) lives in a fixed 16 MiB static
  * device array inside libsmm, which every GPU that loads the library holds
  * until process exit: N <= 2048 in the fp32 modes with N % 4 == 0 and
- * 16-byte-aligned A, B (about 1180 when padded copies are needed), N <= 1290
+ * 16-byte-aligned A, B, N <= 1180 when padded copies are needed, N <= 1294
  * in bf16 mode (the bf16 copies share it).  S is expanded into a dense copy
- * only when the scratch has room left for it, else mirrored on chip.  Larger N returns
- * SMM_ERR_WORKSPACE.  Calls no
+ * only when the scratch has room left for it (fp32 aligned: N <= 1448), else
+ * mirrored on chip.  Larger N returns SMM_ERR_WORKSPACE.  Calls no
  * cudaMalloc/cudaFree.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress) and must come before any stream
  * capture.  Every call shares the one array and it keeps the last call's
@@ -357,6 +357,24 @@ int smm_debug_timeout_probe(unsigned long long wait_limit_ns, void* stream);
  * tensor-memory base, k-block count, first staged operand words, matrix and
  * instruction descriptors, first accumulator words).  NULL disables. */
 int smm_debug_trace_next(unsigned* trace);
+
+/* Measurement: the next tensor-core contraction kernel launched from the
+ * calling thread is bracketed by cudaEventRecord(event_before) and
+ * cudaEventRecord(event_after) (cudaEvent_t handles) on its stream, so that
+ * kernel can be timed alone, without the staging or expansion kernels of the
+ * same call.  Either may be NULL.  No counterpart in the reference, whose
+ * generated wrappers time their one kernel the same way
+ * (src/dsl/codegen_cuda.py:257-275). */
+int smm_debug_time_next(void* event_before, void* event_after);
+
+/* Failure-path test: the next tensor-core contraction kernel launched from
+ * the calling thread gives each pipeline wait `wait_limit_ns` nanoseconds
+ * instead of the default (SMM_WAIT_LIMIT_MS, 2000 ms when unset); teardown
+ * waits for copies and MMAs already issued keep at least one second.  A limit
+ * shorter than the first TMA round trip makes the kernel give up, record
+ * the expiry, write no output and exit cleanly; smm_device_status then
+ * returns SMM_ERR_DEVICE_TIMEOUT.  0 restores the default; at most 10 s. */
+int smm_debug_wait_limit_next(unsigned long long wait_limit_ns);
 
 #ifdef __cplusplus
 }
