@@ -20,12 +20,14 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
   diag      weak scaling: every rank scales its own 8192 x 8192 row slab;
             no collective on the data path (the rows are independent).
   others    strong scaling: the output is split into row slabs (equal-work
-            boundaries for the triangular operand); the shared operand B (S
-            and B for A S B) is broadcast from rank 0 each step inside the
-            timed region, double-buffered so that the broadcast for the next
-            step overlaps this step's compute; the line also carries the
-            compute-only time.  A S B computes row slabs of X = S B, all-gathers
-            X, then row slabs of A X.
+            boundaries for the triangular operand); each step is one libsmm
+            multi-GPU call (smm_mg_*): the shared operand B (S and B for
+            A S B) is broadcast from rank 0 in K-chunks inside the call and
+            every rank accumulates its slab chunk by chunk as they land, so
+            the transfer overlaps the contraction within one product.  A S B
+            computes (A_slab S) B per slab.  The line also carries the
+            compute-only time and the fused call's roofline (MMA time vs the
+            NVLink time of the broadcast bytes).
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launching stream, max over
@@ -307,39 +309,6 @@ def cpu_baseline(op: str, n: int, budget_s: float = 12.0):
 
 
 # ---------------------------------------------------------------- our arm
-class SharedOperandPipeline:
-    """Double-buffered NCCL broadcast of the operands every rank needs (held
-    by rank 0): step i computes with buffer i % 2 while the broadcast for step
-    i+1 fills the other buffer on a side stream.  Every rank issues the same
-    collectives in the same order."""
-
-    def __init__(self, shared, stream):
-        import torch
-        self.torch = torch
-        self.bufs = [list(shared), [t.clone() for t in shared]]
-        self.stream = stream
-        self.comm = torch.cuda.Stream()
-        self.done = [torch.cuda.Event(), torch.cuda.Event()]
-        self.works = [None, None]
-        self.i = 0
-        self._issue(0)
-
-    def _issue(self, idx):
-        import torch.distributed as dist
-        with self.torch.cuda.stream(self.comm):
-            self.comm.wait_event(self.done[idx])  # buffer idx no longer read by compute
-            self.works[idx] = [dist.broadcast(t, src=0, async_op=True) for t in self.bufs[idx]]
-
-    def step(self, compute):
-        idx = self.i % 2
-        for w in self.works[idx]:
-            w.wait()  # the compute stream waits for this buffer's broadcast
-        compute(self.bufs[idx])
-        self.done[idx].record(self.stream)
-        self._issue(1 - idx)
-        self.i += 1
-
-
 def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
@@ -374,14 +343,9 @@ def run_ours(args, rank, world, local):
         h_in = [w["A"], w["S"]]
     d_in = [torch.from_numpy(x).cuda() for x in h_in]
 
-    from cpp1_b200.multigpu import row_slabs, slab_useful_flops
-    if op in HBM_OPS:
-        bounds = None
-    elif op == "sandwich":
-        from cpp1_b200.multigpu import uniform_shares
-        bounds = uniform_shares(n, world)
-    else:
-        bounds = row_slabs(n, world, triangular=(op == "upper"))
+    from cpp1_b200 import multigpu as MG
+    from cpp1_b200.multigpu import slab_useful_flops
+    bounds = None if op in HBM_OPS else MG.lib_row_slabs(n, world, triangular=(op == "upper"))
     r0, r1 = (bounds[rank], bounds[rank + 1]) if bounds else (0, n)
     nrows = r1 - r0
     out = torch.empty((nrows, n), dtype=torch.float32, device="cuda")
@@ -406,75 +370,68 @@ def run_ours(args, rank, world, local):
                        "add")
         units_per_rank_call = hbm_bytes(op, n)
     else:
-        # Contractions: compute(shared) runs this rank's row slab with the
-        # shared operands (B; S and B for the sandwich).  At G > 1 they are
-        # broadcast from rank 0 every step, double-buffered: the broadcast for
-        # step i+1 runs on a side stream while step i computes.
+        # Contractions.  One GPU: the single-GPU entry point.  G > 1: one
+        # libsmm multi-GPU call per step (smm_mg_*): B (S and B for the
+        # sandwich) is broadcast from rank 0 in K-chunks inside the call and
+        # this rank's row slab is accumulated chunk by chunk as they land.
+        # slab_local() runs the same slab with the operands already in place (the
+        # single-GPU slab entry points), for the compute-only time.
+        comm = MG.Communicator(rank, world) if world > 1 else None
         if op == "gemm":
             A, B = d_in
-            shared0 = [B]
-            ws, wsb = ws_for(L.smm_gemm_workspace_size(nrows, n, n, m))
+            A_slab = A[r0:r1]
+            ws, wsb = ws_for(L.smm_gemm_workspace_size(max(nrows, 1), n, n, m))
 
-            def compute(sh):
-                Ap = A.data_ptr() + r0 * n * 4
-                _lib.check(L.smm_gemm(Ap, sh[0].data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+            def slab_local():
+                if nrows:
+                    _lib.check(L.smm_gemm(A_slab.data_ptr(), B.data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb,
+                                          sp), "gemm")
+
+            def step():
+                comm.gemm(A_slab, B, out, mode) if comm else slab_local()
             units_per_rank_call = 2 * nrows * n * n
         elif op == "upper":
             U, B = d_in
-            shared0 = [B]
             ws, wsb = ws_for(L.smm_upper_left_workspace_size(n, n, _lib.FMT_PACKED, m))
 
-            def compute(sh):
-                _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, sh[0].data_ptr(), out.data_ptr(), n,
-                                                 n, r0, nrows, m, ws, wsb, sp), "upper")
+            def slab_local():
+                _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, B.data_ptr(), out.data_ptr(), n, n,
+                                                 r0, nrows, m, ws, wsb, sp), "upper")
+
+            def step():
+                comm.upper_left(U, B, out, r0, mode) if comm else slab_local()
             units_per_rank_call = slab_useful_flops("upper", n, r0, r1)
         elif op == "sandwich":
             A, S, B = d_in
-            shared0 = [S, B]
-            from cpp1_b200.multigpu import uniform_shares, allgather_rows
-            xb = uniform_shares(n, world)
-            x0, x1 = xb[rank], xb[rank + 1]
-            per = xb[1] - xb[0]
-            X = torch.empty((max(per * world, n), n), dtype=torch.float32, device="cuda")
-            X_share = torch.empty((per, n), dtype=torch.float32, device="cuda")
-            ws, wsb = ws_for(max(L.smm_gemm_workspace_size(nrows, n, n, m), L.smm_symm_left_workspace_size(n, n, m)))
+            A_slab = A[r0:r1]
+            ws, wsb = ws_for(L.smm_symm_sandwich_workspace_size(n, m))
 
-            def compute(sh):
-                # X rows [x0, x1) = S[x0:x1] B on this rank, X all-gathered,
-                # then this rank's rows of C = A X: no work is repeated.
-                if world > 1:
-                    if x1 > x0:
-                        _lib.check(L.smm_symm_left_rows(sh[0].data_ptr(), sh[1].data_ptr(), X_share.data_ptr(), n, n,
-                                                        x0, x1 - x0, m, ws, wsb, sp), "symm")
-                    allgather_rows(X_share, world, n, out=X)
-                else:
-                    _lib.check(L.smm_symm_left(sh[0].data_ptr(), sh[1].data_ptr(), X.data_ptr(), n, n, m, ws, wsb,
-                                               sp), "symm")
-                if nrows > 0:
-                    Ap = A.data_ptr() + r0 * n * 4
-                    _lib.check(L.smm_gemm(Ap, X.data_ptr(), out.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
-            units_per_rank_call = (4 * n ** 3) // world
+            def slab_local():
+                if world == 1:
+                    _lib.check(L.smm_symm_sandwich(A.data_ptr(), S.data_ptr(), B.data_ptr(), out.data_ptr(), n, m,
+                                                   ws, wsb, sp), "sandwich")
+                elif nrows:  # (A_slab S) B, the order the multi-GPU call uses
+                    ops.gemm(ops.gen_x_symm(A_slab, S, mode=mode), B, mode=mode, out=out)
+
+            def step():
+                comm.symm_sandwich(A_slab, S, B, out, mode) if comm else slab_local()
+            units_per_rank_call = 4 * nrows * n * n
         else:
             g, B = d_in
-            shared0 = [B]
             ws, wsb = ws_for(L.smm_toeplitz_left_workspace_size(n, n, m))
 
-            def compute(sh):
-                _lib.check(L.smm_toeplitz_left_rows(g.data_ptr(), sh[0].data_ptr(), out.data_ptr(), n, n, r0, nrows,
+            def slab_local():
+                _lib.check(L.smm_toeplitz_left_rows(g.data_ptr(), B.data_ptr(), out.data_ptr(), n, n, r0, nrows,
                                                     m, ws, wsb, sp), "toeplitz")
-            units_per_rank_call = 2 * nrows * n * n
-        if world > 1:
-            pipe = SharedOperandPipeline(shared0, stream)
 
             def step():
-                pipe.step(compute)
-        else:
-            def step():
-                compute(shared0)
+                comm.toeplitz_left(g, B, out, r0, mode) if comm else slab_local()
+            units_per_rank_call = 2 * nrows * n * n
+
     # useful FLOPs of the first contraction kernel of one call (the one the
     # roofline times alone): the slab product; for the sandwich its S B part
     if op == "sandwich":
-        kernel_useful = 2 * (n if world == 1 else (x1 - x0)) * n * n
+        kernel_useful = 2 * n * n * n  # its first product, S B (one GPU)
     elif op not in HBM_OPS:
         kernel_useful = units_per_rank_call
     else:
@@ -512,9 +469,11 @@ def run_ours(args, rank, world, local):
     ms = max_over_ranks(ms_local, world)
     ms_per_step = ms / args.steps
 
-    # ---- G > 1: the same steps without the operand broadcasts (the
-    # sandwich keeps its X all-gather, part of the algorithm), so the line
-    # shows compute-only and broadcast-inclusive times side by side.
+    # ---- G > 1: the same slabs with the operands already in place (no
+    # broadcast), so the line shows compute-only and broadcast-inclusive times
+    # side by side, and the roofline of the fused call: the slower of the
+    # heaviest slab's MMA work at the TF32 (bf16) peak and the bytes each
+    # receiving rank must take in over NVLink at the measured 770 GB/s.
     multi = None
     if world > 1 and op not in HBM_OPS:
         barrier(world)
@@ -522,15 +481,30 @@ def run_ours(args, rank, world, local):
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         c0.record(stream)
         for _ in range(args.steps):
-            compute(shared0)
+            slab_local()
         c1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
         ms_c = max_over_ranks(c0.elapsed_time(c1), world) / args.steps
+        bcast = 4 * n * n + (2 * n * (n + 1) if op == "sandwich" else 0)
+        passes = {"3xtf32": 3, "tf32": 1, "bf16": 1}[mode]
+        peak = peaks["bf16_tflops"] / (1 if mode == "bf16" else 2)
+        heaviest = max_over_ranks(float(units_per_rank_call), world)
+        t_mma = passes * heaviest / (peak * 1e12) * 1e3
+        t_link = bcast / 770e9 * 1e3
         multi = {"compute_only_ms_per_step": round(ms_c, 4), "broadcast_inclusive_ms_per_step": round(ms_per_step, 4),
-                 "broadcast_bytes_per_step": int(sum(t.numel() * 4 for t in shared0)),
-                 "overlap": "broadcast of step i+1 on a side stream during step i (double-buffered operands)",
-                 "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)]}
+                 "broadcast_bytes_per_step": int(bcast),
+                 "k_chunks": MG.lib_chunks(n, world),
+                 "overlap": "B broadcast from rank 0 in K-chunks inside each call (libsmm smm_mg_*, NCCL on a "
+                            "high-priority stream); each chunk's contraction starts as soon as it lands",
+                 "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)],
+                 "roofline": {"bound": "tensor" if t_mma >= t_link else "nvlink",
+                              "t_mma_ms": round(t_mma, 4), "t_nvlink_ms": round(t_link, 4),
+                              "target_ms": round(max(t_mma, t_link), 4),
+                              "frac": round(max(t_mma, t_link) / ms_per_step, 4),
+                              "basis": f"heaviest slab's {passes}-pass MMA FLOPs at {peak:.1f} TFLOP/s; "
+                                       "broadcast bytes at the measured 770 GB/s peer bandwidth"}}
+        comm.close()
 
     total_units = units_per_rank_call * world if op in HBM_OPS else (
         n * n * (n + 1) if op == "upper" else (4 * n ** 3 if op == "sandwich" else 2 * n ** 3))

@@ -116,6 +116,21 @@ SIGNATURES = [
     ("smm_debug_timeout_probe", _i, [_ull, _vp]),
     ("smm_debug_trace_next", _i, [_vp]),
     ("smm_debug_time_next", _i, [_vp, _vp]),
+    ("smm_mg_unique_id", _i, [_vp]),
+    ("smm_mg_comm_init", _i, [_vp, _i, _i, _vp]),
+    ("smm_mg_comm_destroy", _i, [_vp]),
+    ("smm_mg_comm_abort", _i, [_vp]),
+    ("smm_mg_comm_status", _i, [_vp]),
+    ("smm_mg_row_slabs", _i, [_i, _i, _i, _vp]),
+    ("smm_mg_chunks", _i, [_i, _i, _vp]),
+    ("smm_mg_gemm_workspace_size", _sz, [_i, _i, _i, _i]),
+    ("smm_mg_gemm", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_mg_upper_left_workspace_size", _sz, [_i, _i, _i, _i, _i]),
+    ("smm_mg_upper_left", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_mg_toeplitz_left_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_mg_toeplitz_left", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_mg_symm_sandwich_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_mg_symm_sandwich", _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_debug_wait_limit_next", _i, [_ull]),
 ]
 

@@ -1,4 +1,5 @@
-"""Row-slab partition of a structured product across the GPUs of one node.
+"""Row-slab partition of a structured product across the GPUs of one node,
+and the host side of libsmm's multi-GPU products (``Communicator``).
 
 One process per GPU (torchrun), torch.distributed over NCCL for the
 plumbing.  For C = X B with X one of the library's left operands (dense A,
@@ -13,6 +14,11 @@ packed U, Toeplitz generator, packed S):
   equal-work: boundary g of G sits at N (1 - sqrt(1 - g/G)), rounded to the
   128-row tile height;
 * the diagonal scale shards with no collective at all (rows independent).
+
+``Communicator`` wraps libsmm's own NCCL communicator (``smm_mg_*``): each
+product call broadcasts B from the root in K-chunks on a high-priority
+stream and accumulates this rank's slab chunk by chunk as they land, so the
+transfer overlaps the tensor-core work inside one call.
 
 No kernel reads another GPU's memory; remote data reaches local HBM through
 NCCL before any kernel touches it.
@@ -181,3 +187,127 @@ def distributed_sandwich(x_rows: Callable[[int, int], object], c_rows: Callable[
     X = x_rows(r0, r1)
     X_full = allgather_rows(X, world, n, out=x_out) if world > 1 else X
     return c_rows(X_full, r0, r1)
+
+
+# ---------------------------------------------------------------- libsmm multi-GPU communicator
+class Communicator:
+    """This rank's libsmm multi-GPU communicator (NCCL, one process per GPU),
+    on the current CUDA device.  Collective: every rank constructs it.  The
+    NCCL unique id is made by rank 0 and handed to the others over
+    torch.distributed (any initialised backend), or passed in as ``uid``."""
+
+    def __init__(self, rank: int, world: int, uid: Optional[bytes] = None):
+        import ctypes
+        from . import _lib
+        self._lib = _lib
+        L = _lib.load()
+        self.rank, self.world = rank, world
+        idbuf = ctypes.create_string_buffer(128)
+        if world > 1:
+            if uid is None:
+                import torch.distributed as dist
+                obj = [None]
+                if rank == 0:
+                    _lib.check(L.smm_mg_unique_id(idbuf), "smm_mg_unique_id")
+                    obj = [bytes(idbuf.raw)]
+                dist.broadcast_object_list(obj, src=0)
+                uid = obj[0]
+            idbuf = ctypes.create_string_buffer(bytes(uid), 128)
+        h = ctypes.c_void_p()
+        _lib.check(L.smm_mg_comm_init(ctypes.byref(h), rank, world, idbuf), "smm_mg_comm_init")
+        self.h = h
+
+    def close(self) -> None:
+        if self.h is not None:
+            self._lib.check(self._lib.load().smm_mg_comm_destroy(self.h), "smm_mg_comm_destroy")
+            self.h = None
+
+    def abort(self) -> None:
+        if self.h is not None:
+            self._lib.load().smm_mg_comm_abort(self.h)
+            self.h = None
+
+    def status(self) -> None:
+        self._lib.check(self._lib.load().smm_mg_comm_status(self.h), "smm_mg_comm_status")
+
+    # ---- helpers
+    @staticmethod
+    def _stream(stream):
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream()
+        return s.cuda_stream or None
+
+    def _ws(self, nbytes, device):
+        from . import ops
+        buf = ops.workspace(nbytes, device)
+        return (buf.data_ptr(), buf.numel()) if buf is not None else (None, 0)
+
+    # ---- products (every rank calls them with the same shapes, mode and root)
+    def gemm(self, A_slab, B, C_slab, mode: str = "3xtf32", root: int = 0, stream=None):
+        """C_slab = A_slab @ B with B broadcast from `root` (B is overwritten
+        with the root's data on the other ranks)."""
+        L = self._lib.load()
+        m = self._lib.MODES[mode]
+        nrows, K = A_slab.shape
+        N = B.shape[1]
+        ws, wsb = self._ws(L.smm_mg_gemm_workspace_size(nrows, N, K, m), B.device)
+        self._lib.check(L.smm_mg_gemm(self.h, A_slab.data_ptr(), B.data_ptr(), C_slab.data_ptr(), nrows, N, K, m,
+                                      root, ws, wsb, self._stream(stream)), "smm_mg_gemm")
+        return C_slab
+
+    def upper_left(self, U, B, C_slab, row0: int, mode: str = "3xtf32", root: int = 0, stream=None):
+        """C_slab = U[row0:row0+nrows] @ B, U packed upper on every rank."""
+        L = self._lib.load()
+        m = self._lib.MODES[mode]
+        N, ncols = B.shape
+        nrows = C_slab.shape[0] if C_slab is not None else 0
+        ws, wsb = self._ws(L.smm_mg_upper_left_workspace_size(N, ncols, row0, nrows, m), B.device)
+        cp = C_slab.data_ptr() if nrows else None
+        self._lib.check(L.smm_mg_upper_left(self.h, U.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m, root,
+                                            ws, wsb, self._stream(stream)), "smm_mg_upper_left")
+        return C_slab
+
+    def toeplitz_left(self, g, B, C_slab, row0: int, mode: str = "3xtf32", root: int = 0, stream=None):
+        """C_slab = T[row0:row0+nrows] @ B, T of generator g on every rank."""
+        L = self._lib.load()
+        m = self._lib.MODES[mode]
+        N, ncols = B.shape
+        nrows = C_slab.shape[0] if C_slab is not None else 0
+        ws, wsb = self._ws(L.smm_mg_toeplitz_left_workspace_size(N, ncols, m), B.device)
+        cp = C_slab.data_ptr() if nrows else None
+        self._lib.check(L.smm_mg_toeplitz_left(self.h, g.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m,
+                                               root, ws, wsb, self._stream(stream)), "smm_mg_toeplitz_left")
+        return C_slab
+
+    def symm_sandwich(self, A_slab, S, B, C_slab, mode: str = "3xtf32", root: int = 0, stream=None):
+        """C_slab = (A_slab @ S) @ B with packed S and B broadcast from `root`."""
+        L = self._lib.load()
+        m = self._lib.MODES[mode]
+        N = B.shape[0]
+        nrows = A_slab.shape[0] if A_slab is not None else 0
+        ws, wsb = self._ws(L.smm_mg_symm_sandwich_workspace_size(N, nrows, m), B.device)
+        ap = A_slab.data_ptr() if nrows else None
+        cp = C_slab.data_ptr() if nrows else None
+        self._lib.check(L.smm_mg_symm_sandwich(self.h, ap, S.data_ptr(), B.data_ptr(), cp, N, nrows, m, root, ws,
+                                               wsb, self._stream(stream)), "smm_mg_symm_sandwich")
+        return C_slab
+
+
+def lib_row_slabs(n: int, world: int, triangular: bool = False) -> List[int]:
+    """The library's own slab boundaries (smm_mg_row_slabs)."""
+    import ctypes
+    from . import _lib
+    b = (ctypes.c_int * (world + 1))()
+    _lib.check(_lib.load().smm_mg_row_slabs(n, world, 1 if triangular else 0, b), "smm_mg_row_slabs")
+    return list(b)
+
+
+def lib_chunks(k: int, world: int) -> List[int]:
+    """The K-chunk boundaries the library's broadcasts use (smm_mg_chunks)."""
+    import ctypes
+    from . import _lib
+    b = (ctypes.c_int * 17)()
+    nch = _lib.load().smm_mg_chunks(k, world, b)
+    if nch < 1:
+        _lib.check(nch if nch else 1, "smm_mg_chunks")
+    return list(b)[: nch + 1]

@@ -181,6 +181,69 @@ int smm_symm_sandwich(const float* A, const float* S_packed, const float* B, flo
 int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float* B, float* C, int N, int mode,
                               void* stream);
 
+/* ---- multi-GPU products (one process per GPU, NCCL over NVLink) ------- */
+
+/* A product C = X B is partitioned by output row slabs, one per rank (GPU).
+ * The shared right operand B lives on the root rank; inside each call it is
+ * broadcast in K-chunks (row chunks of B) on the communicator's
+ * high-priority stream, and this rank's slab is accumulated chunk by chunk
+ * on `stream` as the chunks land, so the transfer of chunk j+1 overlaps the
+ * tensor-core work on chunk j.  On every rank but the root, B is a device
+ * buffer of the same shape that receives it (16-byte aligned rows).  Calls
+ * are collective: every rank makes the same calls with the same shapes,
+ * mode and root, in the same order.  No kernel reads another GPU's memory.
+ * The reference has no multi-GPU code; this is the row-slab partition with a
+ * broadcast of the shared operand that its single-GPU kernels scale to.
+ * NCCL is loaded at run time (libnccl.so.2, the copy already in the process
+ * when there is one).  At world = 1 the calls compute without any
+ * collective. */
+#define SMM_MG_ID_BYTES 128
+typedef struct smm_mg_comm smm_mg_comm;
+
+/* NCCL unique id (SMM_MG_ID_BYTES bytes) made on one rank and handed to the
+ * others by any host means before smm_mg_comm_init. */
+int smm_mg_unique_id(void* id_out);
+/* Communicator of rank `rank` of `world` on the current device (collective:
+ * blocks until every rank has joined). */
+int smm_mg_comm_init(smm_mg_comm** comm, int rank, int world, const void* id);
+/* Waits for this rank's collectives, then frees the communicator. */
+int smm_mg_comm_destroy(smm_mg_comm* comm);
+/* Frees the communicator without waiting for peers (a failed or departed
+ * rank): pending collectives end with an error instead of blocking. */
+int smm_mg_comm_abort(smm_mg_comm* comm);
+/* SMM_ERR_NCCL if the communicator saw an asynchronous NCCL error. */
+int smm_mg_comm_status(smm_mg_comm* comm);
+
+/* Row-slab boundaries bounds[0] = 0 <= ... <= bounds[world] = N on 128-row
+ * tiles, minimising the largest slab's work: rows cost 1, or N - i for an
+ * upper-triangular left operand (triangular != 0). */
+int smm_mg_row_slabs(int N, int world, int triangular, int* bounds);
+/* K-chunk boundaries the calls use for a broadcast of K rows at this world
+ * size (bounds needs 17 ints); returns the chunk count. */
+int smm_mg_chunks(int K, int world, int* bounds);
+
+/* C_slab (nrows x N) = A_slab (nrows x K, this rank's rows of A) B (K x N). */
+size_t smm_mg_gemm_workspace_size(int nrows, int N, int K, int mode);
+int smm_mg_gemm(smm_mg_comm* comm, const float* A_slab, float* B, float* C_slab, int nrows, int N, int K, int mode,
+                int root, void* ws, size_t ws_bytes, void* stream);
+/* C_slab (nrows x ncols) = U[row0 : row0+nrows, :] B, U packed upper (the whole
+ * packed array on every rank; only the slab's rows are read).  B's chunks
+ * travel last rows first: a slab needs only B's rows from row0 on. */
+size_t smm_mg_upper_left_workspace_size(int N, int ncols, int row0, int nrows, int mode);
+int smm_mg_upper_left(smm_mg_comm* comm, const float* U_packed, float* B, float* C_slab, int N, int ncols, int row0,
+                      int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
+/* C_slab (nrows x ncols) = T[row0 : row0+nrows, :] B, T of generator g[2N-1]
+ * (on every rank). */
+size_t smm_mg_toeplitz_left_workspace_size(int N, int ncols, int mode);
+int smm_mg_toeplitz_left(smm_mg_comm* comm, const float* g, float* B, float* C_slab, int N, int ncols, int row0,
+                         int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
+/* C_slab (nrows x N) = (A_slab S) B, S packed symmetric and B broadcast from
+ * the root (S_packed and B are receive buffers on the other ranks): the
+ * reference's run_graph order, (A S) then times B, per row slab. */
+size_t smm_mg_symm_sandwich_workspace_size(int N, int nrows, int mode);
+int smm_mg_symm_sandwich(smm_mg_comm* comm, const float* A_slab, float* S_packed, float* B, float* C_slab, int N,
+                         int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
+
 /* ---- host-buffer contractions ------------------------------------------ */
 
 /* The contractions above with A, B, C (and U, S, g) in HOST memory: the

@@ -1,0 +1,148 @@
+"""libsmm's multi-GPU products on two GPUs (skipped with fewer).
+
+Two processes, one per GPU.  Rank 0 holds B (and S for the sandwich); the
+other rank starts with NaN-filled receive buffers, so a slab is right only if
+the K-chunked broadcast inside the call delivered every chunk before the
+contraction that consumes it.  Each rank checks its own output slab against
+an fp64 recomputation of the whole product (torch float64 on its GPU,
+test-only), within the mode's bound: 3xTF32 1e-5, TF32 5e-3, bf16 1e-2.
+Shapes cover equal-work triangular slabs with last-first chunk order, a
+ragged last chunk (K not a multiple of the chunk), a chunk count forced by
+SMM_MG_CHUNKS, and the sandwich's S broadcast.  NVLS is off (NCCL_NVLS_ENABLE=0)
+and every rank issues the same calls in the same order."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"3xtf32": 1e-5, "tf32": 5e-3, "bf16": 1e-2}
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _relerr(C, R):
+    return float(torch.linalg.vector_norm(C.double() - R) / torch.linalg.vector_norm(R))
+
+
+def _worker(rank, world, port, results):
+    import torch.distributed as dist
+
+    from cpp1_b200 import multigpu as MG
+    from cpp1_b200 import ops
+    from cpp1_b200 import workloads as W
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    comm = None
+    errs = {}
+    try:
+        comm = MG.Communicator(rank, world)
+
+        def dev(x):
+            return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+        def recv(x):  # B on the root, a NaN receive buffer elsewhere
+            t = dev(x)
+            if rank != 0:
+                t.fill_(float("nan"))
+            return t
+
+        for mode in ("3xtf32", "tf32", "bf16"):
+            # GEMM: A row slabs, B (K x N) broadcast
+            M, K, N = 2048, 2304, 1024
+            w = W.make_gemm(M, N, K, seed=31)
+            b = MG.lib_row_slabs(M, world)
+            r0, r1 = b[rank], b[rank + 1]
+            B = recv(w["B"])
+            C = torch.empty((r1 - r0, N), device="cuda")
+            comm.gemm(dev(w["A"][r0:r1]), B, C, mode=mode)
+            torch.cuda.synchronize()
+            R = dev(w["A"][r0:r1]).double() @ dev(w["B"]).double()
+            errs[f"gemm_{mode}"] = _relerr(C, R)
+
+            # U B, packed U on every rank, equal-work slabs, chunks last-first; N not a chunk multiple
+            for n, ncols in ((4096, 1024), (1000, 512)):
+                w = W.make_upper(n, ncols, seed=32)
+                b = MG.lib_row_slabs(n, world, triangular=True)
+                r0, r1 = b[rank], b[rank + 1]
+                B = recv(w["B"])
+                C = torch.empty((r1 - r0, ncols), device="cuda")
+                comm.upper_left(dev(w["U"]), B, C, r0, mode=mode)
+                torch.cuda.synchronize()
+                Ud = ops.unpack(dev(w["U"]), "upper", n).double()
+                R = Ud[r0:r1] @ dev(w["B"]).double()
+                errs[f"upper{n}_{mode}"] = _relerr(C, R)
+
+            # T B with 5 chunks forced
+            os.environ["SMM_MG_CHUNKS"] = "5"
+            n, ncols = 4096, 512
+            w = W.make_toeplitz(n, ncols, seed=33)
+            b = MG.lib_row_slabs(n, world)
+            r0, r1 = b[rank], b[rank + 1]
+            B = recv(w["B"])
+            C = torch.empty((r1 - r0, ncols), device="cuda")
+            comm.toeplitz_left(dev(w["g"]), B, C, r0, mode=mode)
+            torch.cuda.synchronize()
+            del os.environ["SMM_MG_CHUNKS"]
+            T = dev(W.toeplitz_dense(w["g"], n)).double()
+            errs[f"toeplitz_{mode}"] = _relerr(C, T[r0:r1] @ dev(w["B"]).double())
+
+            # A S B: A row slabs; S (packed) and B broadcast
+            n = 2048
+            w = W.make_sandwich(n, seed=34)
+            b = MG.lib_row_slabs(n, world)
+            r0, r1 = b[rank], b[rank + 1]
+            S, B = recv(w["S"]), recv(w["B"])
+            C = torch.empty((r1 - r0, n), device="cuda")
+            comm.symm_sandwich(dev(w["A"][r0:r1]), S, B, C, mode=mode)
+            torch.cuda.synchronize()
+            Sd = dev(W.unpack_symmetric(w["S"], n)).double()
+            R = (dev(w["A"][r0:r1]).double() @ Sd) @ dev(w["B"]).double()
+            errs[f"sandwich_{mode}"] = _relerr(C, R)
+        ops.device_status()
+        comm.status()
+        dist.barrier()
+        comm.close()
+        comm = None
+        results[rank] = errs
+    finally:
+        if comm is not None:
+            comm.abort()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_products_match_fp64(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    port = _free_port()
+    with mp.Manager() as m:
+        results = m.dict()
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(600)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        res = dict(results)
+    assert set(res) == {0, 1}
+    for rank, errs in res.items():
+        for key, e in errs.items():
+            mode = key.split("_")[-1]
+            assert e <= TOL[mode], (rank, key, e, errs)

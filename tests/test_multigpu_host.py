@@ -141,3 +141,20 @@ def test_two_rank_sandwich_slabs_gloo():
             p.join(120)
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         assert results["ok"], results
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_library_slabs_match_host_partition(world):
+    """libsmm's smm_mg_row_slabs and the host restatement agree."""
+    for n in (0, 1, 100, 1024, 4096, 8192, 16384, 1000):
+        for tri in (False, True):
+            assert MG.lib_row_slabs(n, world, tri) == MG.row_slabs(n, world, tri), (n, world, tri)
+
+
+@pytest.mark.parametrize("k,world", [(8192, 8), (16384, 8), (4096, 2), (1000, 2), (300, 4), (8192, 1)])
+def test_library_k_chunks(k, world):
+    kb = MG.lib_chunks(k, world)
+    assert kb[0] == 0 and kb[-1] == k
+    assert all(a < b for a, b in zip(kb, kb[1:]))
+    assert all(x % 256 == 0 for x in kb[:-1])  # k-block and TMA alignment in every mode
+    assert (len(kb) == 2) == (world == 1 or k <= 256)
