@@ -132,6 +132,16 @@ SIGNATURES = [
     ("smm_mg_symm_sandwich_workspace_size", _sz, [_i, _i, _i]),
     ("smm_mg_symm_sandwich", _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_debug_wait_limit_next", _i, [_ull]),
+    ("smm_gen_x_toeplitz_workspace_size", _sz, [_i, _i, _i, _i]),
+    ("smm_gen_x_toeplitz", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_gen_x_upper_host_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_gen_x_upper_host", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz]),
+    ("smm_gen_x_symm_host_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_gen_x_symm_host", _i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz]),
+    ("smm_gen_x_toeplitz_host_workspace_size", _sz, [_i, _i, _i, _i]),
+    ("smm_gen_x_toeplitz_host", _i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz]),
+    ("smm_diag_cols_host_workspace_size", _sz, [_i, _i]),
+    ("smm_diag_cols_host", _i, [_vp, _vp, _vp, _i, _i, _vp, _sz]),
 ]
 
 _lib = None

@@ -80,6 +80,10 @@ size_t expanded_bytes(int rows, int n, int mode);
 // or _SYMM) as a dense copy (fp32, or bf16 in bf16 mode) at ws_cur.
 int expand_operand(const float* P, int sf, int n, int row0, int rows, int mode, uint8_t*& ws_cur, Staged* out,
                    cudaStream_t st);
+// Bytes of, and the dense copy of, the K x N Toeplitz matrix of generator g
+// (K + N - 1 floats; T[k][n] = g[(K-1) + (n-k)]), fp32 or bf16 by mode.
+size_t toeplitz_expanded_bytes(int K, int N, int mode);
+int expand_toeplitz(const float* g, int K, int N, int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st);
 // Whether to expand a packed operand: the workspace holds need_expanded
 // bytes and SMM_EXPAND is not 0.
 bool expand_packed(void* ws, size_t ws_bytes, size_t need_expanded);

@@ -143,12 +143,9 @@ extern "C" int smm_diag_rows(const float* d, const float* B, float* C, int M, in
   return launch_rows(d, B, C, M, N, as_stream(stream));
 }
 
-extern "C" int smm_diag_cols(const float* A, const float* b, float* C, int M, int N, void* stream) {
-  SMM_RANGE("smm_diag_cols");
-  if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "smm_diag_cols: negative shape %d x %d", M, N);
-  if (M == 0 || N == 0) return SMM_OK;
-  if (!A || !b || !C) return set_error(SMM_ERR_INVALID, "smm_diag_cols: null pointer");
-  cudaStream_t st = as_stream(stream);
+namespace smm {
+namespace {
+int launch_cols(const float* A, const float* b, float* C, int M, int N, cudaStream_t st) {
   const bool vec = (N % 4 == 0) && aligned16(A) && aligned16(b) && aligned16(C);
   const int cols = vec ? N / 4 : N;
   const int segs = (cols + kSegVec - 1) / kSegVec;
@@ -162,6 +159,16 @@ extern "C" int smm_diag_cols(const float* A, const float* b, float* C, int M, in
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "diag_cols launch");
   return SMM_OK;
+}
+}  // namespace
+}  // namespace smm
+
+extern "C" int smm_diag_cols(const float* A, const float* b, float* C, int M, int N, void* stream) {
+  SMM_RANGE("smm_diag_cols");
+  if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "smm_diag_cols: negative shape %d x %d", M, N);
+  if (M == 0 || N == 0) return SMM_OK;
+  if (!A || !b || !C) return set_error(SMM_ERR_INVALID, "smm_diag_cols: null pointer");
+  return launch_cols(A, b, C, M, N, as_stream(stream));
 }
 
 // ---------------------------------------------------------------- host-buffer path
@@ -188,25 +195,28 @@ size_t chunk_rows(int M, int N) {
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 }  // namespace
 
-extern "C" size_t smm_diag_rows_host_workspace_size(int M, int N) {
+namespace {
+// Host-buffer scale, rows (C = diag(d) B, d has M entries) or columns
+// (C = A diag(b), b has N entries): the vector is copied once, then the
+// matrix goes through in row chunks alternating between two streams.
+size_t diag_host_ws(int M, int N, bool cols) {
   if (M <= 0 || N <= 0) return 0;
   const size_t rows = chunk_rows(M, N);
   const size_t chunk = round256(rows * static_cast<size_t>(N) * sizeof(float));
-  return round256(static_cast<size_t>(M) * sizeof(float)) + 4 * chunk;  // d + 2 x (B chunk, C chunk)
+  return round256(static_cast<size_t>(cols ? N : M) * sizeof(float)) + 4 * chunk;  // vector + 2 x (in, out)
 }
 
-extern "C" int smm_diag_rows_host(const float* d_host, const float* B_host, float* C_host, int M, int N,
-                                  void* dev_ws, size_t ws_bytes) {
-  SMM_RANGE("smm_diag_rows_host");
-  if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "smm_diag_rows_host: negative shape");
+int diag_host(const char* who, bool cols, const float* v_host, const float* X_host, float* C_host, int M, int N,
+              void* dev_ws, size_t ws_bytes) {
+  if (M < 0 || N < 0) return set_error(SMM_ERR_INVALID, "%s: negative shape", who);
   if (M == 0 || N == 0) return SMM_OK;
-  if (!d_host || !B_host || !C_host) return set_error(SMM_ERR_INVALID, "smm_diag_rows_host: null pointer");
-  const size_t need = smm_diag_rows_host_workspace_size(M, N);
+  if (!v_host || !X_host || !C_host) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
+  const size_t need = diag_host_ws(M, N, cols);
   if (!dev_ws || ws_bytes < need)
-    return set_error(SMM_ERR_WORKSPACE, "smm_diag_rows_host: workspace %zu bytes < %zu required", ws_bytes, need);
+    return set_error(SMM_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu required", who, ws_bytes, need);
   int dev = 0;
   SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return set_error(SMM_ERR_UNSUPPORTED, "smm_diag_rows_host: device index %d >= 64", dev);
+  if (dev < 0 || dev >= 64) return set_error(SMM_ERR_UNSUPPORTED, "%s: device index %d >= 64", who, dev);
   HostPipe& hp = host_pipe(dev);
   {
     // first call on this device: create its streams (once, even when several
@@ -221,13 +231,15 @@ extern "C" int smm_diag_rows_host(const float* d_host, const float* B_host, floa
   }
   const size_t rows = chunk_rows(M, N);
   const size_t chunk = round256(rows * static_cast<size_t>(N) * sizeof(float));
+  const size_t vlen = static_cast<size_t>(cols ? N : M);
   uint8_t* ws = static_cast<uint8_t*>(dev_ws);
-  float* d_dev = reinterpret_cast<float*>(ws);
-  uint8_t* bufs = ws + round256(static_cast<size_t>(M) * sizeof(float));
+  float* v_dev = reinterpret_cast<float*>(ws);
+  uint8_t* bufs = ws + round256(vlen * sizeof(float));
   float* bin[2] = {reinterpret_cast<float*>(bufs), reinterpret_cast<float*>(bufs + chunk)};
   float* cout[2] = {reinterpret_cast<float*>(bufs + 2 * chunk), reinterpret_cast<float*>(bufs + 3 * chunk)};
 
-  SMM_CUDA_TRY(cudaMemcpyAsync(d_dev, d_host, sizeof(float) * M, cudaMemcpyHostToDevice, hp.st[0]), "copy d");
+  SMM_CUDA_TRY(cudaMemcpyAsync(v_dev, v_host, sizeof(float) * vlen, cudaMemcpyHostToDevice, hp.st[0]),
+               "copy scale vector");
   SMM_CUDA_TRY(cudaEventRecord(hp.d_ready, hp.st[0]), "event record");
   SMM_CUDA_TRY(cudaStreamWaitEvent(hp.st[1], hp.d_ready, 0), "stream wait");
   // Chunk c alternates between the two streams; within a stream the copy-in,
@@ -240,11 +252,30 @@ extern "C" int smm_diag_rows_host(const float* d_host, const float* B_host, floa
     const size_t nr = std::min(rows, static_cast<size_t>(M) - r0);
     const size_t off = r0 * static_cast<size_t>(N);
     const size_t bytes = nr * static_cast<size_t>(N) * sizeof(float);
-    SMM_CUDA_TRY(cudaMemcpyAsync(bin[k], B_host + off, bytes, cudaMemcpyHostToDevice, hp.st[k]), "copy B chunk");
-    if (int rc = launch_rows(d_dev + r0, bin[k], cout[k], static_cast<int>(nr), N, hp.st[k])) return rc;
-    SMM_CUDA_TRY(cudaMemcpyAsync(C_host + off, cout[k], bytes, cudaMemcpyDeviceToHost, hp.st[k]), "copy C chunk");
+    SMM_CUDA_TRY(cudaMemcpyAsync(bin[k], X_host + off, bytes, cudaMemcpyHostToDevice, hp.st[k]), "copy chunk in");
+    const int rc = cols ? launch_cols(bin[k], v_dev, cout[k], static_cast<int>(nr), N, hp.st[k])
+                        : launch_rows(v_dev + r0, bin[k], cout[k], static_cast<int>(nr), N, hp.st[k]);
+    if (rc) return rc;
+    SMM_CUDA_TRY(cudaMemcpyAsync(C_host + off, cout[k], bytes, cudaMemcpyDeviceToHost, hp.st[k]), "copy chunk out");
   }
   for (auto& s : hp.st) SMM_CUDA_TRY(cudaStreamSynchronize(s), "stream sync");
   clear_error();
   return SMM_OK;
+}
+}  // namespace
+
+extern "C" size_t smm_diag_rows_host_workspace_size(int M, int N) { return diag_host_ws(M, N, false); }
+
+extern "C" int smm_diag_rows_host(const float* d_host, const float* B_host, float* C_host, int M, int N,
+                                  void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_diag_rows_host");
+  return diag_host("smm_diag_rows_host", false, d_host, B_host, C_host, M, N, dev_ws, ws_bytes);
+}
+
+extern "C" size_t smm_diag_cols_host_workspace_size(int M, int N) { return diag_host_ws(M, N, true); }
+
+extern "C" int smm_diag_cols_host(const float* A_host, const float* b_host, float* C_host, int M, int N,
+                                  void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_diag_cols_host");
+  return diag_host("smm_diag_cols_host", true, b_host, A_host, C_host, M, N, dev_ws, ws_bytes);
 }

@@ -195,10 +195,133 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
   return smm_device_status(s0);
 }
 
+// ---------------------------------------------------------------- right-side structured operand
+// C (M x N) = A (M x K) X (K x N) with X structured (packed upper or
+// symmetric, K = N; or a K + N - 1 Toeplitz generator): the orientation of
+// the reference's CPU kernels (upper_triag_matmul.cpp:41-137 A*U,
+// symmetric_matmul.cpp:84-211 A*S, toeplitz_matmul2.cpp:44-144 A*T).  X
+// crosses PCIe once and is expanded into a dense copy on stream 0; A goes
+// through in row chunks (contiguous in host memory) alternating between the
+// two streams, each chunk's copy-in, product and copy-out ordered on its
+// stream and overlapping the other stream's.
+enum class HostRight { Upper, Symm, Toeplitz };
+
+int host_row_chunk(int M) { return std::min(M, std::max(1024, (M / 8 + 255) / 256 * 256)); }
+
+size_t right_raw_bytes(HostRight k, int N, int K) {
+  return k == HostRight::Toeplitz ? round256((static_cast<size_t>(K) + N - 1) * 4)
+                                  : round256(static_cast<size_t>(K) * (K + 1) / 2 * 4);
+}
+size_t right_chunk_bytes(int M, int N, int K, int mode) {
+  const int h = host_row_chunk(M);
+  return round256(static_cast<size_t>(h) * K * 4) + staged_bytes_bound(h, K, mode) +
+         round256(static_cast<size_t>(h) * N * 4);
+}
+size_t host_right_ws(HostRight k, int M, int N, int K, int mode) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return right_raw_bytes(k, N, K) + toeplitz_expanded_bytes(K, N, mode) + 2 * right_chunk_bytes(M, N, K, mode);
+}
+
+int host_right_product(const char* who, HostRight kind, int M, int N, int K, int mode, const float* A,
+                       const float* X, float* C, void* dev_ws, size_t ws_bytes) {
+  if (M < 0 || N < 0 || K < 0) return set_error(SMM_ERR_INVALID, "%s: negative shape", who);
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
+  if (kind != HostRight::Toeplitz && K != N) return set_error(SMM_ERR_INVALID, "%s: K must equal N", who);
+  if (M == 0 || N == 0) return SMM_OK;
+  if (!A || !X || !C) return set_error(SMM_ERR_INVALID, "%s: null pointer", who);
+  if (kind != HostRight::Toeplitz)
+    if (int rc = check_packed(who, N)) return rc;
+  if (K == 0) {
+    std::memset(C, 0, sizeof(float) * static_cast<size_t>(M) * N);
+    return SMM_OK;
+  }
+  if (int rc = check_ws(who, dev_ws, ws_bytes, host_right_ws(kind, M, N, K, mode))) return rc;
+  HostStreams* hs = nullptr;
+  if (int rc = host_streams(&hs)) return rc;
+  cudaStream_t s0 = hs->st[0];
+
+  // ---- X: copy in once, expand on stream 0
+  uint8_t* cur = static_cast<uint8_t*>(dev_ws);
+  const size_t xlen = kind == HostRight::Toeplitz ? static_cast<size_t>(K) + N - 1 : static_cast<size_t>(K) * (K + 1) / 2;
+  float* xraw = reinterpret_cast<float*>(cur);
+  cur += right_raw_bytes(kind, N, K);
+  SMM_CUDA_TRY(cudaMemcpyAsync(xraw, X, xlen * 4, cudaMemcpyHostToDevice, s0), "copy structured operand");
+  Staged ex;  // the dense K x N copy (the packed expansions with K = N have the same size)
+  uint8_t* xcur = cur;
+  cur += toeplitz_expanded_bytes(K, N, mode);
+  if (kind == HostRight::Toeplitz) {
+    if (int rc = expand_toeplitz(xraw, K, N, mode, xcur, &ex, s0)) return rc;
+  } else {
+    if (int rc = expand_operand(xraw, kind == HostRight::Upper ? SMM_STRUCT_UPPER : SMM_STRUCT_SYMM, N, 0, N, mode,
+                                xcur, &ex, s0))
+      return rc;
+  }
+  Operand xop = dense_op(ex.ptr, nullptr, ex.ld, ex.bf16);
+  if (kind == HostRight::Upper) xop.tri = 1;  // K range clipped per column tile
+  SMM_CUDA_TRY(cudaEventRecord(hs->left_ready, s0), "event record");
+  SMM_CUDA_TRY(cudaStreamWaitEvent(hs->st[1], hs->left_ready, 0), "stream wait");
+
+  // ---- A in row chunks, alternating streams
+  const int h = host_row_chunk(M);
+  uint8_t* region[2] = {cur, cur + right_chunk_bytes(M, N, K, mode)};
+  int c = 0;
+  for (int r0 = 0; r0 < M; r0 += h, ++c) {
+    const int k = c & 1;
+    const int rows = std::min(h, M - r0);
+    cudaStream_t st = hs->st[k];
+    uint8_t* r = region[k];
+    float* araw = reinterpret_cast<float*>(r);
+    r += round256(static_cast<size_t>(h) * K * 4);
+    uint8_t* stage_cur = r;
+    r += staged_bytes_bound(h, K, mode);
+    float* cch = reinterpret_cast<float*>(r);
+    SMM_CUDA_TRY(cudaMemcpyAsync(araw, A + static_cast<size_t>(r0) * K, static_cast<size_t>(rows) * K * 4,
+                                 cudaMemcpyHostToDevice, st),
+                 "copy A chunk");
+    Staged as;
+    if (int rc = stage_operand(araw, rows, K, mode, stage_cur, &as, st)) return rc;
+    if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(as.ptr, as.lo, as.ld, as.bf16), xop, cch,
+                                 N, rows, N, K, st))
+      return rc;
+    SMM_CUDA_TRY(cudaMemcpyAsync(C + static_cast<size_t>(r0) * N, cch, static_cast<size_t>(rows) * N * 4,
+                                 cudaMemcpyDeviceToHost, st),
+                 "copy C chunk");
+  }
+  SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[1]), "stream sync");
+  return smm_device_status(s0);
+}
+
 }  // namespace
 }  // namespace smm
 
 using namespace smm;
+
+extern "C" size_t smm_gen_x_upper_host_workspace_size(int M, int N, int mode) {
+  return host_right_ws(HostRight::Upper, M, N, N, mode);
+}
+extern "C" int smm_gen_x_upper_host(const float* A, const float* U_packed, float* C, int M, int N, int mode,
+                                    void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_gen_x_upper_host");
+  return host_right_product("smm_gen_x_upper_host", HostRight::Upper, M, N, N, mode, A, U_packed, C, dev_ws,
+                            ws_bytes);
+}
+extern "C" size_t smm_gen_x_symm_host_workspace_size(int M, int N, int mode) {
+  return host_right_ws(HostRight::Symm, M, N, N, mode);
+}
+extern "C" int smm_gen_x_symm_host(const float* A, const float* S_packed, float* C, int M, int N, int mode,
+                                   void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_gen_x_symm_host");
+  return host_right_product("smm_gen_x_symm_host", HostRight::Symm, M, N, N, mode, A, S_packed, C, dev_ws, ws_bytes);
+}
+extern "C" size_t smm_gen_x_toeplitz_host_workspace_size(int M, int N, int K, int mode) {
+  return host_right_ws(HostRight::Toeplitz, M, N, K, mode);
+}
+extern "C" int smm_gen_x_toeplitz_host(const float* A, const float* g, float* C, int M, int N, int K, int mode,
+                                       void* dev_ws, size_t ws_bytes) {
+  SMM_RANGE("smm_gen_x_toeplitz_host");
+  return host_right_product("smm_gen_x_toeplitz_host", HostRight::Toeplitz, M, N, K, mode, A, g, C, dev_ws,
+                            ws_bytes);
+}
 
 extern "C" size_t smm_gemm_host_workspace_size(int M, int N, int K, int mode) {
   return host_ws_bytes({HostLeft::Gemm, M, N, K, mode});

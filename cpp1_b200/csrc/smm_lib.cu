@@ -537,6 +537,40 @@ extern "C" int smm_gen_x_lower(const float* A, const float* Lp, float* C, int M,
   return gen_x_struct("smm_gen_x_lower", BKind::LowerPacked, A, Lp, C, M, N, mode, ws, ws_bytes, as_stream(stream));
 }
 
+extern "C" size_t smm_gen_x_toeplitz_workspace_size(int M, int N, int K, int mode) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return staged_bytes_bound(M, K, mode) + toeplitz_expanded_bytes(K, N, mode);
+}
+
+extern "C" int smm_gen_x_toeplitz(const float* A, const float* g, float* C, int M, int N, int K, int mode, void* ws,
+                                  size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_gen_x_toeplitz");
+  if (M < 0 || N < 0 || K < 0) return set_error(SMM_ERR_INVALID, "smm_gen_x_toeplitz: negative shape");
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_gen_x_toeplitz: unknown mode %d", mode);
+  if (M == 0 || N == 0) return SMM_OK;
+  if (!C || (K > 0 && (!A || !g))) return set_error(SMM_ERR_INVALID, "smm_gen_x_toeplitz: null pointer");
+  cudaStream_t st = as_stream(stream);
+  if (K == 0) return zero_output(C, M, N, st);
+  // The Toeplitz right operand is expanded into a dense K x N copy (TMA-fed)
+  // when the workspace has room for it, else built on chip from the
+  // generator by the transform warps.
+  const size_t need_a = staged_bytes(A, M, K, mode);
+  const bool expand = expand_packed(ws, ws_bytes, need_a + toeplitz_expanded_bytes(K, N, mode));
+  if (int rc = check_ws("smm_gen_x_toeplitz", ws, ws_bytes, need_a + (expand ? toeplitz_expanded_bytes(K, N, mode) : 0)))
+    return rc;
+  uint8_t* cur = static_cast<uint8_t*>(ws);
+  Staged a;
+  if (int rc = stage_operand(A, M, K, mode, cur, &a, st)) return rc;
+  const Operand ao = dense_op(a.ptr, a.lo, a.ld, a.bf16);
+  if (expand) {
+    Staged t;
+    if (int rc = expand_toeplitz(g, K, N, mode, cur, &t, st)) return rc;
+    return run_contraction(AKind::Dense, BKind::Dense, mode, ao, dense_op(t.ptr, nullptr, t.ld, t.bf16), C, N, M, N,
+                           K, st);
+  }
+  return run_contraction(AKind::Dense, BKind::Toeplitz, mode, ao, structured_op(g, K), C, N, M, N, K, st);
+}
+
 extern "C" int smm_symm_x_symm(const float* S1, const float* S2, float* C, int N, int mode, void* stream) {
   SMM_RANGE("smm_symm_x_symm");
   return smm_symm_x_symm_ws(S1, S2, C, N, mode, nullptr, 0, stream);

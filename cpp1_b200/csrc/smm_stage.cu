@@ -121,6 +121,23 @@ __global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P
   }
 }
 
+// Dense copy of the K x N Toeplitz matrix of generator g (K + N - 1 floats),
+// T[k][n] = g[(K-1) + (n-k)]: row k is the window g[K-1-k ..].  Threads write
+// column pairs of a row (coalesced window reads and row writes); blocks run
+// along a row (x) and stride over rows (y).  Columns N .. ld-1 are zero.
+template <typename T>
+__global__ void __launch_bounds__(256) toeplitz_expand_kernel(const float* __restrict__ g, int K, int N,
+                                                              T* __restrict__ dst, int ld) {
+  const int j = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (j >= ld) return;
+  for (int k = blockIdx.y; k < K; k += gridDim.y) {
+    const float* w = g + (K - 1 - k);
+    const float a = j < N ? __ldg(w + j) : 0.0f;
+    const float b = j + 1 < N ? __ldg(w + j + 1) : 0.0f;
+    store_pair(dst + static_cast<long long>(k) * ld + j, a, b);
+  }
+}
+
 template <typename T>
 void launch_expand(const float* P, int sf, int n, int row0, int rows, T* dst, int ld, cudaStream_t st) {
   const dim3 grid((ld + 63) / 64, (rows + 63) / 64);
@@ -203,6 +220,29 @@ int expand_operand(const float* P, int sf, int n, int row0, int rows, int mode, 
   ws_cur += expanded_bytes(rows, n, mode);
   count_launch();
   SMM_CUDA_TRY(cudaGetLastError(), "packed operand expansion launch");
+  return SMM_OK;
+}
+
+size_t toeplitz_expanded_bytes(int K, int N, int mode) {
+  return mode == SMM_MODE_BF16 ? bf16_plane_bytes(K, N) : plane_bytes(K, N);
+}
+int expand_toeplitz(const float* g, int K, int N, int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st) {
+  const bool bf = mode == SMM_MODE_BF16;
+  const int ld = bf ? round8(N) : round4(N);
+  const int gx = (ld / 2 + 255) / 256;
+  const int gy = std::max(1, std::min(K, std::max(1, 148 * 16 / gx)));
+  if (bf) {
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
+    toeplitz_expand_kernel<__nv_bfloat16><<<dim3(gx, gy), 256, 0, st>>>(g, K, N, dst, ld);
+    *out = {nullptr, nullptr, ld, dst};
+  } else {
+    float* dst = reinterpret_cast<float*>(ws_cur);
+    toeplitz_expand_kernel<float><<<dim3(gx, gy), 256, 0, st>>>(g, K, N, dst, ld);
+    *out = {dst, nullptr, ld};
+  }
+  ws_cur += toeplitz_expanded_bytes(K, N, mode);
+  count_launch();
+  SMM_CUDA_TRY(cudaGetLastError(), "Toeplitz expansion launch");
   return SMM_OK;
 }
 

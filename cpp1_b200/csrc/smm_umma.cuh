@@ -29,6 +29,8 @@
 //     BKind::UpperPacked/SymmPacked/LowerPacked  built on chip (the DSL's
 //                                 Gen@Upper, Gen@Symm, Symm@Symm, Gen@Lower,
 //                                 Lower@Lower)
+//     BKind::Toeplitz             built on chip from a K + N - 1 generator
+//                                 (Gen@Toeplitz without room for a dense copy)
 //
 // 3xTF32 (SPLIT3): three MMAs per k-step, hi*hi + hi*lo + lo*hi.  The tensor
 // core's fp32 accumulation truncates on every update, so with same-sign data
@@ -63,7 +65,7 @@ namespace smm {
 enum class AKind : int { Dense = 0, UpperPacked = 1, Toeplitz = 2, SymmPacked = 3, UpperDense = 4, LowerPacked = 5 };
 // Right operand: a dense row-major matrix loaded by TMA, or a packed
 // upper-triangular / symmetric matrix built on chip by the transform warps.
-enum class BKind : int { Dense = 0, UpperPacked = 1, SymmPacked = 2, LowerPacked = 3 };
+enum class BKind : int { Dense = 0, UpperPacked = 1, SymmPacked = 2, LowerPacked = 3, Toeplitz = 4 };
 
 // Arithmetic of the contraction (values match smm_mode).
 enum class Mode : int { TF32x3 = 0, TF32 = 1, BF16 = 2 };
@@ -520,7 +522,12 @@ __device__ __forceinline__ void b_build(const UmmaParams& p, uint8_t* bh, uint8_
     for (int e = 0; e < kBatch; ++e) {
       int kr, n;
       b_coord<BN, KS>(mirror, t, b0 + e, kr, n);
-      v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
+      if constexpr (BK == BKind::Toeplitz) {  // K x N Toeplitz of generator b_src: T[k][n] = g[(K-1) + (n-k)]
+        const int k = k0 + kr, nn = n0 + n;
+        v[e] = (k < p.K && nn < p.N) ? __ldg(p.b_src + (p.K - 1 + nn - k)) : 0.0f;
+      } else {
+        v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
+      }
     }
 #pragma unroll
     for (int e = 0; e < kBatch; ++e) {

@@ -116,6 +116,11 @@ def _lower(lk: str, rk: str):
     if (lk, rk) == ("gen", "upper"):
         return (lambda a, u, M, N, K, mode, out: ops.gen_x_upper(a.view(M, K), u, mode=mode, out=out),
                 lambda M, N, K: 2.0 * M * N * K)
+    if (lk, rk) == ("gen", "toeplitz"):
+        # the reference's own Toeplitz orientation (Cuda kernels/toeplitz.cu:76-253),
+        # which its DSL CUDA backend does not lower (codegen_cuda.py:1681-1682)
+        return (lambda a, g, M, N, K, mode, out: ops.gen_x_toeplitz(a.view(M, K), g, N, mode=mode, out=out),
+                lambda M, N, K: 2.0 * M * N * K)
     if (lk, rk) == ("symm", "symm"):
         return (lambda s1, s2, M, N, K, mode, out: ops.symm_x_symm(s1, s2, mode=mode, out=out),
                 lambda M, N, K: 2.0 * M * N * K)
@@ -257,10 +262,14 @@ def _sandwich_parts(node):
 
 
 def run_graph(outs, inputs, backend="cuda", **kwargs):
-    """Execute a multi-operation expression.  A @ S @ B runs as one fused
-    sandwich call; anything else runs operation by operation in post-order,
-    each intermediate stored in ``inputs`` under its operation name, like the
-    reference (src/dsl/runner_cuda.py:147-197)."""
+    """Execute a multi-operation expression, returning every operation's
+    tensor under its name, like the reference (src/dsl/runner_cuda.py:147-197).
+    A @ S @ B (S symmetric, A and B general) runs as the library's two
+    structured products in the expression's own association: (A @ S) @ B as
+    Gen@Symm then a GEMM, A @ (S @ B) as Symm@Gen then a GEMM, the symmetric
+    operand expanded from its packed storage on the device, the intermediate
+    returned under its name too.  Anything else runs operation by operation
+    in post-order, each intermediate stored in ``inputs`` under its name."""
     mode = kwargs.get("mode", "3xtf32")
     if len(outs) == 1:
         parts = _sandwich_parts(outs[0])
@@ -271,9 +280,20 @@ def run_graph(outs, inputs, backend="cuda", **kwargs):
                 A = _device_tensor(inputs[a.name]).view(n, n)
                 S = _device_tensor(inputs[s.name])
                 B = _device_tensor(inputs[b.name]).view(n, n)
+                root = outs[0]
+                inner = root.operands[0] if isinstance(root.operands[0], Operation) else root.operands[1]
+                mid = torch.zeros(n * n, dtype=torch.float32, device=A.device)
                 out = torch.zeros(n * n, dtype=torch.float32, device=A.device)
-                _, ms = _timed(lambda: ops.symm_sandwich(A, S, B, mode=mode, out=out.view(n, n)))
-                return {outs[0].name: out}, ms, 0.0
+
+                def both():
+                    if inner is root.operands[0]:  # (A @ S) @ B
+                        ops.gen_x_symm(A, S, mode=mode, out=mid.view(n, n))
+                        ops.gemm(mid.view(n, n), B, mode=mode, out=out.view(n, n))
+                    else:  # A @ (S @ B)
+                        ops.symm_left(S, B, mode=mode, out=mid.view(n, n))
+                        ops.gemm(A, mid.view(n, n), mode=mode, out=out.view(n, n))
+                _, ms = _timed(both)
+                return {inner.name: mid, root.name: out}, ms, 0.0
 
     schedule, visited = [], set()
     for o in outs:

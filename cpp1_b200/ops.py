@@ -206,6 +206,23 @@ def gen_x_lower(A: torch.Tensor, Lp: torch.Tensor, mode: str = "3xtf32", out: Op
     return _gen_x_struct("smm_gen_x_lower", A, Lp, mode, out, stream)
 
 
+def gen_x_toeplitz(A: torch.Tensor, g: torch.Tensor, N: Optional[int] = None, mode: str = "3xtf32",
+                   out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """C = A @ T with T (K x N) the Toeplitz matrix of generator g (K + N - 1),
+    T[k][n] = g[(K-1) + (n-k)]; N defaults to K (square T, 2K - 1 generator)."""
+    A = _check_f32("A", A)
+    M, K = A.shape
+    N = K if N is None else N
+    g = _check_f32("g", g, K + N - 1)
+    m = _mode(mode)
+    L = _lib.load()
+    ws, wsb = _ws_args(L.smm_gen_x_toeplitz_workspace_size(M, N, K, m), A.device)
+    C = _out(out, (M, N), A)
+    _lib.check(L.smm_gen_x_toeplitz(_ptr(A), _ptr(g), _ptr(C), M, N, K, m, ws, wsb, _stream_ptr(stream)),
+               "smm_gen_x_toeplitz")
+    return C
+
+
 def _packed_order(name: str, t: torch.Tensor) -> int:
     p = t.numel()
     N = int((-1 + (1 + 8 * p) ** 0.5) // 2)
@@ -358,7 +375,7 @@ def _check_host(name: str, t: torch.Tensor, numel: Optional[int] = None) -> torc
 
 
 def host_product(op: str, *inputs: torch.Tensor, mode: str = "3xtf32",
-                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 out: Optional[torch.Tensor] = None, toeplitz_cols: Optional[int] = None) -> torch.Tensor:
     """C = the product ``op`` of HOST tensors through the smm_*_host entry
     points: the left operand(s) cross PCIe once, B streams through in column
     chunks whose copies overlap the products (pinned tensors overlap; pageable
@@ -366,8 +383,12 @@ def host_product(op: str, *inputs: torch.Tensor, mode: str = "3xtf32",
     ``out`` is given).
 
     op: "gemm" (A, B), "upper" (U_packed, B), "symm" (S_packed, B),
-    "toeplitz" (g, B), "sandwich" (A, S_packed, B)."""
-    arity = {"gemm": 2, "upper": 2, "symm": 2, "toeplitz": 2, "sandwich": 3}
+    "toeplitz" (g, B), "sandwich" (A, S_packed, B); the right-side
+    orientation of the reference's CPU drivers: "gen_x_upper" (A, U_packed),
+    "gen_x_symm" (A, S_packed), "gen_x_toeplitz" (A, g; T square unless
+    ``toeplitz_cols`` is given), "diag_cols" (A, b)."""
+    arity = {"gemm": 2, "upper": 2, "symm": 2, "toeplitz": 2, "sandwich": 3, "gen_x_upper": 2, "gen_x_symm": 2,
+             "gen_x_toeplitz": 2, "diag_cols": 2}
     if op not in arity:
         raise ValueError(f"unknown host product {op!r}; expected one of {sorted(arity)}")
     if len(inputs) != arity[op]:
@@ -401,6 +422,30 @@ def host_product(op: str, *inputs: torch.Tensor, mode: str = "3xtf32",
         size = L.smm_symm_sandwich_host_workspace_size(N, m)
         call = lambda C, ws, wsb: L.smm_symm_sandwich_host(A.data_ptr(), S.data_ptr(), B.data_ptr(), C.data_ptr(),
                                                            N, m, ws, wsb)
+    elif op in ("gen_x_upper", "gen_x_symm"):
+        A = _check_host("A", inputs[0])
+        M, N = A.shape
+        X = _check_host("right operand", inputs[1], N * (N + 1) // 2)
+        shape = (M, N)
+        size = getattr(L, f"smm_{op}_host_workspace_size")(M, N, m)
+        fn = getattr(L, f"smm_{op}_host")
+        call = lambda C, ws, wsb: fn(A.data_ptr(), X.data_ptr(), C.data_ptr(), M, N, m, ws, wsb)
+    elif op == "gen_x_toeplitz":
+        A = _check_host("A", inputs[0])
+        M, K = A.shape
+        N = K if toeplitz_cols is None else toeplitz_cols
+        g = _check_host("g", inputs[1], K + N - 1)
+        shape = (M, N)
+        size = L.smm_gen_x_toeplitz_host_workspace_size(M, N, K, m)
+        call = lambda C, ws, wsb: L.smm_gen_x_toeplitz_host(A.data_ptr(), g.data_ptr(), C.data_ptr(), M, N, K, m,
+                                                            ws, wsb)
+    elif op == "diag_cols":
+        A = _check_host("A", inputs[0])
+        M, N = A.shape
+        b = _check_host("b", inputs[1], N)
+        shape = (M, N)
+        size = L.smm_diag_cols_host_workspace_size(M, N)
+        call = lambda C, ws, wsb: L.smm_diag_cols_host(A.data_ptr(), b.data_ptr(), C.data_ptr(), M, N, ws, wsb)
     if out is None:
         C = torch.empty(shape, dtype=torch.float32, pin_memory=True)
     else:

@@ -278,6 +278,32 @@ size_t smm_symm_sandwich_host_workspace_size(int N, int mode);
 int smm_symm_sandwich_host(const float* A, const float* S_packed, const float* B, float* C, int N, int mode,
                            void* dev_ws, size_t ws_bytes);
 
+/* The reference CPU drivers' own orientation with HOST arrays: C (M x N) =
+ * A (M x K) X, X packed upper (upper_triag_matmul.cpp:41-137), packed
+ * symmetric (symmetric_matmul.cpp:84-211) or a Toeplitz generator of K+N-1
+ * floats (toeplitz_matmul2.cpp:44-144); K = N for the packed ones.  X crosses
+ * PCIe once and is expanded on the device; A goes through in row chunks on
+ * two internal streams, each chunk's copy-in, product and copy-out
+ * overlapping the neighbouring chunks'.  Synchronous; workspace and stream
+ * rules as for the host-buffer entries above. */
+size_t smm_gen_x_upper_host_workspace_size(int M, int N, int mode);
+int smm_gen_x_upper_host(const float* A, const float* U_packed, float* C, int M, int N, int mode, void* dev_ws,
+                         size_t ws_bytes);
+size_t smm_gen_x_symm_host_workspace_size(int M, int N, int mode);
+int smm_gen_x_symm_host(const float* A, const float* S_packed, float* C, int M, int N, int mode, void* dev_ws,
+                        size_t ws_bytes);
+size_t smm_gen_x_toeplitz_host_workspace_size(int M, int N, int K, int mode);
+int smm_gen_x_toeplitz_host(const float* A, const float* g, float* C, int M, int N, int K, int mode, void* dev_ws,
+                            size_t ws_bytes);
+
+/* Column scale with HOST buffers, C = A diag(b) (diag_matmul.cpp:45-111
+ * optimized_compute, the reference driver's orientation): b is copied once,
+ * A and C go through in row chunks on two internal streams.  Synchronous,
+ * bit-exact; dev_ws must hold smm_diag_cols_host_workspace_size(M, N) bytes. */
+size_t smm_diag_cols_host_workspace_size(int M, int N);
+int smm_diag_cols_host(const float* A_host, const float* b_host, float* C_host, int M, int N, void* dev_ws,
+                       size_t ws_bytes);
+
 /* ---- structured right operand (the reference's own orientation) ------- */
 
 /* Workspace for smm_gen_x_upper / smm_gen_x_symm / smm_gen_x_lower: a padded
@@ -306,6 +332,17 @@ int smm_gen_x_symm(const float* A, const float* S_packed, float* C, int M, int N
  * diagonal are never visited.  Workspace: smm_gen_x_struct_workspace_size. */
 int smm_gen_x_lower(const float* A, const float* L_packed, float* C, int M, int N, int mode, void* ws,
                     size_t ws_bytes, void* stream);
+
+/* C(M x N) = A(M x K) T(K x N), T the Toeplitz matrix of generator
+ * g[K+N-1], T[k][n] = g[(K-1) + (n-k)]: the orientation of the reference's
+ * Toeplitz kernels, gemm_toeplitz_double_buffer (Cuda kernels/toeplitz.cu:
+ * 76-253, t_idx = (K-1)+(n-k) at :91) and compute_matrix_multi1
+ * (toeplitz_matmul2.cpp:44-144).  With smm_gen_x_toeplitz_workspace_size
+ * bytes T is expanded into a dense copy and read by TMA; with room for the
+ * staged A only, T is built on chip from the generator. */
+size_t smm_gen_x_toeplitz_workspace_size(int M, int N, int K, int mode);
+int smm_gen_x_toeplitz(const float* A, const float* g, float* C, int M, int N, int K, int mode, void* ws,
+                       size_t ws_bytes, void* stream);
 
 /* C(N x N) = S1 S2, both packed upper symmetric.  Replaces kernel_symm_x_symm
  * (src/dsl/codegen_cuda.py:1340-1613).  No workspace: both operands are built

@@ -124,7 +124,8 @@ def outputs() -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("CPP1_REFERENCE", "/root/reference"),
+                    help="reference checkout (default: $CPP1_REFERENCE, else this container's mount point)")
     args = ap.parse_args()
     O.build(with_reference=True)
     if not O.ref_available():

@@ -109,6 +109,7 @@ def recorder(monkeypatch):
     (GeneralMatrix, LowerTriangularMatrix, "gen_x_lower"),
     (LowerTriangularMatrix, GeneralMatrix, "lower_left"),
     (LowerTriangularMatrix, LowerTriangularMatrix, "lower_x_lower"),
+    (GeneralMatrix, ToeplitzMatrix, "gen_x_toeplitz"),
 ])
 def test_lowering_table(recorder, lhs, rhs, entry):
     n = Var("n")
@@ -140,14 +141,24 @@ def test_non_cuda_backend_rejected(recorder):
                backend="numpy")
 
 
-def test_run_graph_fuses_sandwich(recorder):
+def test_run_graph_sandwich_returns_every_operation(recorder):
+    """A @ S @ B runs as the library's structured products in the
+    expression's association and returns the intermediate under its name too,
+    as the reference's run_graph does (src/dsl/runner_cuda.py:147-197)."""
     n = Var("n")
     A, S, B = GeneralMatrix((n, n), "A"), SymmetricMatrix((n, n), "S"), GeneralMatrix((n, n), "B")
-    expr = A @ S @ B
     inputs = {"n": 4, "A": np.ones(16, np.float32), "S": np.ones(10, np.float32), "B": np.ones(16, np.float32)}
+    inner = A @ S
+    expr = inner @ B
     res, ms, _ = RC.run_graph([expr], inputs, "cuda")
-    assert [c[0] for c in recorder.calls] == ["symm_sandwich"]
-    assert list(res) == [expr.name]
+    assert [c[0] for c in recorder.calls] == ["gen_x_symm", "gemm"]
+    assert list(res) == [inner.name, expr.name]
+    recorder.calls.clear()
+    inner = S @ B
+    expr = A @ inner
+    res, ms, _ = RC.run_graph([expr], inputs, "cuda")
+    assert [c[0] for c in recorder.calls] == ["symm_left", "gemm"]
+    assert list(res) == [inner.name, expr.name]
 
 
 def test_run_graph_chains_in_post_order(recorder):

@@ -137,10 +137,14 @@ def test_dsl_run_graph_sandwich_and_chain(cuda):
     s = W.make_sandwich(256, seed=8)
     A, S, B = GeneralMatrix((n, n), "A"), SymmetricMatrix((n, n), "S"), GeneralMatrix((n, n), "B")
     inputs = {"n": 256, "A": dev(s["A"]), "S": dev(s["S"]), "B": dev(s["B"])}
-    expr = A @ S @ B
+    inner = A @ S
+    expr = inner @ B
     res, ms, _ = run_graph([expr], inputs, "cuda")
     R = O.sandwich_rows_f64(s["A"], s["S"], s["B"], np.arange(256))
     assert relerr64(res[expr.name].view(256, 256).cpu().numpy(), R) <= 1e-5
+    # the intermediate A @ S is returned under its own name
+    Rm = O.symm_right_rows_f64(s["A"], s["S"], np.arange(256))
+    assert relerr64(res[inner.name].view(256, 256).cpu().numpy(), Rm) <= 1e-5
     # a plain chain runs op by op
     G1, G2, G3 = (GeneralMatrix((n, n), x) for x in ("G1", "G2", "G3"))
     w = [W.make_gemm(256, 256, 256, seed=k)["A"] for k in range(3)]
