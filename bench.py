@@ -22,12 +22,12 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
   others    strong scaling: the output is split into row slabs (equal-work
             boundaries for the triangular operand); each step is one libsmm
             multi-GPU call (smm_mg_*): the shared operand B (S and B for
-            A S B) is broadcast from rank 0 in K-chunks inside the call and
-            every rank accumulates its slab chunk by chunk as they land, so
-            the transfer overlaps the contraction within one product.  A S B
+            A S B) is broadcast from rank 0 in column blocks inside the call
+            and every rank computes its slab's columns block by block as they
+            land, so the transfer overlaps the contraction within one product.  A S B
             computes (A_slab S) B per slab.  The line also carries the
-            compute-only time and the fused call's roofline (MMA time vs the
-            NVLink time of the broadcast bytes).
+            compute-only and broadcast-only times and the fused call's
+            roofline (MMA time vs the NVLink time of the broadcast bytes).
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launching stream, max over
@@ -372,8 +372,8 @@ def run_ours(args, rank, world, local):
     else:
         # Contractions.  One GPU: the single-GPU entry point.  G > 1: one
         # libsmm multi-GPU call per step (smm_mg_*): B (S and B for the
-        # sandwich) is broadcast from rank 0 in K-chunks inside the call and
-        # this rank's row slab is accumulated chunk by chunk as they land.
+        # sandwich) is broadcast from rank 0 in column blocks inside the call
+        # and this rank's row slab is computed block by block as they land.
         # slab_local() runs the same slab with the operands already in place (the
         # single-GPU slab entry points), for the compute-only time.
         comm = MG.Communicator(rank, world) if world > 1 else None
@@ -486,6 +486,18 @@ def run_ours(args, rank, world, local):
         torch.cuda.synchronize()
         barrier(world)
         ms_c = max_over_ranks(c0.elapsed_time(c1), world) / args.steps
+        # the broadcast of B alone (a zero-row product: every rank receives B's blocks, none computes)
+        Bsh = d_in[-1]
+        empty_a = torch.empty((0, n), dtype=torch.float32, device="cuda")
+        barrier(world)
+        torch.cuda.synchronize()
+        c0.record(stream)
+        for _ in range(args.steps):
+            comm.gemm(empty_a, Bsh, empty_a, mode)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms_b = max_over_ranks(c0.elapsed_time(c1), world) / args.steps
         bcast = 4 * n * n + (2 * n * (n + 1) if op == "sandwich" else 0)
         passes = {"3xtf32": 3, "tf32": 1, "bf16": 1}[mode]
         peak = peaks["bf16_tflops"] / (1 if mode == "bf16" else 2)
@@ -493,10 +505,13 @@ def run_ours(args, rank, world, local):
         t_mma = passes * heaviest / (peak * 1e12) * 1e3
         t_link = bcast / 770e9 * 1e3
         multi = {"compute_only_ms_per_step": round(ms_c, 4), "broadcast_inclusive_ms_per_step": round(ms_per_step, 4),
+                 "broadcast_only_ms_per_step": round(ms_b, 4),
+                 "broadcast_gbs": round(4 * n * n / (ms_b * 1e-3) / 1e9, 1),
                  "broadcast_bytes_per_step": int(bcast),
-                 "k_chunks": MG.lib_chunks(n, world),
-                 "overlap": "B broadcast from rank 0 in K-chunks inside each call (libsmm smm_mg_*, NCCL on a "
-                            "high-priority stream); each chunk's contraction starts as soon as it lands",
+                 "column_blocks": MG.lib_chunks(n, world),
+                 "overlap": "B broadcast from rank 0 in column blocks inside each call (libsmm smm_mg_*, NCCL on a "
+                            "high-priority stream); each block's columns of the slab are computed as soon as it "
+                            "lands, on internal compute streams",
                  "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)],
                  "roofline": {"bound": "tensor" if t_mma >= t_link else "nvlink",
                               "t_mma_ms": round(t_mma, 4), "t_nvlink_ms": round(t_link, 4),

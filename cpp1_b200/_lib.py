@@ -123,13 +123,13 @@ SIGNATURES = [
     ("smm_mg_comm_status", _i, [_vp]),
     ("smm_mg_row_slabs", _i, [_i, _i, _i, _vp]),
     ("smm_mg_chunks", _i, [_i, _i, _vp]),
-    ("smm_mg_gemm_workspace_size", _sz, [_i, _i, _i, _i]),
+    ("smm_mg_gemm_workspace_size", _sz, [_vp, _i, _i, _i, _i]),
     ("smm_mg_gemm", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
-    ("smm_mg_upper_left_workspace_size", _sz, [_i, _i, _i, _i, _i]),
+    ("smm_mg_upper_left_workspace_size", _sz, [_vp, _i, _i, _i, _i]),
     ("smm_mg_upper_left", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
-    ("smm_mg_toeplitz_left_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_mg_toeplitz_left_workspace_size", _sz, [_vp, _i, _i, _i]),
     ("smm_mg_toeplitz_left", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
-    ("smm_mg_symm_sandwich_workspace_size", _sz, [_i, _i, _i]),
+    ("smm_mg_symm_sandwich_workspace_size", _sz, [_vp, _i, _i, _i]),
     ("smm_mg_symm_sandwich", _i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_debug_wait_limit_next", _i, [_ull]),
     ("smm_gen_x_toeplitz_workspace_size", _sz, [_i, _i, _i, _i]),

@@ -38,20 +38,17 @@ struct Operand {
   int row0 = 0;
   bool lower = false;  // dense A with exact zeros above the diagonal (K range clipped)
   int tri = 0;         // dense B: 1 upper / 2 lower triangular (K range clipped per column tile)
-  int k_off = 0;       // A: column that reduction index 0 maps to (a K-chunk of a longer product);
-                       // dense planes are then given from that column on
 };
 
 Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf = nullptr);
 Operand structured_op(const float* src, int dim, int row0 = 0);
 
-// C(M x N, ldc) = Aop(M x K) * B(K x N) on stream st (C += ... with
-// accumulate).  Optionally also writes lo(C) (C_lo, same ldc) or bf16(C)
-// (C_bf16, ldc_bf16) from the epilogue, so that C can feed a following
-// product (not with accumulate).
+// C(M x N, ldc) = Aop(M x K) * B(K x N) on stream st.  Optionally also
+// writes lo(C) (C_lo, same ldc) or bf16(C) (C_bf16, ldc_bf16) from the
+// epilogue, so that C can feed a following product.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
                     int N, int K, cudaStream_t st, float* C_lo = nullptr, __nv_bfloat16* C_bf16 = nullptr,
-                    int ldc_bf16 = 0, bool accumulate = false);
+                    int ldc_bf16 = 0);
 
 // ---------------------------------------------------------------- staging
 // A TMA-fed operand (rows x cols row-major): the caller's array or a padded

@@ -166,14 +166,8 @@ int check_packed(const char* who, int N) {
 // Core contraction: C(M x N, ldc) = Aop(M x K) * B(K x N, ldb).
 // Preconditions: B (and A when dense) 16-byte aligned with ld % 4 == 0.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
-                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16,
-                    bool accumulate) {
+                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16) {
   const bool bf16 = (mode == SMM_MODE_BF16);
-  if (accumulate && (C_lo || C_bf16))
-    return set_error(SMM_ERR_INVALID, "internal: accumulating contraction with extra outputs");
-  const int ks = bf16 ? 32 : 16;  // K elements per k-block
-  if (a.k_off != 0 && (a.k_off % ks != 0 || bk != BKind::Dense || b.tri != 0))
-    return set_error(SMM_ERR_INVALID, "internal: K offset %d with this right operand", a.k_off);
   const bool pair = use_pairs(M, N);
   const int bn = pick_bn(M, N, pair);
   Maps m;
@@ -207,8 +201,6 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.a_dim = a.dim;
   p.a_row0 = a.row0;
   p.a_lower = a.lower ? 1 : 0;
-  p.k_off = a.k_off;
-  p.accumulate = accumulate ? 1 : 0;
   p.b_tri = b.tri;
   p.b_src = b.src;
   p.b_dim = b.dim;

@@ -2,18 +2,17 @@
 //
 // A product C = X B (X the dense A, packed U, Toeplitz generator, or A S for
 // the sandwich) is partitioned by output row slabs: rank g computes rows
-// [r0, r1) of C.  The shared right operand B lives on the root rank; it is
-// broadcast in K-chunks (row chunks of B, contiguous in memory) on the
-// communicator's high-priority stream, and the slab product is accumulated
-// chunk by chunk on the caller's stream as the chunks arrive:
-//   C_slab  = X[r0:r1, K_0] B[K_0, :]
-//   C_slab += X[r0:r1, K_j] B[K_j, :]   (j = 1 .. c-1, each after chunk j landed)
-// so the broadcast of chunk j+1 overlaps the tensor-core work on chunk j.
-// Each chunk is one contraction launch with a K offset (the tensor maps start
-// at the chunk; triangular and Toeplitz operands use global columns) and an
-// epilogue that adds into C.  For the upper-triangular operand the chunks
-// travel last-first: the slabs of the last rows need only the last rows of
-// B, and they start at once.
+// [r0, r1) of C.  The shared right operand B lives on the root rank and is
+// broadcast inside each call in COLUMN blocks: the root copies column block
+// j of B into a contiguous K x W_j buffer and broadcasts it on the
+// communicator's high-priority stream; every rank computes
+//   C_slab[:, block j] = X[r0:r1, :] B[:, block j]
+// from that buffer as soon as it has landed, on one of several internal
+// compute streams, so block j's tensor-core work overlaps the transfer of the
+// blocks after it, and blocks that arrive while earlier ones still compute
+// run side by side.  Every output element is written once by one full-K
+// contraction (no partial sums: results identical to the single-GPU entry
+// points).
 //
 // No kernel reads another GPU's memory and nothing is multicast: remote data
 // reaches local HBM through NCCL before any kernel touches it.
@@ -88,21 +87,27 @@ int nccl_fail(ncclResult_t r, const char* what) {
   } while (0)
 
 constexpr int kMaxChunks = 16;
+constexpr int kWork = 4;  // internal compute streams
 
 }  // namespace
 }  // namespace smm
 
 // One rank's communicator: the NCCL communicator, the device it was created
-// on, a high-priority stream for the collectives and the events that order
-// them against the caller's stream.
+// on, a high-priority stream for the collectives, the compute streams the
+// column blocks run on, and the events that order them against the caller's
+// stream.
 struct smm_mg_comm {
   ncclComm_t nc = nullptr;
   int rank = 0;
   int world = 1;
   int device = 0;
   cudaStream_t cs = nullptr;
-  cudaEvent_t ev_start = nullptr;
+  cudaStream_t work[smm::kWork] = {};
+  cudaEvent_t ev_start = nullptr;  // caller's stream: inputs ready, previous call's readers done
+  cudaEvent_t ev_prep = nullptr;   // caller's stream: the left operand prepared
+  cudaEvent_t ev_s = nullptr;      // collective stream: the sandwich's S arrived
   cudaEvent_t ev_chunk[smm::kMaxChunks] = {};
+  cudaEvent_t ev_done[smm::kWork] = {};
 };
 
 namespace smm {
@@ -166,23 +171,24 @@ void row_slabs(int n, int world, bool triangular, int* b) {
   for (int g = 0; g <= world; ++g) b[g] = cuts[g];
 }
 
-// K-chunk boundaries of a broadcast of k rows: about k / 1024 chunks (2 to 8;
-// SMM_MG_CHUNKS overrides, 1 .. 15), multiples of 256 rows.
-int chunk_bounds(int k, int world, int* kb) {
+// Column-block boundaries of a broadcast of B (ncols columns): 1 block at
+// world 1, else 4 (SMM_MG_CHUNKS overrides, 1 .. 16), widths multiples of 256
+// (the widest output tile).
+int chunk_bounds(int ncols, int world, int* cb) {
   int c = 1;
   if (world > 1) {
-    c = std::min(8, std::max(2, k / 1024));
+    c = 4;
     if (const char* e = std::getenv("SMM_MG_CHUNKS")) {
       const int v = std::atoi(e);
-      if (v >= 1 && v < kMaxChunks) c = v;  // the last event slot is the sandwich's S
+      if (v >= 1 && v <= kMaxChunks) c = v;
     }
   }
-  int per = (k + c - 1) / c;
-  per = (per + 255) / 256 * 256;
+  int per = (ncols + c - 1) / c;
+  per = std::max(256, (per + 255) / 256 * 256);
   int n = 0;
-  kb[0] = 0;
-  for (int a = 0; a < k; a += per) kb[++n] = std::min(k, a + per);
-  if (n == 0) kb[++n] = k;  // k == 0
+  cb[0] = 0;
+  for (int a = 0; a < ncols; a += per) cb[++n] = std::min(ncols, a + per);
+  if (n == 0) cb[++n] = ncols;  // ncols == 0
   return n;
 }
 
@@ -196,45 +202,84 @@ int check_comm(const smm_mg_comm* c, const char* who) {
   return SMM_OK;
 }
 
-// The chunked broadcast: the comm stream waits for the caller's stream (B and
-// the previous call's readers are done), then broadcasts chunk j (in `order`)
-// and records ev_chunk[j] after it.
-int broadcast_chunks(smm_mg_comm* c, float* B, int ld, const int* kb, int nch, const int* order, int root,
-                     cudaStream_t st) {
+// Workspace of the B side: the packed column blocks (world > 1) and, in bf16
+// mode, their bf16 copies (one plane per block; at world 1 one plane of B).
+size_t b_side_bytes(int world, int K, int ncols, int mode) {
+  int cb[kMaxChunks + 1];
+  const int nch = chunk_bounds(ncols, world, cb);
+  size_t b = world > 1 ? round256(static_cast<size_t>(K) * ncols * 4) : 0;
+  if (mode == SMM_MODE_BF16)
+    for (int j = 0; j < nch; ++j) b += bf16_plane_bytes(K, cb[j + 1] - cb[j]);
+  return b;
+}
+
+// The B side of one call.  world > 1: the collective stream waits for the
+// caller's stream, then per block j the root packs B[:, block j] into its
+// K x W_j buffer (contiguous, at offset K * cb[j] of `pack`) and every rank
+// receives it there; ev_chunk[j] marks its arrival.  (The sandwich's
+// S_packed, s_count floats, is broadcast first, marked by ev_s.)
+int broadcast_blocks(smm_mg_comm* c, const float* B, int K, int ncols, float* pack, const int* cb, int nch, int root,
+                     cudaStream_t st, float* S_packed = nullptr, size_t s_count = 0) {
   if (c->world == 1) return SMM_OK;
   SMM_CUDA_TRY(cudaEventRecord(c->ev_start, st), "record call start");
   SMM_CUDA_TRY(cudaStreamWaitEvent(c->cs, c->ev_start, 0), "order broadcast after the caller's stream");
   const NcclApi& n = nccl();
-  for (int q = 0; q < nch; ++q) {
-    const int j = order[q];
-    float* p = B + static_cast<size_t>(kb[j]) * ld;
-    const size_t count = static_cast<size_t>(kb[j + 1] - kb[j]) * ld;
-    SMM_NCCL_TRY(n.broadcast(p, p, count, ncclFloat, root, c->nc, c->cs), "ncclBroadcast (K-chunk of B)");
-    SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record chunk arrival");
+  if (S_packed) {
+    SMM_NCCL_TRY(n.broadcast(S_packed, S_packed, s_count, ncclFloat, root, c->nc, c->cs), "ncclBroadcast (S)");
+    SMM_CUDA_TRY(cudaEventRecord(c->ev_s, c->cs), "record S arrival");
+  }
+  for (int j = 0; j < nch; ++j) {
+    const int w = cb[j + 1] - cb[j];
+    float* blk = pack + static_cast<size_t>(K) * cb[j];
+    if (c->rank == root)
+      SMM_CUDA_TRY(cudaMemcpy2DAsync(blk, static_cast<size_t>(w) * 4, B + cb[j], static_cast<size_t>(ncols) * 4,
+                                     static_cast<size_t>(w) * 4, K, cudaMemcpyDeviceToDevice, c->cs),
+                   "pack column block of B");
+    SMM_NCCL_TRY(n.broadcast(blk, blk, static_cast<size_t>(K) * w, ncclFloat, root, c->nc, c->cs),
+                 "ncclBroadcast (column block of B)");
+    SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record block arrival");
   }
   return SMM_OK;
 }
 
-int wait_chunk(smm_mg_comm* c, int j, cudaStream_t st) {
-  if (c->world == 1) return SMM_OK;
-  SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_chunk[j], 0), "wait for chunk arrival");
+// Runs block(j, stream) for every column block: at world 1 the single block
+// on the caller's stream; else block j on compute stream j % kWork once the
+// left operand is prepared (ev_prep, recorded on the caller's stream) and the
+// block has landed; the caller's stream then waits for all of them.
+template <typename F>
+int run_blocks(smm_mg_comm* c, int nch, cudaStream_t st, F&& block) {
+  if (c->world == 1) return block(0, st);
+  SMM_CUDA_TRY(cudaEventRecord(c->ev_prep, st), "record operand preparation");
+  const int used = std::min(nch, kWork);
+  for (int w = 0; w < used; ++w) SMM_CUDA_TRY(cudaStreamWaitEvent(c->work[w], c->ev_prep, 0), "fork");
+  for (int j = 0; j < nch; ++j) {
+    cudaStream_t w = c->work[j % kWork];
+    SMM_CUDA_TRY(cudaStreamWaitEvent(w, c->ev_chunk[j], 0), "wait for block arrival");
+    if (int rc = block(j, w)) return rc;
+  }
+  for (int w = 0; w < used; ++w) {
+    SMM_CUDA_TRY(cudaEventRecord(c->ev_done[w], c->work[w]), "record block done");
+    SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_done[w], 0), "join");
+  }
   return SMM_OK;
 }
 
-// The B chunk as a contraction operand: fp32 in place (rows 16-byte aligned),
-// or its bf16 copy converted into rows [kb[j], kb[j+1]) of the bf16 plane
-// `bf` (bf16 mode) once it has arrived.
-int chunk_operand(const float* B, int ld, __nv_bfloat16* bf, int ldb, int k0, int k1, int mode, cudaStream_t st,
-                  Operand* out) {
-  const float* src = B + static_cast<size_t>(k0) * ld;
-  if (mode == SMM_MODE_BF16) {
-    uint8_t* cur = reinterpret_cast<uint8_t*>(bf + static_cast<size_t>(k0) * ldb);
-    Staged s;
-    if (int rc = stage_operand(src, k1 - k0, ld, mode, cur, &s, st)) return rc;
-    *out = dense_op(nullptr, nullptr, s.ld, s.bf16);
-  } else {
-    *out = dense_op(src, nullptr, ld);
+// The B operand of column block j (K x W_j): fp32 in place (the caller's B at
+// world 1, the received block otherwise), or its bf16 copy converted on `st`
+// into the block's bf16 plane.
+int block_operand(const smm_mg_comm* c, const float* B, int K, int ncols, const float* pack, const int* cb, int j,
+                  int mode, uint8_t* bf_base, cudaStream_t st, Operand* out) {
+  const int w = cb[j + 1] - cb[j];
+  const float* src = c->world == 1 ? B : pack + static_cast<size_t>(K) * cb[j];
+  if (mode != SMM_MODE_BF16) {
+    *out = dense_op(src, nullptr, c->world == 1 ? ncols : w);
+    return SMM_OK;
   }
+  uint8_t* cur = bf_base;
+  for (int i = 0; i < j; ++i) cur += bf16_plane_bytes(K, cb[i + 1] - cb[i]);
+  Staged s;
+  if (int rc = stage_operand(src, K, w, mode, cur, &s, st)) return rc;
+  *out = dense_op(nullptr, nullptr, s.ld, s.bf16);
   return SMM_OK;
 }
 
@@ -258,6 +303,21 @@ extern "C" int smm_mg_unique_id(void* id_out) {
   return SMM_OK;
 }
 
+namespace {
+void release(smm_mg_comm* c) {
+  if (c->cs) cudaStreamDestroy(c->cs);
+  for (auto& w : c->work)
+    if (w) cudaStreamDestroy(w);
+  for (cudaEvent_t e : {c->ev_start, c->ev_prep, c->ev_s})
+    if (e) cudaEventDestroy(e);
+  for (auto& e : c->ev_chunk)
+    if (e) cudaEventDestroy(e);
+  for (auto& e : c->ev_done)
+    if (e) cudaEventDestroy(e);
+  delete c;
+}
+}  // namespace
+
 extern "C" int smm_mg_comm_init(smm_mg_comm** out, int rank, int world, const void* id) {
   SMM_RANGE("smm_mg_comm_init");
   if (!out) return set_error(SMM_ERR_INVALID, "smm_mg_comm_init: null output");
@@ -269,11 +329,7 @@ extern "C" int smm_mg_comm_init(smm_mg_comm** out, int rank, int world, const vo
   c->rank = rank;
   c->world = world;
   auto fail = [&](int rc) {
-    if (c->cs) cudaStreamDestroy(c->cs);
-    if (c->ev_start) cudaEventDestroy(c->ev_start);
-    for (auto& e : c->ev_chunk)
-      if (e) cudaEventDestroy(e);
-    delete c;
+    release(c);
     return rc;
   };
   if (cudaGetDevice(&c->device) != cudaSuccess) return fail(set_error(SMM_ERR_CUDA, "cudaGetDevice failed"));
@@ -281,9 +337,16 @@ extern "C" int smm_mg_comm_init(smm_mg_comm** out, int rank, int world, const vo
   if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
       cudaStreamCreateWithPriority(&c->cs, cudaStreamNonBlocking, hi) != cudaSuccess)
     return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: collective stream"));
-  if (cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming) != cudaSuccess)
-    return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: event"));
+  for (auto& w : c->work)
+    if (cudaStreamCreateWithFlags(&w, cudaStreamNonBlocking) != cudaSuccess)
+      return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: compute stream"));
+  for (cudaEvent_t* e : {&c->ev_start, &c->ev_prep, &c->ev_s})
+    if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess)
+      return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: event"));
   for (auto& e : c->ev_chunk)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+      return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: event"));
+  for (auto& e : c->ev_done)
     if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
       return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: event"));
   if (world > 1) {
@@ -303,15 +366,13 @@ extern "C" int smm_mg_comm_destroy(smm_mg_comm* c) {
   if (!c) return SMM_OK;
   int rc = SMM_OK;
   if (c->cs) cudaStreamSynchronize(c->cs);
+  for (auto& w : c->work)
+    if (w) cudaStreamSynchronize(w);
   if (c->nc) {
     ncclResult_t r = nccl().comm_destroy(c->nc);
     if (r != ncclSuccess) rc = nccl_fail(r, "ncclCommDestroy");
   }
-  if (c->cs) cudaStreamDestroy(c->cs);
-  if (c->ev_start) cudaEventDestroy(c->ev_start);
-  for (auto& e : c->ev_chunk)
-    if (e) cudaEventDestroy(e);
-  delete c;
+  release(c);
   return rc;
 }
 
@@ -323,11 +384,7 @@ extern "C" int smm_mg_comm_abort(smm_mg_comm* c) {
     ncclResult_t r = nccl().comm_abort(c->nc);
     if (r != ncclSuccess) rc = nccl_fail(r, "ncclCommAbort");
   }
-  if (c->cs) cudaStreamDestroy(c->cs);
-  if (c->ev_start) cudaEventDestroy(c->ev_start);
-  for (auto& e : c->ev_chunk)
-    if (e) cudaEventDestroy(e);
-  delete c;
+  release(c);
   return rc;
 }
 
@@ -346,230 +403,194 @@ extern "C" int smm_mg_row_slabs(int N, int world, int triangular, int* bounds) {
   return SMM_OK;
 }
 
-extern "C" int smm_mg_chunks(int K, int world, int* bounds) {
-  if (K < 0 || world < 1 || !bounds) return set_error(SMM_ERR_INVALID, "smm_mg_chunks: bad arguments");
-  return chunk_bounds(K, world, bounds);
-}
-
-// ---------------------------------------------------------------- products
-extern "C" size_t smm_mg_gemm_workspace_size(int nrows, int N, int K, int mode) {
-  if (nrows <= 0 || N <= 0 || K <= 0) return 0;
-  // the A slab staged (bf16 copy, or a padded fp32 copy) + B's bf16 plane
-  return staged_bytes_bound(nrows, K, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(K, N) : 0);
-}
-
-extern "C" int smm_mg_gemm(smm_mg_comm* c, const float* A_slab, float* B, float* C_slab, int nrows, int N, int K,
-                           int mode, int root, void* ws, size_t ws_bytes, void* stream) {
-  SMM_RANGE("smm_mg_gemm");
-  if (int rc = check_comm(c, "smm_mg_gemm")) return rc;
-  if (nrows < 0 || N < 0 || K < 0 || root < 0 || root >= c->world)
-    return set_error(SMM_ERR_INVALID, "smm_mg_gemm: bad shape or root");
-  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_mg_gemm: unknown mode %d", mode);
-  if (N == 0 || K == 0) return SMM_OK;
-  if (!B || (nrows > 0 && (!A_slab || !C_slab))) return set_error(SMM_ERR_INVALID, "smm_mg_gemm: null pointer");
-  if (!aligned_rows(B, N)) return set_error(SMM_ERR_INVALID, "smm_mg_gemm: B needs 16-byte aligned rows");
-  cudaStream_t st = as_stream(stream);
-  int kb[kMaxChunks + 1], order[kMaxChunks];
-  const int nch = chunk_bounds(K, c->world, kb);
-  for (int j = 0; j < nch; ++j) order[j] = j;
-  if (int rc = broadcast_chunks(c, B, N, kb, nch, order, root, st)) return rc;
-  if (nrows == 0) return SMM_OK;
-  const size_t need = staged_bytes(A_slab, nrows, K, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(K, N) : 0);
-  if (int rc = check_ws("smm_mg_gemm", ws, ws_bytes, need)) return rc;
-  uint8_t* cur = static_cast<uint8_t*>(ws);
-  Staged a;
-  if (int rc = stage_operand(A_slab, nrows, K, mode, cur, &a, st)) return rc;
-  __nv_bfloat16* bbf = mode == SMM_MODE_BF16 ? reinterpret_cast<__nv_bfloat16*>(cur) : nullptr;
-  const int ldb = round8(N);
-  for (int q = 0; q < nch; ++q) {
-    const int j = order[q];
-    if (int rc = wait_chunk(c, j, st)) return rc;
-    Operand bo;
-    if (int rc = chunk_operand(B, N, bbf, ldb, kb[j], kb[j + 1], mode, st, &bo)) return rc;
-    const size_t off = static_cast<size_t>(kb[j]);
-    Operand ao = dense_op(a.ptr ? a.ptr + off : nullptr, nullptr, a.ld, a.bf16 ? a.bf16 + off : nullptr);
-    ao.k_off = kb[j];
-    if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, ao, bo, C_slab, N, nrows, N, kb[j + 1] - kb[j], st,
-                                 nullptr, nullptr, 0, q > 0))
-      return rc;
-  }
-  return SMM_OK;
-}
-
-extern "C" size_t smm_mg_upper_left_workspace_size(int N, int ncols, int row0, int nrows, int mode) {
-  if (N <= 0 || ncols <= 0 || nrows <= 0) return 0;
-  (void)row0;
-  return expanded_bytes(nrows, N, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, ncols) : 0);
-}
-
-extern "C" int smm_mg_upper_left(smm_mg_comm* c, const float* U_packed, float* B, float* C_slab, int N, int ncols,
-                                 int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream) {
-  SMM_RANGE("smm_mg_upper_left");
-  if (int rc = check_comm(c, "smm_mg_upper_left")) return rc;
-  if (N < 0 || ncols < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N || root < 0 || root >= c->world)
-    return set_error(SMM_ERR_INVALID, "smm_mg_upper_left: bad shape, slab or root");
-  if (int rc = check_packed("smm_mg_upper_left", N)) return rc;
-  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_mg_upper_left: unknown mode %d", mode);
-  if (N == 0 || ncols == 0) return SMM_OK;
-  if (!B || (nrows > 0 && (!U_packed || !C_slab)))
-    return set_error(SMM_ERR_INVALID, "smm_mg_upper_left: null pointer");
-  if (!aligned_rows(B, ncols)) return set_error(SMM_ERR_INVALID, "smm_mg_upper_left: B needs 16-byte aligned rows");
-  cudaStream_t st = as_stream(stream);
-  int kb[kMaxChunks + 1], order[kMaxChunks];
-  const int nch = chunk_bounds(N, c->world, kb);
-  for (int q = 0; q < nch; ++q) order[q] = nch - 1 - q;  // last rows of B first
-  if (int rc = broadcast_chunks(c, B, ncols, kb, nch, order, root, st)) return rc;
-  if (nrows == 0) return SMM_OK;
-  const size_t need = expanded_bytes(nrows, N, mode) + (mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, ncols) : 0);
-  if (int rc = check_ws("smm_mg_upper_left", ws, ws_bytes, need)) return rc;
-  uint8_t* cur = static_cast<uint8_t*>(ws);
-  Staged u;  // rows [row0, row0 + nrows) of U, dense (zeros left of the diagonal)
-  if (int rc = expand_operand(U_packed, SMM_STRUCT_UPPER, N, row0, nrows, mode, cur, &u, st)) return rc;
-  __nv_bfloat16* bbf = mode == SMM_MODE_BF16 ? reinterpret_cast<__nv_bfloat16*>(cur) : nullptr;
-  const int ldb = round8(ncols);
-  bool first = true;
-  for (int q = 0; q < nch; ++q) {
-    const int j = order[q];
-    if (int rc = wait_chunk(c, j, st)) return rc;
-    if (kb[j + 1] <= row0) continue;  // this slab's rows are zero there (the chunk is still received)
-    Operand bo;
-    if (int rc = chunk_operand(B, ncols, bbf, ldb, kb[j], kb[j + 1], mode, st, &bo)) return rc;
-    const size_t off = static_cast<size_t>(kb[j]);
-    Operand ao = dense_op(u.ptr ? u.ptr + off : nullptr, nullptr, u.ld, u.bf16 ? u.bf16 + off : nullptr);
-    ao.dim = N;
-    ao.row0 = row0;
-    ao.k_off = kb[j];
-    if (int rc = run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, bo, C_slab, ncols, nrows, ncols,
-                                 kb[j + 1] - kb[j], st, nullptr, nullptr, 0, !first))
-      return rc;
-    first = false;
-  }
-  return SMM_OK;
-}
-
-extern "C" size_t smm_mg_toeplitz_left_workspace_size(int N, int ncols, int mode) {
-  if (N <= 0 || ncols <= 0) return 0;
-  return mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, ncols) : 0;
-}
-
-extern "C" int smm_mg_toeplitz_left(smm_mg_comm* c, const float* g, float* B, float* C_slab, int N, int ncols,
-                                    int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes,
-                                    void* stream) {
-  SMM_RANGE("smm_mg_toeplitz_left");
-  if (int rc = check_comm(c, "smm_mg_toeplitz_left")) return rc;
-  if (N < 0 || ncols < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N || root < 0 || root >= c->world)
-    return set_error(SMM_ERR_INVALID, "smm_mg_toeplitz_left: bad shape, slab or root");
-  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_mg_toeplitz_left: unknown mode %d", mode);
-  if (N == 0 || ncols == 0) return SMM_OK;
-  if (!B || (nrows > 0 && (!g || !C_slab))) return set_error(SMM_ERR_INVALID, "smm_mg_toeplitz_left: null pointer");
-  if (!aligned_rows(B, ncols))
-    return set_error(SMM_ERR_INVALID, "smm_mg_toeplitz_left: B needs 16-byte aligned rows");
-  cudaStream_t st = as_stream(stream);
-  int kb[kMaxChunks + 1], order[kMaxChunks];
-  const int nch = chunk_bounds(N, c->world, kb);
-  for (int j = 0; j < nch; ++j) order[j] = j;
-  if (int rc = broadcast_chunks(c, B, ncols, kb, nch, order, root, st)) return rc;
-  if (nrows == 0) return SMM_OK;
-  const size_t need = mode == SMM_MODE_BF16 ? bf16_plane_bytes(N, ncols) : 0;
-  if (int rc = check_ws("smm_mg_toeplitz_left", ws, ws_bytes, need)) return rc;
-  __nv_bfloat16* bbf = mode == SMM_MODE_BF16 ? static_cast<__nv_bfloat16*>(ws) : nullptr;
-  const int ldb = round8(ncols);
-  for (int q = 0; q < nch; ++q) {
-    const int j = order[q];
-    if (int rc = wait_chunk(c, j, st)) return rc;
-    Operand bo;
-    if (int rc = chunk_operand(B, ncols, bbf, ldb, kb[j], kb[j + 1], mode, st, &bo)) return rc;
-    Operand ao = structured_op(g, N, row0);
-    ao.k_off = kb[j];
-    if (int rc = run_contraction(AKind::Toeplitz, BKind::Dense, mode, ao, bo, C_slab, ncols, nrows, ncols,
-                                 kb[j + 1] - kb[j], st, nullptr, nullptr, 0, q > 0))
-      return rc;
-  }
-  return SMM_OK;
+extern "C" int smm_mg_chunks(int ncols, int world, int* bounds) {
+  if (ncols < 0 || world < 1 || !bounds) return set_error(SMM_ERR_INVALID, "smm_mg_chunks: bad arguments");
+  return chunk_bounds(ncols, world, bounds);
 }
 
 namespace {
-// Sandwich workspace: Y = A_slab S (fp32, 16-byte rows; plus its bf16 copy in
-// bf16 mode), the dense expansion of S, the staged A slab, B's bf16 plane.
-size_t mg_sandwich_ws(int N, int nrows, int mode) {
-  const bool bf = mode == SMM_MODE_BF16;
-  return plane_bytes(nrows, N) + (bf ? bf16_plane_bytes(nrows, N) : 0) + expanded_bytes(N, N, mode) +
-         staged_bytes_bound(nrows, N, mode) + (bf ? bf16_plane_bytes(N, N) : 0);
+// Validation shared by the products.
+int check_call(const smm_mg_comm* c, const char* who, int mode, int root, const float* B, int ncols) {
+  if (int rc = check_comm(c, who)) return rc;
+  if (root < 0 || root >= c->world) return set_error(SMM_ERR_INVALID, "%s: root %d of %d", who, root, c->world);
+  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
+  if (c->rank == root && (!B || !aligned_rows(B, ncols)))
+    return set_error(SMM_ERR_INVALID, "%s: the root's B must be non-null with 16-byte aligned rows", who);
+  return SMM_OK;
 }
 }  // namespace
 
-extern "C" size_t smm_mg_symm_sandwich_workspace_size(int N, int nrows, int mode) {
-  if (N <= 0 || nrows <= 0) return 0;
-  return mg_sandwich_ws(N, nrows, mode);
+// ---------------------------------------------------------------- products
+extern "C" size_t smm_mg_gemm_workspace_size(const smm_mg_comm* c, int nrows, int N, int K, int mode) {
+  if (!c || nrows < 0 || N <= 0 || K <= 0) return 0;
+  return b_side_bytes(c->world, K, N, mode) + (nrows ? staged_bytes_bound(nrows, K, mode) : 0);
 }
 
-extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* S_packed, float* B, float* C_slab,
-                                    int N, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream) {
+extern "C" int smm_mg_gemm(smm_mg_comm* c, const float* A_slab, const float* B, float* C_slab, int nrows, int N,
+                           int K, int mode, int root, void* ws, size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_mg_gemm");
+  if (int rc = check_call(c, "smm_mg_gemm", mode, root, B, N)) return rc;
+  if (nrows < 0 || N < 0 || K < 0) return set_error(SMM_ERR_INVALID, "smm_mg_gemm: negative shape");
+  if (N == 0 || K == 0) return SMM_OK;
+  if (nrows > 0 && (!A_slab || !C_slab)) return set_error(SMM_ERR_INVALID, "smm_mg_gemm: null pointer");
+  if (int rc = check_ws("smm_mg_gemm", ws, ws_bytes, smm_mg_gemm_workspace_size(c, nrows, N, K, mode))) return rc;
+  cudaStream_t st = as_stream(stream);
+  int cb[kMaxChunks + 1];
+  const int nch = chunk_bounds(N, c->world, cb);
+  uint8_t* cur = static_cast<uint8_t*>(ws);
+  float* pack = reinterpret_cast<float*>(cur);
+  uint8_t* bf = cur + (c->world > 1 ? round256(static_cast<size_t>(K) * N * 4) : 0);
+  cur += b_side_bytes(c->world, K, N, mode);
+  if (int rc = broadcast_blocks(c, B, K, N, pack, cb, nch, root, st)) return rc;
+  Staged a{};
+  if (nrows > 0)
+    if (int rc = stage_operand(A_slab, nrows, K, mode, cur, &a, st)) return rc;
+  return run_blocks(c, nch, st, [&](int j, cudaStream_t w) -> int {
+    if (nrows == 0) return SMM_OK;
+    Operand bo;
+    if (int rc = block_operand(c, B, K, N, pack, cb, j, mode, bf, w, &bo)) return rc;
+    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16), bo,
+                           C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], K, w);
+  });
+}
+
+extern "C" size_t smm_mg_upper_left_workspace_size(const smm_mg_comm* c, int N, int ncols, int nrows, int mode) {
+  if (!c || N <= 0 || ncols <= 0 || nrows < 0) return 0;
+  return b_side_bytes(c->world, N, ncols, mode) + (nrows ? expanded_bytes(nrows, N, mode) : 0);
+}
+
+extern "C" int smm_mg_upper_left(smm_mg_comm* c, const float* U_packed, const float* B, float* C_slab, int N,
+                                 int ncols, int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes,
+                                 void* stream) {
+  SMM_RANGE("smm_mg_upper_left");
+  if (int rc = check_call(c, "smm_mg_upper_left", mode, root, B, ncols)) return rc;
+  if (N < 0 || ncols < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N)
+    return set_error(SMM_ERR_INVALID, "smm_mg_upper_left: bad shape or slab");
+  if (int rc = check_packed("smm_mg_upper_left", N)) return rc;
+  if (N == 0 || ncols == 0) return SMM_OK;
+  if (nrows > 0 && (!U_packed || !C_slab)) return set_error(SMM_ERR_INVALID, "smm_mg_upper_left: null pointer");
+  if (int rc = check_ws("smm_mg_upper_left", ws, ws_bytes, smm_mg_upper_left_workspace_size(c, N, ncols, nrows, mode)))
+    return rc;
+  cudaStream_t st = as_stream(stream);
+  int cb[kMaxChunks + 1];
+  const int nch = chunk_bounds(ncols, c->world, cb);
+  uint8_t* cur = static_cast<uint8_t*>(ws);
+  float* pack = reinterpret_cast<float*>(cur);
+  uint8_t* bf = cur + (c->world > 1 ? round256(static_cast<size_t>(N) * ncols * 4) : 0);
+  cur += b_side_bytes(c->world, N, ncols, mode);
+  if (int rc = broadcast_blocks(c, B, N, ncols, pack, cb, nch, root, st)) return rc;
+  Staged u{};  // rows [row0, row0 + nrows) of U, dense (zeros left of the diagonal)
+  if (nrows > 0)
+    if (int rc = expand_operand(U_packed, SMM_STRUCT_UPPER, N, row0, nrows, mode, cur, &u, st)) return rc;
+  return run_blocks(c, nch, st, [&](int j, cudaStream_t w) -> int {
+    if (nrows == 0) return SMM_OK;
+    Operand bo;
+    if (int rc = block_operand(c, B, N, ncols, pack, cb, j, mode, bf, w, &bo)) return rc;
+    Operand ao = dense_op(u.ptr, nullptr, u.ld, u.bf16);
+    ao.dim = N;
+    ao.row0 = row0;
+    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, bo, C_slab + cb[j], ncols, nrows,
+                           cb[j + 1] - cb[j], N, w);
+  });
+}
+
+extern "C" size_t smm_mg_toeplitz_left_workspace_size(const smm_mg_comm* c, int N, int ncols, int mode) {
+  if (!c || N <= 0 || ncols <= 0) return 0;
+  return b_side_bytes(c->world, N, ncols, mode);
+}
+
+extern "C" int smm_mg_toeplitz_left(smm_mg_comm* c, const float* g, const float* B, float* C_slab, int N, int ncols,
+                                    int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes,
+                                    void* stream) {
+  SMM_RANGE("smm_mg_toeplitz_left");
+  if (int rc = check_call(c, "smm_mg_toeplitz_left", mode, root, B, ncols)) return rc;
+  if (N < 0 || ncols < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N)
+    return set_error(SMM_ERR_INVALID, "smm_mg_toeplitz_left: bad shape or slab");
+  if (N == 0 || ncols == 0) return SMM_OK;
+  if (nrows > 0 && (!g || !C_slab)) return set_error(SMM_ERR_INVALID, "smm_mg_toeplitz_left: null pointer");
+  if (int rc = check_ws("smm_mg_toeplitz_left", ws, ws_bytes, smm_mg_toeplitz_left_workspace_size(c, N, ncols, mode)))
+    return rc;
+  cudaStream_t st = as_stream(stream);
+  int cb[kMaxChunks + 1];
+  const int nch = chunk_bounds(ncols, c->world, cb);
+  float* pack = static_cast<float*>(ws);
+  uint8_t* bf = static_cast<uint8_t*>(ws) + (c->world > 1 ? round256(static_cast<size_t>(N) * ncols * 4) : 0);
+  if (int rc = broadcast_blocks(c, B, N, ncols, pack, cb, nch, root, st)) return rc;
+  return run_blocks(c, nch, st, [&](int j, cudaStream_t w) -> int {
+    if (nrows == 0) return SMM_OK;
+    Operand bo;
+    if (int rc = block_operand(c, B, N, ncols, pack, cb, j, mode, bf, w, &bo)) return rc;
+    return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), bo, C_slab + cb[j], ncols,
+                           nrows, cb[j + 1] - cb[j], N, w);
+  });
+}
+
+namespace {
+// Sandwich workspace beyond the B side: Y = A_slab S (fp32, 16-byte rows;
+// plus its bf16 copy in bf16 mode), the dense expansion of S, the staged A slab.
+size_t mg_sandwich_left(int N, int nrows, int mode) {
+  if (nrows == 0) return 0;
+  const bool bf = mode == SMM_MODE_BF16;
+  return plane_bytes(nrows, N) + (bf ? bf16_plane_bytes(nrows, N) : 0) + expanded_bytes(N, N, mode) +
+         staged_bytes_bound(nrows, N, mode);
+}
+}  // namespace
+
+extern "C" size_t smm_mg_symm_sandwich_workspace_size(const smm_mg_comm* c, int N, int nrows, int mode) {
+  if (!c || N <= 0 || nrows < 0) return 0;
+  return b_side_bytes(c->world, N, N, mode) + mg_sandwich_left(N, nrows, mode);
+}
+
+extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* S_packed, const float* B,
+                                    float* C_slab, int N, int nrows, int mode, int root, void* ws, size_t ws_bytes,
+                                    void* stream) {
   SMM_RANGE("smm_mg_symm_sandwich");
-  if (int rc = check_comm(c, "smm_mg_symm_sandwich")) return rc;
-  if (N < 0 || nrows < 0 || nrows > N || root < 0 || root >= c->world)
-    return set_error(SMM_ERR_INVALID, "smm_mg_symm_sandwich: bad shape or root");
+  if (int rc = check_call(c, "smm_mg_symm_sandwich", mode, root, B, N)) return rc;
+  if (N < 0 || nrows < 0 || nrows > N) return set_error(SMM_ERR_INVALID, "smm_mg_symm_sandwich: bad shape");
   if (int rc = check_packed("smm_mg_symm_sandwich", N)) return rc;
-  if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "smm_mg_symm_sandwich: unknown mode %d", mode);
   if (N == 0) return SMM_OK;
-  if (!S_packed || !B || (nrows > 0 && (!A_slab || !C_slab)))
+  if (!S_packed || (nrows > 0 && (!A_slab || !C_slab)))
     return set_error(SMM_ERR_INVALID, "smm_mg_symm_sandwich: null pointer");
-  if (!aligned_rows(B, N)) return set_error(SMM_ERR_INVALID, "smm_mg_symm_sandwich: B needs 16-byte aligned rows");
+  if (int rc = check_ws("smm_mg_symm_sandwich", ws, ws_bytes, smm_mg_symm_sandwich_workspace_size(c, N, nrows, mode)))
+    return rc;
   cudaStream_t st = as_stream(stream);
   const bool bf = mode == SMM_MODE_BF16;
-  // S travels whole first (packed, N(N+1)/2 floats), then B in K-chunks.
-  int kb[kMaxChunks + 2], order[kMaxChunks];
-  const int nch = chunk_bounds(N, c->world, kb);
-  for (int j = 0; j < nch; ++j) order[j] = j;
-  if (c->world > 1) {
-    SMM_CUDA_TRY(cudaEventRecord(c->ev_start, st), "record call start");
-    SMM_CUDA_TRY(cudaStreamWaitEvent(c->cs, c->ev_start, 0), "order broadcast after the caller's stream");
-    const size_t ns = static_cast<size_t>(N) * (N + 1) / 2;
-    SMM_NCCL_TRY(nccl().broadcast(S_packed, S_packed, ns, ncclFloat, root, c->nc, c->cs), "ncclBroadcast (S)");
-    SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[kMaxChunks - 1], c->cs), "record S arrival");
-    const NcclApi& n = nccl();
-    for (int q = 0; q < nch; ++q) {
-      const int j = order[q];
-      float* p = B + static_cast<size_t>(kb[j]) * N;
-      SMM_NCCL_TRY(n.broadcast(p, p, static_cast<size_t>(kb[j + 1] - kb[j]) * N, ncclFloat, root, c->nc, c->cs),
-                   "ncclBroadcast (K-chunk of B)");
-      SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record chunk arrival");
-    }
-  }
-  if (nrows == 0) return SMM_OK;
-  if (int rc = check_ws("smm_mg_symm_sandwich", ws, ws_bytes, mg_sandwich_ws(N, nrows, mode))) return rc;
+  int cb[kMaxChunks + 1];
+  const int nch = chunk_bounds(N, c->world, cb);
   uint8_t* cur = static_cast<uint8_t*>(ws);
-  float* Y = reinterpret_cast<float*>(cur);
-  const int ldy = round4(N), ldy_bf = round8(N);
-  cur += plane_bytes(nrows, N);
-  __nv_bfloat16* Y_bf = nullptr;
-  if (bf) {
-    Y_bf = reinterpret_cast<__nv_bfloat16*>(cur);
-    cur += bf16_plane_bytes(nrows, N);
-    if (ldy_bf != N) SMM_CUDA_TRY(cudaMemsetAsync(Y_bf, 0, bf16_plane_bytes(nrows, N), st), "zero bf16 rows");
-  }
-  Staged a;
-  if (int rc = stage_operand(A_slab, nrows, N, mode, cur, &a, st)) return rc;
-  if (c->world > 1) SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_chunk[kMaxChunks - 1], 0), "wait for S");
-  Staged s;  // S mirrored into a dense copy: the right operand of Y = A_slab S
-  if (int rc = expand_operand(S_packed, SMM_STRUCT_SYMM, N, 0, N, mode, cur, &s, st)) return rc;
-  if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16),
-                               dense_op(s.ptr, nullptr, s.ld, s.bf16), Y, ldy, nrows, N, N, st, nullptr, Y_bf,
-                               ldy_bf))
+  float* pack = reinterpret_cast<float*>(cur);
+  uint8_t* bfb = cur + (c->world > 1 ? round256(static_cast<size_t>(N) * N * 4) : 0);
+  cur += b_side_bytes(c->world, N, N, mode);
+  // S travels whole first (packed, N(N+1)/2 floats), then B in column blocks.
+  if (int rc = broadcast_blocks(c, B, N, N, pack, cb, nch, root, st, S_packed, static_cast<size_t>(N) * (N + 1) / 2))
     return rc;
-  __nv_bfloat16* bbf = bf ? reinterpret_cast<__nv_bfloat16*>(cur) : nullptr;
-  const int ldb = round8(N);
-  for (int q = 0; q < nch; ++q) {
-    const int j = order[q];
-    if (int rc = wait_chunk(c, j, st)) return rc;
-    Operand bo;
-    if (int rc = chunk_operand(B, N, bbf, ldb, kb[j], kb[j + 1], mode, st, &bo)) return rc;
-    const size_t off = static_cast<size_t>(kb[j]);
-    Operand yo = dense_op(bf ? nullptr : Y + off, nullptr, bf ? ldy_bf : ldy, bf ? Y_bf + off : nullptr);
-    yo.k_off = kb[j];
-    if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, yo, bo, C_slab, N, nrows, N, kb[j + 1] - kb[j], st,
-                                 nullptr, nullptr, 0, q > 0))
+  float* Y = nullptr;
+  __nv_bfloat16* Y_bf = nullptr;
+  const int ldy = round4(N), ldy_bf = round8(N);
+  if (nrows > 0) {
+    // Y = A_slab S: the reference's run_graph order, (A S) first
+    Y = reinterpret_cast<float*>(cur);
+    cur += plane_bytes(nrows, N);
+    if (bf) {
+      Y_bf = reinterpret_cast<__nv_bfloat16*>(cur);
+      cur += bf16_plane_bytes(nrows, N);
+      if (ldy_bf != N) SMM_CUDA_TRY(cudaMemsetAsync(Y_bf, 0, bf16_plane_bytes(nrows, N), st), "zero bf16 rows");
+    }
+    Staged a;
+    if (int rc = stage_operand(A_slab, nrows, N, mode, cur, &a, st)) return rc;
+    if (c->world > 1) SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_s, 0), "wait for S");
+    Staged s;  // S mirrored into a dense copy: the right operand of Y = A_slab S
+    if (int rc = expand_operand(S_packed, SMM_STRUCT_SYMM, N, 0, N, mode, cur, &s, st)) return rc;
+    if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16),
+                                 dense_op(s.ptr, nullptr, s.ld, s.bf16), Y, ldy, nrows, N, N, st, nullptr, Y_bf,
+                                 ldy_bf))
       return rc;
   }
-  return SMM_OK;
+  return run_blocks(c, nch, st, [&](int j, cudaStream_t w) -> int {
+    if (nrows == 0) return SMM_OK;
+    Operand bo;
+    if (int rc = block_operand(c, B, N, N, pack, cb, j, mode, bfb, w, &bo)) return rc;
+    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(bf ? nullptr : Y, nullptr, bf ? ldy_bf : ldy, Y_bf),
+                           bo, C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], N, w);
+  });
 }

@@ -120,10 +120,6 @@ struct UmmaParams {
   const float* a_src;      // packed U / generator / packed S (structured A kinds)
   int a_dim;               // order of the structured matrix
   int a_row0;              // row of the structured matrix that output row 0 maps to
-  int k_off;               // column of the left operand that reduction index 0 maps to (a K-chunk of a
-                           // longer product: the tensor maps start there; structured A and the
-                           // triangular K clipping use global columns)
-  int accumulate;          // C += product (the stored C is read back), else C = product
   int a_lower;             // dense A is lower triangular: rows up to g need k <= g only
   int b_tri;               // dense B is upper (1) / lower (2) triangular: K range clipped per column tile
   const float* b_src;      // packed U / packed S (structured B kinds)
@@ -638,17 +634,13 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   const int nb0 = n0 + static_cast<int>(rank) * kBCols;    // this CTA's B columns
   // Rows of a triangular left operand are zero left of the diagonal: a row
   // tile starting at row g0 needs k >= g0 only.
-  // (local k-blocks: global column = k_off + local column, k_off a multiple of KS)
   int kb_begin = 0;
-  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense)
-    kb_begin = max(p.a_row0 + tile_m0 - p.k_off, 0) / KS;
+  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + tile_m0) / KS;
   int kb_end = (p.K + KS - 1) / KS;
   // A lower-triangular left operand is zero right of its diagonal: rows up
   // to g1 need k <= g1 only.
-  if (AK == AKind::LowerPacked || (AK == AKind::Dense && p.a_lower)) {
-    const int last = p.a_row0 + tile_m0 + (PAIR ? 2 * kBM : kBM) - 1 - p.k_off;  // last needed local column
-    kb_end = min(kb_end, last < 0 ? 0 : last / KS + 1);
-  }
+  if (AK == AKind::LowerPacked || (AK == AKind::Dense && p.a_lower))
+    kb_end = min(kb_end, (p.a_row0 + tile_m0 + (PAIR ? 2 * kBM : kBM) - 1) / KS + 1);
   // An upper-triangular right operand is zero below its diagonal: column
   // tile [n0, n0+BN) needs k < n0 + BN only; a lower-triangular one is zero
   // above it: the tile needs k >= n0 only.
@@ -837,11 +829,11 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         const uint32_t ph = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
         if constexpr (kStaging) {
-          a_stage_fill_toeplitz_bf16(p, stg(s), g_first, (kb_begin + i) * KS + p.k_off, ft);
+          a_stage_fill_toeplitz_bf16(p, stg(s), g_first, (kb_begin + i) * KS, ft);
         } else {
 #pragma unroll
           for (int j = 0; j < kSubs; ++j)
-            a_async_fill<AK>(p, a_hi(s) + j * kATileBytes, g_first, (kb_begin + i * kSubs + j) * KS + p.k_off, ft);
+            a_async_fill<AK>(p, a_hi(s) + j * kATileBytes, g_first, (kb_begin + i * kSubs + j) * KS, ft);
         }
         cp_async_mbar_arrive_noinc(&full[s]);
       }
@@ -902,8 +894,8 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
       uint32_t a_rb[KS / 2];
       if constexpr (!kATma && !kACp) {
         a_row_bases<AK, KS>(a_rb, p, g_first, xw, lane);
-        if (num_kb > 0) a_gather<AK, KS>(a_b0, p, a_rb, g_first, kb_begin * KS + p.k_off, xw, lane);
-        if (num_kb > 1) a_gather<AK, KS>(a_b1, p, a_rb, g_first, (kb_begin + 1) * KS + p.k_off, xw, lane);
+        if (num_kb > 0) a_gather<AK, KS>(a_b0, p, a_rb, g_first, kb_begin * KS, xw, lane);
+        if (num_kb > 1) a_gather<AK, KS>(a_b1, p, a_rb, g_first, (kb_begin + 1) * KS, xw, lane);
       }
       auto stage = [&](int i, const float (&cur)[KS / 2], float (&ahead)[KS / 2]) -> bool {
         const int s = i % STAGES;
@@ -919,16 +911,14 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
           ++folded;
         }
         if constexpr (!kATma && !kACp) {
-          if (i + 2 < num_kb)
-            a_gather<AK, KS>(ahead, p, a_rb, g_first, (kb_begin + i + 2) * KS + p.k_off, xw, lane);
+          if (i + 2 < num_kb) a_gather<AK, KS>(ahead, p, a_rb, g_first, (kb_begin + i + 2) * KS, xw, lane);
         }
         // Warp-uniform outcome: tcgen05.ld/st are .sync.aligned.
         if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, wxf))) return false;
-        const int k0 = (kb_begin + i * kSubs) * KS;  // local (B rows)
-        const int ka = k0 + p.k_off;                   // global (structured A columns)
+        const int k0 = (kb_begin + i * kSubs) * KS;
         // (register-gathered A only with one k-block per stage)
-        if constexpr (!kATma && !kACp) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, ka, xw, lane);
-        if constexpr (kStaging) a_stage_convert_toeplitz_bf16(p, stg(s), a_hi(s), g_first, ka, t);
+        if constexpr (!kATma && !kACp) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
+        if constexpr (kStaging) a_stage_convert_toeplitz_bf16(p, stg(s), a_hi(s), g_first, k0, t);
         if constexpr (!kBTma) {
 #pragma unroll 1
           for (int j = 0; j < kSubs; ++j)
@@ -977,8 +967,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     }
     const bool acc_ok = __all_sync(0xffffffffu, last_ok && !*abort_flag);
     if (tr && t == 0) p.trace[kTrAccOk] = acc_ok ? 1u : 0u;
-    // Accumulating into C, a tile with nothing accumulated leaves C as it is.
-    if (acc_ok && !(no_k && p.accumulate)) {
+    if (acc_ok) {
       tc_fence_after_sync();
       const int row = m0 + q * 32 + lane;
       const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
@@ -1005,23 +994,6 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
           for (int j = 0; j < 16; ++j) p.trace[kTrAcc + j] = r[j];
         const int col = n0 + h * kHalf + c;
         if (row < p.M) {
-          if (p.accumulate) {  // C += product: one fp32 add (round to nearest) per element
-            if (vec && col + 16 <= p.N) {
-              const float4* src = reinterpret_cast<const float4*>(crow + col);
-#pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                const float4 c4 = src[v];
-                r[4 * v] = __float_as_uint(c4.x + __uint_as_float(r[4 * v]));
-                r[4 * v + 1] = __float_as_uint(c4.y + __uint_as_float(r[4 * v + 1]));
-                r[4 * v + 2] = __float_as_uint(c4.z + __uint_as_float(r[4 * v + 2]));
-                r[4 * v + 3] = __float_as_uint(c4.w + __uint_as_float(r[4 * v + 3]));
-              }
-            } else {
-#pragma unroll
-              for (int v = 0; v < 16; ++v)
-                if (col + v < p.N) r[v] = __float_as_uint(crow[col + v] + __uint_as_float(r[v]));
-            }
-          }
           if (vec && col + 16 <= p.N) {
             float4* dst = reinterpret_cast<float4*>(crow + col);
 #pragma unroll

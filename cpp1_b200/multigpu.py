@@ -16,8 +16,8 @@ packed U, Toeplitz generator, packed S):
 * the diagonal scale shards with no collective at all (rows independent).
 
 ``Communicator`` wraps libsmm's own NCCL communicator (``smm_mg_*``): each
-product call broadcasts B from the root in K-chunks on a high-priority
-stream and accumulates this rank's slab chunk by chunk as they land, so the
+product call broadcasts B from the root in column blocks on a high-priority
+stream and computes this rank's slab block by block as they land, so the
 transfer overlaps the tensor-core work inside one call.
 
 No kernel reads another GPU's memory; remote data reaches local HBM through
@@ -244,13 +244,14 @@ class Communicator:
 
     # ---- products (every rank calls them with the same shapes, mode and root)
     def gemm(self, A_slab, B, C_slab, mode: str = "3xtf32", root: int = 0, stream=None):
-        """C_slab = A_slab @ B with B broadcast from `root` (B is overwritten
-        with the root's data on the other ranks)."""
+        """C_slab = A_slab @ B with B broadcast from `root` (read on the root
+        only; other ranks pass a tensor of the same shape, whose content is
+        not used)."""
         L = self._lib.load()
         m = self._lib.MODES[mode]
         nrows, K = A_slab.shape
         N = B.shape[1]
-        ws, wsb = self._ws(L.smm_mg_gemm_workspace_size(nrows, N, K, m), B.device)
+        ws, wsb = self._ws(L.smm_mg_gemm_workspace_size(self.h, nrows, N, K, m), B.device)
         self._lib.check(L.smm_mg_gemm(self.h, A_slab.data_ptr(), B.data_ptr(), C_slab.data_ptr(), nrows, N, K, m,
                                       root, ws, wsb, self._stream(stream)), "smm_mg_gemm")
         return C_slab
@@ -261,7 +262,7 @@ class Communicator:
         m = self._lib.MODES[mode]
         N, ncols = B.shape
         nrows = C_slab.shape[0] if C_slab is not None else 0
-        ws, wsb = self._ws(L.smm_mg_upper_left_workspace_size(N, ncols, row0, nrows, m), B.device)
+        ws, wsb = self._ws(L.smm_mg_upper_left_workspace_size(self.h, N, ncols, nrows, m), B.device)
         cp = C_slab.data_ptr() if nrows else None
         self._lib.check(L.smm_mg_upper_left(self.h, U.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m, root,
                                             ws, wsb, self._stream(stream)), "smm_mg_upper_left")
@@ -273,7 +274,7 @@ class Communicator:
         m = self._lib.MODES[mode]
         N, ncols = B.shape
         nrows = C_slab.shape[0] if C_slab is not None else 0
-        ws, wsb = self._ws(L.smm_mg_toeplitz_left_workspace_size(N, ncols, m), B.device)
+        ws, wsb = self._ws(L.smm_mg_toeplitz_left_workspace_size(self.h, N, ncols, m), B.device)
         cp = C_slab.data_ptr() if nrows else None
         self._lib.check(L.smm_mg_toeplitz_left(self.h, g.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m,
                                                root, ws, wsb, self._stream(stream)), "smm_mg_toeplitz_left")
@@ -285,7 +286,7 @@ class Communicator:
         m = self._lib.MODES[mode]
         N = B.shape[0]
         nrows = A_slab.shape[0] if A_slab is not None else 0
-        ws, wsb = self._ws(L.smm_mg_symm_sandwich_workspace_size(N, nrows, m), B.device)
+        ws, wsb = self._ws(L.smm_mg_symm_sandwich_workspace_size(self.h, N, nrows, m), B.device)
         ap = A_slab.data_ptr() if nrows else None
         cp = C_slab.data_ptr() if nrows else None
         self._lib.check(L.smm_mg_symm_sandwich(self.h, ap, S.data_ptr(), B.data_ptr(), cp, N, nrows, m, root, ws,
@@ -302,12 +303,13 @@ def lib_row_slabs(n: int, world: int, triangular: bool = False) -> List[int]:
     return list(b)
 
 
-def lib_chunks(k: int, world: int) -> List[int]:
-    """The K-chunk boundaries the library's broadcasts use (smm_mg_chunks)."""
+def lib_chunks(ncols: int, world: int) -> List[int]:
+    """The column-block boundaries the library's broadcasts of B use
+    (smm_mg_chunks)."""
     import ctypes
     from . import _lib
     b = (ctypes.c_int * 17)()
-    nch = _lib.load().smm_mg_chunks(k, world, b)
+    nch = _lib.load().smm_mg_chunks(ncols, world, b)
     if nch < 1:
         _lib.check(nch if nch else 1, "smm_mg_chunks")
     return list(b)[: nch + 1]

@@ -185,12 +185,15 @@ int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float
 
 /* A product C = X B is partitioned by output row slabs, one per rank (GPU).
  * The shared right operand B lives on the root rank; inside each call it is
- * broadcast in K-chunks (row chunks of B) on the communicator's
- * high-priority stream, and this rank's slab is accumulated chunk by chunk
- * on `stream` as the chunks land, so the transfer of chunk j+1 overlaps the
- * tensor-core work on chunk j.  On every rank but the root, B is a device
- * buffer of the same shape that receives it (16-byte aligned rows).  Calls
- * are collective: every rank makes the same calls with the same shapes,
+ * broadcast in column blocks on the communicator's high-priority stream (the
+ * root packs each block contiguously into the workspace first), and this
+ * rank computes the block's columns of its slab as soon as the block has
+ * landed, on internal compute streams joined back into `stream` before the
+ * call's work ends, so the transfer of later blocks overlaps the tensor-core
+ * work on earlier ones.  Every output element comes from one full-K
+ * contraction: the slab equals the single-GPU entry point's rows.  B is read
+ * on the root only (16-byte aligned rows); the other ranks may pass NULL.
+ * Calls are collective: every rank makes the same calls with the same shapes,
  * mode and root, in the same order.  No kernel reads another GPU's memory.
  * The reference has no multi-GPU code; this is the row-slab partition with a
  * broadcast of the shared operand that its single-GPU kernels scale to.
@@ -206,7 +209,8 @@ int smm_mg_unique_id(void* id_out);
 /* Communicator of rank `rank` of `world` on the current device (collective:
  * blocks until every rank has joined). */
 int smm_mg_comm_init(smm_mg_comm** comm, int rank, int world, const void* id);
-/* Waits for this rank's collectives, then frees the communicator. */
+/* Waits for this rank's collectives and compute streams, then frees the
+ * communicator. */
 int smm_mg_comm_destroy(smm_mg_comm* comm);
 /* Frees the communicator without waiting for peers (a failed or departed
  * rank): pending collectives end with an error instead of blocking. */
@@ -218,31 +222,31 @@ int smm_mg_comm_status(smm_mg_comm* comm);
  * tiles, minimising the largest slab's work: rows cost 1, or N - i for an
  * upper-triangular left operand (triangular != 0). */
 int smm_mg_row_slabs(int N, int world, int triangular, int* bounds);
-/* K-chunk boundaries the calls use for a broadcast of K rows at this world
- * size (bounds needs 17 ints); returns the chunk count. */
-int smm_mg_chunks(int K, int world, int* bounds);
+/* Column-block boundaries the calls use for a broadcast of B's ncols columns
+ * at this world size (bounds needs 17 ints); returns the block count.
+ * SMM_MG_CHUNKS in the environment sets the count (1 .. 16; default 4). */
+int smm_mg_chunks(int ncols, int world, int* bounds);
 
 /* C_slab (nrows x N) = A_slab (nrows x K, this rank's rows of A) B (K x N). */
-size_t smm_mg_gemm_workspace_size(int nrows, int N, int K, int mode);
-int smm_mg_gemm(smm_mg_comm* comm, const float* A_slab, float* B, float* C_slab, int nrows, int N, int K, int mode,
-                int root, void* ws, size_t ws_bytes, void* stream);
+size_t smm_mg_gemm_workspace_size(const smm_mg_comm* comm, int nrows, int N, int K, int mode);
+int smm_mg_gemm(smm_mg_comm* comm, const float* A_slab, const float* B, float* C_slab, int nrows, int N, int K,
+                int mode, int root, void* ws, size_t ws_bytes, void* stream);
 /* C_slab (nrows x ncols) = U[row0 : row0+nrows, :] B, U packed upper (the whole
- * packed array on every rank; only the slab's rows are read).  B's chunks
- * travel last rows first: a slab needs only B's rows from row0 on. */
-size_t smm_mg_upper_left_workspace_size(int N, int ncols, int row0, int nrows, int mode);
-int smm_mg_upper_left(smm_mg_comm* comm, const float* U_packed, float* B, float* C_slab, int N, int ncols, int row0,
-                      int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
+ * packed array on every rank; only the slab's rows are read). */
+size_t smm_mg_upper_left_workspace_size(const smm_mg_comm* comm, int N, int ncols, int nrows, int mode);
+int smm_mg_upper_left(smm_mg_comm* comm, const float* U_packed, const float* B, float* C_slab, int N, int ncols,
+                      int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
 /* C_slab (nrows x ncols) = T[row0 : row0+nrows, :] B, T of generator g[2N-1]
  * (on every rank). */
-size_t smm_mg_toeplitz_left_workspace_size(int N, int ncols, int mode);
-int smm_mg_toeplitz_left(smm_mg_comm* comm, const float* g, float* B, float* C_slab, int N, int ncols, int row0,
-                         int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
-/* C_slab (nrows x N) = (A_slab S) B, S packed symmetric and B broadcast from
- * the root (S_packed and B are receive buffers on the other ranks): the
- * reference's run_graph order, (A S) then times B, per row slab. */
-size_t smm_mg_symm_sandwich_workspace_size(int N, int nrows, int mode);
-int smm_mg_symm_sandwich(smm_mg_comm* comm, const float* A_slab, float* S_packed, float* B, float* C_slab, int N,
-                         int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
+size_t smm_mg_toeplitz_left_workspace_size(const smm_mg_comm* comm, int N, int ncols, int mode);
+int smm_mg_toeplitz_left(smm_mg_comm* comm, const float* g, const float* B, float* C_slab, int N, int ncols,
+                         int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
+/* C_slab (nrows x N) = (A_slab S) B, S packed symmetric (the root's input; a
+ * receive buffer of N(N+1)/2 floats on the other ranks) and B broadcast from
+ * the root: the reference's run_graph order, (A S) then times B, per row slab. */
+size_t smm_mg_symm_sandwich_workspace_size(const smm_mg_comm* comm, int N, int nrows, int mode);
+int smm_mg_symm_sandwich(smm_mg_comm* comm, const float* A_slab, float* S_packed, const float* B, float* C_slab,
+                         int N, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
 
 /* ---- host-buffer contractions ------------------------------------------ */
 

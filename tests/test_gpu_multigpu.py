@@ -1,14 +1,14 @@
 """libsmm's multi-GPU products on two GPUs (skipped with fewer).
 
 Two processes, one per GPU.  Rank 0 holds B (and S for the sandwich); the
-other rank starts with NaN-filled receive buffers, so a slab is right only if
-the K-chunked broadcast inside the call delivered every chunk before the
+other rank passes NaN-filled buffers, so a slab is right only if the
+column-block broadcast inside the call delivered every block before the
 contraction that consumes it.  Each rank checks its own output slab against
 an fp64 recomputation of the whole product (torch float64 on its GPU,
 test-only), within the mode's bound: 3xTF32 1e-5, TF32 5e-3, bf16 1e-2.
-Shapes cover equal-work triangular slabs with last-first chunk order, a
-ragged last chunk (K not a multiple of the chunk), a chunk count forced by
-SMM_MG_CHUNKS, and the sandwich's S broadcast.  NVLS is off (NCCL_NVLS_ENABLE=0)
+Shapes cover equal-work triangular slabs, a ragged last block (a column
+count that is not a multiple of the block width), more blocks than internal
+compute streams (SMM_MG_CHUNKS=5), and the sandwich's S broadcast.  NVLS is off (NCCL_NVLS_ENABLE=0)
 and every rank issues the same calls in the same order."""
 import os
 import socket
@@ -72,8 +72,8 @@ def _worker(rank, world, port, results):
             R = dev(w["A"][r0:r1]).double() @ dev(w["B"]).double()
             errs[f"gemm_{mode}"] = _relerr(C, R)
 
-            # U B, packed U on every rank, equal-work slabs, chunks last-first; N not a chunk multiple
-            for n, ncols in ((4096, 1024), (1000, 512)):
+            # U B, packed U on every rank, equal-work slabs; ragged last column block
+            for n, ncols in ((4096, 1024), (1000, 1000)):
                 w = W.make_upper(n, ncols, seed=32)
                 b = MG.lib_row_slabs(n, world, triangular=True)
                 r0, r1 = b[rank], b[rank + 1]
@@ -85,9 +85,9 @@ def _worker(rank, world, port, results):
                 R = Ud[r0:r1] @ dev(w["B"]).double()
                 errs[f"upper{n}_{mode}"] = _relerr(C, R)
 
-            # T B with 5 chunks forced
+            # T B with 5 column blocks (more than the 4 compute streams)
             os.environ["SMM_MG_CHUNKS"] = "5"
-            n, ncols = 4096, 512
+            n, ncols = 4096, 2560
             w = W.make_toeplitz(n, ncols, seed=33)
             b = MG.lib_row_slabs(n, world)
             r0, r1 = b[rank], b[rank + 1]
@@ -128,9 +128,9 @@ def test_two_gpu_products_match_fp64(cuda):
         pytest.skip("needs two GPUs")
     world = 2
     port = _free_port()
-    with mp.Manager() as m:
+    ctx = mp.get_context("spawn")  # no fork after CUDA or thread start-up
+    with ctx.Manager() as m:
         results = m.dict()
-        ctx = mp.get_context("spawn")
         procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
         for p in procs:
             p.start()

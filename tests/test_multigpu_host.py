@@ -78,9 +78,9 @@ def _worker(rank, world, port, results):
 def test_two_rank_broadcast_slab_gather_gloo():
     world = 2
     port = _free_port()
-    with mp.Manager() as m:
+    ctx = mp.get_context("spawn")  # no fork after CUDA or thread start-up
+    with ctx.Manager() as m:
         results = m.dict()
-        ctx = mp.get_context("spawn")
         procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
         for p in procs:
             p.start()
@@ -131,9 +131,9 @@ def _sandwich_worker(rank, world, port, results):
 def test_two_rank_sandwich_slabs_gloo():
     world = 2
     port = _free_port()
-    with mp.Manager() as m:
+    ctx = mp.get_context("spawn")  # no fork after CUDA or thread start-up
+    with ctx.Manager() as m:
         results = m.dict()
-        ctx = mp.get_context("spawn")
         procs = [ctx.Process(target=_sandwich_worker, args=(r, world, port, results)) for r in range(world)]
         for p in procs:
             p.start()
@@ -151,10 +151,13 @@ def test_library_slabs_match_host_partition(world):
             assert MG.lib_row_slabs(n, world, tri) == MG.row_slabs(n, world, tri), (n, world, tri)
 
 
-@pytest.mark.parametrize("k,world", [(8192, 8), (16384, 8), (4096, 2), (1000, 2), (300, 4), (8192, 1)])
-def test_library_k_chunks(k, world):
-    kb = MG.lib_chunks(k, world)
-    assert kb[0] == 0 and kb[-1] == k
-    assert all(a < b for a, b in zip(kb, kb[1:]))
-    assert all(x % 256 == 0 for x in kb[:-1])  # k-block and TMA alignment in every mode
-    assert (len(kb) == 2) == (world == 1 or k <= 256)
+@pytest.mark.parametrize("ncols,world", [(8192, 8), (16384, 8), (4096, 2), (1000, 2), (300, 4), (8192, 1)])
+def test_library_column_blocks(ncols, world):
+    cb = MG.lib_chunks(ncols, world)
+    assert cb[0] == 0 and cb[-1] == ncols
+    assert all(a < b for a, b in zip(cb, cb[1:]))
+    assert all(x % 256 == 0 for x in cb[:-1])  # blocks start on whole output tiles
+    if world == 1 or ncols <= 256:
+        assert len(cb) == 2
+    else:
+        assert 2 <= len(cb) - 1 <= 4
