@@ -273,6 +273,14 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// 16-byte store to shared memory of any CTA of the cluster (address from
+// mapa_shared).
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c,
+                                              uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
 // Every thread of both CTAs; orders each CTA's prior writes (barrier
 // initialisation, tensor-memory allocation) before the other's later reads.
 __device__ __forceinline__ void cluster_sync_all() {

@@ -1,4 +1,5 @@
-// Contraction kernels with both operands TMA-loaded: dense GEMM and the dense-with-zeros upper-triangular left operand.
+// Contraction kernels with both operands TMA-loaded: dense GEMM (also split along K over CTA clusters for
+// products with few output tiles) and the dense-with-zeros upper-triangular left operand.
 #include "smm_launch.cuh"
 
 namespace smm {
@@ -7,6 +8,16 @@ int launch_kinds_dense(AKind ak, BKind bk, int bn, bool pair, int mode, const Ma
   if (ak == AKind::Dense && bk == BKind::Dense) return launch_bn<AKind::Dense, BKind::Dense>(bn, pair, mode, m, p, st);
   if (ak == AKind::UpperDense && bk == BKind::Dense) return launch_bn<AKind::UpperDense, BKind::Dense>(bn, pair, mode, m, p, st);
   return set_error(SMM_ERR_INVALID, "unsupported operand kinds");
+}
+
+int launch_dense_split(int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+  constexpr AKind A = AKind::Dense;
+  constexpr BKind B = BKind::Dense;
+  if (mode == SMM_MODE_3XTF32)
+    return launch_umma<A, B, Mode::TF32x3, 128, umma_stages<A, Mode::TF32x3, 128>(), false, 2>(m, p, st);
+  if (mode == SMM_MODE_BF16)
+    return launch_umma<A, B, Mode::BF16, 128, umma_stages<A, Mode::BF16, 128>(), false, 2>(m, p, st);
+  return launch_umma<A, B, Mode::TF32, 128, umma_stages<A, Mode::TF32, 128>(), false, 2>(m, p, st);
 }
 
 }  // namespace smm

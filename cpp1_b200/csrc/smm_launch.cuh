@@ -14,9 +14,10 @@ struct Maps {
   CUtensorMap a{}, b{}, al{}, bl{};
 };
 
-template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR>
+template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR, int SPLITK = 1>
 int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
-  auto kern = umma_gemm_kernel<AK, BK, MD, BN, STAGES, PAIR>;
+  auto kern = umma_gemm_kernel<AK, BK, MD, BN, STAGES, PAIR, SPLITK>;
+  constexpr int kCluster = PAIR ? 2 : SPLITK;
   constexpr int smem = umma_smem_bytes<AK, MD, PAIR ? BN / 2 : BN, STAGES>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
   static bool attr_set[64] = {};
@@ -27,9 +28,9 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
                  "cudaFuncSetAttribute(max dynamic smem)");
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const long long blocks = static_cast<long long>(p.row_tiles) * p.col_tiles * (PAIR ? 2 : 1);
+  const long long blocks = static_cast<long long>(p.row_tiles) * p.col_tiles * kCluster;
   if (blocks > 0x7FFFFFFFLL) return set_error(SMM_ERR_INVALID, "product too large for one launch");
-  if constexpr (PAIR) {
+  if constexpr (kCluster > 1) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
     cfg.blockDim = dim3(umma_threads(AK, MD), 1, 1);
@@ -37,12 +38,12 @@ int launch_umma(const Maps& m, const UmmaParams& p, cudaStream_t st) {
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.x = kCluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    SMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.al, m.bl, p), "tcgen05 pair contraction launch");
+    SMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, m.al, m.bl, p), "tcgen05 cluster contraction launch");
   } else {
     kern<<<static_cast<unsigned>(blocks), umma_threads(AK, MD), smem, st>>>(m.a, m.b, m.al, m.bl, p);
   }
@@ -74,6 +75,10 @@ int launch_bn(int bn, bool pair, int mode, const Maps& m, const UmmaParams& p, c
     default: return launch_mode<AK, BK, 64, false>(mode, m, p, st);
   }
 }
+
+// Dense x Dense with 128 x 128 tiles, each split over two CTAs along K
+// (smm_kern_dense.cu).
+int launch_dense_split(int mode, const Maps& m, const UmmaParams& p, cudaStream_t st);
 
 // One launcher per translation unit; each returns SMM_ERR_INVALID for
 // pairings it does not hold.

@@ -143,6 +143,20 @@ int pick_bn(int M, int N, bool pair) {
   return 64;
 }
 
+// Split the K range of each 128 x 128 output tile over a cluster of two
+// CTAs: dense x dense products whose single-CTA tiles fill well under a
+// wave (at most 74 tiles of 148 SMs) and whose K range gives each half at
+// least 16 k-blocks.  SMM_SPLITK=0 disables it, SMM_SPLITK=2 forces it for
+// every dense product without CTA pairs.
+bool use_split(AKind ak, BKind bk, const Operand& a, const Operand& b, bool pair, int M, int N, int K) {
+  if (ak != AKind::Dense || bk != BKind::Dense || pair || a.lower || b.tri != 0) return false;
+  const char* e = std::getenv("SMM_SPLITK");
+  if (e && e[0] == '0') return false;
+  if (e && e[0] == '2') return true;
+  const long long tiles = static_cast<long long>((M + kBM - 1) / kBM) * ((N + 127) / 128);
+  return tiles <= 74 && K >= 512;
+}
+
 // Diagnostic record target for the next contraction launch (set by
 // smm_debug_trace_next, consumed by one launch).
 thread_local uint32_t* g_trace = nullptr;
@@ -169,7 +183,8 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
                     int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16) {
   const bool bf16 = (mode == SMM_MODE_BF16);
   const bool pair = use_pairs(M, N);
-  const int bn = pick_bn(M, N, pair);
+  const bool split = use_split(ak, bk, a, b, pair, M, N, K);
+  const int bn = split ? 128 : pick_bn(M, N, pair);
   Maps m;
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);
@@ -217,7 +232,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   g_ev_before = g_ev_after = nullptr;
   if (!p.status) return set_error(SMM_ERR_CUDA, "device status word unavailable");
   if (ev_before) SMM_CUDA_TRY(cudaEventRecord(ev_before, st), "record event before the contraction");
-  const int rc = launch_kinds(ak, bk, bn, pair, mode, m, p, st);
+  const int rc = split ? launch_dense_split(mode, m, p, st) : launch_kinds(ak, bk, bn, pair, mode, m, p, st);
   if (rc == SMM_OK && ev_after) SMM_CUDA_TRY(cudaEventRecord(ev_after, st), "record event after the contraction");
   return rc;
 }

@@ -556,11 +556,20 @@ __device__ __forceinline__ void b_build(const UmmaParams& p, uint8_t* bh, uint8_
 // `acc_full` and `accum_full` barriers of both CTAs (one commit per CTA), and
 // the fold warps of both CTAs arrive on the leader's `acc_empty`.  No load is
 // multicast.
-template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR = false>
+//
+// SPLITK (single-CTA tiles only): clusters of SPLITK = 2 CTAs compute the
+// same 128 x BN tile over the two halves of its k-block range (whole stages
+// each), each in its own tensor memory with its own pipeline.  After both
+// pipelines are done, CTA 1 writes its result rows into CTA 0's stage memory
+// (distributed shared memory), and CTA 0 adds them to its own, in that fixed
+// order, and stores C: twice the CTAs for a product with few output tiles,
+// the same result on every run.
+template <AKind AK, BKind BK, Mode MD, int BN, int STAGES, bool PAIR = false, int SPLITK = 1>
 __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmAl, const __grid_constant__ CUtensorMap tmBl,
                      const UmmaParams p) {
+  static_assert(SPLITK == 1 || (SPLITK == 2 && !PAIR), "split-K clusters of two single-CTA tiles");
   using MT = ModeTraits<MD>;
   constexpr bool SPLIT3 = MT::kSplit3;
   constexpr int KS = MT::kStageK;
@@ -608,6 +617,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const uint32_t krank = SPLITK > 1 ? cluster_ctarank() : 0u;  // this CTA's half of the K range
   const bool leader = (rank == 0);
   // shared::cluster address of a barrier of this CTA in CTA `r` of the pair
   auto in_cta = [&](uint64_t* bar, uint32_t r) { return mapa_shared(smem_u32(bar), r); };
@@ -619,7 +629,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // a row tile is 256 rows and both CTAs take the same tile.
   int m_tile, n_tile;
   {
-    const int b = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int b = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x) / SPLITK;
     const int per_group = p.raster_group * p.col_tiles;
     const int g = b / per_group;
     const int first = g * p.raster_group;
@@ -646,6 +656,14 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // above it: the tile needs k >= n0 only.
   if (BK == BKind::UpperPacked || (BK == BKind::Dense && p.b_tri == 1)) kb_end = min(kb_end, (n0 + BN - 1) / KS + 1);
   if (BK == BKind::LowerPacked || (BK == BKind::Dense && p.b_tri == 2)) kb_begin = max(kb_begin, n0 / KS);
+  if constexpr (SPLITK > 1) {
+    // Runs of whole stages, so neither CTA reads into the other's k-blocks.
+    const int total = max(kb_end - kb_begin, 0);
+    const int per = ((total + SPLITK - 1) / SPLITK + kSubs - 1) / kSubs * kSubs;
+    const int b0 = kb_begin + static_cast<int>(krank) * per;
+    kb_end = min(kb_end, b0 + per);
+    kb_begin = min(b0, kb_end);
+  }
   // Empty for a tile of L1 L2 wholly above the diagonal: it is written as
   // zeros.  num_kb counts stages of kSubs k-blocks; a last stage reaching
   // past kb_end multiplies zeros (past K, past a triangle's diagonal).
@@ -709,6 +727,66 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     else
       mbar_arrive(bar);
   };
+
+  // Epilogue helpers of the transform warps: warp w reads TMEM lanes
+  // 32 (w % 4).. and column half ((w - 2) / 4) of the tile.
+  const int eq = warp & 3;
+  const int eh = ((threadIdx.x - 64) >> 5) >> 2;
+  const uint32_t e_acc = tmem_base + (static_cast<uint32_t>(eq * 32) << 16) + static_cast<uint32_t>(eh * kHalf);
+  const uint32_t e_sum = e_acc + static_cast<uint32_t>(BN);
+  const bool no_k = num_kb == 0;  // nothing accumulated: the tile is zero
+  // Result columns c .. c+15 of this thread's row: the running sum (chunks
+  // [0, nch-1)) + the last chunk's accumulator.
+  auto final16 = [&](int c, uint32_t (&r)[16]) {
+    if (no_k) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) r[j] = 0u;
+      return;
+    }
+    tmem_ld_32x32b_x16(e_acc + c, r);
+    if (SPLIT3 && nch > 1) {
+      uint32_t s16[16];
+      tmem_ld_32x32b_x16(e_sum + c, s16);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(s16[j]) + __uint_as_float(r[j]));
+    } else {
+      tmem_wait_ld();
+    }
+  };
+  // Store 16 result columns (col ..) of output row `row` to C (and its bf16 /
+  // lo copies when requested).
+  auto store16 = [&](int row, int col, const uint32_t (&r)[16]) {
+    if (row >= p.M) return;
+    const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+    float* crow = p.C + static_cast<long long>(row) * p.ldc;
+    if (vec && col + 16 <= p.N) {
+      float4* dst = reinterpret_cast<float4*>(crow + col);
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
+                             __uint_as_float(r[4 * v + 3]));
+    } else {
+#pragma unroll
+      for (int v = 0; v < 16; ++v)
+        if (col + v < p.N) crow[col + v] = __uint_as_float(r[v]);
+    }
+    if (p.C_bf16 != nullptr) {
+      __nv_bfloat16* brow = p.C_bf16 + static_cast<long long>(row) * p.ldc_bf16;
+#pragma unroll
+      for (int v = 0; v < 16; ++v)
+        if (col + v < p.N) brow[col + v] = __float2bfloat16_rn(__uint_as_float(r[v]));
+    }
+    if (p.C_lo != nullptr) {
+      float* lrow = p.C_lo + static_cast<long long>(row) * p.ldc;
+#pragma unroll
+      for (int v = 0; v < 16; ++v) {
+        const float x = __uint_as_float(r[v]);
+        if (col + v < p.N) lrow[col + v] = x - tf32_hi(x);
+      }
+    }
+  };
+  bool acc_valid = false;  // transform warps: the accumulator holds this CTA's result
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -956,9 +1034,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     }
 
     // ------------------------------------------------------------ epilogue
-    // Result = running sum (chunks [0, nch-1)) + the last chunk's accumulator.
     bool last_ok = ok;
-    const bool no_k = num_kb == 0;  // nothing accumulated: the tile is zero
     if (!no_k) {
       if constexpr (SPLIT3)
         last_ok = last_ok && mbar_wait(acc_full, (nch - 1) & 1, wepi);
@@ -966,68 +1042,70 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         last_ok = last_ok && mbar_wait(accum_full, 0, wepi);
     }
     const bool acc_ok = __all_sync(0xffffffffu, last_ok && !*abort_flag);
+    acc_valid = acc_ok;
     if (tr && t == 0) p.trace[kTrAccOk] = acc_ok ? 1u : 0u;
-    if (acc_ok) {
+    if (SPLITK == 1 && acc_ok) {
       tc_fence_after_sync();
       const int row = m0 + q * 32 + lane;
-      const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
-      float* crow = p.C + static_cast<long long>(row) * p.ldc;
 #pragma unroll 1
       for (int c = 0; c < kHalf; c += 16) {
         uint32_t r[16];
-        if (no_k) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = 0u;
-        } else {
-        tmem_ld_32x32b_x16(acc_col + c, r);
-        if (SPLIT3 && nch > 1) {
-          uint32_t s16[16];
-          tmem_ld_32x32b_x16(sum_col + c, s16);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__uint_as_float(s16[j]) + __uint_as_float(r[j]));
-        } else {
-          tmem_wait_ld();
-        }
-        }
+        final16(c, r);
         if (tr && q == 0 && lane == 0 && h == 0 && c == 0)
           for (int j = 0; j < 16; ++j) p.trace[kTrAcc + j] = r[j];
-        const int col = n0 + h * kHalf + c;
-        if (row < p.M) {
-          if (vec && col + 16 <= p.N) {
-            float4* dst = reinterpret_cast<float4*>(crow + col);
+        store16(row, n0 + h * kHalf + c, r);
+      }
+    }
+  }
+
+  if constexpr (SPLITK > 1) {
+    // Combine the two halves of the K range: CTA 1's results go to CTA 0's
+    // stage memory (free once both pipelines are done: every MMA has
+    // completed, so every loaded stage was consumed), CTA 0 adds them to its
+    // own and stores C.  Every thread of both CTAs passes both barriers.
+    constexpr int kXld = BN + 4;  // row stride (floats) of the exchange tile: 16-byte rows, few bank conflicts
+    static_assert(kBM * kXld * 4 <= STAGES * kStage, "exchange tile fits the stage memory");
+    float* xbuf = reinterpret_cast<float*>(smem);
+    const bool xf = warp >= 2 && warp < 2 + kXformThreads / 32;
+    const int xrow = eq * 32 + lane;  // tile row of this transform thread
+    tc_fence_before_sync();
+    cluster_sync_all();
+    tc_fence_after_sync();
+    if (xf && krank == 1 && acc_valid) {
+#pragma unroll 1
+      for (int c = 0; c < kHalf; c += 16) {
+        uint32_t r[16];
+        final16(c, r);
+        const uint32_t dst = mapa_shared(smem_u32(xbuf + xrow * kXld + eh * kHalf + c), 0);
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-          } else {
+        for (int v = 0; v < 4; ++v) st_cluster_v4(dst + 16 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+      }
+    }
+    cluster_sync_all();
+    if (xf && krank == 0 && acc_valid) {
+#pragma unroll 1
+      for (int c = 0; c < kHalf; c += 16) {
+        uint32_t r[16];
+        final16(c, r);
+        const float4* src = reinterpret_cast<const float4*>(xbuf + xrow * kXld + eh * kHalf + c);
 #pragma unroll
-            for (int v = 0; v < 16; ++v)
-              if (col + v < p.N) crow[col + v] = __uint_as_float(r[v]);
-          }
-          if (p.C_bf16 != nullptr) {
-            __nv_bfloat16* brow = p.C_bf16 + static_cast<long long>(row) * p.ldc_bf16;
-#pragma unroll
-            for (int v = 0; v < 16; ++v)
-              if (col + v < p.N) brow[col + v] = __float2bfloat16_rn(__uint_as_float(r[v]));
-          }
-          if (p.C_lo != nullptr) {
-            float* lrow = p.C_lo + static_cast<long long>(row) * p.ldc;
-#pragma unroll
-            for (int v = 0; v < 16; ++v) {
-              const float x = __uint_as_float(r[v]);
-              if (col + v < p.N) lrow[col + v] = x - tf32_hi(x);
-            }
-          }
+        for (int v = 0; v < 4; ++v) {
+          const float4 o = src[v];
+          r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + o.x);
+          r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + o.y);
+          r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + o.z);
+          r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + o.w);
         }
+        store16(m0 + xrow, n0 + eh * kHalf + c, r);
       }
     }
   }
 
   tc_fence_before_sync();
-  if constexpr (PAIR) {
+  if constexpr (PAIR || SPLITK > 1) {
     // Neither CTA leaves while the leader's MMAs may still read the other's
-    // shared memory or the other may still arrive on the leader's barriers.
+    // shared memory or the other may still arrive on the leader's barriers
+    // (pair), or access the other's shared memory (split).
     cluster_sync_all();
   } else {
     __syncthreads();

@@ -97,6 +97,25 @@ def test_gemm_shapes(cuda, mode, mnk):
     assert _relerr_full(C, R) <= TOL[mode], (mnk, _relerr_full(C, R))
 
 
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
+@pytest.mark.parametrize("mnk", [(1, 1, 1), (128, 128, 32), (7, 129, 257), (300, 200, 1000), (1024, 1024, 1024),
+                                 (1000, 1000, 4100)])
+def test_gemm_split_k_clusters(cuda, monkeypatch, mode, mnk):
+    """Each 128 x 128 tile split along K over a cluster of two CTAs (the
+    small-product form; SMM_SPLITK=2 forces it): ranges of whole stages, an
+    empty second half for short K, ragged M, N and K.  Same bound as the
+    unsplit product, and the same result on a second run."""
+    monkeypatch.setenv("SMM_SPLITK", "2")
+    M, N, K = mnk
+    w = W.make_gemm(M, N, K, seed=M + 3 * N + 5 * K)
+    A, B = dev(w["A"]), dev(w["B"])
+    C = host(ops.gemm(A, B, mode=mode))
+    rows = np.unique(np.linspace(0, M - 1, min(M, 64)).astype(np.int32))
+    R = O.gemm_rows_f64(w["A"], w["B"], rows)
+    assert _relerr_full(C[rows], R) <= TOL[mode], (mnk, _relerr_full(C[rows], R))
+    assert np.array_equal(host(ops.gemm(A, B, mode=mode)), C)
+
+
 def test_tf32_operand_reading_truncates(cuda):
     """kind::tf32 must ignore the 13 low mantissa bits of an fp32 operand
     (truncation): the 3xTF32 split relies on hi = raw bits & 0xffffe000.
