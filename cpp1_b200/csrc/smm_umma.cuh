@@ -100,10 +100,12 @@ __host__ __device__ constexpr bool a_async_filled(AKind ak, Mode md) {
   return ak != AKind::Dense && ak != AKind::UpperDense && (md != Mode::BF16 || ak == AKind::Toeplitz);
 }
 __host__ __device__ constexpr bool a_staged(AKind ak, Mode md) { return ak == AKind::Toeplitz && md == Mode::BF16; }
-// bf16 Toeplitz staging: generator elements [lo, lo + 159) of a k-block
-// (lo = n - 1 - (last row) + k0) from the 16-byte boundary at or below lo:
-// 41 chunks of 16 bytes, in a 1 KiB slot (stages stay 1 KiB aligned).
-constexpr int kStgGenChunks = 41;
+// bf16 Toeplitz staging: the generator elements [lo, lo + 127 + 32 subs)
+// that the 128 rows of `subs` consecutive k-blocks slide over (lo = n - 1 -
+// (last row) + k0), from the 16-byte boundary at or below lo: 41 chunks of 16
+// bytes for one k-block, 49 for two; a 1 KiB slot per k-block of the stage
+// (stages stay 1 KiB aligned).
+__host__ __device__ constexpr int stg_gen_chunks(int subs) { return (130 + 32 * subs + 3) / 4; }
 constexpr int kStgBytes = 1024;
 // Threads per CTA: producer, MMA and 8 transform warps, plus the 2 fill warps
 // when the kernel has them.
@@ -169,10 +171,14 @@ __host__ __device__ constexpr uint32_t tmem_cols() {
 // Each of those instructions costs that thread ~60 cycles, about half of a
 // 2-MMA stage's tensor time in one-pass modes.  3xTF32 with three blocks (two
 // stages) measured slower.  bf16 structured A, gathered through registers one
-// k-block at a time, keeps one.
+// k-block at a time, keeps one; bf16 Toeplitz A, staged as one generator
+// window per stage, takes two (the MMA issuer's overhead per stage is then
+// spread over 4 MMAs, and the window grows by 32 elements only).
 template <AKind AK, Mode MD, int BCOLS>
 __host__ __device__ constexpr int umma_subs() {
-  return (AK != AKind::Dense && AK != AKind::UpperDense && MD == Mode::BF16)
+  return (AK == AKind::Toeplitz && MD == Mode::BF16)
+             ? 2
+         : (AK != AKind::Dense && AK != AKind::UpperDense && MD == Mode::BF16)
              ? 1
              : ((AK == AKind::Dense || AK == AKind::UpperDense) && MD != Mode::TF32x3 &&
                 3 * 4 * stage_bytes<BCOLS, false>() <= 192 * 1024)
@@ -421,14 +427,18 @@ __device__ __forceinline__ long long toeplitz_lo(long long n, int g_first, int k
   return n - 1 - (g_first + kBM - 1) + k0;
 }
 
-// Stage the generator window of one bf16 k-block (32 k from k0) of this
-// CTA's Toeplitz rows g_first..: 41 aligned 16-byte chunks, one per fill
-// thread.  A chunk wholly outside the generator [g, g + 2n - 1) is skipped
-// (the conversion never reads it); one that overlaps either end is copied
-// element by element, so no byte outside the generator is read.
+// Stage the generator window of SUBS bf16 k-blocks (32 SUBS k from k0) of
+// this CTA's Toeplitz rows g_first..: stg_gen_chunks(SUBS) aligned 16-byte
+// chunks, one per fill thread.  A chunk wholly outside the generator
+// [g, g + 2n - 1) is skipped (the conversion never reads it); one that
+// overlaps either end is copied element by element, so no byte outside the
+// generator is read.
+template <int SUBS>
 __device__ __forceinline__ void a_stage_fill_toeplitz_bf16(const UmmaParams& p, uint8_t* stg, int g_first, int k0,
                                                            int ft) {
-  if (ft >= kStgGenChunks) return;
+  static_assert(stg_gen_chunks(SUBS) <= kAFillThreads && 16 * stg_gen_chunks(SUBS) <= SUBS * kStgBytes,
+                "window chunks: one per fill thread, inside the stage's slots");
+  if (ft >= stg_gen_chunks(SUBS)) return;
   const long long n = p.a_dim;
   const uintptr_t b = reinterpret_cast<uintptr_t>(p.a_src);
   const uintptr_t e = b + 4 * static_cast<uintptr_t>(2 * n - 1);
@@ -446,12 +456,13 @@ __device__ __forceinline__ void a_stage_fill_toeplitz_bf16(const UmmaParams& p, 
   }
 }
 
-// bf16 A tile (128 rows x 32 k, 64-byte swizzle) from the staged window:
-// element (row r, k0 + kk) is window element (127 - r) + kk.  Each transform
-// thread converts 4 groups of 4 consecutive k of one row (rows t/8 + 32 it,
-// columns 4 (t % 8)..), zero outside the matrix.
+// bf16 A tile (128 rows x 32 k, 64-byte swizzle) of the k-block at
+// k0 + jofs from the window staged for the stage starting at k0: element
+// (row r, k0 + jofs + kk) is window element (127 - r) + jofs + kk.  Each
+// transform thread converts 4 groups of 4 consecutive k of one row (rows
+// t/8 + 32 it, columns 4 (t % 8)..), zero outside the matrix.
 __device__ __forceinline__ void a_stage_convert_toeplitz_bf16(const UmmaParams& p, const uint8_t* stg, uint8_t* ah,
-                                                              int g_first, int k0, int t) {
+                                                              int g_first, int k0, int jofs, int t) {
   const long long n = p.a_dim;
   const float* sf = reinterpret_cast<const float*>(stg);
   const int off =
@@ -461,10 +472,10 @@ __device__ __forceinline__ void a_stage_convert_toeplitz_bf16(const UmmaParams& 
   for (int it = 0; it < 4; ++it) {
     const int r = it * 32 + (t >> 3);
     const bool row_in = g_first + r < n;
-    const float* w = sf + off + (kBM - 1 - r) + kk0;
+    const float* w = sf + off + (kBM - 1 - r) + jofs + kk0;
     float v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = (row_in && k0 + kk0 + j < n) ? w[j] : 0.0f;
+    for (int j = 0; j < 4; ++j) v[j] = (row_in && k0 + jofs + kk0 + j < n) ? w[j] : 0.0f;
     __nv_bfloat162 lo2 = __floats2bfloat162_rn(v[0], v[1]), hi2 = __floats2bfloat162_rn(v[2], v[3]);
     uint2 pk;
     pk.x = *reinterpret_cast<uint32_t*>(&lo2);
@@ -579,7 +590,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // kSubs | B lo x kSubs], each block in the one-block layouts below.
   constexpr int kSubs = umma_subs<AK, MD, kBCols>();
   constexpr bool kStaging = a_staged(AK, MD);  // bf16 Toeplitz: fp32 generator window after the tiles
-  static_assert(!kStaging || kSubs == 1, "staged A converts one k-block per stage");
+  static_assert(!kStaging || kSubs <= 2, "staged A: one generator window per stage");
   constexpr int kStage = umma_stage_bytes<AK, MD, kBCols>();
   constexpr int kChunkS = kChunk / kSubs;  // chunk length in stages
   static_assert(kChunk % kSubs == 0, "chunk of whole stages");
@@ -907,7 +918,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         const uint32_t ph = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
         if constexpr (kStaging) {
-          a_stage_fill_toeplitz_bf16(p, stg(s), g_first, (kb_begin + i) * KS, ft);
+          a_stage_fill_toeplitz_bf16<kSubs>(p, stg(s), g_first, (kb_begin + i * kSubs) * KS, ft);
         } else {
 #pragma unroll
           for (int j = 0; j < kSubs; ++j)
@@ -996,7 +1007,11 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         const int k0 = (kb_begin + i * kSubs) * KS;
         // (register-gathered A only with one k-block per stage)
         if constexpr (!kATma && !kACp) a_store<AK, MD>(cur, a_hi(s), a_lo(s), g_first, k0, xw, lane);
-        if constexpr (kStaging) a_stage_convert_toeplitz_bf16(p, stg(s), a_hi(s), g_first, k0, t);
+        if constexpr (kStaging) {
+#pragma unroll
+          for (int j = 0; j < kSubs; ++j)
+            a_stage_convert_toeplitz_bf16(p, stg(s), a_hi(s) + j * kATileBytes, g_first, k0, j * KS, t);
+        }
         if constexpr (!kBTma) {
 #pragma unroll 1
           for (int j = 0; j < kSubs; ++j)
