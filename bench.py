@@ -633,6 +633,7 @@ def roofline(op, n, mode, step, stream, peaks, kernel_useful, call_ms, world, L,
                 clk.summary())
 
     burst_reps = int(min(200, max(3, math.ceil(50.0 / max(call_ms, 1e-3)))))
+    time.sleep(1.0)  # idle first: the burst runs at the clocks of a rested GPU, not under the power cap
     sus_reps = int(min(4000, max(3, math.ceil(1000.0 * seconds / max(call_ms, 1e-3)))))
     launch_ms, whole_ms, clocks = run(burst_reps)
     s_launch_ms, s_whole_ms, s_clocks = run(sus_reps) if seconds > 0 else (None, None, None)

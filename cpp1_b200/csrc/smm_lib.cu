@@ -221,7 +221,11 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.b_dim = b.dim;
   p.row_tiles = pair ? (M + 2 * kBM - 1) / (2 * kBM) : (M + kBM - 1) / kBM;
   p.col_tiles = (N + bn - 1) / bn;
-  p.raster_group = 8;
+  // Rasterisation group (row tiles per group): 8 balances the re-reads of
+  // A and B for TMA-fed operands (a wave of 74 pair tiles spans ~8 x 9
+  // tiles); a Toeplitz A is built on chip from a generator that stays in L2,
+  // so a group spans every row tile and each B column slab is read once.
+  p.raster_group = ak == AKind::Toeplitz ? std::max(p.row_tiles, 1) : 8;
   p.status = device_status_word();
   p.wait_limit_ns = g_wait_next ? g_wait_next : wait_limit_ns();
   p.drain_limit_ns = std::max(p.wait_limit_ns, kMinDrainNs);
