@@ -75,3 +75,23 @@ def test_compat_reports_invalid_arguments(cuda):
     gf, ms = ctypes.c_float(), ctypes.c_float()
     rc = _lib.load().smm_compat_gen_x_gen(None, None, None, ctypes.addressof(gf), 64, ctypes.addressof(ms))
     assert rc == _lib.SMM_ERR_INVALID
+
+
+def test_generated_wrapper_order_of_the_reference_runner(cuda):
+    """cpp1_b200.compat.generated_wrapper takes the arguments the way the
+    reference's runner passes them (sorted names: C = U @ B gives B_data,
+    C_data, U_data, gflops_out, n, time_ms_out) and matches the primary
+    entry point bit for bit."""
+    from cpp1_b200 import compat
+    n = 320
+    U, B = rnd(n * (n + 1) // 2, 21), rnd((n, n), 22)
+    C = torch.full((n, n), float("nan"), device="cuda")
+    arg_names = sorted(["U_data", "B_data", "C_data", "n", "gflops_out", "time_ms_out"])
+    fn = compat.generated_wrapper(arg_names, "U", "B", "C", "upper", "gen")
+    gf, ms = ctypes.c_float(), ctypes.c_float()
+    by_name = {"U_data": ctypes.c_void_p(U.data_ptr()), "B_data": ctypes.c_void_p(B.data_ptr()),
+               "C_data": ctypes.c_void_p(C.data_ptr()), "n": ctypes.c_int(n), "gflops_out": ctypes.byref(gf),
+               "time_ms_out": ctypes.byref(ms)}
+    fn(*[by_name[a] for a in arg_names])
+    assert torch.equal(C, ops.upper_left(U, B))
+    assert ms.value > 0 and gf.value > 0
