@@ -107,23 +107,6 @@ __host__ __device__ constexpr bool a_staged(AKind ak, Mode md) { return ak == AK
 // (stages stay 1 KiB aligned).
 __host__ __device__ constexpr int stg_gen_chunks(int subs) { return (130 + 32 * subs + 3) / 4; }
 constexpr int kStgBytes = 1024;
-// fp32 modes, packed (upper / symmetric / lower) and Toeplitz A: each k-block
-// of a tile that lies wholly on one side of the diagonal is staged with
-// 16-byte copies of whole memory segments (a_vstage_fill) and shifted into
-// the swizzled tile by the transform warps.  Slot of one k-block: 128 row
-// segments of 16 floats (5 chunks, 80 bytes each) or 16 mirrored column
-// segments of 128 floats (33 chunks, 528 bytes each), whichever is larger.
-constexpr int kVRowChunks = 5, kVColChunks = 33;
-constexpr int kVStgBytes = 10240;
-static_assert(128 * kVRowChunks * 16 <= kVStgBytes && 16 * kVColChunks * 16 <= kVStgBytes, "vector staging slot");
-__host__ __device__ constexpr bool a_vstaged(AKind ak, Mode md) {
-  return md != Mode::BF16 &&
-         (ak == AKind::UpperPacked || ak == AKind::SymmPacked || ak == AKind::LowerPacked || ak == AKind::Toeplitz);
-}
-// Staging bytes per k-block of a stage.
-__host__ __device__ constexpr int a_stage_slot(AKind ak, Mode md) {
-  return a_staged(ak, md) ? kStgBytes : (a_vstaged(ak, md) ? kVStgBytes : 0);
-}
 // Threads per CTA: producer, MMA and 8 transform warps, plus the 2 fill warps
 // when the kernel has them.
 __host__ __device__ constexpr int umma_threads(AKind ak, Mode md) { return a_async_filled(ak, md) ? 384 : 320; }
@@ -170,9 +153,9 @@ struct TileGeom {
   static constexpr int kBChunkBytes = 16 * 128;     // one 32-column box
 };
 
-template <int BN, bool SPLIT3, int STG = 0>
+template <int BN, bool SPLIT3, bool STAGING = false>
 __host__ __device__ constexpr int stage_bytes() {
-  return (SPLIT3 ? 2 : 1) * (kATileBytes + TileGeom<BN>::kBTileBytes) + STG;
+  return (SPLIT3 ? 2 : 1) * (kATileBytes + TileGeom<BN>::kBTileBytes) + (STAGING ? kStgBytes : 0);
 }
 
 template <int BN, bool SPLIT3>
@@ -200,12 +183,12 @@ __host__ __device__ constexpr int umma_subs() {
              : ((AK == AKind::Dense || AK == AKind::UpperDense) && MD != Mode::TF32x3 &&
                 3 * 4 * stage_bytes<BCOLS, false>() <= 192 * 1024)
                    ? 4  // one-pass modes on TMA-fed operands: 8 MMAs per stage
-                   : (3 * 2 * stage_bytes<BCOLS, MD == Mode::TF32x3, a_stage_slot(AK, MD)>() <= 192 * 1024 ? 2 : 1);
+                   : (3 * 2 * stage_bytes<BCOLS, MD == Mode::TF32x3>() <= 192 * 1024 ? 2 : 1);
 }
 // Bytes of one pipeline stage.
 template <AKind AK, Mode MD, int BCOLS>
 __host__ __device__ constexpr int umma_stage_bytes() {
-  return umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3, a_stage_slot(AK, MD)>();
+  return umma_subs<AK, MD, BCOLS>() * stage_bytes<BCOLS, MD == Mode::TF32x3, a_staged(AK, MD)>();
 }
 // Pipeline stages: as many as fit into 192 KiB, at most 8.
 template <AKind AK, Mode MD, int BCOLS>
@@ -437,129 +420,6 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
   }
 }
 
-// ---------------------------------------------------------------- vector-staged A (fp32 modes)
-// Which form a k-block (k0 .. k0+15) of the tile rows g_first .. g_first+127
-// takes: 1 = every row's 16 elements are one contiguous memory segment (a
-// packed row right of an upper / symmetric diagonal or left of a lower one,
-// or a Toeplitz generator window); 2 = symmetric block wholly below the
-// diagonal, every column's 128 elements one contiguous segment (packed row k
-// from g_first); 0 = the block crosses the diagonal (element by element).
-template <AKind AK>
-__device__ __forceinline__ int a_vclass(int g_first, int k0) {
-  if constexpr (AK == AKind::Toeplitz) return 1;
-  if constexpr (AK == AKind::LowerPacked) return (k0 + kBK - 1 <= g_first) ? 1 : 0;
-  if (AK == AKind::SymmPacked && k0 + kBK <= g_first) return 2;
-  return (k0 >= g_first + kBM - 1) ? 1 : 0;
-}
-
-// Offset of element (gr, 0) of a class-1 row in the operand's storage
-// (packed upper / symmetric row start minus gr, packed lower row start, or
-// n - 1 - gr in the generator), and the storage length in floats.
-template <AKind AK>
-__device__ __forceinline__ long long a_vrow_base(long long gr, long long n) {
-  if constexpr (AK == AKind::Toeplitz) return n - 1 - gr;
-  else if constexpr (AK == AKind::LowerPacked) return gr * (gr + 1) / 2;
-  else return gr * n - gr * (gr - 1) / 2 - gr;
-}
-template <AKind AK>
-__device__ __forceinline__ long long a_vlen(long long n) {
-  return AK == AKind::Toeplitz ? 2 * n - 1 : n * (n + 1) / 2;
-}
-
-// One 16-byte chunk at element address e (chunk-aligned) of storage [0, len)
-// into shared memory: whole inside -> one 16-byte cp.async; across an end ->
-// the inside elements one by one; wholly outside -> nothing (the conversion
-// never reads it).
-__device__ __forceinline__ void vchunk(uint32_t dst, const float* src, long long e, long long len) {
-  if (e + 4 <= 0 || e >= len) return;
-  if (e >= 0 && e + 4 <= len) {
-    cp_async_16(dst, src + e);
-    return;
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    if (e + j >= 0 && e + j < len) cp_async_4(dst + 4 * j, src + e + j, 4u);
-}
-
-// Fill warps: stage k-block k0 of this CTA's rows (class 1 or 2) into `slot`
-// with 16-byte copies from the 16-byte boundary at or below each segment's
-// start; class 0 blocks are filled element by element into the tile itself.
-template <AKind AK>
-__device__ __forceinline__ void a_vstage_fill(const UmmaParams& p, uint8_t* ah, uint8_t* slot, int g_first, int k0,
-                                              int ft) {
-  const int cls = a_vclass<AK>(g_first, k0);
-  if (cls == 0) {
-    if constexpr (AK != AKind::Toeplitz) a_async_fill<AK>(p, ah, g_first, k0, ft);
-    return;
-  }
-  const long long n = p.a_dim, len = a_vlen<AK>(n);
-  const float* src = p.a_src;
-  const uint32_t d0 = smem_u32(slot);
-  // element index e of a segment start -> its chunk-aligned index (the
-  // storage pointer is 4-byte aligned; alignment is of the address)
-  auto floor16 = [&](long long e) {
-    return e - static_cast<long long>((reinterpret_cast<uintptr_t>(src + e) & 15) >> 2);
-  };
-  if (cls == 1) {
-    for (int idx = ft; idx < kBM * kVRowChunks; idx += kAFillThreads) {
-      const int r = idx / kVRowChunks, c = idx - r * kVRowChunks;
-      const long long gr = g_first + r;
-      if (gr >= n) continue;
-      vchunk(d0 + r * (kVRowChunks * 16) + 16 * c, src, floor16(a_vrow_base<AK>(gr, n) + k0) + 4 * c, len);
-    }
-  } else {
-    for (int idx = ft; idx < kBK * kVColChunks; idx += kAFillThreads) {
-      const int kk = idx / kVColChunks, c = idx - kk * kVColChunks;
-      const long long k = k0 + kk;  // < g_first <= n - 1
-      vchunk(d0 + kk * (kVColChunks * 16) + 16 * c, src, floor16(k * n - k * (k - 1) / 2 - k + g_first) + 4 * c, len);
-    }
-  }
-}
-
-// Transform warps: k-block k0 of class 1 or 2 from its slot into the
-// swizzled A tile (hi = the fp32 value, which kind::tf32 truncates; lo = the
-// 3xTF32 remainder when SPLIT3), zero outside the matrix.  Thread t writes
-// 8 consecutive k of one row as two 16-byte chunks.
-template <AKind AK, bool SPLIT3>
-__device__ __forceinline__ void a_vstage_convert(const UmmaParams& p, const uint8_t* slot, uint8_t* ah, uint8_t* al,
-                                                 int g_first, int k0, int cls, int t) {
-  const long long n = p.a_dim;
-  const float* src = p.a_src;
-  const float* sf = reinterpret_cast<const float*>(slot);
-  float v[8];
-  int r, kh;
-  if (cls == 1) {
-    r = t >> 1;
-    kh = t & 1;
-    const long long gr = g_first + r;
-    const long long e = a_vrow_base<AK>(gr, n) + k0;
-    const int off = static_cast<int>((reinterpret_cast<uintptr_t>(src + e) & 15) >> 2);
-    const float* w = sf + r * (kVRowChunks * 4) + off + 8 * kh;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = (gr < n && k0 + 8 * kh + j < n) ? w[j] : 0.0f;
-  } else {
-    r = t & (kBM - 1);
-    kh = t >> 7;
-    const bool in = g_first + r < n;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const long long k = k0 + 8 * kh + j;
-      const int off =
-          static_cast<int>((reinterpret_cast<uintptr_t>(src + (k * n - k * (k - 1) / 2 - k + g_first)) & 15) >> 2);
-      v[j] = in ? sf[(8 * kh + j) * (kVColChunks * 4) + off + r] : 0.0f;
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint32_t o = swz_offset(r, 2 * kh + h, 64);
-    const float4 x = make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
-    *reinterpret_cast<float4*>(ah + o) = x;
-    if constexpr (SPLIT3)
-      *reinterpret_cast<float4*>(al + o) =
-          make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
-  }
-}
-
 // ---------------------------------------------------------------- Toeplitz A, bf16
 // Generator index of element (g_first + 127, k0), the lowest one a k-block of
 // the tile reads (negative when the window starts before the generator).
@@ -730,7 +590,6 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // kSubs | B lo x kSubs], each block in the one-block layouts below.
   constexpr int kSubs = umma_subs<AK, MD, kBCols>();
   constexpr bool kStaging = a_staged(AK, MD);  // bf16 Toeplitz: fp32 generator window after the tiles
-  constexpr bool kVStage = a_vstaged(AK, MD);  // fp32 packed / Toeplitz A: 16-byte segment staging
   static_assert(!kStaging || kSubs <= 2, "staged A: one generator window per stage");
   constexpr int kStage = umma_stage_bytes<AK, MD, kBCols>();
   constexpr int kChunkS = kChunk / kSubs;  // chunk length in stages
@@ -764,8 +623,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   auto b_hi = [&](int s) { return smem + s * kStage + kSubs * kATileBytes; };
   auto a_lo = [&](int s) { return smem + s * kStage + kSubs * (kATileBytes + kBTile); };
   auto b_lo = [&](int s) { return smem + s * kStage + kSubs * (2 * kATileBytes + kBTile); };
-  // staging slots after the stage's tiles (bf16 Toeplitz window, or one vector slot per k-block)
-  auto stg = [&](int s) { return smem + s * kStage + kSubs * (SPLIT3 ? 2 : 1) * (kATileBytes + kBTile); };
+  auto stg = [&](int s) { return smem + s * kStage + kSubs * (kATileBytes + kBTile); };  // bf16 only
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1061,11 +919,6 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         if (!mbar_wait(&empty[s], ph ^ 1, wprod)) break;
         if constexpr (kStaging) {
           a_stage_fill_toeplitz_bf16<kSubs>(p, stg(s), g_first, (kb_begin + i * kSubs) * KS, ft);
-        } else if constexpr (kVStage) {
-#pragma unroll
-          for (int j = 0; j < kSubs; ++j)
-            a_vstage_fill<AK>(p, a_hi(s) + j * kATileBytes, stg(s) + j * kVStgBytes, g_first,
-                              (kb_begin + i * kSubs + j) * KS, ft);
         } else {
 #pragma unroll
           for (int j = 0; j < kSubs; ++j)
@@ -1176,29 +1029,8 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
               out[j] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
             }
           };
-          if constexpr (!kVStage) lo_of(a_hi(s), a_lo(s), kSubs * kATileBytes, t);
+          lo_of(a_hi(s), a_lo(s), kSubs * kATileBytes, t);
           if constexpr (kBTma) lo_of(b_hi(s), b_lo(s), kSubs * kBTile, t);
-        }
-        if constexpr (kVStage) {
-          // staged k-blocks: shift into the tile (hi and lo); blocks across
-          // the diagonal were filled element by element: lo only
-#pragma unroll
-          for (int j = 0; j < kSubs; ++j) {
-            const int kj = k0 + j * KS;
-            const int cls = a_vclass<AK>(g_first, kj);
-            if (cls != 0) {
-              a_vstage_convert<AK, SPLIT3>(p, stg(s) + j * kVStgBytes, a_hi(s) + j * kATileBytes,
-                                           a_lo(s) + j * kATileBytes, g_first, kj, cls, t);
-            } else if constexpr (SPLIT3) {
-              const float4* in = reinterpret_cast<const float4*>(a_hi(s) + j * kATileBytes);
-              float4* out = reinterpret_cast<float4*>(a_lo(s) + j * kATileBytes);
-#pragma unroll 2
-              for (int e = t; e < kATileBytes / 16; e += kXformThreads) {
-                const float4 x = in[e];
-                out[e] = make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
-              }
-            }
-          }
         }
         fence_proxy_async_smem();
         __syncwarp();
