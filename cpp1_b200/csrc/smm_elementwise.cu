@@ -19,7 +19,6 @@
 
 #include <algorithm>
 #include <cstdint>
-#include <cstdlib>
 
 #include "smm_host.h"
 
@@ -198,76 +197,6 @@ __global__ void __launch_bounds__(kEwThreads) symm_pair_kernel(const float* __re
   }
 }
 
-// Symmetric operand, one CTA per 32-row x 128-column tile of C, the same
-// tiles and row-wise 128-bit A/C traffic as the other structured formats:
-//   tiles on or above the diagonal read packed row i along j (contiguous);
-//   tiles wholly below it (every j < i) need S[j][i] from packed row j: the
-//     CTA reads the 128 x 32 block of packed rows j0.., columns i0.. (one warp
-//     per packed row, 128 contiguous bytes each) into shared memory and
-//     writes C rows from its transpose;
-//   the few tiles crossing the diagonal read each element where it lies.
-// Each C row segment is written once, in full 512-byte row segments, and the
-// packed triangle is read twice overall (once per orientation).
-template <bool HAS_A>
-__global__ void __launch_bounds__(kEwThreads) symm_stripe_kernel(const float* __restrict__ A,
-                                                                 const float* __restrict__ P, float* __restrict__ C,
-                                                                 int n, int vec) {
-  __shared__ float tile[kTileR][kTileC + 1];  // [i - i0][j - j0] of the lower block
-  const int row0 = blockIdx.y * kTileR;
-  const int col0 = blockIdx.x * kTileC;
-  const int t = threadIdx.x;
-  const int cq = t & 31;
-  const int rr = t >> 5;
-  const bool below = row0 > col0 + kTileC - 1;  // every i > every j: mirrored block
-  const bool above = row0 + kTileR - 1 <= col0;  // every i <= every j: packed rows
-  if (below) {
-    // packed row j (warp w: rows j0 + w, j0 + w + 8, ...), columns i0 + lane
-    const int i = row0 + cq;
-#pragma unroll 4
-    for (int jl = rr; jl < kTileC; jl += 8) {
-      const int j = col0 + jl;
-      tile[cq][jl] = (i < n && j < n) ? __ldg(P + pk_upper(j, i, n)) : 0.0f;
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int it = 0; it < kTileR / 8; ++it) {
-    const int r = rr + 8 * it;
-    const int i = row0 + r;
-    if (i >= n) break;
-    const int j0 = col0 + 4 * cq;
-    if (j0 >= n) continue;
-    const long long base = static_cast<long long>(i) * n;
-    float s[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int j = j0 + e;
-      if (j >= n)
-        s[e] = 0.0f;
-      else if (below)
-        s[e] = tile[r][4 * cq + e];
-      else if (above || j >= i)
-        s[e] = __ldg(P + pk_upper(i, j, n));
-      else
-        s[e] = __ldg(P + pk_upper(j, i, n));
-    }
-    if (vec && j0 + 4 <= n) {
-      float4 c = make_float4(s[0], s[1], s[2], s[3]);
-      if constexpr (HAS_A) {
-        const float4 a = __ldcs(reinterpret_cast<const float4*>(A + base + j0));
-        c = make_float4(__fadd_rn(a.x, c.x), __fadd_rn(a.y, c.y), __fadd_rn(a.z, c.z), __fadd_rn(a.w, c.w));
-      }
-      __stcs(reinterpret_cast<float4*>(C + base + j0), c);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = j0 + e;
-        if (j < n) C[base + j] = HAS_A ? __fadd_rn(A[base + j], s[e]) : s[e];
-      }
-    }
-  }
-}
-
 // C[k] = A[k] + B[k], k < count: 128-bit path over the 16-byte-aligned body.
 __global__ void __launch_bounds__(kEwThreads) add_vec4_kernel(const float4* __restrict__ A,
                                                               const float4* __restrict__ B, float4* __restrict__ C,
@@ -371,13 +300,6 @@ int launch_dense_struct(const float* A, const float* S, int fmt, float* C, int n
   const dim3 grid((n + kTileC - 1) / kTileC, (n + kTileR - 1) / kTileR);
   if (grid.y > 65535u) return set_error(SMM_ERR_INVALID, "order %d too large for the tile grid", n);
   const int vec = (n % 4 == 0) && aligned16(C) && (!HAS_A || aligned16(A)) ? 1 : 0;
-  const char* e = std::getenv("SMM_SYMM_PAIRS");
-  if (fmt == SMM_STRUCT_SYMM && !(e && e[0] == '1')) {
-    symm_stripe_kernel<HAS_A><<<grid, kEwThreads, 0, st>>>(A, S, C, n, vec);
-    count_launch();
-    SMM_CUDA_TRY(cudaGetLastError(), "symmetric elementwise launch");
-    return SMM_OK;
-  }
   if (fmt == SMM_STRUCT_SYMM) {
     const long long nt = (n + kSymT - 1) / kSymT;
     const long long pairs = nt * (nt + 1) / 2;
