@@ -20,4 +20,14 @@ int launch_dense_split(int mode, const Maps& m, const UmmaParams& p, cudaStream_
   return launch_umma<A, B, Mode::TF32, 128, umma_stages<A, Mode::TF32, 128>(), false, 2>(m, p, st);
 }
 
+int launch_dense_persist(AKind ak, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st) {
+  if (ak == AKind::Dense)
+    return mode == SMM_MODE_BF16 ? launch_persist<AKind::Dense, Mode::BF16>(m, p, st)
+                                 : launch_persist<AKind::Dense, Mode::TF32>(m, p, st);
+  if (ak == AKind::UpperDense)
+    return mode == SMM_MODE_BF16 ? launch_persist<AKind::UpperDense, Mode::BF16>(m, p, st)
+                                 : launch_persist<AKind::UpperDense, Mode::TF32>(m, p, st);
+  return set_error(SMM_ERR_INVALID, "persistent contraction: unsupported operand kinds");
+}
+
 }  // namespace smm

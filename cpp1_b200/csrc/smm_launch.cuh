@@ -3,10 +3,12 @@
 // unit (smm_kern_*.cu), so the kernel variants compile in parallel.
 #pragma once
 #include <cuda.h>
+#include <algorithm>
 #include <cuda_runtime.h>
 
 #include "smm_host.h"
 #include "smm_umma.cuh"
+#include "smm_umma_persist.cuh"
 
 namespace smm {
 
@@ -75,6 +77,46 @@ int launch_bn(int bn, bool pair, int mode, const Maps& m, const UmmaParams& p, c
     default: return launch_mode<AK, BK, 64, false>(mode, m, p, st);
   }
 }
+
+// Persistent pair kernel (one-pass modes, TMA-fed A and B, 256 x 256 tiles):
+// one cluster per SM pair, at most one per tile.
+template <AKind AK, Mode MD>
+int launch_persist(const Maps& m, const UmmaParams& p, cudaStream_t st) {
+  auto kern = umma_persist_kernel<AK, MD>;
+  constexpr int smem = persist_smem_bytes<AK, MD>();
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+  static bool attr_set[64] = {};
+  int dev = 0;
+  SMM_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    SMM_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                 "cudaFuncSetAttribute(max dynamic smem)");
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  int sms = 0;
+  SMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+  const long long tiles = static_cast<long long>(p.row_tiles) * p.col_tiles;
+  const long long clusters = std::min<long long>(tiles, std::max(1, sms / 2));
+  if (clusters <= 0) return SMM_OK;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+  cfg.blockDim = dim3(kPersistThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SMM_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m.a, m.b, p), "tcgen05 persistent contraction launch");
+  count_launch();
+  SMM_CUDA_TRY(cudaGetLastError(), "tcgen05 persistent contraction launch");
+  return SMM_OK;
+}
+// Dense / UpperDense x Dense, TF32 or bf16 (smm_kern_dense.cu).
+int launch_dense_persist(AKind ak, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st);
 
 // Dense x Dense with 128 x 128 tiles, each split over two CTAs along K
 // (smm_kern_dense.cu).

@@ -236,7 +236,16 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   g_ev_before = g_ev_after = nullptr;
   if (!p.status) return set_error(SMM_ERR_CUDA, "device status word unavailable");
   if (ev_before) SMM_CUDA_TRY(cudaEventRecord(ev_before, st), "record event before the contraction");
-  const int rc = split ? launch_dense_split(mode, m, p, st) : launch_kinds(ak, bk, bn, pair, mode, m, p, st);
+  // One-pass modes on TMA-fed operands with 256 x 256 pair tiles run
+  // persistent: one CTA pair per SM pair walks the tiles with the
+  // accumulator double-buffered in tensor memory (SMM_PERSIST=0 disables it).
+  const char* pe = std::getenv("SMM_PERSIST");
+  const bool persist = !(pe && pe[0] == '0') && !split && pair && bn == 256 && mode != SMM_MODE_3XTF32 &&
+                       (ak == AKind::Dense || ak == AKind::UpperDense) && bk == BKind::Dense && !a.lower &&
+                       b.tri == 0 && C_lo == nullptr && C_bf16 == nullptr;
+  const int rc = split     ? launch_dense_split(mode, m, p, st)
+                 : persist ? launch_dense_persist(ak, mode, m, p, st)
+                           : launch_kinds(ak, bk, bn, pair, mode, m, p, st);
   if (rc == SMM_OK && ev_after) SMM_CUDA_TRY(cudaEventRecord(ev_after, st), "record event after the contraction");
   return rc;
 }

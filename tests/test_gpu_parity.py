@@ -275,3 +275,32 @@ def test_timeout_probe_returns_status_and_context_survives(cuda):
     R = O.gemm_rows_f64(w["A"], w["B"], np.arange(128))
     assert O.relerr(C, R) <= 1e-5
     ops.device_status()
+
+
+@pytest.mark.parametrize("mode", ["tf32", "bf16"])
+@pytest.mark.parametrize("mnk", [(2048, 2048, 2048), (2300, 2100, 1000), (4096, 2048, 3000), (1536, 7936, 520)])
+def test_persistent_pair_kernel_matches_per_tile_kernel(cuda, monkeypatch, mode, mnk):
+    """One-pass modes on 256 x 256 pair tiles run the persistent kernel (one
+    CTA pair per SM pair, double-buffered accumulator).  Each tile's MMA
+    sequence is the per-tile kernel's, so the results are bit-identical
+    (SMM_PERSIST=0 selects the per-tile kernel); ragged M, N and K."""
+    M, N, K = mnk
+    w = W.make_gemm(M, N, K, seed=M + N + K)
+    A, B = dev(w["A"]), dev(w["B"])
+    C_p = host(ops.gemm(A, B, mode=mode))
+    monkeypatch.setenv("SMM_PERSIST", "0")
+    C_t = host(ops.gemm(A, B, mode=mode))
+    assert np.array_equal(C_p, C_t)
+    rows = np.unique(np.linspace(0, M - 1, 48).astype(np.int32))
+    assert _relerr_full(C_p[rows], O.gemm_rows_f64(w["A"], w["B"], rows)) <= TOL[mode]
+
+
+@pytest.mark.parametrize("mode", ["tf32", "bf16"])
+def test_persistent_upper_matches_per_tile_kernel(cuda, monkeypatch, mode):
+    n = 3000
+    w = W.make_upper(n, 2560, seed=41)
+    U, B = dev(w["U"]), dev(w["B"])
+    C_p = host(ops.upper_left(U, B, mode=mode))
+    monkeypatch.setenv("SMM_PERSIST", "0")
+    C_t = host(ops.upper_left(U, B, mode=mode))
+    assert np.array_equal(C_p, C_t)
