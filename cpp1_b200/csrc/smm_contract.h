@@ -45,10 +45,13 @@ Operand structured_op(const float* src, int dim, int row0 = 0);
 
 // C(M x N, ldc) = Aop(M x K) * B(K x N) on stream st.  Optionally also
 // writes lo(C) (C_lo, same ldc) or bf16(C) (C_bf16, ldc_bf16) from the
-// epilogue, so that C can feed a following product.
+// epilogue, so that C can feed a following product.  `wide`: the launch
+// shares the GPU with concurrent launches of the same product (the
+// multi-GPU column blocks), so it takes the efficient 256-row pair tiles
+// even when it alone would fill less than a wave.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
                     int N, int K, cudaStream_t st, float* C_lo = nullptr, __nv_bfloat16* C_bf16 = nullptr,
-                    int ldc_bf16 = 0);
+                    int ldc_bf16 = 0, bool wide = false);
 
 // ---------------------------------------------------------------- staging
 // A TMA-fed operand (rows x cols row-major): the caller's array or a padded

@@ -248,14 +248,20 @@ int broadcast_blocks(smm_mg_comm* c, const float* B, int K, int ncols, float* pa
     SMM_NCCL_TRY(n.broadcast(S_packed, S_packed, s_count, ncclFloat, root, c->nc, c->cs), "ncclBroadcast (S)");
     SMM_CUDA_TRY(cudaEventRecord(c->ev_s, c->cs), "record S arrival");
   }
-  for (int j = 0; j < nch; ++j) {
-    const int w = cb[j + 1] - cb[j];
-    float* blk = pack + static_cast<size_t>(K) * cb[j];
-    if (c->rank == root) {
-      pack_cols_kernel<<<148 * 4, 256, 0, c->cs>>>(B, ncols, cb[j], K, w, blk);
+  // The root packs every block first: the packs are enqueued before its own
+  // slab's contractions, so they take the SMs at once instead of competing
+  // with them between broadcasts.
+  if (c->rank == root) {
+    for (int j = 0; j < nch; ++j) {
+      pack_cols_kernel<<<148 * 4, 256, 0, c->cs>>>(B, ncols, cb[j], K, cb[j + 1] - cb[j],
+                                                   pack + static_cast<size_t>(K) * cb[j]);
       count_launch();
       SMM_CUDA_TRY(cudaGetLastError(), "pack column block of B");
     }
+  }
+  for (int j = 0; j < nch; ++j) {
+    const int w = cb[j + 1] - cb[j];
+    float* blk = pack + static_cast<size_t>(K) * cb[j];
     SMM_NCCL_TRY(n.broadcast(blk, blk, static_cast<size_t>(K) * w, ncclFloat, root, c->nc, c->cs),
                  "ncclBroadcast (column block of B)");
     SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record block arrival");
@@ -480,7 +486,7 @@ extern "C" int smm_mg_gemm(smm_mg_comm* c, const float* A_slab, const float* B, 
     Operand bo;
     if (int rc = block_operand(c, B, K, N, pack, cb, j, mode, bf, w, &bo, root)) return rc;
     return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16), bo,
-                           C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], K, w);
+                           C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], K, w, nullptr, nullptr, 0, true);
   });
 }
 
@@ -520,7 +526,7 @@ extern "C" int smm_mg_upper_left(smm_mg_comm* c, const float* U_packed, const fl
     ao.dim = N;
     ao.row0 = row0;
     return run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, bo, C_slab + cb[j], ncols, nrows,
-                           cb[j + 1] - cb[j], N, w);
+                           cb[j + 1] - cb[j], N, w, nullptr, nullptr, 0, true);
   });
 }
 
@@ -551,7 +557,7 @@ extern "C" int smm_mg_toeplitz_left(smm_mg_comm* c, const float* g, const float*
     Operand bo;
     if (int rc = block_operand(c, B, N, ncols, pack, cb, j, mode, bf, w, &bo, root)) return rc;
     return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), bo, C_slab + cb[j], ncols,
-                           nrows, cb[j + 1] - cb[j], N, w);
+                           nrows, cb[j + 1] - cb[j], N, w, nullptr, nullptr, 0, true);
   });
 }
 
@@ -621,6 +627,6 @@ extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* 
     Operand bo;
     if (int rc = block_operand(c, B, N, N, pack, cb, j, mode, bfb, w, &bo, root)) return rc;
     return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(bf ? nullptr : Y, nullptr, bf ? ldy_bf : ldy, Y_bf),
-                           bo, C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], N, w);
+                           bo, C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], N, w, nullptr, nullptr, 0, true);
   });
 }
