@@ -494,11 +494,13 @@ extern "C" int smm_symm_sandwich(const float* A, const float* S, const float* B,
   Staged a, b;
   if (int rc = stage_operand(A, N, N, mode, cur, &a, st)) return rc;
   if (int rc = stage_operand(B, N, N, mode, cur, &b, st)) return rc;
-  // X = S B (S expanded, or packed and mirrored on chip; the epilogue also
-  // writes X's bf16 copy in bf16 mode), then C = A X.
+  // X = S B (S expanded, or packed and mirrored on chip; in bf16 mode the
+  // epilogue writes only X's bf16 copy, the second product's operand), then
+  // C = A X.
   const Operand s_op = expand ? dense_op(s_ex.ptr, nullptr, s_ex.ld, s_ex.bf16) : structured_op(S, N);
   if (int rc = run_contraction(expand ? AKind::Dense : AKind::SymmPacked, BKind::Dense, mode, s_op,
-                               dense_op(b.ptr, b.lo, b.ld, b.bf16), X, ldx, N, N, N, st, X_lo, X_bf, ldx_bf))
+                               dense_op(b.ptr, b.lo, b.ld, b.bf16), bf ? nullptr : X, ldx, N, N, N, st, X_lo, X_bf,
+                               ldx_bf))
     return rc;
   return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, a.lo, a.ld, a.bf16),
                          dense_op(X, X_lo, bf ? ldx_bf : ldx, X_bf), C, N, N, N, N, st);

@@ -618,7 +618,7 @@ extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* 
     Staged s;  // S mirrored into a dense copy: the right operand of Y = A_slab S
     if (int rc = expand_operand(S_packed, SMM_STRUCT_SYMM, N, 0, N, mode, cur, &s, st)) return rc;
     if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16),
-                                 dense_op(s.ptr, nullptr, s.ld, s.bf16), Y, ldy, nrows, N, N, st, nullptr, Y_bf,
+                                 dense_op(s.ptr, nullptr, s.ld, s.bf16), bf ? nullptr : Y, ldy, nrows, N, N, st, nullptr, Y_bf,
                                  ldy_bf))
       return rc;
   }

@@ -765,28 +765,47 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
       tmem_wait_ld();
     }
   };
-  // Store 16 result columns (col ..) of output row `row` to C (and its bf16 /
-  // lo copies when requested).
+  // Store 16 result columns (col ..) of output row `row` to C (skipped when
+  // C is null: a bf16-only intermediate) and its bf16 / lo copies when
+  // requested.  Whole 16-column runs go out as 16-byte vectors: a warp's
+  // lanes hold 32 different rows, so every store instruction touches 32
+  // lines, and scalar 2-byte bf16 stores (16 instructions per run instead
+  // of 2) made the epilogue of a bf16-copy product cost most of a tile's MMA time.
   auto store16 = [&](int row, int col, const uint32_t (&r)[16]) {
     if (row >= p.M) return;
-    const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
-    float* crow = p.C + static_cast<long long>(row) * p.ldc;
-    if (vec && col + 16 <= p.N) {
-      float4* dst = reinterpret_cast<float4*>(crow + col);
+    if (p.C != nullptr) {
+      const bool vec = (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+      float* crow = p.C + static_cast<long long>(row) * p.ldc;
+      if (vec && col + 16 <= p.N) {
+        float4* dst = reinterpret_cast<float4*>(crow + col);
 #pragma unroll
-      for (int v = 0; v < 4; ++v)
-        dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]), __uint_as_float(r[4 * v + 2]),
-                             __uint_as_float(r[4 * v + 3]));
-    } else {
+        for (int v = 0; v < 4; ++v)
+          dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+      } else {
 #pragma unroll
-      for (int v = 0; v < 16; ++v)
-        if (col + v < p.N) crow[col + v] = __uint_as_float(r[v]);
+        for (int v = 0; v < 16; ++v)
+          if (col + v < p.N) crow[col + v] = __uint_as_float(r[v]);
+      }
     }
     if (p.C_bf16 != nullptr) {
       __nv_bfloat16* brow = p.C_bf16 + static_cast<long long>(row) * p.ldc_bf16;
+      const bool bvec = (p.ldc_bf16 % 8 == 0) && ((reinterpret_cast<uintptr_t>(p.C_bf16) & 15) == 0);
+      if (bvec && col + 16 <= p.N) {
+        uint32_t h[8];
 #pragma unroll
-      for (int v = 0; v < 16; ++v)
-        if (col + v < p.N) brow[col + v] = __float2bfloat16_rn(__uint_as_float(r[v]));
+        for (int v = 0; v < 8; ++v) {
+          __nv_bfloat162 t2 = __floats2bfloat162_rn(__uint_as_float(r[2 * v]), __uint_as_float(r[2 * v + 1]));
+          h[v] = *reinterpret_cast<uint32_t*>(&t2);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(brow + col);
+        dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+        dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < 16; ++v)
+          if (col + v < p.N) brow[col + v] = __float2bfloat16_rn(__uint_as_float(r[v]));
+      }
     }
     if (p.C_lo != nullptr) {
       float* lrow = p.C_lo + static_cast<long long>(row) * p.ldc;
