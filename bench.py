@@ -83,6 +83,9 @@ def parse_args():
                     help="override the problem order (--order under torchrun, whose parser claims --n)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--b-placement", choices=["sharded", "root"], default="sharded",
+                    help="G > 1: B arrives sharded by rows (all-gathered inside each call) or whole on rank 0 "
+                         "(broadcast inside each call)")
     ap.add_argument("--roofline-s", type=float, default=1.0,
                     help="seconds of repeated calls over which the roofline kernel is timed")
     a = ap.parse_args()
@@ -371,12 +374,24 @@ def run_ours(args, rank, world, local):
         units_per_rank_call = hbm_bytes(op, n)
     else:
         # Contractions.  One GPU: the single-GPU entry point.  G > 1: one
-        # libsmm multi-GPU call per step (smm_mg_*): B (S and B for the
-        # sandwich) is broadcast from rank 0 in column blocks inside the call
-        # and this rank's row slab is computed block by block as they land.
+        # libsmm multi-GPU call per step (smm_mg_*): B reaches every rank in
+        # column blocks inside the call (all-gathered from the row shares, or
+        # broadcast from rank 0; the sandwich's S from rank 0) and this
+        # rank's row slab is computed block by block as they land.
         # slab_local() runs the same slab with the operands already in place (the
         # single-GPU slab entry points), for the compute-only time.
         comm = MG.Communicator(rank, world) if world > 1 else None
+        # B as this rank passes it to the call: its row share (sharded
+        # placement: rows [rank s, rank s + s) of the resident B) or the
+        # whole B (read on rank 0 only).
+        root = MG.SHARDED if args.b_placement == "sharded" else 0
+        B_full = d_in[-1]
+        if root == MG.SHARDED:
+            s_rows = MG.share_rows(n, world)
+            lo_b, hi_b = min(n, rank * s_rows), min(n, (rank + 1) * s_rows)
+            B_arg = B_full[lo_b:hi_b] if hi_b > lo_b else B_full[:1]
+        else:
+            B_arg = B_full
         if op == "gemm":
             A, B = d_in
             A_slab = A[r0:r1]
@@ -388,7 +403,7 @@ def run_ours(args, rank, world, local):
                                           sp), "gemm")
 
             def step():
-                comm.gemm(A_slab, B, out, mode) if comm else slab_local()
+                comm.gemm(A_slab, B_arg, out, mode, root=root) if comm else slab_local()
             units_per_rank_call = 2 * nrows * n * n
         elif op == "upper":
             U, B = d_in
@@ -399,7 +414,7 @@ def run_ours(args, rank, world, local):
                                                  r0, nrows, m, ws, wsb, sp), "upper")
 
             def step():
-                comm.upper_left(U, B, out, r0, mode) if comm else slab_local()
+                comm.upper_left(U, B_arg, out, r0, mode, root=root) if comm else slab_local()
             units_per_rank_call = slab_useful_flops("upper", n, r0, r1)
         elif op == "sandwich":
             A, S, B = d_in
@@ -414,7 +429,7 @@ def run_ours(args, rank, world, local):
                     ops.gemm(ops.gen_x_symm(A_slab, S, mode=mode), B, mode=mode, out=out)
 
             def step():
-                comm.symm_sandwich(A_slab, S, B, out, mode) if comm else slab_local()
+                comm.symm_sandwich(A_slab, S, B_arg, out, mode, root=root) if comm else slab_local()
             units_per_rank_call = 4 * nrows * n * n
         else:
             g, B = d_in
@@ -425,7 +440,7 @@ def run_ours(args, rank, world, local):
                                                     m, ws, wsb, sp), "toeplitz")
 
             def step():
-                comm.toeplitz_left(g, B, out, r0, mode) if comm else slab_local()
+                comm.toeplitz_left(g, B_arg, out, r0, mode, root=root) if comm else slab_local()
             units_per_rank_call = 2 * nrows * n * n
 
     # useful FLOPs of the first contraction kernel of one call (the one the
@@ -486,39 +501,46 @@ def run_ours(args, rank, world, local):
         torch.cuda.synchronize()
         barrier(world)
         ms_c = max_over_ranks(c0.elapsed_time(c1), world) / args.steps
-        # the broadcast of B alone (a zero-row product: every rank receives B's blocks, none computes)
-        Bsh = d_in[-1]
+        # B's transfer alone (a zero-row product: every rank receives B's
+        # blocks, none computes)
         empty_a = torch.empty((0, n), dtype=torch.float32, device="cuda")
         barrier(world)
         torch.cuda.synchronize()
         c0.record(stream)
         for _ in range(args.steps):
-            comm.gemm(empty_a, Bsh, empty_a, mode)
+            comm.gemm(empty_a, B_arg, empty_a, mode, root=root)
         c1.record(stream)
         torch.cuda.synchronize()
         barrier(world)
         ms_b = max_over_ranks(c0.elapsed_time(c1), world) / args.steps
-        bcast = 4 * n * n + (2 * n * (n + 1) if op == "sandwich" else 0)
+        b_bytes = (2 if mode == "bf16" else 4) * n * n  # B's blocks travel as bf16 in bf16 mode
+        s_bytes = 2 * n * (n + 1) if op == "sandwich" else 0  # packed S, fp32, from rank 0
+        # bytes the busiest receiving rank takes in over NVLink per step
+        link_in = (b_bytes * (world - 1) // world if root == MG.SHARDED else b_bytes) + s_bytes
         passes = {"3xtf32": 3, "tf32": 1, "bf16": 1}[mode]
         peak = peaks["bf16_tflops"] / (1 if mode == "bf16" else 2)
         heaviest = max_over_ranks(float(units_per_rank_call), world)
         t_mma = passes * heaviest / (peak * 1e12) * 1e3
-        t_link = bcast / 770e9 * 1e3
-        multi = {"compute_only_ms_per_step": round(ms_c, 4), "broadcast_inclusive_ms_per_step": round(ms_per_step, 4),
-                 "broadcast_only_ms_per_step": round(ms_b, 4),
-                 "broadcast_gbs": round(4 * n * n / (ms_b * 1e-3) / 1e9, 1),
-                 "broadcast_bytes_per_step": int(bcast),
+        t_link = link_in / 770e9 * 1e3
+        how = ("all-gathered from every rank's row share" if root == MG.SHARDED else "broadcast from rank 0")
+        multi = {"compute_only_ms_per_step": round(ms_c, 4), "transfer_inclusive_ms_per_step": round(ms_per_step, 4),
+                 "transfer_only_ms_per_step": round(ms_b, 4),
+                 "b_placement": args.b_placement,
+                 "b_transfer_gbs": round(b_bytes / (ms_b * 1e-3) / 1e9, 1),
+                 "b_bytes_per_step": int(b_bytes),
+                 "nvlink_in_bytes_per_rank": int(link_in),
                  "column_blocks": MG.lib_chunks(n, world),
-                 "overlap": "B broadcast from rank 0 in column blocks inside each call (libsmm smm_mg_*, NCCL on a "
-                            "high-priority stream); each block's columns of the slab are computed as soon as it "
-                            "lands, on internal compute streams",
+                 "overlap": f"B {how} in column blocks inside each call (libsmm smm_mg_*, NCCL on a high-priority "
+                            "stream); each block's columns of the slab are computed as soon as it lands, on "
+                            "internal compute streams",
                  "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)],
                  "roofline": {"bound": "tensor" if t_mma >= t_link else "nvlink",
                               "t_mma_ms": round(t_mma, 4), "t_nvlink_ms": round(t_link, 4),
                               "target_ms": round(max(t_mma, t_link), 4),
                               "frac": round(max(t_mma, t_link) / ms_per_step, 4),
-                              "basis": f"heaviest slab's {passes}-pass MMA FLOPs at {peak:.1f} TFLOP/s; "
-                                       "broadcast bytes at the measured 770 GB/s peer bandwidth"}}
+                              "basis": f"heaviest slab's {passes}-pass MMA FLOPs at {peak:.1f} TFLOP/s; the bytes "
+                                       "the busiest rank receives over NVLink at the measured 770 GB/s peer "
+                                       "bandwidth"}}
         comm.close()
 
     total_units = units_per_rank_call * world if op in HBM_OPS else (
@@ -537,7 +559,8 @@ def run_ours(args, rank, world, local):
                                              "bf16": "bf16 (fp32 accumulate)"}[mode],
         "data": "synthetic (seeded numpy PCG64, cpp1_b200.workloads)",
         "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "mode": mode if op not in HBM_OPS else "f32",
-                   "parallelism": f"row-slabs x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"row-slabs x{world}, B {args.b_placement}" if world > 1 and op not in HBM_OPS
+                                   else (f"row-slabs x{world}" if world > 1 else "single GPU")),
                    "l2": "inputs larger than L2 (126 MB): no flush needed"},
         "roofline": roof,
         "check": check,
@@ -750,65 +773,58 @@ def e2e_ours(args, h_in, n):
 
 
 def e2e_dist(args, h_in, n, rank, world):
-    """Host-buffer end to end at G > 1 for the contractions.  Every rank copies
-    only its share of the host inputs over its own PCIe link: its row slab of
-    the left operand (the whole 128 KiB generator for T B) and 1/G of the rows
-    of B (for the sandwich also 1/G of packed S).  The shared operands are
-    assembled by NVLink all-gathers, each rank computes its slab and copies
-    its rows of C back to the host.  Wall time per step, max over ranks."""
+    """Host-buffer end to end at G > 1 for the contractions, through the
+    library's multi-GPU calls.  Every rank copies only its share of the host
+    inputs over its own PCIe link -- its row slab of the left operand (the
+    whole 128 KiB generator for T B; packed S on rank 0 for the sandwich)
+    and its row share of B -- then one smm_mg_* call all-gathers B's column
+    blocks over NVLink and computes the slab, and the rank copies its rows of
+    C back to the host.  Wall time per step, max over ranks."""
     import torch
-    from cpp1_b200 import _lib, ops
-    from cpp1_b200.multigpu import allgather_rows, row_slabs, uniform_shares
-    L = _lib.load()
+    from cpp1_b200 import _lib
+    from cpp1_b200 import multigpu as MG
     op = args.op
-    m = _lib.MODES[args.mode]
+    mode = args.mode
     stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream or None
     dev = torch.device("cuda", torch.cuda.current_device())
-    bounds = uniform_shares(n, world) if op == "sandwich" else row_slabs(n, world, triangular=(op == "upper"))
+    bounds = MG.lib_row_slabs(n, world, triangular=(op == "upper"))
     r0, r1 = bounds[rank], bounds[rank + 1]
     nrows = r1 - r0
-    sb = uniform_shares(n, world)
-    s0, s1 = sb[rank], sb[rank + 1]
-    per = sb[1] - sb[0]
+    per = MG.share_rows(n, world)
+    s0, s1 = min(n, rank * per), min(n, (rank + 1) * per)
 
     def pin(x):
         return torch.from_numpy(np.ascontiguousarray(x)).pin_memory()
 
+    comm = MG.Communicator(rank, world)
     Bh = h_in[-1]  # B is the last input of every contraction
     hB = pin(Bh[s0:s1])
-    B_share = torch.zeros((per, n), dtype=torch.float32, device=dev)
-    B_full = torch.empty((per * world, n), dtype=torch.float32, device=dev)
+    B_share = torch.zeros((max(s1 - s0, 1), n), dtype=torch.float32, device=dev)
     C = torch.empty((max(nrows, 1), n), dtype=torch.float32, device=dev)
     hC = torch.empty((nrows, n), dtype=torch.float32).pin_memory()
-    need = max(L.smm_gemm_workspace_size(max(nrows, 1), n, n, m), L.smm_symm_left_workspace_size(n, n, m),
-               L.smm_upper_left_workspace_size(n, n, _lib.FMT_PACKED, m), L.smm_toeplitz_left_workspace_size(n, n, m))
-    wbuf = ops.workspace(need, dev)
-    ws, wsb = (wbuf.data_ptr(), wbuf.numel()) if wbuf is not None else (None, 0)
     h2d = Bh.nbytes
     if op in ("gemm", "sandwich"):
         hA = pin(h_in[0][r0:r1])
-        A = torch.empty((max(nrows, 1), n), dtype=torch.float32, device=dev)
+        A = torch.empty((nrows, n), dtype=torch.float32, device=dev)
         h2d += h_in[0].nbytes
     if op == "gemm":
         def load():
-            A[:nrows].copy_(hA, non_blocking=True)
+            A.copy_(hA, non_blocking=True)
 
-        def comp(Bf):
-            _lib.check(L.smm_gemm(A.data_ptr(), Bf.data_ptr(), C.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+        def comp():
+            comm.gemm(A, B_share, C[:nrows], mode, root=MG.SHARDED)
     elif op == "upper":
         Up = h_in[0]
         lo, hi = r0 * n - r0 * (r0 - 1) // 2, r1 * n - r1 * (r1 - 1) // 2  # packed rows [r0, r1)
         hU = pin(Up[lo:hi])
-        U = torch.empty(Up.size, dtype=torch.float32, device=dev)
+        U = torch.zeros(Up.size, dtype=torch.float32, device=dev)
         h2d += Up.nbytes
 
         def load():
             U[lo:hi].copy_(hU, non_blocking=True)
 
-        def comp(Bf):
-            _lib.check(L.smm_upper_left_rows(U.data_ptr(), _lib.FMT_PACKED, Bf.data_ptr(), C.data_ptr(), n, n, r0,
-                                             nrows, m, ws, wsb, sp), "upper")
+        def comp():
+            comm.upper_left(U, B_share, C[:nrows], r0, mode, root=MG.SHARDED)
     elif op == "toeplitz":
         hg = pin(h_in[0])
         g = torch.empty(h_in[0].size, dtype=torch.float32, device=dev)
@@ -817,38 +833,27 @@ def e2e_dist(args, h_in, n, rank, world):
         def load():
             g.copy_(hg, non_blocking=True)
 
-        def comp(Bf):
-            _lib.check(L.smm_toeplitz_left_rows(g.data_ptr(), Bf.data_ptr(), C.data_ptr(), n, n, r0, nrows, m, ws,
-                                                wsb, sp), "toeplitz")
+        def comp():
+            comm.toeplitz_left(g, B_share, C[:nrows], r0, mode, root=MG.SHARDED)
     else:
         Sh = h_in[1]
-        pb = uniform_shares(Sh.size, world)
-        sper = pb[1] - pb[0]
-        hS = pin(Sh[pb[rank]:pb[rank + 1]])
-        S_share = torch.zeros((sper, 1), dtype=torch.float32, device=dev)
-        S_full = torch.empty((sper * world, 1), dtype=torch.float32, device=dev)
-        X_share = torch.empty((per, n), dtype=torch.float32, device=dev)
-        X_full = torch.empty((per * world, n), dtype=torch.float32, device=dev)
-        h2d += Sh.nbytes
+        hS = pin(Sh) if rank == 0 else None
+        S = torch.empty(Sh.size, dtype=torch.float32, device=dev)
+        h2d += Sh.nbytes  # rank 0 alone copies packed S; the call broadcasts it
 
         def load():
-            A[:nrows].copy_(hA, non_blocking=True)
-            S_share[:pb[rank + 1] - pb[rank]].copy_(hS.view(-1, 1), non_blocking=True)
+            A.copy_(hA, non_blocking=True)
+            if hS is not None:
+                S.copy_(hS, non_blocking=True)
 
-        def comp(Bf):
-            Sf = allgather_rows(S_share, world, Sh.size, out=S_full)
-            if s1 > s0:
-                _lib.check(L.smm_symm_left_rows(Sf.data_ptr(), Bf.data_ptr(), X_share.data_ptr(), n, n, s0, s1 - s0,
-                                                m, ws, wsb, sp), "symm")
-            Xf = allgather_rows(X_share, world, n, out=X_full)
-            if nrows > 0:
-                _lib.check(L.smm_gemm(A.data_ptr(), Xf.data_ptr(), C.data_ptr(), nrows, n, n, m, ws, wsb, sp), "gemm")
+        def comp():
+            comm.symm_sandwich(A, S, B_share, C[:nrows], mode, root=MG.SHARDED)
 
     def step():
         load()
-        B_share[:s1 - s0].copy_(hB, non_blocking=True)
-        Bf = allgather_rows(B_share, world, n, out=B_full)
-        comp(Bf)
+        if s1 > s0:
+            B_share[:s1 - s0].copy_(hB, non_blocking=True)
+        comp()
         if nrows > 0:
             hC.copy_(C[:nrows], non_blocking=True)
         stream.synchronize()
@@ -862,11 +867,13 @@ def e2e_dist(args, h_in, n, rank, world):
         step()
     torch.cuda.synchronize()
     dt = max_over_ranks(time.perf_counter() - t0, world) / steps
+    barrier(world)
+    comm.close()
     units = {"gemm": 2 * n ** 3, "upper": n * n * (n + 1), "sandwich": 4 * n ** 3, "toeplitz": 2 * n ** 3}[op]
     return {"value": round(units / dt / 1e12, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(n * n * 4), "steps": steps, "ms_per_step": round(dt * 1e3, 3),
-            "api": "C ABI with pinned host buffers; per-rank input shares over each GPU's PCIe link, "
-                   "NVLink all-gather of the shared operands (whole-job bytes)"}
+            "api": "libsmm smm_mg_* (B sharded) with pinned host buffers: per-rank input shares over each GPU's "
+                   "PCIe link, B's column blocks all-gathered over NVLink inside the call (whole-job bytes)"}
 
 
 # ---------------------------------------------------------------- reference arm

@@ -45,13 +45,10 @@ Operand structured_op(const float* src, int dim, int row0 = 0);
 
 // C(M x N, ldc) = Aop(M x K) * B(K x N) on stream st.  Optionally also
 // writes lo(C) (C_lo, same ldc) or bf16(C) (C_bf16, ldc_bf16) from the
-// epilogue, so that C can feed a following product.  `wide`: the launch
-// shares the GPU with concurrent launches of the same product (the
-// multi-GPU column blocks), so it takes the efficient 256-row pair tiles
-// even when it alone would fill less than a wave.
+// epilogue, so that C can feed a following product.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
                     int N, int K, cudaStream_t st, float* C_lo = nullptr, __nv_bfloat16* C_bf16 = nullptr,
-                    int ldc_bf16 = 0, bool wide = false);
+                    int ldc_bf16 = 0);
 
 // ---------------------------------------------------------------- staging
 // A TMA-fed operand (rows x cols row-major): the caller's array or a padded
@@ -73,6 +70,13 @@ size_t staged_bytes_bound(int rows, int cols, int mode);
 // Stages src (rows x cols, leading dimension cols) for TMA, advancing ws_cur
 // past any copy it writes.
 int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st);
+
+// bf16 copy (round to nearest even) of a rows x cols block of an fp32 matrix
+// with leading dimension ld_src (src and ld_src 16-byte aligned for vector
+// loads, else scalar) into dst with leading dimension ld_dst (a multiple of
+// 8; columns cols .. ld_dst - 1 written as zeros).
+int convert_block_bf16(const float* src, int rows, int cols, int ld_src, __nv_bfloat16* dst, int ld_dst,
+                       cudaStream_t st);
 
 // Bytes of the dense copy of `rows` rows of a packed operand of order n.
 size_t expanded_bytes(int rows, int n, int mode);

@@ -118,9 +118,9 @@ int launch_persist(const Maps& m, const UmmaParams& p, cudaStream_t st) {
 // Dense / UpperDense x Dense, TF32 or bf16 (smm_kern_dense.cu).
 int launch_dense_persist(AKind ak, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st);
 
-// Dense x Dense with 128 x 128 tiles, each split over two CTAs along K
-// (smm_kern_dense.cu).
-int launch_dense_split(int mode, const Maps& m, const UmmaParams& p, cudaStream_t st);
+// Dense / UpperDense x Dense with 128 x 128 tiles, each split over two CTAs
+// along K (smm_kern_dense.cu).
+int launch_dense_split(AKind ak, int mode, const Maps& m, const UmmaParams& p, cudaStream_t st);
 
 // One launcher per translation unit; each returns SMM_ERR_INVALID for
 // pairings it does not hold.

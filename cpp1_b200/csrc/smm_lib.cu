@@ -144,17 +144,22 @@ int pick_bn(int M, int N, bool pair) {
 }
 
 // Split the K range of each 128 x 128 output tile over a cluster of two
-// CTAs: dense x dense products whose single-CTA tiles fill well under a
-// wave (at most 74 tiles of 148 SMs) and whose K range gives each half at
-// least 16 k-blocks.  SMM_SPLITK=0 disables it, SMM_SPLITK=2 forces it for
-// every dense product without CTA pairs.
+// CTAs: dense (or dense upper-triangular) x dense products whose
+// single-CTA tiles fill well under a wave (at most 74 tiles of 148 SMs) and
+// whose longest K range gives each half at least 16 k-blocks (the heaviest
+// row slab of a multi-GPU U B at 8 GPUs: 512 rows with K ~ 8000, where one
+// 256 x 256 pair tile alone takes longer than the whole slab should).
+// SMM_SPLITK=0 disables it, SMM_SPLITK=2 forces it for every such product
+// without CTA pairs.
 bool use_split(AKind ak, BKind bk, const Operand& a, const Operand& b, bool pair, int M, int N, int K) {
-  if (ak != AKind::Dense || bk != BKind::Dense || pair || a.lower || b.tri != 0) return false;
+  if ((ak != AKind::Dense && ak != AKind::UpperDense) || bk != BKind::Dense || pair || a.lower || b.tri != 0)
+    return false;
   const char* e = std::getenv("SMM_SPLITK");
   if (e && e[0] == '0') return false;
   if (e && e[0] == '2') return true;
   const long long tiles = static_cast<long long>((M + kBM - 1) / kBM) * ((N + 127) / 128);
-  return tiles <= 74 && K >= 512;
+  const int k_longest = ak == AKind::UpperDense ? K - a.row0 : K;
+  return tiles <= 74 && k_longest >= 512;
 }
 
 // Diagnostic record target for the next contraction launch (set by
@@ -180,11 +185,11 @@ int check_packed(const char* who, int N) {
 // Core contraction: C(M x N, ldc) = Aop(M x K) * B(K x N, ldb).
 // Preconditions: B (and A when dense) 16-byte aligned with ld % 4 == 0.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
-                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16, bool wide) {
+                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16) {
   const bool bf16 = (mode == SMM_MODE_BF16);
-  const bool pair = (wide && M > kBM) || use_pairs(M, N);
-  const bool split = !wide && use_split(ak, bk, a, b, pair, M, N, K);
-  const int bn = split ? 128 : ((wide && pair) ? (N > 128 ? 256 : 128) : pick_bn(M, N, pair));
+  const bool pair = use_pairs(M, N);
+  const bool split = use_split(ak, bk, a, b, pair, M, N, K);
+  const int bn = split ? 128 : pick_bn(M, N, pair);
   Maps m;
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);
@@ -243,7 +248,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   const bool persist = !(pe && pe[0] == '0') && !split && pair && bn == 256 && mode != SMM_MODE_3XTF32 &&
                        (ak == AKind::Dense || ak == AKind::UpperDense) && bk == BKind::Dense && !a.lower &&
                        b.tri == 0 && C_lo == nullptr && C_bf16 == nullptr;
-  const int rc = split     ? launch_dense_split(mode, m, p, st)
+  const int rc = split     ? launch_dense_split(ak, mode, m, p, st)
                  : persist ? launch_dense_persist(ak, mode, m, p, st)
                            : launch_kinds(ak, bk, bn, pair, mode, m, p, st);
   if (rc == SMM_OK && ev_after) SMM_CUDA_TRY(cudaEventRecord(ev_after, st), "record event after the contraction");

@@ -44,6 +44,7 @@ struct NcclApi {
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*allgather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
@@ -66,9 +67,11 @@ const NcclApi& nccl() {
     api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
     api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
     api.broadcast = reinterpret_cast<decltype(api.broadcast)>(sym("ncclBroadcast"));
+    api.allgather = reinterpret_cast<decltype(api.allgather)>(sym("ncclAllGather"));
     api.comm_get_async_error = reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
     api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.comm_abort && api.broadcast &&
+             api.allgather &&
              api.comm_get_async_error && api.error_string;
     if (!api.ok) snprintf(api.why, sizeof(api.why), "libnccl.so.2 lacks an entry point libsmm needs");
   });
@@ -222,47 +225,141 @@ int check_comm(const smm_mg_comm* c, const char* who) {
   return SMM_OK;
 }
 
-// Workspace of the B side: the packed column blocks (world > 1) and, in bf16
-// mode, their bf16 copies (one plane per block; at world 1 one plane of B).
-size_t b_side_bytes(int world, int K, int ncols, int mode) {
-  int cb[kMaxChunks + 1];
-  const int nch = chunk_bounds(ncols, world, cb);
-  size_t b = world > 1 ? round256(static_cast<size_t>(K) * ncols * 4) : 0;
-  if (mode == SMM_MODE_BF16)
-    for (int j = 0; j < nch; ++j) b += bf16_plane_bytes(K, cb[j + 1] - cb[j]);
+// Rows of each rank's share of B when B arrives sharded by rows: ceil(K / world).
+int share_rows(int K, int world) { return (K + world - 1) / world; }
+
+// The shared right operand B of one call, in column blocks.  At world > 1
+// every block travels into a contiguous plane of the workspace: from the
+// root (ncclBroadcast; the root first packs the block out of its B), or,
+// when B is sharded by rows, gathered from every rank's share (each rank
+// packs its share's columns of the block, ncclAllGather concatenates the
+// shares: rank r's rows land at r * share).  In bf16 mode the blocks travel
+// as bf16 (converted before the collective: half the NVLink bytes, the same
+// rounding as converting after it).  At world 1 the fp32 modes read B in
+// place and bf16 converts it once.
+struct BSide {
+  int K = 0, ncols = 0, nch = 0;
+  int cb[kMaxChunks + 1] = {};
+  bool bf = false;       // blocks are bf16
+  bool sharded = false;  // B arrives as row shares
+  int world = 1, rank = 0, root = 0;
+  int share = 0, valid = 0;  // sharded: rows per share, rows of this rank's share inside K
+  int rows = 0;              // rows of a block plane
+  uint8_t* planes = nullptr;
+  uint8_t* send = nullptr;   // sharded: this rank's part of each block
+  int width(int j) const { return cb[j + 1] - cb[j]; }
+  int ld(int j) const { return bf ? round8(width(j)) : width(j); }
+  size_t esz() const { return bf ? 2 : 4; }
+  size_t plane_bytes_of(int j, int r) const { return round256(static_cast<size_t>(r) * ld(j) * esz()); }
+  uint8_t* plane(int j) const {
+    uint8_t* p = planes;
+    for (int i = 0; i < j; ++i) p += plane_bytes_of(i, rows);
+    return p;
+  }
+  uint8_t* send_part(int j) const {
+    uint8_t* p = send;
+    for (int i = 0; i < j; ++i) p += plane_bytes_of(i, share);
+    return p;
+  }
+  bool travels() const { return world > 1; }
+  // Whether block j's contraction reads the caller's B in place (no wait).
+  bool in_place() const { return !bf && (world == 1 || (!sharded && rank == root)); }
+};
+
+BSide make_bside(const smm_mg_comm* c, int K, int ncols, int mode, int root, void* ws) {
+  BSide b;
+  b.K = K;
+  b.ncols = ncols;
+  b.nch = chunk_bounds(ncols, c->world, b.cb);
+  b.bf = mode == SMM_MODE_BF16;
+  b.sharded = root == SMM_MG_SHARDED;
+  b.world = c->world;
+  b.rank = c->rank;
+  b.root = b.sharded ? 0 : root;
+  b.share = share_rows(K, c->world);
+  b.valid = std::max(0, std::min(b.share, K - c->rank * b.share));
+  b.rows = (b.sharded && c->world > 1) ? c->world * b.share : K;
+  b.planes = static_cast<uint8_t*>(ws);
+  size_t pb = 0;
+  if (b.travels() || b.bf)
+    for (int j = 0; j < b.nch; ++j) pb += b.plane_bytes_of(j, std::max(K, c->world * b.share));
+  b.send = b.planes + pb;
   return b;
 }
 
-// The B side of one call.  world > 1: the collective stream waits for the
-// caller's stream, then per block j the root packs B[:, block j] into its
-// K x W_j buffer (contiguous, at offset K * cb[j] of `pack`) and every rank
-// receives it there; ev_chunk[j] marks its arrival.  (The sandwich's
-// S_packed, s_count floats, is broadcast first, marked by ev_s.)
-int broadcast_blocks(smm_mg_comm* c, const float* B, int K, int ncols, float* pack, const int* cb, int nch, int root,
-                     cudaStream_t st, float* S_packed = nullptr, size_t s_count = 0) {
-  if (c->world == 1) return SMM_OK;
-  SMM_CUDA_TRY(cudaEventRecord(c->ev_start, st), "record call start");
-  SMM_CUDA_TRY(cudaStreamWaitEvent(c->cs, c->ev_start, 0), "order broadcast after the caller's stream");
-  const NcclApi& n = nccl();
-  if (S_packed) {
-    SMM_NCCL_TRY(n.broadcast(S_packed, S_packed, s_count, ncclFloat, root, c->nc, c->cs), "ncclBroadcast (S)");
-    SMM_CUDA_TRY(cudaEventRecord(c->ev_s, c->cs), "record S arrival");
-  }
-  // The root packs every block first: the packs are enqueued before its own
-  // slab's contractions, so they take the SMs at once instead of competing
-  // with them between broadcasts.
-  if (c->rank == root) {
-    for (int j = 0; j < nch; ++j) {
-      pack_cols_kernel<<<148 * 4, 256, 0, c->cs>>>(B, ncols, cb[j], K, cb[j + 1] - cb[j],
-                                                   pack + static_cast<size_t>(K) * cb[j]);
+// Workspace of the B side: the block planes (world > 1, or bf16), sized for
+// the larger sharded row count, and the send parts of a sharded call.
+size_t b_side_bytes(int world, int K, int ncols, int mode) {
+  smm_mg_comm probe;
+  probe.world = world;
+  const BSide b = make_bside(&probe, K, ncols, mode, 0, nullptr);
+  size_t total = 0;
+  if (b.travels() || b.bf)
+    for (int j = 0; j < b.nch; ++j) total += b.plane_bytes_of(j, std::max(K, world * b.share));
+  if (b.travels())
+    for (int j = 0; j < b.nch; ++j) total += b.plane_bytes_of(j, b.share);
+  return total;
+}
+
+// Copies rows [0, rows) of column block j of src (leading dimension ncols)
+// into dst (leading dimension ld(j)), fp32 or bf16; rows [rows, pad_rows) of
+// dst are zeroed.
+int pack_block(const BSide& b, const float* src, int rows, int pad_rows, int j, uint8_t* dst, cudaStream_t st) {
+  const int w = b.width(j);
+  if (rows > 0) {
+    if (b.bf) {
+      if (int rc = convert_block_bf16(src + b.cb[j], rows, w, b.ncols, reinterpret_cast<__nv_bfloat16*>(dst), b.ld(j),
+                                      st))
+        return rc;
+    } else {
+      pack_cols_kernel<<<148 * 4, 256, 0, st>>>(src, b.ncols, b.cb[j], rows, w, reinterpret_cast<float*>(dst));
       count_launch();
       SMM_CUDA_TRY(cudaGetLastError(), "pack column block of B");
     }
   }
-  for (int j = 0; j < nch; ++j) {
-    const int w = cb[j + 1] - cb[j];
-    float* blk = pack + static_cast<size_t>(K) * cb[j];
-    SMM_NCCL_TRY(n.broadcast(blk, blk, static_cast<size_t>(K) * w, ncclFloat, root, c->nc, c->cs),
+  if (pad_rows > rows)
+    SMM_CUDA_TRY(cudaMemsetAsync(dst + static_cast<size_t>(std::max(rows, 0)) * b.ld(j) * b.esz(), 0,
+                                 static_cast<size_t>(pad_rows - std::max(rows, 0)) * b.ld(j) * b.esz(), st),
+                 "zero share padding");
+  return SMM_OK;
+}
+
+// Starts the B side of one call on the collective stream (ordered after the
+// caller's stream): ev_chunk[j] marks block j's arrival.  The sandwich's
+// S_packed (s_count floats) is broadcast first from the root (rank 0 when B
+// is sharded), marked by ev_s.  At world 1, bf16 converts B on `st`.
+int start_bside(smm_mg_comm* c, const BSide& b, const float* B, cudaStream_t st, float* S_packed = nullptr,
+                size_t s_count = 0) {
+  if (!b.travels()) {
+    if (b.bf)
+      return convert_block_bf16(B, b.K, b.ncols, b.ncols, reinterpret_cast<__nv_bfloat16*>(b.planes), b.ld(0), st);
+    return SMM_OK;
+  }
+  SMM_CUDA_TRY(cudaEventRecord(c->ev_start, st), "record call start");
+  SMM_CUDA_TRY(cudaStreamWaitEvent(c->cs, c->ev_start, 0), "order the collectives after the caller's stream");
+  const NcclApi& n = nccl();
+  if (S_packed) {
+    SMM_NCCL_TRY(n.broadcast(S_packed, S_packed, s_count, ncclFloat, b.root, c->nc, c->cs), "ncclBroadcast (S)");
+    SMM_CUDA_TRY(cudaEventRecord(c->ev_s, c->cs), "record S arrival");
+  }
+  const ncclDataType_t ty = b.bf ? ncclBfloat16 : ncclFloat;
+  // Every pack first: enqueued before this rank's contractions, they take
+  // the SMs at once instead of competing with them between collectives.
+  if (b.sharded) {
+    for (int j = 0; j < b.nch; ++j)
+      if (int rc = pack_block(b, B, b.valid, b.share, j, b.send_part(j), c->cs)) return rc;
+    for (int j = 0; j < b.nch; ++j) {
+      SMM_NCCL_TRY(n.allgather(b.send_part(j), b.plane(j), static_cast<size_t>(b.share) * b.ld(j), ty, c->nc, c->cs),
+                   "ncclAllGather (column block of B)");
+      SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record block arrival");
+    }
+    return SMM_OK;
+  }
+  if (c->rank == b.root)
+    for (int j = 0; j < b.nch; ++j)
+      if (int rc = pack_block(b, B, b.K, b.K, j, b.plane(j), c->cs)) return rc;
+  for (int j = 0; j < b.nch; ++j) {
+    SMM_NCCL_TRY(n.broadcast(b.plane(j), b.plane(j), static_cast<size_t>(b.K) * b.ld(j), ty, b.root, c->nc, c->cs),
                  "ncclBroadcast (column block of B)");
     SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record block arrival");
   }
@@ -272,17 +369,17 @@ int broadcast_blocks(smm_mg_comm* c, const float* B, int K, int ncols, float* pa
 // Runs block(j, stream) for every column block: at world 1 the single block
 // on the caller's stream; else block j on compute stream j % kWork once the
 // left operand is prepared (ev_prep, recorded on the caller's stream) and,
-// with wait_blocks, the block has landed; the caller's stream then waits for
-// all of them.
+// unless it reads B in place, the block has landed; the caller's stream then
+// waits for all of them.
 template <typename F>
-int run_blocks(smm_mg_comm* c, int nch, cudaStream_t st, bool wait_blocks, F&& block) {
+int run_blocks(smm_mg_comm* c, const BSide& b, cudaStream_t st, F&& block) {
   if (c->world == 1) return block(0, st);
   SMM_CUDA_TRY(cudaEventRecord(c->ev_prep, st), "record operand preparation");
-  const int used = std::min(nch, kWork);
+  const int used = std::min(b.nch, kWork);
   for (int w = 0; w < used; ++w) SMM_CUDA_TRY(cudaStreamWaitEvent(c->work[w], c->ev_prep, 0), "fork");
-  for (int j = 0; j < nch; ++j) {
+  for (int j = 0; j < b.nch; ++j) {
     cudaStream_t w = c->work[j % kWork];
-    if (wait_blocks) SMM_CUDA_TRY(cudaStreamWaitEvent(w, c->ev_chunk[j], 0), "wait for block arrival");
+    if (!b.in_place()) SMM_CUDA_TRY(cudaStreamWaitEvent(w, c->ev_chunk[j], 0), "wait for block arrival");
     if (int rc = block(j, w)) return rc;
   }
   for (int w = 0; w < used; ++w) {
@@ -292,31 +389,12 @@ int run_blocks(smm_mg_comm* c, int nch, cudaStream_t st, bool wait_blocks, F&& b
   return SMM_OK;
 }
 
-// Whether column block j's contraction must wait for the block's broadcast:
-// the root reads its own B in place in the fp32 modes (bf16 converts the
-// packed block).
-bool waits_for_blocks(const smm_mg_comm* c, int root, int mode) { return c->rank != root || mode == SMM_MODE_BF16; }
-
-// The B operand of column block j (K x W_j): fp32 in place (the caller's B at
-// world 1 and on the root, the received block otherwise), or its bf16 copy
-// converted on `st` into the block's bf16 plane.
-int block_operand(const smm_mg_comm* c, const float* B, int K, int ncols, const float* pack, const int* cb, int j,
-                  int mode, uint8_t* bf_base, cudaStream_t st, Operand* out, int root) {
-  const int w = cb[j + 1] - cb[j];
-  if (mode != SMM_MODE_BF16) {
-    if (c->world == 1 || c->rank == root)
-      *out = dense_op(B + cb[j], nullptr, ncols);
-    else
-      *out = dense_op(pack + static_cast<size_t>(K) * cb[j], nullptr, w);
-    return SMM_OK;
-  }
-  const float* src = c->world == 1 ? B : pack + static_cast<size_t>(K) * cb[j];
-  uint8_t* cur = bf_base;
-  for (int i = 0; i < j; ++i) cur += bf16_plane_bytes(K, cb[i + 1] - cb[i]);
-  Staged s;
-  if (int rc = stage_operand(src, K, w, mode, cur, &s, st)) return rc;
-  *out = dense_op(nullptr, nullptr, s.ld, s.bf16);
-  return SMM_OK;
+// The B operand of column block j (K x W_j): the caller's B in place, or the
+// block's plane (fp32 or bf16).
+Operand block_operand(const BSide& b, const float* B, int j) {
+  if (b.in_place()) return dense_op(B + b.cb[j], nullptr, b.ncols);
+  if (b.bf) return dense_op(nullptr, nullptr, b.ld(j), reinterpret_cast<const __nv_bfloat16*>(b.plane(j)));
+  return dense_op(reinterpret_cast<const float*>(b.plane(j)), nullptr, b.ld(j));
 }
 
 bool aligned_rows(const float* p, int ld) { return aligned16(p) && ld % 4 == 0; }
@@ -445,16 +523,26 @@ extern "C" int smm_mg_chunks(int ncols, int world, int* bounds) {
 }
 
 namespace {
-// Validation shared by the products.
-int check_call(const smm_mg_comm* c, const char* who, int mode, int root, const float* B, int ncols) {
+// Validation shared by the products: B (K x ncols) is the root's whole B,
+// or with root SMM_MG_SHARDED this rank's share (rows [rank * s, rank * s +
+// valid) of B, s = smm_mg_share_rows(K, world)); either with 16-byte aligned
+// rows when it holds any.
+int check_call(const smm_mg_comm* c, const char* who, int mode, int root, const float* B, int K, int ncols) {
   if (int rc = check_comm(c, who)) return rc;
-  if (root < 0 || root >= c->world) return set_error(SMM_ERR_INVALID, "%s: root %d of %d", who, root, c->world);
+  if (root != SMM_MG_SHARDED && (root < 0 || root >= c->world))
+    return set_error(SMM_ERR_INVALID, "%s: root %d of %d", who, root, c->world);
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
-  if (c->rank == root && (!B || !aligned_rows(B, ncols)))
-    return set_error(SMM_ERR_INVALID, "%s: the root's B must be non-null with 16-byte aligned rows", who);
+  const bool holds = root == SMM_MG_SHARDED ? (K - c->rank * share_rows(K, c->world) > 0) : c->rank == root;
+  if (holds && K > 0 && ncols > 0 && (!B || !aligned_rows(B, ncols)))
+    return set_error(SMM_ERR_INVALID, "%s: this rank's B must be non-null with 16-byte aligned rows", who);
   return SMM_OK;
 }
 }  // namespace
+
+extern "C" int smm_mg_share_rows(int K, int world) {
+  if (K < 0 || world < 1) return set_error(SMM_ERR_INVALID, "smm_mg_share_rows: bad arguments");
+  return share_rows(K, world);
+}
 
 // ---------------------------------------------------------------- products
 extern "C" size_t smm_mg_gemm_workspace_size(const smm_mg_comm* c, int nrows, int N, int K, int mode) {
@@ -465,28 +553,22 @@ extern "C" size_t smm_mg_gemm_workspace_size(const smm_mg_comm* c, int nrows, in
 extern "C" int smm_mg_gemm(smm_mg_comm* c, const float* A_slab, const float* B, float* C_slab, int nrows, int N,
                            int K, int mode, int root, void* ws, size_t ws_bytes, void* stream) {
   SMM_RANGE("smm_mg_gemm");
-  if (int rc = check_call(c, "smm_mg_gemm", mode, root, B, N)) return rc;
+  if (int rc = check_call(c, "smm_mg_gemm", mode, root, B, K, N)) return rc;
   if (nrows < 0 || N < 0 || K < 0) return set_error(SMM_ERR_INVALID, "smm_mg_gemm: negative shape");
   if (N == 0 || K == 0) return SMM_OK;
   if (nrows > 0 && (!A_slab || !C_slab)) return set_error(SMM_ERR_INVALID, "smm_mg_gemm: null pointer");
   if (int rc = check_ws("smm_mg_gemm", ws, ws_bytes, smm_mg_gemm_workspace_size(c, nrows, N, K, mode))) return rc;
   cudaStream_t st = as_stream(stream);
-  int cb[kMaxChunks + 1];
-  const int nch = chunk_bounds(N, c->world, cb);
-  uint8_t* cur = static_cast<uint8_t*>(ws);
-  float* pack = reinterpret_cast<float*>(cur);
-  uint8_t* bf = cur + (c->world > 1 ? round256(static_cast<size_t>(K) * N * 4) : 0);
-  cur += b_side_bytes(c->world, K, N, mode);
-  if (int rc = broadcast_blocks(c, B, K, N, pack, cb, nch, root, st)) return rc;
+  const BSide b = make_bside(c, K, N, mode, root, ws);
+  uint8_t* cur = static_cast<uint8_t*>(ws) + b_side_bytes(c->world, K, N, mode);
+  if (int rc = start_bside(c, b, B, st)) return rc;
   Staged a{};
   if (nrows > 0)
     if (int rc = stage_operand(A_slab, nrows, K, mode, cur, &a, st)) return rc;
-  return run_blocks(c, nch, st, waits_for_blocks(c, root, mode), [&](int j, cudaStream_t w) -> int {
+  return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
     if (nrows == 0) return SMM_OK;
-    Operand bo;
-    if (int rc = block_operand(c, B, K, N, pack, cb, j, mode, bf, w, &bo, root)) return rc;
-    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16), bo,
-                           C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], K, w, nullptr, nullptr, 0, true);
+    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16),
+                           block_operand(b, B, j), C_slab + b.cb[j], N, nrows, b.width(j), K, w);
   });
 }
 
@@ -499,7 +581,7 @@ extern "C" int smm_mg_upper_left(smm_mg_comm* c, const float* U_packed, const fl
                                  int ncols, int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes,
                                  void* stream) {
   SMM_RANGE("smm_mg_upper_left");
-  if (int rc = check_call(c, "smm_mg_upper_left", mode, root, B, ncols)) return rc;
+  if (int rc = check_call(c, "smm_mg_upper_left", mode, root, B, N, ncols)) return rc;
   if (N < 0 || ncols < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N)
     return set_error(SMM_ERR_INVALID, "smm_mg_upper_left: bad shape or slab");
   if (int rc = check_packed("smm_mg_upper_left", N)) return rc;
@@ -508,25 +590,19 @@ extern "C" int smm_mg_upper_left(smm_mg_comm* c, const float* U_packed, const fl
   if (int rc = check_ws("smm_mg_upper_left", ws, ws_bytes, smm_mg_upper_left_workspace_size(c, N, ncols, nrows, mode)))
     return rc;
   cudaStream_t st = as_stream(stream);
-  int cb[kMaxChunks + 1];
-  const int nch = chunk_bounds(ncols, c->world, cb);
-  uint8_t* cur = static_cast<uint8_t*>(ws);
-  float* pack = reinterpret_cast<float*>(cur);
-  uint8_t* bf = cur + (c->world > 1 ? round256(static_cast<size_t>(N) * ncols * 4) : 0);
-  cur += b_side_bytes(c->world, N, ncols, mode);
-  if (int rc = broadcast_blocks(c, B, N, ncols, pack, cb, nch, root, st)) return rc;
+  const BSide b = make_bside(c, N, ncols, mode, root, ws);
+  uint8_t* cur = static_cast<uint8_t*>(ws) + b_side_bytes(c->world, N, ncols, mode);
+  if (int rc = start_bside(c, b, B, st)) return rc;
   Staged u{};  // rows [row0, row0 + nrows) of U, dense (zeros left of the diagonal)
   if (nrows > 0)
     if (int rc = expand_operand(U_packed, SMM_STRUCT_UPPER, N, row0, nrows, mode, cur, &u, st)) return rc;
-  return run_blocks(c, nch, st, waits_for_blocks(c, root, mode), [&](int j, cudaStream_t w) -> int {
+  return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
     if (nrows == 0) return SMM_OK;
-    Operand bo;
-    if (int rc = block_operand(c, B, N, ncols, pack, cb, j, mode, bf, w, &bo, root)) return rc;
     Operand ao = dense_op(u.ptr, nullptr, u.ld, u.bf16);
     ao.dim = N;
     ao.row0 = row0;
-    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, bo, C_slab + cb[j], ncols, nrows,
-                           cb[j + 1] - cb[j], N, w, nullptr, nullptr, 0, true);
+    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, block_operand(b, B, j), C_slab + b.cb[j],
+                           ncols, nrows, b.width(j), N, w);
   });
 }
 
@@ -539,7 +615,7 @@ extern "C" int smm_mg_toeplitz_left(smm_mg_comm* c, const float* g, const float*
                                     int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes,
                                     void* stream) {
   SMM_RANGE("smm_mg_toeplitz_left");
-  if (int rc = check_call(c, "smm_mg_toeplitz_left", mode, root, B, ncols)) return rc;
+  if (int rc = check_call(c, "smm_mg_toeplitz_left", mode, root, B, N, ncols)) return rc;
   if (N < 0 || ncols < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N)
     return set_error(SMM_ERR_INVALID, "smm_mg_toeplitz_left: bad shape or slab");
   if (N == 0 || ncols == 0) return SMM_OK;
@@ -547,27 +623,22 @@ extern "C" int smm_mg_toeplitz_left(smm_mg_comm* c, const float* g, const float*
   if (int rc = check_ws("smm_mg_toeplitz_left", ws, ws_bytes, smm_mg_toeplitz_left_workspace_size(c, N, ncols, mode)))
     return rc;
   cudaStream_t st = as_stream(stream);
-  int cb[kMaxChunks + 1];
-  const int nch = chunk_bounds(ncols, c->world, cb);
-  float* pack = static_cast<float*>(ws);
-  uint8_t* bf = static_cast<uint8_t*>(ws) + (c->world > 1 ? round256(static_cast<size_t>(N) * ncols * 4) : 0);
-  if (int rc = broadcast_blocks(c, B, N, ncols, pack, cb, nch, root, st)) return rc;
-  return run_blocks(c, nch, st, waits_for_blocks(c, root, mode), [&](int j, cudaStream_t w) -> int {
+  const BSide b = make_bside(c, N, ncols, mode, root, ws);
+  if (int rc = start_bside(c, b, B, st)) return rc;
+  return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
     if (nrows == 0) return SMM_OK;
-    Operand bo;
-    if (int rc = block_operand(c, B, N, ncols, pack, cb, j, mode, bf, w, &bo, root)) return rc;
-    return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), bo, C_slab + cb[j], ncols,
-                           nrows, cb[j + 1] - cb[j], N, w, nullptr, nullptr, 0, true);
+    return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), block_operand(b, B, j),
+                           C_slab + b.cb[j], ncols, nrows, b.width(j), N, w);
   });
 }
 
 namespace {
-// Sandwich workspace beyond the B side: Y = A_slab S (fp32, 16-byte rows;
-// plus its bf16 copy in bf16 mode), the dense expansion of S, the staged A slab.
+// Sandwich workspace beyond the B side: Y = A_slab S (bf16 in bf16 mode,
+// else fp32; 16-byte rows), the dense expansion of S, the staged A slab.
 size_t mg_sandwich_left(int N, int nrows, int mode) {
   if (nrows == 0) return 0;
   const bool bf = mode == SMM_MODE_BF16;
-  return plane_bytes(nrows, N) + (bf ? bf16_plane_bytes(nrows, N) : 0) + expanded_bytes(N, N, mode) +
+  return (bf ? bf16_plane_bytes(nrows, N) : plane_bytes(nrows, N)) + expanded_bytes(N, N, mode) +
          staged_bytes_bound(nrows, N, mode);
 }
 }  // namespace
@@ -581,7 +652,7 @@ extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* 
                                     float* C_slab, int N, int nrows, int mode, int root, void* ws, size_t ws_bytes,
                                     void* stream) {
   SMM_RANGE("smm_mg_symm_sandwich");
-  if (int rc = check_call(c, "smm_mg_symm_sandwich", mode, root, B, N)) return rc;
+  if (int rc = check_call(c, "smm_mg_symm_sandwich", mode, root, B, N, N)) return rc;
   if (N < 0 || nrows < 0 || nrows > N) return set_error(SMM_ERR_INVALID, "smm_mg_symm_sandwich: bad shape");
   if (int rc = check_packed("smm_mg_symm_sandwich", N)) return rc;
   if (N == 0) return SMM_OK;
@@ -591,26 +662,24 @@ extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* 
     return rc;
   cudaStream_t st = as_stream(stream);
   const bool bf = mode == SMM_MODE_BF16;
-  int cb[kMaxChunks + 1];
-  const int nch = chunk_bounds(N, c->world, cb);
-  uint8_t* cur = static_cast<uint8_t*>(ws);
-  float* pack = reinterpret_cast<float*>(cur);
-  uint8_t* bfb = cur + (c->world > 1 ? round256(static_cast<size_t>(N) * N * 4) : 0);
-  cur += b_side_bytes(c->world, N, N, mode);
-  // S travels whole first (packed, N(N+1)/2 floats), then B in column blocks.
-  if (int rc = broadcast_blocks(c, B, N, N, pack, cb, nch, root, st, S_packed, static_cast<size_t>(N) * (N + 1) / 2))
-    return rc;
+  const BSide b = make_bside(c, N, N, mode, root, ws);
+  uint8_t* cur = static_cast<uint8_t*>(ws) + b_side_bytes(c->world, N, N, mode);
+  // S travels whole first (packed, N(N+1)/2 floats, from the root; rank 0
+  // when B is sharded), then B in column blocks.
+  if (int rc = start_bside(c, b, B, st, S_packed, static_cast<size_t>(N) * (N + 1) / 2)) return rc;
   float* Y = nullptr;
   __nv_bfloat16* Y_bf = nullptr;
-  const int ldy = round4(N), ldy_bf = round8(N);
+  const int ldy = bf ? round8(N) : round4(N);
   if (nrows > 0) {
-    // Y = A_slab S: the reference's run_graph order, (A S) first
-    Y = reinterpret_cast<float*>(cur);
-    cur += plane_bytes(nrows, N);
+    // Y = A_slab S: the reference's run_graph order, (A S) first; in bf16
+    // mode only Y's bf16 copy is written (the second product's operand)
     if (bf) {
       Y_bf = reinterpret_cast<__nv_bfloat16*>(cur);
       cur += bf16_plane_bytes(nrows, N);
-      if (ldy_bf != N) SMM_CUDA_TRY(cudaMemsetAsync(Y_bf, 0, bf16_plane_bytes(nrows, N), st), "zero bf16 rows");
+      if (ldy != N) SMM_CUDA_TRY(cudaMemsetAsync(Y_bf, 0, bf16_plane_bytes(nrows, N), st), "zero bf16 rows");
+    } else {
+      Y = reinterpret_cast<float*>(cur);
+      cur += plane_bytes(nrows, N);
     }
     Staged a;
     if (int rc = stage_operand(A_slab, nrows, N, mode, cur, &a, st)) return rc;
@@ -618,15 +687,13 @@ extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* 
     Staged s;  // S mirrored into a dense copy: the right operand of Y = A_slab S
     if (int rc = expand_operand(S_packed, SMM_STRUCT_SYMM, N, 0, N, mode, cur, &s, st)) return rc;
     if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16),
-                                 dense_op(s.ptr, nullptr, s.ld, s.bf16), bf ? nullptr : Y, ldy, nrows, N, N, st, nullptr, Y_bf,
-                                 ldy_bf))
+                                 dense_op(s.ptr, nullptr, s.ld, s.bf16), Y, ldy, nrows, N, N, st, nullptr, Y_bf,
+                                 ldy))
       return rc;
   }
-  return run_blocks(c, nch, st, waits_for_blocks(c, root, mode), [&](int j, cudaStream_t w) -> int {
+  return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
     if (nrows == 0) return SMM_OK;
-    Operand bo;
-    if (int rc = block_operand(c, B, N, N, pack, cb, j, mode, bfb, w, &bo, root)) return rc;
-    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(bf ? nullptr : Y, nullptr, bf ? ldy_bf : ldy, Y_bf),
-                           bo, C_slab + cb[j], N, nrows, cb[j + 1] - cb[j], N, w, nullptr, nullptr, 0, true);
+    return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(Y, nullptr, ldy, Y_bf), block_operand(b, B, j),
+                           C_slab + b.cb[j], N, nrows, b.width(j), N, w);
   });
 }

@@ -162,6 +162,18 @@ size_t staged_bytes_bound(int rows, int cols, int mode) {
   return plane_bytes(rows, cols);
 }
 
+int convert_block_bf16(const float* src, int rows, int cols, int ld_src, __nv_bfloat16* dst, int ld_dst,
+                       cudaStream_t st) {
+  if (rows <= 0 || ld_dst <= 0) return SMM_OK;
+  const int gx = (ld_dst / 8 + 255) / 256;
+  const int gy = std::max(1, std::min(rows, std::max(1, 148 * 16 / gx)));
+  const int vec = (ld_src % 4 == 0 && aligned16(src)) ? 1 : 0;
+  to_bf16_kernel<<<dim3(gx, gy), 256, 0, st>>>(src, rows, cols, ld_src, dst, ld_dst, vec);
+  count_launch();
+  SMM_CUDA_TRY(cudaGetLastError(), "bf16 block conversion launch");
+  return SMM_OK;
+}
+
 int stage_operand(const float* src, int rows, int cols, int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st) {
   if (mode == SMM_MODE_BF16) {
     const int ld = round8(cols);

@@ -16,9 +16,10 @@ packed U, Toeplitz generator, packed S):
 * the diagonal scale shards with no collective at all (rows independent).
 
 ``Communicator`` wraps libsmm's own NCCL communicator (``smm_mg_*``): each
-product call broadcasts B from the root in column blocks on a high-priority
-stream and computes this rank's slab block by block as they land, so the
-transfer overlaps the tensor-core work inside one call.
+product call brings B to every rank in column blocks on a high-priority
+stream -- broadcast from a root rank, or all-gathered from row shares when B
+is sharded -- and computes this rank's slab block by block as they land, so
+the transfer overlaps the tensor-core work inside one call.
 
 No kernel reads another GPU's memory; remote data reaches local HBM through
 NCCL before any kernel touches it.
@@ -243,55 +244,96 @@ class Communicator:
         return (buf.data_ptr(), buf.numel()) if buf is not None else (None, 0)
 
     # ---- products (every rank calls them with the same shapes, mode and root)
-    def gemm(self, A_slab, B, C_slab, mode: str = "3xtf32", root: int = 0, stream=None):
-        """C_slab = A_slab @ B with B broadcast from `root` (read on the root
-        only; other ranks pass a tensor of the same shape, whose content is
-        not used)."""
+    # root: the rank holding all of B (broadcast), or SHARDED: B is this
+    # rank's share, rows [rank * s, rank * s + s) of B with s = share_rows(K,
+    # world) (all-gathered inside the call).
+    @staticmethod
+    def _root(root) -> int:
+        return SHARDED if root in (SHARDED, "sharded") else int(root)
+
+    def gemm(self, A_slab, B, C_slab, mode: str = "3xtf32", root=0, stream=None):
+        """C_slab = A_slab @ B.  Broadcast: B is read on the root only (the
+        other ranks pass a tensor of the same shape, whose content is not
+        used).  Sharded: B is this rank's share of B's rows."""
         L = self._lib.load()
         m = self._lib.MODES[mode]
         nrows, K = A_slab.shape
         N = B.shape[1]
         ws, wsb = self._ws(L.smm_mg_gemm_workspace_size(self.h, nrows, N, K, m), B.device)
         self._lib.check(L.smm_mg_gemm(self.h, A_slab.data_ptr(), B.data_ptr(), C_slab.data_ptr(), nrows, N, K, m,
-                                      root, ws, wsb, self._stream(stream)), "smm_mg_gemm")
+                                      self._root(root), ws, wsb, self._stream(stream)), "smm_mg_gemm")
         return C_slab
 
-    def upper_left(self, U, B, C_slab, row0: int, mode: str = "3xtf32", root: int = 0, stream=None):
-        """C_slab = U[row0:row0+nrows] @ B, U packed upper on every rank."""
+    def upper_left(self, U, B, C_slab, row0: int, mode: str = "3xtf32", root=0, stream=None):
+        """C_slab = U[row0:row0+nrows] @ B, U packed upper on every rank (its
+        order N from the packed length)."""
         L = self._lib.load()
         m = self._lib.MODES[mode]
-        N, ncols = B.shape
+        N = packed_order(U.numel())
+        ncols = B.shape[1]
         nrows = C_slab.shape[0] if C_slab is not None else 0
         ws, wsb = self._ws(L.smm_mg_upper_left_workspace_size(self.h, N, ncols, nrows, m), B.device)
         cp = C_slab.data_ptr() if nrows else None
-        self._lib.check(L.smm_mg_upper_left(self.h, U.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m, root,
-                                            ws, wsb, self._stream(stream)), "smm_mg_upper_left")
+        self._lib.check(L.smm_mg_upper_left(self.h, U.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m,
+                                            self._root(root), ws, wsb, self._stream(stream)), "smm_mg_upper_left")
         return C_slab
 
-    def toeplitz_left(self, g, B, C_slab, row0: int, mode: str = "3xtf32", root: int = 0, stream=None):
-        """C_slab = T[row0:row0+nrows] @ B, T of generator g on every rank."""
+    def toeplitz_left(self, g, B, C_slab, row0: int, mode: str = "3xtf32", root=0, stream=None):
+        """C_slab = T[row0:row0+nrows] @ B, T of generator g (2N - 1 values)
+        on every rank."""
         L = self._lib.load()
         m = self._lib.MODES[mode]
-        N, ncols = B.shape
+        N = (g.numel() + 1) // 2
+        ncols = B.shape[1]
         nrows = C_slab.shape[0] if C_slab is not None else 0
         ws, wsb = self._ws(L.smm_mg_toeplitz_left_workspace_size(self.h, N, ncols, m), B.device)
         cp = C_slab.data_ptr() if nrows else None
         self._lib.check(L.smm_mg_toeplitz_left(self.h, g.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m,
-                                               root, ws, wsb, self._stream(stream)), "smm_mg_toeplitz_left")
+                                               self._root(root), ws, wsb, self._stream(stream)),
+                        "smm_mg_toeplitz_left")
         return C_slab
 
-    def symm_sandwich(self, A_slab, S, B, C_slab, mode: str = "3xtf32", root: int = 0, stream=None):
-        """C_slab = (A_slab @ S) @ B with packed S and B broadcast from `root`."""
+    def symm_sandwich(self, A_slab, S, B, C_slab, mode: str = "3xtf32", root=0, stream=None):
+        """C_slab = (A_slab @ S) @ B with packed S (from the root; rank 0 when
+        B is sharded) and B from the root or sharded."""
         L = self._lib.load()
         m = self._lib.MODES[mode]
-        N = B.shape[0]
+        N = packed_order(S.numel())
         nrows = A_slab.shape[0] if A_slab is not None else 0
         ws, wsb = self._ws(L.smm_mg_symm_sandwich_workspace_size(self.h, N, nrows, m), B.device)
         ap = A_slab.data_ptr() if nrows else None
         cp = C_slab.data_ptr() if nrows else None
-        self._lib.check(L.smm_mg_symm_sandwich(self.h, ap, S.data_ptr(), B.data_ptr(), cp, N, nrows, m, root, ws,
-                                               wsb, self._stream(stream)), "smm_mg_symm_sandwich")
+        self._lib.check(L.smm_mg_symm_sandwich(self.h, ap, S.data_ptr(), B.data_ptr(), cp, N, nrows, m,
+                                               self._root(root), ws, wsb, self._stream(stream)),
+                        "smm_mg_symm_sandwich")
         return C_slab
+
+
+SHARDED = -1  # root value of a call whose B is sharded by rows (SMM_MG_SHARDED)
+
+
+def packed_order(length: int) -> int:
+    """Order N of a packed triangle of N (N + 1) / 2 values."""
+    n = int((math.isqrt(8 * length + 1) - 1) // 2)
+    if n * (n + 1) // 2 != length:
+        raise ValueError(f"{length} values are not a packed triangle")
+    return n
+
+
+def share_rows(k: int, world: int) -> int:
+    """Rows in each rank's share of a K-row B sharded over `world` ranks
+    (ceil(K / world), libsmm's smm_mg_share_rows)."""
+    if world < 1 or k < 0:
+        raise ValueError("bad share arguments")
+    return -(-k // world)
+
+
+def lib_share_rows(k: int, world: int) -> int:
+    from . import _lib
+    r = _lib.load().smm_mg_share_rows(k, world)
+    if r < 0:
+        _lib.check(r, "smm_mg_share_rows")
+    return r
 
 
 def lib_row_slabs(n: int, world: int, triangular: bool = False) -> List[int]:

@@ -184,22 +184,28 @@ int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float
 /* ---- multi-GPU products (one process per GPU, NCCL over NVLink) ------- */
 
 /* A product C = X B is partitioned by output row slabs, one per rank (GPU).
- * The shared right operand B lives on the root rank; inside each call it is
- * broadcast in column blocks on the communicator's high-priority stream (the
- * root packs each block contiguously into the workspace first), and this
- * rank computes the block's columns of its slab as soon as the block has
- * landed, on internal compute streams joined back into `stream` before the
- * call's work ends, so the transfer of later blocks overlaps the tensor-core
- * work on earlier ones.  Every output element comes from one full-K
- * contraction: the slab equals the single-GPU entry point's rows.  B is read
- * on the root only (16-byte aligned rows); the other ranks may pass NULL.
- * Calls are collective: every rank makes the same calls with the same shapes,
- * mode and root, in the same order.  No kernel reads another GPU's memory.
- * The reference has no multi-GPU code; this is the row-slab partition with a
- * broadcast of the shared operand that its single-GPU kernels scale to.
- * NCCL is loaded at run time (libnccl.so.2, the copy already in the process
- * when there is one).  At world = 1 the calls compute without any
- * collective. */
+ * The shared right operand B reaches every rank inside each call, in column
+ * blocks, on the communicator's high-priority stream, and this rank computes
+ * the block's columns of its slab as soon as the block has landed, on
+ * internal compute streams joined back into `stream` before the call's work
+ * ends, so the transfer of later blocks overlaps the tensor-core work on
+ * earlier ones.  B comes either from one root rank (`root` = its rank; the
+ * root packs each block contiguously and broadcasts it; B is read on the
+ * root only, the other ranks may pass NULL), or sharded by rows (`root` =
+ * SMM_MG_SHARDED: each rank passes its share, rows [rank * s, min(K, (rank +
+ * 1) * s)) of B with s = smm_mg_share_rows(K, world), and the blocks are
+ * all-gathered from the shares).  Either way B's rows are 16-byte aligned.
+ * In bf16 mode the blocks travel as bf16 (half the bytes; the same rounding
+ * as the single-GPU conversion).  Every output element comes from one
+ * full-K contraction: the slab equals the single-GPU entry point's rows.
+ * Calls are collective: every rank makes the same calls with the same
+ * shapes, mode and root, in the same order.  No kernel reads another GPU's
+ * memory.  The reference has no multi-GPU code; this is the row-slab
+ * partition with the shared operand sent over NVLink that its single-GPU
+ * kernels scale to.  NCCL is loaded at run time (libnccl.so.2, the copy
+ * already in the process when there is one).  At world = 1 the calls
+ * compute without any collective. */
+#define SMM_MG_SHARDED (-1)
 #define SMM_MG_ID_BYTES 128
 typedef struct smm_mg_comm smm_mg_comm;
 
@@ -227,6 +233,10 @@ int smm_mg_row_slabs(int N, int world, int triangular, int* bounds);
  * SMM_MG_CHUNKS in the environment sets the count (1 .. 16; default 4). */
 int smm_mg_chunks(int ncols, int world, int* bounds);
 
+/* Rows in each rank's share of a K-row B sharded over `world` ranks:
+ * ceil(K / world) (the last shares may hold fewer rows of B, or none). */
+int smm_mg_share_rows(int K, int world);
+
 /* C_slab (nrows x N) = A_slab (nrows x K, this rank's rows of A) B (K x N). */
 size_t smm_mg_gemm_workspace_size(const smm_mg_comm* comm, int nrows, int N, int K, int mode);
 int smm_mg_gemm(smm_mg_comm* comm, const float* A_slab, const float* B, float* C_slab, int nrows, int N, int K,
@@ -241,9 +251,10 @@ int smm_mg_upper_left(smm_mg_comm* comm, const float* U_packed, const float* B, 
 size_t smm_mg_toeplitz_left_workspace_size(const smm_mg_comm* comm, int N, int ncols, int mode);
 int smm_mg_toeplitz_left(smm_mg_comm* comm, const float* g, const float* B, float* C_slab, int N, int ncols,
                          int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
-/* C_slab (nrows x N) = (A_slab S) B, S packed symmetric (the root's input; a
- * receive buffer of N(N+1)/2 floats on the other ranks) and B broadcast from
- * the root: the reference's run_graph order, (A S) then times B, per row slab. */
+/* C_slab (nrows x N) = (A_slab S) B, S packed symmetric (the root's input,
+ * rank 0's when B is sharded; a receive buffer of N(N+1)/2 floats on the
+ * other ranks): the reference's run_graph order, (A S) then times B, per row
+ * slab. */
 size_t smm_mg_symm_sandwich_workspace_size(const smm_mg_comm* comm, int N, int nrows, int mode);
 int smm_mg_symm_sandwich(smm_mg_comm* comm, const float* A_slab, float* S_packed, const float* B, float* C_slab,
                          int N, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);

@@ -1,14 +1,16 @@
 """libsmm's multi-GPU products on two GPUs (skipped with fewer).
 
-Two processes, one per GPU.  Rank 0 holds B (and S for the sandwich); the
-other rank passes NaN-filled buffers, so a slab is right only if the
-column-block broadcast inside the call delivered every block before the
-contraction that consumes it.  Each rank checks its own output slab against
+Two processes, one per GPU.  B comes from rank 0 (the other rank passes
+NaN-filled buffers) or sharded by rows (each rank passes only its share),
+and S for the sandwich from rank 0, so a slab is right only if the column
+blocks sent inside the call (broadcast, or all-gathered from the shares)
+delivered every block before the contraction that consumes it.  Each rank checks its own output slab against
 an fp64 recomputation of the whole product (torch float64 on its GPU,
 test-only), within the mode's bound: 3xTF32 1e-5, TF32 5e-3, bf16 1e-2.
 Shapes cover equal-work triangular slabs, a ragged last block (a column
-count that is not a multiple of the block width), more blocks than internal
-compute streams (SMM_MG_CHUNKS=5), and the sandwich's S broadcast.  NVLS is off (NCCL_NVLS_ENABLE=0)
+count that is not a multiple of the block width), a short last share (K not
+a multiple of the world size), more blocks than internal compute streams
+(SMM_MG_CHUNKS=5), and the sandwich's S broadcast.  NVLS is off (NCCL_NVLS_ENABLE=0)
 and every rank issues the same calls in the same order."""
 import os
 import socket
@@ -59,58 +61,67 @@ def _worker(rank, world, port, results):
                 t.fill_(float("nan"))
             return t
 
-        for mode in ("3xtf32", "tf32", "bf16"):
-            # GEMM: A row slabs, B (K x N) broadcast
-            M, K, N = 2048, 2304, 1024
-            w = W.make_gemm(M, N, K, seed=31)
-            b = MG.lib_row_slabs(M, world)
-            r0, r1 = b[rank], b[rank + 1]
-            B = recv(w["B"])
-            C = torch.empty((r1 - r0, N), device="cuda")
-            comm.gemm(dev(w["A"][r0:r1]), B, C, mode=mode)
-            torch.cuda.synchronize()
-            R = dev(w["A"][r0:r1]).double() @ dev(w["B"]).double()
-            errs[f"gemm_{mode}"] = _relerr(C, R)
+        def barg(x, k, placement):
+            """B as this rank passes it: the root's whole B (a NaN buffer on
+            the other ranks), or this rank's row share."""
+            if placement == "root":
+                return recv(x)
+            s = MG.share_rows(k, world)
+            lo, hi = min(k, rank * s), min(k, (rank + 1) * s)
+            return dev(x[lo:hi]) if hi > lo else torch.empty((1, x.shape[1]), device="cuda")
 
-            # U B, packed U on every rank, equal-work slabs; ragged last column block
-            for n, ncols in ((4096, 1024), (1000, 1000)):
-                w = W.make_upper(n, ncols, seed=32)
-                b = MG.lib_row_slabs(n, world, triangular=True)
+        for placement in ("root", "sharded"):
+            root = 0 if placement == "root" else MG.SHARDED
+            for mode in ("3xtf32", "tf32", "bf16"):
+                tag = f"{placement}_{mode}"
+                # GEMM: A row slabs, B (K x N); K = 2301 leaves a short last share
+                for M, K, N in ((2048, 2304, 1024), (640, 2301, 520)):
+                    w = W.make_gemm(M, N, K, seed=31 + K)
+                    b = MG.lib_row_slabs(M, world)
+                    r0, r1 = b[rank], b[rank + 1]
+                    C = torch.empty((r1 - r0, N), device="cuda")
+                    comm.gemm(dev(w["A"][r0:r1]), barg(w["B"], K, placement), C, mode=mode, root=root)
+                    torch.cuda.synchronize()
+                    R = dev(w["A"][r0:r1]).double() @ dev(w["B"]).double()
+                    errs[f"gemm{K}_{tag}"] = _relerr(C, R)
+
+                # U B, packed U on every rank, equal-work slabs; ragged last column block
+                for n, ncols in ((4096, 1024), (1000, 1000)):
+                    w = W.make_upper(n, ncols, seed=32)
+                    b = MG.lib_row_slabs(n, world, triangular=True)
+                    r0, r1 = b[rank], b[rank + 1]
+                    C = torch.empty((r1 - r0, ncols), device="cuda")
+                    comm.upper_left(dev(w["U"]), barg(w["B"], n, placement), C, r0, mode=mode, root=root)
+                    torch.cuda.synchronize()
+                    Ud = ops.unpack(dev(w["U"]), "upper", n).double()
+                    R = Ud[r0:r1] @ dev(w["B"]).double()
+                    errs[f"upper{n}_{tag}"] = _relerr(C, R)
+
+                # T B with 5 column blocks (more than the 4 compute streams)
+                os.environ["SMM_MG_CHUNKS"] = "5"
+                n, ncols = 4096, 2560
+                w = W.make_toeplitz(n, ncols, seed=33)
+                b = MG.lib_row_slabs(n, world)
                 r0, r1 = b[rank], b[rank + 1]
-                B = recv(w["B"])
                 C = torch.empty((r1 - r0, ncols), device="cuda")
-                comm.upper_left(dev(w["U"]), B, C, r0, mode=mode)
+                comm.toeplitz_left(dev(w["g"]), barg(w["B"], n, placement), C, r0, mode=mode, root=root)
                 torch.cuda.synchronize()
-                Ud = ops.unpack(dev(w["U"]), "upper", n).double()
-                R = Ud[r0:r1] @ dev(w["B"]).double()
-                errs[f"upper{n}_{mode}"] = _relerr(C, R)
+                del os.environ["SMM_MG_CHUNKS"]
+                T = dev(W.toeplitz_dense(w["g"], n)).double()
+                errs[f"toeplitz_{tag}"] = _relerr(C, T[r0:r1] @ dev(w["B"]).double())
 
-            # T B with 5 column blocks (more than the 4 compute streams)
-            os.environ["SMM_MG_CHUNKS"] = "5"
-            n, ncols = 4096, 2560
-            w = W.make_toeplitz(n, ncols, seed=33)
-            b = MG.lib_row_slabs(n, world)
-            r0, r1 = b[rank], b[rank + 1]
-            B = recv(w["B"])
-            C = torch.empty((r1 - r0, ncols), device="cuda")
-            comm.toeplitz_left(dev(w["g"]), B, C, r0, mode=mode)
-            torch.cuda.synchronize()
-            del os.environ["SMM_MG_CHUNKS"]
-            T = dev(W.toeplitz_dense(w["g"], n)).double()
-            errs[f"toeplitz_{mode}"] = _relerr(C, T[r0:r1] @ dev(w["B"]).double())
-
-            # A S B: A row slabs; S (packed) and B broadcast
-            n = 2048
-            w = W.make_sandwich(n, seed=34)
-            b = MG.lib_row_slabs(n, world)
-            r0, r1 = b[rank], b[rank + 1]
-            S, B = recv(w["S"]), recv(w["B"])
-            C = torch.empty((r1 - r0, n), device="cuda")
-            comm.symm_sandwich(dev(w["A"][r0:r1]), S, B, C, mode=mode)
-            torch.cuda.synchronize()
-            Sd = dev(W.unpack_symmetric(w["S"], n)).double()
-            R = (dev(w["A"][r0:r1]).double() @ Sd) @ dev(w["B"]).double()
-            errs[f"sandwich_{mode}"] = _relerr(C, R)
+                # A S B: A row slabs; S (packed) from rank 0, B from the root or sharded
+                n = 2048
+                w = W.make_sandwich(n, seed=34)
+                b = MG.lib_row_slabs(n, world)
+                r0, r1 = b[rank], b[rank + 1]
+                C = torch.empty((r1 - r0, n), device="cuda")
+                comm.symm_sandwich(dev(w["A"][r0:r1]), recv(w["S"]), barg(w["B"], n, placement), C, mode=mode,
+                                   root=root)
+                torch.cuda.synchronize()
+                Sd = dev(W.unpack_symmetric(w["S"], n)).double()
+                R = (dev(w["A"][r0:r1]).double() @ Sd) @ dev(w["B"]).double()
+                errs[f"sandwich_{tag}"] = _relerr(C, R)
         ops.device_status()
         comm.status()
         dist.barrier()

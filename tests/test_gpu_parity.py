@@ -150,6 +150,32 @@ def test_upper_shapes(cuda, expand, packed, n_cols, mode):
 
 
 @pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
+@pytest.mark.parametrize("n_cols", [(1, 1), (130, 70), (300, 260), (1024, 1024), (1100, 257)])
+def test_upper_split_k_clusters(cuda, monkeypatch, n_cols, mode):
+    """U B (U expanded, zeros skipped per row tile) with each 128 x 128 tile
+    split along K over a two-CTA cluster (SMM_SPLITK=2 forces it): row tiles
+    near the bottom leave the second CTA an empty K range.  Whole products
+    and row slabs off the tile grid, against fp64; a second run is identical."""
+    from cpp1_b200 import _lib
+    monkeypatch.setenv("SMM_SPLITK", "2")
+    N, ncols = n_cols
+    w = W.make_upper(N, ncols, seed=N + 2 * ncols)
+    U, B = dev(w["U"]), dev(w["B"])
+    C = host(ops.upper_left(U, B, packed=True, mode=mode))
+    R = O.upper_left_rows_f64(w["U"], w["B"], np.arange(N))
+    assert _relerr_full(C, R) <= TOL[mode], (n_cols, _relerr_full(C, R))
+    assert np.array_equal(host(ops.upper_left(U, B, packed=True, mode=mode)), C)
+    L = _lib.load()
+    m = ops._mode(mode)
+    ws = ops.workspace(L.smm_upper_left_workspace_size(N, ncols, _lib.FMT_PACKED, m), torch.device("cuda"))
+    r0 = N // 3
+    nrows = N - r0
+    Cs = torch.full((nrows, ncols), float("nan"), device="cuda")
+    _slab_call("smm_upper_left_rows", L, U, B, Cs, N, ncols, r0, nrows, m, ws.data_ptr(), ws.numel())
+    assert _relerr_full(host(Cs), R[r0:]) <= TOL[mode]
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
 def test_toeplitz_golden(cuda, golden, mode):
     g, B = golden["toeplitz_g"], golden["toeplitz_B"]
     C = host(ops.toeplitz_left(dev(g), dev(B), mode=mode))

@@ -161,3 +161,21 @@ def test_library_column_blocks(ncols, world):
         assert len(cb) == 2
     else:
         assert 2 <= len(cb) - 1 <= 4
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_library_share_rows(world):
+    """smm_mg_share_rows agrees with the host rule (ceil(K / world)), and the
+    shares [r s, min(K, (r + 1) s)) cover B's rows exactly once."""
+    for k in (0, 1, 7, 1000, 2301, 8192, 16384):
+        s = MG.lib_share_rows(k, world)
+        assert s == MG.share_rows(k, world) == -(-k // world)
+        rows = [i for r in range(world) for i in range(min(k, r * s), min(k, (r + 1) * s))]
+        assert rows == list(range(k))
+
+
+def test_packed_order():
+    for n in (1, 2, 1000, 8192):
+        assert MG.packed_order(n * (n + 1) // 2) == n
+    with pytest.raises(ValueError):
+        MG.packed_order(4)
