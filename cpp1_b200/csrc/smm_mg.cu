@@ -2,17 +2,20 @@
 //
 // A product C = X B (X the dense A, packed U, Toeplitz generator, or A S for
 // the sandwich) is partitioned by output row slabs: rank g computes rows
-// [r0, r1) of C.  The shared right operand B lives on the root rank and is
-// broadcast inside each call in COLUMN blocks: the root copies column block
-// j of B into a contiguous K x W_j buffer and broadcasts it on the
-// communicator's high-priority stream; every rank computes
+// [r0, r1) of C.  The shared right operand B reaches every rank inside each
+// call in COLUMN blocks: either broadcast from a root rank (which packs
+// column block j of its B into a contiguous K x W_j buffer first), or
+// all-gathered from row shares when B is sharded over the ranks (each rank
+// packs its share's columns of block j; the gather concatenates the shares).
+// The packs run on a pack stream, the collectives on a high-priority
+// collective stream, and every rank computes
 //   C_slab[:, block j] = X[r0:r1, :] B[:, block j]
-// from that buffer as soon as it has landed, on one of several internal
+// from the block as soon as it has landed, on one of several internal
 // compute streams, so block j's tensor-core work overlaps the transfer of the
 // blocks after it, and blocks that arrive while earlier ones still compute
 // run side by side.  Every output element is written once by one full-K
 // contraction (no partial sums: results identical to the single-GPU entry
-// points).
+// points).  In bf16 mode the blocks travel as bf16.
 //
 // No kernel reads another GPU's memory and nothing is multicast: remote data
 // reaches local HBM through NCCL before any kernel touches it.
@@ -96,20 +99,23 @@ constexpr int kWork = 4;  // internal compute streams
 }  // namespace smm
 
 // One rank's communicator: the NCCL communicator, the device it was created
-// on, a high-priority stream for the collectives, the compute streams the
-// column blocks run on, and the events that order them against the caller's
-// stream.
+// on, a high-priority stream for the collectives and one for packing the
+// blocks they send, the compute streams the column blocks run on, and the
+// events that order them against the caller's stream.
 struct smm_mg_comm {
   ncclComm_t nc = nullptr;
   int rank = 0;
   int world = 1;
   int device = 0;
   cudaStream_t cs = nullptr;
+  cudaStream_t ps = nullptr;  // packs of the blocks this rank sends
   cudaStream_t work[smm::kWork] = {};
   cudaEvent_t ev_start = nullptr;  // caller's stream: inputs ready, previous call's readers done
   cudaEvent_t ev_prep = nullptr;   // caller's stream: the left operand prepared
   cudaEvent_t ev_s = nullptr;      // collective stream: the sandwich's S arrived
+  cudaEvent_t ev_cs_done = nullptr;  // collective stream: every collective (and pack) of the call done
   cudaEvent_t ev_chunk[smm::kMaxChunks] = {};
+  cudaEvent_t ev_packed[smm::kMaxChunks] = {};  // pack stream: block j ready to send
   cudaEvent_t ev_done[smm::kWork] = {};
 };
 
@@ -325,9 +331,11 @@ int pack_block(const BSide& b, const float* src, int rows, int pad_rows, int j, 
 }
 
 // Starts the B side of one call on the collective stream (ordered after the
-// caller's stream): ev_chunk[j] marks block j's arrival.  The sandwich's
-// S_packed (s_count floats) is broadcast first from the root (rank 0 when B
-// is sharded), marked by ev_s.  At world 1, bf16 converts B on `st`.
+// caller's stream): ev_chunk[j] marks block j's arrival.  The blocks this
+// rank sends are packed on the pack stream, block j+1's pack overlapping
+// block j's collective.  The sandwich's S_packed (s_count floats) is
+// broadcast first from the root (rank 0 when B is sharded), marked by ev_s.
+// At world 1, bf16 converts B on `st`.
 int start_bside(smm_mg_comm* c, const BSide& b, const float* B, cudaStream_t st, float* S_packed = nullptr,
                 size_t s_count = 0) {
   if (!b.travels()) {
@@ -337,30 +345,30 @@ int start_bside(smm_mg_comm* c, const BSide& b, const float* B, cudaStream_t st,
   }
   SMM_CUDA_TRY(cudaEventRecord(c->ev_start, st), "record call start");
   SMM_CUDA_TRY(cudaStreamWaitEvent(c->cs, c->ev_start, 0), "order the collectives after the caller's stream");
+  const bool packs = b.sharded || c->rank == b.root;
+  if (packs) {
+    SMM_CUDA_TRY(cudaStreamWaitEvent(c->ps, c->ev_start, 0), "order the packs after the caller's stream");
+    for (int j = 0; j < b.nch; ++j) {
+      const int rc = b.sharded ? pack_block(b, B, b.valid, b.share, j, b.send_part(j), c->ps)
+                               : pack_block(b, B, b.K, b.K, j, b.plane(j), c->ps);
+      if (rc) return rc;
+      SMM_CUDA_TRY(cudaEventRecord(c->ev_packed[j], c->ps), "record block packed");
+    }
+  }
   const NcclApi& n = nccl();
   if (S_packed) {
     SMM_NCCL_TRY(n.broadcast(S_packed, S_packed, s_count, ncclFloat, b.root, c->nc, c->cs), "ncclBroadcast (S)");
     SMM_CUDA_TRY(cudaEventRecord(c->ev_s, c->cs), "record S arrival");
   }
   const ncclDataType_t ty = b.bf ? ncclBfloat16 : ncclFloat;
-  // Every pack first: enqueued before this rank's contractions, they take
-  // the SMs at once instead of competing with them between collectives.
-  if (b.sharded) {
-    for (int j = 0; j < b.nch; ++j)
-      if (int rc = pack_block(b, B, b.valid, b.share, j, b.send_part(j), c->cs)) return rc;
-    for (int j = 0; j < b.nch; ++j) {
+  for (int j = 0; j < b.nch; ++j) {
+    if (packs) SMM_CUDA_TRY(cudaStreamWaitEvent(c->cs, c->ev_packed[j], 0), "wait for the block's pack");
+    if (b.sharded)
       SMM_NCCL_TRY(n.allgather(b.send_part(j), b.plane(j), static_cast<size_t>(b.share) * b.ld(j), ty, c->nc, c->cs),
                    "ncclAllGather (column block of B)");
-      SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record block arrival");
-    }
-    return SMM_OK;
-  }
-  if (c->rank == b.root)
-    for (int j = 0; j < b.nch; ++j)
-      if (int rc = pack_block(b, B, b.K, b.K, j, b.plane(j), c->cs)) return rc;
-  for (int j = 0; j < b.nch; ++j) {
-    SMM_NCCL_TRY(n.broadcast(b.plane(j), b.plane(j), static_cast<size_t>(b.K) * b.ld(j), ty, b.root, c->nc, c->cs),
-                 "ncclBroadcast (column block of B)");
+    else
+      SMM_NCCL_TRY(n.broadcast(b.plane(j), b.plane(j), static_cast<size_t>(b.K) * b.ld(j), ty, b.root, c->nc, c->cs),
+                   "ncclBroadcast (column block of B)");
     SMM_CUDA_TRY(cudaEventRecord(c->ev_chunk[j], c->cs), "record block arrival");
   }
   return SMM_OK;
@@ -386,6 +394,12 @@ int run_blocks(smm_mg_comm* c, const BSide& b, cudaStream_t st, F&& block) {
     SMM_CUDA_TRY(cudaEventRecord(c->ev_done[w], c->work[w]), "record block done");
     SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_done[w], 0), "join");
   }
+  // The caller's stream also waits for the collectives (and, through them,
+  // the packs that read B): the root computing from B in place does not wait
+  // for its own sends, and the next call's packs must not overwrite a block
+  // still being sent.
+  SMM_CUDA_TRY(cudaEventRecord(c->ev_cs_done, c->cs), "record collectives done");
+  SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_cs_done, 0), "join the collectives");
   return SMM_OK;
 }
 
@@ -420,11 +434,14 @@ extern "C" int smm_mg_unique_id(void* id_out) {
 namespace {
 void release(smm_mg_comm* c) {
   if (c->cs) cudaStreamDestroy(c->cs);
+  if (c->ps) cudaStreamDestroy(c->ps);
   for (auto& w : c->work)
     if (w) cudaStreamDestroy(w);
-  for (cudaEvent_t e : {c->ev_start, c->ev_prep, c->ev_s})
+  for (cudaEvent_t e : {c->ev_start, c->ev_prep, c->ev_s, c->ev_cs_done})
     if (e) cudaEventDestroy(e);
   for (auto& e : c->ev_chunk)
+    if (e) cudaEventDestroy(e);
+  for (auto& e : c->ev_packed)
     if (e) cudaEventDestroy(e);
   for (auto& e : c->ev_done)
     if (e) cudaEventDestroy(e);
@@ -449,15 +466,19 @@ extern "C" int smm_mg_comm_init(smm_mg_comm** out, int rank, int world, const vo
   if (cudaGetDevice(&c->device) != cudaSuccess) return fail(set_error(SMM_ERR_CUDA, "cudaGetDevice failed"));
   int lo = 0, hi = 0;
   if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
-      cudaStreamCreateWithPriority(&c->cs, cudaStreamNonBlocking, hi) != cudaSuccess)
-    return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: collective stream"));
+      cudaStreamCreateWithPriority(&c->cs, cudaStreamNonBlocking, hi) != cudaSuccess ||
+      cudaStreamCreateWithPriority(&c->ps, cudaStreamNonBlocking, hi) != cudaSuccess)
+    return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: collective streams"));
   for (auto& w : c->work)
     if (cudaStreamCreateWithFlags(&w, cudaStreamNonBlocking) != cudaSuccess)
       return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: compute stream"));
-  for (cudaEvent_t* e : {&c->ev_start, &c->ev_prep, &c->ev_s})
+  for (cudaEvent_t* e : {&c->ev_start, &c->ev_prep, &c->ev_s, &c->ev_cs_done})
     if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess)
       return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: event"));
   for (auto& e : c->ev_chunk)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+      return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: event"));
+  for (auto& e : c->ev_packed)
     if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
       return fail(set_error(SMM_ERR_CUDA, "smm_mg_comm_init: event"));
   for (auto& e : c->ev_done)
@@ -480,6 +501,7 @@ extern "C" int smm_mg_comm_destroy(smm_mg_comm* c) {
   if (!c) return SMM_OK;
   int rc = SMM_OK;
   if (c->cs) cudaStreamSynchronize(c->cs);
+  if (c->ps) cudaStreamSynchronize(c->ps);
   for (auto& w : c->work)
     if (w) cudaStreamSynchronize(w);
   if (c->nc) {
