@@ -127,12 +127,14 @@ long long range_cost(long long n, long long a, long long b) {  // sum_{i=a}^{b-1
   return (b - a) * n - (b * (b - 1) - a * (a - 1)) / 2;
 }
 
-// Slab boundaries b[0] = 0 <= ... <= b[world] = n on 128-row tiles,
+// Slab boundaries b[0] = 0 <= ... <= b[world] = n on 256-row tiles (the
+// height of a CTA-pair tile: a slab of an odd number of 128-row tiles would
+// end in a half-empty pair tile that costs a full one),
 // minimising the largest slab's work: rows cost 1 (dense operands) or n - i
 // (upper-triangular).  Binary search on the largest slab's work, then a
 // greedy cut.  Slabs may be empty when n has fewer tiles than ranks.
 void row_slabs(int n, int world, bool triangular, int* b) {
-  constexpr int kTile = 128;
+  constexpr int kTile = 256;
   if (n <= 0) {
     for (int g = 0; g <= world; ++g) b[g] = 0;
     return;
@@ -200,13 +202,17 @@ __global__ void __launch_bounds__(256) pack_cols_kernel(const float* __restrict_
   }
 }
 
-// Column-block boundaries of a broadcast of B (ncols columns): 1 block at
-// world 1, else 4 (SMM_MG_CHUNKS overrides, 1 .. 16), widths multiples of 256
-// (the widest output tile).
+// Column-block boundaries of a transfer of B (ncols columns), widths
+// multiples of 256 (the widest output tile).  Block count by world size
+// (SMM_MG_CHUNKS overrides, 1 .. 16): 1 at world 1; 4 at world 2, where a
+// rank's compute (~1.2 ms for U B 8192) outweighs the transfer and overlap
+// hides it; 2 at 3-4; 1 from 5 up, where the transfer outweighs the compute
+// and the blocks' collectives, competing with the contractions for SMs,
+// measured slower than one transfer followed by the product (U B 8192 at 8
+// GPUs, B sharded: 0.89 ms per call with 1 block, 0.91 with 2, 1.17 with 4).
 int chunk_bounds(int ncols, int world, int* cb) {
-  int c = 1;
+  int c = world == 1 ? 1 : world == 2 ? 4 : world <= 4 ? 2 : 1;
   if (world > 1) {
-    c = 4;
     if (const char* e = std::getenv("SMM_MG_CHUNKS")) {
       const int v = std::atoi(e);
       if (v >= 1 && v <= kMaxChunks) c = v;

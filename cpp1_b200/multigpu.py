@@ -12,7 +12,7 @@ packed U, Toeplitz generator, packed S):
   triangle) or row-sliced, so it is replicated or sliced locally;
 * for the triangular operand row i costs N - i, so slab boundaries are
   equal-work: boundary g of G sits at N (1 - sqrt(1 - g/G)), rounded to the
-  128-row tile height;
+  256-row pair-tile height;
 * the diagonal scale shards with no collective at all (rows independent).
 
 ``Communicator`` wraps libsmm's own NCCL communicator (``smm_mg_*``): each
@@ -32,7 +32,7 @@ from __future__ import annotations
 import math
 from typing import Callable, List, Optional, Sequence, Tuple
 
-TILE_ROWS = 128
+TILE_ROWS = 256  # a CTA-pair tile's height
 
 
 def _tile_work(n: int, triangular: bool, align: int) -> List[int]:

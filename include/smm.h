@@ -224,13 +224,14 @@ int smm_mg_comm_abort(smm_mg_comm* comm);
 /* SMM_ERR_NCCL if the communicator saw an asynchronous NCCL error. */
 int smm_mg_comm_status(smm_mg_comm* comm);
 
-/* Row-slab boundaries bounds[0] = 0 <= ... <= bounds[world] = N on 128-row
- * tiles, minimising the largest slab's work: rows cost 1, or N - i for an
- * upper-triangular left operand (triangular != 0). */
+/* Row-slab boundaries bounds[0] = 0 <= ... <= bounds[world] = N on 256-row
+ * tiles (a CTA-pair tile's height), minimising the largest slab's work: rows
+ * cost 1, or N - i for an upper-triangular left operand (triangular != 0). */
 int smm_mg_row_slabs(int N, int world, int triangular, int* bounds);
-/* Column-block boundaries the calls use for a broadcast of B's ncols columns
- * at this world size (bounds needs 17 ints); returns the block count.
- * SMM_MG_CHUNKS in the environment sets the count (1 .. 16; default 4). */
+/* Column-block boundaries the calls use for a transfer of B's ncols columns
+ * at this world size (bounds needs 17 ints); returns the block count: 1 at
+ * world 1, 4 at world 2, 2 at 3-4, 1 from 5 up (SMM_MG_CHUNKS in the
+ * environment sets it, 1 .. 16). */
 int smm_mg_chunks(int ncols, int world, int* bounds);
 
 /* Rows in each rank's share of a K-row B sharded over `world` ranks:

@@ -21,7 +21,7 @@ def test_slabs_cover_rows(world):
             b = MG.row_slabs(n, world, tri)
             assert b[0] == 0 and b[-1] == n and len(b) == world + 1
             assert all(b[i] <= b[i + 1] for i in range(world))
-            assert all(x % 128 == 0 or x == n for x in b[1:-1])
+            assert all(x % 256 == 0 or x == n for x in b[1:-1])
 
 
 def test_triangular_slabs_balance_work():
@@ -30,9 +30,10 @@ def test_triangular_slabs_balance_work():
     work = [MG.slab_useful_flops("upper", n, b[i], b[i + 1]) for i in range(world)]
     total = MG.slab_useful_flops("upper", n, 0, n)
     assert sum(work) == total == n * n * (n + 1)
-    # the slowest rank sets the time: within 10% of an equal share (the first
-    # 128-row tile alone is a quarter of a share, so tile granularity costs ~9%)
-    assert max(work) <= 1.10 * total / world
+    # the slowest rank sets the time: within 15% of an equal share (the first
+    # 256-row tile alone is half a share, so tile granularity costs ~15%; the
+    # pair tiles it avoids leaving half empty cost more)
+    assert max(work) <= 1.15 * total / world
     uniform = MG.row_slabs(n, world, triangular=False)
     uw = [MG.slab_useful_flops("upper", n, uniform[i], uniform[i + 1]) for i in range(world)]
     assert max(uw) > 1.7 * total / world  # uniform rows would be 1.9x slower
@@ -157,10 +158,8 @@ def test_library_column_blocks(ncols, world):
     assert cb[0] == 0 and cb[-1] == ncols
     assert all(a < b for a, b in zip(cb, cb[1:]))
     assert all(x % 256 == 0 for x in cb[:-1])  # blocks start on whole output tiles
-    if world == 1 or ncols <= 256:
-        assert len(cb) == 2
-    else:
-        assert 2 <= len(cb) - 1 <= 4
+    want = 1 if world == 1 else 4 if world == 2 else 2 if world <= 4 else 1
+    assert len(cb) - 1 == min(want, -(-ncols // 256))
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
