@@ -86,6 +86,8 @@ def parse_args():
     ap.add_argument("--b-placement", choices=["sharded", "root"], default="sharded",
                     help="G > 1: B arrives sharded by rows (all-gathered inside each call) or whole on rank 0 "
                          "(broadcast inside each call)")
+    ap.add_argument("--transfer", choices=["ce", "nccl"], default="ce",
+                    help="G > 1 with B sharded: gather B's blocks by copy engines (IPC peer copies) or by NCCL")
     ap.add_argument("--roofline-s", type=float, default=1.0,
                     help="seconds of repeated calls over which the roofline kernel is timed")
     a = ap.parse_args()
@@ -385,6 +387,8 @@ def run_ours(args, rank, world, local):
         # placement: rows [rank s, rank s + s) of the resident B) or the
         # whole B (read on rank 0 only).
         root = MG.SHARDED if args.b_placement == "sharded" else 0
+        if comm is not None and root == MG.SHARDED and args.transfer == "ce":
+            comm.enable_copy_engines(comm.plane_bytes(n, n, mode))
         B_full = d_in[-1]
         if root == MG.SHARDED:
             s_rows = MG.share_rows(n, world)
@@ -541,7 +545,9 @@ def run_ours(args, rank, world, local):
         heaviest = max_over_ranks(float(units_per_rank_call), world)
         t_mma = passes * heaviest / (peak * 1e12) * 1e3
         t_link = link_in / 770e9 * 1e3
-        how = ("all-gathered from every rank's row share" if root == MG.SHARDED else "broadcast from rank 0")
+        how = ((f"gathered from every rank's row share by "
+                f"{'copy engines (IPC peer copies, no SM)' if comm.copy_engines_enabled() else 'NCCL all-gather'}")
+               if root == MG.SHARDED else "broadcast from rank 0 (NCCL)")
         multi = {"compute_only_ms_per_step": round(ms_c, 4), "transfer_inclusive_ms_per_step": round(ms_per_step, 4),
                  "transfer_only_ms_per_step": round(ms_b, 4),
                  "b_placement": args.b_placement,
@@ -549,9 +555,9 @@ def run_ours(args, rank, world, local):
                  "b_bytes_per_step": int(b_bytes),
                  "nvlink_in_bytes_per_rank": int(link_in),
                  "column_blocks": MG.lib_chunks(n, world),
-                 "overlap": f"B {how} in column blocks inside each call (libsmm smm_mg_*, NCCL on a high-priority "
-                            "stream); each block's columns of the slab are computed as soon as it lands, on "
-                            "internal compute streams",
+                 "transfer": "copy engines" if comm.copy_engines_enabled() else "nccl",
+                 "overlap": f"B {how} in column blocks inside each call (libsmm smm_mg_*); each block's columns of "
+                            "the slab are computed as soon as it lands, on internal compute streams",
                  "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)],
                  "roofline": {"bound": "tensor" if t_mma >= t_link else "nvlink",
                               "t_mma_ms": round(t_mma, 4), "t_nvlink_ms": round(t_link, 4),
@@ -578,7 +584,10 @@ def run_ours(args, rank, world, local):
                                              "bf16": "bf16 (fp32 accumulate)"}[mode],
         "data": "synthetic (seeded numpy PCG64, cpp1_b200.workloads)",
         "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "mode": mode if op not in HBM_OPS else "f32",
-                   "parallelism": (f"row-slabs x{world}, B {args.b_placement}" if world > 1 and op not in HBM_OPS
+                   "parallelism": (f"row-slabs x{world}, B {args.b_placement}"
+                                   + (f" ({'copy engines' if args.transfer == 'ce' else 'NCCL'})"
+                                      if args.b_placement == "sharded" else " (NCCL)")
+                                   if world > 1 and op not in HBM_OPS
                                    else (f"row-slabs x{world}" if world > 1 else "single GPU")),
                    "l2": ("inputs smaller than L2: a 256 MiB write flushes it before every step, each step "
                           "timed alone between its own CUDA events" if l2_resident
@@ -818,6 +827,8 @@ def e2e_dist(args, h_in, n, rank, world):
         return torch.from_numpy(np.ascontiguousarray(x)).pin_memory()
 
     comm = MG.Communicator(rank, world)
+    if args.transfer == "ce":
+        comm.enable_copy_engines(comm.plane_bytes(n, n, mode))
     Bh = h_in[-1]  # B is the last input of every contraction
     hB = pin(Bh[s0:s1])
     B_share = torch.zeros((max(s1 - s0, 1), n), dtype=torch.float32, device=dev)
@@ -894,7 +905,8 @@ def e2e_dist(args, h_in, n, rank, world):
     return {"value": round(units / dt / 1e12, 3), "unit": WORKLOADS[op]["unit"], "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(n * n * 4), "steps": steps, "ms_per_step": round(dt * 1e3, 3),
             "api": "libsmm smm_mg_* (B sharded) with pinned host buffers: per-rank input shares over each GPU's "
-                   "PCIe link, B's column blocks all-gathered over NVLink inside the call (whole-job bytes)"}
+                   "PCIe link, B's column blocks gathered over NVLink inside the call "
+                   f"({'copy engines' if args.transfer == 'ce' else 'NCCL'}; whole-job bytes)"}
 
 
 # ---------------------------------------------------------------- reference arm

@@ -124,6 +124,9 @@ SIGNATURES = [
     ("smm_mg_row_slabs", _i, [_i, _i, _i, _vp]),
     ("smm_mg_chunks", _i, [_i, _i, _vp]),
     ("smm_mg_share_rows", _i, [_i, _i]),
+    ("smm_mg_plane_bytes", _sz, [_vp, _i, _i, _i]),
+    ("smm_mg_enable_copy_engines", _i, [_vp, _sz]),
+    ("smm_mg_copy_engines_enabled", _i, [_vp]),
     ("smm_mg_gemm_workspace_size", _sz, [_vp, _i, _i, _i, _i]),
     ("smm_mg_gemm", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_mg_upper_left_workspace_size", _sz, [_vp, _i, _i, _i, _i]),

@@ -127,22 +127,19 @@ bool use_pairs(int M, int N) {
 
 // Output tile width: the widest tile that still yields about a wave of CTAs
 // (of CTA pairs when pair is set).
-// Triangular left operands (tri): 256-wide pair tiles only when they fit one
-// wave or make at least four -- in between, the ragged last wave of tiles
-// whose K ranges reach ~8000 (a row slab of a multi-GPU U B) costs more than
-// the narrower tiles' lower efficiency (a simulated schedule of the 8-GPU
-// slabs: heaviest rank 0.49 -> 0.39 ms).
-int pick_bn(int M, int N, bool pair, bool tri = false) {
+int pick_bn(int M, int N, bool pair) {
   const char* e = std::getenv("SMM_TILE_N");
   if (e) {
     int v = std::atoi(e);
     if (v == 256 || v == 128 || (v == 64 && !pair)) return v;
   }
+  // 128-wide pair tiles only when 256-wide ones would leave most pairs idle:
+  // they measured far slower per FLOP (U B 4096 3xTF32: 146 against 198
+  // TFLOP/s with 256-wide tiles, bf16 447 against 569), more than any wave
+  // quantisation they save.
   if (pair) {
     const long long rp = (M + 2 * kBM - 1) / (2 * kBM);
-    const long long t256 = rp * ((N + 255) / 256);
-    if (tri && N > 128 && t256 > 74 && t256 < 4 * 74) return 128;
-    return (N > 128 && t256 >= 60) ? 256 : 128;
+    return (N > 128 && rp * ((N + 255) / 256) >= 60) ? 256 : 128;
   }
   const long long rt = (M + kBM - 1) / kBM;
   if (N > 128 && rt * ((N + 255) / 256) >= 120) return 256;
@@ -196,7 +193,7 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   const bool bf16 = (mode == SMM_MODE_BF16);
   const bool pair = use_pairs(M, N);
   const bool split = use_split(ak, bk, a, b, pair, M, N, K);
-  const int bn = split ? 128 : pick_bn(M, N, pair, ak == AKind::UpperDense || ak == AKind::UpperPacked);
+  const int bn = split ? 128 : pick_bn(M, N, pair);
   Maps m;
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);

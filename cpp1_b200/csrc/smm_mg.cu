@@ -27,7 +27,14 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <fcntl.h>
+#include <sched.h>
+#include <sys/mman.h>
+#include <time.h>
+#include <unistd.h>
+
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -96,6 +103,49 @@ constexpr int kMaxChunks = 16;
 constexpr int kWork = 4;  // internal compute streams
 
 }  // namespace
+
+// ---------------------------------------------------------------- copy-engine gather state
+// With copy engines enabled (smm_mg_enable_copy_engines), a sharded B is
+// gathered without NCCL: every rank packs its share of block j into its own
+// slot of a plane buffer it registered, and its copy engines push that slot
+// into the same place of every peer's plane buffer (cudaMemcpyAsync to the
+// peer's buffer, mapped here through CUDA IPC).  No SM takes part in the
+// transfer, so it runs beside the contractions at full speed.  Ordering
+// across processes uses interprocess events -- "block j copied into rank d"
+// and "rank d has finished reading its planes" -- and two host barriers per
+// call (in shared memory), which make every rank's event records of a call
+// precede the other ranks' waits on them.
+constexpr int kMaxCeRanks = 8;
+constexpr int kBarrierSeconds = 60;
+
+struct ShmBarrier {
+  std::atomic<uint32_t> arrived;
+  std::atomic<uint32_t> gen;
+};
+
+struct CeState {
+  uint8_t* planes = nullptr;                            // this rank's plane buffer (cudaMalloc)
+  size_t bytes = 0;
+  uint8_t* peer[kMaxCeRanks] = {};                      // every rank's planes, mapped here (own: planes)
+  cudaStream_t xs[kMaxCeRanks] = {};                    // copy stream per destination rank
+  cudaEvent_t sent[kMaxCeRanks][kMaxChunks] = {};       // recorded here: block j copied into rank d
+  cudaEvent_t sent_in[kMaxCeRanks][kMaxChunks] = {};    // opened: rank s copied block j into ours
+  cudaEvent_t done = nullptr;                           // recorded here: this call's readers of our planes done
+  cudaEvent_t done_in[kMaxCeRanks] = {};                // opened: rank d's readers done
+  cudaEvent_t xs_done[kMaxCeRanks] = {};                // local: copy stream d drained
+  ShmBarrier* bar = nullptr;
+  char shm_name[64] = "";
+  bool owner = false;  // created the shared-memory segment (unlinks it)
+};
+
+// What each rank publishes when copy engines are enabled.
+struct CeInfo {
+  cudaIpcMemHandle_t mem;
+  unsigned long long bytes;
+  cudaIpcEventHandle_t sent[kMaxCeRanks][kMaxChunks];
+  cudaIpcEventHandle_t done;
+};
+
 }  // namespace smm
 
 // One rank's communicator: the NCCL communicator, the device it was created
@@ -117,6 +167,8 @@ struct smm_mg_comm {
   cudaEvent_t ev_chunk[smm::kMaxChunks] = {};
   cudaEvent_t ev_packed[smm::kMaxChunks] = {};  // pack stream: block j ready to send
   cudaEvent_t ev_done[smm::kWork] = {};
+  unsigned char uid[SMM_MG_ID_BYTES] = {};
+  smm::CeState* ce = nullptr;  // copy-engine gather, when enabled
 };
 
 namespace smm {
@@ -210,8 +262,10 @@ __global__ void __launch_bounds__(256) pack_cols_kernel(const float* __restrict_
 // and the blocks' collectives, competing with the contractions for SMs,
 // measured slower than one transfer followed by the product (U B 8192 at 8
 // GPUs, B sharded: 0.89 ms per call with 1 block, 0.91 with 2, 1.17 with 4).
-int chunk_bounds(int ncols, int world, int* cb) {
+// A copy-engine gather (ce) uses no SM and always takes 4 blocks.
+int chunk_bounds(int ncols, int world, int* cb, bool ce = false) {
   int c = world == 1 ? 1 : world == 2 ? 4 : world <= 4 ? 2 : 1;
+  if (ce && world > 1) c = 4;  // copy engines take no SM from the contractions: always overlap
   if (world > 1) {
     if (const char* e = std::getenv("SMM_MG_CHUNKS")) {
       const int v = std::atoi(e);
@@ -259,6 +313,7 @@ struct BSide {
   int rows = 0;              // rows of a block plane
   uint8_t* planes = nullptr;
   uint8_t* send = nullptr;   // sharded: this rank's part of each block
+  bool ce = false;           // sharded, gathered by copy engines into the registered planes
   int width(int j) const { return cb[j + 1] - cb[j]; }
   int ld(int j) const { return bf ? round8(width(j)) : width(j); }
   size_t esz() const { return bf ? 2 : 4; }
@@ -268,6 +323,15 @@ struct BSide {
     for (int i = 0; i < j; ++i) p += plane_bytes_of(i, rows);
     return p;
   }
+  // Bytes of all block planes (rows each).
+  size_t planes_bytes(int r) const {
+    size_t t = 0;
+    for (int j = 0; j < nch; ++j) t += plane_bytes_of(j, r);
+    return t;
+  }
+  // This rank's slot of block j's plane (copy-engine gather): rows
+  // [rank * share, rank * share + share).
+  uint8_t* own_slot(int j) const { return plane(j) + static_cast<size_t>(rank) * share * ld(j) * esz(); }
   uint8_t* send_part(int j) const {
     uint8_t* p = send;
     for (int i = 0; i < j; ++i) p += plane_bytes_of(i, share);
@@ -282,7 +346,8 @@ BSide make_bside(const smm_mg_comm* c, int K, int ncols, int mode, int root, voi
   BSide b;
   b.K = K;
   b.ncols = ncols;
-  b.nch = chunk_bounds(ncols, c->world, b.cb);
+  const bool try_ce = c->ce && root == SMM_MG_SHARDED && c->world > 1;
+  b.nch = chunk_bounds(ncols, c->world, b.cb, try_ce);
   b.bf = mode == SMM_MODE_BF16;
   b.sharded = root == SMM_MG_SHARDED;
   b.world = c->world;
@@ -291,12 +356,54 @@ BSide make_bside(const smm_mg_comm* c, int K, int ncols, int mode, int root, voi
   b.share = share_rows(K, c->world);
   b.valid = std::max(0, std::min(b.share, K - c->rank * b.share));
   b.rows = (b.sharded && c->world > 1) ? c->world * b.share : K;
+  if (try_ce && c->ce->bytes >= b.planes_bytes(b.rows)) {
+    b.ce = true;
+    b.planes = c->ce->planes;
+    return b;
+  }
+  if (try_ce) b.nch = chunk_bounds(ncols, c->world, b.cb, false);  // the planes do not fit: NCCL
   b.planes = static_cast<uint8_t*>(ws);
   size_t pb = 0;
   if (b.travels() || b.bf)
     for (int j = 0; j < b.nch; ++j) pb += b.plane_bytes_of(j, std::max(K, c->world * b.share));
   b.send = b.planes + pb;
   return b;
+}
+
+// Host barrier of the ranks of a copy-engine communicator (shared memory,
+// generation counting); gives up after kBarrierSeconds.
+int ce_barrier(CeState* e, int world, const char* who) {
+  ShmBarrier* b = e->bar;
+  const uint32_t g = b->gen.load(std::memory_order_acquire);
+  if (b->arrived.fetch_add(1, std::memory_order_acq_rel) + 1 == static_cast<uint32_t>(world)) {
+    b->arrived.store(0, std::memory_order_relaxed);
+    b->gen.fetch_add(1, std::memory_order_release);
+    return SMM_OK;
+  }
+  timespec t0;
+  clock_gettime(CLOCK_MONOTONIC, &t0);
+  for (unsigned long it = 0; b->gen.load(std::memory_order_acquire) == g; ++it) {
+    if ((it & 255) == 255) {
+      timespec t;
+      clock_gettime(CLOCK_MONOTONIC, &t);
+      if (t.tv_sec - t0.tv_sec > kBarrierSeconds)
+        return set_error(SMM_ERR_NCCL, "%s: a peer rank did not reach the host barrier within %d s", who,
+                         kBarrierSeconds);
+      sched_yield();
+    }
+  }
+  return SMM_OK;
+}
+
+// Plane buffer bytes a sharded call of this shape gathers into.
+size_t ce_planes_needed(int world, int K, int ncols, int mode) {
+  BSide b;
+  b.K = K;
+  b.ncols = ncols;
+  b.nch = chunk_bounds(ncols, world, b.cb, true);
+  b.bf = mode == SMM_MODE_BF16;
+  b.share = share_rows(K, world);
+  return b.planes_bytes(world * b.share);
 }
 
 // Workspace of the B side: the block planes (world > 1, or bf16), sized for
@@ -351,6 +458,41 @@ int start_bside(smm_mg_comm* c, const BSide& b, const float* B, cudaStream_t st,
   }
   SMM_CUDA_TRY(cudaEventRecord(c->ev_start, st), "record call start");
   SMM_CUDA_TRY(cudaStreamWaitEvent(c->cs, c->ev_start, 0), "order the collectives after the caller's stream");
+  if (b.ce) {
+    CeState* e = c->ce;
+    const NcclApi& n = nccl();
+    if (S_packed) {
+      SMM_NCCL_TRY(n.broadcast(S_packed, S_packed, s_count, ncclFloat, b.root, c->nc, c->cs), "ncclBroadcast (S)");
+      SMM_CUDA_TRY(cudaEventRecord(c->ev_s, c->cs), "record S arrival");
+    }
+    // Barrier A: every rank has recorded its end-of-call 'done' of the
+    // previous call, so the waits below see this call's predecessors.
+    if (int rc = ce_barrier(e, c->world, "copy-engine gather")) return rc;
+    SMM_CUDA_TRY(cudaStreamWaitEvent(c->ps, c->ev_start, 0), "order the packs after the caller's stream");
+    for (int j = 0; j < b.nch; ++j) {
+      if (int rc = pack_block(b, B, b.valid, b.share, j, b.own_slot(j), c->ps)) return rc;
+      SMM_CUDA_TRY(cudaEventRecord(c->ev_packed[j], c->ps), "record block packed");
+    }
+    const size_t slot_bytes_base = static_cast<size_t>(b.share) * b.esz();
+    for (int d = 0; d < c->world; ++d) {
+      if (d == c->rank) continue;
+      // rank d's previous call has finished reading the planes we overwrite
+      SMM_CUDA_TRY(cudaStreamWaitEvent(e->xs[d], e->done_in[d], 0), "wait for the peer's readers");
+    }
+    for (int j = 0; j < b.nch; ++j) {
+      const size_t off = static_cast<size_t>(b.own_slot(j) - b.planes);
+      const size_t bytes = slot_bytes_base * b.ld(j);
+      for (int d = 0; d < c->world; ++d) {
+        if (d == c->rank) continue;
+        SMM_CUDA_TRY(cudaStreamWaitEvent(e->xs[d], c->ev_packed[j], 0), "wait for the block's pack");
+        SMM_CUDA_TRY(cudaMemcpyAsync(e->peer[d] + off, b.own_slot(j), bytes, cudaMemcpyDeviceToDevice, e->xs[d]),
+                     "copy-engine push of a share");
+        SMM_CUDA_TRY(cudaEventRecord(e->sent[d][j], e->xs[d]), "record block sent");
+      }
+    }
+    // Barrier B: every rank has recorded this call's 'sent' events.
+    return ce_barrier(e, c->world, "copy-engine gather");
+  }
   const bool packs = b.sharded || c->rank == b.root;
   if (packs) {
     SMM_CUDA_TRY(cudaStreamWaitEvent(c->ps, c->ev_start, 0), "order the packs after the caller's stream");
@@ -393,12 +535,27 @@ int run_blocks(smm_mg_comm* c, const BSide& b, cudaStream_t st, F&& block) {
   for (int w = 0; w < used; ++w) SMM_CUDA_TRY(cudaStreamWaitEvent(c->work[w], c->ev_prep, 0), "fork");
   for (int j = 0; j < b.nch; ++j) {
     cudaStream_t w = c->work[j % kWork];
-    if (!b.in_place()) SMM_CUDA_TRY(cudaStreamWaitEvent(w, c->ev_chunk[j], 0), "wait for block arrival");
+    if (b.ce) {
+      SMM_CUDA_TRY(cudaStreamWaitEvent(w, c->ev_packed[j], 0), "wait for this rank's slot");
+      for (int s = 0; s < c->world; ++s)
+        if (s != c->rank) SMM_CUDA_TRY(cudaStreamWaitEvent(w, c->ce->sent_in[s][j], 0), "wait for a peer's share");
+    } else if (!b.in_place()) {
+      SMM_CUDA_TRY(cudaStreamWaitEvent(w, c->ev_chunk[j], 0), "wait for block arrival");
+    }
     if (int rc = block(j, w)) return rc;
   }
   for (int w = 0; w < used; ++w) {
     SMM_CUDA_TRY(cudaEventRecord(c->ev_done[w], c->work[w]), "record block done");
     SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_done[w], 0), "join");
+  }
+  if (b.ce) {
+    // our pushes have read our slots; then our planes are fully read
+    for (int d = 0; d < c->world; ++d) {
+      if (d == c->rank) continue;
+      SMM_CUDA_TRY(cudaEventRecord(c->ce->xs_done[d], c->ce->xs[d]), "record pushes done");
+      SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ce->xs_done[d], 0), "join the pushes");
+    }
+    SMM_CUDA_TRY(cudaEventRecord(c->ce->done, st), "record planes read");
   }
   // The caller's stream also waits for the collectives (and, through them,
   // the packs that read B): the root computing from B in place does not wait
@@ -438,7 +595,40 @@ extern "C" int smm_mg_unique_id(void* id_out) {
 }
 
 namespace {
+// Frees the copy-engine state.  `wait_peers`: first close this rank's
+// mappings of the peers' planes and wait (host barrier) until every rank has
+// closed its mappings of ours before freeing them (a normal destroy; an abort
+// does not wait for peers).
+void ce_release(smm_mg_comm* c, bool wait_peers) {
+  CeState* e = c->ce;
+  if (!e) return;
+  for (auto& x : e->xs)
+    if (x) cudaStreamSynchronize(x);
+  for (int s = 0; s < kMaxCeRanks; ++s) {
+    if (s != c->rank && e->peer[s]) cudaIpcCloseMemHandle(e->peer[s]);
+    e->peer[s] = nullptr;
+    for (auto& ev : e->sent_in[s])
+      if (ev) cudaEventDestroy(ev);
+    if (e->done_in[s]) cudaEventDestroy(e->done_in[s]);
+  }
+  if (wait_peers && e->bar) ce_barrier(e, c->world, "copy-engine teardown");
+  for (auto& row : e->sent)
+    for (auto& ev : row)
+      if (ev) cudaEventDestroy(ev);
+  if (e->done) cudaEventDestroy(e->done);
+  for (auto& ev : e->xs_done)
+    if (ev) cudaEventDestroy(ev);
+  for (auto& x : e->xs)
+    if (x) cudaStreamDestroy(x);
+  if (e->planes) cudaFree(e->planes);
+  if (e->bar) munmap(e->bar, sizeof(ShmBarrier));
+  if (e->owner) shm_unlink(e->shm_name);
+  delete e;
+  c->ce = nullptr;
+}
+
 void release(smm_mg_comm* c) {
+  ce_release(c, false);
   if (c->cs) cudaStreamDestroy(c->cs);
   if (c->ps) cudaStreamDestroy(c->ps);
   for (auto& w : c->work)
@@ -495,6 +685,7 @@ extern "C" int smm_mg_comm_init(smm_mg_comm** out, int rank, int world, const vo
     if (!n.ok) return fail(set_error(SMM_ERR_NCCL, "%s", n.why));
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
+    std::memcpy(c->uid, id, sizeof(c->uid));
     ncclResult_t r = n.comm_init_rank(&c->nc, world, uid, rank);
     if (r != ncclSuccess) return fail(nccl_fail(r, "ncclCommInitRank"));
   }
@@ -510,6 +701,7 @@ extern "C" int smm_mg_comm_destroy(smm_mg_comm* c) {
   if (c->ps) cudaStreamSynchronize(c->ps);
   for (auto& w : c->work)
     if (w) cudaStreamSynchronize(w);
+  ce_release(c, true);
   if (c->nc) {
     ncclResult_t r = nccl().comm_destroy(c->nc);
     if (r != ncclSuccess) rc = nccl_fail(r, "ncclCommDestroy");
@@ -538,6 +730,128 @@ extern "C" int smm_mg_comm_status(smm_mg_comm* c) {
   if (a != ncclSuccess && a != ncclInProgress) return nccl_fail(a, "asynchronous NCCL error");
   return SMM_OK;
 }
+
+// ---------------------------------------------------------------- copy-engine gather
+namespace {
+int ce_enable(smm_mg_comm* c, size_t plane_bytes) {
+  auto* e = new CeState();
+  c->ce = e;
+  const int world = c->world, rank = c->rank;
+  // Host barrier segment, named by the communicator's unique id: rank 0
+  // creates it before the exchange below, the others open it after.
+  unsigned long long h0 = 0, h1 = 0;
+  std::memcpy(&h0, c->uid, 8);
+  std::memcpy(&h1, c->uid + 8, 8);
+  snprintf(e->shm_name, sizeof(e->shm_name), "/smm_mg_%016llx%016llx", h0, h1);
+  auto map_bar = [&](bool create) -> int {
+    int fd = create ? shm_open(e->shm_name, O_CREAT | O_EXCL | O_RDWR, 0600) : shm_open(e->shm_name, O_RDWR, 0);
+    if (fd < 0) return set_error(SMM_ERR_CUDA, "copy engines: shm_open(%s) failed", e->shm_name);
+    if (create && ftruncate(fd, sizeof(ShmBarrier)) != 0) {
+      close(fd);
+      return set_error(SMM_ERR_CUDA, "copy engines: ftruncate of the barrier segment failed");
+    }
+    void* p = mmap(nullptr, sizeof(ShmBarrier), PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) return set_error(SMM_ERR_CUDA, "copy engines: mmap of the barrier segment failed");
+    e->bar = static_cast<ShmBarrier*>(p);
+    e->owner = create;
+    return SMM_OK;
+  };
+  // Local set-up.  A failure here still takes part in the exchange (with a
+  // zero byte count), so that every rank returns the error instead of
+  // leaving the others in the collective.
+  CeInfo info;
+  std::memset(&info, 0, sizeof(info));
+  auto local = [&]() -> int {
+    if (rank == 0) {
+      shm_unlink(e->shm_name);  // a stale segment of a crashed run with the same id
+      if (int rc = map_bar(true)) return rc;
+    }
+    SMM_CUDA_TRY(cudaMalloc(&e->planes, plane_bytes), "copy engines: plane buffer");
+    e->bytes = plane_bytes;
+    SMM_CUDA_TRY(cudaIpcGetMemHandle(&info.mem, e->planes), "cudaIpcGetMemHandle");
+    int lo = 0, hi = 0;
+    SMM_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&lo, &hi), "stream priorities");
+    for (int d = 0; d < world; ++d) {
+      if (d == rank) continue;
+      SMM_CUDA_TRY(cudaStreamCreateWithPriority(&e->xs[d], cudaStreamNonBlocking, hi), "copy stream");
+      SMM_CUDA_TRY(cudaEventCreateWithFlags(&e->xs_done[d], cudaEventDisableTiming), "event");
+      for (int j = 0; j < kMaxChunks; ++j) {
+        SMM_CUDA_TRY(cudaEventCreateWithFlags(&e->sent[d][j], cudaEventDisableTiming | cudaEventInterprocess),
+                     "interprocess event");
+        SMM_CUDA_TRY(cudaIpcGetEventHandle(&info.sent[d][j], e->sent[d][j]), "cudaIpcGetEventHandle");
+      }
+    }
+    SMM_CUDA_TRY(cudaEventCreateWithFlags(&e->done, cudaEventDisableTiming | cudaEventInterprocess),
+                 "interprocess event");
+    SMM_CUDA_TRY(cudaIpcGetEventHandle(&info.done, e->done), "cudaIpcGetEventHandle");
+    info.bytes = plane_bytes;
+    return SMM_OK;
+  };
+  const int local_rc = local();
+  if (local_rc) info.bytes = 0;
+  // Exchange (one NCCL all-gather of the records; set-up only).
+  CeInfo* dev = nullptr;
+  SMM_CUDA_TRY(cudaMalloc(&dev, sizeof(CeInfo) * world), "exchange buffer");
+  std::vector<CeInfo> all(world);
+  int rc = SMM_OK;
+  if (cudaMemcpy(dev + rank, &info, sizeof(CeInfo), cudaMemcpyHostToDevice) != cudaSuccess) {
+    rc = set_error(SMM_ERR_CUDA, "copy engines: exchange copy");
+  } else {
+    ncclResult_t r = nccl().allgather(dev + rank, dev, sizeof(CeInfo), ncclUint8, c->nc, c->cs);
+    if (r != ncclSuccess)
+      rc = nccl_fail(r, "ncclAllGather (copy-engine exchange)");
+    else if (cudaStreamSynchronize(c->cs) != cudaSuccess ||
+             cudaMemcpy(all.data(), dev, sizeof(CeInfo) * world, cudaMemcpyDeviceToHost) != cudaSuccess)
+      rc = set_error(SMM_ERR_CUDA, "copy engines: exchange");
+  }
+  cudaFree(dev);
+  if (local_rc) return local_rc;
+  if (rc) return rc;
+  for (int s = 0; s < world; ++s)
+    if (all[s].bytes != plane_bytes)
+      return set_error(SMM_ERR_INVALID,
+                       "smm_mg_enable_copy_engines: rank %d set up %llu plane bytes (0: its set-up failed), this "
+                       "rank %zu",
+                       s, all[s].bytes, plane_bytes);
+  e->peer[rank] = e->planes;
+  for (int s = 0; s < world; ++s) {
+    if (s == rank) continue;
+    void* p = nullptr;
+    SMM_CUDA_TRY(cudaIpcOpenMemHandle(&p, all[s].mem, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    e->peer[s] = static_cast<uint8_t*>(p);
+    for (int j = 0; j < kMaxChunks; ++j)
+      SMM_CUDA_TRY(cudaIpcOpenEventHandle(&e->sent_in[s][j], all[s].sent[rank][j]), "cudaIpcOpenEventHandle");
+    SMM_CUDA_TRY(cudaIpcOpenEventHandle(&e->done_in[s], all[s].done), "cudaIpcOpenEventHandle");
+  }
+  if (rank != 0)
+    if (int rc2 = map_bar(false)) return rc2;
+  return ce_barrier(e, world, "smm_mg_enable_copy_engines");
+}
+}  // namespace
+
+extern "C" size_t smm_mg_plane_bytes(const smm_mg_comm* c, int K, int ncols, int mode) {
+  if (!c || K <= 0 || ncols <= 0 || !valid_mode(mode) || c->world < 2) return 0;
+  return ce_planes_needed(c->world, K, ncols, mode);
+}
+
+extern "C" int smm_mg_enable_copy_engines(smm_mg_comm* c, size_t plane_bytes) {
+  SMM_RANGE("smm_mg_enable_copy_engines");
+  if (int rc = check_comm(c, "smm_mg_enable_copy_engines")) return rc;
+  if (c->world == 1) return SMM_OK;  // nothing travels
+  if (c->world > kMaxCeRanks)
+    return set_error(SMM_ERR_UNSUPPORTED, "smm_mg_enable_copy_engines: at most %d ranks", kMaxCeRanks);
+  if (plane_bytes == 0) return set_error(SMM_ERR_INVALID, "smm_mg_enable_copy_engines: zero plane bytes");
+  if (c->ce) {
+    for (auto& w : c->work) cudaStreamSynchronize(w);
+    ce_release(c, true);
+  }
+  const int rc = ce_enable(c, plane_bytes);
+  if (rc) ce_release(c, false);
+  return rc;
+}
+
+extern "C" int smm_mg_copy_engines_enabled(const smm_mg_comm* c) { return c && c->ce ? 1 : 0; }
 
 extern "C" int smm_mg_row_slabs(int N, int world, int triangular, int* bounds) {
   if (N < 0 || world < 1 || !bounds) return set_error(SMM_ERR_INVALID, "smm_mg_row_slabs: bad arguments");

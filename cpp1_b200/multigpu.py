@@ -243,6 +243,21 @@ class Communicator:
         buf = ops.workspace(nbytes, device)
         return (buf.data_ptr(), buf.numel()) if buf is not None else (None, 0)
 
+    # ---- copy-engine gather of a sharded B (collective)
+    def plane_bytes(self, k: int, ncols: int, mode: str = "3xtf32") -> int:
+        """Plane-buffer bytes a sharded call with a K x ncols B gathers into."""
+        return int(self._lib.load().smm_mg_plane_bytes(self.h, k, ncols, self._lib.MODES[mode]))
+
+    def enable_copy_engines(self, plane_bytes: int) -> None:
+        """Collective: every rank allocates `plane_bytes` (the same on every
+        rank) and maps every peer's buffer; from then on sharded calls whose
+        planes fit are gathered by copy engines instead of NCCL."""
+        self._lib.check(self._lib.load().smm_mg_enable_copy_engines(self.h, int(plane_bytes)),
+                        "smm_mg_enable_copy_engines")
+
+    def copy_engines_enabled(self) -> bool:
+        return bool(self._lib.load().smm_mg_copy_engines_enabled(self.h))
+
     # ---- products (every rank calls them with the same shapes, mode and root)
     # root: the rank holding all of B (broadcast), or SHARDED: B is this
     # rank's share, rows [rank * s, rank * s + s) of B with s = share_rows(K,

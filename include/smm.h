@@ -234,6 +234,21 @@ int smm_mg_row_slabs(int N, int world, int triangular, int* bounds);
  * environment sets it, 1 .. 16). */
 int smm_mg_chunks(int ncols, int world, int* bounds);
 
+/* Copy-engine gather of a sharded B (collective; at most 8 ranks on one
+ * node).  Every rank allocates plane_bytes of device memory (the same count
+ * on every rank) and maps every peer's allocation through CUDA IPC; from
+ * then on a sharded call whose column blocks fit (smm_mg_plane_bytes) packs
+ * this rank's share of each block into its slot of its own buffer and the
+ * copy engines push that slot into every peer's buffer -- no NCCL kernel and
+ * no SM in the transfer, which therefore runs beside the contractions.
+ * Interprocess events order the pushes against the consumers, and two host
+ * barriers per call (POSIX shared memory named by the unique id) order the
+ * event records across processes.  Enabling again replaces the buffer;
+ * smm_mg_comm_destroy releases it. */
+size_t smm_mg_plane_bytes(const smm_mg_comm* comm, int K, int ncols, int mode);
+int smm_mg_enable_copy_engines(smm_mg_comm* comm, size_t plane_bytes);
+int smm_mg_copy_engines_enabled(const smm_mg_comm* comm);
+
 /* Rows in each rank's share of a K-row B sharded over `world` ranks:
  * ceil(K / world) (the last shares may hold fewer rows of B, or none). */
 int smm_mg_share_rows(int K, int world);

@@ -1,10 +1,11 @@
 """libsmm's multi-GPU products on two GPUs (skipped with fewer).
 
 Two processes, one per GPU.  B comes from rank 0 (the other rank passes
-NaN-filled buffers) or sharded by rows (each rank passes only its share),
-and S for the sandwich from rank 0, so a slab is right only if the column
-blocks sent inside the call (broadcast, or all-gathered from the shares)
-delivered every block before the contraction that consumes it.  Each rank checks its own output slab against
+NaN-filled buffers) or sharded by rows (each rank passes only its share;
+gathered by NCCL, then again by the copy engines after
+smm_mg_enable_copy_engines), and S for the sandwich from rank 0, so a slab
+is right only if the column blocks sent inside the call delivered every
+block before the contraction that consumes it.  Each rank checks its own output slab against
 an fp64 recomputation of the whole product (torch float64 on its GPU,
 test-only), within the mode's bound: 3xTF32 1e-5, TF32 5e-3, bf16 1e-2.
 Shapes cover equal-work triangular slabs, a ragged last block (a column
@@ -65,13 +66,26 @@ def _worker(rank, world, port, results):
             """B as this rank passes it: the root's whole B (a NaN buffer on
             the other ranks), or this rank's row share."""
             if placement == "root":
-                return recv(x)
+                return recv(x)  # "sharded" and "ce" pass this rank's share
             s = MG.share_rows(k, world)
             lo, hi = min(k, rank * s), min(k, (rank + 1) * s)
             return dev(x[lo:hi]) if hi > lo else torch.empty((1, x.shape[1]), device="cuda")
 
-        for placement in ("root", "sharded"):
+        def plane_need():  # the largest plane set of the shapes below (5 blocks for T B)
+            need = 0
+            for mode in ("3xtf32", "tf32", "bf16"):
+                for k, nc in ((2304, 1024), (2301, 520), (4096, 1024), (1000, 1000), (2048, 2048)):
+                    need = max(need, comm.plane_bytes(k, nc, mode))
+                os.environ["SMM_MG_CHUNKS"] = "5"
+                need = max(need, comm.plane_bytes(4096, 2560, mode))
+                del os.environ["SMM_MG_CHUNKS"]
+            return need
+
+        for placement in ("root", "sharded", "ce"):
             root = 0 if placement == "root" else MG.SHARDED
+            if placement == "ce":
+                comm.enable_copy_engines(plane_need())
+                assert comm.copy_engines_enabled()
             for mode in ("3xtf32", "tf32", "bf16"):
                 tag = f"{placement}_{mode}"
                 # GEMM: A row slabs, B (K x N); K = 2301 leaves a short last share
