@@ -371,8 +371,15 @@ BSide make_bside(const smm_mg_comm* c, int K, int ncols, int mode, int root, voi
 }
 
 // Host barrier of the ranks of a copy-engine communicator (shared memory,
-// generation counting); gives up after kBarrierSeconds.
+// generation counting); gives up after kBarrierSeconds (SMM_MG_BARRIER_MS
+// sets the limit in milliseconds) with SMM_ERR_NCCL: a rank that left or
+// failed is seen here, on the host, before this rank enqueues any wait on it.
 int ce_barrier(CeState* e, int world, const char* who) {
+  long long limit_ms = 1000LL * kBarrierSeconds;
+  if (const char* env = std::getenv("SMM_MG_BARRIER_MS")) {
+    const long long v = std::atoll(env);
+    if (v > 0) limit_ms = v;
+  }
   ShmBarrier* b = e->bar;
   const uint32_t g = b->gen.load(std::memory_order_acquire);
   if (b->arrived.fetch_add(1, std::memory_order_acq_rel) + 1 == static_cast<uint32_t>(world)) {
@@ -386,9 +393,10 @@ int ce_barrier(CeState* e, int world, const char* who) {
     if ((it & 255) == 255) {
       timespec t;
       clock_gettime(CLOCK_MONOTONIC, &t);
-      if (t.tv_sec - t0.tv_sec > kBarrierSeconds)
-        return set_error(SMM_ERR_NCCL, "%s: a peer rank did not reach the host barrier within %d s", who,
-                         kBarrierSeconds);
+      const long long ms = (t.tv_sec - t0.tv_sec) * 1000LL + (t.tv_nsec - t0.tv_nsec) / 1000000;
+      if (ms > limit_ms)
+        return set_error(SMM_ERR_NCCL, "%s: a peer rank did not reach the host barrier within %lld ms", who,
+                         limit_ms);
       sched_yield();
     }
   }

@@ -171,3 +171,75 @@ def test_two_gpu_products_match_fp64(cuda):
         for key, e in errs.items():
             mode = key.split("_")[-1]
             assert e <= TOL[mode], (rank, key, e, errs)
+
+
+def _leave_worker(rank, world, port, results):
+    """Rank 1 leaves between calls (it aborts its communicator and exits);
+    rank 0's next copy-engine call sees it at the host barrier, before
+    enqueuing any wait on rank 1, and returns SMM_ERR_NCCL within the
+    barrier limit; rank 0 then aborts its communicator."""
+    import time
+
+    import torch.distributed as dist
+
+    from cpp1_b200 import _lib
+    from cpp1_b200 import multigpu as MG
+    from cpp1_b200 import workloads as W
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["SMM_MG_BARRIER_MS"] = "2000"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    comm = MG.Communicator(rank, world)
+    try:
+        M, K, N = 512, 1024, 512
+        w = W.make_gemm(M, N, K, seed=41)
+        s = MG.share_rows(K, world)
+        A = torch.from_numpy(w["A"][rank * (M // 2):(rank + 1) * (M // 2)]).cuda()
+        Bs = torch.from_numpy(np.ascontiguousarray(w["B"][rank * s:(rank + 1) * s])).cuda()
+        C = torch.empty((M // 2, N), device="cuda")
+        comm.enable_copy_engines(comm.plane_bytes(K, N, "3xtf32"))
+        comm.gemm(A, Bs, C, "3xtf32", root=MG.SHARDED)  # one good call
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 1:
+            comm.abort()
+            comm = None
+            results[rank] = "left"
+            return
+        time.sleep(0.5)
+        t0 = time.time()
+        try:
+            comm.gemm(A, Bs, C, "3xtf32", root=MG.SHARDED)
+            results[rank] = "no error"
+        except _lib.SmmError as e:
+            results[rank] = (int(e.status), round(time.time() - t0, 2), str(e))
+    finally:
+        if comm is not None:
+            comm.abort()
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def test_rank_leaving_is_seen_at_the_host_barrier(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from cpp1_b200 import _lib
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        procs = [ctx.Process(target=_leave_worker, args=(r, world, port, results)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        res = dict(results)
+    assert res.get(1) == "left"
+    code, seconds, msg = res[0]
+    assert code == _lib.SMM_ERR_NCCL and "host barrier" in msg, res[0]
+    assert seconds < 30, res[0]
