@@ -10,7 +10,10 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libsmm.so")
+# SMM_LIB=debug selects the bounds-checked build (libsmm_debug.so: every
+# computed offset into a structured operand is range-checked on the device;
+# a violation is skipped and reported as SMM_ERR_BOUNDS by smm_device_status).
+LIB_PATH = os.path.join(_HERE, "libsmm_debug.so" if os.environ.get("SMM_LIB") == "debug" else "libsmm.so")
 
 SMM_OK = 0
 SMM_ERR_INVALID = 1
@@ -19,6 +22,7 @@ SMM_ERR_NCCL = 3
 SMM_ERR_DEVICE_TIMEOUT = 4
 SMM_ERR_WORKSPACE = 5
 SMM_ERR_UNSUPPORTED = 6
+SMM_ERR_BOUNDS = 7
 
 STATUS_NAMES = {
     SMM_OK: "SMM_OK",
@@ -28,6 +32,7 @@ STATUS_NAMES = {
     SMM_ERR_DEVICE_TIMEOUT: "SMM_ERR_DEVICE_TIMEOUT",
     SMM_ERR_WORKSPACE: "SMM_ERR_WORKSPACE",
     SMM_ERR_UNSUPPORTED: "SMM_ERR_UNSUPPORTED",
+    SMM_ERR_BOUNDS: "SMM_ERR_BOUNDS",
 }
 
 MODES = {"3xtf32": 0, "tf32": 1, "bf16": 2}

@@ -11,6 +11,11 @@ namespace smm {
 // Device error word bits (written with atomicOr into the per-call status).
 enum : uint32_t {
   kDevErrTimeout = 1u << 0,
+  kDevErrBounds = 1u << 1,  // debug builds: an index check caught an out-of-range read (skipped)
+  // Which check fired (ORed with kDevErrBounds).
+  kBoundsA = 1u << 16,       // structured left operand (packed triangle / Toeplitz generator)
+  kBoundsB = 1u << 17,       // structured right operand
+  kBoundsExpand = 1u << 18,  // packed-operand expansion
   // Which wait gave up (ORed with kDevErrTimeout).
   kWaitProducer = 1u << 8,   // producer waiting for a free stage
   kWaitMma = 1u << 9,        // MMA issuer waiting for a staged k-block
@@ -19,6 +24,30 @@ enum : uint32_t {
   kWaitDrain = 1u << 12,     // teardown drain
   kWaitProbe = 1u << 13,     // timeout probe
 };
+
+// Bounds-checked debug build (compiled with -DSMM_DEBUG_BOUNDS: the
+// library's libsmm_debug.so).  Every computed offset into a structured
+// operand is checked against the operand's element count; an offset outside
+// it sets kDevErrBounds | where in the status word and the read is skipped
+// (zero) instead of made.  In the normal build the checks compile away.
+#ifdef SMM_DEBUG_BOUNDS
+constexpr bool kDebugBounds = true;
+#else
+constexpr bool kDebugBounds = false;
+#endif
+__device__ __forceinline__ bool dbg_ok(long long off, long long limit, uint32_t* status, uint32_t where) {
+  if constexpr (kDebugBounds) {
+    if (off < 0 || off >= limit) {
+      if (status) atomicOr(status, kDevErrBounds | where);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ float ld_chk(const float* __restrict__ src, long long off, long long limit,
+                                        uint32_t* status, uint32_t where) {
+  return dbg_ok(off, limit, status, where) ? __ldg(src + off) : 0.0f;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

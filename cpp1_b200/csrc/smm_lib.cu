@@ -294,6 +294,8 @@ extern "C" int smm_device_status(void* stream) {
     SMM_CUDA_TRY(cudaMemset(w, 0, sizeof(v)), "clear status word");
     if (v & kDevErrTimeout)
       return set_error(SMM_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired (status 0x%x); it exited cleanly", v);
+    if (v & kDevErrBounds)
+      return set_error(SMM_ERR_BOUNDS, "a bounds check caught an out-of-range read (status 0x%x); it was skipped", v);
   }
   return SMM_OK;
 }

@@ -9,6 +9,8 @@
 #include <cstdlib>
 
 #include "smm_contract.h"
+#include "smm_device.cuh"
+#include "smm_host.h"
 
 namespace smm {
 namespace {
@@ -79,7 +81,8 @@ __device__ __forceinline__ void store_pair(__nv_bfloat16* p, float a, float b) {
 }
 template <int SF, typename T>
 __global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P, int n, int row0, int rows,
-                                                     T* __restrict__ dst, int ld) {
+                                                     T* __restrict__ dst, int ld, uint32_t* status) {
+  const long long len = static_cast<long long>(n) * (n + 1) / 2;
   __shared__ float tile[64][65];
   const int r0 = blockIdx.y * 64;  // slab row of the tile
   const int c0 = blockIdx.x * 64;  // column of the tile
@@ -90,7 +93,7 @@ __global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P
     const int i = row0 + r0 + il;
     for (int jl = t >> 6; jl < 64; jl += 4) {
       const int j = c0 + jl;  // j < i for every element of the tile
-      tile[jl][il] = (r0 + il < rows && j < n) ? __ldg(P + packed_idx(j, i, n)) : 0.0f;
+      tile[jl][il] = (r0 + il < rows && j < n) ? ld_chk(P, packed_idx(j, i, n), len, status, kBoundsExpand) : 0.0f;
     }
     __syncthreads();
   }
@@ -110,11 +113,11 @@ __global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P
       } else if (jj >= n) {
         v[e] = 0.0f;
       } else if constexpr (SF == SMM_STRUCT_UPPER) {
-        v[e] = jj >= i ? __ldg(P + packed_idx(i, jj, n)) : 0.0f;
+        v[e] = jj >= i ? ld_chk(P, packed_idx(i, jj, n), len, status, kBoundsExpand) : 0.0f;
       } else if constexpr (SF == SMM_STRUCT_LOWER) {
-        v[e] = jj <= i ? __ldg(P + (static_cast<long long>(i) * (i + 1) / 2 + jj)) : 0.0f;
+        v[e] = jj <= i ? ld_chk(P, static_cast<long long>(i) * (i + 1) / 2 + jj, len, status, kBoundsExpand) : 0.0f;
       } else {
-        v[e] = __ldg(P + (jj >= i ? packed_idx(i, jj, n) : packed_idx(jj, i, n)));
+        v[e] = ld_chk(P, jj >= i ? packed_idx(i, jj, n) : packed_idx(jj, i, n), len, status, kBoundsExpand);
       }
     }
     store_pair(dst + static_cast<long long>(r) * ld + j, v[0], v[1]);
@@ -127,13 +130,14 @@ __global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P
 // along a row (x) and stride over rows (y).  Columns N .. ld-1 are zero.
 template <typename T>
 __global__ void __launch_bounds__(256) toeplitz_expand_kernel(const float* __restrict__ g, int K, int N,
-                                                              T* __restrict__ dst, int ld) {
+                                                              T* __restrict__ dst, int ld, uint32_t* status) {
   const int j = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= ld) return;
+  const long long len = static_cast<long long>(K) + N - 1;
   for (int k = blockIdx.y; k < K; k += gridDim.y) {
-    const float* w = g + (K - 1 - k);
-    const float a = j < N ? __ldg(w + j) : 0.0f;
-    const float b = j + 1 < N ? __ldg(w + j + 1) : 0.0f;
+    const long long w = K - 1 - k;
+    const float a = j < N ? ld_chk(g, w + j, len, status, kBoundsExpand) : 0.0f;
+    const float b = j + 1 < N ? ld_chk(g, w + j + 1, len, status, kBoundsExpand) : 0.0f;
     store_pair(dst + static_cast<long long>(k) * ld + j, a, b);
   }
 }
@@ -142,9 +146,15 @@ template <typename T>
 void launch_expand(const float* P, int sf, int n, int row0, int rows, T* dst, int ld, cudaStream_t st) {
   const dim3 grid((ld + 63) / 64, (rows + 63) / 64);
   switch (sf) {
-    case SMM_STRUCT_UPPER: expand_kernel<SMM_STRUCT_UPPER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
-    case SMM_STRUCT_LOWER: expand_kernel<SMM_STRUCT_LOWER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
-    default: expand_kernel<SMM_STRUCT_SYMM, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld); break;
+    case SMM_STRUCT_UPPER:
+      expand_kernel<SMM_STRUCT_UPPER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word());
+      break;
+    case SMM_STRUCT_LOWER:
+      expand_kernel<SMM_STRUCT_LOWER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word());
+      break;
+    default:
+      expand_kernel<SMM_STRUCT_SYMM, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word());
+      break;
   }
 }
 
@@ -245,11 +255,11 @@ int expand_toeplitz(const float* g, int K, int N, int mode, uint8_t*& ws_cur, St
   const int gy = std::max(1, std::min(K, std::max(1, 148 * 16 / gx)));
   if (bf) {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
-    toeplitz_expand_kernel<__nv_bfloat16><<<dim3(gx, gy), 256, 0, st>>>(g, K, N, dst, ld);
+    toeplitz_expand_kernel<__nv_bfloat16><<<dim3(gx, gy), 256, 0, st>>>(g, K, N, dst, ld, device_status_word());
     *out = {nullptr, nullptr, ld, dst};
   } else {
     float* dst = reinterpret_cast<float*>(ws_cur);
-    toeplitz_expand_kernel<float><<<dim3(gx, gy), 256, 0, st>>>(g, K, N, dst, ld);
+    toeplitz_expand_kernel<float><<<dim3(gx, gy), 256, 0, st>>>(g, K, N, dst, ld, device_status_word());
     *out = {dst, nullptr, ld};
   }
   ws_cur += toeplitz_expanded_bytes(K, N, mode);

@@ -204,16 +204,20 @@ __device__ __forceinline__ long long packed_idx(long long i, long long j, long l
   return i * n - i * (i - 1) / 2 + (j - i);
 }
 
+// Elements of a packed triangle of order n.
+__device__ __forceinline__ long long packed_len(long long n) { return n * (n + 1) / 2; }
+
 // Value of the structured right operand at (row k, column n); zero outside.
 template <BKind BK>
-__device__ __forceinline__ float b_value(const float* __restrict__ src, int nd, int k, int n) {
+__device__ __forceinline__ float b_value(const float* __restrict__ src, int nd, int k, int n, uint32_t* status) {
   if (k >= nd || n >= nd) return 0.0f;
+  const long long len = packed_len(nd);
   if constexpr (BK == BKind::UpperPacked) {
-    return n >= k ? __ldg(src + packed_idx(k, n, nd)) : 0.0f;
+    return n >= k ? ld_chk(src, packed_idx(k, n, nd), len, status, kBoundsB) : 0.0f;
   } else if constexpr (BK == BKind::LowerPacked) {
-    return n <= k ? __ldg(src + (static_cast<long long>(k) * (k + 1) / 2 + n)) : 0.0f;
+    return n <= k ? ld_chk(src, static_cast<long long>(k) * (k + 1) / 2 + n, len, status, kBoundsB) : 0.0f;
   } else {  // SymmPacked
-    return n >= k ? __ldg(src + packed_idx(k, n, nd)) : __ldg(src + packed_idx(n, k, nd));
+    return ld_chk(src, n >= k ? packed_idx(k, n, nd) : packed_idx(n, k, nd), len, status, kBoundsB);
   }
 }
 
@@ -282,11 +286,19 @@ __device__ __forceinline__ void a_row_bases(uint32_t (&rb)[KS / 2], const UmmaPa
   }
 }
 
+// Elements of a structured left operand of order n: a Toeplitz generator
+// (2n - 1) or a packed triangle.
+template <AKind AK>
+__device__ __forceinline__ long long a_src_len(long long n) {
+  return AK == AKind::Toeplitz ? 2 * n - 1 : packed_len(n);
+}
+
 template <AKind AK, int KS>
 __device__ __forceinline__ void a_gather(float (&v)[KS / 2], const UmmaParams& p, const uint32_t (&rb)[KS / 2],
                                          int g_first, int k0, int xw, int lane) {
   const int n = p.a_dim;
   const float* __restrict__ src = p.a_src;
+  const long long len = a_src_len<AK>(n);
   if (a_rows_mapping<AK, KS>(g_first, k0)) {
     // symmetric tile wholly below the diagonal: element (gr, k) = S[k][gr],
     // at row start of packed row k (+ gr), k consecutive per thread
@@ -297,7 +309,7 @@ __device__ __forceinline__ void a_gather(float (&v)[KS / 2], const UmmaParams& p
 #pragma unroll
     for (int it = 0; it < KS / 2; ++it) {
       const int k = k0 + kl + it;
-      v[it] = (gr < n && k < n) ? __ldg(src + (base + static_cast<uint32_t>(gr))) : 0.0f;
+      v[it] = (gr < n && k < n) ? ld_chk(src, base + static_cast<uint32_t>(gr), len, p.status, kBoundsA) : 0.0f;
       base += static_cast<uint32_t>(n - k - 1);  // row start of packed row k+1
     }
     return;
@@ -314,13 +326,15 @@ __device__ __forceinline__ void a_gather(float (&v)[KS / 2], const UmmaParams& p
     const int gr = g_first + r;
     const bool in = gr < n && k < n;
     if constexpr (AK == AKind::UpperPacked) {
-      v[it] = (in && k >= gr) ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
+      v[it] = (in && k >= gr) ? ld_chk(src, rb[it] + static_cast<uint32_t>(k), len, p.status, kBoundsA) : 0.0f;
     } else if constexpr (AK == AKind::LowerPacked) {
-      v[it] = (in && k <= gr) ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
+      v[it] = (in && k <= gr) ? ld_chk(src, rb[it] + static_cast<uint32_t>(k), len, p.status, kBoundsA) : 0.0f;
     } else if constexpr (AK == AKind::Toeplitz) {
-      v[it] = in ? __ldg(src + (rb[it] + static_cast<uint32_t>(k))) : 0.0f;
+      v[it] = in ? ld_chk(src, rb[it] + static_cast<uint32_t>(k), len, p.status, kBoundsA) : 0.0f;
     } else {
-      v[it] = in ? __ldg(src + (k >= gr ? rb[it] + static_cast<uint32_t>(k) : mbase + static_cast<uint32_t>(gr))) : 0.0f;
+      v[it] = in ? ld_chk(src, k >= gr ? rb[it] + static_cast<uint32_t>(k) : mbase + static_cast<uint32_t>(gr), len,
+                          p.status, kBoundsA)
+                 : 0.0f;
     }
   }
 }
@@ -362,6 +376,7 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
   const float* __restrict__ src = p.a_src;
   const uint32_t dst0 = smem_u32(ah);
   const int fw = ft >> 5, lane = ft & 31;
+  const long long len = a_src_len<AK>(n);
   if (a_rows_mapping<AK, KS>(g_first, k0)) {
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
@@ -372,7 +387,7 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
       for (int rg = 0; rg < 4; ++rg) {
         const int r = rg * 32 + lane;
         const int gr = g_first + r;
-        const bool in = gr < n && k < n;
+        const bool in = gr < n && k < n && dbg_ok(kb + static_cast<uint32_t>(gr), len, p.status, kBoundsA);
         cp_async_4(dst0 + swz_offset(r, kl >> 2, 64) + (kl & 3) * 4, in ? src + (kb + static_cast<uint32_t>(gr)) : src,
                    in ? 4u : 0u);
       }
@@ -407,6 +422,7 @@ __device__ __forceinline__ void a_async_fill(const UmmaParams& p, uint8_t* ah, i
       valid = in;
       so = k >= gr ? rb + static_cast<uint32_t>(k) : mbase + static_cast<uint32_t>(gr);
     }
+    valid = valid && dbg_ok(so, len, p.status, kBoundsA);
     cp_async_4(dst0 + swz_offset(r, kl >> 2, 64) + (kl & 3) * 4, valid ? src + so : src, valid ? 4u : 0u);
     // next row of this lane: two rows down
     if constexpr (AK == AKind::Toeplitz)
@@ -531,9 +547,12 @@ __device__ __forceinline__ void b_build(const UmmaParams& p, uint8_t* bh, uint8_
       b_coord<BN, KS>(mirror, t, b0 + e, kr, n);
       if constexpr (BK == BKind::Toeplitz) {  // K x N Toeplitz of generator b_src: T[k][n] = g[(K-1) + (n-k)]
         const int k = k0 + kr, nn = n0 + n;
-        v[e] = (k < p.K && nn < p.N) ? __ldg(p.b_src + (p.K - 1 + nn - k)) : 0.0f;
+        v[e] = (k < p.K && nn < p.N)
+                   ? ld_chk(p.b_src, static_cast<long long>(p.K) - 1 + nn - k,
+                            static_cast<long long>(p.K) + p.N - 1, p.status, kBoundsB)
+                   : 0.0f;
       } else {
-        v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n);
+        v[e] = b_value<BK>(p.b_src, p.b_dim, k0 + kr, n0 + n, p.status);
       }
     }
 #pragma unroll

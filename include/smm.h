@@ -52,7 +52,9 @@ typedef enum {
   SMM_ERR_NCCL = 3,           /* reserved for the multi-GPU layer */
   SMM_ERR_DEVICE_TIMEOUT = 4, /* a kernel's bounded wait expired; the kernel exited cleanly */
   SMM_ERR_WORKSPACE = 5,      /* caller workspace missing or too small */
-  SMM_ERR_UNSUPPORTED = 6     /* device is not sm_100 or feature not built */
+  SMM_ERR_UNSUPPORTED = 6,    /* device is not sm_100 or feature not built */
+  SMM_ERR_BOUNDS = 7          /* bounds-checked debug build (libsmm_debug.so): an out-of-range read was
+                                 caught and skipped */
 } smm_status;
 
 typedef enum { SMM_MODE_3XTF32 = 0, SMM_MODE_TF32 = 1, SMM_MODE_BF16 = 2 } smm_mode;

@@ -27,6 +27,16 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
 
 
+def test_debug_bounds_library_exports_every_declared_symbol():
+    """The bounds-checked build (libsmm_debug.so, -DSMM_DEBUG_BOUNDS) is a
+    drop-in of the same ABI."""
+    path = os.path.join(os.path.dirname(_lib.LIB_PATH), "libsmm_debug.so")
+    assert os.path.exists(path), "build it with python -m cpp1_b200.build --debug-bounds"
+    L = ctypes.CDLL(path)
+    missing = [f for f in declared_functions() if not hasattr(L, f)]
+    assert not missing, missing
+
+
 def test_version_and_error_text():
     L = _lib.load()
     assert L.smm_version() >= 100
