@@ -13,18 +13,21 @@
 // C = L B with L, B and C in host memory (pinned for overlap; pageable works,
 // synchronously): the drop-in for callers of the reference's CPU kernels,
 // which take host arrays.  The left operand(s) cross PCIe once and are
-// prepared on the device (staged, or a packed operand expanded); B then
-// streams through in column chunks.  Chunk j alternates between two streams:
-// its 2-D copy-in, its product and its 2-D copy-out into C's columns are
-// ordered on that stream, and they overlap the other stream's (PCIe is full
-// duplex: chunk j's copy-out runs beside chunk j+1's copy-in).
+// prepared on the device (staged, or a packed operand expanded) on a stream
+// of their own; B streams through in column chunks.  Chunk j alternates
+// between two streams: its 2-D copy-in (which does not wait for the left
+// operand, so B's first chunks cross PCIe while the left operand is being
+// expanded), its product (which does) and its 2-D copy-out into C's columns
+// are ordered on that stream, and they overlap the other stream's (PCIe is
+// full duplex: chunk j's copy-out runs beside chunk j+1's copy-in).
 namespace smm {
 namespace {
 
 enum class HostLeft { Gemm, Upper, Symm, Toeplitz, Sandwich };
 
 struct HostStreams {
-  cudaStream_t st[2] = {nullptr, nullptr};
+  cudaStream_t st[2] = {nullptr, nullptr};  // B chunks, alternating
+  cudaStream_t sl = nullptr;                // the left operand(s): copy in and prepare
   cudaEvent_t left_ready = nullptr;
   bool init = false;
 };
@@ -41,6 +44,7 @@ int host_streams(HostStreams** out) {
   std::lock_guard<std::mutex> lock(init_mu);
   if (!h.init) {
     for (auto& s : h.st) SMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
+    SMM_CUDA_TRY(cudaStreamCreateWithFlags(&h.sl, cudaStreamNonBlocking), "stream create");
     SMM_CUDA_TRY(cudaEventCreateWithFlags(&h.left_ready, cudaEventDisableTiming), "event create");
     h.init = true;
   }
@@ -106,9 +110,9 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
   if (int rc = check_ws(who, dev_ws, ws_bytes, host_ws_bytes(h))) return rc;
   HostStreams* hs = nullptr;
   if (int rc = host_streams(&hs)) return rc;
-  cudaStream_t s0 = hs->st[0];
+  cudaStream_t s0 = hs->sl;  // the left operand's stream
 
-  // ---- left operand(s): copy in once, prepare on stream 0
+  // ---- left operand(s): copy in once, prepare on their own stream
   uint8_t* cur = static_cast<uint8_t*>(dev_ws);
   Operand left, amat;  // amat: the sandwich's A
   if (h.kind == HostLeft::Gemm || h.kind == HostLeft::Sandwich) {
@@ -141,7 +145,6 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
                    : h.kind == HostLeft::Upper  ? AKind::UpperDense
                                                 : AKind::Dense;
   SMM_CUDA_TRY(cudaEventRecord(hs->left_ready, s0), "event record");
-  SMM_CUDA_TRY(cudaStreamWaitEvent(hs->st[1], hs->left_ready, 0), "stream wait");
 
   // ---- B in column chunks, alternating streams
   const int w = host_chunk_cols(N);
@@ -171,6 +174,7 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
     Staged bs;
     if (int rc = stage_operand(braw, K, wc, mode, stage_cur, &bs, st)) return rc;
     const Operand bop = dense_op(bs.ptr, bs.lo, bs.ld, bs.bf16);
+    if (c < 2) SMM_CUDA_TRY(cudaStreamWaitEvent(st, hs->left_ready, 0), "wait for the left operand");
     if (h.kind == HostLeft::Sandwich) {
       // X_j = S B_j (its bf16 copy too in bf16 mode), then C_j = A X_j
       const int ldx = round4(wc), ldx_bf = round8(wc);
@@ -191,7 +195,8 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
                                    static_cast<size_t>(wc) * 4, M, cudaMemcpyDeviceToHost, st),
                  "copy C chunk");
   }
-  SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[1]), "stream sync");
+  // the caller's view: both chunk streams and the left stream drained
+  for (int k = 0; k < 2; ++k) SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[k]), "stream sync");
   return smm_device_status(s0);
 }
 
@@ -238,9 +243,10 @@ int host_right_product(const char* who, HostRight kind, int M, int N, int K, int
   if (int rc = check_ws(who, dev_ws, ws_bytes, host_right_ws(kind, M, N, K, mode))) return rc;
   HostStreams* hs = nullptr;
   if (int rc = host_streams(&hs)) return rc;
-  cudaStream_t s0 = hs->st[0];
+  cudaStream_t s0 = hs->sl;  // the structured operand's stream
 
-  // ---- X: copy in once, expand on stream 0
+  // ---- X: copy in once, expand on its own stream (the A chunks' copies
+  // do not wait for it; their products do)
   uint8_t* cur = static_cast<uint8_t*>(dev_ws);
   const size_t xlen = kind == HostRight::Toeplitz ? static_cast<size_t>(K) + N - 1 : static_cast<size_t>(K) * (K + 1) / 2;
   float* xraw = reinterpret_cast<float*>(cur);
@@ -259,7 +265,6 @@ int host_right_product(const char* who, HostRight kind, int M, int N, int K, int
   Operand xop = dense_op(ex.ptr, nullptr, ex.ld, ex.bf16);
   if (kind == HostRight::Upper) xop.tri = 1;  // K range clipped per column tile
   SMM_CUDA_TRY(cudaEventRecord(hs->left_ready, s0), "event record");
-  SMM_CUDA_TRY(cudaStreamWaitEvent(hs->st[1], hs->left_ready, 0), "stream wait");
 
   // ---- A in row chunks, alternating streams
   const int h = host_row_chunk(M);
@@ -280,6 +285,7 @@ int host_right_product(const char* who, HostRight kind, int M, int N, int K, int
                  "copy A chunk");
     Staged as;
     if (int rc = stage_operand(araw, rows, K, mode, stage_cur, &as, st)) return rc;
+    if (c < 2) SMM_CUDA_TRY(cudaStreamWaitEvent(st, hs->left_ready, 0), "wait for the structured operand");
     if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(as.ptr, as.lo, as.ld, as.bf16), xop, cch,
                                  N, rows, N, K, st))
       return rc;
@@ -287,7 +293,8 @@ int host_right_product(const char* who, HostRight kind, int M, int N, int K, int
                                  cudaMemcpyDeviceToHost, st),
                  "copy C chunk");
   }
-  SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[1]), "stream sync");
+  // the caller's view: both chunk streams and the left stream drained
+  for (int k = 0; k < 2; ++k) SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[k]), "stream sync");
   return smm_device_status(s0);
 }
 
