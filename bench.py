@@ -21,13 +21,16 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
             no collective on the data path (the rows are independent).
   others    strong scaling: the output is split into row slabs (equal-work
             boundaries for the triangular operand); each step is one libsmm
-            multi-GPU call (smm_mg_*): the shared operand B (S and B for
-            A S B) is broadcast from rank 0 in column blocks inside the call
-            and every rank computes its slab's columns block by block as they
-            land, so the transfer overlaps the contraction within one product.  A S B
-            computes (A_slab S) B per slab.  The line also carries the
-            compute-only and broadcast-only times and the fused call's
-            roofline (MMA time vs the NVLink time of the broadcast bytes).
+            multi-GPU call (smm_mg_*).  By default B arrives sharded by rows
+            (--b-placement sharded) and is gathered in column blocks inside
+            the call by the copy engines through CUDA IPC (--transfer ce; or
+            by NCCL all-gathers, --transfer nccl); --b-placement root keeps
+            B on rank 0 and broadcasts it by NCCL.  Every rank computes its
+            slab's columns block by block as they land, so the transfer
+            overlaps the contraction within one product.  A S B computes
+            (A_slab S) B per slab.  The line also carries the compute-only
+            and transfer-only times and the fused call's roofline (MMA time
+            vs the NVLink time of the bytes each rank receives).
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, CUDA events on the launching stream, max over

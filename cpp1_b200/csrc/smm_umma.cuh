@@ -136,7 +136,15 @@ struct UmmaParams {
 };
 
 // Slots of the diagnostic record (UmmaParams::trace, 64 words).
-enum : int { kTrTmem = 0, kTrNumKb = 1, kTrAccOk = 2, kTrMmas = 3, kTrAcc = 4 /*16 words*/, kTrWords = 64 };
+enum : int {
+  kTrTmem = 0,
+  kTrNumKb = 1,
+  kTrAccOk = 2,
+  kTrMmas = 3,
+  kTrAcc = 4 /*16 words*/,
+  kTrTime = 24 /*8 phase stamps (low 32 bits of %globaltimer, ns) of CTA 0, then 8 of the grid's last CTA*/,
+  kTrWords = 64
+};
 
 constexpr int kBM = 128;
 constexpr int kBK = 16;                     // fp32 elements per k-block (64 bytes)
@@ -700,6 +708,12 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   const int num_kb = (max(kb_end - kb_begin, 0) + kSubs - 1) / kSubs;
   const int nch = SPLIT3 ? (num_kb + kChunkS - 1) / kChunkS : 1;
 
+  // Phase stamps of the diagnostic record (CTA 0 and the grid's last CTA).
+  const int trb = p.trace == nullptr ? -1 : blockIdx.x == 0 ? 0 : blockIdx.x == gridDim.x - 1 ? 1 : -1;
+  auto stamp = [&](int i) {
+    if (trb >= 0) p.trace[kTrTime + 8 * trb + i] = static_cast<uint32_t>(globaltimer_ns());
+  };
+  if (threadIdx.x == 0) stamp(0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1 + (kACp ? kAFillThreads : 0));  // TMA producer (+ fill threads)
@@ -729,6 +743,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) stamp(1);
   const bool tr = p.trace != nullptr && blockIdx.x == 0;
   if (tr && threadIdx.x == 0) {
     p.trace[kTrTmem] = tmem_base;
@@ -835,6 +850,33 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
       }
     }
   };
+  // Whole-warp stores of 32 result columns through shared memory.  A warp's
+  // lanes hold 32 different rows (tensor-memory lane = output row), so a
+  // direct store instruction touches 32 rows; transposed through a per-warp
+  // 32 x 32 buffer (at wbase, in the then idle stage memory), each store
+  // instruction writes four whole 128-byte row segments.  Used once the main
+  // loop is done, for fp32 C with 16-byte rows, on whole 32-column runs.
+  constexpr int kWs = 36;  // buffer row stride (floats): 16-byte rows, conflict-free quarter-warp phases
+  static_assert(8 * 32 * kWs * 4 <= STAGES * kStage, "epilogue transpose buffers fit the stage memory");
+  const bool c_vec = p.C != nullptr && (p.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+  const bool c_plain = c_vec && p.C_bf16 == nullptr && p.C_lo == nullptr;  // nothing but fp32 C to write
+  auto store32 = [&](float* wbase, int row0, int col, const uint32_t (&r)[32]) {
+    float* wb = wbase + (warp - 2) * 32 * kWs;
+    float* mine = wb + lane * kWs;
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      reinterpret_cast<float4*>(mine)[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                       __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = j * 32 + lane, rr = i >> 3, c4 = i & 7;
+      if (row0 + rr < p.M)
+        *reinterpret_cast<float4*>(p.C + static_cast<long long>(row0 + rr) * p.ldc + col + 4 * c4) =
+            *reinterpret_cast<const float4*>(wb + rr * kWs + 4 * c4);
+    }
+    __syncwarp();
+  };
   bool acc_valid = false;  // transform warps: the accumulator holds this CTA's result
 
   if (warp == 0) {
@@ -858,6 +900,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         }
         ++issued;
       }
+      stamp(2);
       if (*abort_flag) {
         // Drain: wait (bounded, ignoring the abort flag) for the last copy
         // issued into each stage, so no bulk copy lands in shared memory
@@ -938,6 +981,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
         }
       }
       if (tr) p.trace[kTrMmas] = static_cast<uint32_t>(issued);
+      stamp(3);
       // Signals the epilogue; on abort it still fires once every MMA issued
       // so far has finished.  The issuer waits for it too (bounded, ignoring
       // the abort flag) so tensor memory is quiescent before it is freed.
@@ -1096,17 +1140,25 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     }
     const bool acc_ok = __all_sync(0xffffffffu, last_ok && !*abort_flag);
     acc_valid = acc_ok;
+    if (t == 0) stamp(4);
     if (tr && t == 0) p.trace[kTrAccOk] = acc_ok ? 1u : 0u;
     if (SPLITK == 1 && acc_ok) {
       tc_fence_after_sync();
-      const int row = m0 + q * 32 + lane;
+      const int row0 = m0 + q * 32;
 #pragma unroll 1
-      for (int c = 0; c < kHalf; c += 16) {
-        uint32_t r[16];
-        final16(c, r);
+      for (int c = 0; c < kHalf; c += 32) {
+        uint32_t r[32];
+        final16(c, *reinterpret_cast<uint32_t(*)[16]>(r));
+        final16(c + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
         if (tr && q == 0 && lane == 0 && h == 0 && c == 0)
           for (int j = 0; j < 16; ++j) p.trace[kTrAcc + j] = r[j];
-        store16(row, n0 + h * kHalf + c, r);
+        const int col = n0 + h * kHalf + c;
+        if (c_plain && col + 32 <= p.N) {
+          store32(reinterpret_cast<float*>(smem), row0, col, r);
+        } else {
+          store16(row0 + lane, col, *reinterpret_cast<uint32_t(*)[16]>(r));
+          store16(row0 + lane, col + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+        }
       }
     }
   }
@@ -1115,41 +1167,70 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
     // Combine the two halves of the K range: CTA 1's results go to CTA 0's
     // stage memory (free once both pipelines are done: every MMA has
     // completed, so every loaded stage was consumed), CTA 0 adds them to its
-    // own and stores C.  Every thread of both CTAs passes both barriers.
+    // own and stores C.  Both sides move whole rows: CTA 1 transposes each
+    // 32 x 32 block through its own buffers so that eight lanes write one
+    // 128-byte row segment into CTA 0, and CTA 0 stores its sums the same way
+    // (buffers past the exchange tile).  Every thread of both CTAs passes
+    // both barriers.
     constexpr int kXld = BN + 4;  // row stride (floats) of the exchange tile: 16-byte rows, few bank conflicts
-    static_assert(kBM * kXld * 4 <= STAGES * kStage, "exchange tile fits the stage memory");
+    static_assert((kBM * kXld + 8 * 32 * kWs) * 4 <= STAGES * kStage,
+                  "exchange tile and transpose buffers fit the stage memory");
     float* xbuf = reinterpret_cast<float*>(smem);
+    float* wbase = xbuf + kBM * kXld;
     const bool xf = warp >= 2 && warp < 2 + kXformThreads / 32;
     const int xrow = eq * 32 + lane;  // tile row of this transform thread
     tc_fence_before_sync();
     cluster_sync_all();
     tc_fence_after_sync();
     if (xf && krank == 1 && acc_valid) {
+      float* wb = wbase + (warp - 2) * 32 * kWs;
+      float* mine = wb + lane * kWs;
 #pragma unroll 1
-      for (int c = 0; c < kHalf; c += 16) {
-        uint32_t r[16];
-        final16(c, r);
-        const uint32_t dst = mapa_shared(smem_u32(xbuf + xrow * kXld + eh * kHalf + c), 0);
+      for (int c = 0; c < kHalf; c += 32) {
+        uint32_t r[32];
+        final16(c, *reinterpret_cast<uint32_t(*)[16]>(r));
+        final16(c + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
 #pragma unroll
-        for (int v = 0; v < 4; ++v) st_cluster_v4(dst + 16 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+        for (int v = 0; v < 8; ++v)
+          reinterpret_cast<float4*>(mine)[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                           __uint_as_float(r[4 * v + 2]),
+                                                           __uint_as_float(r[4 * v + 3]));
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = j * 32 + lane, rr = i >> 3, c4 = i & 7;
+          const float4 v4 = *reinterpret_cast<const float4*>(wb + rr * kWs + 4 * c4);
+          const uint32_t dst = mapa_shared(smem_u32(xbuf + (eq * 32 + rr) * kXld + eh * kHalf + c + 4 * c4), 0);
+          st_cluster_v4(dst, __float_as_uint(v4.x), __float_as_uint(v4.y), __float_as_uint(v4.z),
+                        __float_as_uint(v4.w));
+        }
+        __syncwarp();
       }
     }
     cluster_sync_all();
+    if (threadIdx.x == 64) stamp(5);
     if (xf && krank == 0 && acc_valid) {
 #pragma unroll 1
-      for (int c = 0; c < kHalf; c += 16) {
-        uint32_t r[16];
-        final16(c, r);
+      for (int c = 0; c < kHalf; c += 32) {
+        uint32_t r[32];
+        final16(c, *reinterpret_cast<uint32_t(*)[16]>(r));
+        final16(c + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
         const float4* src = reinterpret_cast<const float4*>(xbuf + xrow * kXld + eh * kHalf + c);
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
+        for (int v = 0; v < 8; ++v) {
           const float4 o = src[v];
           r[4 * v] = __float_as_uint(__uint_as_float(r[4 * v]) + o.x);
           r[4 * v + 1] = __float_as_uint(__uint_as_float(r[4 * v + 1]) + o.y);
           r[4 * v + 2] = __float_as_uint(__uint_as_float(r[4 * v + 2]) + o.z);
           r[4 * v + 3] = __float_as_uint(__uint_as_float(r[4 * v + 3]) + o.w);
         }
-        store16(m0 + xrow, n0 + eh * kHalf + c, r);
+        const int col = n0 + eh * kHalf + c;
+        if (c_plain && col + 32 <= p.N) {
+          store32(wbase, m0 + eq * 32, col, r);
+        } else {
+          store16(m0 + xrow, col, *reinterpret_cast<uint32_t(*)[16]>(r));
+          store16(m0 + xrow, col + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+        }
       }
     }
   }
@@ -1163,6 +1244,7 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   } else {
     __syncthreads();
   }
+  if (threadIdx.x == 64) stamp(7);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after_sync();
