@@ -89,8 +89,11 @@ def parse_args():
     ap.add_argument("--b-placement", choices=["sharded", "root"], default="sharded",
                     help="G > 1: B arrives sharded by rows (all-gathered inside each call) or whole on rank 0 "
                          "(broadcast inside each call)")
-    ap.add_argument("--transfer", choices=["ce", "nccl"], default="ce",
-                    help="G > 1 with B sharded: gather B's blocks by copy engines (IPC peer copies) or by NCCL")
+    ap.add_argument("--transfer", choices=["ce", "nccl"], default=None,
+                    help="G > 1 with B sharded: gather B's blocks by copy engines (IPC peer copies) or by NCCL "
+                         "(default: copy engines up to 4 GPUs, NCCL above: U B 8192 at 8 GPUs measured 1.03 ms "
+                         "per call with NCCL against 1.11 with copy engines, whose pushes add up to ~320 GB/s "
+                         "per rank there)")
     ap.add_argument("--roofline-s", type=float, default=1.0,
                     help="seconds of repeated calls over which the roofline kernel is timed")
     a = ap.parse_args()
@@ -98,6 +101,8 @@ def parse_args():
         a.steps = {"diag": 400, "gemm": 20, "upper": 30, "sandwich": 30, "toeplitz": 6, "add": 300}[a.op]
     if a.warmup is None:
         a.warmup = {"diag": 20, "gemm": 3, "upper": 3, "sandwich": 3, "toeplitz": 3, "add": 20}[a.op]
+    if a.transfer is None:
+        a.transfer = "ce" if int(os.environ.get("WORLD_SIZE", "1")) <= 4 else "nccl"
     return a
 
 
@@ -557,7 +562,7 @@ def run_ours(args, rank, world, local):
                  "b_transfer_gbs": round(b_bytes / (ms_b * 1e-3) / 1e9, 1),
                  "b_bytes_per_step": int(b_bytes),
                  "nvlink_in_bytes_per_rank": int(link_in),
-                 "column_blocks": MG.lib_chunks(n, world),
+                 "column_blocks": MG.lib_chunks(n, world, comm.copy_engines_enabled() and root == MG.SHARDED),
                  "transfer": "copy engines" if comm.copy_engines_enabled() else "nccl",
                  "overlap": f"B {how} in column blocks inside each call (libsmm smm_mg_*); each block's columns of "
                             "the slab are computed as soon as it lands, on internal compute streams",

@@ -128,6 +128,7 @@ SIGNATURES = [
     ("smm_mg_comm_status", _i, [_vp]),
     ("smm_mg_row_slabs", _i, [_i, _i, _i, _vp]),
     ("smm_mg_chunks", _i, [_i, _i, _vp]),
+    ("smm_mg_gather_chunks", _i, [_i, _i, _vp]),
     ("smm_mg_share_rows", _i, [_i, _i]),
     ("smm_mg_plane_bytes", _sz, [_vp, _i, _i, _i]),
     ("smm_mg_enable_copy_engines", _i, [_vp, _sz]),

@@ -43,12 +43,20 @@ struct Operand {
 Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf = nullptr);
 Operand structured_op(const float* src, int dim, int row0 = 0);
 
+// Tile choice of one contraction.  Auto sizes the tiles for a launch that
+// has the GPU to itself (about a wave of CTAs: narrower tiles, or K split
+// over a cluster, when the product is small).  WidePairs always takes 256 x
+// 256 CTA-pair tiles (the fastest per flop) when M > 128: for launches that
+// share the GPU with other launches of the same call, such as the column
+// blocks of a multi-GPU product running side by side.
+enum class TilePolicy { Auto, WidePairs };
+
 // C(M x N, ldc) = Aop(M x K) * B(K x N) on stream st.  Optionally also
 // writes lo(C) (C_lo, same ldc) or bf16(C) (C_bf16, ldc_bf16) from the
 // epilogue, so that C can feed a following product.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
                     int N, int K, cudaStream_t st, float* C_lo = nullptr, __nv_bfloat16* C_bf16 = nullptr,
-                    int ldc_bf16 = 0);
+                    int ldc_bf16 = 0, TilePolicy policy = TilePolicy::Auto);
 
 // ---------------------------------------------------------------- staging
 // A TMA-fed operand (rows x cols row-major): the caller's array or a padded

@@ -14,23 +14,54 @@
 // synchronously): the drop-in for callers of the reference's CPU kernels,
 // which take host arrays.  The left operand(s) cross PCIe once and are
 // prepared on the device (staged, or a packed operand expanded) on a stream
-// of their own; B streams through in column chunks.  Chunk j alternates
-// between two streams: its 2-D copy-in (which does not wait for the left
-// operand, so B's first chunks cross PCIe while the left operand is being
-// expanded), its product (which does) and its 2-D copy-out into C's columns
-// are ordered on that stream, and they overlap the other stream's (PCIe is
-// full duplex: chunk j's copy-out runs beside chunk j+1's copy-in).
+// of their own; B streams through in column chunks, chunk j in buffer region
+// j % 2.  The region's chunk stream orders chunk j's 2-D copy-in (which does
+// not wait for the left operand, so B's first chunks cross PCIe while the
+// left operand is being expanded) and its product (which does); the 2-D
+// copy-out into C's columns runs on the region's copy-out stream once the
+// product is done.  So chunk j+2's copy-in waits only for chunk j's product
+// (its B buffer), not for chunk j's copy-out: PCIe is full duplex, and the
+// host-to-device copies keep flowing while results drain.  Chunk j+2's
+// product waits for chunk j's copy-out (its C buffer).
 namespace smm {
 namespace {
 
 enum class HostLeft { Gemm, Upper, Symm, Toeplitz, Sandwich };
 
 struct HostStreams {
-  cudaStream_t st[2] = {nullptr, nullptr};  // B chunks, alternating
+  cudaStream_t st[2] = {nullptr, nullptr};  // chunks of region k: copy-in, product
+  cudaStream_t so[2] = {nullptr, nullptr};  // chunks of region k: copy-out
   cudaStream_t sl = nullptr;                // the left operand(s): copy in and prepare
   cudaEvent_t left_ready = nullptr;
+  cudaEvent_t prod_done[2] = {nullptr, nullptr};  // region k's latest product
+  cudaEvent_t out_done[2] = {nullptr, nullptr};   // region k's latest copy-out
   bool init = false;
 };
+
+// After chunk product(s) on st: the copy-out on the region's copy-out stream,
+// then record its completion (the region's next product waits for it).
+int chunk_copy_out(HostStreams* hs, int k, void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                   size_t height) {
+  SMM_CUDA_TRY(cudaEventRecord(hs->prod_done[k], hs->st[k]), "event record");
+  SMM_CUDA_TRY(cudaStreamWaitEvent(hs->so[k], hs->prod_done[k], 0), "wait for the chunk product");
+  if (height == 1)
+    SMM_CUDA_TRY(cudaMemcpyAsync(dst, src, width, cudaMemcpyDeviceToHost, hs->so[k]), "copy C chunk");
+  else
+    SMM_CUDA_TRY(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDeviceToHost, hs->so[k]),
+                 "copy C chunk");
+  SMM_CUDA_TRY(cudaEventRecord(hs->out_done[k], hs->so[k]), "event record");
+  return SMM_OK;
+}
+
+// The caller's view at the end of a host-buffer product: every stream drained.
+int drain_host_streams(HostStreams* hs) {
+  for (int k = 0; k < 2; ++k) {
+    SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[k]), "stream sync");
+    SMM_CUDA_TRY(cudaStreamSynchronize(hs->so[k]), "stream sync");
+  }
+  SMM_CUDA_TRY(cudaStreamSynchronize(hs->sl), "stream sync");
+  return SMM_OK;
+}
 
 int host_streams(HostStreams** out) {
   static HostStreams per_dev[64];
@@ -44,8 +75,13 @@ int host_streams(HostStreams** out) {
   std::lock_guard<std::mutex> lock(init_mu);
   if (!h.init) {
     for (auto& s : h.st) SMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
+    for (auto& s : h.so) SMM_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
     SMM_CUDA_TRY(cudaStreamCreateWithFlags(&h.sl, cudaStreamNonBlocking), "stream create");
     SMM_CUDA_TRY(cudaEventCreateWithFlags(&h.left_ready, cudaEventDisableTiming), "event create");
+    for (int k = 0; k < 2; ++k) {
+      SMM_CUDA_TRY(cudaEventCreateWithFlags(&h.prod_done[k], cudaEventDisableTiming), "event create");
+      SMM_CUDA_TRY(cudaEventCreateWithFlags(&h.out_done[k], cudaEventDisableTiming), "event create");
+    }
     h.init = true;
   }
   *out = &h;
@@ -175,6 +211,7 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
     if (int rc = stage_operand(braw, K, wc, mode, stage_cur, &bs, st)) return rc;
     const Operand bop = dense_op(bs.ptr, bs.lo, bs.ld, bs.bf16);
     if (c < 2) SMM_CUDA_TRY(cudaStreamWaitEvent(st, hs->left_ready, 0), "wait for the left operand");
+    if (c >= 2) SMM_CUDA_TRY(cudaStreamWaitEvent(st, hs->out_done[k], 0), "wait for the C buffer");
     if (h.kind == HostLeft::Sandwich) {
       // X_j = S B_j (its bf16 copy too in bf16 mode), then C_j = A X_j
       const int ldx = round4(wc), ldx_bf = round8(wc);
@@ -191,12 +228,11 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
     } else {
       if (int rc = run_contraction(lk, BKind::Dense, mode, left, bop, cch, wc, M, wc, K, st)) return rc;
     }
-    SMM_CUDA_TRY(cudaMemcpy2DAsync(C + c0, static_cast<size_t>(N) * 4, cch, static_cast<size_t>(wc) * 4,
-                                   static_cast<size_t>(wc) * 4, M, cudaMemcpyDeviceToHost, st),
-                 "copy C chunk");
+    if (int rc = chunk_copy_out(hs, k, C + c0, static_cast<size_t>(N) * 4, cch, static_cast<size_t>(wc) * 4,
+                                static_cast<size_t>(wc) * 4, M))
+      return rc;
   }
-  // the caller's view: both chunk streams and the left stream drained
-  for (int k = 0; k < 2; ++k) SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[k]), "stream sync");
+  if (int rc = drain_host_streams(hs)) return rc;
   return smm_device_status(s0);
 }
 
@@ -205,10 +241,10 @@ int host_product(const char* who, const HostShape& h, const float* L1, const flo
 // symmetric, K = N; or a K + N - 1 Toeplitz generator): the orientation of
 // the reference's CPU kernels (upper_triag_matmul.cpp:41-137 A*U,
 // symmetric_matmul.cpp:84-211 A*S, toeplitz_matmul2.cpp:44-144 A*T).  X
-// crosses PCIe once and is expanded into a dense copy on stream 0; A goes
-// through in row chunks (contiguous in host memory) alternating between the
-// two streams, each chunk's copy-in, product and copy-out ordered on its
-// stream and overlapping the other stream's.
+// crosses PCIe once and is expanded into a dense copy on its own stream; A
+// goes through in row chunks (contiguous in host memory) alternating between
+// the two buffer regions, with the same streams and ordering as the column
+// chunks of B above.
 enum class HostRight { Upper, Symm, Toeplitz };
 
 int host_row_chunk(int M) { return std::min(M, std::max(1024, (M / 8 + 255) / 256 * 256)); }
@@ -286,15 +322,15 @@ int host_right_product(const char* who, HostRight kind, int M, int N, int K, int
     Staged as;
     if (int rc = stage_operand(araw, rows, K, mode, stage_cur, &as, st)) return rc;
     if (c < 2) SMM_CUDA_TRY(cudaStreamWaitEvent(st, hs->left_ready, 0), "wait for the structured operand");
+    if (c >= 2) SMM_CUDA_TRY(cudaStreamWaitEvent(st, hs->out_done[k], 0), "wait for the C buffer");
     if (int rc = run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(as.ptr, as.lo, as.ld, as.bf16), xop, cch,
                                  N, rows, N, K, st))
       return rc;
-    SMM_CUDA_TRY(cudaMemcpyAsync(C + static_cast<size_t>(r0) * N, cch, static_cast<size_t>(rows) * N * 4,
-                                 cudaMemcpyDeviceToHost, st),
-                 "copy C chunk");
+    // rows of C are contiguous: one copy of rows * N floats
+    const size_t bytes = static_cast<size_t>(rows) * N * 4;
+    if (int rc = chunk_copy_out(hs, k, C + static_cast<size_t>(r0) * N, bytes, cch, bytes, bytes, 1)) return rc;
   }
-  // the caller's view: both chunk streams and the left stream drained
-  for (int k = 0; k < 2; ++k) SMM_CUDA_TRY(cudaStreamSynchronize(hs->st[k]), "stream sync");
+  if (int rc = drain_host_streams(hs)) return rc;
   return smm_device_status(s0);
 }
 

@@ -189,11 +189,13 @@ int check_packed(const char* who, int N) {
 // Core contraction: C(M x N, ldc) = Aop(M x K) * B(K x N, ldb).
 // Preconditions: B (and A when dense) 16-byte aligned with ld % 4 == 0.
 int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operand& b, float* C, int ldc, int M,
-                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16) {
+                    int N, int K, cudaStream_t st, float* C_lo, __nv_bfloat16* C_bf16, int ldc_bf16,
+                    TilePolicy policy) {
   const bool bf16 = (mode == SMM_MODE_BF16);
-  const bool pair = use_pairs(M, N);
-  const bool split = use_split(ak, bk, a, b, pair, M, N, K);
-  const int bn = split ? 128 : pick_bn(M, N, pair);
+  const bool wide = policy == TilePolicy::WidePairs && M > kBM && N > 128;
+  const bool pair = wide || use_pairs(M, N);
+  const bool split = !wide && use_split(ak, bk, a, b, pair, M, N, K);
+  const int bn = wide ? 256 : split ? 128 : pick_bn(M, N, pair);
   Maps m;
   const bool a_tma = (ak == AKind::Dense || ak == AKind::UpperDense);
   const bool b_tma = (bk == BKind::Dense);

@@ -451,6 +451,16 @@ int pack_block(const BSide& b, const float* src, int rows, int pad_rows, int j, 
   return SMM_OK;
 }
 
+// Streams the copy-engine pushes of one rank go out on (SMM_MG_CE_LANES, 1 ..
+// world - 1; default 1): see start_bside.
+int ce_lanes(int world) {
+  static const int v = [] {
+    const char* e = std::getenv("SMM_MG_CE_LANES");
+    return e ? std::atoi(e) : 1;
+  }();
+  return std::max(1, std::min(v, world - 1));
+}
+
 // Starts the B side of one call on the collective stream (ordered after the
 // caller's stream): ev_chunk[j] marks block j's arrival.  The blocks this
 // rank sends are packed on the pack stream, block j+1's pack overlapping
@@ -482,20 +492,31 @@ int start_bside(smm_mg_comm* c, const BSide& b, const float* B, cudaStream_t st,
       SMM_CUDA_TRY(cudaEventRecord(c->ev_packed[j], c->ps), "record block packed");
     }
     const size_t slot_bytes_base = static_cast<size_t>(b.share) * b.esz();
+    // Pushes in ring order: for each block, to ranks rank+1, rank+2, ... in
+    // turn, on `lanes` streams (the copy streams of the first `lanes` of those
+    // destinations), so that in step s every rank sends to rank+s and
+    // receives from rank-s: one outgoing and one incoming copy per rank at a
+    // time with one lane.  One stream per destination (all peers at once)
+    // measured slower at 4 and 8 GPUs than at 2: a rank's pushes added up to
+    // 512 GB/s with one peer, 371 with three, 314 with seven.
+    const int lanes = ce_lanes(c->world);
+    auto lane_of = [&](int step) { return e->xs[(c->rank + 1 + (step - 1) % lanes) % c->world]; };
     for (int d = 0; d < c->world; ++d) {
       if (d == c->rank) continue;
       // rank d's previous call has finished reading the planes we overwrite
-      SMM_CUDA_TRY(cudaStreamWaitEvent(e->xs[d], e->done_in[d], 0), "wait for the peer's readers");
+      const int step = (d - c->rank + c->world) % c->world;
+      SMM_CUDA_TRY(cudaStreamWaitEvent(lane_of(step), e->done_in[d], 0), "wait for the peer's readers");
     }
     for (int j = 0; j < b.nch; ++j) {
       const size_t off = static_cast<size_t>(b.own_slot(j) - b.planes);
       const size_t bytes = slot_bytes_base * b.ld(j);
-      for (int d = 0; d < c->world; ++d) {
-        if (d == c->rank) continue;
-        SMM_CUDA_TRY(cudaStreamWaitEvent(e->xs[d], c->ev_packed[j], 0), "wait for the block's pack");
-        SMM_CUDA_TRY(cudaMemcpyAsync(e->peer[d] + off, b.own_slot(j), bytes, cudaMemcpyDeviceToDevice, e->xs[d]),
+      for (int step = 1; step < c->world; ++step) {
+        const int d = (c->rank + step) % c->world;
+        cudaStream_t xs = lane_of(step);
+        SMM_CUDA_TRY(cudaStreamWaitEvent(xs, c->ev_packed[j], 0), "wait for the block's pack");
+        SMM_CUDA_TRY(cudaMemcpyAsync(e->peer[d] + off, b.own_slot(j), bytes, cudaMemcpyDeviceToDevice, xs),
                      "copy-engine push of a share");
-        SMM_CUDA_TRY(cudaEventRecord(e->sent[d][j], e->xs[d]), "record block sent");
+        SMM_CUDA_TRY(cudaEventRecord(e->sent[d][j], xs), "record block sent");
       }
     }
     // Barrier B: every rank has recorded this call's 'sent' events.
@@ -572,6 +593,21 @@ int run_blocks(smm_mg_comm* c, const BSide& b, cudaStream_t st, F&& block) {
   SMM_CUDA_TRY(cudaEventRecord(c->ev_cs_done, c->cs), "record collectives done");
   SMM_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_cs_done, 0), "join the collectives");
   return SMM_OK;
+}
+
+// Tiles of the column-block products.  With more than one rank the blocks'
+// products run side by side on the compute streams, so each takes 256 x 256
+// pair tiles (the fastest per flop) instead of the narrower or K-split tiles
+// a launch that had the GPU to itself would take: at 8 GPUs the first slab
+// of U B 8192 (512 rows, K ~ 8000) ran as 512 single-CTA split tiles, about
+// four waves, against one wave of 64 pair tiles.  SMM_MG_TILES=auto restores
+// the single-launch choice.
+TilePolicy block_tiles(const smm_mg_comm* c) {
+  static const bool forced_auto = [] {
+    const char* e = std::getenv("SMM_MG_TILES");
+    return e && std::strcmp(e, "auto") == 0;
+  }();
+  return (c->world > 1 && !forced_auto) ? TilePolicy::WidePairs : TilePolicy::Auto;
 }
 
 // The B operand of column block j (K x W_j): the caller's B in place, or the
@@ -872,6 +908,11 @@ extern "C" int smm_mg_chunks(int ncols, int world, int* bounds) {
   return chunk_bounds(ncols, world, bounds);
 }
 
+extern "C" int smm_mg_gather_chunks(int ncols, int world, int* bounds) {
+  if (ncols < 0 || world < 1 || !bounds) return set_error(SMM_ERR_INVALID, "smm_mg_gather_chunks: bad arguments");
+  return chunk_bounds(ncols, world, bounds, true);
+}
+
 namespace {
 // Validation shared by the products: B (K x ncols) is the root's whole B,
 // or with root SMM_MG_SHARDED this rank's share (rows [rank * s, rank * s +
@@ -918,7 +959,8 @@ extern "C" int smm_mg_gemm(smm_mg_comm* c, const float* A_slab, const float* B, 
   return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
     if (nrows == 0) return SMM_OK;
     return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(a.ptr, nullptr, a.ld, a.bf16),
-                           block_operand(b, B, j), C_slab + b.cb[j], N, nrows, b.width(j), K, w);
+                           block_operand(b, B, j), C_slab + b.cb[j], N, nrows, b.width(j), K, w, nullptr, nullptr, 0,
+                           block_tiles(c));
   });
 }
 
@@ -952,7 +994,7 @@ extern "C" int smm_mg_upper_left(smm_mg_comm* c, const float* U_packed, const fl
     ao.dim = N;
     ao.row0 = row0;
     return run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, block_operand(b, B, j), C_slab + b.cb[j],
-                           ncols, nrows, b.width(j), N, w);
+                           ncols, nrows, b.width(j), N, w, nullptr, nullptr, 0, block_tiles(c));
   });
 }
 
@@ -978,7 +1020,7 @@ extern "C" int smm_mg_toeplitz_left(smm_mg_comm* c, const float* g, const float*
   return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
     if (nrows == 0) return SMM_OK;
     return run_contraction(AKind::Toeplitz, BKind::Dense, mode, structured_op(g, N, row0), block_operand(b, B, j),
-                           C_slab + b.cb[j], ncols, nrows, b.width(j), N, w);
+                           C_slab + b.cb[j], ncols, nrows, b.width(j), N, w, nullptr, nullptr, 0, block_tiles(c));
   });
 }
 
@@ -1044,6 +1086,6 @@ extern "C" int smm_mg_symm_sandwich(smm_mg_comm* c, const float* A_slab, float* 
   return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
     if (nrows == 0) return SMM_OK;
     return run_contraction(AKind::Dense, BKind::Dense, mode, dense_op(Y, nullptr, ldy, Y_bf), block_operand(b, B, j),
-                           C_slab + b.cb[j], N, nrows, b.width(j), N, w);
+                           C_slab + b.cb[j], N, nrows, b.width(j), N, w, nullptr, nullptr, 0, block_tiles(c));
   });
 }

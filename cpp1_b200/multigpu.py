@@ -360,13 +360,15 @@ def lib_row_slabs(n: int, world: int, triangular: bool = False) -> List[int]:
     return list(b)
 
 
-def lib_chunks(ncols: int, world: int) -> List[int]:
-    """The column-block boundaries the library's broadcasts of B use
-    (smm_mg_chunks)."""
+def lib_chunks(ncols: int, world: int, copy_engines: bool = False) -> List[int]:
+    """The column-block boundaries the library's transfers of B use: NCCL
+    broadcasts and all-gathers (smm_mg_chunks), or the copy-engine gather
+    (smm_mg_gather_chunks)."""
     import ctypes
     from . import _lib
     b = (ctypes.c_int * 17)()
-    nch = _lib.load().smm_mg_chunks(ncols, world, b)
+    fn = "smm_mg_gather_chunks" if copy_engines else "smm_mg_chunks"
+    nch = getattr(_lib.load(), fn)(ncols, world, b)
     if nch < 1:
-        _lib.check(nch if nch else 1, "smm_mg_chunks")
+        _lib.check(nch if nch else 1, fn)
     return list(b)[: nch + 1]

@@ -235,6 +235,11 @@ int smm_mg_row_slabs(int N, int world, int triangular, int* bounds);
  * world 1, 4 at world 2, 2 at 3-4, 1 from 5 up (SMM_MG_CHUNKS in the
  * environment sets it, 1 .. 16). */
 int smm_mg_chunks(int ncols, int world, int* bounds);
+/* The same for a copy-engine gather of a sharded B (smm_mg_enable_copy_engines),
+ * whose pushes take no SM: 4 blocks at every world size above 1
+ * (SMM_MG_CHUNKS sets it, 1 .. 16).  No counterpart in the reference (it has
+ * no multi-GPU code). */
+int smm_mg_gather_chunks(int ncols, int world, int* bounds);
 
 /* Copy-engine gather of a sharded B (collective; at most 8 ranks on one
  * node).  Every rank allocates plane_bytes of device memory (the same count
