@@ -162,6 +162,18 @@ def test_library_column_blocks(ncols, world):
     assert len(cb) - 1 == min(want, -(-ncols // 256))
 
 
+@pytest.mark.parametrize("ncols,world", [(8192, 8), (16384, 8), (4096, 2), (1000, 4), (300, 4), (8192, 1)])
+def test_library_gather_column_blocks(ncols, world):
+    """The copy-engine gather's blocks (smm_mg_gather_chunks): the same
+    256-column tiling, 4 blocks at every world size above 1."""
+    cb = MG.lib_chunks(ncols, world, copy_engines=True)
+    assert cb[0] == 0 and cb[-1] == ncols
+    assert all(a < b for a, b in zip(cb, cb[1:]))
+    assert all(x % 256 == 0 for x in cb[:-1])
+    want = 1 if world == 1 else 4
+    assert len(cb) - 1 == min(want, -(-ncols // 256))
+
+
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_library_share_rows(world):
     """smm_mg_share_rows agrees with the host rule (ceil(K / world)), and the
