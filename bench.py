@@ -91,9 +91,7 @@ def parse_args():
                          "(broadcast inside each call)")
     ap.add_argument("--transfer", choices=["ce", "nccl"], default=None,
                     help="G > 1 with B sharded: gather B's blocks by copy engines (IPC peer copies) or by NCCL "
-                         "(default: copy engines up to 4 GPUs, NCCL above: U B 8192 at 8 GPUs measured 1.03 ms "
-                         "per call with NCCL against 1.11 with copy engines, whose pushes add up to ~320 GB/s "
-                         "per rank there)")
+                         "(default: see default_transfer)")
     ap.add_argument("--roofline-s", type=float, default=1.0,
                     help="seconds of repeated calls over which the roofline kernel is timed")
     a = ap.parse_args()
@@ -102,8 +100,36 @@ def parse_args():
     if a.warmup is None:
         a.warmup = {"diag": 20, "gemm": 3, "upper": 3, "sandwich": 3, "toeplitz": 3, "add": 20}[a.op]
     if a.transfer is None:
-        a.transfer = "ce" if int(os.environ.get("WORLD_SIZE", "1")) <= 4 else "nccl"
+        n = a.n or WORKLOADS[a.op]["N"]
+        a.transfer = default_transfer(a.op, n, a.mode, int(os.environ.get("WORLD_SIZE", "1")))
     return a
+
+
+def default_transfer(op: str, n: int, mode: str, world: int) -> str:
+    """How a sharded B is gathered by default.  The copy engines use no SM, so
+    their transfer overlaps the contractions fully, but from 5 GPUs their
+    pushes add up to only ~320 GB/s per rank (512 with one peer); NCCL's
+    all-gather moves ~560 GB/s per rank there but competes with the
+    contractions for SMs, so it runs as one block before them.  Measured at
+    8 GPUs: U B 8192 (MMA time per rank ~ NVLink time) 1.03 ms per call with
+    NCCL against 1.11 with copy engines; T B 16384 (MMA time 3x the NVLink
+    time) hides the copy-engine gather (5.53 ms, compute alone 4.53).  So:
+    copy engines up to 4 GPUs, and above that when the heaviest rank's MMA
+    time at the TF32 (bf16) peak is at least twice the time its share of B
+    takes at 770 GB/s; NCCL otherwise."""
+    if world <= 4 or op in HBM_OPS:
+        return "ce"
+    from cpp1_b200.multigpu import row_slabs, slab_useful_flops
+    b = row_slabs(n, world, triangular=(op == "upper"))
+    kind = "gemm" if op in ("sandwich", "toeplitz") else op
+    heaviest = max(slab_useful_flops(kind, n, b[g], b[g + 1]) for g in range(world))
+    if op == "sandwich":
+        heaviest *= 2  # (A_slab S) B: two products per slab
+    passes = 3 if mode == "3xtf32" else 1
+    peak = measured_peaks()["bf16_tflops"] * 1e12 / (1 if mode == "bf16" else 2)
+    t_mma = passes * heaviest / peak
+    t_link = (2 if mode == "bf16" else 4) * n * n * (world - 1) / world / 770e9
+    return "ce" if t_mma >= 2 * t_link else "nccl"
 
 
 # ---------------------------------------------------------------- peaks

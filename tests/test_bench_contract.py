@@ -35,3 +35,17 @@ def test_reference_arm_prints_one_json_line():
     assert line["impl"] == "reference"
     if "unavailable" not in line:
         assert line["value"] > 0 and line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_default_transfer_follows_the_compute_to_link_balance():
+    """Copy engines up to 4 GPUs; above, copy engines only where the MMA time
+    hides their slower gather (T B 16384), NCCL where the transfer dominates
+    (U B and GEMM at 8192)."""
+    b = load_bench()
+    for op in ("upper", "gemm", "toeplitz", "sandwich"):
+        n = b.WORKLOADS[op]["N"]
+        assert [b.default_transfer(op, n, "3xtf32", w) for w in (1, 2, 4)] == ["ce"] * 3
+    assert b.default_transfer("toeplitz", 16384, "3xtf32", 8) == "ce"
+    assert b.default_transfer("upper", 8192, "3xtf32", 8) == "nccl"
+    assert b.default_transfer("gemm", 8192, "3xtf32", 8) == "nccl"
+    assert b.default_transfer("diag", 8192, "3xtf32", 8) == "ce"
