@@ -20,8 +20,9 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
   diag      weak scaling: every rank scales its own 8192 x 8192 row slab;
             no collective on the data path (the rows are independent).
   others    strong scaling: the output is split into row slabs (equal-work
-            boundaries for the triangular operand); each step is one libsmm
-            multi-GPU call (smm_mg_*).  By default B arrives sharded by rows
+            boundaries for the triangular operand; --partition tiles deals
+            U B's rows out as interleaved 256-row tiles instead); each step
+            is one libsmm multi-GPU call (smm_mg_*).  By default B arrives sharded by rows
             (--b-placement sharded) and is gathered in column blocks inside
             the call by the copy engines through CUDA IPC (--transfer ce; or
             by NCCL all-gathers, --transfer nccl); --b-placement root keeps
@@ -92,6 +93,9 @@ def parse_args():
     ap.add_argument("--transfer", choices=["ce", "nccl"], default=None,
                     help="G > 1 with B sharded: gather B's blocks by copy engines (IPC peer copies) or by NCCL "
                          "(default: see default_transfer)")
+    ap.add_argument("--partition", choices=["slabs", "tiles"], default="slabs",
+                    help="U B at G > 1: one contiguous equal-work slab per rank (smm_mg_row_slabs), or interleaved "
+                         "256-row tiles of U per rank (smm_mg_upper_row_tiles; measured 7%% slower at 2 GPUs)")
     ap.add_argument("--roofline-s", type=float, default=1.0,
                     help="seconds of repeated calls over which the roofline kernel is timed")
     a = ap.parse_args()
@@ -387,6 +391,12 @@ def run_ours(args, rank, world, local):
     bounds = None if op in HBM_OPS else MG.lib_row_slabs(n, world, triangular=(op == "upper"))
     r0, r1 = (bounds[rank], bounds[rank + 1]) if bounds else (0, n)
     nrows = r1 - r0
+    # U B on several GPUs: interleaved 256-row tiles of U per rank (the
+    # partition whose tile schedules come out even) instead of one slab.
+    tiles = (MG.lib_upper_row_tiles(n, world, rank)
+             if (op == "upper" and world > 1 and args.partition == "tiles") else None)
+    row_ids = MG.tile_rows_of(n, tiles) if tiles is not None else list(range(r0, r1))
+    nrows = len(row_ids)
     out = torch.empty((nrows, n), dtype=torch.float32, device="cuda")
     m = _lib.MODES[mode]
 
@@ -443,6 +453,16 @@ def run_ours(args, rank, world, local):
             def step():
                 comm.gemm(A_slab, B_arg, out, mode, root=root) if comm else slab_local()
             units_per_rank_call = 2 * nrows * n * n
+        elif op == "upper" and tiles is not None:
+            U, B = d_in
+
+            def slab_local():  # the same tiles with B whole on every rank: nothing travels
+                comm.upper_left_tiles(U, B_full, out, tiles, mode, root=MG.REPLICATED)
+
+            def step():
+                comm.upper_left_tiles(U, B_arg, out, tiles, mode, root=root)
+            units_per_rank_call = sum(slab_useful_flops("upper", n, t * MG.TILE_ROWS_MG,
+                                                        min(n, (t + 1) * MG.TILE_ROWS_MG)) for t in tiles)
         elif op == "upper":
             U, B = d_in
             ws, wsb = ws_for(L.smm_upper_left_workspace_size(n, n, _lib.FMT_PACKED, m))
@@ -497,7 +517,7 @@ def run_ours(args, rank, world, local):
     step()
     torch.cuda.synchronize()
     ops.device_status()
-    check = check_slab(op, w, r0, r1, out, mode)
+    check = check_slab(op, w, row_ids, out, mode)
     check["relerr"] = max_over_ranks(check["relerr"], world)
     if not check["relerr"] <= check["tol"]:
         raise RuntimeError(f"{op}: sampled rows differ from the oracle: relerr {check['relerr']:.3e} "
@@ -592,7 +612,8 @@ def run_ours(args, rank, world, local):
                  "transfer": "copy engines" if comm.copy_engines_enabled() else "nccl",
                  "overlap": f"B {how} in column blocks inside each call (libsmm smm_mg_*); each block's columns of "
                             "the slab are computed as soon as it lands, on internal compute streams",
-                 "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)],
+                 "slab_rows": [bounds[g + 1] - bounds[g] for g in range(world)] if tiles is None else None,
+                 "row_tiles_of_rank0": MG.lib_upper_row_tiles(n, world, 0) if tiles is not None else None,
                  "roofline": {"bound": "tensor" if t_mma >= t_link else "nvlink",
                               "t_mma_ms": round(t_mma, 4), "t_nvlink_ms": round(t_link, 4),
                               "target_ms": round(max(t_mma, t_link), 4),
@@ -618,7 +639,8 @@ def run_ours(args, rank, world, local):
                                              "bf16": "bf16 (fp32 accumulate)"}[mode],
         "data": "synthetic (seeded numpy PCG64, cpp1_b200.workloads)",
         "config": {"workload": WORKLOADS[op]["desc"], "op": op, "N": n, "mode": mode if op not in HBM_OPS else "f32",
-                   "parallelism": (f"row-slabs x{world}, B {args.b_placement}"
+                   "parallelism": (f"{'interleaved row tiles' if tiles is not None else 'row-slabs'} x{world}, "
+                                   f"B {args.b_placement}"
                                    + (f" ({'copy engines' if args.transfer == 'ce' else 'NCCL'})"
                                       if args.b_placement == "sharded" else " (NCCL)")
                                    if world > 1 and op not in HBM_OPS
@@ -635,17 +657,20 @@ def run_ours(args, rank, world, local):
     return res, d_in, h_in
 
 
-def check_slab(op, w, r0, r1, out, mode):
-    """Normwise relative error of sampled rows of this rank's slab [r0, r1)
-    of C against the oracle's fp64 rows (diag and add: bit-exact against the
-    oracle's fp32 result, reported as 0 or inf)."""
+def check_slab(op, w, row_ids, out, mode):
+    """Normwise relative error of sampled rows of this rank's output (global
+    rows row_ids, stacked in out) against the oracle's fp64 rows (diag and
+    add: bit-exact against the oracle's fp32 result, reported as 0 or inf).
+    The first and last rows are always among them."""
     import oracle as O
-    rng = np.random.default_rng(r0 + 7)
-    k = min(r1 - r0, 8)
-    if k <= 0:
+    nr = len(row_ids)
+    if nr == 0:
         return {"relerr": 0.0, "rows": 0, "tol": 0.0, "against": "no rows on this rank"}
-    rows = np.unique(np.concatenate([[r0, r1 - 1], rng.integers(r0, r1, size=max(k - 2, 0))])).astype(np.int32)
-    got = out[(rows - r0).tolist()].cpu().numpy()
+    rng = np.random.default_rng(int(row_ids[0]) + 7)
+    k = min(nr, 8)
+    local = np.unique(np.concatenate([[0, nr - 1], rng.integers(0, nr, size=max(k - 2, 0))])).astype(np.int64)
+    rows = np.asarray(row_ids, dtype=np.int32)[local]
+    got = out[local.tolist()].cpu().numpy()
     if op == "diag":
         ref = w["d"][rows, None] * w["B"][rows]
         return {"relerr": 0.0 if np.array_equal(got, ref) else float("inf"), "rows": len(rows), "tol": 0.0,
@@ -854,6 +879,10 @@ def e2e_dist(args, h_in, n, rank, world):
     bounds = MG.lib_row_slabs(n, world, triangular=(op == "upper"))
     r0, r1 = bounds[rank], bounds[rank + 1]
     nrows = r1 - r0
+    tiles = (MG.lib_upper_row_tiles(n, world, rank)  # interleaved rows of U B
+             if (op == "upper" and args.partition == "tiles") else None)
+    if tiles is not None:
+        nrows = len(MG.tile_rows_of(n, tiles))
     per = MG.share_rows(n, world)
     s0, s1 = min(n, rank * per), min(n, (rank + 1) * per)
 
@@ -879,7 +908,7 @@ def e2e_dist(args, h_in, n, rank, world):
 
         def comp():
             comm.gemm(A, B_share, C[:nrows], mode, root=MG.SHARDED)
-    elif op == "upper":
+    elif op == "upper" and tiles is None:
         Up = h_in[0]
         lo, hi = r0 * n - r0 * (r0 - 1) // 2, r1 * n - r1 * (r1 - 1) // 2  # packed rows [r0, r1)
         hU = pin(Up[lo:hi])
@@ -891,6 +920,22 @@ def e2e_dist(args, h_in, n, rank, world):
 
         def comp():
             comm.upper_left(U, B_share, C[:nrows], r0, mode, root=MG.SHARDED)
+    elif op == "upper":
+        Up = h_in[0]
+        segs = []  # the packed rows of each of this rank's row tiles
+        for t in tiles:
+            a, e = t * MG.TILE_ROWS_MG, min(n, (t + 1) * MG.TILE_ROWS_MG)
+            lo, hi = a * n - a * (a - 1) // 2, e * n - e * (e - 1) // 2
+            segs.append((lo, hi, pin(Up[lo:hi])))
+        U = torch.zeros(Up.size, dtype=torch.float32, device=dev)
+        h2d += Up.nbytes
+
+        def load():
+            for lo, hi, hU in segs:
+                U[lo:hi].copy_(hU, non_blocking=True)
+
+        def comp():
+            comm.upper_left_tiles(U, B_share, C[:nrows], tiles, mode, root=MG.SHARDED)
     elif op == "toeplitz":
         hg = pin(h_in[0])
         g = torch.empty(h_in[0].size, dtype=torch.float32, device=dev)

@@ -137,6 +137,9 @@ SIGNATURES = [
     ("smm_mg_gemm", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_mg_upper_left_workspace_size", _sz, [_vp, _i, _i, _i, _i]),
     ("smm_mg_upper_left", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    ("smm_mg_upper_row_tiles", _i, [_i, _i, _i, _vp, _i, _vp]),
+    ("smm_mg_upper_left_tiles_workspace_size", _sz, [_vp, _i, _i, _i, _i]),
+    ("smm_mg_upper_left_tiles", _i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_mg_toeplitz_left_workspace_size", _sz, [_vp, _i, _i, _i]),
     ("smm_mg_toeplitz_left", _i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     ("smm_mg_symm_sandwich_workspace_size", _sz, [_vp, _i, _i, _i]),

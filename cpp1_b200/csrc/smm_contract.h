@@ -38,6 +38,11 @@ struct Operand {
   int row0 = 0;
   bool lower = false;  // dense A with exact zeros above the diagonal (K range clipped)
   int tri = 0;         // dense B: 1 upper / 2 lower triangular (K range clipped per column tile)
+  // Dense-with-zeros upper-triangular A stacked from row tiles of U (host
+  // array of ntiles first rows, tile_rows rows each; see UmmaParams).
+  int tile_rows = 0;
+  const int* tile_row0 = nullptr;
+  int ntiles = 0;
 };
 
 Operand dense_op(const float* ptr, const float* lo, int ld, const __nv_bfloat16* bf = nullptr);

@@ -226,6 +226,14 @@ int run_contraction(AKind ak, BKind bk, int mode, const Operand& a, const Operan
   p.a_src = a.src;
   p.a_dim = a.dim;
   p.a_row0 = a.row0;
+  if (a.tile_rows > 0) {
+    if (ak != AKind::UpperDense || a.ntiles < 1 || a.ntiles > kMaxMappedTiles || !a.tile_row0 ||
+        static_cast<long long>(a.ntiles) * a.tile_rows < M || a.tile_rows % (2 * kBM) != 0)
+      return set_error(SMM_ERR_INVALID, "internal: bad row-tile map (%d tiles of %d rows for %d rows)", a.ntiles,
+                       a.tile_rows, M);
+    p.a_tile_rows = a.tile_rows;
+    for (int i = 0; i < a.ntiles; ++i) p.a_tile_row0[i] = a.tile_row0[i];
+  }
   p.a_lower = a.lower ? 1 : 0;
   p.b_tri = b.tri;
   p.b_src = b.src;

@@ -337,15 +337,26 @@ struct BSide {
     for (int i = 0; i < j; ++i) p += plane_bytes_of(i, share);
     return p;
   }
-  bool travels() const { return world > 1; }
+  bool replicated = false;  // the whole B on every rank: nothing travels
+  bool travels() const { return world > 1 && !replicated; }
   // Whether block j's contraction reads the caller's B in place (no wait).
-  bool in_place() const { return !bf && (world == 1 || (!sharded && rank == root)); }
+  bool in_place() const { return !bf && (world == 1 || replicated || (!sharded && rank == root)); }
 };
 
 BSide make_bside(const smm_mg_comm* c, int K, int ncols, int mode, int root, void* ws) {
   BSide b;
   b.K = K;
   b.ncols = ncols;
+  if (root == SMM_MG_REPLICATED) {  // one block, B (or its bf16 copy) in place on every rank
+    b.replicated = true;
+    b.nch = chunk_bounds(ncols, 1, b.cb);
+    b.bf = mode == SMM_MODE_BF16;
+    b.world = c->world;
+    b.rank = c->rank;
+    b.rows = K;
+    b.planes = static_cast<uint8_t*>(ws);
+    return b;
+  }
   const bool try_ce = c->ce && root == SMM_MG_SHARDED && c->world > 1;
   b.nch = chunk_bounds(ncols, c->world, b.cb, try_ce);
   b.bf = mode == SMM_MODE_BF16;
@@ -426,6 +437,32 @@ size_t b_side_bytes(int world, int K, int ncols, int mode) {
   if (b.travels())
     for (int j = 0; j < b.nch; ++j) total += b.plane_bytes_of(j, b.share);
   return total;
+}
+
+// Interleaved row tiles of an upper-triangular U (kMgTileRows rows each, the
+// last one possibly shorter): tiles in decreasing order of work (row i costs
+// n - i) each go to the rank with the least work so far (ties: the lower
+// rank).  Every rank then holds long and short rows alike -- 32 tiles on 8
+// ranks: {r, 15 - r, 16 + r, 31 - r} -- so the ranks' pair-tile schedules,
+// and not only their work, come out even; contiguous equal-work slabs give
+// the ranks with few long rows a fraction of a wave of tiles in excess.
+// Writes this rank's tiles in ascending order; returns their count.
+constexpr int kMgTileRows = 256;
+int upper_row_tiles(int n, int world, int rank, int* tiles) {
+  const int nt = (n + kMgTileRows - 1) / kMgTileRows;
+  std::vector<long long> load(world, 0);
+  std::vector<int> mine;
+  for (int t = 0; t < nt; ++t) {  // tile t's work is larger than tile t+1's
+    const long long a = static_cast<long long>(t) * kMgTileRows, e = std::min<long long>(n, a + kMgTileRows);
+    const long long cost = (e - a) * n - (e * (e - 1) - a * (a - 1)) / 2;
+    int g = 0;
+    for (int h = 1; h < world; ++h)
+      if (load[h] < load[g]) g = h;
+    load[g] += cost;
+    if (g == rank) mine.push_back(t);
+  }
+  for (size_t i = 0; i < mine.size(); ++i) tiles[i] = mine[i];
+  return static_cast<int>(mine.size());
 }
 
 // Copies rows [0, rows) of column block j of src (leading dimension ncols)
@@ -558,7 +595,7 @@ int start_bside(smm_mg_comm* c, const BSide& b, const float* B, cudaStream_t st,
 // waits for all of them.
 template <typename F>
 int run_blocks(smm_mg_comm* c, const BSide& b, cudaStream_t st, F&& block) {
-  if (c->world == 1) return block(0, st);
+  if (!b.travels()) return block(0, st);
   SMM_CUDA_TRY(cudaEventRecord(c->ev_prep, st), "record operand preparation");
   const int used = std::min(b.nch, kWork);
   for (int w = 0; w < used; ++w) SMM_CUDA_TRY(cudaStreamWaitEvent(c->work[w], c->ev_prep, 0), "fork");
@@ -897,6 +934,18 @@ extern "C" int smm_mg_enable_copy_engines(smm_mg_comm* c, size_t plane_bytes) {
 
 extern "C" int smm_mg_copy_engines_enabled(const smm_mg_comm* c) { return c && c->ce ? 1 : 0; }
 
+extern "C" int smm_mg_upper_row_tiles(int N, int world, int rank, int* tiles, int max_tiles, int* count) {
+  if (N < 0 || world < 1 || rank < 0 || rank >= world || max_tiles < 0 || (!tiles && max_tiles > 0) || !count)
+    return set_error(SMM_ERR_INVALID, "smm_mg_upper_row_tiles: bad arguments");
+  const int nt = (N + kMgTileRows - 1) / kMgTileRows;
+  std::vector<int> all(static_cast<size_t>(nt) + 1);
+  const int k = upper_row_tiles(N, world, rank, all.data());
+  if (k > max_tiles) return set_error(SMM_ERR_INVALID, "smm_mg_upper_row_tiles: %d tiles, room for %d", k, max_tiles);
+  for (int i = 0; i < k; ++i) tiles[i] = all[i];
+  *count = k;
+  return SMM_OK;
+}
+
 extern "C" int smm_mg_row_slabs(int N, int world, int triangular, int* bounds) {
   if (N < 0 || world < 1 || !bounds) return set_error(SMM_ERR_INVALID, "smm_mg_row_slabs: bad arguments");
   row_slabs(N, world, triangular != 0, bounds);
@@ -920,10 +969,12 @@ namespace {
 // rows when it holds any.
 int check_call(const smm_mg_comm* c, const char* who, int mode, int root, const float* B, int K, int ncols) {
   if (int rc = check_comm(c, who)) return rc;
-  if (root != SMM_MG_SHARDED && (root < 0 || root >= c->world))
+  if (root != SMM_MG_SHARDED && root != SMM_MG_REPLICATED && (root < 0 || root >= c->world))
     return set_error(SMM_ERR_INVALID, "%s: root %d of %d", who, root, c->world);
   if (!valid_mode(mode)) return set_error(SMM_ERR_INVALID, "%s: unknown mode %d", who, mode);
-  const bool holds = root == SMM_MG_SHARDED ? (K - c->rank * share_rows(K, c->world) > 0) : c->rank == root;
+  const bool holds = root == SMM_MG_SHARDED      ? (K - c->rank * share_rows(K, c->world) > 0)
+                     : root == SMM_MG_REPLICATED ? true
+                                                 : c->rank == root;
   if (holds && K > 0 && ncols > 0 && (!B || !aligned_rows(B, ncols)))
     return set_error(SMM_ERR_INVALID, "%s: this rank's B must be non-null with 16-byte aligned rows", who);
   return SMM_OK;
@@ -995,6 +1046,65 @@ extern "C" int smm_mg_upper_left(smm_mg_comm* c, const float* U_packed, const fl
     ao.row0 = row0;
     return run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, block_operand(b, B, j), C_slab + b.cb[j],
                            ncols, nrows, b.width(j), N, w, nullptr, nullptr, 0, block_tiles(c));
+  });
+}
+
+extern "C" size_t smm_mg_upper_left_tiles_workspace_size(const smm_mg_comm* c, int N, int ncols, int ntiles,
+                                                        int mode) {
+  if (!c || N <= 0 || ncols <= 0 || ntiles < 0) return 0;
+  return b_side_bytes(c->world, N, ncols, mode) +
+         (ntiles ? expanded_bytes(std::min(N, ntiles * kMgTileRows), N, mode) : 0);
+}
+
+extern "C" int smm_mg_upper_left_tiles(smm_mg_comm* c, const float* U_packed, const float* B, float* C_rows, int N,
+                                       int ncols, const int* tiles, int ntiles, int mode, int root, void* ws,
+                                       size_t ws_bytes, void* stream) {
+  SMM_RANGE("smm_mg_upper_left_tiles");
+  if (int rc = check_call(c, "smm_mg_upper_left_tiles", mode, root, B, N, ncols)) return rc;
+  if (N < 0 || ncols < 0 || ntiles < 0 || ntiles > kMaxMappedTiles)
+    return set_error(SMM_ERR_INVALID, "smm_mg_upper_left_tiles: bad shape or tile count %d (at most %d)", ntiles,
+                     kMaxMappedTiles);
+  if (int rc = check_packed("smm_mg_upper_left_tiles", N)) return rc;
+  const int nt = (N + kMgTileRows - 1) / kMgTileRows;
+  int rows = 0;
+  int row0[kMaxMappedTiles];
+  for (int i = 0; i < ntiles; ++i) {
+    if (!tiles || tiles[i] < 0 || tiles[i] >= nt || (i > 0 && tiles[i] <= tiles[i - 1]))
+      return set_error(SMM_ERR_INVALID, "smm_mg_upper_left_tiles: tiles must be ascending row tiles of U (0 .. %d)",
+                       nt - 1);
+    row0[i] = tiles[i] * kMgTileRows;
+    rows += std::min(kMgTileRows, N - row0[i]);
+  }
+  if (N == 0 || ncols == 0) return SMM_OK;
+  if (rows > 0 && (!U_packed || !C_rows)) return set_error(SMM_ERR_INVALID, "smm_mg_upper_left_tiles: null pointer");
+  if (int rc = check_ws("smm_mg_upper_left_tiles", ws, ws_bytes,
+                        smm_mg_upper_left_tiles_workspace_size(c, N, ncols, ntiles, mode)))
+    return rc;
+  cudaStream_t st = as_stream(stream);
+  const BSide b = make_bside(c, N, ncols, mode, root, ws);
+  uint8_t* cur = static_cast<uint8_t*>(ws) + b_side_bytes(c->world, N, ncols, mode);
+  if (int rc = start_bside(c, b, B, st)) return rc;
+  // The tiles' rows of U, dense (zeros left of the diagonal), stacked in
+  // order: every tile but the last is kMgTileRows rows, whose expansions are
+  // whole 256-byte multiples, so the copies are contiguous with one leading
+  // dimension.
+  Staged u{};
+  for (int i = 0; i < ntiles; ++i) {
+    Staged ti;
+    if (int rc = expand_operand(U_packed, SMM_STRUCT_UPPER, N, row0[i], std::min(kMgTileRows, N - row0[i]), mode,
+                                cur, &ti, st))
+      return rc;
+    if (i == 0) u = ti;
+  }
+  return run_blocks(c, b, st, [&](int j, cudaStream_t w) -> int {
+    if (rows == 0) return SMM_OK;
+    Operand ao = dense_op(u.ptr, nullptr, u.ld, u.bf16);
+    ao.dim = N;
+    ao.tile_rows = kMgTileRows;
+    ao.tile_row0 = row0;
+    ao.ntiles = ntiles;
+    return run_contraction(AKind::UpperDense, BKind::Dense, mode, ao, block_operand(b, B, j), C_rows + b.cb[j],
+                           ncols, rows, b.width(j), N, w, nullptr, nullptr, 0, block_tiles(c));
   });
 }
 

@@ -111,6 +111,8 @@ constexpr int kStgBytes = 1024;
 // when the kernel has them.
 __host__ __device__ constexpr int umma_threads(AKind ak, Mode md) { return a_async_filled(ak, md) ? 384 : 320; }
 
+constexpr int kMaxMappedTiles = 64;  // row tiles of a mapped upper-triangular A (UmmaParams::a_tile_row0)
+
 struct UmmaParams {
   int M, N, K;             // C is M x N; reduction length K
   float* C;                // row-major, leading dimension ldc
@@ -133,7 +135,20 @@ struct UmmaParams {
   unsigned long long wait_limit_ns;   // pipeline waits
   unsigned long long drain_limit_ns;  // teardown waits for copies / MMAs already issued (>= wait_limit_ns)
   uint32_t* trace;         // optional diagnostic record of CTA 0; null in normal use
+  // Row-tile map of a dense-with-zeros upper-triangular A whose rows are a
+  // stack of a_tile_rows-row tiles of U taken from anywhere in U: output row
+  // tile i (of a_tile_rows rows) holds U's rows from a_tile_row0[i] on, so
+  // its K range starts there.  a_tile_rows = 0: the rows are contiguous from
+  // a_row0.
+  int a_tile_rows;
+  int a_tile_row0[kMaxMappedTiles];
 };
+
+// U's row behind output row r0 (a row-tile map, or contiguous from a_row0).
+__device__ __forceinline__ int a_struct_row(const UmmaParams& p, int r0) {
+  if (p.a_tile_rows > 0) return p.a_tile_row0[r0 / p.a_tile_rows] + r0 % p.a_tile_rows;
+  return p.a_row0 + r0;
+}
 
 // Slots of the diagnostic record (UmmaParams::trace, 64 words).
 enum : int {
@@ -683,7 +698,8 @@ __global__ void __launch_bounds__(umma_threads(AK, MD), 1)
   // Rows of a triangular left operand are zero left of the diagonal: a row
   // tile starting at row g0 needs k >= g0 only.
   int kb_begin = 0;
-  if constexpr (AK == AKind::UpperPacked || AK == AKind::UpperDense) kb_begin = (p.a_row0 + tile_m0) / KS;
+  if constexpr (AK == AKind::UpperPacked) kb_begin = (p.a_row0 + tile_m0) / KS;
+  if constexpr (AK == AKind::UpperDense) kb_begin = a_struct_row(p, tile_m0) / KS;
   int kb_end = (p.K + KS - 1) / KS;
   // A lower-triangular left operand is zero right of its diagonal: rows up
   // to g1 need k <= g1 only.

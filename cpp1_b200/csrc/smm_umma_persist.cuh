@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     tile_m0 = (first + in % rows_here) * 2 * kBM;
     n0 = (in / rows_here) * BN;
     kb_begin = 0;
-    if constexpr (AK == AKind::UpperDense) kb_begin = (p.a_row0 + tile_m0) / KS;
+    if constexpr (AK == AKind::UpperDense) kb_begin = a_struct_row(p, tile_m0) / KS;
     const int kb_end = (p.K + KS - 1) / KS;
     num_kb = (max(kb_end - kb_begin, 0) + kSubs - 1) / kSubs;
   };

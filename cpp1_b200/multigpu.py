@@ -264,7 +264,11 @@ class Communicator:
     # world) (all-gathered inside the call).
     @staticmethod
     def _root(root) -> int:
-        return SHARDED if root in (SHARDED, "sharded") else int(root)
+        if root in (SHARDED, "sharded"):
+            return SHARDED
+        if root in (REPLICATED, "replicated"):
+            return REPLICATED
+        return int(root)
 
     def gemm(self, A_slab, B, C_slab, mode: str = "3xtf32", root=0, stream=None):
         """C_slab = A_slab @ B.  Broadcast: B is read on the root only (the
@@ -292,6 +296,23 @@ class Communicator:
         self._lib.check(L.smm_mg_upper_left(self.h, U.data_ptr(), B.data_ptr(), cp, N, ncols, row0, nrows, m,
                                             self._root(root), ws, wsb, self._stream(stream)), "smm_mg_upper_left")
         return C_slab
+
+    def upper_left_tiles(self, U, B, C_rows, tiles, mode: str = "3xtf32", root=0, stream=None):
+        """C_rows = the rows of U @ B in `tiles` (ascending indices of 256-row
+        tiles of U; upper_row_tiles gives the balanced interleaved share),
+        stacked in that order; U packed upper on every rank."""
+        import ctypes
+        L = self._lib.load()
+        m = self._lib.MODES[mode]
+        N = packed_order(U.numel())
+        ncols = B.shape[1]
+        t = (ctypes.c_int * max(1, len(tiles)))(*tiles)
+        ws, wsb = self._ws(L.smm_mg_upper_left_tiles_workspace_size(self.h, N, ncols, len(tiles), m), B.device)
+        cp = C_rows.data_ptr() if len(tiles) else None
+        self._lib.check(L.smm_mg_upper_left_tiles(self.h, U.data_ptr(), B.data_ptr(), cp, N, ncols, t, len(tiles), m,
+                                                  self._root(root), ws, wsb, self._stream(stream)),
+                        "smm_mg_upper_left_tiles")
+        return C_rows
 
     def toeplitz_left(self, g, B, C_slab, row0: int, mode: str = "3xtf32", root=0, stream=None):
         """C_slab = T[row0:row0+nrows] @ B, T of generator g (2N - 1 values)
@@ -325,6 +346,42 @@ class Communicator:
 
 
 SHARDED = -1  # root value of a call whose B is sharded by rows (SMM_MG_SHARDED)
+REPLICATED = -2  # root value of a call whose B is whole on every rank (SMM_MG_REPLICATED)
+TILE_ROWS_MG = 256  # rows of a tile of U in the interleaved partition
+
+
+def upper_row_tiles(n: int, world: int, rank: int) -> List[int]:
+    """This rank's row tiles of U in the interleaved partition (restatement
+    of libsmm's smm_mg_upper_row_tiles): tiles in decreasing order of work
+    (row i costs n - i) each to the rank with the least work so far, ties to
+    the lower rank."""
+    nt = -(-n // TILE_ROWS_MG)
+    load = [0] * world
+    mine = []
+    for t in range(nt):
+        a, e = t * TILE_ROWS_MG, min(n, (t + 1) * TILE_ROWS_MG)
+        cost = (e - a) * n - (e * (e - 1) - a * (a - 1)) // 2
+        g = min(range(world), key=lambda h: (load[h], h))
+        load[g] += cost
+        if g == rank:
+            mine.append(t)
+    return mine
+
+
+def tile_rows_of(n: int, tiles: List[int]) -> List[int]:
+    """Rows of U (and of C) that a list of row tiles covers, in stacked order."""
+    return [i for t in tiles for i in range(t * TILE_ROWS_MG, min(n, (t + 1) * TILE_ROWS_MG))]
+
+
+def lib_upper_row_tiles(n: int, world: int, rank: int) -> List[int]:
+    """The library's interleaved row tiles (smm_mg_upper_row_tiles)."""
+    import ctypes
+    from . import _lib
+    cap = max(1, -(-n // TILE_ROWS_MG))
+    b = (ctypes.c_int * cap)()
+    k = ctypes.c_int(0)
+    _lib.check(_lib.load().smm_mg_upper_row_tiles(n, world, rank, b, cap, ctypes.byref(k)), "smm_mg_upper_row_tiles")
+    return list(b)[:k.value]
 
 
 def packed_order(length: int) -> int:

@@ -208,6 +208,9 @@ int smm_symm_sandwich_noalloc(const float* A, const float* S_packed, const float
  * already in the process when there is one).  At world = 1 the calls
  * compute without any collective. */
 #define SMM_MG_SHARDED (-1)
+/* `root` = SMM_MG_REPLICATED: B is whole on every rank (and the sandwich's S):
+ * nothing travels, every rank computes its rows from its own B in place. */
+#define SMM_MG_REPLICATED (-2)
 #define SMM_MG_ID_BYTES 128
 typedef struct smm_mg_comm smm_mg_comm;
 
@@ -269,6 +272,24 @@ int smm_mg_gemm(smm_mg_comm* comm, const float* A_slab, const float* B, float* C
 size_t smm_mg_upper_left_workspace_size(const smm_mg_comm* comm, int N, int ncols, int nrows, int mode);
 int smm_mg_upper_left(smm_mg_comm* comm, const float* U_packed, const float* B, float* C_slab, int N, int ncols,
                       int row0, int nrows, int mode, int root, void* ws, size_t ws_bytes, void* stream);
+/* Interleaved ownership of U's rows (the alternative to one contiguous slab
+ * per rank): U's 256-row tiles in decreasing order of work each go to the
+ * rank with the least work so far, so every rank holds long and short rows
+ * alike and the ranks' tile schedules come out even (32 tiles on 8 ranks:
+ * {r, 15 - r, 16 + r, 31 - r}).  Writes this rank's tile indices, ascending,
+ * into tiles (room for max_tiles; ceil(N / 256) always suffices) and their
+ * number into *count.  No counterpart in the reference (it has no
+ * multi-GPU code). */
+int smm_mg_upper_row_tiles(int N, int world, int rank, int* tiles, int max_tiles, int* count);
+/* C_rows = the rows of U B in this rank's row tiles (ascending indices of
+ * 256-row tiles of U, at most 64), stacked in that order: tile i's rows at
+ * C_rows + (256 i) ncols (the last tile of U may be shorter).  U packed upper
+ * on every rank; B as for the other calls.  One call moves B once and
+ * computes all the tiles.  No counterpart in the reference. */
+size_t smm_mg_upper_left_tiles_workspace_size(const smm_mg_comm* comm, int N, int ncols, int ntiles, int mode);
+int smm_mg_upper_left_tiles(smm_mg_comm* comm, const float* U_packed, const float* B, float* C_rows, int N,
+                            int ncols, const int* tiles, int ntiles, int mode, int root, void* ws, size_t ws_bytes,
+                            void* stream);
 /* C_slab (nrows x ncols) = T[row0 : row0+nrows, :] B, T of generator g[2N-1]
  * (on every rank). */
 size_t smm_mg_toeplitz_left_workspace_size(const smm_mg_comm* comm, int N, int ncols, int mode);

@@ -111,6 +111,19 @@ def _worker(rank, world, port, results):
                     R = Ud[r0:r1] @ dev(w["B"]).double()
                     errs[f"upper{n}_{tag}"] = _relerr(C, R)
 
+                # U B by interleaved row tiles (the balanced partition), ragged
+                # last tile at 1000
+                for n, ncols in ((4096, 1024), (1000, 1000)):
+                    w = W.make_upper(n, ncols, seed=35)
+                    tiles = MG.lib_upper_row_tiles(n, world, rank)
+                    rows = MG.tile_rows_of(n, tiles)
+                    C = torch.empty((max(len(rows), 1), ncols), device="cuda")
+                    comm.upper_left_tiles(dev(w["U"]), barg(w["B"], n, placement), C, tiles, mode=mode, root=root)
+                    torch.cuda.synchronize()
+                    Ud = ops.unpack(dev(w["U"]), "upper", n).double()
+                    R = Ud[torch.tensor(rows, device="cuda")] @ dev(w["B"]).double()
+                    errs[f"uppertiles{n}_{tag}"] = _relerr(C[:len(rows)], R)
+
                 # T B with 5 column blocks (more than the 4 compute streams)
                 os.environ["SMM_MG_CHUNKS"] = "5"
                 n, ncols = 4096, 2560
@@ -136,6 +149,16 @@ def _worker(rank, world, port, results):
                 Sd = dev(W.unpack_symmetric(w["S"], n)).double()
                 R = (dev(w["A"][r0:r1]).double() @ Sd) @ dev(w["B"]).double()
                 errs[f"sandwich_{tag}"] = _relerr(C, R)
+        # B whole on every rank (nothing travels)
+        n, ncols = 2048, 768
+        w = W.make_upper(n, ncols, seed=36)
+        tiles = MG.lib_upper_row_tiles(n, world, rank)
+        rows = MG.tile_rows_of(n, tiles)
+        C = torch.empty((len(rows), ncols), device="cuda")
+        comm.upper_left_tiles(dev(w["U"]), dev(w["B"]), C, tiles, mode="3xtf32", root=MG.REPLICATED)
+        torch.cuda.synchronize()
+        Ud = ops.unpack(dev(w["U"]), "upper", n).double()
+        errs["uppertiles_replicated_3xtf32"] = _relerr(C, Ud[torch.tensor(rows, device="cuda")] @ dev(w["B"]).double())
         ops.device_status()
         comm.status()
         dist.barrier()
@@ -171,6 +194,41 @@ def test_two_gpu_products_match_fp64(cuda):
         for key, e in errs.items():
             mode = key.split("_")[-1]
             assert e <= TOL[mode], (rank, key, e, errs)
+
+
+@pytest.mark.parametrize("mode", ["3xtf32", "tf32", "bf16"])
+@pytest.mark.parametrize("tiles_env", ["auto", "pairs", "nosplit"])
+def test_single_rank_interleaved_row_tiles(cuda, monkeypatch, mode, tiles_env):
+    """smm_mg_upper_left_tiles on one rank: rows of U B from arbitrary
+    ascending 256-row tiles of U, stacked; each output row tile takes its K
+    range from its own U row (the kernels' row-tile map), in the single-CTA
+    split, per-tile pair and persistent pair kernels (SMM_PAIR=1 forces pairs,
+    SMM_SPLITK=0 the unsplit single-CTA tiles); B in place and replicated."""
+    from cpp1_b200 import multigpu as MG
+    from cpp1_b200 import ops
+    from cpp1_b200 import workloads as W
+    if tiles_env == "pairs":  # 256-wide pair tiles: the persistent kernel in the one-pass modes
+        monkeypatch.setenv("SMM_PAIR", "1")
+        monkeypatch.setenv("SMM_TILE_N", "256")
+    elif tiles_env == "nosplit":
+        monkeypatch.setenv("SMM_SPLITK", "0")
+    comm = MG.Communicator(0, 1)
+    try:
+        for n, ncols, tiles in ((2048, 1024, [1, 2, 6, 7]), (2048, 520, [0, 5]), (1000, 600, [0, 3]),
+                                (1000, 260, [3]), (1024, 512, [0, 1, 2, 3])):
+            w = W.make_upper(n, ncols, seed=n + ncols + len(tiles))
+            U = torch.from_numpy(w["U"]).cuda()
+            B = torch.from_numpy(w["B"]).cuda()
+            rows = MG.tile_rows_of(n, tiles)
+            R = ops.unpack(U, "upper", n).double()[torch.tensor(rows, device="cuda")] @ B.double()
+            for root in (0, MG.REPLICATED):
+                C = torch.full((len(rows), ncols), float("nan"), device="cuda")
+                comm.upper_left_tiles(U, B, C, tiles, mode=mode, root=root)
+                torch.cuda.synchronize()
+                assert _relerr(C, R) <= TOL[mode], (n, ncols, tiles, root, _relerr(C, R))
+        ops.device_status()
+    finally:
+        comm.close()
 
 
 def _leave_worker(rank, world, port, results):

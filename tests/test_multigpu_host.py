@@ -190,3 +190,21 @@ def test_packed_order():
         assert MG.packed_order(n * (n + 1) // 2) == n
     with pytest.raises(ValueError):
         MG.packed_order(4)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_interleaved_row_tiles(world):
+    """smm_mg_upper_row_tiles agrees with the host restatement; the ranks'
+    tiles cover U's 256-row tiles exactly once, ascending; the work per rank
+    is within one tile's work of the others; 32 tiles on 8 ranks give rank r
+    the tiles {r, 15 - r, 16 + r, 31 - r}."""
+    for n in (1, 255, 256, 1000, 4096, 8192, 8193):
+        nt = -(-n // 256)
+        own = [MG.lib_upper_row_tiles(n, world, r) for r in range(world)]
+        assert own == [MG.upper_row_tiles(n, world, r) for r in range(world)]
+        assert sorted(t for o in own for t in o) == list(range(nt))
+        assert all(o == sorted(o) for o in own)
+        work = [sum(n - i for i in MG.tile_rows_of(n, o)) for o in own]
+        assert max(work) - min(work) <= n * 256
+    assert [MG.lib_upper_row_tiles(8192, 8, r) for r in range(8)] == \
+        [sorted([r, 15 - r, 16 + r, 31 - r]) for r in range(8)]
