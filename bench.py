@@ -95,7 +95,7 @@ def parse_args():
                          "(default: see default_transfer)")
     ap.add_argument("--partition", choices=["slabs", "tiles"], default="slabs",
                     help="U B at G > 1: one contiguous equal-work slab per rank (smm_mg_row_slabs), or interleaved "
-                         "256-row tiles of U per rank (smm_mg_upper_row_tiles; measured 7%% slower at 2 GPUs)")
+                         "256-row tiles of U per rank (smm_mg_upper_row_tiles)")
     ap.add_argument("--roofline-s", type=float, default=1.0,
                     help="seconds of repeated calls over which the roofline kernel is timed")
     a = ap.parse_args()

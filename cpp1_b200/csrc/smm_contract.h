@@ -97,6 +97,16 @@ size_t expanded_bytes(int rows, int n, int mode);
 // or _SYMM) as a dense copy (fp32, or bf16 in bf16 mode) at ws_cur.
 int expand_operand(const float* P, int sf, int n, int row0, int rows, int mode, uint8_t*& ws_cur, Staged* out,
                    cudaStream_t st);
+// Row map of an expansion: slab row r holds matrix row row0[r / tile_rows] +
+// r % tile_rows (tile_rows = 0: row0 of the call + r).
+struct ExpandRowMap {
+  int tile_rows = 0;
+  int row0[kMaxMappedTiles] = {};
+};
+// The same for `rows` rows stacked from ntiles tiles of tile_rows rows (a
+// multiple of 64) starting at the matrix rows tile_row0[i]: one launch.
+int expand_operand_tiles(const float* P, int sf, int n, const int* tile_row0, int ntiles, int tile_rows, int rows,
+                         int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st);
 // Bytes of, and the dense copy of, the K x N Toeplitz matrix of generator g
 // (K + N - 1 floats; T[k][n] = g[(K-1) + (n-k)]), fp32 or bf16 by mode.
 size_t toeplitz_expanded_bytes(int K, int N, int mode);

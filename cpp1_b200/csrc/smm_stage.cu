@@ -81,16 +81,19 @@ __device__ __forceinline__ void store_pair(__nv_bfloat16* p, float a, float b) {
 }
 template <int SF, typename T>
 __global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P, int n, int row0, int rows,
-                                                     T* __restrict__ dst, int ld, uint32_t* status) {
+                                                     T* __restrict__ dst, int ld, uint32_t* status,
+                                                     const ExpandRowMap map) {
   const long long len = static_cast<long long>(n) * (n + 1) / 2;
   __shared__ float tile[64][65];
   const int r0 = blockIdx.y * 64;  // slab row of the tile
   const int c0 = blockIdx.x * 64;  // column of the tile
   const int t = threadIdx.x;
-  const bool mirror = SF == SMM_STRUCT_SYMM && c0 + 63 < row0 + r0;
+  // matrix row of slab row r0 (the 64-row tile lies inside one mapped tile)
+  const int g0 = map.tile_rows > 0 ? map.row0[r0 / map.tile_rows] + r0 % map.tile_rows : row0 + r0;
+  const bool mirror = SF == SMM_STRUCT_SYMM && c0 + 63 < g0;
   if (mirror) {
     const int il = t & 63;
-    const int i = row0 + r0 + il;
+    const int i = g0 + il;
     for (int jl = t >> 6; jl < 64; jl += 4) {
       const int j = c0 + jl;  // j < i for every element of the tile
       tile[jl][il] = (r0 + il < rows && j < n) ? ld_chk(P, packed_idx(j, i, n), len, status, kBoundsExpand) : 0.0f;
@@ -103,7 +106,7 @@ __global__ void __launch_bounds__(256) expand_kernel(const float* __restrict__ P
   for (int rl = t >> 5; rl < 64; rl += 8) {
     const int r = r0 + rl;
     if (r >= rows) break;
-    const int i = row0 + r;
+    const int i = g0 + rl;
     float v[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -143,17 +146,18 @@ __global__ void __launch_bounds__(256) toeplitz_expand_kernel(const float* __res
 }
 
 template <typename T>
-void launch_expand(const float* P, int sf, int n, int row0, int rows, T* dst, int ld, cudaStream_t st) {
+void launch_expand(const float* P, int sf, int n, int row0, int rows, T* dst, int ld, cudaStream_t st,
+                   const ExpandRowMap& map = ExpandRowMap{}) {
   const dim3 grid((ld + 63) / 64, (rows + 63) / 64);
   switch (sf) {
     case SMM_STRUCT_UPPER:
-      expand_kernel<SMM_STRUCT_UPPER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word());
+      expand_kernel<SMM_STRUCT_UPPER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word(), map);
       break;
     case SMM_STRUCT_LOWER:
-      expand_kernel<SMM_STRUCT_LOWER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word());
+      expand_kernel<SMM_STRUCT_LOWER, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word(), map);
       break;
     default:
-      expand_kernel<SMM_STRUCT_SYMM, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word());
+      expand_kernel<SMM_STRUCT_SYMM, T><<<grid, 256, 0, st>>>(P, n, row0, rows, dst, ld, device_status_word(), map);
       break;
   }
 }
@@ -237,6 +241,32 @@ int expand_operand(const float* P, int sf, int n, int row0, int rows, int mode, 
     const int ld = round4(n);
     float* dst = reinterpret_cast<float*>(ws_cur);
     launch_expand(P, sf, n, row0, rows, dst, ld, st);
+    *out = {dst, nullptr, ld};
+  }
+  ws_cur += expanded_bytes(rows, n, mode);
+  count_launch();
+  SMM_CUDA_TRY(cudaGetLastError(), "packed operand expansion launch");
+  return SMM_OK;
+}
+
+int expand_operand_tiles(const float* P, int sf, int n, const int* tile_row0, int ntiles, int tile_rows, int rows,
+                         int mode, uint8_t*& ws_cur, Staged* out, cudaStream_t st) {
+  if (ntiles < 1 || ntiles > kMaxMappedTiles || tile_rows < 64 || tile_rows % 64 != 0 ||
+      static_cast<long long>(ntiles) * tile_rows < rows)
+    return set_error(SMM_ERR_INVALID, "internal: bad expansion row map (%d tiles of %d rows for %d rows)", ntiles,
+                     tile_rows, rows);
+  ExpandRowMap map;
+  map.tile_rows = tile_rows;
+  for (int i = 0; i < ntiles; ++i) map.row0[i] = tile_row0[i];
+  if (mode == SMM_MODE_BF16) {
+    const int ld = round8(n);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(ws_cur);
+    launch_expand(P, sf, n, 0, rows, dst, ld, st, map);
+    *out = {nullptr, nullptr, ld, dst};
+  } else {
+    const int ld = round4(n);
+    float* dst = reinterpret_cast<float*>(ws_cur);
+    launch_expand(P, sf, n, 0, rows, dst, ld, st, map);
     *out = {dst, nullptr, ld};
   }
   ws_cur += expanded_bytes(rows, n, mode);
