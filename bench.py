@@ -22,11 +22,12 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
   others    strong scaling: the output is split into row slabs (equal-work
             boundaries for the triangular operand; --partition tiles deals
             U B's rows out as interleaved 256-row tiles instead); each step
-            is one libsmm multi-GPU call (smm_mg_*).  By default B arrives sharded by rows
-            (--b-placement sharded) and is gathered in column blocks inside
-            the call by the copy engines through CUDA IPC (--transfer ce; or
-            by NCCL all-gathers, --transfer nccl); --b-placement root keeps
-            B on rank 0 and broadcasts it by NCCL.  Every rank computes its
+            is one libsmm multi-GPU call (smm_mg_*).  By default B arrives
+            sharded by rows (--b-placement sharded) and is gathered in column
+            blocks inside the call by the copy engines through CUDA IPC
+            (--transfer ce) or by NCCL all-gathers (--transfer nccl), as
+            default_transfer chooses; --b-placement root keeps B on rank 0
+            and broadcasts it by NCCL.  Every rank computes its
             slab's columns block by block as they land, so the transfer
             overlaps the contraction within one product.  A S B computes
             (A_slab S) B per slab.  The line also carries the compute-only
